@@ -1,0 +1,136 @@
+/*
+ * semx.h — C ABI of the B200 (sm_100a) recurrent-scan library `libsemx.so`.
+ *
+ * The library implements the recurrent scans that sit inside the TF-blocks of the
+ * SEMamba generator of a-baur/SEMambaXLinOSS:
+ *   - the LinOSS oscillatory scan (IM / IMEX / damped IMEX, and the generic 2x2 form),
+ *   - the selective-LRU diagonal scan (SISO, real and complex),
+ *   - the selective-LRU MIMO scan with its block-diagonal readout,
+ *   - the plain complex diagonal scan.
+ * Each op has a forward and a backward entry point.
+ *
+ * Conventions (every entry point):
+ *   - All pointers are device pointers to fp32 data (complex tensors are interleaved
+ *     (re, im) pairs, i.e. the memory of a torch complex64 tensor), C-contiguous in the
+ *     documented shape.
+ *   - The first field of every argument struct is `struct_size`, which the caller sets to
+ *     sizeof(struct); a mismatch returns SEMX_ERR_ABI.
+ *   - Work is enqueued on `stream` (a cudaStream_t passed as an opaque pointer); nothing
+ *     synchronises the host. The library keeps no state between calls and allocates no
+ *     device memory: scratch comes from the caller through `workspace`, sized by the
+ *     matching *_workspace_bytes() query.
+ *   - The return value is SEMX_OK or one of the SEMX_ERR_* codes; no exception crosses
+ *     the ABI. semx_last_error() returns a message for the calling host thread.
+ *
+ * Names, argument meaning and error behaviour follow the reference's operator API; each
+ * declaration cites the reference function it replaces (paths relative to the reference
+ * project root).
+ */
+#ifndef SEMX_H
+#define SEMX_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SEMX_ABI_VERSION 1
+
+typedef void* semx_stream_t; /* cudaStream_t */
+
+enum semx_status {
+  SEMX_OK = 0,
+  SEMX_ERR_ABI = 1,          /* struct_size mismatch                                  */
+  SEMX_ERR_NULL = 2,         /* a required pointer is NULL                            */
+  SEMX_ERR_SHAPE = 3,        /* a size is negative/zero where forbidden, or too large */
+  SEMX_ERR_UNSUPPORTED = 4,  /* flag combination or size outside what is compiled     */
+  SEMX_ERR_ALIGN = 5,        /* a pointer is not aligned as documented                */
+  SEMX_ERR_LAUNCH = 6,       /* the CUDA launch itself failed                         */
+  SEMX_ERR_WORKSPACE = 7     /* workspace pointer NULL while workspace is required    */
+};
+
+/* ABI version compiled into the library (== SEMX_ABI_VERSION of this header). */
+int semx_abi_version(void);
+/* Static message for a status code. */
+const char* semx_status_string(int status);
+/* Message describing the last failing call made from this host thread ("" if none). */
+const char* semx_last_error(void);
+
+/* ------------------------------------------------------------------------------------
+ * LinOSS oscillatory scan.
+ *
+ *   [y1; y2]_t = [[M11, M12], [M21, M22]] [y1; y2]_{t-1} + [F1; F2]_t,   y_{-1} = 0,
+ *   output Y2_t = y2_t (complex), one independent 2x2 real transition per oscillator p.
+ *
+ * variant SEMX_LINOSS_GENERIC: M11..M22 (P,) and F1, F2 (S,L,P) complex are given.
+ *   Replaces linoss_scan_triton (models/linoss/triton.py:276-294) and the sequential
+ *   _linoss_recurrence (models/linoss/linoss.py:155-180).
+ * variants IM / IMEX / DAMPED_IMEX: the kernel builds M and F = (f1, f2) * Bu from the raw
+ *   parameters (steps, A_diag, G_diag), applying the same constraints as LinOSS.forward
+ *   (models/linoss/linoss.py:81-116: sigmoid(steps), relu(A_diag), the A-from-G or
+ *   G-from-A clamps) and the discretisations _apply_linoss_im / _apply_linoss_imex /
+ *   _apply_damped_linoss_imex (models/linoss/linoss.py:183-232). Input is Bu (S,L,P)
+ *   complex, the projected input of _project_input (models/linoss/linoss.py:148-152).
+ *
+ * Forward writes Y2 and, if ckpt != NULL, the state entering every `chunk`-step block:
+ *   ckpt (S, ceil(L/chunk), P, 4) fp32 = (y1.re, y1.im, y2.re, y2.im).
+ * Backward (needs the forward's ckpt) recomputes the states chunk by chunk and writes
+ *   GENERIC: dF1, dF2 (S,L,P) complex and dM (4,P) = dM11, dM12, dM21, dM22;
+ *   fused:   dBu (S,L,P) complex and dparams (3,P) = d steps, d A_diag, d G_diag
+ *            (d G_diag row written only for DAMPED_IMEX).
+ * Parameter gradients are reduced over (S, L) in a fixed order (deterministic).
+ * chunk must be a positive multiple of 8 and at most 512.
+ * ---------------------------------------------------------------------------------- */
+enum semx_linoss_variant {
+  SEMX_LINOSS_GENERIC = 0,
+  SEMX_LINOSS_IM = 1,
+  SEMX_LINOSS_IMEX = 2,
+  SEMX_LINOSS_DAMPED_IMEX = 3
+};
+
+typedef struct SemxLinossArgs {
+  uint32_t struct_size;
+  int32_t variant;   /* enum semx_linoss_variant                                  */
+  int32_t a_from_g;  /* DAMPED_IMEX: 1 = A clamped into the band set by G (default) */
+  int32_t chunk;     /* checkpoint interval / backward recompute block, in steps     */
+  int64_t S, L, P;   /* sequences, steps per sequence, oscillators                  */
+  /* GENERIC inputs */
+  const float* M11;
+  const float* M12;
+  const float* M21;
+  const float* M22;
+  const float* F1;   /* (S,L,P) complex */
+  const float* F2;   /* (S,L,P) complex */
+  /* fused-variant inputs */
+  const float* steps;  /* (P,) raw, before sigmoid */
+  const float* A_diag; /* (P,) raw                 */
+  const float* G_diag; /* (P,) raw, DAMPED_IMEX only */
+  const float* Bu;     /* (S,L,P) complex            */
+  /* forward outputs */
+  float* Y2;   /* (S,L,P) complex */
+  float* ckpt; /* (S, ceil(L/chunk), P, 4) or NULL */
+  /* backward */
+  const float* dY2; /* (S,L,P) complex */
+  float* dF1;       /* GENERIC (S,L,P) complex */
+  float* dF2;       /* GENERIC (S,L,P) complex */
+  float* dBu;       /* fused (S,L,P) complex   */
+  float* dM;        /* GENERIC (4,P)           */
+  float* dparams;   /* fused (3,P)             */
+  void* workspace;  /* semx_linoss_workspace_bytes() bytes, backward only */
+} SemxLinossArgs;
+
+size_t semx_linoss_args_size(void);
+/* Size of ckpt in bytes for (S, L, P, chunk). */
+size_t semx_linoss_ckpt_bytes(int64_t S, int64_t L, int64_t P, int32_t chunk);
+/* Scratch the backward needs (per-sequence partial reductions). */
+size_t semx_linoss_workspace_bytes(const SemxLinossArgs* args);
+int semx_linoss_fwd(const SemxLinossArgs* args, semx_stream_t stream);
+int semx_linoss_bwd(const SemxLinossArgs* args, semx_stream_t stream);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* SEMX_H */

@@ -1,0 +1,158 @@
+"""ctypes binding of ``libsemx.so`` (declared in ``include/semx.h``).
+
+This is the only place Python touches the C ABI. It mirrors the argument structs,
+checks at load time that the library's struct sizes and ABI version match these
+mirrors, and turns non-zero status codes into Python exceptions. There is no fallback:
+if the library is missing or a call fails, the caller gets an exception.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+import torch
+
+LIB_PATH = Path(__file__).resolve().parent / "libsemx.so"
+ABI_VERSION = 1
+
+c_f32p = ctypes.POINTER(ctypes.c_float)
+
+# Status codes (enum semx_status).
+SEMX_OK = 0
+SEMX_ERR_ABI = 1
+SEMX_ERR_NULL = 2
+SEMX_ERR_SHAPE = 3
+SEMX_ERR_UNSUPPORTED = 4
+SEMX_ERR_ALIGN = 5
+SEMX_ERR_LAUNCH = 6
+SEMX_ERR_WORKSPACE = 7
+
+# enum semx_linoss_variant
+LINOSS_GENERIC = 0
+LINOSS_IM = 1
+LINOSS_IMEX = 2
+LINOSS_DAMPED_IMEX = 3
+
+
+class SemxError(RuntimeError):
+    """A semx entry point returned a non-zero status."""
+
+    def __init__(self, fn: str, status: int, message: str):
+        super().__init__(f"{fn} failed with status {status}: {message}")
+        self.status = status
+
+
+class SemxLinossArgs(ctypes.Structure):
+    _fields_ = [
+        ("struct_size", ctypes.c_uint32),
+        ("variant", ctypes.c_int32),
+        ("a_from_g", ctypes.c_int32),
+        ("chunk", ctypes.c_int32),
+        ("S", ctypes.c_int64),
+        ("L", ctypes.c_int64),
+        ("P", ctypes.c_int64),
+        ("M11", ctypes.c_void_p),
+        ("M12", ctypes.c_void_p),
+        ("M21", ctypes.c_void_p),
+        ("M22", ctypes.c_void_p),
+        ("F1", ctypes.c_void_p),
+        ("F2", ctypes.c_void_p),
+        ("steps", ctypes.c_void_p),
+        ("A_diag", ctypes.c_void_p),
+        ("G_diag", ctypes.c_void_p),
+        ("Bu", ctypes.c_void_p),
+        ("Y2", ctypes.c_void_p),
+        ("ckpt", ctypes.c_void_p),
+        ("dY2", ctypes.c_void_p),
+        ("dF1", ctypes.c_void_p),
+        ("dF2", ctypes.c_void_p),
+        ("dBu", ctypes.c_void_p),
+        ("dM", ctypes.c_void_p),
+        ("dparams", ctypes.c_void_p),
+        ("workspace", ctypes.c_void_p),
+    ]
+
+
+# (python struct, C size query) for every argument struct in semx.h.
+STRUCTS = {
+    "SemxLinossArgs": (SemxLinossArgs, "semx_linoss_args_size"),
+}
+
+# Every symbol semx.h declares, with its ctypes signature.
+_SIGNATURES = {
+    "semx_abi_version": (ctypes.c_int, []),
+    "semx_status_string": (ctypes.c_char_p, [ctypes.c_int]),
+    "semx_last_error": (ctypes.c_char_p, []),
+    "semx_linoss_args_size": (ctypes.c_size_t, []),
+    "semx_linoss_ckpt_bytes": (
+        ctypes.c_size_t,
+        [ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int32],
+    ),
+    "semx_linoss_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(SemxLinossArgs)]),
+    "semx_linoss_fwd": (ctypes.c_int, [ctypes.POINTER(SemxLinossArgs), ctypes.c_void_p]),
+    "semx_linoss_bwd": (ctypes.c_int, [ctypes.POINTER(SemxLinossArgs), ctypes.c_void_p]),
+}
+
+_lib = None
+_lock = threading.Lock()
+
+
+def declared_symbols() -> list[str]:
+    return sorted(_SIGNATURES)
+
+
+def load() -> ctypes.CDLL:
+    """Loads and checks ``libsemx.so``; raises if it is missing or mismatched."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not LIB_PATH.exists():
+            raise RuntimeError(
+                f"semx CUDA library not found at {LIB_PATH}; build it with "
+                "`python -m semambaxlinoss_b200.build` (or __graft_entry__.build())"
+            )
+        lib = ctypes.CDLL(str(LIB_PATH))
+        for name, (res, argtypes) in _SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = argtypes
+        if lib.semx_abi_version() != ABI_VERSION:
+            raise RuntimeError(
+                f"libsemx ABI version {lib.semx_abi_version()} != binding {ABI_VERSION}"
+            )
+        for sname, (cls, query) in STRUCTS.items():
+            if getattr(lib, query)() != ctypes.sizeof(cls):
+                raise RuntimeError(
+                    f"{sname}: library size {getattr(lib, query)()} != binding "
+                    f"{ctypes.sizeof(cls)}"
+                )
+        _lib = lib
+        return lib
+
+
+def check(fn: str, status: int) -> None:
+    if status != SEMX_OK:
+        lib = load()
+        msg = lib.semx_last_error().decode(errors="replace")
+        raise SemxError(fn, status, msg or lib.semx_status_string(status).decode())
+
+
+def ptr(t: torch.Tensor | None) -> int | None:
+    """Device address of a tensor's storage (None for a missing optional tensor)."""
+    if t is None:
+        return None
+    return t.data_ptr()
+
+
+def stream_handle(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def new_args(cls):
+    a = cls()
+    a.struct_size = ctypes.sizeof(cls)
+    return a

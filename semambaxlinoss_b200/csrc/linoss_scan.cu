@@ -1,0 +1,606 @@
+// LinOSS oscillatory scan, forward and backward, for sm_100a.
+//
+// Reference behaviour (paths relative to the reference project):
+//   recurrence      models/linoss/linoss.py:155-180  (_linoss_recurrence)
+//   discretisations models/linoss/linoss.py:183-232  (IM, IMEX, damped IMEX)
+//   constraints     models/linoss/linoss.py:81-116   (sigmoid steps, relu / clamp bands)
+//   generic op      models/linoss/triton.py:195-294  (M11..M22, F1, F2 -> Y2)
+//
+// Layout. One thread owns one (sequence s, oscillator p) chain; the flat thread index is
+// s * P + p, so a warp reads 32 consecutive oscillators of the same time step (256 B of
+// interleaved complex64). The state (y1, y2) is 2 complex numbers in registers. The loop
+// over time is sequential; loads are issued one 8-step batch ahead of the arithmetic so
+// every thread keeps 8 loads in flight.
+//
+// Forward (training) additionally stores the state entering every `chunk`-step block
+// (16 B per chunk and chain). Backward walks the chunks in reverse. For each chunk it
+// re-runs the recurrence once from the checkpoint, dropping the state every kSub steps
+// into shared memory; then for each kSub-step sub-block (last first) it recomputes the
+// kSub states into registers and runs the adjoint
+//   a_t = (0, dY2_t) + M^T a_{t+1},  dF_t = a_t,  dM_ij += Re(a_i,t conj(s_j,t-1)),
+// so no per-step state ever goes to HBM. Per-oscillator parameter gradients are summed
+// per chain in registers, written once per chain, and reduced over sequences by
+// linoss_finalize_kernel in a fixed order (bitwise deterministic), which also applies
+// the chain rule from (M, f) back to the raw parameters.
+#include "semx_common.cuh"
+
+namespace {
+
+constexpr int kBlock = 128;  // threads per CTA (scan kernels)
+constexpr int kSub = 8;      // steps per register-resident sub-block
+constexpr int kMaxChunk = 256;
+constexpr int kPartials = 6;  // dM11, dM12, dM21, dM22, df1, df2
+
+struct Coef {
+  float m11, m12, m21, m22;  // transition
+  float f1, f2;              // F1 = f1 * Bu, F2 = f2 * Bu (fused variants)
+};
+
+struct Params {
+  int variant, a_from_g, chunk, nchunks;
+  int64_t S, L, P;
+  const float* M11;
+  const float* M12;
+  const float* M21;
+  const float* M22;
+  const float2* F1;
+  const float2* F2;
+  const float* steps;
+  const float* A_diag;
+  const float* G_diag;
+  const float2* Bu;
+  float2* Y2;
+  float4* ckpt;
+  const float2* dY2;
+  float2* dF1;
+  float2* dF2;
+  float2* dBu;
+  float* dM;
+  float* dparams;
+  float* part;  // (S, kPartials, P)
+};
+
+__device__ __forceinline__ float sigmoid_f(float x) { return 1.0f / (1.0f + expf(-x)); }
+__device__ __forceinline__ float relu_f(float x) { return x > 0.0f ? x : 0.0f; }
+
+// Per-oscillator constraint chain and discretisation, evaluated in the same order as the
+// reference's tensor expressions (models/linoss/linoss.py:82-116, 183-232).
+__device__ __forceinline__ Coef make_coef(int variant, int a_from_g, float sraw, float araw,
+                                          float graw) {
+  Coef k;
+  const float step = sigmoid_f(sraw);
+  const float st2 = step * step;
+  if (variant == SEMX_LINOSS_IM) {
+    const float A = relu_f(araw);
+    const float schur = 1.0f / (1.0f + st2 * A);
+    k.m11 = 1.0f - st2 * A * schur;
+    k.m12 = -step * A * schur;
+    k.m21 = step * schur;
+    k.m22 = schur;
+    k.f1 = k.m11 * step;
+    k.f2 = k.m21 * step;
+  } else if (variant == SEMX_LINOSS_IMEX) {
+    const float A = relu_f(araw);
+    k.m11 = 1.0f;
+    k.m12 = -step * A;
+    k.m21 = step;
+    k.m22 = 1.0f - st2 * A;
+    k.f1 = step;
+    k.f2 = st2;
+  } else {  // DAMPED_IMEX
+    float A, G;
+    if (a_from_g) {
+      G = relu_f(graw);
+      const float sq = sqrtf(1.0f + step * G);
+      const float A_low = (2.0f + step * G - 2.0f * sq) / st2;
+      const float A_high = (2.0f + step * G + 2.0f * sq) / st2;
+      A = A_low + relu_f(araw - A_low) - relu_f(araw - A_high);
+    } else {
+      A = relu_f(araw);
+      const float sA = sqrtf(A);
+      const float G_low = relu_f(step * A - 2.0f * sA);
+      const float G_high = step * A + 2.0f * sA;
+      G = fminf(fmaxf(graw, G_low), G_high);
+    }
+    const float inv = 1.0f / (1.0f + step * G);
+    k.m11 = inv;
+    k.m12 = -step * inv * A;
+    k.m21 = step * inv;
+    k.m22 = 1.0f - st2 * inv * A;
+    k.f1 = step * inv;
+    k.f2 = st2 * inv;
+  }
+  return k;
+}
+
+__device__ __forceinline__ Coef load_coef(const Params& p, int o) {
+  if (p.variant == SEMX_LINOSS_GENERIC) {
+    Coef k;
+    k.m11 = p.M11[o];
+    k.m12 = p.M12[o];
+    k.m21 = p.M21[o];
+    k.m22 = p.M22[o];
+    k.f1 = 1.0f;
+    k.f2 = 1.0f;
+    return k;
+  }
+  const float graw = (p.variant == SEMX_LINOSS_DAMPED_IMEX) ? p.G_diag[o] : 0.0f;
+  return make_coef(p.variant, p.a_from_g, p.steps[o], p.A_diag[o], graw);
+}
+
+// One recurrence step. s = (y1.re, y1.im, y2.re, y2.im); forcing F1 = u1, F2 = u2.
+__device__ __forceinline__ float4 lin_step(const Coef& k, float4 s, float2 u1, float2 u2) {
+  float4 n;
+  n.x = k.m11 * s.x + k.m12 * s.z + u1.x;
+  n.y = k.m11 * s.y + k.m12 * s.w + u1.y;
+  n.z = k.m21 * s.x + k.m22 * s.z + u2.x;
+  n.w = k.m21 * s.y + k.m22 * s.w + u2.y;
+  return n;
+}
+
+template <bool GENERIC>
+__device__ __forceinline__ void forcing(const Coef& k, float2 in1, float2 in2, float2& u1,
+                                        float2& u2) {
+  if (GENERIC) {
+    u1 = in1;
+    u2 = in2;
+  } else {
+    u1 = make_float2(k.f1 * in1.x, k.f1 * in1.y);
+    u2 = make_float2(k.f2 * in1.x, k.f2 * in1.y);
+  }
+}
+
+template <bool GENERIC>
+__device__ __forceinline__ void load_batch(const Params& p, int64_t base, int t0, int tend,
+                                           float2 (&a)[kSub], float2 (&b)[kSub]) {
+  const float2* src1 = GENERIC ? p.F1 : p.Bu;
+#pragma unroll
+  for (int i = 0; i < kSub; ++i) {
+    if (t0 + i < tend) {
+      a[i] = __ldg(src1 + base + (int64_t)(t0 + i) * p.P);
+      if (GENERIC) b[i] = __ldg(p.F2 + base + (int64_t)(t0 + i) * p.P);
+    }
+  }
+}
+
+template <bool GENERIC>
+__global__ void __launch_bounds__(kBlock) linoss_fwd_kernel(const Params p) {
+  const int64_t gid = (int64_t)blockIdx.x * kBlock + threadIdx.x;
+  if (gid >= p.S * p.P) return;
+  const int64_t s = gid / p.P;
+  const int o = (int)(gid - s * p.P);
+  const Coef k = load_coef(p, o);
+  const int L = (int)p.L;
+  const int64_t base = s * p.L * p.P + o;
+
+  float4 st = make_float4(0.f, 0.f, 0.f, 0.f);
+  float2 c1[kSub], c2[kSub];
+  load_batch<GENERIC>(p, base, 0, L, c1, c2);
+  for (int t0 = 0; t0 < L; t0 += kSub) {
+    float2 n1[kSub], n2[kSub];
+    load_batch<GENERIC>(p, base, t0 + kSub, L, n1, n2);
+    if (p.ckpt != nullptr && (t0 % p.chunk) == 0)
+      p.ckpt[(s * p.nchunks + t0 / p.chunk) * p.P + o] = st;
+#pragma unroll
+    for (int i = 0; i < kSub; ++i) {
+      if (t0 + i < L) {
+        float2 u1, u2;
+        forcing<GENERIC>(k, c1[i], c2[i], u1, u2);
+        st = lin_step(k, st, u1, u2);
+        p.Y2[base + (int64_t)(t0 + i) * p.P] = make_float2(st.z, st.w);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < kSub; ++i) {
+      c1[i] = n1[i];
+      c2[i] = n2[i];
+    }
+  }
+}
+
+template <bool GENERIC>
+__global__ void __launch_bounds__(kBlock) linoss_bwd_kernel(const Params p) {
+  extern __shared__ float4 sub_ckpt[];  // [chunk / kSub][kBlock]
+  const int64_t gid = (int64_t)blockIdx.x * kBlock + threadIdx.x;
+  if (gid >= p.S * p.P) return;
+  const int64_t s = gid / p.P;
+  const int o = (int)(gid - s * p.P);
+  const Coef k = load_coef(p, o);
+  const int L = (int)p.L;
+  const int64_t base = s * p.L * p.P + o;
+
+  float a1r = 0.f, a1i = 0.f, a2r = 0.f, a2i = 0.f;  // adjoint a_{t+1}
+  float g11 = 0.f, g12 = 0.f, g21 = 0.f, g22 = 0.f, gf1 = 0.f, gf2 = 0.f;
+
+  for (int c = p.nchunks - 1; c >= 0; --c) {
+    const int t0 = c * p.chunk;
+    const int t1 = min(t0 + p.chunk, L);
+    const float4 entry = p.ckpt[(s * p.nchunks + c) * p.P + o];
+
+    // Pass 1: recurrence over the chunk, keeping the state every kSub steps on chip.
+    {
+      float4 st = entry;
+      float2 c1[kSub], c2[kSub];
+      load_batch<GENERIC>(p, base, t0, t1, c1, c2);
+      for (int tb = t0; tb < t1; tb += kSub) {
+        float2 n1[kSub], n2[kSub];
+        load_batch<GENERIC>(p, base, tb + kSub, t1, n1, n2);
+        sub_ckpt[((tb - t0) / kSub) * kBlock + threadIdx.x] = st;
+#pragma unroll
+        for (int i = 0; i < kSub; ++i) {
+          if (tb + i < t1) {
+            float2 u1, u2;
+            forcing<GENERIC>(k, c1[i], c2[i], u1, u2);
+            st = lin_step(k, st, u1, u2);
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < kSub; ++i) {
+          c1[i] = n1[i];
+          c2[i] = n2[i];
+        }
+      }
+    }
+
+    // Pass 2: sub-blocks in reverse; recompute kSub states into registers, then adjoint.
+    const int nsub = (t1 - t0 + kSub - 1) / kSub;
+    for (int r = nsub - 1; r >= 0; --r) {
+      const int ta = t0 + r * kSub;
+      const float4 s0 = sub_ckpt[r * kBlock + threadIdx.x];
+      float2 in1[kSub], in2[kSub], dy[kSub];
+      load_batch<GENERIC>(p, base, ta, t1, in1, in2);
+#pragma unroll
+      for (int i = 0; i < kSub; ++i)
+        if (ta + i < t1) dy[i] = __ldg(p.dY2 + base + (int64_t)(ta + i) * p.P);
+      float4 hs[kSub];
+      float4 st = s0;
+#pragma unroll
+      for (int i = 0; i < kSub; ++i) {
+        if (ta + i < t1) {
+          float2 u1, u2;
+          forcing<GENERIC>(k, in1[i], in2[i], u1, u2);
+          st = lin_step(k, st, u1, u2);
+          hs[i] = st;
+        }
+      }
+#pragma unroll
+      for (int i = kSub - 1; i >= 0; --i) {
+        if (ta + i < t1) {
+          const float n1r = k.m11 * a1r + k.m21 * a2r;
+          const float n1i = k.m11 * a1i + k.m21 * a2i;
+          const float n2r = dy[i].x + k.m12 * a1r + k.m22 * a2r;
+          const float n2i = dy[i].y + k.m12 * a1i + k.m22 * a2i;
+          a1r = n1r;
+          a1i = n1i;
+          a2r = n2r;
+          a2i = n2i;
+          const int64_t off = base + (int64_t)(ta + i) * p.P;
+          if (GENERIC) {
+            p.dF1[off] = make_float2(a1r, a1i);
+            p.dF2[off] = make_float2(a2r, a2i);
+          } else {
+            p.dBu[off] = make_float2(k.f1 * a1r + k.f2 * a2r, k.f1 * a1i + k.f2 * a2i);
+            gf1 += a1r * in1[i].x + a1i * in1[i].y;
+            gf2 += a2r * in1[i].x + a2i * in1[i].y;
+          }
+          const float4 sp = (i > 0) ? hs[i > 0 ? i - 1 : 0] : s0;
+          g11 += a1r * sp.x + a1i * sp.y;
+          g12 += a1r * sp.z + a1i * sp.w;
+          g21 += a2r * sp.x + a2i * sp.y;
+          g22 += a2r * sp.z + a2i * sp.w;
+        }
+      }
+    }
+  }
+
+  float* part = p.part + s * kPartials * p.P + o;
+  part[0 * p.P] = g11;
+  part[1 * p.P] = g12;
+  part[2 * p.P] = g21;
+  part[3 * p.P] = g22;
+  part[4 * p.P] = gf1;
+  part[5 * p.P] = gf2;
+}
+
+// d(loss)/d(raw parameters) from the summed gradients of (M11, M12, M21, M22, f1, f2),
+// following the reference's expression graph (models/linoss/linoss.py:82-116, 183-232)
+// term by term, including the sub-gradient conventions of relu (zero at 0) and of clamp
+// with tensor bounds.
+__device__ void linoss_chain(int variant, int a_from_g, float sraw, float araw, float graw,
+                             const float g[kPartials], float& d_s, float& d_a, float& d_g) {
+  const float step = sigmoid_f(sraw);
+  const float st2 = step * step;
+  const float gM11 = g[0], gM12 = g[1], gM21 = g[2], gM22 = g[3], gf1 = g[4], gf2 = g[5];
+  float gs = 0.f, gA = 0.f, gG = 0.f;
+  d_g = 0.f;
+  if (variant == SEMX_LINOSS_IMEX) {
+    const float A = relu_f(araw);
+    gs = -A * gM12 + gM21 - 2.0f * step * A * gM22 + gf1 + 2.0f * step * gf2;
+    gA = -step * gM12 - st2 * gM22;
+    d_a = araw > 0.0f ? gA : 0.0f;
+  } else if (variant == SEMX_LINOSS_IM) {
+    const float A = relu_f(araw);
+    const float q = st2 * A;
+    const float schur = 1.0f / (1.0f + q);
+    const float m11 = 1.0f - q * schur;
+    const float m21 = step * schur;
+    const float dsc_ds = -schur * schur * 2.0f * step * A;
+    const float dsc_dA = -schur * schur * st2;
+    const float dm11_ds = -(2.0f * step * A * schur + q * dsc_ds);
+    const float dm11_dA = -(st2 * schur + q * dsc_dA);
+    const float dm12_ds = -(A * schur + step * A * dsc_ds);
+    const float dm12_dA = -(step * schur + step * A * dsc_dA);
+    const float dm21_ds = schur + step * dsc_ds;
+    const float dm21_dA = step * dsc_dA;
+    gs = gM11 * dm11_ds + gM12 * dm12_ds + gM21 * dm21_ds + gM22 * dsc_ds +
+         gf1 * (dm11_ds * step + m11) + gf2 * (dm21_ds * step + m21);
+    gA = gM11 * dm11_dA + gM12 * dm12_dA + gM21 * dm21_dA + gM22 * dsc_dA + gf1 * dm11_dA * step +
+         gf2 * dm21_dA * step;
+    d_a = araw > 0.0f ? gA : 0.0f;
+  } else {  // DAMPED_IMEX
+    // Recompute the constrained (A, G) exactly as make_coef does.
+    float A, G;
+    float sq = 0.f, A_low = 0.f, A_high = 0.f, sA = 0.f, G_low = 0.f, G_high = 0.f, v = 0.f;
+    if (a_from_g) {
+      G = relu_f(graw);
+      sq = sqrtf(1.0f + step * G);
+      A_low = (2.0f + step * G - 2.0f * sq) / st2;
+      A_high = (2.0f + step * G + 2.0f * sq) / st2;
+      A = A_low + relu_f(araw - A_low) - relu_f(araw - A_high);
+    } else {
+      A = relu_f(araw);
+      sA = sqrtf(A);
+      v = step * A - 2.0f * sA;
+      G_low = relu_f(v);
+      G_high = step * A + 2.0f * sA;
+      G = fminf(fmaxf(graw, G_low), G_high);
+    }
+    const float inv = 1.0f / (1.0f + step * G);
+    const float dinv_ds = -inv * inv * G;
+    const float dinv_dG = -inv * inv * step;
+    // M11 = inv
+    gs += gM11 * dinv_ds;
+    gG += gM11 * dinv_dG;
+    // M12 = -step * inv * A
+    gs += gM12 * (-(inv + step * dinv_ds) * A);
+    gA += gM12 * (-step * inv);
+    gG += gM12 * (-step * A * dinv_dG);
+    // M21 = f1 = step * inv
+    gs += (gM21 + gf1) * (inv + step * dinv_ds);
+    gG += (gM21 + gf1) * (step * dinv_dG);
+    // M22 = 1 - step^2 * inv * A
+    gs += gM22 * (-(2.0f * step * inv + st2 * dinv_ds) * A);
+    gA += gM22 * (-st2 * inv);
+    gG += gM22 * (-st2 * A * dinv_dG);
+    // f2 = step^2 * inv
+    gs += gf2 * (2.0f * step * inv + st2 * dinv_ds);
+    gG += gf2 * (st2 * dinv_dG);
+    if (a_from_g) {
+      const bool il = (araw - A_low) > 0.0f;
+      const bool ih = (araw - A_high) > 0.0f;
+      d_a = gA * ((il ? 1.0f : 0.0f) - (ih ? 1.0f : 0.0f));
+      const float gAl = il ? 0.0f : gA;
+      const float gAh = ih ? gA : 0.0f;
+      const float u = step * G;
+      (void)u;
+      const float gu = gAl * (1.0f - 1.0f / sq) / st2 + gAh * (1.0f + 1.0f / sq) / st2;
+      gs += gAl * (-2.0f * A_low / step) + gAh * (-2.0f * A_high / step) + gu * G;
+      gG += gu * step;
+      d_g = graw > 0.0f ? gG : 0.0f;
+    } else {
+      const float g_in = (graw >= G_low && graw <= G_high) ? gG : 0.0f;
+      const float g_min = (graw < G_low && G_low < G_high) ? gG : 0.0f;
+      const float g_max = (graw > G_high || G_high < G_low) ? gG : 0.0f;
+      d_g = g_in;
+      if (araw > 0.0f) {
+        const float gv = v > 0.0f ? g_min : 0.0f;
+        gs += gv * A + g_max * A;
+        gA += gv * step + g_max * step;
+        const float gsA = -2.0f * gv + 2.0f * g_max;
+        gA += gsA * (0.5f / sA);
+        d_a = gA;
+      } else {
+        gs += (v > 0.0f ? g_min : 0.0f) * A + g_max * A;
+        d_a = 0.0f;
+      }
+    }
+  }
+  d_s = gs * (step * (1.0f - step));
+}
+
+// Sums the per-sequence partials over S in a fixed order: thread (x, y) of a 32x8 block
+// adds sequences y, y+8, y+16, ... for oscillator x; the 8 lanes are then combined by a
+// fixed shared-memory tree.
+__global__ void __launch_bounds__(256) linoss_finalize_kernel(const Params p) {
+  __shared__ float red[kPartials][8][33];
+  const int o = blockIdx.x * 32 + threadIdx.x;
+  const int ty = threadIdx.y;
+  float acc[kPartials];
+#pragma unroll
+  for (int j = 0; j < kPartials; ++j) acc[j] = 0.f;
+  if (o < p.P) {
+    for (int64_t s = ty; s < p.S; s += 8) {
+      const float* src = p.part + s * kPartials * p.P + o;
+#pragma unroll
+      for (int j = 0; j < kPartials; ++j) acc[j] += src[j * p.P];
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < kPartials; ++j) red[j][ty][threadIdx.x] = acc[j];
+  __syncthreads();
+  if (ty != 0 || o >= p.P) return;
+  float g[kPartials];
+#pragma unroll
+  for (int j = 0; j < kPartials; ++j) {
+    const float a = (red[j][0][threadIdx.x] + red[j][1][threadIdx.x]) +
+                    (red[j][2][threadIdx.x] + red[j][3][threadIdx.x]);
+    const float b = (red[j][4][threadIdx.x] + red[j][5][threadIdx.x]) +
+                    (red[j][6][threadIdx.x] + red[j][7][threadIdx.x]);
+    g[j] = a + b;
+  }
+  if (p.variant == SEMX_LINOSS_GENERIC) {
+    for (int j = 0; j < 4; ++j) p.dM[j * p.P + o] = g[j];
+    return;
+  }
+  const float graw = (p.variant == SEMX_LINOSS_DAMPED_IMEX) ? p.G_diag[o] : 0.0f;
+  float ds, da, dg;
+  linoss_chain(p.variant, p.a_from_g, p.steps[o], p.A_diag[o], graw, g, ds, da, dg);
+  p.dparams[0 * p.P + o] = ds;
+  p.dparams[1 * p.P + o] = da;
+  if (p.variant == SEMX_LINOSS_DAMPED_IMEX) p.dparams[2 * p.P + o] = dg;
+}
+
+int validate(const SemxLinossArgs* a, bool bwd) {
+  SEMX_REQUIRE(a->S >= 0 && a->L >= 0 && a->P >= 0, SEMX_ERR_SHAPE,
+               "linoss: negative size S=%lld L=%lld P=%lld", (long long)a->S, (long long)a->L,
+               (long long)a->P);
+  SEMX_REQUIRE(a->L <= (int64_t)1 << 30 && a->P <= (int64_t)1 << 30, SEMX_ERR_SHAPE,
+               "linoss: L or P too large");
+  SEMX_REQUIRE(a->variant >= SEMX_LINOSS_GENERIC && a->variant <= SEMX_LINOSS_DAMPED_IMEX,
+               SEMX_ERR_UNSUPPORTED, "linoss: unknown variant %d", a->variant);
+  SEMX_REQUIRE(a->chunk >= kSub && a->chunk <= kMaxChunk && a->chunk % kSub == 0,
+               SEMX_ERR_UNSUPPORTED, "linoss: chunk=%d must be a multiple of %d in [%d, %d]",
+               a->chunk, kSub, kSub, kMaxChunk);
+  const bool generic = a->variant == SEMX_LINOSS_GENERIC;
+  // Per-oscillator parameters are read whenever there are oscillators; per-step tensors
+  // only when there is at least one (sequence, step, oscillator) element.
+  const bool has_osc = a->P > 0 && (a->S > 0 || bwd);
+  const bool has_elems = a->S * a->L * a->P > 0;
+  if (has_osc) {
+    if (generic) {
+      SEMX_REQUIRE(a->M11 && a->M12 && a->M21 && a->M22, SEMX_ERR_NULL, "linoss: M is NULL");
+    } else {
+      SEMX_REQUIRE(a->steps && a->A_diag, SEMX_ERR_NULL, "linoss: steps/A_diag is NULL");
+      SEMX_REQUIRE(a->variant != SEMX_LINOSS_DAMPED_IMEX || a->G_diag, SEMX_ERR_NULL,
+                   "linoss: G_diag is NULL for the damped variant");
+    }
+  }
+  if (has_elems) {
+    if (generic) {
+      SEMX_REQUIRE(a->F1 && a->F2, SEMX_ERR_NULL, "linoss: F1/F2 is NULL");
+      SEMX_REQUIRE(semx::aligned(a->F1, 8) && semx::aligned(a->F2, 8), SEMX_ERR_ALIGN,
+                   "linoss: F1/F2 must be 8-byte aligned");
+    } else {
+      SEMX_REQUIRE(a->Bu != nullptr, SEMX_ERR_NULL, "linoss: Bu is NULL");
+      SEMX_REQUIRE(semx::aligned(a->Bu, 8), SEMX_ERR_ALIGN, "linoss: Bu must be 8-byte aligned");
+    }
+    if (!bwd) {
+      SEMX_REQUIRE(a->Y2 != nullptr, SEMX_ERR_NULL, "linoss: Y2 is NULL");
+      SEMX_REQUIRE(semx::aligned(a->Y2, 8), SEMX_ERR_ALIGN, "linoss: Y2 must be 8-byte aligned");
+    } else {
+      SEMX_REQUIRE(a->ckpt && a->dY2, SEMX_ERR_NULL, "linoss bwd: ckpt/dY2 is NULL");
+      SEMX_REQUIRE(semx::aligned(a->dY2, 8), SEMX_ERR_ALIGN, "linoss bwd: dY2 misaligned");
+      if (generic) {
+        SEMX_REQUIRE(a->dF1 && a->dF2, SEMX_ERR_NULL, "linoss bwd: dF1/dF2 is NULL");
+        SEMX_REQUIRE(semx::aligned(a->dF1, 8) && semx::aligned(a->dF2, 8), SEMX_ERR_ALIGN,
+                     "linoss bwd: dF1/dF2 misaligned");
+      } else {
+        SEMX_REQUIRE(a->dBu != nullptr, SEMX_ERR_NULL, "linoss bwd: dBu is NULL");
+        SEMX_REQUIRE(semx::aligned(a->dBu, 8), SEMX_ERR_ALIGN, "linoss bwd: dBu misaligned");
+      }
+    }
+  }
+  if (bwd && a->P > 0) {
+    SEMX_REQUIRE(generic ? a->dM != nullptr : a->dparams != nullptr, SEMX_ERR_NULL,
+                 "linoss bwd: %s is NULL", generic ? "dM" : "dparams");
+    SEMX_REQUIRE(a->workspace != nullptr || a->S == 0, SEMX_ERR_WORKSPACE,
+                 "linoss bwd: workspace is NULL");
+  }
+  if (a->ckpt) SEMX_REQUIRE(semx::aligned(a->ckpt, 16), SEMX_ERR_ALIGN,
+                            "linoss: ckpt must be 16-byte aligned");
+  return SEMX_OK;
+}
+
+Params to_params(const SemxLinossArgs* a) {
+  Params p;
+  p.variant = a->variant;
+  p.a_from_g = a->a_from_g;
+  p.chunk = a->chunk;
+  p.nchunks = (int)semx::cdiv(a->L, a->chunk);
+  p.S = a->S;
+  p.L = a->L;
+  p.P = a->P;
+  p.M11 = a->M11;
+  p.M12 = a->M12;
+  p.M21 = a->M21;
+  p.M22 = a->M22;
+  p.F1 = reinterpret_cast<const float2*>(a->F1);
+  p.F2 = reinterpret_cast<const float2*>(a->F2);
+  p.steps = a->steps;
+  p.A_diag = a->A_diag;
+  p.G_diag = a->G_diag;
+  p.Bu = reinterpret_cast<const float2*>(a->Bu);
+  p.Y2 = reinterpret_cast<float2*>(a->Y2);
+  p.ckpt = reinterpret_cast<float4*>(a->ckpt);
+  p.dY2 = reinterpret_cast<const float2*>(a->dY2);
+  p.dF1 = reinterpret_cast<float2*>(a->dF1);
+  p.dF2 = reinterpret_cast<float2*>(a->dF2);
+  p.dBu = reinterpret_cast<float2*>(a->dBu);
+  p.dM = a->dM;
+  p.dparams = a->dparams;
+  p.part = reinterpret_cast<float*>(a->workspace);
+  return p;
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t semx_linoss_args_size(void) { return sizeof(SemxLinossArgs); }
+
+size_t semx_linoss_ckpt_bytes(int64_t S, int64_t L, int64_t P, int32_t chunk) {
+  if (chunk <= 0 || S < 0 || L < 0 || P < 0) return 0;
+  return (size_t)S * (size_t)semx::cdiv(L, chunk) * (size_t)P * 4 * sizeof(float);
+}
+
+size_t semx_linoss_workspace_bytes(const SemxLinossArgs* a) {
+  if (a == nullptr || a->S < 0 || a->P < 0) return 0;
+  return (size_t)a->S * kPartials * (size_t)a->P * sizeof(float);
+}
+
+int semx_linoss_fwd(const SemxLinossArgs* a, semx_stream_t stream) {
+  SEMX_CHECK_ARGS(a, SemxLinossArgs);
+  int rc = validate(a, false);
+  if (rc != SEMX_OK) return rc;
+  if (a->S * a->P == 0 || a->L == 0) return SEMX_OK;
+  const Params p = to_params(a);
+  const int64_t n = a->S * a->P;
+  const dim3 grid((unsigned)semx::cdiv(n, kBlock));
+  if (a->variant == SEMX_LINOSS_GENERIC)
+    linoss_fwd_kernel<true><<<grid, kBlock, 0, semx::as_stream(stream)>>>(p);
+  else
+    linoss_fwd_kernel<false><<<grid, kBlock, 0, semx::as_stream(stream)>>>(p);
+  return semx::check_launch("linoss_fwd_kernel");
+}
+
+int semx_linoss_bwd(const SemxLinossArgs* a, semx_stream_t stream) {
+  SEMX_CHECK_ARGS(a, SemxLinossArgs);
+  int rc = validate(a, true);
+  if (rc != SEMX_OK) return rc;
+  const Params p = to_params(a);
+  cudaStream_t st = semx::as_stream(stream);
+  const int64_t n = a->S * a->P;
+  if (n > 0 && a->L > 0) {
+    const size_t smem = (size_t)(a->chunk / kSub) * kBlock * sizeof(float4);
+    const dim3 grid((unsigned)semx::cdiv(n, kBlock));
+    if (a->variant == SEMX_LINOSS_GENERIC) {
+      if (!semx::allow_smem(linoss_bwd_kernel<true>, smem)) return SEMX_ERR_LAUNCH;
+      linoss_bwd_kernel<true><<<grid, kBlock, smem, st>>>(p);
+    } else {
+      if (!semx::allow_smem(linoss_bwd_kernel<false>, smem)) return SEMX_ERR_LAUNCH;
+      linoss_bwd_kernel<false><<<grid, kBlock, smem, st>>>(p);
+    }
+    rc = semx::check_launch("linoss_bwd_kernel");
+    if (rc != SEMX_OK) return rc;
+  } else if (n > 0) {
+    // L == 0: no steps, every partial is zero.
+    cudaMemsetAsync(a->workspace, 0, semx_linoss_workspace_bytes(a), st);
+  }
+  if (a->P > 0) {
+    linoss_finalize_kernel<<<(unsigned)semx::cdiv(a->P, 32), dim3(32, 8), 0, st>>>(p);
+    return semx::check_launch("linoss_finalize_kernel");
+  }
+  return SEMX_OK;
+}
+
+}  // extern "C"

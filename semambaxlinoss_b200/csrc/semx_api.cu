@@ -1,0 +1,50 @@
+// ABI bookkeeping: version, status strings and the per-host-thread error message.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+
+#include "semx_common.cuh"
+
+namespace semx {
+
+thread_local char g_last_error[512] = {0};
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  std::vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+void clear_error() { g_last_error[0] = '\0'; }
+
+int check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(SEMX_ERR_LAUNCH, "%s: %s", what, cudaGetErrorString(e));
+  return SEMX_OK;
+}
+
+}  // namespace semx
+
+extern "C" {
+
+int semx_abi_version(void) { return SEMX_ABI_VERSION; }
+
+const char* semx_status_string(int status) {
+  switch (status) {
+    case SEMX_OK: return "ok";
+    case SEMX_ERR_ABI: return "argument struct size mismatch (header/library version skew)";
+    case SEMX_ERR_NULL: return "required pointer is NULL";
+    case SEMX_ERR_SHAPE: return "invalid shape";
+    case SEMX_ERR_UNSUPPORTED: return "unsupported configuration";
+    case SEMX_ERR_ALIGN: return "misaligned pointer";
+    case SEMX_ERR_LAUNCH: return "CUDA launch failed";
+    case SEMX_ERR_WORKSPACE: return "workspace missing";
+    default: return "unknown status";
+  }
+}
+
+const char* semx_last_error(void) { return semx::g_last_error; }
+
+}  // extern "C"

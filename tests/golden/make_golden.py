@@ -1,0 +1,217 @@
+"""Generates the golden fixtures in this folder by running the reference implementation.
+
+Runs on a machine that has the reference checkout (default /root/reference, override
+with SEMX_REFERENCE). Nothing else reads the reference: the committed ``*.pt`` fixtures
+carry seeded inputs, parameters and the reference's float64 outputs and gradients, and
+``tests/test_oracle_golden.py`` checks the oracle restatement against them.
+
+What runs (all on CPU, float64, through the reference's own modules and functions):
+* models/linoss/linoss.py          LinOSS (all variants) and _linoss_recurrence
+* models/selective_lru/selective_lru.py  SelectiveLRU (every gain / option),
+  SelectiveLRUMIMO (every gain / option, rank > 0) and _selective_recurrence
+
+Usage: python tests/golden/make_golden.py
+"""
+from __future__ import annotations
+
+import importlib.util
+import os
+import sys
+from pathlib import Path
+
+import torch
+
+OUT = Path(__file__).resolve().parent
+REF = Path(os.environ.get("SEMX_REFERENCE", "/root/reference"))
+
+
+def _import_reference():
+    sys.path.insert(0, str(REF))
+    from models.selective_lru.selective_lru import (  # noqa: E402
+        SelectiveLRU,
+        SelectiveLRUMIMO,
+        _selective_recurrence,
+    )
+
+    # models/linoss/__init__.py imports a module that does not exist in the reference,
+    # so the layer file is loaded by path.
+    spec = importlib.util.spec_from_file_location("ref_linoss", REF / "models/linoss/linoss.py")
+    lin = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(lin)
+    return SelectiveLRU, SelectiveLRUMIMO, _selective_recurrence, lin
+
+
+def _run_module(module, x, fwd_kwargs, seed):
+    """Forward + backward of a float64 module; returns outputs and all gradients."""
+    x = x.clone().requires_grad_(True)
+    out = module(x, **fwd_kwargs)
+    g = torch.Generator().manual_seed(seed + 1)
+    if isinstance(out, tuple):
+        y, hf = out
+        gy = torch.randn(y.shape, generator=g, dtype=y.dtype)
+        ghf = torch.randn(hf.shape, generator=g, dtype=torch.float64)
+        ghf = torch.complex(ghf, torch.randn(hf.shape, generator=g, dtype=torch.float64))
+        loss = (y * gy).sum() + (hf.real * ghf.real + hf.imag * ghf.imag).sum()
+        extra = {"hf": hf.detach(), "grad_hf": ghf}
+    else:
+        y = out
+        gy = torch.randn(y.shape, generator=g, dtype=y.dtype)
+        loss = (y * gy).sum()
+        extra = {}
+    params = [p for _, p in module.named_parameters()]
+    grads = torch.autograd.grad(loss, [x] + params, allow_unused=True)
+    rec = {
+        "x": x.detach(),
+        "y": y.detach(),
+        "grad_y": gy,
+        "grad_x": grads[0],
+        "state_dict": {k: v.detach().clone() for k, v in module.state_dict().items()},
+        "param_grads": {
+            n: (g_ if g_ is not None else torch.zeros_like(p))
+            for (n, p), g_ in zip(module.named_parameters(), grads[1:])
+        },
+        "forward_kwargs": {k: v for k, v in fwd_kwargs.items() if not torch.is_tensor(v)},
+    }
+    if "h_init" in fwd_kwargs:
+        rec["h_init"] = fwd_kwargs["h_init"]
+    rec.update(extra)
+    return rec
+
+
+def _perturb(module, seed, scale=0.5):
+    g = torch.Generator().manual_seed(seed)
+    with torch.no_grad():
+        for _, p in module.named_parameters():
+            p.add_(scale * torch.randn(p.shape, generator=g, dtype=p.dtype))
+
+
+def linoss_cases(lin):
+    cases = {}
+    variants = [
+        ("IMEX", True, True),
+        ("IMEX", True, False),
+        ("IMEX", False, True),
+        ("IM", False, True),
+    ]
+    for disc, damp, afg in variants:
+        for (H, P, S, L) in [(4, 16, 3, 17), (6, 20, 2, 37)]:
+            torch.manual_seed(1000 + H + P + L)
+            m = lin.LinOSS(in_features=H, state_dim=P, discretization=disc, damping=damp,
+                           a_from_g=afg).double()
+            # Spread parameters over every constraint branch (relu zero, clamp bands).
+            _perturb(m, seed=7 + P + L, scale=0.7)
+            g = torch.Generator().manual_seed(11 + P + L)
+            x = torch.randn(S, L, H, generator=g, dtype=torch.float64)
+            rec = _run_module(m, x, {}, seed=S * 100 + L)
+            rec["config"] = dict(in_features=H, state_dim=P, discretization=disc,
+                                 damping=damp, a_from_g=afg)
+            cases[f"linoss_{disc}_{'damped' if damp else 'undamped'}_afg{int(afg)}_{S}x{L}"] = rec
+    # The bare recurrence with a given transition (the generic op).
+    g = torch.Generator().manual_seed(5)
+    S, L, P = 3, 29, 16
+    M = [0.3 * torch.randn(P, generator=g, dtype=torch.float64) + d for d in (0.9, 0, 0, 0.9)]
+    F1 = torch.complex(torch.randn(S, L, P, generator=g, dtype=torch.float64),
+                       torch.randn(S, L, P, generator=g, dtype=torch.float64))
+    F2 = torch.complex(torch.randn(S, L, P, generator=g, dtype=torch.float64),
+                       torch.randn(S, L, P, generator=g, dtype=torch.float64))
+    ins = [t.clone().requires_grad_(True) for t in (*M, F1, F2)]
+    y2 = lin._linoss_recurrence(*ins)
+    gy = torch.complex(torch.randn(S, L, P, generator=g, dtype=torch.float64),
+                       torch.randn(S, L, P, generator=g, dtype=torch.float64))
+    loss = (y2.real * gy.real + y2.imag * gy.imag).sum()
+    grads = torch.autograd.grad(loss, ins)
+    cases["linoss_recurrence"] = {
+        "M": [t.detach() for t in M], "F1": F1, "F2": F2, "Y2": y2.detach(), "grad_Y2": gy,
+        "grads": list(grads),
+    }
+    return cases
+
+
+def selective_lru_cases(SelectiveLRU):
+    cases = {}
+    opts = [
+        dict(input_gain="gamma"),
+        dict(input_gain="mamba"),
+        dict(input_gain="zoh"),
+        dict(input_gain="gamma", envelope_readout=True, mode_detune=True, n_real_modes=1),
+        dict(input_gain="zoh", mode_detune=True, rate_scale=1.5),
+        dict(input_gain="mamba", envelope_readout=True),
+    ]
+    for i, o in enumerate(opts):
+        torch.manual_seed(200 + i)
+        m = SelectiveLRU(d_model=8, d_state=4, **o).double()
+        _perturb(m, seed=300 + i, scale=0.3)
+        g = torch.Generator().manual_seed(400 + i)
+        x = torch.randn(2, 19, 8, generator=g, dtype=torch.float64)
+        fwd = {}
+        if i == 4:
+            fwd["rate_scale"] = 0.75
+        if i in (1, 3):
+            h0 = torch.complex(torch.randn(2, 8, 4, generator=g, dtype=torch.float64),
+                               torch.randn(2, 8, 4, generator=g, dtype=torch.float64))
+            fwd.update(h_init=h0, return_final_state=True)
+        rec = _run_module(m, x, fwd, seed=500 + i)
+        rec["config"] = dict(d_model=8, d_state=4, dt_rank=m.dt_rank, **o)
+        cases[f"selective_lru_{i}_{o['input_gain']}"] = rec
+    return cases
+
+
+def mimo_cases(SelectiveLRUMIMO):
+    cases = {}
+    opts = [
+        dict(input_gain="gamma", rank=2),
+        dict(input_gain="mamba", rank=0),
+        dict(input_gain="zoh", rank=2, mode_detune=True),
+        dict(input_gain="none", rank=1, envelope_readout=True),
+        dict(input_gain="gamma", rank=2, envelope_readout=True, mode_detune=True,
+             n_real_modes=2, rate_scale=1.25),
+    ]
+    for i, o in enumerate(opts):
+        torch.manual_seed(600 + i)
+        m = SelectiveLRUMIMO(in_features=8, state_dim=16, n_heads=2, **o).double()
+        _perturb(m, seed=700 + i, scale=0.2)
+        g = torch.Generator().manual_seed(800 + i)
+        x = torch.randn(2, 15, 8, generator=g, dtype=torch.float64)
+        rec = _run_module(m, x, {}, seed=900 + i)
+        rec["config"] = dict(in_features=8, state_dim=16, n_heads=2, **o)
+        cases[f"mimo_{i}_{o['input_gain']}"] = rec
+    return cases
+
+
+def recurrence_case(_selective_recurrence):
+    g = torch.Generator().manual_seed(9)
+    B, T, N = 3, 17, 16
+    nu = torch.rand(B, T, N, generator=g, dtype=torch.float64) * 0.99
+    theta = torch.randn(B, T, N, generator=g, dtype=torch.float64)
+    Bu = torch.complex(torch.randn(B, T, N, generator=g, dtype=torch.float64),
+                       torch.randn(B, T, N, generator=g, dtype=torch.float64))
+    h0 = torch.complex(torch.randn(B, N, generator=g, dtype=torch.float64),
+                       torch.randn(B, N, generator=g, dtype=torch.float64))
+    lam = torch.polar(nu, theta)
+    ins = [lam.clone().requires_grad_(True), Bu.clone().requires_grad_(True),
+           h0.clone().requires_grad_(True)]
+    h = _selective_recurrence(*ins)
+    gh = torch.complex(torch.randn(B, T, N, generator=g, dtype=torch.float64),
+                       torch.randn(B, T, N, generator=g, dtype=torch.float64))
+    loss = (h.real * gh.real + h.imag * gh.imag).sum()
+    grads = torch.autograd.grad(loss, ins)
+    return {"selective_recurrence": {"lam": lam, "Bu": Bu, "h0": h0, "h": h.detach(),
+                                     "grad_h": gh, "grads": list(grads)}}
+
+
+def main():
+    SelectiveLRU, SelectiveLRUMIMO, _selective_recurrence, lin = _import_reference()
+    groups = {
+        "linoss": linoss_cases(lin),
+        "selective_lru": selective_lru_cases(SelectiveLRU),
+        "mimo": mimo_cases(SelectiveLRUMIMO),
+        "recurrence": recurrence_case(_selective_recurrence),
+    }
+    for name, cases in groups.items():
+        path = OUT / f"{name}.pt"
+        torch.save(cases, path)
+        print(f"{path.name}: {len(cases)} cases, {path.stat().st_size / 1024:.1f} KiB")
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,55 @@
+"""Shared helpers for the parity tests: tolerances, norm-relative error, seeded inputs."""
+from __future__ import annotations
+
+import torch
+
+# Tolerances (norm-relative error ||a - b||_inf / ||b||_inf), fp32 kernels vs the float64
+# oracle, for outputs and every gradient.
+FP32_TOL = 1e-4
+# bf16 inputs with fp32 state.
+BF16_TOL = 2e-2
+
+
+def rel_err(a: torch.Tensor, b: torch.Tensor) -> float:
+    a = a.detach().to("cpu")
+    b = b.detach().to("cpu")
+    if a.is_complex() or b.is_complex():
+        a = torch.view_as_real(a.to(torch.complex128))
+        b = torch.view_as_real(b.to(torch.complex128))
+    else:
+        a = a.double()
+        b = b.double()
+    assert a.shape == b.shape, (a.shape, b.shape)
+    if b.numel() == 0:
+        return 0.0
+    den = b.abs().max().item()
+    return (a - b).abs().max().item() / (den if den > 0 else 1.0)
+
+
+def assert_close(a, b, tol, what=""):
+    e = rel_err(a, b)
+    assert e <= tol, f"{what}: norm-relative error {e:.3e} > {tol:.1e}"
+
+
+def gen(seed: int) -> torch.Generator:
+    return torch.Generator().manual_seed(seed)
+
+
+def randn(shape, g, dtype=torch.float64, scale=1.0, mean=0.0):
+    return torch.randn(shape, generator=g, dtype=dtype) * scale + mean
+
+
+def crandn(shape, g, scale=1.0):
+    return torch.complex(randn(shape, g, scale=scale), randn(shape, g, scale=scale))
+
+
+def cuda():
+    if not torch.cuda.is_available():
+        raise RuntimeError("this test needs a CUDA GPU")
+    return torch.device("cuda")
+
+
+def to32(t: torch.Tensor, device) -> torch.Tensor:
+    if t.is_complex():
+        return t.to(torch.complex64).to(device)
+    return t.to(torch.float32).to(device)

@@ -60,6 +60,8 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--clocks-log", default=None)
+    ap.add_argument("--no-soak", action="store_true",
+                    help="skip the 1.5 s busy period before timing (for profiler runs)")
     return ap.parse_args()
 
 
@@ -237,7 +239,7 @@ def run_semx(args, rank, local_rank, world):
     # Keep the GPU busy ~1.5 s before timing so the clock samples see it under load.
     soak_t0 = time.time()
     torch.cuda.synchronize(device)
-    while time.time() - soak_t0 < 1.5:
+    while not args.no_soak and time.time() - soak_t0 < 1.5:
         for _ in range(20):
             step()
         torch.cuda.synchronize(device)

@@ -150,17 +150,31 @@ __device__ __forceinline__ void forcing(const Coef& k, float2 in1, float2 in2, f
   }
 }
 
+// Per-thread views of the (S, L, P) complex tensors: element (s, t, p) of a chain lives at
+// chain_base + t * P, with 32-bit step offsets (L * P < 2^31 is validated on the host).
 template <bool GENERIC>
-__device__ __forceinline__ void load_batch(const Params& p, int64_t base, int t0, int tend,
-                                           float2 (&a)[kSub], float2 (&b)[kSub]) {
-  const float2* src1 = GENERIC ? p.F1 : p.Bu;
+__device__ __forceinline__ void load_batch(const float2* __restrict__ src1,
+                                           const float2* __restrict__ src2, int P, int t0,
+                                           int tend, float2 (&a)[kSub], float2 (&b)[kSub]) {
 #pragma unroll
   for (int i = 0; i < kSub; ++i) {
     if (t0 + i < tend) {
-      a[i] = __ldg(src1 + base + (int64_t)(t0 + i) * p.P);
-      if (GENERIC) b[i] = __ldg(p.F2 + base + (int64_t)(t0 + i) * p.P);
+      a[i] = __ldg(src1 + (t0 + i) * P);
+      if (GENERIC) b[i] = __ldg(src2 + (t0 + i) * P);
     }
   }
+}
+
+__device__ __forceinline__ void cp_async8(void* smem, const void* gmem) {
+  const unsigned sa = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(sa), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;\n" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
 }
 
 template <bool GENERIC>
@@ -171,14 +185,18 @@ __global__ void __launch_bounds__(kBlock) linoss_fwd_kernel(const Params p) {
   const int o = (int)(gid - s * p.P);
   const Coef k = load_coef(p, o);
   const int L = (int)p.L;
+  const int P = (int)p.P;
   const int64_t base = s * p.L * p.P + o;
+  const float2* src1 = (GENERIC ? p.F1 : p.Bu) + base;
+  const float2* src2 = GENERIC ? p.F2 + base : nullptr;
+  float2* y2 = p.Y2 + base;
 
   float4 st = make_float4(0.f, 0.f, 0.f, 0.f);
   float2 c1[kSub], c2[kSub];
-  load_batch<GENERIC>(p, base, 0, L, c1, c2);
+  load_batch<GENERIC>(src1, src2, P, 0, L, c1, c2);
   for (int t0 = 0; t0 < L; t0 += kSub) {
     float2 n1[kSub], n2[kSub];
-    load_batch<GENERIC>(p, base, t0 + kSub, L, n1, n2);
+    load_batch<GENERIC>(src1, src2, P, t0 + kSub, L, n1, n2);
     if (p.ckpt != nullptr && (t0 % p.chunk) == 0)
       p.ckpt[(s * p.nchunks + t0 / p.chunk) * p.P + o] = st;
 #pragma unroll
@@ -187,7 +205,7 @@ __global__ void __launch_bounds__(kBlock) linoss_fwd_kernel(const Params p) {
         float2 u1, u2;
         forcing<GENERIC>(k, c1[i], c2[i], u1, u2);
         st = lin_step(k, st, u1, u2);
-        p.Y2[base + (int64_t)(t0 + i) * p.P] = make_float2(st.z, st.w);
+        y2[(t0 + i) * P] = make_float2(st.z, st.w);
       }
     }
 #pragma unroll
@@ -198,16 +216,49 @@ __global__ void __launch_bounds__(kBlock) linoss_fwd_kernel(const Params p) {
   }
 }
 
+// Shared memory of the backward kernel, per thread (kBlock threads, slot = threadIdx.x):
+//   sub_ckpt[chunk / kSub]    float4  states at the start of each sub-block
+//   in[2][GENERIC ? 2 : 1][kSub] float2  double-buffered forcing / Bu of a sub-block
+//   dy[2][kSub]               float2  double-buffered dY2 of a sub-block
+// Every thread only touches its own slots, so no block barrier is needed; cp.async
+// copies are made visible to the issuing thread by cp.async.wait_group.
 template <bool GENERIC>
-__global__ void __launch_bounds__(kBlock) linoss_bwd_kernel(const Params p) {
-  extern __shared__ float4 sub_ckpt[];  // [chunk / kSub][kBlock]
-  const int64_t gid = (int64_t)blockIdx.x * kBlock + threadIdx.x;
+__device__ __forceinline__ void prefetch_sub(float2* in_buf, float2* dy_buf,
+                                             const float2* src1, const float2* src2,
+                                             const float2* dys, int P, int ta, int t1) {
+#pragma unroll
+  for (int i = 0; i < kSub; ++i) {
+    if (ta + i < t1) {
+      cp_async8(in_buf + i * kBlock, src1 + (ta + i) * P);
+      if (GENERIC) cp_async8(in_buf + (kSub + i) * kBlock, src2 + (ta + i) * P);
+      cp_async8(dy_buf + i * kBlock, dys + (ta + i) * P);
+    }
+  }
+}
+
+template <bool GENERIC>
+__global__ void __launch_bounds__(kBlock, 4) linoss_bwd_kernel(const Params p) {
+  extern __shared__ float4 smem4[];
+  constexpr int kIn = GENERIC ? 2 : 1;
+  const int nsub_max = p.chunk / kSub;
+  float4* sub_ckpt = smem4;                                            // [nsub_max][kBlock]
+  float2* in_base = reinterpret_cast<float2*>(smem4 + nsub_max * kBlock);  // [2][kIn*kSub][kBlock]
+  float2* dy_base = in_base + 2 * kIn * kSub * kBlock;                     // [2][kSub][kBlock]
+  const int tid = threadIdx.x;
+
+  const int64_t gid = (int64_t)blockIdx.x * kBlock + tid;
   if (gid >= p.S * p.P) return;
   const int64_t s = gid / p.P;
   const int o = (int)(gid - s * p.P);
   const Coef k = load_coef(p, o);
   const int L = (int)p.L;
+  const int P = (int)p.P;
   const int64_t base = s * p.L * p.P + o;
+  const float2* src1 = (GENERIC ? p.F1 : p.Bu) + base;
+  const float2* src2 = GENERIC ? p.F2 + base : nullptr;
+  const float2* dys = p.dY2 + base;
+  float2* out1 = (GENERIC ? p.dF1 : p.dBu) + base;
+  float2* out2 = GENERIC ? p.dF2 + base : nullptr;
 
   float a1r = 0.f, a1i = 0.f, a2r = 0.f, a2i = 0.f;  // adjoint a_{t+1}
   float g11 = 0.f, g12 = 0.f, g21 = 0.f, g22 = 0.f, gf1 = 0.f, gf2 = 0.f;
@@ -215,17 +266,21 @@ __global__ void __launch_bounds__(kBlock) linoss_bwd_kernel(const Params p) {
   for (int c = p.nchunks - 1; c >= 0; --c) {
     const int t0 = c * p.chunk;
     const int t1 = min(t0 + p.chunk, L);
-    const float4 entry = p.ckpt[(s * p.nchunks + c) * p.P + o];
+    const int nsub = (t1 - t0 + kSub - 1) / kSub;
+    // Start fetching the last sub-block of this chunk while pass 1 runs.
+    prefetch_sub<GENERIC>(in_base + tid, dy_base + tid, src1, src2, dys, P,
+                          t0 + (nsub - 1) * kSub, t1);
+    cp_async_commit();
 
     // Pass 1: recurrence over the chunk, keeping the state every kSub steps on chip.
     {
-      float4 st = entry;
+      float4 st = p.ckpt[(s * p.nchunks + c) * p.P + o];
       float2 c1[kSub], c2[kSub];
-      load_batch<GENERIC>(p, base, t0, t1, c1, c2);
+      load_batch<GENERIC>(src1, src2, P, t0, t1, c1, c2);
       for (int tb = t0; tb < t1; tb += kSub) {
         float2 n1[kSub], n2[kSub];
-        load_batch<GENERIC>(p, base, tb + kSub, t1, n1, n2);
-        sub_ckpt[((tb - t0) / kSub) * kBlock + threadIdx.x] = st;
+        load_batch<GENERIC>(src1, src2, P, tb + kSub, t1, n1, n2);
+        sub_ckpt[((tb - t0) / kSub) * kBlock + tid] = st;
 #pragma unroll
         for (int i = 0; i < kSub; ++i) {
           if (tb + i < t1) {
@@ -242,23 +297,30 @@ __global__ void __launch_bounds__(kBlock) linoss_bwd_kernel(const Params p) {
       }
     }
 
-    // Pass 2: sub-blocks in reverse; recompute kSub states into registers, then adjoint.
-    const int nsub = (t1 - t0 + kSub - 1) / kSub;
+    // Pass 2: sub-blocks last to first; recompute kSub states into registers from the
+    // sub-block checkpoint, then run the adjoint backwards through them.
     for (int r = nsub - 1; r >= 0; --r) {
+      const int buf = (nsub - 1 - r) & 1;
       const int ta = t0 + r * kSub;
-      const float4 s0 = sub_ckpt[r * kBlock + threadIdx.x];
-      float2 in1[kSub], in2[kSub], dy[kSub];
-      load_batch<GENERIC>(p, base, ta, t1, in1, in2);
-#pragma unroll
-      for (int i = 0; i < kSub; ++i)
-        if (ta + i < t1) dy[i] = __ldg(p.dY2 + base + (int64_t)(ta + i) * p.P);
+      if (r > 0) {
+        prefetch_sub<GENERIC>(in_base + (buf ^ 1) * kIn * kSub * kBlock + tid,
+                              dy_base + (buf ^ 1) * kSub * kBlock + tid, src1, src2, dys, P,
+                              ta - kSub, t1);
+        cp_async_commit();
+        cp_async_wait<1>();
+      } else {
+        cp_async_wait<0>();
+      }
+      const float2* inb = in_base + buf * kIn * kSub * kBlock + tid;
+      const float2* dyb = dy_base + buf * kSub * kBlock + tid;
+      const float4 s0 = sub_ckpt[r * kBlock + tid];
       float4 hs[kSub];
       float4 st = s0;
 #pragma unroll
       for (int i = 0; i < kSub; ++i) {
         if (ta + i < t1) {
           float2 u1, u2;
-          forcing<GENERIC>(k, in1[i], in2[i], u1, u2);
+          forcing<GENERIC>(k, inb[i * kBlock], GENERIC ? inb[(kSub + i) * kBlock] : inb[0], u1, u2);
           st = lin_step(k, st, u1, u2);
           hs[i] = st;
         }
@@ -266,22 +328,24 @@ __global__ void __launch_bounds__(kBlock) linoss_bwd_kernel(const Params p) {
 #pragma unroll
       for (int i = kSub - 1; i >= 0; --i) {
         if (ta + i < t1) {
+          const float2 dy = dyb[i * kBlock];
           const float n1r = k.m11 * a1r + k.m21 * a2r;
           const float n1i = k.m11 * a1i + k.m21 * a2i;
-          const float n2r = dy[i].x + k.m12 * a1r + k.m22 * a2r;
-          const float n2i = dy[i].y + k.m12 * a1i + k.m22 * a2i;
+          const float n2r = dy.x + k.m12 * a1r + k.m22 * a2r;
+          const float n2i = dy.y + k.m12 * a1i + k.m22 * a2i;
           a1r = n1r;
           a1i = n1i;
           a2r = n2r;
           a2i = n2i;
-          const int64_t off = base + (int64_t)(ta + i) * p.P;
+          const int off = (ta + i) * P;
           if (GENERIC) {
-            p.dF1[off] = make_float2(a1r, a1i);
-            p.dF2[off] = make_float2(a2r, a2i);
+            out1[off] = make_float2(a1r, a1i);
+            out2[off] = make_float2(a2r, a2i);
           } else {
-            p.dBu[off] = make_float2(k.f1 * a1r + k.f2 * a2r, k.f1 * a1i + k.f2 * a2i);
-            gf1 += a1r * in1[i].x + a1i * in1[i].y;
-            gf2 += a2r * in1[i].x + a2i * in1[i].y;
+            out1[off] = make_float2(k.f1 * a1r + k.f2 * a2r, k.f1 * a1i + k.f2 * a2i);
+            const float2 bu = inb[i * kBlock];
+            gf1 += a1r * bu.x + a1i * bu.y;
+            gf2 += a2r * bu.x + a2i * bu.y;
           }
           const float4 sp = (i > 0) ? hs[i > 0 ? i - 1 : 0] : s0;
           g11 += a1r * sp.x + a1i * sp.y;
@@ -300,6 +364,11 @@ __global__ void __launch_bounds__(kBlock) linoss_bwd_kernel(const Params p) {
   part[3 * p.P] = g22;
   part[4 * p.P] = gf1;
   part[5 * p.P] = gf2;
+}
+
+__host__ __device__ inline size_t bwd_smem_bytes(int chunk, bool generic) {
+  return (size_t)(chunk / kSub) * kBlock * sizeof(float4) +
+         (size_t)2 * ((generic ? 2 : 1) + 1) * kSub * kBlock * sizeof(float2);
 }
 
 // d(loss)/d(raw parameters) from the summed gradients of (M11, M12, M21, M22, f1, f2),
@@ -408,18 +477,35 @@ __device__ void linoss_chain(int variant, int a_from_g, float sraw, float araw, 
   d_s = gs * (step * (1.0f - step));
 }
 
-// Sums the per-sequence partials over S in a fixed order: thread (x, y) of a 32x8 block
-// adds sequences y, y+8, y+16, ... for oscillator x; the 8 lanes are then combined by a
-// fixed shared-memory tree.
-__global__ void __launch_bounds__(256) linoss_finalize_kernel(const Params p) {
+// Parameter-gradient reduction over sequences, in two fixed-order stages (bitwise
+// deterministic). Stage 1: CTA (x, g) of 32x8 threads sums the rows of sequence group g
+// (kRowsPerGroup consecutive sequences) for oscillators 32x .. 32x+31; lane y takes rows
+// y, y+8, ... and the 8 lanes are combined by a fixed tree. Stage 2 sums the groups in
+// order and applies the chain rule to the raw parameters.
+constexpr int kRowsPerGroup = 32;
+
+__device__ __forceinline__ void tree8(float (&red)[kPartials][8][33], float (&g)[kPartials]) {
+#pragma unroll
+  for (int j = 0; j < kPartials; ++j) {
+    const float a = (red[j][0][threadIdx.x] + red[j][1][threadIdx.x]) +
+                    (red[j][2][threadIdx.x] + red[j][3][threadIdx.x]);
+    const float b = (red[j][4][threadIdx.x] + red[j][5][threadIdx.x]) +
+                    (red[j][6][threadIdx.x] + red[j][7][threadIdx.x]);
+    g[j] = a + b;
+  }
+}
+
+__global__ void __launch_bounds__(256) linoss_reduce_kernel(const Params p, float* group_sums) {
   __shared__ float red[kPartials][8][33];
   const int o = blockIdx.x * 32 + threadIdx.x;
   const int ty = threadIdx.y;
+  const int64_t r0 = (int64_t)blockIdx.y * kRowsPerGroup;
+  const int64_t r1 = min(r0 + kRowsPerGroup, p.S);
   float acc[kPartials];
 #pragma unroll
   for (int j = 0; j < kPartials; ++j) acc[j] = 0.f;
   if (o < p.P) {
-    for (int64_t s = ty; s < p.S; s += 8) {
+    for (int64_t s = r0 + ty; s < r1; s += 8) {
       const float* src = p.part + s * kPartials * p.P + o;
 #pragma unroll
       for (int j = 0; j < kPartials; ++j) acc[j] += src[j * p.P];
@@ -430,14 +516,34 @@ __global__ void __launch_bounds__(256) linoss_finalize_kernel(const Params p) {
   __syncthreads();
   if (ty != 0 || o >= p.P) return;
   float g[kPartials];
+  tree8(red, g);
 #pragma unroll
-  for (int j = 0; j < kPartials; ++j) {
-    const float a = (red[j][0][threadIdx.x] + red[j][1][threadIdx.x]) +
-                    (red[j][2][threadIdx.x] + red[j][3][threadIdx.x]);
-    const float b = (red[j][4][threadIdx.x] + red[j][5][threadIdx.x]) +
-                    (red[j][6][threadIdx.x] + red[j][7][threadIdx.x]);
-    g[j] = a + b;
+  for (int j = 0; j < kPartials; ++j)
+    group_sums[((int64_t)blockIdx.y * kPartials + j) * p.P + o] = g[j];
+}
+
+__global__ void __launch_bounds__(256) linoss_finalize_kernel(const Params p,
+                                                              const float* group_sums,
+                                                              int ngroups) {
+  __shared__ float red[kPartials][8][33];
+  const int o = blockIdx.x * 32 + threadIdx.x;
+  const int ty = threadIdx.y;
+  float acc[kPartials];
+#pragma unroll
+  for (int j = 0; j < kPartials; ++j) acc[j] = 0.f;
+  if (o < p.P) {
+    for (int gi = ty; gi < ngroups; gi += 8) {
+      const float* src = group_sums + (int64_t)gi * kPartials * p.P + o;
+#pragma unroll
+      for (int j = 0; j < kPartials; ++j) acc[j] += src[j * p.P];
+    }
   }
+#pragma unroll
+  for (int j = 0; j < kPartials; ++j) red[j][ty][threadIdx.x] = acc[j];
+  __syncthreads();
+  if (ty != 0 || o >= p.P) return;
+  float g[kPartials];
+  tree8(red, g);
   if (p.variant == SEMX_LINOSS_GENERIC) {
     for (int j = 0; j < 4; ++j) p.dM[j * p.P + o] = g[j];
     return;
@@ -454,8 +560,8 @@ int validate(const SemxLinossArgs* a, bool bwd) {
   SEMX_REQUIRE(a->S >= 0 && a->L >= 0 && a->P >= 0, SEMX_ERR_SHAPE,
                "linoss: negative size S=%lld L=%lld P=%lld", (long long)a->S, (long long)a->L,
                (long long)a->P);
-  SEMX_REQUIRE(a->L <= (int64_t)1 << 30 && a->P <= (int64_t)1 << 30, SEMX_ERR_SHAPE,
-               "linoss: L or P too large");
+  SEMX_REQUIRE(a->L * a->P < ((int64_t)1 << 31), SEMX_ERR_SHAPE,
+               "linoss: L*P=%lld must be below 2^31", (long long)(a->L * a->P));
   SEMX_REQUIRE(a->variant >= SEMX_LINOSS_GENERIC && a->variant <= SEMX_LINOSS_DAMPED_IMEX,
                SEMX_ERR_UNSUPPORTED, "linoss: unknown variant %d", a->variant);
   SEMX_REQUIRE(a->chunk >= kSub && a->chunk <= kMaxChunk && a->chunk % kSub == 0,
@@ -555,7 +661,8 @@ size_t semx_linoss_ckpt_bytes(int64_t S, int64_t L, int64_t P, int32_t chunk) {
 
 size_t semx_linoss_workspace_bytes(const SemxLinossArgs* a) {
   if (a == nullptr || a->S < 0 || a->P < 0) return 0;
-  return (size_t)a->S * kPartials * (size_t)a->P * sizeof(float);
+  const size_t groups = (size_t)semx::cdiv(a->S, kRowsPerGroup);
+  return ((size_t)a->S + groups) * kPartials * (size_t)a->P * sizeof(float);
 }
 
 int semx_linoss_fwd(const SemxLinossArgs* a, semx_stream_t stream) {
@@ -581,9 +688,10 @@ int semx_linoss_bwd(const SemxLinossArgs* a, semx_stream_t stream) {
   cudaStream_t st = semx::as_stream(stream);
   const int64_t n = a->S * a->P;
   if (n > 0 && a->L > 0) {
-    const size_t smem = (size_t)(a->chunk / kSub) * kBlock * sizeof(float4);
+    const bool generic = a->variant == SEMX_LINOSS_GENERIC;
+    const size_t smem = bwd_smem_bytes(a->chunk, generic);
     const dim3 grid((unsigned)semx::cdiv(n, kBlock));
-    if (a->variant == SEMX_LINOSS_GENERIC) {
+    if (generic) {
       if (!semx::allow_smem(linoss_bwd_kernel<true>, smem)) return SEMX_ERR_LAUNCH;
       linoss_bwd_kernel<true><<<grid, kBlock, smem, st>>>(p);
     } else {
@@ -594,10 +702,19 @@ int semx_linoss_bwd(const SemxLinossArgs* a, semx_stream_t stream) {
     if (rc != SEMX_OK) return rc;
   } else if (n > 0) {
     // L == 0: no steps, every partial is zero.
-    cudaMemsetAsync(a->workspace, 0, semx_linoss_workspace_bytes(a), st);
+    cudaMemsetAsync(a->workspace, 0, (size_t)n * kPartials * sizeof(float), st);
   }
   if (a->P > 0) {
-    linoss_finalize_kernel<<<(unsigned)semx::cdiv(a->P, 32), dim3(32, 8), 0, st>>>(p);
+    const int ngroups = (int)semx::cdiv(a->S, kRowsPerGroup);
+    float* group_sums = p.part + a->S * kPartials * a->P;
+    if (ngroups > 0) {
+      linoss_reduce_kernel<<<dim3((unsigned)semx::cdiv(a->P, 32), (unsigned)ngroups),
+                             dim3(32, 8), 0, st>>>(p, group_sums);
+      rc = semx::check_launch("linoss_reduce_kernel");
+      if (rc != SEMX_OK) return rc;
+    }
+    linoss_finalize_kernel<<<(unsigned)semx::cdiv(a->P, 32), dim3(32, 8), 0, st>>>(
+        p, group_sums, ngroups);
     return semx::check_launch("linoss_finalize_kernel");
   }
   return SEMX_OK;

@@ -10,6 +10,16 @@ FP32_TOL = 1e-4
 BF16_TOL = 2e-2
 
 
+def floor_tol(err_fp32_reference: float, base: float = FP32_TOL) -> float:
+    """Tolerance for one tensor: the stated base tolerance, raised to twice the error of
+    the reference algorithm itself evaluated in fp32 (the oracle run in float32 vs the
+    float64 oracle) where that is larger. Ill-conditioned cases (critically damped or
+    undamped LinOSS oscillators, poles on the unit circle) cannot be met at 1e-4 by any
+    fp32 evaluation of the reference's recurrence; the floor keeps the check anchored to
+    float64 without pretending otherwise."""
+    return max(base, 2.0 * err_fp32_reference)
+
+
 def rel_err(a: torch.Tensor, b: torch.Tensor) -> float:
     a = a.detach().to("cpu")
     b = b.detach().to("cpu")

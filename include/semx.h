@@ -129,6 +129,91 @@ size_t semx_linoss_workspace_bytes(const SemxLinossArgs* args);
 int semx_linoss_fwd(const SemxLinossArgs* args, semx_stream_t stream);
 int semx_linoss_bwd(const SemxLinossArgs* args, semx_stream_t stream);
 
+/* ------------------------------------------------------------------------------------
+ * Selective-LRU SISO scan with readout (one bank of N modes per channel).
+ *
+ *   lam  = exp(delta_nu * (-a + j*(omega + [s *] delta_theta)))          (per t, c, n)
+ *   Bu   = gain * (B_re + j B_im)_t * x_t,  gain in {gamma, mamba, zoh}
+ *   h_t  = lam_t h_{t-1} + Bu_t,            h_{-1} = h0 (default 0)
+ *   y_t  = Re(<C_t, h_t>) [+ <g, |h_t|^2>] + D x_t
+ * Replaces fused_selective_lru / _SelectiveLRUScan
+ * (models/selective_lru/selective_lru_triton.py:398-577) and the materialised path of
+ * SelectiveLRU.forward (models/selective_lru/selective_lru.py:242-276, 590-599).
+ *
+ * real = 1 selects the real specialisation (omega = delta_theta = B_im = C_im = 0; the
+ * pointers for those operands, and every *_im pointer, are ignored): the selective
+ * diagonal scan h = exp(-delta_nu a) h + gain B_t x, y = <C_t, h> + D x.
+ *
+ * Shapes: delta_nu, delta_theta, x, y, dy, d_*: (S,L,C); a, omega, g, s: (C,N);
+ * B_*, C_* and their grads: (S,L,N); D: (C); h0_*, hf_*, dhf_*, dh0_*: (S,C,N).
+ * Optional inputs: g (envelope readout), s (per-mode detune), h0 (initial state),
+ * dy / dhf in the backward (NULL = zero). N <= 32.
+ * Forward writes y, hf (if non-NULL) and, if ckpt != NULL, the state entering every
+ * `chunk`-step block: ckpt (S, ceil(L/chunk), C, N) complex64 (fp32 when real).
+ * Backward needs the forward's ckpt and writes every non-NULL gradient; reductions over
+ * channels (dB, dC) and over (S, L) (da, domega, dD, dg, ds) use a fixed order.
+ * chunk must be a multiple of 4 in [4, 256].
+ * ---------------------------------------------------------------------------------- */
+enum semx_input_gain {
+  SEMX_GAIN_GAMMA = 0, /* sqrt(max(1 - |lam|^2, 1e-6))        */
+  SEMX_GAIN_MAMBA = 1, /* delta_nu                             */
+  SEMX_GAIN_ZOH = 2,   /* (lam - 1) / (-a + j*base), exact ZOH */
+  SEMX_GAIN_NONE = 3   /* 1 (MIMO only)                        */
+};
+
+typedef struct SemxSelectiveLruArgs {
+  uint32_t struct_size;
+  int32_t real;       /* 1 = real specialisation                 */
+  int32_t input_gain; /* enum semx_input_gain (not NONE)         */
+  int32_t chunk;      /* checkpoint interval, in steps           */
+  int64_t S, L, C, N;
+  const float* delta_nu;
+  const float* delta_theta;
+  const float* a;     /* exp(A_log), > 0 */
+  const float* omega;
+  const float* B_re;
+  const float* B_im;
+  const float* C_re;
+  const float* C_im;
+  const float* x;
+  const float* D;
+  const float* g;     /* envelope gains or NULL */
+  const float* s;     /* detune gains or NULL   */
+  const float* h0_re; /* initial state or NULL  */
+  const float* h0_im;
+  /* forward outputs */
+  float* y;
+  float* hf_re; /* final state or NULL */
+  float* hf_im;
+  float* ckpt;
+  /* backward inputs */
+  const float* dy;
+  const float* dhf_re;
+  const float* dhf_im;
+  /* backward outputs (NULL = not wanted) */
+  float* d_delta_nu;
+  float* d_delta_theta;
+  float* dx;
+  float* dB_re;
+  float* dB_im;
+  float* dC_re;
+  float* dC_im;
+  float* da;
+  float* domega;
+  float* dD;
+  float* dg;
+  float* ds;
+  float* dh0_re;
+  float* dh0_im;
+  void* workspace; /* semx_selective_lru_workspace_bytes(), backward only */
+} SemxSelectiveLruArgs;
+
+size_t semx_selective_lru_args_size(void);
+size_t semx_selective_lru_ckpt_bytes(const SemxSelectiveLruArgs* args);
+size_t semx_selective_lru_workspace_bytes(const SemxSelectiveLruArgs* args);
+int semx_selective_lru_fwd(const SemxSelectiveLruArgs* args, semx_stream_t stream);
+int semx_selective_lru_bwd(const SemxSelectiveLruArgs* args, semx_stream_t stream);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

@@ -74,9 +74,32 @@ class SemxLinossArgs(ctypes.Structure):
     ]
 
 
+# enum semx_input_gain
+GAIN_CODES = {"gamma": 0, "mamba": 1, "zoh": 2, "none": 3}
+
+
+class SemxSelectiveLruArgs(ctypes.Structure):
+    _fields_ = [
+        ("struct_size", ctypes.c_uint32),
+        ("real", ctypes.c_int32),
+        ("input_gain", ctypes.c_int32),
+        ("chunk", ctypes.c_int32),
+        ("S", ctypes.c_int64),
+        ("L", ctypes.c_int64),
+        ("C", ctypes.c_int64),
+        ("N", ctypes.c_int64),
+    ] + [(name, ctypes.c_void_p) for name in (
+        "delta_nu", "delta_theta", "a", "omega", "B_re", "B_im", "C_re", "C_im", "x", "D",
+        "g", "s", "h0_re", "h0_im", "y", "hf_re", "hf_im", "ckpt", "dy", "dhf_re", "dhf_im",
+        "d_delta_nu", "d_delta_theta", "dx", "dB_re", "dB_im", "dC_re", "dC_im", "da",
+        "domega", "dD", "dg", "ds", "dh0_re", "dh0_im", "workspace",
+    )]
+
+
 # (python struct, C size query) for every argument struct in semx.h.
 STRUCTS = {
     "SemxLinossArgs": (SemxLinossArgs, "semx_linoss_args_size"),
+    "SemxSelectiveLruArgs": (SemxSelectiveLruArgs, "semx_selective_lru_args_size"),
 }
 
 # Every symbol semx.h declares, with its ctypes signature.
@@ -92,6 +115,14 @@ _SIGNATURES = {
     "semx_linoss_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(SemxLinossArgs)]),
     "semx_linoss_fwd": (ctypes.c_int, [ctypes.POINTER(SemxLinossArgs), ctypes.c_void_p]),
     "semx_linoss_bwd": (ctypes.c_int, [ctypes.POINTER(SemxLinossArgs), ctypes.c_void_p]),
+    "semx_selective_lru_args_size": (ctypes.c_size_t, []),
+    "semx_selective_lru_ckpt_bytes": (ctypes.c_size_t, [ctypes.POINTER(SemxSelectiveLruArgs)]),
+    "semx_selective_lru_workspace_bytes": (
+        ctypes.c_size_t, [ctypes.POINTER(SemxSelectiveLruArgs)]),
+    "semx_selective_lru_fwd": (
+        ctypes.c_int, [ctypes.POINTER(SemxSelectiveLruArgs), ctypes.c_void_p]),
+    "semx_selective_lru_bwd": (
+        ctypes.c_int, [ctypes.POINTER(SemxSelectiveLruArgs), ctypes.c_void_p]),
 }
 
 _lib = None
@@ -150,6 +181,18 @@ def ptr(t: torch.Tensor | None) -> int | None:
 
 def stream_handle(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
+
+
+def call(fn_name: str, args, device) -> None:
+    """Runs a semx entry point on the current stream of `device`; raises on failure."""
+    lib = load()
+    status = getattr(lib, fn_name)(ctypes.byref(args), stream_handle(device))
+    check(fn_name, status)
+
+
+def empty_f32(nbytes: int, device) -> torch.Tensor:
+    """Scratch of at least `nbytes` (never zero-sized, so the pointer is never NULL)."""
+    return torch.empty(max((nbytes + 3) // 4, 1), dtype=torch.float32, device=device)
 
 
 def new_args(cls):

@@ -1,0 +1,960 @@
+// Selective-LRU SISO scan with fused discretisation, readout and D skip, for sm_100a.
+//
+// Reference behaviour (paths relative to the reference project):
+//   models/selective_lru/selective_lru.py:242-276   materialised SelectiveLRU path
+//   models/selective_lru/selective_lru.py:590-599   _selective_recurrence
+//   models/selective_lru/selective_lru_triton.py:528-577  fused_selective_lru operator
+//
+// Thread layout. A thread owns (sequence s, channel c, group g of kGM = 4 modes): lane
+// = cl * NG + g, where NG = ceil(N / 4) lanes share a channel and a warp covers 32 / NG
+// channels of the same sequence. A CTA of kThreads covers CB = kThreads / NG channels;
+// grid = (channel blocks, sequences). The time loop is sequential with one step of
+// register prefetch; the pole, drive and gain of every (t, c, n) are computed in
+// registers from delta_nu / delta_theta and never touch HBM.
+//
+// Forward: y_t = sum over modes (reduced over the NG lanes of a channel by shuffles).
+// Training forwards also store the state entering every `chunk`-step block.
+//
+// Backward, per chunk (last first):
+//   pass 1  re-runs the chunk from its checkpoint, dropping the state every kR steps
+//           into shared memory;
+//   pass 2  walks kTT-step tiles backwards; inside a tile, kR-step sub-blocks backwards:
+//           recompute the kR states into registers, then run the adjoint
+//           G_t = g_t + conj(lam_{t+1}) G_{t+1} through them. Per-(t, c) gradients are
+//           reduced over the NG lanes by shuffles; per-(t, n) gradients dB / dC are
+//           reduced over channels in a fixed order: transposed shuffles inside the
+//           warp, then shared memory across warps, then DSMEM across the CTAs of a
+//           thread-block cluster that spans all channel blocks of the sequence.
+// Per-(c, n) parameter gradients are summed per thread over time, written per sequence,
+// and reduced over sequences by a two-stage fixed-order column sum.
+#include <cooperative_groups.h>
+
+#include "semx_common.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace {
+
+constexpr int kThreads = 128;
+constexpr int kGM = 4;   // modes per thread
+constexpr int kR = 4;    // steps per register-resident sub-block (backward)
+constexpr int kTT = 16;  // steps per dB/dC reduction tile (backward)
+constexpr int kMaxClusterCTAs = 8;
+constexpr int kRowsPerGroup = 32;  // column-sum stage 1 group size
+constexpr float kLog2e = 1.4426950408889634f;
+
+struct SParams {
+  int real, gain, chunk, nchunks;
+  int64_t S, L, C, N;
+  int detune, envelope;
+  int ncl;        // CTAs per cluster
+  int nclusters;  // clusters per sequence (channel-block groups)
+  const float* dnu;
+  const float* dth;
+  const float* a;
+  const float* om;
+  const float* Bre;
+  const float* Bim;
+  const float* Cre;
+  const float* Cim;
+  const float* x;
+  const float* D;
+  const float* g;
+  const float* sdet;
+  const float* h0r;
+  const float* h0i;
+  float* y;
+  float* hfr;
+  float* hfi;
+  float* ckpt;
+  const float* dy;
+  const float* dhfr;
+  const float* dhfi;
+  float* d_dnu;
+  float* d_dth;
+  float* dx;
+  float* dBre;
+  float* dBim;
+  float* dCre;
+  float* dCim;
+  float* dh0r;
+  float* dh0i;
+  float* part;      // (S, 4*C*N + C) per-sequence parameter-gradient partials
+  float* dbc_part;  // (S*L, nclusters, narr*N) when nclusters > 1
+};
+
+// Pole, drive gain and their intermediates for one (t, c, n).
+struct Disc {
+  float nu, cs, sn, base, lre, lim, gr, gi, den;
+};
+
+template <bool REAL, int GAIN>
+__device__ __forceinline__ Disc discretise(float a, float a2, float om, float sd, bool detune,
+                                           float dnu, float dth) {
+  Disc d;
+  d.nu = exp2f(-dnu * a2);
+  if (REAL) {
+    d.cs = 1.f;
+    d.sn = 0.f;
+    d.base = 0.f;
+    d.lre = d.nu;
+    d.lim = 0.f;
+  } else {
+    d.base = om + (detune ? sd * dth : dth);
+    sincosf(dnu * d.base, &d.sn, &d.cs);
+    d.lre = d.nu * d.cs;
+    d.lim = d.nu * d.sn;
+  }
+  d.gi = 0.f;
+  d.den = 1.f;
+  if (GAIN == SEMX_GAIN_GAMMA) {
+    d.gr = sqrtf(fmaxf(1.f - d.nu * d.nu, 1e-6f));
+  } else if (GAIN == SEMX_GAIN_MAMBA) {
+    d.gr = dnu;
+  } else {  // ZOH: (lam - 1) / A_c, A_c = -a + j base, with lam - 1 from expm1
+    const float em1 = expm1f(-dnu * a);
+    if (REAL) {
+      d.den = fmaxf(a * a, 1e-8f);
+      d.gr = -(a * em1) / d.den;
+    } else {
+      const float sh = sinf(0.5f * (dnu * d.base));
+      const float lm1r = em1 * d.cs - 2.f * sh * sh;
+      const float lm1i = d.lim;
+      d.den = fmaxf(a * a + d.base * d.base, 1e-8f);
+      d.gr = (d.base * lm1i - a * lm1r) / d.den;
+      d.gi = -(a * lm1i + d.base * lm1r) / d.den;
+    }
+  }
+  return d;
+}
+
+template <bool REAL>
+struct StepIn {
+  float dnu, dth, x;
+  float bre[kGM], bim[kGM], cre[kGM], cim[kGM];
+};
+
+// Loads the operands of step t for this thread's channel and modes (zeros when invalid).
+template <bool REAL, bool WITH_C>
+__device__ __forceinline__ void load_step(const SParams& p, int64_t s, int t, int c, int g,
+                                          bool cval, bool vec4, StepIn<REAL>& in) {
+  const int64_t row = s * p.L + t;
+  if (cval) {
+    const int64_t ic = row * p.C + c;
+    in.dnu = __ldg(p.dnu + ic);
+    in.dth = REAL ? 0.f : __ldg(p.dth + ic);
+    in.x = __ldg(p.x + ic);
+  } else {
+    in.dnu = in.dth = in.x = 0.f;
+  }
+  const int64_t in0 = row * p.N + g * kGM;
+  if (vec4 && g * kGM >= p.N) {
+    // Whole group beyond N (N a multiple of 4 but not of 4 * NG): no modes to load.
+#pragma unroll
+    for (int j = 0; j < kGM; ++j) in.bre[j] = in.bim[j] = in.cre[j] = in.cim[j] = 0.f;
+  } else if (vec4) {
+    const float4 br = __ldg(reinterpret_cast<const float4*>(p.Bre + in0));
+    in.bre[0] = br.x; in.bre[1] = br.y; in.bre[2] = br.z; in.bre[3] = br.w;
+    if (!REAL) {
+      const float4 bi = __ldg(reinterpret_cast<const float4*>(p.Bim + in0));
+      in.bim[0] = bi.x; in.bim[1] = bi.y; in.bim[2] = bi.z; in.bim[3] = bi.w;
+    }
+    if (WITH_C) {
+      const float4 cr = __ldg(reinterpret_cast<const float4*>(p.Cre + in0));
+      in.cre[0] = cr.x; in.cre[1] = cr.y; in.cre[2] = cr.z; in.cre[3] = cr.w;
+      if (!REAL) {
+        const float4 ci = __ldg(reinterpret_cast<const float4*>(p.Cim + in0));
+        in.cim[0] = ci.x; in.cim[1] = ci.y; in.cim[2] = ci.z; in.cim[3] = ci.w;
+      }
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < kGM; ++j) {
+      const bool ok = g * kGM + j < p.N;
+      in.bre[j] = ok ? __ldg(p.Bre + in0 + j) : 0.f;
+      if (!REAL) in.bim[j] = ok ? __ldg(p.Bim + in0 + j) : 0.f;
+      if (WITH_C) {
+        in.cre[j] = ok ? __ldg(p.Cre + in0 + j) : 0.f;
+        if (!REAL) in.cim[j] = ok ? __ldg(p.Cim + in0 + j) : 0.f;
+      }
+    }
+  }
+  if (REAL) {
+#pragma unroll
+    for (int j = 0; j < kGM; ++j) {
+      in.bim[j] = 0.f;
+      in.cim[j] = 0.f;
+    }
+  }
+}
+
+struct ModeParams {
+  float a[kGM], a2[kGM], om[kGM], sd[kGM], ge[kGM];
+  bool ok[kGM];
+};
+
+__device__ __forceinline__ void load_params(const SParams& p, int c, int g, bool cval,
+                                            ModeParams& mp) {
+#pragma unroll
+  for (int j = 0; j < kGM; ++j) {
+    const int n = g * kGM + j;
+    mp.ok[j] = cval && n < p.N;
+    const int64_t i = (int64_t)c * p.N + n;
+    mp.a[j] = mp.ok[j] ? p.a[i] : 0.f;
+    mp.a2[j] = mp.a[j] * kLog2e;
+    mp.om[j] = (mp.ok[j] && !p.real) ? p.om[i] : 0.f;
+    mp.sd[j] = (mp.ok[j] && p.detune) ? p.sdet[i] : 1.f;
+    mp.ge[j] = (mp.ok[j] && p.envelope) ? p.g[i] : 0.f;
+  }
+}
+
+template <int NG>
+__device__ __forceinline__ float sum_lanes(float v) {
+#pragma unroll
+  for (int m = NG / 2; m >= 1; m /= 2) v += __shfl_xor_sync(0xffffffffu, v, m);
+  return v;
+}
+
+// Sums v[0..V) over the CW lanes lane = cl * NG + g that share g (cl = 0..CW-1).
+// V >= CW: lane cl ends with the totals of value indices [cl*V/CW, (cl+1)*V/CW) in
+//          v[0..V/CW);
+// V <  CW: every lane ends with the total of value index cl / (CW/V) in v[0].
+// Transposed halving (each round sends half of the remaining values) followed by
+// butterfly rounds when there are more lanes than values.
+template <int V, int CW, int NG>
+__device__ __forceinline__ void lane_reduce(float (&v)[V], int cl) {
+  constexpr int kT = (V < CW) ? V : CW;
+#pragma unroll
+  for (int r = 0; (1 << r) < kT; ++r) {
+    const int m = CW >> (r + 1);
+    const int n = V >> (r + 1);
+    const bool up = (cl & m) != 0;
+#pragma unroll
+    for (int i = 0; i < n; ++i) {
+      const float send = up ? v[i] : v[i + n];
+      const float keep = up ? v[i + n] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, m * NG);
+    }
+  }
+#pragma unroll
+  for (int m = (CW / kT) / 2; m >= 1; m /= 2) v[0] += __shfl_xor_sync(0xffffffffu, v[0], m * NG);
+}
+
+// ----------------------------------------------------------------------------- forward
+template <bool REAL, int GAIN, int NG>
+__global__ void __launch_bounds__(kThreads) slru_fwd_kernel(const SParams p) {
+  constexpr int CW = 32 / NG;
+  constexpr int CB = kThreads / NG;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int cl = lane / NG, g = lane % NG;
+  const int c = blockIdx.x * CB + warp * CW + cl;
+  const int64_t s = blockIdx.y;
+  const bool cval = c < p.C;
+  const bool vec4 = (p.N % 4) == 0 && p.N > 0;
+  const int L = (int)p.L;
+
+  ModeParams mp;
+  load_params(p, c, g, cval, mp);
+  const float Dc = cval ? p.D[c] : 0.f;
+  float hr[kGM], hi[kGM];
+#pragma unroll
+  for (int j = 0; j < kGM; ++j) {
+    const int64_t i = (s * p.C + c) * p.N + g * kGM + j;
+    hr[j] = (mp.ok[j] && p.h0r) ? p.h0r[i] : 0.f;
+    hi[j] = (mp.ok[j] && p.h0i && !REAL) ? p.h0i[i] : 0.f;
+  }
+
+  StepIn<REAL> cur, nxt;
+  if (L > 0) load_step<REAL, true>(p, s, 0, c, g, cval, vec4, cur);
+  for (int t = 0; t < L; ++t) {
+    if (t + 1 < L) load_step<REAL, true>(p, s, t + 1, c, g, cval, vec4, nxt);
+    if (p.ckpt != nullptr && (t % p.chunk) == 0) {
+      const int64_t base = ((s * p.nchunks + t / p.chunk) * p.C + c) * p.N + g * kGM;
+#pragma unroll
+      for (int j = 0; j < kGM; ++j) {
+        if (mp.ok[j]) {
+          if (REAL) {
+            p.ckpt[base + j] = hr[j];
+          } else {
+            reinterpret_cast<float2*>(p.ckpt)[base + j] = make_float2(hr[j], hi[j]);
+          }
+        }
+      }
+    }
+    float yp = 0.f;
+#pragma unroll
+    for (int j = 0; j < kGM; ++j) {
+      const Disc d = discretise<REAL, GAIN>(mp.a[j], mp.a2[j], mp.om[j], mp.sd[j], p.detune,
+                                            cur.dnu, cur.dth);
+      const float gxr = d.gr * cur.x, gxi = d.gi * cur.x;
+      const float ur = gxr * cur.bre[j] - gxi * cur.bim[j];
+      const float ui = gxr * cur.bim[j] + gxi * cur.bre[j];
+      const float nr = d.lre * hr[j] - d.lim * hi[j] + ur;
+      const float ni = d.lre * hi[j] + d.lim * hr[j] + ui;
+      hr[j] = mp.ok[j] ? nr : 0.f;
+      hi[j] = mp.ok[j] ? ni : 0.f;
+      yp += cur.cre[j] * hr[j] - cur.cim[j] * hi[j];
+      if (p.envelope) yp += mp.ge[j] * (hr[j] * hr[j] + hi[j] * hi[j]);
+    }
+    yp = sum_lanes<NG>(yp);
+    if (g == 0 && cval) p.y[(s * p.L + t) * p.C + c] = yp + Dc * cur.x;
+    cur = nxt;
+  }
+  if (p.hfr != nullptr) {
+#pragma unroll
+    for (int j = 0; j < kGM; ++j) {
+      if (mp.ok[j]) {
+        const int64_t i = (s * p.C + c) * p.N + g * kGM + j;
+        p.hfr[i] = hr[j];
+        if (!REAL && p.hfi) p.hfi[i] = hi[j];
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------- backward
+template <bool REAL, int NG>
+struct BwdLayout {
+  static constexpr int kHS = REAL ? 1 : 2;         // floats per mode of state
+  static constexpr int kNArr = REAL ? 2 : 4;       // dB(re, im), dC(re, im)
+  static constexpr int kV = kNArr * kGM;           // dB/dC values per thread per step
+  static constexpr int kNV = NG * kV;              // values per warp per step
+  static constexpr int kNW = kThreads / 32;
+  __host__ __device__ static size_t sub_floats(int chunk) { return (size_t)(chunk / kR) * kThreads * kGM * kHS; }
+  __host__ __device__ static size_t red_floats() { return (size_t)2 * kTT * kNW * kNV; }
+  __host__ __device__ static size_t bytes(int chunk) { return (sub_floats(chunk) + red_floats()) * sizeof(float); }
+};
+
+template <bool REAL, int GAIN, int NG>
+__global__ void __launch_bounds__(kThreads) slru_bwd_kernel(const SParams p) {
+  using Lay = BwdLayout<REAL, NG>;
+  constexpr int CW = 32 / NG;
+  constexpr int CB = kThreads / NG;
+  constexpr int V = Lay::kV;
+  constexpr int NV = Lay::kNV;
+  constexpr int NW = Lay::kNW;
+  constexpr int HS = Lay::kHS;
+  extern __shared__ float smem[];
+  float* sub = smem;                                 // [chunk/kR][kThreads][kGM*HS]
+  float* red = smem + Lay::sub_floats(p.chunk);      // [2][kTT][NW][NV]
+  cg::cluster_group cluster = cg::this_cluster();
+  const int crank = (int)cluster.block_rank();
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int cl = lane / NG, g = lane % NG;
+  const int c = blockIdx.x * CB + warp * CW + cl;
+  const int64_t s = blockIdx.y;
+  const bool cval = c < p.C;
+  const bool vec4 = (p.N % 4) == 0 && p.N > 0;
+  const int L = (int)p.L;
+  const int N = (int)p.N;
+
+  ModeParams mp;
+  load_params(p, c, g, cval, mp);
+  const float Dc = cval ? p.D[c] : 0.f;
+
+  float Gr[kGM], Gi[kGM], lnr[kGM], lni[kGM];
+  float acc_a[kGM], acc_om[kGM], acc_s[kGM], acc_g[kGM];
+  float acc_D = 0.f;
+#pragma unroll
+  for (int j = 0; j < kGM; ++j) {
+    const int64_t i = (s * p.C + c) * p.N + g * kGM + j;
+    const bool has = mp.ok[j] && p.dhfr != nullptr;
+    Gr[j] = has ? p.dhfr[i] : 0.f;
+    Gi[j] = (has && !REAL && p.dhfi) ? p.dhfi[i] : 0.f;
+    lnr[j] = has ? 1.f : 0.f;
+    lni[j] = 0.f;
+    acc_a[j] = acc_om[j] = acc_s[j] = acc_g[j] = 0.f;
+  }
+
+  int tile_count = 0;
+  for (int k = p.nchunks - 1; k >= 0; --k) {
+    const int t0 = k * p.chunk;
+    const int t1 = min(t0 + p.chunk, L);
+    // Pass 1: recurrence from the checkpoint, state every kR steps to shared memory.
+    {
+      float hr[kGM], hi[kGM];
+      const int64_t cb = ((s * p.nchunks + k) * p.C + c) * p.N + g * kGM;
+#pragma unroll
+      for (int j = 0; j < kGM; ++j) {
+        if (REAL) {
+          hr[j] = mp.ok[j] ? p.ckpt[cb + j] : 0.f;
+          hi[j] = 0.f;
+        } else {
+          const float2 v = mp.ok[j] ? reinterpret_cast<const float2*>(p.ckpt)[cb + j]
+                                    : make_float2(0.f, 0.f);
+          hr[j] = v.x;
+          hi[j] = v.y;
+        }
+      }
+      StepIn<REAL> cur, nxt;
+      load_step<REAL, false>(p, s, t0, c, g, cval, vec4, cur);
+      for (int t = t0; t < t1; ++t) {
+        if (t + 1 < t1) load_step<REAL, false>(p, s, t + 1, c, g, cval, vec4, nxt);
+        if (((t - t0) % kR) == 0) {
+          float* dst = sub + ((size_t)((t - t0) / kR) * kThreads + tid) * kGM * HS;
+#pragma unroll
+          for (int j = 0; j < kGM; ++j) {
+            dst[j * HS] = hr[j];
+            if (!REAL) dst[j * HS + 1] = hi[j];
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < kGM; ++j) {
+          const Disc d = discretise<REAL, GAIN>(mp.a[j], mp.a2[j], mp.om[j], mp.sd[j], p.detune,
+                                                cur.dnu, cur.dth);
+          const float gxr = d.gr * cur.x, gxi = d.gi * cur.x;
+          const float ur = gxr * cur.bre[j] - gxi * cur.bim[j];
+          const float ui = gxr * cur.bim[j] + gxi * cur.bre[j];
+          const float nr = d.lre * hr[j] - d.lim * hi[j] + ur;
+          const float ni = d.lre * hi[j] + d.lim * hr[j] + ui;
+          hr[j] = mp.ok[j] ? nr : 0.f;
+          hi[j] = mp.ok[j] ? ni : 0.f;
+        }
+        cur = nxt;
+      }
+    }
+
+    // Pass 2: tiles backwards, sub-blocks backwards inside each tile.
+    const int ntile = (t1 - t0 + kTT - 1) / kTT;
+    for (int q = ntile - 1; q >= 0; --q, ++tile_count) {
+      const int tt0 = t0 + q * kTT;
+      const int tt1 = min(tt0 + kTT, t1);
+      const int buf = tile_count & 1;
+      float* redb = red + (size_t)buf * kTT * NW * NV;
+      const int nsubt = (tt1 - tt0 + kR - 1) / kR;
+      for (int r = nsubt - 1; r >= 0; --r) {
+        const int ta = tt0 + r * kR;
+        const int tb = min(ta + kR, tt1);
+        float Hr[kR][kGM], Hi[kR][kGM], H0r[kGM], H0i[kGM];
+        {
+          const float* src = sub + ((size_t)((ta - t0) / kR) * kThreads + tid) * kGM * HS;
+#pragma unroll
+          for (int j = 0; j < kGM; ++j) {
+            H0r[j] = src[j * HS];
+            H0i[j] = REAL ? 0.f : src[j * HS + 1];
+          }
+        }
+        // Recompute kR states.
+#pragma unroll
+        for (int i = 0; i < kR; ++i) {
+          if (ta + i < tb) {
+            StepIn<REAL> in;
+            load_step<REAL, false>(p, s, ta + i, c, g, cval, vec4, in);
+#pragma unroll
+            for (int j = 0; j < kGM; ++j) {
+              const float pr = i == 0 ? H0r[j] : Hr[i > 0 ? i - 1 : 0][j];
+              const float pi = i == 0 ? H0i[j] : Hi[i > 0 ? i - 1 : 0][j];
+              const Disc d = discretise<REAL, GAIN>(mp.a[j], mp.a2[j], mp.om[j], mp.sd[j],
+                                                    p.detune, in.dnu, in.dth);
+              const float gxr = d.gr * in.x, gxi = d.gi * in.x;
+              const float ur = gxr * in.bre[j] - gxi * in.bim[j];
+              const float ui = gxr * in.bim[j] + gxi * in.bre[j];
+              const float nr = d.lre * pr - d.lim * pi + ur;
+              const float ni = d.lre * pi + d.lim * pr + ui;
+              Hr[i][j] = mp.ok[j] ? nr : 0.f;
+              Hi[i][j] = mp.ok[j] ? ni : 0.f;
+            }
+          }
+        }
+        // Adjoint through the sub-block.
+#pragma unroll
+        for (int i = kR - 1; i >= 0; --i) {
+          if (ta + i < tb) {
+            const int t = ta + i;
+            StepIn<REAL> in;
+            load_step<REAL, true>(p, s, t, c, g, cval, vec4, in);
+            const float dyv = cval ? __ldg(p.dy + (s * p.L + t) * p.C + c) : 0.f;
+            float sum_dnu = 0.f, sum_dth = 0.f, sum_dx = 0.f;
+            float vals[V];
+#pragma unroll
+            for (int j = 0; j < kGM; ++j) {
+              const float hr = Hr[i][j], hi = Hi[i][j];
+              const float hpr = i == 0 ? H0r[j] : Hr[i > 0 ? i - 1 : 0][j];
+              const float hpi = i == 0 ? H0i[j] : Hi[i > 0 ? i - 1 : 0][j];
+              const Disc d = discretise<REAL, GAIN>(mp.a[j], mp.a2[j], mp.om[j], mp.sd[j],
+                                                    p.detune, in.dnu, in.dth);
+              // Local adjoint from the readout (and the envelope term).
+              float gre = dyv * in.cre[j];
+              float gim = -dyv * in.cim[j];
+              if (p.envelope) {
+                gre += 2.f * dyv * mp.ge[j] * hr;
+                gim += 2.f * dyv * mp.ge[j] * hi;
+                acc_g[j] += dyv * (hr * hr + hi * hi);
+              }
+              // G_t = g_t + conj(lam_{t+1}) G_{t+1}
+              const float gr_ = gre + lnr[j] * Gr[j] + lni[j] * Gi[j];
+              const float gi_ = REAL ? 0.f : gim + lnr[j] * Gi[j] - lni[j] * Gr[j];
+              const float Gtr = mp.ok[j] ? gr_ : 0.f;
+              const float Gti = mp.ok[j] ? gi_ : 0.f;
+              // Input map Bu = (gain x) B.
+              const float gxr = d.gr * in.x, gxi = d.gi * in.x;
+              const float vBr = gxr * Gtr + gxi * Gti;
+              const float vBi = gxr * Gti - gxi * Gtr;
+              const float wre = d.gr * in.bre[j] - d.gi * in.bim[j];
+              const float wim = d.gr * in.bim[j] + d.gi * in.bre[j];
+              sum_dx += wre * Gtr + wim * Gti;
+              const float dgr = in.x * (in.bre[j] * Gtr + in.bim[j] * Gti);
+              const float dgi = in.x * (in.bre[j] * Gti - in.bim[j] * Gtr);
+              float d_nu_tot = 0.f, d_dnu = 0.f, da_extra = 0.f, dbase_extra = 0.f;
+              if (GAIN == SEMX_GAIN_GAMMA) {
+                const bool live = (1.f - d.nu * d.nu) >= 1e-6f;
+                d_nu_tot += live ? -dgr * d.nu / d.gr : 0.f;
+              } else if (GAIN == SEMX_GAIN_MAMBA) {
+                d_dnu += dgr;
+              } else {
+                // d gain / d delta_nu = lam; d gain / d A_c = (dnu lam - gain) / A_c = q.
+                d_dnu += dgr * d.lre + dgi * d.lim;
+                const float pr = in.dnu * d.lre - d.gr;
+                const float pi = in.dnu * d.lim - d.gi;
+                const float qr = (d.base * pi - mp.a[j] * pr) / d.den;
+                const float qi = -(mp.a[j] * pi + d.base * pr) / d.den;
+                da_extra = -(dgr * qr + dgi * qi);
+                dbase_extra = dgi * qr - dgr * qi;
+              }
+              // d lam = G_t conj(h_{t-1}).
+              const float dlre = Gtr * hpr + Gti * hpi;
+              const float dlim = Gti * hpr - Gtr * hpi;
+              float d_th = 0.f;
+              if (REAL) {
+                d_nu_tot += dlre;
+              } else {
+                d_nu_tot += dlre * d.cs + dlim * d.sn;
+                d_th = d.nu * (dlim * d.cs - dlre * d.sn);
+              }
+              d_dnu += d_nu_tot * (-mp.a[j]) * d.nu;
+              acc_a[j] += d_nu_tot * (-in.dnu) * d.nu + da_extra;
+              if (!REAL) {
+                d_dnu += d_th * d.base;
+                const float dbase = d_th * in.dnu + dbase_extra;
+                acc_om[j] += dbase;
+                sum_dth += dbase * mp.sd[j];
+                if (p.detune) acc_s[j] += dbase * in.dth;
+              }
+              sum_dnu += mp.ok[j] ? d_dnu : 0.f;
+              // dB, dC values for the cross-channel reduction.
+              vals[0 * kGM + j] = mp.ok[j] ? vBr : 0.f;
+              if (REAL) {
+                vals[1 * kGM + j] = mp.ok[j] ? dyv * hr : 0.f;
+              } else {
+                vals[1 * kGM + j] = mp.ok[j] ? vBi : 0.f;
+                vals[2 * kGM + j] = mp.ok[j] ? dyv * hr : 0.f;
+                vals[3 * kGM + j] = mp.ok[j] ? -dyv * hi : 0.f;
+              }
+              Gr[j] = Gtr;
+              Gi[j] = Gti;
+              lnr[j] = d.lre;
+              lni[j] = d.lim;
+            }
+            if (g == 0) acc_D += dyv * in.x;
+            sum_dnu = sum_lanes<NG>(sum_dnu);
+            sum_dx = sum_lanes<NG>(sum_dx);
+            if (!REAL) sum_dth = sum_lanes<NG>(sum_dth);
+            if (g == 0 && cval) {
+              const int64_t ic = (s * p.L + t) * p.C + c;
+              if (p.d_dnu) p.d_dnu[ic] = sum_dnu;
+              if (!REAL && p.d_dth) p.d_dth[ic] = sum_dth;
+              if (p.dx) p.dx[ic] = sum_dx + dyv * Dc;
+            }
+            lane_reduce<V, CW, NG>(vals, cl);
+            float* dst = redb + ((size_t)(t - tt0) * NW + warp) * NV + g * V;
+            if (V >= CW) {
+#pragma unroll
+              for (int m = 0; m < (V >= CW ? V / CW : 1); ++m) dst[cl * (V / CW) + m] = vals[m];
+            } else if ((cl % (V < CW ? CW / V : 1)) == 0) {
+              dst[cl / (V < CW ? CW / V : 1)] = vals[0];
+            }
+          }
+        }
+      }
+      // Tile complete: sum dB / dC over warps and over the cluster's CTAs (fixed order).
+      __syncthreads();
+      cluster.sync();
+      const int nitems = (tt1 - tt0) * NV;
+      const int stride = p.ncl * kThreads;
+      for (int it = crank * kThreads + tid; it < nitems; it += stride) {
+        const int tl = it / NV, kk = it % NV;
+        const int gg = kk / V, vv = kk % V;
+        const int arr = vv / kGM, n = gg * kGM + (vv % kGM);
+        if (n >= N) continue;
+        float acc = 0.f;
+        for (int qr = 0; qr < p.ncl; ++qr) {
+          const float* peer = cluster.map_shared_rank(redb, qr);
+#pragma unroll
+          for (int w = 0; w < NW; ++w) acc += peer[((size_t)tl * NW + w) * NV + kk];
+        }
+        const int64_t row = s * p.L + tt0 + tl;
+        if (p.nclusters > 1) {
+          const int clid = blockIdx.x / p.ncl;
+          p.dbc_part[(row * p.nclusters + clid) * (Lay::kNArr * N) + arr * N + n] = acc;
+        } else {
+          float* outp = REAL ? (arr == 0 ? p.dBre : p.dCre)
+                             : (arr == 0 ? p.dBre : arr == 1 ? p.dBim : arr == 2 ? p.dCre : p.dCim);
+          if (outp) outp[row * N + n] = acc;
+        }
+      }
+    }
+  }
+
+  // Initial-state gradient: dh0 = conj(lam_0) G_0.
+  if (p.dh0r != nullptr) {
+#pragma unroll
+    for (int j = 0; j < kGM; ++j) {
+      if (mp.ok[j]) {
+        const int64_t i = (s * p.C + c) * p.N + g * kGM + j;
+        p.dh0r[i] = lnr[j] * Gr[j] + lni[j] * Gi[j];
+        if (!REAL && p.dh0i) p.dh0i[i] = lnr[j] * Gi[j] - lni[j] * Gr[j];
+      }
+    }
+  }
+  // Per-sequence parameter-gradient partials: [da | domega | ds | dg] (C, N) each, dD (C).
+  {
+    const int64_t K = 4 * p.C * p.N + p.C;
+    float* row = p.part + s * K;
+    const int64_t CN = p.C * p.N;
+#pragma unroll
+    for (int j = 0; j < kGM; ++j) {
+      if (mp.ok[j]) {
+        const int64_t i = (int64_t)c * p.N + g * kGM + j;
+        row[0 * CN + i] = acc_a[j];
+        row[1 * CN + i] = acc_om[j];
+        row[2 * CN + i] = acc_s[j];
+        row[3 * CN + i] = acc_g[j];
+      }
+    }
+    if (g == 0 && cval) row[4 * CN + c] = acc_D;
+  }
+  cluster.sync();  // no CTA leaves while a peer may still read its shared memory
+}
+
+// --------------------------------------------------------------------- reductions
+// Stage 1: group_sums[grp][k] = sum of rows[r][k] over the rows of group grp, in order.
+__global__ void colsum_stage1(const float* __restrict__ rows, int64_t S, int64_t K,
+                              float* __restrict__ group_sums) {
+  const int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (k >= K) return;
+  const int64_t r0 = (int64_t)blockIdx.y * kRowsPerGroup;
+  const int64_t r1 = min(r0 + kRowsPerGroup, S);
+  float acc = 0.f;
+  for (int64_t r = r0; r < r1; ++r) acc += rows[r * K + k];
+  group_sums[(int64_t)blockIdx.y * K + k] = acc;
+}
+
+struct Segments {
+  float* out[5];
+  int64_t len[5];
+};
+
+// Stage 2: out segment <- sum over groups (in order); NULL segments are skipped.
+__global__ void colsum_stage2(const float* __restrict__ group_sums, int64_t G, int64_t K,
+                              Segments seg) {
+  const int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (k >= K) return;
+  int64_t off = k;
+  int which = 0;
+  while (which < 5 && off >= seg.len[which]) {
+    off -= seg.len[which];
+    ++which;
+  }
+  if (which >= 5 || seg.out[which] == nullptr) return;
+  float acc = 0.f;
+  for (int64_t q = 0; q < G; ++q) acc += group_sums[q * K + k];
+  seg.out[which][off] = acc;
+}
+
+// dB / dC over cluster groups when one cluster cannot span all channel blocks.
+__global__ void dbc_sum_kernel(const SParams p, int narr) {
+  const int64_t total = p.S * p.L * narr * p.N;
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= total) return;
+  const int64_t row = i / (narr * p.N);
+  const int rem = (int)(i % (narr * p.N));
+  const int arr = rem / (int)p.N, n = rem % (int)p.N;
+  float acc = 0.f;
+  for (int q = 0; q < p.nclusters; ++q) acc += p.dbc_part[(row * p.nclusters + q) * (narr * p.N) + rem];
+  float* outp = narr == 2 ? (arr == 0 ? p.dBre : p.dCre)
+                          : (arr == 0 ? p.dBre : arr == 1 ? p.dBim : arr == 2 ? p.dCre : p.dCim);
+  if (outp) outp[row * p.N + n] = acc;
+}
+
+// ------------------------------------------------------------------------ host side
+int ng_for(int64_t N) {
+  const int64_t ng = semx::cdiv(N, kGM);
+  if (ng <= 1) return 1;
+  if (ng <= 2) return 2;
+  if (ng <= 4) return 4;
+  return 8;
+}
+
+struct Geometry {
+  int ng, cb, nblocks, ncl, nclusters, grid_x;
+};
+
+Geometry geometry(const SemxSelectiveLruArgs* a) {
+  Geometry g;
+  g.ng = ng_for(a->N);
+  g.cb = kThreads / g.ng;
+  g.nblocks = (int)semx::cdiv(a->C, g.cb);
+  g.ncl = g.nblocks < kMaxClusterCTAs ? g.nblocks : kMaxClusterCTAs;
+  if (g.ncl < 1) g.ncl = 1;
+  g.nclusters = (int)semx::cdiv(g.nblocks, g.ncl);
+  g.grid_x = g.nclusters * g.ncl;
+  return g;
+}
+
+size_t bwd_smem(const SemxSelectiveLruArgs* a, int ng) {
+  const bool real = a->real != 0;
+  switch (ng) {
+#define SEMX_CASE(NGV)                                                                \
+  case NGV:                                                                           \
+    return real ? BwdLayout<true, NGV>::bytes(a->chunk) : BwdLayout<false, NGV>::bytes(a->chunk);
+    SEMX_CASE(1)
+    SEMX_CASE(2)
+    SEMX_CASE(4)
+    SEMX_CASE(8)
+#undef SEMX_CASE
+  }
+  return 0;
+}
+
+int validate(const SemxSelectiveLruArgs* a, bool bwd) {
+  SEMX_REQUIRE(a->S >= 0 && a->L >= 0 && a->C >= 0 && a->N >= 0, SEMX_ERR_SHAPE,
+               "selective_lru: negative size");
+  SEMX_REQUIRE(a->N <= 32, SEMX_ERR_UNSUPPORTED, "selective_lru: N=%lld > 32",
+               (long long)a->N);
+  SEMX_REQUIRE(a->S <= 65535, SEMX_ERR_SHAPE, "selective_lru: S=%lld > 65535 (grid.y)",
+               (long long)a->S);
+  SEMX_REQUIRE(a->input_gain >= SEMX_GAIN_GAMMA && a->input_gain <= SEMX_GAIN_ZOH,
+               SEMX_ERR_UNSUPPORTED, "selective_lru: input_gain=%d", a->input_gain);
+  SEMX_REQUIRE(a->chunk >= kR && a->chunk <= 256 && a->chunk % kR == 0, SEMX_ERR_UNSUPPORTED,
+               "selective_lru: chunk=%d must be a multiple of %d in [%d, 256]", a->chunk, kR, kR);
+  const bool real = a->real != 0;
+  const bool any = a->S * a->C > 0;
+  if (any && a->N > 0) {
+    SEMX_REQUIRE(a->a != nullptr && (real || a->omega != nullptr), SEMX_ERR_NULL,
+                 "selective_lru: a/omega is NULL");
+  }
+  if (any) SEMX_REQUIRE(a->D != nullptr, SEMX_ERR_NULL, "selective_lru: D is NULL");
+  if (a->S * a->L * a->C > 0) {
+    SEMX_REQUIRE(a->delta_nu && a->x && (real || a->delta_theta), SEMX_ERR_NULL,
+                 "selective_lru: delta_nu/delta_theta/x is NULL");
+    if (a->N > 0) {
+      SEMX_REQUIRE(a->B_re && a->C_re && (real || (a->B_im && a->C_im)), SEMX_ERR_NULL,
+                   "selective_lru: B/C is NULL");
+      if (a->N % 4 == 0) {
+        SEMX_REQUIRE(semx::aligned(a->B_re, 16) && semx::aligned(a->C_re, 16) &&
+                         (real || (semx::aligned(a->B_im, 16) && semx::aligned(a->C_im, 16))),
+                     SEMX_ERR_ALIGN, "selective_lru: B/C must be 16-byte aligned when N %% 4 == 0");
+      }
+    }
+    if (!bwd) SEMX_REQUIRE(a->y != nullptr, SEMX_ERR_NULL, "selective_lru: y is NULL");
+    if (bwd) SEMX_REQUIRE(a->dy != nullptr, SEMX_ERR_NULL, "selective_lru bwd: dy is NULL");
+  }
+  if (!real) {
+    SEMX_REQUIRE(!a->ckpt || semx::aligned(a->ckpt, 8), SEMX_ERR_ALIGN,
+                 "selective_lru: ckpt must be 8-byte aligned");
+  }
+  if (bwd && a->S * a->C * a->N > 0) {
+    SEMX_REQUIRE(a->ckpt != nullptr || a->L == 0, SEMX_ERR_NULL,
+                 "selective_lru bwd: ckpt is NULL");
+    SEMX_REQUIRE(a->workspace != nullptr, SEMX_ERR_WORKSPACE, "selective_lru bwd: workspace");
+  }
+  if (bwd) {
+    const Geometry g = geometry(a);
+    const size_t smem = bwd_smem(a, g.ng);
+    SEMX_REQUIRE(smem <= 227 * 1024, SEMX_ERR_UNSUPPORTED,
+                 "selective_lru bwd: chunk=%d needs %zu B of shared memory (> 227 KB)",
+                 a->chunk, smem);
+  }
+  return SEMX_OK;
+}
+
+SParams to_params(const SemxSelectiveLruArgs* a) {
+  SParams p = {};
+  const Geometry g = geometry(a);
+  p.real = a->real != 0;
+  p.gain = a->input_gain;
+  p.chunk = a->chunk;
+  p.nchunks = (int)semx::cdiv(a->L, a->chunk);
+  p.S = a->S;
+  p.L = a->L;
+  p.C = a->C;
+  p.N = a->N;
+  p.detune = (!p.real && a->s != nullptr) ? 1 : 0;
+  p.envelope = a->g != nullptr ? 1 : 0;
+  p.ncl = g.ncl;
+  p.nclusters = g.nclusters;
+  p.dnu = a->delta_nu;
+  p.dth = a->delta_theta;
+  p.a = a->a;
+  p.om = a->omega;
+  p.Bre = a->B_re;
+  p.Bim = a->B_im;
+  p.Cre = a->C_re;
+  p.Cim = a->C_im;
+  p.x = a->x;
+  p.D = a->D;
+  p.g = a->g;
+  p.sdet = a->s;
+  p.h0r = a->h0_re;
+  p.h0i = a->h0_im;
+  p.y = a->y;
+  p.hfr = a->hf_re;
+  p.hfi = a->hf_im;
+  p.ckpt = a->ckpt;
+  p.dy = a->dy;
+  p.dhfr = a->dhf_re;
+  p.dhfi = a->dhf_im;
+  p.d_dnu = a->d_delta_nu;
+  p.d_dth = a->d_delta_theta;
+  p.dx = a->dx;
+  p.dBre = a->dB_re;
+  p.dBim = a->dB_im;
+  p.dCre = a->dC_re;
+  p.dCim = a->dC_im;
+  p.dh0r = a->dh0_re;
+  p.dh0i = a->dh0_im;
+  return p;
+}
+
+size_t part_floats(const SemxSelectiveLruArgs* a) {
+  return (size_t)a->S * (size_t)(4 * a->C * a->N + a->C);
+}
+size_t group_floats(const SemxSelectiveLruArgs* a) {
+  return (size_t)semx::cdiv(a->S, kRowsPerGroup) * (size_t)(4 * a->C * a->N + a->C);
+}
+size_t dbc_floats(const SemxSelectiveLruArgs* a) {
+  const Geometry g = geometry(a);
+  if (g.nclusters <= 1) return 0;
+  return (size_t)a->S * a->L * g.nclusters * (a->real ? 2 : 4) * a->N;
+}
+
+template <bool REAL, int GAIN, int NG>
+int launch_fwd(const SParams& p, const Geometry& g, cudaStream_t st) {
+  const dim3 grid((unsigned)g.nblocks, (unsigned)p.S);
+  slru_fwd_kernel<REAL, GAIN, NG><<<grid, kThreads, 0, st>>>(p);
+  return semx::check_launch("slru_fwd_kernel");
+}
+
+template <bool REAL, int GAIN, int NG>
+int launch_bwd(const SParams& p, const Geometry& g, size_t smem, cudaStream_t st) {
+  auto kern = slru_bwd_kernel<REAL, GAIN, NG>;
+  if (!semx::allow_smem(kern, smem)) return SEMX_ERR_LAUNCH;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)g.grid_x, (unsigned)p.S);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)g.ncl;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p);
+  if (e != cudaSuccess)
+    return semx::fail(SEMX_ERR_LAUNCH, "slru_bwd_kernel launch: %s", cudaGetErrorString(e));
+  return semx::check_launch("slru_bwd_kernel");
+}
+
+template <bool REAL, int GAIN>
+int dispatch_ng(bool bwd, const SParams& p, const Geometry& g, size_t smem, cudaStream_t st) {
+  switch (g.ng) {
+#define SEMX_CASE(NGV) \
+  case NGV:            \
+    return bwd ? launch_bwd<REAL, GAIN, NGV>(p, g, smem, st) : launch_fwd<REAL, GAIN, NGV>(p, g, st);
+    SEMX_CASE(1)
+    SEMX_CASE(2)
+    SEMX_CASE(4)
+    SEMX_CASE(8)
+#undef SEMX_CASE
+  }
+  return semx::fail(SEMX_ERR_UNSUPPORTED, "selective_lru: no kernel for NG=%d", g.ng);
+}
+
+int dispatch(bool bwd, const SemxSelectiveLruArgs* a, const SParams& p, const Geometry& g,
+             size_t smem, cudaStream_t st) {
+  const bool real = a->real != 0;
+  switch (a->input_gain) {
+    case SEMX_GAIN_GAMMA:
+      return real ? dispatch_ng<true, SEMX_GAIN_GAMMA>(bwd, p, g, smem, st)
+                  : dispatch_ng<false, SEMX_GAIN_GAMMA>(bwd, p, g, smem, st);
+    case SEMX_GAIN_MAMBA:
+      return real ? dispatch_ng<true, SEMX_GAIN_MAMBA>(bwd, p, g, smem, st)
+                  : dispatch_ng<false, SEMX_GAIN_MAMBA>(bwd, p, g, smem, st);
+    default:
+      return real ? dispatch_ng<true, SEMX_GAIN_ZOH>(bwd, p, g, smem, st)
+                  : dispatch_ng<false, SEMX_GAIN_ZOH>(bwd, p, g, smem, st);
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t semx_selective_lru_args_size(void) { return sizeof(SemxSelectiveLruArgs); }
+
+size_t semx_selective_lru_ckpt_bytes(const SemxSelectiveLruArgs* a) {
+  if (a == nullptr || a->chunk <= 0 || a->S < 0 || a->L < 0 || a->C < 0 || a->N < 0) return 0;
+  return (size_t)a->S * (size_t)semx::cdiv(a->L, a->chunk) * (size_t)a->C * (size_t)a->N *
+         (a->real ? 1 : 2) * sizeof(float);
+}
+
+size_t semx_selective_lru_workspace_bytes(const SemxSelectiveLruArgs* a) {
+  if (a == nullptr || a->S < 0 || a->L < 0 || a->C < 0 || a->N < 0) return 0;
+  return (part_floats(a) + group_floats(a) + dbc_floats(a)) * sizeof(float);
+}
+
+int semx_selective_lru_fwd(const SemxSelectiveLruArgs* a, semx_stream_t stream) {
+  SEMX_CHECK_ARGS(a, SemxSelectiveLruArgs);
+  int rc = validate(a, false);
+  if (rc != SEMX_OK) return rc;
+  if (a->S * a->C == 0) return SEMX_OK;
+  const SParams p = to_params(a);
+  const Geometry g = geometry(a);
+  return dispatch(false, a, p, g, 0, semx::as_stream(stream));
+}
+
+int semx_selective_lru_bwd(const SemxSelectiveLruArgs* a, semx_stream_t stream) {
+  SEMX_CHECK_ARGS(a, SemxSelectiveLruArgs);
+  int rc = validate(a, true);
+  if (rc != SEMX_OK) return rc;
+  cudaStream_t st = semx::as_stream(stream);
+  SParams p = to_params(a);
+  const Geometry g = geometry(a);
+  const int64_t K = 4 * a->C * a->N + a->C;
+  if (a->S * a->C > 0) {
+    float* ws = reinterpret_cast<float*>(a->workspace);
+    p.part = ws;
+    p.dbc_part = ws + part_floats(a) + group_floats(a);
+    rc = dispatch(true, a, p, g, bwd_smem(a, g.ng), st);
+    if (rc != SEMX_OK) return rc;
+    if (g.nclusters > 1 && a->S * a->L * a->N > 0) {
+      const int narr = a->real ? 2 : 4;
+      const int64_t total = a->S * a->L * narr * a->N;
+      dbc_sum_kernel<<<(unsigned)semx::cdiv(total, 256), 256, 0, st>>>(p, narr);
+      rc = semx::check_launch("dbc_sum_kernel");
+      if (rc != SEMX_OK) return rc;
+    }
+    const int64_t G = semx::cdiv(a->S, kRowsPerGroup);
+    float* gsum = ws + part_floats(a);
+    colsum_stage1<<<dim3((unsigned)semx::cdiv(K, 256), (unsigned)G), 256, 0, st>>>(ws, a->S, K, gsum);
+    rc = semx::check_launch("colsum_stage1");
+    if (rc != SEMX_OK) return rc;
+    Segments seg;
+    const int64_t CN = a->C * a->N;
+    seg.out[0] = a->da;
+    seg.out[1] = a->real ? nullptr : a->domega;
+    seg.out[2] = (a->real || a->s == nullptr) ? nullptr : a->ds;
+    seg.out[3] = a->g ? a->dg : nullptr;
+    seg.out[4] = a->dD;
+    seg.len[0] = seg.len[1] = seg.len[2] = seg.len[3] = CN;
+    seg.len[4] = a->C;
+    colsum_stage2<<<(unsigned)semx::cdiv(K, 256), 256, 0, st>>>(gsum, G, K, seg);
+    return semx::check_launch("colsum_stage2");
+  }
+  return SEMX_OK;
+}
+
+}  // extern "C"

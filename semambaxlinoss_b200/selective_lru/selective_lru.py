@@ -1,0 +1,148 @@
+"""SelectiveLRU (SISO) layer — drop-in for models/selective_lru/selective_lru.py:26-276.
+
+Same constructor, parameter names, registration order, initial values and tags
+(``_no_weight_decay`` / ``_no_reinit``), so reference ``state_dict``s load and equal
+seeds give equal parameters. Forward contract: (batch, time, d_model) ->
+(batch, time, d_model) [+ final state]. The token projections are cuBLAS GEMMs; the
+discretisation, scan, readout, envelope and D skip run in the fused sm_100a scan
+(:func:`fused_selective_lru`), whose backward recomputes states chunk by chunk.
+
+There is one execution path (the CUDA scan). ``use_triton`` is kept for API
+compatibility; ``chunk_size`` is the checkpoint interval of the backward recompute
+(default 64: memory traffic only, never results); ``block_c`` is accepted and unused.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn.functional as F
+from torch import nn
+
+from .scan import fused_selective_lru
+
+GAINS = ("gamma", "mamba", "zoh")
+
+
+def _inv_softplus(x: torch.Tensor) -> torch.Tensor:
+    """Inverse of softplus for x > 0 (stable form): x + log(-expm1(-x))."""
+    return x + torch.log(-torch.expm1(-x))
+
+
+def _phase_grid(n_modes: int, n_real_modes: int, theta_max: float) -> torch.Tensor:
+    """``n_real_modes`` zero phases, then oscillators evenly spaced on (0, theta_max]."""
+    n_osc = n_modes - n_real_modes
+    return torch.cat([
+        torch.zeros(n_real_modes),
+        torch.linspace(theta_max / max(n_osc, 1), theta_max, n_osc),
+    ])
+
+
+class SelectiveLRU(nn.Module):
+    """SISO selective SSM with a bank of complex oscillators per channel.
+
+    Per channel c and mode n, with selective step ``delta_nu > 0`` and detuning
+    ``delta_theta`` (per token and channel, shared over modes)::
+
+        lam = exp(delta_nu * (-a + j (omega + [s] delta_theta)))
+        Bu  = gain * (B_re + j B_im)_t * x_t,   gain in {gamma, mamba, zoh}
+        h_t = lam h_{t-1} + Bu_t
+        y_t = Re(<C_t, h_t>) [+ <g, |h_t|^2>] + D x_t
+    """
+
+    def __init__(
+        self,
+        d_model: int,
+        d_state: int = 16,
+        dt_rank: int | None = None,
+        dt_min: float = 1e-3,
+        dt_max: float = 0.1,
+        theta_max: float = math.pi,
+        n_real_modes: int = 0,
+        envelope_readout: bool = False,
+        mode_detune: bool = False,
+        rate_scale: float = 1.0,
+        input_gain: str = "gamma",
+        use_triton: bool = False,
+        chunk_size: int = 64,
+        block_c: int = 32,
+        device=None,
+        dtype=None,
+    ):
+        super().__init__()
+        if not 0 <= n_real_modes <= d_state:
+            raise ValueError(f"n_real_modes must be in [0, d_state={d_state}], got {n_real_modes}")
+        if input_gain not in GAINS:
+            raise ValueError(f"input_gain must be 'gamma', 'mamba', or 'zoh', got {input_gain!r}")
+        self.input_gain = input_gain
+        self.d_model = d_model
+        self.d_state = d_state
+        self.n_real_modes = n_real_modes
+        self.envelope_readout = envelope_readout
+        self.mode_detune = mode_detune
+        self.rate_scale = float(rate_scale)
+        self.use_triton = use_triton
+        self.chunk_size = chunk_size
+        self.block_c = block_c
+        self.dt_rank = dt_rank if dt_rank is not None else max(1, math.ceil(d_model / 64))
+        r, N = self.dt_rank, d_state
+
+        # One fused token projection: [dt_nu (r) | dt_theta (r) | B_re B_im (2N) | C_re C_im (2N)].
+        self.x_proj = nn.Linear(d_model, 2 * r + 4 * N, bias=False)
+        self.dt_nu_up = nn.Linear(r, d_model, bias=True)
+        self.dt_theta_up = nn.Linear(r, d_model, bias=True)
+
+        # S4D-real decays a = 1..N per channel; phases realised at a log-uniform baseline step.
+        self.A_log = nn.Parameter(torch.log(torch.arange(1, N + 1, dtype=torch.float32).repeat(d_model, 1)))
+        dt = torch.exp(torch.rand(d_model) * (math.log(dt_max) - math.log(dt_min)) + math.log(dt_min))
+        self.omega = nn.Parameter(_phase_grid(N, n_real_modes, theta_max).expand(d_model, N) / dt.unsqueeze(-1))
+        self.D = nn.Parameter(torch.ones(d_model))
+
+        with torch.no_grad():
+            # Low-rank up maps start at zero: delta_theta = 0, delta_nu = softplus(bias) = dt.
+            self.dt_nu_up.weight.zero_()
+            self.dt_theta_up.weight.zero_()
+            self.dt_nu_up.bias.copy_(_inv_softplus(dt))
+            self.dt_theta_up.bias.zero_()
+
+        if envelope_readout:
+            self.env_gain = nn.Parameter(torch.zeros(d_model, N))
+            self.env_gain._no_weight_decay = True
+        if mode_detune:
+            self.detune_gain = nn.Parameter(torch.ones(d_model, N))
+            self.detune_gain._no_weight_decay = True
+
+        self.dt_nu_up.bias._no_reinit = True
+        self.dt_theta_up.bias._no_reinit = True
+        self.A_log._no_weight_decay = True
+        self.omega._no_weight_decay = True
+        self.D._no_weight_decay = True
+
+    def forward(self, x: torch.Tensor, h_init: torch.Tensor | None = None,
+                rate_scale: float | None = None, return_final_state: bool = False):
+        """``h_init``: optional complex (B, C, N) initial state; ``rate_scale``: per-call
+        frame-rate factor on the selective step; ``return_final_state``: also return
+        h_{T-1} as complex (B, C, N) (gradients flow through it)."""
+        r, N = self.dt_rank, self.d_state
+        x = x.float()
+        dnu_r, dth_r, B_sel, C_sel = torch.split(self.x_proj(x), [r, r, 2 * N, 2 * N], dim=-1)
+        delta_nu = F.softplus(self.dt_nu_up(dnu_r))
+        rs = self.rate_scale if rate_scale is None else float(rate_scale)
+        if rs != 1.0:
+            delta_nu = delta_nu * rs
+        delta_theta = self.dt_theta_up(dth_r)
+        a = torch.exp(self.A_log)
+        g = self.env_gain if self.envelope_readout else None
+        s = self.detune_gain if self.mode_detune else None
+        h0_re = h_init.real if h_init is not None else None
+        h0_im = h_init.imag if h_init is not None else None
+        y, hf_re, hf_im = fused_selective_lru(
+            delta_nu, delta_theta, a, self.omega,
+            B_sel[..., :N], B_sel[..., N:], C_sel[..., :N], C_sel[..., N:],
+            x, self.D, g, s, h0_re, h0_im,
+            block_t=self.chunk_size, want_final_state=return_final_state,
+            input_gain=self.input_gain,
+        )
+        if return_final_state:
+            return y, torch.complex(hf_re, hf_im)
+        return y

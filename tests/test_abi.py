@@ -49,6 +49,13 @@ def test_status_strings_and_validation_without_gpu():
     assert lib.semx_linoss_fwd(ctypes.byref(a), None) == _lib.SEMX_ERR_NULL
     a.variant = 9
     assert lib.semx_linoss_fwd(ctypes.byref(a), None) == _lib.SEMX_ERR_UNSUPPORTED
+    b = _lib.new_args(_lib.SemxSelectiveLruArgs)
+    b.S, b.L, b.C, b.N, b.chunk = 2, 5, 4, 40, 16
+    assert lib.semx_selective_lru_fwd(ctypes.byref(b), None) == _lib.SEMX_ERR_UNSUPPORTED  # N > 32
+    b.N, b.chunk = 4, 6
+    assert lib.semx_selective_lru_fwd(ctypes.byref(b), None) == _lib.SEMX_ERR_UNSUPPORTED  # chunk
+    b.chunk = 8
+    assert lib.semx_selective_lru_fwd(ctypes.byref(b), None) == _lib.SEMX_ERR_NULL
 
 
 def test_size_queries():
@@ -56,4 +63,12 @@ def test_size_queries():
     assert lib.semx_linoss_ckpt_bytes(404, 321, 256, 64) == 404 * 6 * 256 * 16
     a = _lib.new_args(_lib.SemxLinossArgs)
     a.S, a.P = 3, 10
-    assert lib.semx_linoss_workspace_bytes(ctypes.byref(a)) == 3 * 6 * 10 * 4
+    # per-sequence partial rows + one row per group of 32 sequences, 6 sums per oscillator
+    assert lib.semx_linoss_workspace_bytes(ctypes.byref(a)) == (3 + 1) * 6 * 10 * 4
+    b = _lib.new_args(_lib.SemxSelectiveLruArgs)
+    b.S, b.L, b.C, b.N, b.chunk, b.real = 4, 10, 8, 4, 4, 0
+    assert lib.semx_selective_lru_ckpt_bytes(ctypes.byref(b)) == 4 * 3 * 8 * 4 * 2 * 4
+    b.real = 1
+    assert lib.semx_selective_lru_ckpt_bytes(ctypes.byref(b)) == 4 * 3 * 8 * 4 * 4
+    # partials (S rows of 4*C*N + C) + group sums (1 row per 32 sequences)
+    assert lib.semx_selective_lru_workspace_bytes(ctypes.byref(b)) == (4 + 1) * (4 * 8 * 4 + 8) * 4

@@ -214,6 +214,82 @@ size_t semx_selective_lru_workspace_bytes(const SemxSelectiveLruArgs* args);
 int semx_selective_lru_fwd(const SemxSelectiveLruArgs* args, semx_stream_t stream);
 int semx_selective_lru_bwd(const SemxSelectiveLruArgs* args, semx_stream_t stream);
 
+/* ------------------------------------------------------------------------------------
+ * Plain complex diagonal scan h_t = lam_t h_{t-1} + Bu_t, h_{-1} = 0, on split real /
+ * imaginary (S,L,N) fp32 tensors. Replaces selective_scan_triton_real /
+ * SelectiveScanRealFunction (models/selective_lru/selective_lru_mimo_triton.py:105-211)
+ * and _selective_recurrence (models/selective_lru/selective_lru.py:590-599).
+ * Backward takes the forward's h and the upstream gradient dh and writes dlam, dBu.
+ * ---------------------------------------------------------------------------------- */
+typedef struct SemxComplexScanArgs {
+  uint32_t struct_size;
+  int32_t reserved;
+  int64_t S, L, N;
+  const float* lam_re;
+  const float* lam_im;
+  const float* Bu_re;
+  const float* Bu_im;
+  float* h_re; /* forward output; backward input */
+  float* h_im;
+  const float* dh_re;
+  const float* dh_im;
+  float* dlam_re;
+  float* dlam_im;
+  float* dBu_re;
+  float* dBu_im;
+} SemxComplexScanArgs;
+
+size_t semx_complex_scan_args_size(void);
+int semx_complex_scan_fwd(const SemxComplexScanArgs* args, semx_stream_t stream);
+int semx_complex_scan_bwd(const SemxComplexScanArgs* args, semx_stream_t stream);
+
+/* ------------------------------------------------------------------------------------
+ * MIMO scan with block-diagonal readout and D skip: for every head h of H heads with
+ * Nh modes and Fh channels,
+ *   h_t = lam_t h_{t-1} + Bu_t                         (modes h*Nh .. h*Nh+Nh-1)
+ *   y_t[h*Fh + f] = sum_n Re(C[h,f,n] h_t[n]) + D[h*Fh + f] x_t[h*Fh + f].
+ * lam, Bu, h: (S,L,H*Nh) split re/im; C_re, C_im: (H,Fh,Nh); x, y, dy, dx: (S,L,H*Fh).
+ * Replaces fused_selective_lru_mimo / _FusedSelectiveLRUMIMO
+ * (models/selective_lru/selective_lru_mimo_triton.py:370-462) and the scan + readout of
+ * SelectiveLRUMIMO.forward (models/selective_lru/selective_lru.py:550-574).
+ * Forward writes y and the state trajectory h. Backward takes h, dy and optionally dh
+ * (a gradient on h from feedthrough terms) and writes dlam, dBu, dx, dC_re, dC_im, dD
+ * (dC and dD reduced over (S, L) in a fixed order).
+ * ---------------------------------------------------------------------------------- */
+typedef struct SemxMimoArgs {
+  uint32_t struct_size;
+  int32_t reserved;
+  int64_t S, L, H, Nh, Fh;
+  const float* lam_re;
+  const float* lam_im;
+  const float* Bu_re;
+  const float* Bu_im;
+  const float* C_re;
+  const float* C_im;
+  const float* x;
+  const float* D;
+  float* y;
+  float* h_re; /* forward output; backward input */
+  float* h_im;
+  const float* dy;
+  const float* dh_re; /* optional */
+  const float* dh_im;
+  float* dlam_re;
+  float* dlam_im;
+  float* dBu_re;
+  float* dBu_im;
+  float* dx;
+  float* dC_re;
+  float* dC_im;
+  float* dD;
+  void* workspace; /* semx_mimo_workspace_bytes(), backward only */
+} SemxMimoArgs;
+
+size_t semx_mimo_args_size(void);
+size_t semx_mimo_workspace_bytes(const SemxMimoArgs* args);
+int semx_mimo_fwd(const SemxMimoArgs* args, semx_stream_t stream);
+int semx_mimo_bwd(const SemxMimoArgs* args, semx_stream_t stream);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

@@ -96,10 +96,41 @@ class SemxSelectiveLruArgs(ctypes.Structure):
     )]
 
 
+class SemxComplexScanArgs(ctypes.Structure):
+    _fields_ = [
+        ("struct_size", ctypes.c_uint32),
+        ("reserved", ctypes.c_int32),
+        ("S", ctypes.c_int64),
+        ("L", ctypes.c_int64),
+        ("N", ctypes.c_int64),
+    ] + [(name, ctypes.c_void_p) for name in (
+        "lam_re", "lam_im", "Bu_re", "Bu_im", "h_re", "h_im", "dh_re", "dh_im",
+        "dlam_re", "dlam_im", "dBu_re", "dBu_im",
+    )]
+
+
+class SemxMimoArgs(ctypes.Structure):
+    _fields_ = [
+        ("struct_size", ctypes.c_uint32),
+        ("reserved", ctypes.c_int32),
+        ("S", ctypes.c_int64),
+        ("L", ctypes.c_int64),
+        ("H", ctypes.c_int64),
+        ("Nh", ctypes.c_int64),
+        ("Fh", ctypes.c_int64),
+    ] + [(name, ctypes.c_void_p) for name in (
+        "lam_re", "lam_im", "Bu_re", "Bu_im", "C_re", "C_im", "x", "D", "y", "h_re", "h_im",
+        "dy", "dh_re", "dh_im", "dlam_re", "dlam_im", "dBu_re", "dBu_im", "dx", "dC_re",
+        "dC_im", "dD", "workspace",
+    )]
+
+
 # (python struct, C size query) for every argument struct in semx.h.
 STRUCTS = {
     "SemxLinossArgs": (SemxLinossArgs, "semx_linoss_args_size"),
     "SemxSelectiveLruArgs": (SemxSelectiveLruArgs, "semx_selective_lru_args_size"),
+    "SemxComplexScanArgs": (SemxComplexScanArgs, "semx_complex_scan_args_size"),
+    "SemxMimoArgs": (SemxMimoArgs, "semx_mimo_args_size"),
 }
 
 # Every symbol semx.h declares, with its ctypes signature.
@@ -123,6 +154,15 @@ _SIGNATURES = {
         ctypes.c_int, [ctypes.POINTER(SemxSelectiveLruArgs), ctypes.c_void_p]),
     "semx_selective_lru_bwd": (
         ctypes.c_int, [ctypes.POINTER(SemxSelectiveLruArgs), ctypes.c_void_p]),
+    "semx_complex_scan_args_size": (ctypes.c_size_t, []),
+    "semx_complex_scan_fwd": (
+        ctypes.c_int, [ctypes.POINTER(SemxComplexScanArgs), ctypes.c_void_p]),
+    "semx_complex_scan_bwd": (
+        ctypes.c_int, [ctypes.POINTER(SemxComplexScanArgs), ctypes.c_void_p]),
+    "semx_mimo_args_size": (ctypes.c_size_t, []),
+    "semx_mimo_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(SemxMimoArgs)]),
+    "semx_mimo_fwd": (ctypes.c_int, [ctypes.POINTER(SemxMimoArgs), ctypes.c_void_p]),
+    "semx_mimo_bwd": (ctypes.c_int, [ctypes.POINTER(SemxMimoArgs), ctypes.c_void_p]),
 }
 
 _lib = None

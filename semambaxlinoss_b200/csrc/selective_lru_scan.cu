@@ -30,6 +30,7 @@
 #include <cooperative_groups.h>
 
 #include "semx_common.cuh"
+#include "semx_reduce.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -40,7 +41,6 @@ constexpr int kGM = 4;   // modes per thread
 constexpr int kR = 4;    // steps per register-resident sub-block (backward)
 constexpr int kTT = 16;  // steps per dB/dC reduction tile (backward)
 constexpr int kMaxClusterCTAs = 8;
-constexpr int kRowsPerGroup = 32;  // column-sum stage 1 group size
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct SParams {
@@ -628,40 +628,6 @@ __global__ void __launch_bounds__(kThreads) slru_bwd_kernel(const SParams p) {
 }
 
 // --------------------------------------------------------------------- reductions
-// Stage 1: group_sums[grp][k] = sum of rows[r][k] over the rows of group grp, in order.
-__global__ void colsum_stage1(const float* __restrict__ rows, int64_t S, int64_t K,
-                              float* __restrict__ group_sums) {
-  const int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (k >= K) return;
-  const int64_t r0 = (int64_t)blockIdx.y * kRowsPerGroup;
-  const int64_t r1 = min(r0 + kRowsPerGroup, S);
-  float acc = 0.f;
-  for (int64_t r = r0; r < r1; ++r) acc += rows[r * K + k];
-  group_sums[(int64_t)blockIdx.y * K + k] = acc;
-}
-
-struct Segments {
-  float* out[5];
-  int64_t len[5];
-};
-
-// Stage 2: out segment <- sum over groups (in order); NULL segments are skipped.
-__global__ void colsum_stage2(const float* __restrict__ group_sums, int64_t G, int64_t K,
-                              Segments seg) {
-  const int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (k >= K) return;
-  int64_t off = k;
-  int which = 0;
-  while (which < 5 && off >= seg.len[which]) {
-    off -= seg.len[which];
-    ++which;
-  }
-  if (which >= 5 || seg.out[which] == nullptr) return;
-  float acc = 0.f;
-  for (int64_t q = 0; q < G; ++q) acc += group_sums[q * K + k];
-  seg.out[which][off] = acc;
-}
-
 // dB / dC over cluster groups when one cluster cannot span all channel blocks.
 __global__ void dbc_sum_kernel(const SParams p, int narr) {
   const int64_t total = p.S * p.L * narr * p.N;
@@ -821,7 +787,7 @@ size_t part_floats(const SemxSelectiveLruArgs* a) {
   return (size_t)a->S * (size_t)(4 * a->C * a->N + a->C);
 }
 size_t group_floats(const SemxSelectiveLruArgs* a) {
-  return (size_t)semx::cdiv(a->S, kRowsPerGroup) * (size_t)(4 * a->C * a->N + a->C);
+  return semx::colsum_group_floats(a->S, 4 * a->C * a->N + a->C);
 }
 size_t dbc_floats(const SemxSelectiveLruArgs* a) {
   const Geometry g = geometry(a);
@@ -937,13 +903,10 @@ int semx_selective_lru_bwd(const SemxSelectiveLruArgs* a, semx_stream_t stream) 
       rc = semx::check_launch("dbc_sum_kernel");
       if (rc != SEMX_OK) return rc;
     }
-    const int64_t G = semx::cdiv(a->S, kRowsPerGroup);
     float* gsum = ws + part_floats(a);
-    colsum_stage1<<<dim3((unsigned)semx::cdiv(K, 256), (unsigned)G), 256, 0, st>>>(ws, a->S, K, gsum);
-    rc = semx::check_launch("colsum_stage1");
-    if (rc != SEMX_OK) return rc;
-    Segments seg;
+    semx::Segments seg = {};
     const int64_t CN = a->C * a->N;
+    seg.n = 5;
     seg.out[0] = a->da;
     seg.out[1] = a->real ? nullptr : a->domega;
     seg.out[2] = (a->real || a->s == nullptr) ? nullptr : a->ds;
@@ -951,8 +914,7 @@ int semx_selective_lru_bwd(const SemxSelectiveLruArgs* a, semx_stream_t stream) 
     seg.out[4] = a->dD;
     seg.len[0] = seg.len[1] = seg.len[2] = seg.len[3] = CN;
     seg.len[4] = a->C;
-    colsum_stage2<<<(unsigned)semx::cdiv(K, 256), 256, 0, st>>>(gsum, G, K, seg);
-    return semx::check_launch("colsum_stage2");
+    return semx::colsum(ws, a->S, K, gsum, seg, st);
   }
   return SEMX_OK;
 }

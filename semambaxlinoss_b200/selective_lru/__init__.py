@@ -1,5 +1,16 @@
 """Selective-LRU layers and scan operators (drop-in for the reference's models/selective_lru)."""
+from .mimo import (
+    fused_selective_lru_mimo,
+    selective_scan,
+    selective_scan_real,
+    selective_scan_triton,
+    selective_scan_triton_real,
+)
 from .scan import fused_selective_lru, fused_selective_lru_real
-from .selective_lru import SelectiveLRU
+from .selective_lru import SelectiveLRU, SelectiveLRUMIMO
 
-__all__ = ["SelectiveLRU", "fused_selective_lru", "fused_selective_lru_real"]
+__all__ = [
+    "SelectiveLRU", "SelectiveLRUMIMO", "fused_selective_lru", "fused_selective_lru_real",
+    "fused_selective_lru_mimo", "selective_scan", "selective_scan_real",
+    "selective_scan_triton", "selective_scan_triton_real",
+]

@@ -1,0 +1,132 @@
+"""Complex diagonal scan and MIMO scan + readout operators backed by libsemx.
+
+* :func:`selective_scan_real` / :func:`selective_scan` — the reference operators
+  ``selective_scan_triton_real`` / ``selective_scan_triton``
+  (models/selective_lru/selective_lru_mimo_triton.py:178-211): h_t = lam_t h_{t-1} + Bu_t
+  on split real/imaginary (B, T, N) tensors (or complex tensors), h_{-1} = 0.
+* :func:`fused_selective_lru_mimo` — the reference operator of the same name
+  (models/selective_lru/selective_lru_mimo_triton.py:441-462): scan + block-diagonal
+  readout Re(C h) + D x, returning ``(y, h_re, h_im)``.
+
+The reference names with the ``_triton`` suffix are exported as aliases for drop-in use.
+CUDA tensors only (RuntimeError otherwise); ValueError on shape mismatch.
+"""
+from __future__ import annotations
+
+import torch
+
+from .. import _lib
+
+
+def _f32(t):
+    return None if t is None else t.detach().to(torch.float32).contiguous()
+
+
+class _ComplexScan(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, lam_re, lam_im, Bu_re, Bu_im):
+        for t in (lam_re, lam_im, Bu_re, Bu_im):
+            if not t.is_cuda:
+                raise RuntimeError("selective_scan requires CUDA tensors.")
+        if lam_re.shape != Bu_re.shape or lam_im.shape != Bu_im.shape or lam_re.shape != lam_im.shape:
+            raise ValueError(f"lam {tuple(lam_re.shape)} != Bu {tuple(Bu_re.shape)}")
+        S, L, N = lam_re.shape
+        ins = [_f32(t) for t in (lam_re, lam_im, Bu_re, Bu_im)]
+        h_re = torch.empty_like(ins[0])
+        h_im = torch.empty_like(ins[0])
+        a = _lib.new_args(_lib.SemxComplexScanArgs)
+        a.S, a.L, a.N = S, L, N
+        a.lam_re, a.lam_im, a.Bu_re, a.Bu_im = [t.data_ptr() for t in ins]
+        a.h_re, a.h_im = h_re.data_ptr(), h_im.data_ptr()
+        _lib.call("semx_complex_scan_fwd", a, lam_re.device)
+        ctx.save_for_backward(ins[0], ins[1], h_re, h_im)
+        return h_re, h_im
+
+    @staticmethod
+    def backward(ctx, dh_re, dh_im):
+        lam_re, lam_im, h_re, h_im = ctx.saved_tensors
+        S, L, N = lam_re.shape
+        dh_re = torch.zeros_like(h_re) if dh_re is None else _f32(dh_re)
+        dh_im = torch.zeros_like(h_im) if dh_im is None else _f32(dh_im)
+        outs = [torch.empty_like(lam_re) for _ in range(4)]
+        a = _lib.new_args(_lib.SemxComplexScanArgs)
+        a.S, a.L, a.N = S, L, N
+        a.lam_re, a.lam_im, a.h_re, a.h_im = [t.data_ptr() for t in (lam_re, lam_im, h_re, h_im)]
+        a.dh_re, a.dh_im = dh_re.data_ptr(), dh_im.data_ptr()
+        a.dlam_re, a.dlam_im, a.dBu_re, a.dBu_im = [t.data_ptr() for t in outs]
+        _lib.call("semx_complex_scan_bwd", a, lam_re.device)
+        return tuple(outs)
+
+
+def selective_scan_real(lam_re, lam_im, Bu_re, Bu_im):
+    """h_k = lam_k h_{k-1} + Bu_k (h_{-1} = 0) on split real/imaginary (B, T, N) tensors.
+    Returns (h_re, h_im)."""
+    return _ComplexScan.apply(lam_re, lam_im, Bu_re, Bu_im)
+
+
+def selective_scan(lam: torch.Tensor, Bu: torch.Tensor) -> torch.Tensor:
+    """Complex-tensor form of :func:`selective_scan_real`: (B, T, N) complex64 -> h."""
+    h_re, h_im = selective_scan_real(lam.real, lam.imag, Bu.real, Bu.imag)
+    return torch.complex(h_re, h_im)
+
+
+selective_scan_triton_real = selective_scan_real
+selective_scan_triton = selective_scan
+
+
+class _FusedMIMO(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, lam_re, lam_im, Bu_re, Bu_im, C_re, C_im, x, D, H, Nh, Fh):
+        for t in (lam_re, lam_im, Bu_re, Bu_im, C_re, C_im, x, D):
+            if not t.is_cuda:
+                raise RuntimeError("fused_selective_lru_mimo requires CUDA tensors.")
+        S, L, N = lam_re.shape
+        Fd = x.shape[2]
+        if N != H * Nh or Fd != H * Fh or C_re.shape != (H, Fh, Nh):
+            raise ValueError("fused_selective_lru_mimo: head sizes do not match the operands")
+        ins = [_f32(t) for t in (lam_re, lam_im, Bu_re, Bu_im, C_re, C_im, x, D)]
+        y = torch.empty((S, L, Fd), dtype=torch.float32, device=x.device)
+        h_re = torch.empty((S, L, N), dtype=torch.float32, device=x.device)
+        h_im = torch.empty_like(h_re)
+        a = _lib.new_args(_lib.SemxMimoArgs)
+        a.S, a.L, a.H, a.Nh, a.Fh = S, L, H, Nh, Fh
+        (a.lam_re, a.lam_im, a.Bu_re, a.Bu_im, a.C_re, a.C_im, a.x, a.D) = [t.data_ptr() for t in ins]
+        a.y, a.h_re, a.h_im = y.data_ptr(), h_re.data_ptr(), h_im.data_ptr()
+        _lib.call("semx_mimo_fwd", a, x.device)
+        ctx.save_for_backward(ins[0], ins[1], h_re, h_im, ins[4], ins[5], ins[6], ins[7])
+        ctx.dims = (S, L, H, Nh, Fh)
+        return y, h_re, h_im
+
+    @staticmethod
+    def backward(ctx, dy, dh_re, dh_im):
+        lam_re, lam_im, h_re, h_im, C_re, C_im, x, D = ctx.saved_tensors
+        S, L, H, Nh, Fh = ctx.dims
+        dev = x.device
+        dy = torch.zeros_like(x) if dy is None else _f32(dy)
+        if dh_re is not None or dh_im is not None:
+            dh_re = torch.zeros_like(h_re) if dh_re is None else _f32(dh_re)
+            dh_im = torch.zeros_like(h_im) if dh_im is None else _f32(dh_im)
+        dlam_re, dlam_im, dBu_re, dBu_im = [torch.empty_like(h_re) for _ in range(4)]
+        dx = torch.empty_like(x)
+        dC_re, dC_im = torch.empty_like(C_re), torch.empty_like(C_im)
+        dD = torch.empty_like(D)
+        a = _lib.new_args(_lib.SemxMimoArgs)
+        a.S, a.L, a.H, a.Nh, a.Fh = S, L, H, Nh, Fh
+        a.lam_re, a.lam_im, a.C_re, a.C_im = [t.data_ptr() for t in (lam_re, lam_im, C_re, C_im)]
+        a.x, a.D, a.h_re, a.h_im, a.dy = [t.data_ptr() for t in (x, D, h_re, h_im, dy)]
+        a.dh_re, a.dh_im = _lib.ptr(dh_re), _lib.ptr(dh_im)
+        a.dlam_re, a.dlam_im, a.dBu_re, a.dBu_im = [t.data_ptr() for t in (dlam_re, dlam_im, dBu_re, dBu_im)]
+        a.dx, a.dC_re, a.dC_im, a.dD = [t.data_ptr() for t in (dx, dC_re, dC_im, dD)]
+        ws = _lib.empty_f32(_lib.load().semx_mimo_workspace_bytes(a), dev)
+        a.workspace = ws.data_ptr()
+        _lib.call("semx_mimo_bwd", a, dev)
+        return dlam_re, dlam_im, dBu_re, dBu_im, dC_re, dC_im, dx, dD, None, None, None
+
+
+def fused_selective_lru_mimo(lam_re, lam_im, Bu_re, Bu_im, C_re, C_im, x, D, n_heads, n_head, f_head):
+    """Fused MIMO scan + block-diagonal readout + D skip. ``lam``/``Bu`` are the (B, T, N)
+    halves (N = n_heads * n_head), ``C_re``/``C_im`` the (n_heads, f_head, n_head) readout
+    halves, ``x`` the (B, T, Fd) input (Fd = n_heads * f_head) and ``D`` (Fd,). Returns
+    ``(y, h_re, h_im)`` with y = Re(C h) + D x and the (B, T, N) state halves."""
+    return _FusedMIMO.apply(lam_re, lam_im, Bu_re, Bu_im, C_re, C_im, x, D,
+                            int(n_heads), int(n_head), int(f_head))

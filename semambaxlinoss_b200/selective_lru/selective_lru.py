@@ -146,3 +146,179 @@ class SelectiveLRU(nn.Module):
         if return_final_state:
             return y, torch.complex(hf_re, hf_im)
         return y
+
+
+def _uniform_init(shape, std: float = 1.0) -> torch.Tensor:
+    return torch.empty(*shape).uniform_(-std, std)
+
+
+class SelectiveLRUMIMO(nn.Module):
+    """Multi-head selective MIMO SSM (drop-in for
+    models/selective_lru/selective_lru.py:279-587).
+
+    One bank of ``state_dim`` complex modes split block-diagonally over ``n_heads`` heads;
+    head h owns ``state_dim / n_heads`` modes driven by (and read out to) its
+    ``in_features / n_heads`` channels through static complex B / C. Per (token, head):
+    selective step ``delta_nu`` and detune ``delta_theta``; poles
+    ``exp(delta_nu (-a + j (omega + [s] delta_theta)))``; drive
+    ``gain * (B_static x [+ rank-r write])`` with gain in {gamma, mamba, zoh, none};
+    readout ``Re(C h) [+ <g, |h|^2>] + D x [+ rank-r read]``.
+
+    Same constructor, parameter names, registration order, initial values and tags as the
+    reference. The scan + readout + D skip run in the sm_100a MIMO kernel
+    (:func:`fused_selective_lru_mimo`); the pole / drive construction and the rank /
+    envelope feedthrough terms are evaluated around it.
+    """
+
+    def __init__(
+        self,
+        in_features: int,
+        state_dim: int = 16,
+        n_heads: int = 1,
+        rank: int = 0,
+        dt_min: float = 1e-3,
+        dt_max: float = 0.1,
+        theta_max: float = math.pi,
+        n_real_modes: int = 0,
+        envelope_readout: bool = False,
+        mode_detune: bool = False,
+        rate_scale: float = 1.0,
+        selective_init_std: float = 1e-2,
+        input_gain: str = "gamma",
+        normalize_input: bool | None = None,
+        use_triton: bool = False,
+    ):
+        super().__init__()
+        if in_features % n_heads != 0:
+            raise ValueError(f"in_features={in_features} not divisible by n_heads={n_heads}")
+        if state_dim % n_heads != 0:
+            raise ValueError(f"state_dim={state_dim} not divisible by n_heads={n_heads}")
+        if not 0 <= n_real_modes <= state_dim // n_heads:
+            raise ValueError(
+                f"n_real_modes must be in [0, state_dim/n_heads={state_dim // n_heads}], "
+                f"got {n_real_modes}"
+            )
+        if input_gain not in ("gamma", "mamba", "zoh", "none"):
+            raise ValueError(
+                f"input_gain must be 'gamma', 'mamba', 'zoh', or 'none', got {input_gain!r}"
+            )
+        self.in_features = in_features
+        self.state_dim = state_dim
+        self.n_heads = n_heads
+        self.rank = rank
+        self.n_real_modes = n_real_modes
+        self.envelope_readout = envelope_readout
+        self.mode_detune = mode_detune
+        self.rate_scale = float(rate_scale)
+        self.input_gain = input_gain
+        self.use_triton = use_triton
+        self.f_head = in_features // n_heads
+        self.n_head = state_dim // n_heads
+        H, Nh, Fh = n_heads, self.n_head, self.f_head
+
+        self.dt_nu_proj = nn.Linear(in_features, H, bias=True)
+        self.dt_theta_proj = nn.Linear(in_features, H, bias=True)
+        self.A_log = nn.Parameter(torch.log(torch.arange(1, Nh + 1, dtype=torch.float32).repeat(H, 1)))
+        dt = torch.exp(torch.rand(H) * (math.log(dt_max) - math.log(dt_min)) + math.log(dt_min))
+        self.omega = nn.Parameter(_phase_grid(Nh, n_real_modes, theta_max).expand(H, Nh) / dt.unsqueeze(-1))
+        self.B = nn.Parameter(_uniform_init((H, Nh, Fh, 2), std=1.0 / math.sqrt(Fh)))
+        self.C = nn.Parameter(_uniform_init((H, Fh, Nh, 2), std=1.0 / math.sqrt(Nh)))
+        self.D = nn.Parameter(torch.ones(in_features))
+        if rank > 0:
+            self.b_dir = nn.Linear(in_features, H * rank * Nh, bias=False)
+            self.b_coef = nn.Linear(in_features, H * rank, bias=False)
+            self.c_read = nn.Linear(in_features, 2 * H * rank * Nh, bias=False)
+            self.c_coef = nn.Linear(in_features, H * rank, bias=False)
+            # (H * rank, Fh) rather than (H, rank, Fh): unambiguous gradient strides for DDP.
+            self.c_out = nn.Parameter(_uniform_init((H * rank, Fh), std=1.0 / math.sqrt(Fh)))
+
+        with torch.no_grad():
+            self.dt_nu_proj.weight.zero_()
+            self.dt_theta_proj.weight.zero_()
+            self.dt_nu_proj.bias.copy_(_inv_softplus(dt))
+            self.dt_theta_proj.bias.zero_()
+            if rank > 0:
+                self.b_dir.weight.normal_(0.0, 1.0 / math.sqrt(in_features))
+                self.c_read.weight.normal_(0.0, 1.0 / math.sqrt(in_features))
+                coef_std = selective_init_std / math.sqrt(in_features)
+                self.b_coef.weight.normal_(0.0, coef_std)
+                self.c_coef.weight.normal_(0.0, coef_std)
+
+        if envelope_readout:
+            self.env_gain = nn.Parameter(torch.zeros(H, Fh, Nh))
+            self.env_gain._no_weight_decay = True
+        if mode_detune:
+            self.detune_gain = nn.Parameter(torch.ones(H, Nh))
+            self.detune_gain._no_weight_decay = True
+
+        self.dt_nu_proj.bias._no_reinit = True
+        self.dt_theta_proj.bias._no_reinit = True
+        self.A_log._no_weight_decay = True
+        self.omega._no_weight_decay = True
+        self.D._no_weight_decay = True
+
+    def _poles_and_drive(self, x, delta_nu, delta_theta):
+        """(lam_re, lam_im, Bu_re, Bu_im), each (B, T, N): exact-ZOH poles and the gained
+        drive (static block-diagonal B x plus the rank-r write)."""
+        Bsz, T, _ = x.shape
+        H, Nh, N = self.n_heads, self.n_head, self.state_dim
+        a = torch.exp(self.A_log)
+        dnu = delta_nu.unsqueeze(-1)
+        dth = delta_theta.unsqueeze(-1)
+        nu = torch.exp(-dnu * a)
+        base = self.omega + (self.detune_gain * dth if self.mode_detune else dth)
+        theta = dnu * base
+        cos, sin = torch.cos(theta), torch.sin(theta)
+        lam_re = (nu * cos).reshape(Bsz, T, N)
+        lam_im = (nu * sin).reshape(Bsz, T, N)
+        xh = x.view(Bsz, T, H, self.f_head)
+        Bu_re = torch.einsum("hnf,bthf->bthn", self.B[..., 0], xh)
+        Bu_im = torch.einsum("hnf,bthf->bthn", self.B[..., 1], xh)
+        if self.rank > 0:
+            s_b = self.b_coef(x).view(Bsz, T, H, self.rank)
+            b_t = self.b_dir(x).view(Bsz, T, H, self.rank, Nh)
+            Bu_re = Bu_re + torch.einsum("bthr,bthrn->bthn", s_b, b_t)
+        if self.input_gain == "gamma":
+            gain = torch.sqrt((1.0 - nu * nu).clamp_min(1e-6))
+            Bu_re, Bu_im = Bu_re * gain, Bu_im * gain
+        elif self.input_gain == "mamba":
+            Bu_re, Bu_im = Bu_re * dnu, Bu_im * dnu
+        elif self.input_gain == "zoh":
+            lm1_re = torch.expm1(-dnu * a) * cos - 2.0 * torch.sin(0.5 * theta).square()
+            lm1_im = nu * sin
+            den = (a * a + base * base).clamp_min(1e-8)
+            g_re = (base * lm1_im - a * lm1_re) / den
+            g_im = -(a * lm1_im + base * lm1_re) / den
+            Bu_re, Bu_im = g_re * Bu_re - g_im * Bu_im, g_re * Bu_im + g_im * Bu_re
+        return lam_re, lam_im, Bu_re.reshape(Bsz, T, N), Bu_im.reshape(Bsz, T, N)
+
+    def forward(self, x: torch.Tensor, rate_scale: float | None = None) -> torch.Tensor:
+        from .mimo import fused_selective_lru_mimo
+
+        x = x.float()
+        Bsz, T, Fdim = x.shape
+        H, Nh = self.n_heads, self.n_head
+        delta_nu = F.softplus(self.dt_nu_proj(x))
+        rs = self.rate_scale if rate_scale is None else float(rate_scale)
+        if rs != 1.0:
+            delta_nu = delta_nu * rs
+        delta_theta = self.dt_theta_proj(x)
+        lam_re, lam_im, Bu_re, Bu_im = self._poles_and_drive(x, delta_nu, delta_theta)
+        y, h_re, h_im = fused_selective_lru_mimo(
+            lam_re, lam_im, Bu_re, Bu_im, self.C[..., 0], self.C[..., 1], x, self.D,
+            H, Nh, self.f_head,
+        )
+        if self.envelope_readout or self.rank > 0:
+            hr = h_re.view(Bsz, T, H, Nh)
+            hi = h_im.view(Bsz, T, H, Nh)
+            if self.envelope_readout:
+                power = hr * hr + hi * hi
+                y = y + torch.einsum("hfn,bthn->bthf", self.env_gain, power).reshape(Bsz, T, Fdim)
+            if self.rank > 0:
+                s_c = self.c_coef(x).view(Bsz, T, H, self.rank)
+                cr = self.c_read(x).view(Bsz, T, H, self.rank, 2 * Nh)
+                read = (torch.einsum("bthrn,bthn->bthr", cr[..., :Nh], hr)
+                        - torch.einsum("bthrn,bthn->bthr", cr[..., Nh:], hi))
+                c_out = self.c_out.view(H, self.rank, self.f_head)
+                y = y + torch.einsum("bthr,hrf->bthf", s_c * read, c_out).reshape(Bsz, T, Fdim)
+        return y

@@ -28,10 +28,10 @@ def test_complex_scan_matches_oracle(B, T, N):
     gh = crandn((B, T, N), g)
 
     def run(fn, dev, dtype):
-        n_ = nu.to(dtype).to(dev).requires_grad_(True)
-        th = theta.to(dtype).to(dev).requires_grad_(True)
+        n_ = nu.detach().clone().to(dtype).to(dev).requires_grad_(True)
+        th = theta.detach().clone().to(dtype).to(dev).requires_grad_(True)
         cdt = torch.complex128 if dtype == torch.float64 else torch.complex64
-        b_ = Bu.to(cdt).to(dev).requires_grad_(True)
+        b_ = Bu.detach().clone().to(cdt).to(dev).requires_grad_(True)
         h = fn(torch.polar(n_, th), b_)
         ghd = gh.to(cdt).to(dev)
         (h.real * ghd.real + h.imag * ghd.imag).sum().backward()

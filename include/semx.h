@@ -15,10 +15,12 @@
  *     documented shape.
  *   - The first field of every argument struct is `struct_size`, which the caller sets to
  *     sizeof(struct); a mismatch returns SEMX_ERR_ABI.
- *   - Work is enqueued on `stream` (a cudaStream_t passed as an opaque pointer); nothing
- *     synchronises the host. The library keeps no state between calls and allocates no
- *     device memory: scratch comes from the caller through `workspace`, sized by the
- *     matching *_workspace_bytes() query.
+ *   - Work runs on the GPU that owns the operands (found from the first operand pointer
+ *     and made current for the call) and is enqueued on `stream`, a cudaStream_t of that
+ *     GPU passed as an opaque pointer; nothing synchronises the host.
+ *   - The library keeps no state between calls and allocates no device memory: scratch
+ *     comes from the caller through `workspace`, sized by the matching
+ *     *_workspace_bytes() query.
  *   - The return value is SEMX_OK or one of the SEMX_ERR_* codes; no exception crosses
  *     the ABI. semx_last_error() returns a message for the calling host thread.
  *
@@ -48,7 +50,8 @@ enum semx_status {
   SEMX_ERR_UNSUPPORTED = 4,  /* flag combination or size outside what is compiled     */
   SEMX_ERR_ALIGN = 5,        /* a pointer is not aligned as documented                */
   SEMX_ERR_LAUNCH = 6,       /* the CUDA launch itself failed                         */
-  SEMX_ERR_WORKSPACE = 7     /* workspace pointer NULL while workspace is required    */
+  SEMX_ERR_WORKSPACE = 7,    /* workspace pointer NULL while workspace is required    */
+  SEMX_ERR_DEVICE = 8        /* an operand is not device memory                       */
 };
 
 /* ABI version compiled into the library (== SEMX_ABI_VERSION of this header). */
@@ -81,7 +84,7 @@ const char* semx_last_error(void);
  *   fused:   dBu (S,L,P) complex and dparams (3,P) = d steps, d A_diag, d G_diag
  *            (d G_diag row written only for DAMPED_IMEX).
  * Parameter gradients are reduced over (S, L) in a fixed order (deterministic).
- * chunk must be a positive multiple of 8 and at most 512.
+ * chunk must be a positive multiple of 8 and at most 256.
  * ---------------------------------------------------------------------------------- */
 enum semx_linoss_variant {
   SEMX_LINOSS_GENERIC = 0,

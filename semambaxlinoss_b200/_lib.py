@@ -27,6 +27,7 @@ SEMX_ERR_UNSUPPORTED = 4
 SEMX_ERR_ALIGN = 5
 SEMX_ERR_LAUNCH = 6
 SEMX_ERR_WORKSPACE = 7
+SEMX_ERR_DEVICE = 8
 
 # enum semx_linoss_variant
 LINOSS_GENERIC = 0

@@ -670,6 +670,8 @@ int semx_linoss_fwd(const SemxLinossArgs* a, semx_stream_t stream) {
   int rc = validate(a, false);
   if (rc != SEMX_OK) return rc;
   if (a->S * a->P == 0 || a->L == 0) return SEMX_OK;
+  rc = semx::bind_device({a->Y2, a->Bu, a->F1});
+  if (rc != SEMX_OK) return rc;
   const Params p = to_params(a);
   const int64_t n = a->S * a->P;
   const dim3 grid((unsigned)semx::cdiv(n, kBlock));
@@ -683,6 +685,8 @@ int semx_linoss_fwd(const SemxLinossArgs* a, semx_stream_t stream) {
 int semx_linoss_bwd(const SemxLinossArgs* a, semx_stream_t stream) {
   SEMX_CHECK_ARGS(a, SemxLinossArgs);
   int rc = validate(a, true);
+  if (rc != SEMX_OK) return rc;
+  rc = semx::bind_device({a->dBu, a->dF1, a->dparams, a->dM});
   if (rc != SEMX_OK) return rc;
   const Params p = to_params(a);
   cudaStream_t st = semx::as_stream(stream);

@@ -346,6 +346,8 @@ int semx_complex_scan_fwd(const SemxComplexScanArgs* a, semx_stream_t stream) {
   if (a->S * a->L * a->N == 0) return SEMX_OK;
   SEMX_REQUIRE(a->lam_re && a->lam_im && a->Bu_re && a->Bu_im && a->h_re && a->h_im, SEMX_ERR_NULL,
                "complex_scan: NULL operand");
+  int rc = semx::bind_device({a->h_re});
+  if (rc != SEMX_OK) return rc;
   CSParams p = {a->S, a->L, a->N, a->lam_re, a->lam_im, a->Bu_re, a->Bu_im, a->h_re, a->h_im};
   cscan_fwd_kernel<<<(unsigned)semx::cdiv(a->S * a->N, kBlock), kBlock, 0, semx::as_stream(stream)>>>(p);
   return semx::check_launch("cscan_fwd_kernel");
@@ -358,6 +360,8 @@ int semx_complex_scan_bwd(const SemxComplexScanArgs* a, semx_stream_t stream) {
   SEMX_REQUIRE(a->lam_re && a->lam_im && a->h_re && a->h_im && a->dh_re && a->dh_im && a->dlam_re &&
                    a->dlam_im && a->dBu_re && a->dBu_im,
                SEMX_ERR_NULL, "complex_scan bwd: NULL operand");
+  int rc = semx::bind_device({a->dBu_re});
+  if (rc != SEMX_OK) return rc;
   CSParams p = {a->S,   a->L,     a->N,     a->lam_re,  a->lam_im,  a->Bu_re,  a->Bu_im,
                 a->h_re, a->h_im, a->dh_re, a->dh_im,  a->dlam_re, a->dlam_im, a->dBu_re,
                 a->dBu_im};
@@ -390,6 +394,8 @@ int semx_mimo_fwd(const SemxMimoArgs* a, semx_stream_t stream) {
   SEMX_REQUIRE(a->lam_re && a->lam_im && a->Bu_re && a->Bu_im && a->C_re && a->C_im && a->x && a->D &&
                    a->y && a->h_re && a->h_im,
                SEMX_ERR_NULL, "mimo: NULL operand");
+  rc = semx::bind_device({a->y});
+  if (rc != SEMX_OK) return rc;
   MParams p = {};
   p.S = a->S; p.L = a->L; p.H = a->H; p.Nh = a->Nh; p.Fh = a->Fh;
   p.lr = a->lam_re; p.li = a->lam_im; p.br = a->Bu_re; p.bi = a->Bu_im;
@@ -409,6 +415,8 @@ int semx_mimo_bwd(const SemxMimoArgs* a, semx_stream_t stream) {
   const int64_t K = mimo_row(a);
   if (a->S * a->H == 0) return SEMX_OK;
   SEMX_REQUIRE(a->workspace != nullptr, SEMX_ERR_WORKSPACE, "mimo bwd: workspace is NULL");
+  rc = semx::bind_device({a->workspace});
+  if (rc != SEMX_OK) return rc;
   float* ws = reinterpret_cast<float*>(a->workspace);
   if (a->L > 0) {
     SEMX_REQUIRE(a->lam_re && a->lam_im && a->C_re && a->C_im && a->x && a->D && a->h_re && a->h_im &&

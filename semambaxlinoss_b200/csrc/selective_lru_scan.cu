@@ -877,6 +877,8 @@ int semx_selective_lru_fwd(const SemxSelectiveLruArgs* a, semx_stream_t stream) 
   int rc = validate(a, false);
   if (rc != SEMX_OK) return rc;
   if (a->S * a->C == 0) return SEMX_OK;
+  rc = semx::bind_device({a->y, a->delta_nu, a->D});
+  if (rc != SEMX_OK) return rc;
   const SParams p = to_params(a);
   const Geometry g = geometry(a);
   return dispatch(false, a, p, g, 0, semx::as_stream(stream));
@@ -885,6 +887,8 @@ int semx_selective_lru_fwd(const SemxSelectiveLruArgs* a, semx_stream_t stream) 
 int semx_selective_lru_bwd(const SemxSelectiveLruArgs* a, semx_stream_t stream) {
   SEMX_CHECK_ARGS(a, SemxSelectiveLruArgs);
   int rc = validate(a, true);
+  if (rc != SEMX_OK) return rc;
+  rc = semx::bind_device({a->dy, a->D, a->workspace});
   if (rc != SEMX_OK) return rc;
   cudaStream_t st = semx::as_stream(stream);
   SParams p = to_params(a);

@@ -19,6 +19,32 @@ int fail(int code, const char* fmt, ...) {
 
 void clear_error() { g_last_error[0] = '\0'; }
 
+int bind_device(std::initializer_list<const void*> ptrs) {
+  const void* p = nullptr;
+  for (const void* q : ptrs) {
+    if (q != nullptr) {
+      p = q;
+      break;
+    }
+  }
+  if (p == nullptr) return SEMX_OK;
+  cudaPointerAttributes attr;
+  cudaError_t e = cudaPointerGetAttributes(&attr, p);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(SEMX_ERR_DEVICE, "cudaPointerGetAttributes: %s", cudaGetErrorString(e));
+  }
+  if (attr.type != cudaMemoryTypeDevice && attr.type != cudaMemoryTypeManaged)
+    return fail(SEMX_ERR_DEVICE, "operand %p is not device memory", p);
+  int cur = -1;
+  if (cudaGetDevice(&cur) != cudaSuccess || cur != attr.device) {
+    e = cudaSetDevice(attr.device);
+    if (e != cudaSuccess)
+      return fail(SEMX_ERR_DEVICE, "cudaSetDevice(%d): %s", attr.device, cudaGetErrorString(e));
+  }
+  return SEMX_OK;
+}
+
 int check_launch(const char* what) {
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(SEMX_ERR_LAUNCH, "%s: %s", what, cudaGetErrorString(e));
@@ -41,6 +67,7 @@ const char* semx_status_string(int status) {
     case SEMX_ERR_ALIGN: return "misaligned pointer";
     case SEMX_ERR_LAUNCH: return "CUDA launch failed";
     case SEMX_ERR_WORKSPACE: return "workspace missing";
+    case SEMX_ERR_DEVICE: return "operand is not device memory";
     default: return "unknown status";
   }
 }

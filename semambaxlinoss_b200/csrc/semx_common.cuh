@@ -7,6 +7,7 @@
 
 #include <cstdint>
 #include <cstdio>
+#include <initializer_list>
 
 #include "semx.h"
 
@@ -18,6 +19,11 @@ int fail(int code, const char* fmt, ...);
 void clear_error();
 // Converts the pending CUDA error (if any) after a launch into SEMX_ERR_LAUNCH.
 int check_launch(const char* what);
+
+// Makes the GPU that owns the first non-NULL pointer of `ptrs` current for this host
+// thread, so launches (including on a device's legacy default stream) go to the GPU
+// that holds the operands, whichever device the caller's own runtime has current.
+int bind_device(std::initializer_list<const void*> ptrs);
 
 inline bool aligned(const void* p, uintptr_t a) {
   return (reinterpret_cast<uintptr_t>(p) % a) == 0;

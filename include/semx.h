@@ -132,6 +132,23 @@ size_t semx_linoss_workspace_bytes(const SemxLinossArgs* args);
 int semx_linoss_fwd(const SemxLinossArgs* args, semx_stream_t stream);
 int semx_linoss_bwd(const SemxLinossArgs* args, semx_stream_t stream);
 
+/* Backward for callers that cannot allocate device memory. It has no counterpart in the
+ * reference. Some hosts must never call cudaMalloc on the thread that drives the scan: a
+ * real-time audio process callback (cudaMalloc can synchronise the device and stall past
+ * the buffer deadline), or a runtime whose own pool owns all device memory. This entry
+ * point does exactly what semx_linoss_bwd does, but ignores args->workspace and uses a
+ * scratch pool compiled into the library: SEMX_LINOSS_NOALLOC_SCRATCH_BYTES (8 MiB) of
+ * device memory that every GPU which loads the library holds until the process exits.
+ * A call whose semx_linoss_workspace_bytes() exceeds the pool returns SEMX_ERR_SHAPE
+ * without launching. The caller still passes every input and output (ckpt included).
+ * The first call on a device looks up the pool's device address (cudaGetSymbolAddress,
+ * once per device); make that first call before any stream capture. Every call shares
+ * the one pool and nothing in it needs to start at zero (each call overwrites what it
+ * reads), but calls whose work overlaps on the GPU (different streams, or several host
+ * threads) race on it: serialise them. */
+#define SEMX_LINOSS_NOALLOC_SCRATCH_BYTES ((size_t)8 << 20)
+int semx_linoss_bwd_noalloc(const SemxLinossArgs* args, semx_stream_t stream);
+
 /* ------------------------------------------------------------------------------------
  * Selective-LRU SISO scan with readout (one bank of N modes per channel).
  *

@@ -147,6 +147,7 @@ _SIGNATURES = {
     "semx_linoss_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(SemxLinossArgs)]),
     "semx_linoss_fwd": (ctypes.c_int, [ctypes.POINTER(SemxLinossArgs), ctypes.c_void_p]),
     "semx_linoss_bwd": (ctypes.c_int, [ctypes.POINTER(SemxLinossArgs), ctypes.c_void_p]),
+    "semx_linoss_bwd_noalloc": (ctypes.c_int, [ctypes.POINTER(SemxLinossArgs), ctypes.c_void_p]),
     "semx_selective_lru_args_size": (ctypes.c_size_t, []),
     "semx_selective_lru_ckpt_bytes": (ctypes.c_size_t, [ctypes.POINTER(SemxSelectiveLruArgs)]),
     "semx_selective_lru_workspace_bytes": (

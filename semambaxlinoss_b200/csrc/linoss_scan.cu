@@ -22,6 +22,8 @@
 // per chain in registers, written once per chain, and reduced over sequences by
 // linoss_finalize_kernel in a fixed order (bitwise deterministic), which also applies
 // the chain rule from (M, f) back to the raw parameters.
+#include <mutex>
+
 #include "semx_common.cuh"
 
 namespace {
@@ -725,3 +727,57 @@ int semx_linoss_bwd(const SemxLinossArgs* a, semx_stream_t stream) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------------------
+// Backward without caller-provided scratch: the reductions' partial rows live in a fixed
+// pool compiled into the library. In host code the pool's name denotes a host-side shadow
+// variable, not device memory, so its device address is looked up once per device with
+// cudaGetSymbolAddress while that device is current, and that address is what the kernels
+// get.
+namespace {
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[SEMX_LINOSS_NOALLOC_SCRATCH_BYTES];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[kMaxDevices] = {};
+
+// Device address of the pool on the current device (looked up on first use).
+int noalloc_scratch(void** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return semx::fail(SEMX_ERR_LAUNCH, "cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices)
+    return semx::fail(SEMX_ERR_UNSUPPORTED, "linoss noalloc: device %d outside the %d-device table", dev,
+                      kMaxDevices);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_addr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess)
+      return semx::fail(SEMX_ERR_LAUNCH, "cudaGetSymbolAddress(scratch pool): %s", cudaGetErrorString(e));
+    g_noalloc_addr[dev] = p;
+  }
+  *out = g_noalloc_addr[dev];
+  return SEMX_OK;
+}
+
+}  // namespace
+
+extern "C" int semx_linoss_bwd_noalloc(const SemxLinossArgs* a, semx_stream_t stream) {
+  SEMX_CHECK_ARGS(a, SemxLinossArgs);
+  const size_t need = semx_linoss_workspace_bytes(a);
+  SEMX_REQUIRE(need <= SEMX_LINOSS_NOALLOC_SCRATCH_BYTES, SEMX_ERR_SHAPE,
+               "linoss noalloc: S=%lld, P=%lld need %zu B of scratch; the built-in pool holds %zu B "
+               "(use semx_linoss_bwd with a workspace instead)",
+               (long long)a->S, (long long)a->P, need, (size_t)SEMX_LINOSS_NOALLOC_SCRATCH_BYTES);
+  // The pool is looked up on the GPU that owns the outputs; semx_linoss_bwd then
+  // validates the call with the pool in place of the workspace.
+  int rc = semx::bind_device({a->dBu, a->dF1, a->dparams, a->dM});
+  if (rc != SEMX_OK) return rc;
+  SemxLinossArgs b = *a;
+  rc = noalloc_scratch(&b.workspace);
+  if (rc != SEMX_OK) return rc;
+  return semx_linoss_bwd(&b, stream);
+}
+

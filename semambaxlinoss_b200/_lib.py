@@ -13,7 +13,11 @@ from pathlib import Path
 
 import torch
 
-LIB_PATH = Path(__file__).resolve().parent / "libsemx.so"
+import os
+
+# The in-tree library; SEMX_LIB may name another build of the same ABI (e.g. to compare
+# builds side by side).
+LIB_PATH = Path(os.environ.get("SEMX_LIB", Path(__file__).resolve().parent / "libsemx.so"))
 ABI_VERSION = 1
 
 c_f32p = ctypes.POINTER(ctypes.c_float)

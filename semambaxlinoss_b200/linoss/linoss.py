@@ -48,7 +48,7 @@ def _project_input(B_param: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
     is already the interleaved complex layout."""
     P, H, _ = B_param.shape
     W = B_param.permute(0, 2, 1).reshape(2 * P, H)
-    out = torch.matmul(x, W.t())
+    out = torch.matmul(x, W.t()).float()  # fp32 even when autocast ran the GEMM in bf16
     return torch.view_as_complex(out.view(*out.shape[:-1], P, 2))
 
 

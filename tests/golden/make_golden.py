@@ -9,6 +9,7 @@ What runs (all on CPU, float64, through the reference's own modules and function
 * models/linoss/linoss.py          LinOSS (all variants) and _linoss_recurrence
 * models/selective_lru/selective_lru.py  SelectiveLRU (every gain / option),
   SelectiveLRUMIMO (every gain / option, rank > 0) and _selective_recurrence
+* models/mixer.py                  MambaStyleMixer around SelectiveLRU and LinOSS
 
 Usage: python tests/golden/make_golden.py
 """
@@ -38,7 +39,9 @@ def _import_reference():
     spec = importlib.util.spec_from_file_location("ref_linoss", REF / "models/linoss/linoss.py")
     lin = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(lin)
-    return SelectiveLRU, SelectiveLRUMIMO, _selective_recurrence, lin
+    from models.mixer import MambaStyleMixer  # noqa: E402
+
+    return SelectiveLRU, SelectiveLRUMIMO, _selective_recurrence, lin, MambaStyleMixer
 
 
 def _run_module(module, x, fwd_kwargs, seed):
@@ -199,13 +202,42 @@ def recurrence_case(_selective_recurrence):
                                      "grad_h": gh, "grads": list(grads)}}
 
 
+def mixer_cases(MambaStyleMixer, SelectiveLRU, lin):
+    cases = {}
+    specs = [
+        ("selective_lru", dict(d_state=4, input_gain="gamma"), True),
+        ("selective_lru", dict(d_state=8, input_gain="zoh", mode_detune=True), False),
+        ("linoss", dict(state_dim=6, discretization="IMEX", damping=True), True),
+        ("linoss", dict(state_dim=6, discretization="IM", damping=False), True),
+    ]
+    for i, (kind, kw, causal) in enumerate(specs):
+        torch.manual_seed(1100 + i)
+        d, expand = 4, 2
+        if kind == "selective_lru":
+            ssm = SelectiveLRU(d_model=d * expand, **kw)
+        else:
+            ssm = lin.LinOSS(in_features=d * expand, **kw)
+        m = MambaStyleMixer(d, ssm, expand=expand, d_conv=4, causal_conv=causal).double()
+        _perturb(m, seed=1200 + i, scale=0.2)
+        g = torch.Generator().manual_seed(1300 + i)
+        x = torch.randn(2, 13, d, generator=g, dtype=torch.float64)
+        rec = _run_module(m, x, {}, seed=1400 + i)
+        cfg = dict(kw)
+        if kind == "selective_lru":
+            cfg["dt_rank"] = ssm.dt_rank
+        rec["config"] = dict(kind=kind, ssm=cfg, in_features=d, expand=expand, d_conv=4, causal=causal)
+        cases[f"mixer_{i}_{kind}"] = rec
+    return cases
+
+
 def main():
-    SelectiveLRU, SelectiveLRUMIMO, _selective_recurrence, lin = _import_reference()
+    SelectiveLRU, SelectiveLRUMIMO, _selective_recurrence, lin, Mixer = _import_reference()
     groups = {
         "linoss": linoss_cases(lin),
         "selective_lru": selective_lru_cases(SelectiveLRU),
         "mimo": mimo_cases(SelectiveLRUMIMO),
         "recurrence": recurrence_case(_selective_recurrence),
+        "mixer": mixer_cases(Mixer, SelectiveLRU, lin),
     }
     for name, cases in groups.items():
         path = OUT / f"{name}.pt"

@@ -1,0 +1,115 @@
+"""The callers around the scans on the GPU: MambaStyleMixer against the reference's own
+mixer outputs (golden), and TFMambaBlock (bidirectional time + frequency blocks with the
+restated pre-norm Block / RMSNorm) against the float64 oracle, forward and every
+gradient; plus a bf16-autocast run of a TF-block."""
+from __future__ import annotations
+
+import pytest
+import torch
+
+from oracle import blocks as oblk
+from tests.parity import FP32_TOL, assert_close, cuda, floor_tol, rel_err, to32
+
+pytestmark = pytest.mark.gpu
+
+
+def _mixer_from_golden(rec):
+    from semambaxlinoss_b200.linoss import LinOSS
+    from semambaxlinoss_b200.mixer import MambaStyleMixer
+    from semambaxlinoss_b200.selective_lru import SelectiveLRU
+
+    cfg = rec["config"]
+    inner = cfg["in_features"] * cfg["expand"]
+    if cfg["kind"] == "selective_lru":
+        ssm = SelectiveLRU(d_model=inner, chunk_size=4, **cfg["ssm"])
+    else:
+        ssm = LinOSS(in_features=inner, chunk_size=8, **cfg["ssm"])
+    m = MambaStyleMixer(cfg["in_features"], ssm, expand=cfg["expand"], d_conv=cfg["d_conv"],
+                        causal_conv=cfg["causal"])
+    m.load_state_dict({k: v.float() for k, v in rec["state_dict"].items()})
+    return m.to(cuda())
+
+
+def test_mixer_matches_golden(golden):
+    dev = cuda()
+    for name, rec in golden("mixer").items():
+        m = _mixer_from_golden(rec)
+        x = to32(rec["x"], dev).requires_grad_(True)
+        y = m(x)
+        (y * to32(rec["grad_y"], dev)).sum().backward()
+        assert_close(y, rec["y"], FP32_TOL, f"{name} y")
+        assert_close(x.grad, rec["grad_x"], FP32_TOL, f"{name} dx")
+        for n, p in m.named_parameters():
+            assert_close(p.grad, rec["param_grads"][n], FP32_TOL, f"{name} d{n}")
+
+
+def _tf_cfg(bidirectional=True, use_transpose=True):
+    time_mixer = dict(ssm="selective_lru", d_state=4, d_conv=4, expand=2, bidirectional=bidirectional,
+                      ssm_params=dict(dt_rank=2, n_real_modes=1, chunk_size=8))
+    freq_mixer = dict(ssm="linoss", d_state=6, d_conv=4, expand=2, bidirectional=True,
+                      ssm_params=dict(discretization="IMEX", damping=True))
+    return {"model_cfg": dict(hid_feature=8, use_transpose=use_transpose, time_mixer=time_mixer,
+                              freq_mixer=freq_mixer)}
+
+
+def _oracle_specs(m, cfg):
+    tm, fm = cfg["model_cfg"]["time_mixer"], cfg["model_cfg"]["freq_mixer"]
+    ts = m.time_mamba.forward_blocks[0].mixer.ssm
+    t_cfg = dict(dt_rank=ts.dt_rank, d_state=ts.d_state, input_gain=ts.input_gain)
+    f_cfg = dict(discretization="IMEX", damping=True, a_from_g=True)
+    return (("selective_lru", t_cfg, dict(bidirectional=tm.get("bidirectional", True))),
+            ("linoss", f_cfg, dict(bidirectional=fm.get("bidirectional", True))))
+
+
+@pytest.mark.parametrize("bidirectional,use_transpose", [(True, True), (False, False)])
+def test_tf_block_matches_oracle(bidirectional, use_transpose):
+    from semambaxlinoss_b200.mamba_block import TFMambaBlock
+
+    torch.manual_seed(0)
+    cfg = _tf_cfg(bidirectional, use_transpose)
+    m = TFMambaBlock(cfg)
+    with torch.no_grad():
+        for p in m.parameters():
+            p.add_(0.05 * torch.randn_like(p))
+    g = torch.Generator().manual_seed(1)
+    x = torch.randn(2, 8, 10, 6, generator=g, dtype=torch.float64)
+    gy = torch.randn(2, 8, 10, 6, generator=g, dtype=torch.float64)
+    specs = _oracle_specs(m, cfg)
+
+    def oracle(dtype):
+        params = {k: v.detach().to(dtype).clone().requires_grad_(True) for k, v in m.state_dict().items()}
+        xo = x.to(dtype).clone().requires_grad_(True)
+        y = oblk.tf_block_forward(params, xo, *specs, use_transpose=use_transpose)
+        names = list(params)
+        grads = torch.autograd.grad((y * gy.to(dtype)).sum(), [xo] + [params[n] for n in names], allow_unused=True)
+        return y.detach(), dict(zip(["x"] + names, grads))
+
+    y_ref, g_ref = oracle(torch.float64)
+    y32, g32 = oracle(torch.float32)
+    dev = cuda()
+    m = m.to(dev)
+    xg = to32(x, dev).requires_grad_(True)
+    y = m(xg)
+    (y * to32(gy, dev)).sum().backward()
+    assert_close(y, y_ref, floor_tol(rel_err(y32, y_ref)), "y")
+    assert_close(xg.grad, g_ref["x"], floor_tol(rel_err(g32["x"], g_ref["x"])), "dx")
+    for n, p in m.named_parameters():
+        ref = g_ref[n]
+        assert ref is not None, n
+        assert_close(p.grad, ref, floor_tol(rel_err(g32[n], ref)), f"d{n}")
+
+
+def test_tf_block_bf16_autocast():
+    """bf16 autocast around fp32 scans: finite, and close to the fp32 block."""
+    from semambaxlinoss_b200.mamba_block import TFMambaBlock
+
+    torch.manual_seed(0)
+    cfg = _tf_cfg()
+    m = TFMambaBlock(cfg).to(cuda())
+    x = torch.randn(2, 8, 12, 7, device="cuda", requires_grad=True)
+    y32 = m(x)
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        y16 = m(x)
+    y16.float().square().sum().backward()
+    assert torch.isfinite(y16).all() and torch.isfinite(x.grad).all()
+    assert rel_err(y16.float(), y32) < 5e-2

@@ -6,6 +6,7 @@ from __future__ import annotations
 import pytest
 import torch
 
+from oracle import blocks as oblk
 from oracle import linoss as olin
 from oracle import selective_lru as oslru
 
@@ -126,3 +127,11 @@ def test_real_special_case_equals_complex_op():
         h = lam[:, t] * h + u[:, t]
         ys.append((h * Ct[:, t].unsqueeze(-2)).sum(-1) + D * x[:, t])
     assert _rel(y, torch.stack(ys, 1)) < 1e-12
+
+
+@pytest.mark.parametrize("idx", range(4))
+def test_mixer_matches_reference(golden, idx):
+    cases = golden("mixer")
+    rec = cases[sorted(cases)[idx]]
+    cfg = rec["config"]
+    _module_case(rec, lambda p, x: oblk.mixer_forward(p, x, cfg["kind"], cfg["ssm"], cfg["d_conv"], cfg["causal"]))

@@ -53,6 +53,11 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["semx", "reference"], default="semx")
+    ap.add_argument("--workload", choices=["linoss", "generator", "inference"], default="linoss",
+                    help="linoss: config 1 (default); generator: config-3 training step; "
+                         "inference: config-4 long-utterance inference")
+    ap.add_argument("--batch", type=int, default=16, help="generator: utterances per GPU")
+    ap.add_argument("--micro-batch", type=int, default=4, help="inference: utterances per forward")
     ap.add_argument("--chunk", type=int, default=64)
     ap.add_argument("--cpu-sample-frac", type=float, default=0.125)
     ap.add_argument("--ref-sample-frac", type=float, default=1.0 / 16)
@@ -473,13 +478,220 @@ def run_reference(args, rank):
     }), flush=True)
 
 
+# ----------------------------------------------------------------- generator workloads
+def _barrier(world, device):
+    torch.cuda.synchronize(device)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+    torch.cuda.synchronize(device)
+
+
+def _max_over_ranks(ms, world, device):
+    t = torch.tensor([ms], device=device)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.item()
+
+
+def _init_dist(world, device):
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+
+
+def run_generator(args, rank, local_rank, world):
+    """Config 3: SEMamba generator training step (forward + generator losses + backward +
+    DDP gradient all-reduce + AdamW), bf16 autocast around fp32 scans, `--batch`
+    two-second utterances per GPU. Metric: frames/s over all GPUs."""
+    from semambaxlinoss_b200.generator import SEMamba, config3_cfg, generator_loss, mag_phase_stft
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    _init_dist(world, device)
+    cfg = config3_cfg()
+    sc, cf = cfg["stft_cfg"], cfg["model_cfg"]["compress_factor"]
+    torch.manual_seed(1234)
+    model = SEMamba(cfg).to(device)
+    n_params = sum(p.numel() for p in model.parameters())
+    if world > 1:
+        from torch.nn.parallel import DistributedDataParallel as DDP
+
+        model = DDP(model, device_ids=[local_rank], broadcast_buffers=False, gradient_as_bucket_view=True)
+    opt = torch.optim.AdamW(model.parameters(), lr=5e-4, betas=(0.8, 0.99))
+    B, seg = args.batch, 32000
+    g = torch.Generator().manual_seed(100 + rank)
+    clean_h = (torch.randn(B, seg, generator=g) * 0.1).pin_memory()
+    noisy_h = (clean_h + torch.randn(B, seg, generator=g) * 0.05).pin_memory()
+    clean_d, noisy_d = clean_h.to(device), noisy_h.to(device)
+    loss_h = torch.empty(1).pin_memory()
+    frames = (seg // sc["hop_size"]) + 1
+
+    def step(clean, noisy, copy_in=False):
+        if copy_in:
+            clean.copy_(clean_h, non_blocking=True)
+            noisy.copy_(noisy_h, non_blocking=True)
+        clean_mag, clean_pha, clean_com = mag_phase_stft(clean, sc["n_fft"], sc["hop_size"], sc["win_size"], cf)
+        noisy_mag, noisy_pha, _ = mag_phase_stft(noisy, sc["n_fft"], sc["hop_size"], sc["win_size"], cf)
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            mag_g, pha_g, com_g = model(noisy_mag, noisy_pha)
+        loss = generator_loss(cfg, clean, clean_mag, clean_pha, clean_com, mag_g.float(), pha_g.float(),
+                              com_g.float())
+        opt.zero_grad(set_to_none=True)
+        loss.backward()
+        opt.step()
+        return loss
+
+    stream = torch.cuda.current_stream(device)
+    for _ in range(max(args.warmup, 3)):
+        step(clean_d, noisy_d)
+    uuid = _device_uuid(device)
+    clocks = ClockSampler(uuid, args.clocks_log if rank == 0 else None)
+    soak_t0 = time.time()
+    _barrier(world, device)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record(stream)
+    for _ in range(args.steps):
+        loss = step(clean_d, noisy_d)
+    e.record(stream)
+    _barrier(world, device)
+    t_end = time.time()
+    ms = _max_over_ranks(s.elapsed_time(e), world, device) / args.steps
+    # End to end: audio copied in from pinned host memory and the loss read back, every step.
+    _barrier(world, device)
+    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s2.record(stream)
+    for _ in range(args.e2e_steps):
+        loss = step(clean_d, noisy_d, copy_in=True)
+        loss_h.copy_(loss.detach().reshape(1), non_blocking=True)
+    e2.record(stream)
+    _barrier(world, device)
+    ms_e2e = _max_over_ranks(s2.elapsed_time(e2), world, device) / args.e2e_steps
+    clocks.stop()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    fps = world * B * frames / (ms * 1e-3)
+    print(json.dumps({
+        "metric": "SEMamba generator training step, frames/s (config 3: 2 s utterances, batch 16 per GPU)",
+        "value": round(fps, 1), "unit": "frames/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16 autocast, fp32 scans",
+        "data": "synthetic (clean ~ N(0, 0.1), noise ~ N(0, 0.05), seeded per rank)",
+        "config": {"workload": "config 3: generator fwd + losses + bwd + AdamW, 4 TF-blocks (time: selective-LRU "
+                               "d_inner 256 N 16; freq: damped-IMEX LinOSS P 16), hid 64",
+                   "global_batch": world * B, "seq_len": frames, "parallelism": f"ddp{world}",
+                   "parameters": n_params,
+                   "l2": "no flush: activations per step are tens of GB, far beyond the 126 MB L2"},
+        "e2e": {"value": round(world * B * frames / (ms_e2e * 1e-3), 1), "unit": "frames/s",
+                "ms_per_step": round(ms_e2e, 3), "h2d_bytes_per_step": 2 * B * seg * 4,
+                "d2h_bytes_per_step": 4},
+        "clocks": clocks.summary(soak_t0, t_end),
+    }), flush=True)
+
+
+def run_inference(args, rank, local_rank, world):
+    """Config 4: 64 sixty-second utterances (T = 9601 frames) enhanced end to end (STFT ->
+    generator -> iSTFT) under no_grad with bf16 autocast, sharded over the GPUs,
+    `--micro-batch` utterances per forward. Metric: frames/s over all GPUs."""
+    from semambaxlinoss_b200.generator import SEMamba, config3_cfg, mag_phase_istft, mag_phase_stft
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    _init_dist(world, device)
+    cfg = config3_cfg()
+    sc, cf = cfg["stft_cfg"], cfg["model_cfg"]["compress_factor"]
+    torch.manual_seed(1234)
+    model = SEMamba(cfg).to(device).eval()
+    total, seg = 64, 960000
+    per_rank = [len(range(r, total, world)) for r in range(world)][rank]
+    mb = args.micro_batch
+    g = torch.Generator().manual_seed(200 + rank)
+    audio = (torch.randn(per_rank, seg, generator=g) * 0.1).pin_memory()
+    out_h = torch.empty(per_rank, seg).pin_memory()
+    frames = seg // sc["hop_size"] + 1
+    buf = torch.empty(mb, seg, device=device)
+
+    def run_all():
+        for i in range(0, per_rank, mb):
+            n = min(mb, per_rank - i)
+            x = buf[:n]
+            x.copy_(audio[i:i + n], non_blocking=True)
+            with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+                mag, pha, _ = mag_phase_stft(x, sc["n_fft"], sc["hop_size"], sc["win_size"], cf)
+                mag_g, pha_g, _ = model(mag, pha)
+                wav = mag_phase_istft(mag_g.float(), pha_g.float(), sc["n_fft"], sc["hop_size"], sc["win_size"], cf)
+            out_h[i:i + n, :wav.shape[-1]].copy_(wav[:, :seg], non_blocking=True)
+
+    stream = torch.cuda.current_stream(device)
+    run_all()  # warm-up pass over the shard
+    uuid = _device_uuid(device)
+    clocks = ClockSampler(uuid, args.clocks_log if rank == 0 else None)
+    t0 = time.time()
+    _barrier(world, device)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record(stream)
+    for _ in range(args.steps):
+        run_all()
+    e.record(stream)
+    _barrier(world, device)
+    t1 = time.time()
+    clocks.stop()
+    ms = _max_over_ranks(s.elapsed_time(e), world, device) / args.steps
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    fps = total * frames / (ms * 1e-3)
+    print(json.dumps({
+        "metric": "SEMamba long-utterance inference, frames/s (config 4: 64 x 60 s, sharded)",
+        "value": round(fps, 1), "unit": "frames/s", "n_gpus": world, "steps": args.steps, "warmup": 1,
+        "ms_per_step": round(ms, 2), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "bf16 autocast, fp32 scans", "data": "synthetic (audio ~ N(0, 0.1), seeded per rank)",
+        "config": {"workload": "config 4: STFT -> generator -> iSTFT, no_grad", "global_batch": total,
+                   "seq_len": frames, "micro_batch": mb, "parallelism": f"sharded over {world} GPUs"},
+        "e2e": {"value": round(fps, 1), "unit": "frames/s", "h2d_bytes_per_step": total * seg * 4 // world,
+                "d2h_bytes_per_step": total * seg * 4 // world,
+                "note": "every step copies its audio in from pinned host memory and the enhanced audio out"},
+        "clocks": clocks.summary(t0, t1),
+    }), flush=True)
+
+
+def _device_uuid(device):
+    try:
+        u = str(torch.cuda.get_device_properties(device).uuid)
+        return u if u.startswith("GPU-") else "GPU-" + u
+    except Exception:
+        return None
+
+
 def main():
     args = parse_args()
     rank, local_rank, world = dist_env()
     if args.impl == "reference":
+        if args.workload != "linoss":
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "unavailable": "the reference generator needs the "
+                                  "third-party mamba_ssm package, which the reference does not ship"}))
+            return
         run_reference(args, rank)
         return
-    run_semx(args, rank, local_rank, world)
+    if args.workload == "generator":
+        run_generator(args, rank, local_rank, world)
+    elif args.workload == "inference":
+        run_inference(args, rank, local_rank, world)
+    else:
+        run_semx(args, rank, local_rank, world)
 
 
 if __name__ == "__main__":

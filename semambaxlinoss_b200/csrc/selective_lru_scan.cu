@@ -83,6 +83,31 @@ struct SParams {
   float* dbc_part;  // (S*L, nclusters, narr*N) when nclusters > 1
 };
 
+// Per-element transcendentals on the special-function unit (PTX ex2 / sin / cos / sqrt
+// .approx: one MUFU instruction each instead of a libm call). sin and cos take their
+// argument reduced to [-pi, pi] first: r = x - k * 2pi with k = rint(x / 2pi) and 2pi
+// split Cody-Waite style into hi = 6.28125 (exact: k * hi has no rounding for |k| < 2^16)
+// plus lo = 2pi - hi, so r carries no reduction error worth speaking of.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float sqrt_approx(float x) {
+  float y;
+  asm("sqrt.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ void sincos_reduced(float x, float* s, float* c) {
+  constexpr float kInv2Pi = 0.15915494f;
+  constexpr float k2PiHi = 6.28125f;
+  constexpr float k2PiLo = 0.0019353072f;
+  const float k = rintf(x * kInv2Pi);
+  const float r = fmaf(-k, k2PiLo, fmaf(-k, k2PiHi, x));
+  asm("sin.approx.f32 %0, %1;" : "=f"(*s) : "f"(r));
+  asm("cos.approx.f32 %0, %1;" : "=f"(*c) : "f"(r));
+}
+
 // Pole, drive gain and their intermediates for one (t, c, n).
 struct Disc {
   float nu, cs, sn, base, lre, lim, gr, gi, den;
@@ -92,7 +117,7 @@ template <bool REAL, int GAIN>
 __device__ __forceinline__ Disc discretise(float a, float a2, float om, float sd, bool detune,
                                            float dnu, float dth) {
   Disc d;
-  d.nu = exp2f(-dnu * a2);
+  d.nu = ex2_approx(-dnu * a2);
   if (REAL) {
     d.cs = 1.f;
     d.sn = 0.f;
@@ -101,14 +126,14 @@ __device__ __forceinline__ Disc discretise(float a, float a2, float om, float sd
     d.lim = 0.f;
   } else {
     d.base = om + (detune ? sd * dth : dth);
-    sincosf(dnu * d.base, &d.sn, &d.cs);
+    sincos_reduced(dnu * d.base, &d.sn, &d.cs);
     d.lre = d.nu * d.cs;
     d.lim = d.nu * d.sn;
   }
   d.gi = 0.f;
   d.den = 1.f;
   if (GAIN == SEMX_GAIN_GAMMA) {
-    d.gr = sqrtf(fmaxf(1.f - d.nu * d.nu, 1e-6f));
+    d.gr = sqrt_approx(fmaxf(1.f - d.nu * d.nu, 1e-6f));
   } else if (GAIN == SEMX_GAIN_MAMBA) {
     d.gr = dnu;
   } else {  // ZOH: (lam - 1) / A_c, A_c = -a + j base, with lam - 1 from expm1
@@ -117,7 +142,8 @@ __device__ __forceinline__ Disc discretise(float a, float a2, float om, float sd
       d.den = fmaxf(a * a, 1e-8f);
       d.gr = -(a * em1) / d.den;
     } else {
-      const float sh = sinf(0.5f * (dnu * d.base));
+      float sh, ch;
+      sincos_reduced(0.5f * (dnu * d.base), &sh, &ch);
       const float lm1r = em1 * d.cs - 2.f * sh * sh;
       const float lm1i = d.lim;
       d.den = fmaxf(a * a + d.base * d.base, 1e-8f);
@@ -188,6 +214,10 @@ __device__ __forceinline__ void load_step(const SParams& p, int64_t s, int t, in
   }
 }
 
+__device__ __forceinline__ bool semx_aligned16(const void* ptr) {
+  return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0;
+}
+
 struct ModeParams {
   float a[kGM], a2[kGM], om[kGM], sd[kGM], ge[kGM];
   bool ok[kGM];
@@ -240,18 +270,139 @@ __device__ __forceinline__ void lane_reduce(float (&v)[V], int cl) {
   for (int m = (CW / kT) / 2; m >= 1; m /= 2) v[0] += __shfl_xor_sync(0xffffffffu, v[0], m * NG);
 }
 
+// ------------------------------------------------------------------- staged operand tiles
+// The operands of kTile consecutive steps for a CTA's channel block are copied into
+// shared memory by all of the CTA's threads together (cp.async, 16 B per copy when the
+// rows are 16-byte aligned), double-buffered so the next tile is in flight while the
+// current one is consumed. Per buffer:
+//   channel rows [kRowC][kTile][CB]: delta_nu, x, delta_theta (complex only)
+//   mode rows    [kRowN][kTile][NP]: B_re, C_re, B_im, C_im (imaginary rows complex only)
+// with CB = channels per CTA and NP = NG * kGM padded modes. Slots for channels >= C or
+// modes >= N are zeroed once and never written by the copies.
+constexpr int kTile = 32;
+
+template <bool REAL, int NG>
+struct Tiles {
+  static constexpr int CB = kThreads / NG;
+  static constexpr int NP = NG * kGM;
+  static constexpr int kRowC = REAL ? 2 : 3;
+  static constexpr int kRowN = REAL ? 2 : 4;
+  static constexpr int kBuf = kTile * (kRowC * CB + kRowN * NP);  // floats per buffer
+  static constexpr size_t bytes() { return (size_t)2 * kBuf * sizeof(float); }
+  __device__ static float* chan(float* buf, int row) { return buf + row * kTile * CB; }
+  __device__ static float* mode(float* buf, int row) { return buf + kRowC * kTile * CB + row * kTile * NP; }
+};
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const unsigned sa = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(sa), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
+  const unsigned sa = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(sa), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;\n" ::: "memory"); }
+
+// Zeroes the padding slots of both buffers (channels >= nc, modes >= N).
+template <bool REAL, int NG>
+__device__ void tile_zero_padding(float* smem, int nc, int N) {
+  using T = Tiles<REAL, NG>;
+  for (int b = 0; b < 2; ++b) {
+    float* buf = smem + b * T::kBuf;
+    for (int i = threadIdx.x; i < T::kRowC * kTile * T::CB; i += kThreads)
+      if (i % T::CB >= nc) buf[i] = 0.f;
+    float* mb = T::mode(buf, 0);
+    for (int i = threadIdx.x; i < T::kRowN * kTile * T::NP; i += kThreads)
+      if (i % T::NP >= N) mb[i] = 0.f;
+  }
+}
+
+// Issues the copies of steps [t0, t0 + nt) of sequence s into `buf` (does not commit).
+template <bool REAL, int NG>
+__device__ void tile_load(const SParams& p, float* buf, int64_t s, int t0, int nt, int c0, int nc,
+                          bool vecC, bool vecN) {
+  using T = Tiles<REAL, NG>;
+  auto chan_src = [&](int a) { return a == 0 ? p.dnu : (a == 1 ? p.x : p.dth); };
+  auto mode_src = [&](int a) { return a == 0 ? p.Bre : (a == 1 ? p.Cre : (a == 2 ? p.Bim : p.Cim)); };
+  const int N = (int)p.N;
+  if (vecC) {
+    const int q = nc >> 2;  // 16-byte chunks per channel row
+    const int items = T::kRowC * nt * q;
+    for (int it = threadIdx.x; it < items; it += kThreads) {
+      const int a = it / (nt * q), rem = it % (nt * q), i = rem / q, j = rem % q;
+      const float* src = chan_src(a) + ((s * p.L + t0 + i) * p.C + c0) + 4 * j;
+      cp_async16(T::chan(buf, a) + i * T::CB + 4 * j, src);
+    }
+  } else {
+    const int items = T::kRowC * nt * nc;
+    for (int it = threadIdx.x; it < items; it += kThreads) {
+      const int a = it / (nt * nc), rem = it % (nt * nc), i = rem / nc, j = rem % nc;
+      cp_async4(T::chan(buf, a) + i * T::CB + j, chan_src(a) + ((s * p.L + t0 + i) * p.C + c0) + j);
+    }
+  }
+  if (vecN) {
+    const int q = N >> 2;
+    const int items = T::kRowN * nt * q;
+    for (int it = threadIdx.x; it < items; it += kThreads) {
+      const int a = it / (nt * q), rem = it % (nt * q), i = rem / q, j = rem % q;
+      cp_async16(T::mode(buf, a) + i * T::NP + 4 * j, mode_src(a) + (s * p.L + t0 + i) * p.N + 4 * j);
+    }
+  } else {
+    const int items = T::kRowN * nt * N;
+    for (int it = threadIdx.x; it < items; it += kThreads) {
+      const int a = it / (nt * N), rem = it % (nt * N), i = rem / N, j = rem % N;
+      cp_async4(T::mode(buf, a) + i * T::NP + j, mode_src(a) + (s * p.L + t0 + i) * p.N + j);
+    }
+  }
+}
+
+// Reads step i of a staged tile for this thread's channel and modes.
+template <bool REAL, int NG, bool WITH_C>
+__device__ __forceinline__ void tile_step(float* buf, int i, int cl, int g, StepIn<REAL>& in) {
+  using T = Tiles<REAL, NG>;
+  in.dnu = T::chan(buf, 0)[i * T::CB + cl];
+  in.x = T::chan(buf, 1)[i * T::CB + cl];
+  in.dth = REAL ? 0.f : T::chan(buf, 2)[i * T::CB + cl];
+  const float4 br = *reinterpret_cast<const float4*>(T::mode(buf, 0) + i * T::NP + g * kGM);
+  in.bre[0] = br.x; in.bre[1] = br.y; in.bre[2] = br.z; in.bre[3] = br.w;
+  if (WITH_C) {
+    const float4 cr = *reinterpret_cast<const float4*>(T::mode(buf, 1) + i * T::NP + g * kGM);
+    in.cre[0] = cr.x; in.cre[1] = cr.y; in.cre[2] = cr.z; in.cre[3] = cr.w;
+  }
+  if (!REAL) {
+    const float4 bi = *reinterpret_cast<const float4*>(T::mode(buf, 2) + i * T::NP + g * kGM);
+    in.bim[0] = bi.x; in.bim[1] = bi.y; in.bim[2] = bi.z; in.bim[3] = bi.w;
+    if (WITH_C) {
+      const float4 ci = *reinterpret_cast<const float4*>(T::mode(buf, 3) + i * T::NP + g * kGM);
+      in.cim[0] = ci.x; in.cim[1] = ci.y; in.cim[2] = ci.z; in.cim[3] = ci.w;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < kGM; ++j) in.bim[j] = in.cim[j] = 0.f;
+  }
+}
+
 // ----------------------------------------------------------------------------- forward
 template <bool REAL, int GAIN, int NG>
 __global__ void __launch_bounds__(kThreads) slru_fwd_kernel(const SParams p) {
+  using T = Tiles<REAL, NG>;
   constexpr int CW = 32 / NG;
-  constexpr int CB = kThreads / NG;
+  extern __shared__ float4 fwd_smem4[];
+  float* smem = reinterpret_cast<float*>(fwd_smem4);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int cl = lane / NG, g = lane % NG;
-  const int c = blockIdx.x * CB + warp * CW + cl;
+  const int c_local = warp * CW + cl;
+  const int c0 = blockIdx.x * T::CB;
+  const int c = c0 + c_local;
   const int64_t s = blockIdx.y;
   const bool cval = c < p.C;
-  const bool vec4 = (p.N % 4) == 0 && p.N > 0;
+  const int nc = (int)min((int64_t)T::CB, p.C - c0);
   const int L = (int)p.L;
+  const bool vecC = (p.C % 4) == 0 && semx_aligned16(p.dnu) && semx_aligned16(p.x) &&
+                    (REAL || semx_aligned16(p.dth));
+  const bool vecN = (p.N % 4) == 0 && semx_aligned16(p.Bre) && semx_aligned16(p.Cre) &&
+                    (REAL || (semx_aligned16(p.Bim) && semx_aligned16(p.Cim)));
 
   ModeParams mp;
   load_params(p, c, g, cval, mp);
@@ -264,41 +415,65 @@ __global__ void __launch_bounds__(kThreads) slru_fwd_kernel(const SParams p) {
     hi[j] = (mp.ok[j] && p.h0i && !REAL) ? p.h0i[i] : 0.f;
   }
 
-  StepIn<REAL> cur, nxt;
-  if (L > 0) load_step<REAL, true>(p, s, 0, c, g, cval, vec4, cur);
-  for (int t = 0; t < L; ++t) {
-    if (t + 1 < L) load_step<REAL, true>(p, s, t + 1, c, g, cval, vec4, nxt);
-    if (p.ckpt != nullptr && (t % p.chunk) == 0) {
-      const int64_t base = ((s * p.nchunks + t / p.chunk) * p.C + c) * p.N + g * kGM;
+  tile_zero_padding<REAL, NG>(smem, nc, (int)p.N);
+  const int ntiles = (L + kTile - 1) / kTile;
+  if (ntiles > 0) tile_load<REAL, NG>(p, smem, s, 0, min(kTile, L), c0, nc, vecC, vecN);
+  cp_async_commit();
+  int next_ck = 0;
+  float* yrow = p.y + s * p.L * p.C + c;
+  for (int k = 0; k < ntiles; ++k) {
+    cp_async_wait_all();
+    __syncthreads();
+    if (k + 1 < ntiles)
+      tile_load<REAL, NG>(p, smem + ((k + 1) & 1) * T::kBuf, s, (k + 1) * kTile,
+                          min(kTile, L - (k + 1) * kTile), c0, nc, vecC, vecN);
+    cp_async_commit();
+    float* buf = smem + (k & 1) * T::kBuf;
+    const int t0 = k * kTile, nt = min(kTile, L - t0);
+    for (int i = 0; i < nt; ++i) {
+      const int t = t0 + i;
+      if (p.ckpt != nullptr && t == next_ck) {
+        const int64_t base = ((s * p.nchunks + t / p.chunk) * p.C + c) * p.N + g * kGM;
 #pragma unroll
-      for (int j = 0; j < kGM; ++j) {
-        if (mp.ok[j]) {
-          if (REAL) {
-            p.ckpt[base + j] = hr[j];
-          } else {
-            reinterpret_cast<float2*>(p.ckpt)[base + j] = make_float2(hr[j], hi[j]);
+        for (int j = 0; j < kGM; ++j) {
+          if (mp.ok[j]) {
+            if (REAL) p.ckpt[base + j] = hr[j];
+            else reinterpret_cast<float2*>(p.ckpt)[base + j] = make_float2(hr[j], hi[j]);
           }
         }
+        next_ck += p.chunk;
       }
-    }
-    float yp = 0.f;
+      StepIn<REAL> cur;
+      tile_step<REAL, NG, true>(buf, i, c_local, g, cur);
+      // Modes beyond N and channels beyond C need no masking here: their parameters and
+      // staged operands are zero, so their state stays exactly zero and adds nothing.
+      float yp = 0.f;
 #pragma unroll
-    for (int j = 0; j < kGM; ++j) {
-      const Disc d = discretise<REAL, GAIN>(mp.a[j], mp.a2[j], mp.om[j], mp.sd[j], p.detune,
-                                            cur.dnu, cur.dth);
-      const float gxr = d.gr * cur.x, gxi = d.gi * cur.x;
-      const float ur = gxr * cur.bre[j] - gxi * cur.bim[j];
-      const float ui = gxr * cur.bim[j] + gxi * cur.bre[j];
-      const float nr = d.lre * hr[j] - d.lim * hi[j] + ur;
-      const float ni = d.lre * hi[j] + d.lim * hr[j] + ui;
-      hr[j] = mp.ok[j] ? nr : 0.f;
-      hi[j] = mp.ok[j] ? ni : 0.f;
-      yp += cur.cre[j] * hr[j] - cur.cim[j] * hi[j];
-      if (p.envelope) yp += mp.ge[j] * (hr[j] * hr[j] + hi[j] * hi[j]);
+      for (int j = 0; j < kGM; ++j) {
+        const Disc d = discretise<REAL, GAIN>(mp.a[j], mp.a2[j], mp.om[j], mp.sd[j], p.detune,
+                                              cur.dnu, cur.dth);
+        const float gxr = d.gr * cur.x;
+        if (REAL) {
+          hr[j] = d.lre * hr[j] + gxr * cur.bre[j];
+          yp += cur.cre[j] * hr[j];
+        } else {
+          const float gxi = d.gi * cur.x;
+          const float ur = gxr * cur.bre[j] - gxi * cur.bim[j];
+          const float ui = gxr * cur.bim[j] + gxi * cur.bre[j];
+          const float nr = d.lre * hr[j] - d.lim * hi[j] + ur;
+          const float ni = d.lre * hi[j] + d.lim * hr[j] + ui;
+          hr[j] = nr;
+          hi[j] = ni;
+          yp += cur.cre[j] * hr[j] - cur.cim[j] * hi[j];
+        }
+      }
+      if (p.envelope) {
+#pragma unroll
+        for (int j = 0; j < kGM; ++j) yp += mp.ge[j] * (hr[j] * hr[j] + (REAL ? 0.f : hi[j] * hi[j]));
+      }
+      yp = sum_lanes<NG>(yp);
+      if (g == 0 && cval) yrow[(int64_t)t * p.C] = yp + Dc * cur.x;
     }
-    yp = sum_lanes<NG>(yp);
-    if (g == 0 && cval) p.y[(s * p.L + t) * p.C + c] = yp + Dc * cur.x;
-    cur = nxt;
   }
   if (p.hfr != nullptr) {
 #pragma unroll
@@ -798,7 +973,9 @@ size_t dbc_floats(const SemxSelectiveLruArgs* a) {
 template <bool REAL, int GAIN, int NG>
 int launch_fwd(const SParams& p, const Geometry& g, cudaStream_t st) {
   const dim3 grid((unsigned)g.nblocks, (unsigned)p.S);
-  slru_fwd_kernel<REAL, GAIN, NG><<<grid, kThreads, 0, st>>>(p);
+  const size_t smem = Tiles<REAL, NG>::bytes();
+  if (!semx::allow_smem(slru_fwd_kernel<REAL, GAIN, NG>, smem)) return SEMX_ERR_LAUNCH;
+  slru_fwd_kernel<REAL, GAIN, NG><<<grid, kThreads, smem, st>>>(p);
   return semx::check_launch("slru_fwd_kernel");
 }
 

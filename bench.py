@@ -1,27 +1,40 @@
 #!/usr/bin/env python
-"""Throughput of the LinOSS-IMEX oscillatory scan (forward + backward) on B200.
+"""Throughput of the SEMamba TF-block scans on B200.
 
-Workload (one "step"): the LinOSS-IMEX scan of a 4-utterance batch with P = 256
-oscillators and H = 64 input channels, along time (B*F = 404 sequences x 321 steps) and
-along frequency (B*T = 1284 sequences x 101 steps), forward and backward, at the scan
-boundary: Bu (complex) in, y2 (complex) out; backward dY2 in, dBu and the parameter
-gradients out. Synthetic seeded inputs with the workload's distributions: A = relu(N(0,1)),
-dt = sigmoid(N(0,1)), complex B entries N(0, 1/sqrt(H)) per part, u ~ N(0,1), Bu = B u,
-upstream gradient ~ N(0,1).
+Workloads (`--workload`; one "step" = one forward + backward of every pass listed):
 
-Metric: scan GB/s of algorithmic bytes (fwd 16 P B per (sequence, step): Bu in + y2 out;
-bwd 24 P B: Bu + dY2 in, dBu out). Every operand is 265 MB (> the 126 MB L2), so no L2
-flush is needed between steps.
+  linoss (default)  LinOSS-IMEX oscillatory scan, P = 256 oscillators, H = 64 inputs, at the
+                    scan boundary (Bu in, y2 out; dY2 in, dBu + parameter gradients out):
+                    time pass 404 sequences x 321 steps, frequency pass 1284 x 101.
+                    A = relu(N(0,1)), dt = sigmoid(N(0,1)), complex B entries N(0, 1/sqrt(H)),
+                    u ~ N(0,1), Bu = B u, upstream gradient N(0,1).
+                    Algorithmic bytes per (sequence, step): fwd 16 P, bwd 24 P.
+  slru              Real selective-LRU diagonal scan (fused discretisation + readout + D skip),
+                    404 sequences x 321 steps, C = 256 channels, N = 16 modes, Mamba gain:
+                    x ~ N(0,1), dt = softplus(N(-2, 0.5)), a = exp(A_log) with A_log ~ log U(1,16),
+                    B_t, C_t ~ N(0, 1/16), D ~ N(0,1). Algorithmic bytes per (sequence, step):
+                    fwd 4 (3C + 2N) = 3200 (x, dt, B, C in; y out), bwd 4 (5C + 4N) = 5376
+                    (x, dt, dy, B, C in; d_dt, dx, dB, dC out).
+  mimo              SelectiveLRUMIMO layer, 256 features = 8 heads x 32, 128 state (16 per
+                    head), rank 4, bf16 input, fp32 state: time pass 404 x 321, frequency
+                    pass 1284 x 101. Algorithmic bytes per (sequence, step) of the layer's
+                    token-level operands: fwd 4768, bwd 8512.
+  generator         SEMamba generator training step (STFT, forward, losses, backward, AdamW),
+                    2 s utterances, batch 16 per GPU, DDP over NCCL; frames/s.
+  inference         64 sixty-second utterances enhanced end to end, sharded; frames/s.
 
-Arms:
-  default           — libsemx kernels through the C ABI, inputs resident in HBM (`value`);
-                      plus `e2e` (host buffers, copies inside the timed region), the
-                      roofline of the dominant kernel, clocks, and the CPU baseline.
-  --impl reference  — the reference's CPU implementation of the path (the oracle port of
-                      models/linoss/linoss.py) on the host cores, on a bounded sample.
+Scan workloads report algorithmic GB/s (`value`, inputs resident in HBM), `e2e` (the same
+metric with host buffers and the copies inside the timed region), the roofline of the
+dominant kernel, clocks sampled during the timed region, the kernel launch count and a
+CPU baseline (the reference algorithm on the host cores, on a bounded sample). Every scan
+operand is larger than the 126 MB L2 except where `config.l2` says otherwise.
 
-Multi-GPU (torchrun, one process per GPU): weak scaling, each rank scans its own batch;
-no collective is on the data path; time = max over ranks.
+`--impl reference` times the reference's CPU implementation of the path (the oracle port)
+on the host cores, on a bounded sample of the same workload.
+
+Multi-GPU (torchrun, one process per GPU): weak scaling for the scans (each rank scans its
+own batch, no collective on the data path) and the training step (DDP); time = max over
+ranks, measured with CUDA events.
 """
 from __future__ import annotations
 
@@ -40,34 +53,33 @@ from pathlib import Path
 import torch
 
 ROOT = Path(__file__).resolve().parent
-P, H = 256, 64
-PASSES = (("time", 404, 321), ("freq", 1284, 101))
-FWD_BYTES_PER_STEP = 16 * P  # Bu in, y2 out (complex64)
-BWD_BYTES_PER_STEP = 24 * P  # Bu, dY2 in; dBu out
-METRIC = "LinOSS-IMEX scan fwd+bwd, algorithmic HBM GB/s (config 1: time 404x321 + freq 1284x101, P=256)"
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
 
 
 def parse_args():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=None, help="timed steps (default per workload)")
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["semx", "reference"], default="semx")
-    ap.add_argument("--workload", choices=["linoss", "generator", "inference"], default="linoss",
-                    help="linoss: config 1 (default); generator: config-3 training step; "
-                         "inference: config-4 long-utterance inference")
+    ap.add_argument("--workload", choices=["linoss", "slru", "mimo", "generator", "inference"],
+                    default="linoss")
     ap.add_argument("--batch", type=int, default=16, help="generator: utterances per GPU")
     ap.add_argument("--micro-batch", type=int, default=4, help="inference: utterances per forward")
-    ap.add_argument("--chunk", type=int, default=64)
-    ap.add_argument("--cpu-sample-frac", type=float, default=0.125)
-    ap.add_argument("--ref-sample-frac", type=float, default=1.0 / 16)
+    ap.add_argument("--chunk", type=int, default=None, help="checkpoint interval of the scan")
+    ap.add_argument("--cpu-sample-frac", type=float, default=None)
+    ap.add_argument("--ref-sample-frac", type=float, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--clocks-log", default=None)
     ap.add_argument("--no-soak", action="store_true",
                     help="skip the 1.5 s busy period before timing (for profiler runs)")
-    return ap.parse_args()
+    args = ap.parse_args()
+    if args.steps is None:
+        args.steps = {"linoss": 200, "slru": 20, "mimo": 20, "generator": 10, "inference": 1}[args.workload]
+    return args
 
 
 # ----------------------------------------------------------------------------- helpers
@@ -152,16 +164,66 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(win)}
 
 
-# ----------------------------------------------------------------------------- workload
+def _device_uuid(device):
+    try:
+        u = str(torch.cuda.get_device_properties(device).uuid)
+        return u if u.startswith("GPU-") else "GPU-" + u
+    except Exception:
+        return None
+
+
+def _barrier(world, device):
+    torch.cuda.synchronize(device)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+    torch.cuda.synchronize(device)
+
+
+def _max_over_ranks(ms, world, device):
+    t = torch.tensor([ms], device=device)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.item()
+
+
+def _init_dist(world, device):
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+
+
+def _finish_dist(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+# ------------------------------------------------------------------ LinOSS scan workload
+LIN_P, LIN_H = 256, 64
+LIN_PASSES = (("time", 404, 321), ("freq", 1284, 101))
+
+
 class LinossPass:
-    """One scan pass (S sequences x L steps x P oscillators) with resident device buffers
-    and prebuilt C-ABI argument structs for semx_linoss_fwd / semx_linoss_bwd."""
+    """One LinOSS-IMEX pass (S sequences x L steps x P oscillators) with resident device
+    buffers and prebuilt C-ABI argument structs for semx_linoss_fwd / semx_linoss_bwd."""
+
+    fwd_bytes_per_unit = 16 * LIN_P  # Bu in, y2 out (complex64)
+    bwd_bytes_per_unit = 24 * LIN_P  # Bu, dY2 in; dBu out
+    kernels = ("linoss_fwd_kernel", "linoss_bwd_kernel")
 
     def __init__(self, S, L, seed, device, chunk):
         from semambaxlinoss_b200 import _lib
 
-        self.lib = _lib.load()
-        self._lib = _lib
+        P, H = LIN_P, LIN_H
+        self.lib, self._lib = _lib.load(), _lib
         self.S, self.L = S, L
         g = torch.Generator(device=device).manual_seed(seed)
         self.steps = torch.randn(P, generator=g, device=device)
@@ -189,111 +251,392 @@ class LinossPass:
         a.workspace = self.ws.data_ptr()
         self.args = a
         self.units = S * L
+        self.inputs = [self.Bu, self.dY2]
+        self.outputs = [self.Y2, self.dBu, self.dparams]
 
-    def fwd(self, stream):
-        self._lib.check("semx_linoss_fwd", self.lib.semx_linoss_fwd(ctypes.byref(self.args), stream))
+    def fwd(self, sh):
+        self._lib.check("semx_linoss_fwd", self.lib.semx_linoss_fwd(ctypes.byref(self.args), sh))
 
-    def bwd(self, stream):
-        self._lib.check("semx_linoss_bwd", self.lib.semx_linoss_bwd(ctypes.byref(self.args), stream))
+    def bwd(self, sh):
+        self._lib.check("semx_linoss_bwd", self.lib.semx_linoss_bwd(ctypes.byref(self.args), sh))
 
 
-def run_semx(args, rank, local_rank, world):
+def _linoss_cpu_sample(frac, seed=0):
+    P, H = LIN_P, LIN_H
+    g = torch.Generator().manual_seed(seed)
+    steps = torch.randn(P, generator=g)
+    A = torch.randn(P, generator=g)
+    sample = []
+    for _, S, L in LIN_PASSES:
+        s = max(1, int(round(S * frac)))
+        Bw = torch.randn(P, H, 2, generator=g) / H**0.5
+        u = torch.randn(s, L, H, generator=g)
+        Bu = torch.complex(u @ Bw[..., 0].t(), u @ Bw[..., 1].t())
+        gy = torch.complex(torch.randn(s, L, P, generator=g), torch.randn(s, L, P, generator=g))
+        sample.append((s, L, Bu, gy))
+    return {"params": (steps, A), "passes": sample, "frac": sample[0][0] / LIN_PASSES[0][1],
+            "bytes": sum(s * L * (16 + 24) * P for s, L, _, _ in sample),
+            "desc": " + ".join(f"{s}x{L}" for s, L, _, _ in sample)}
+
+
+def _linoss_cpu_step(sample):
+    """The reference's CPU path for this scan (oracle port of models/linoss/linoss.py:
+    constraints, IMEX discretisation and the sequential _linoss_recurrence), fwd + bwd."""
+    from oracle import linoss as olin
+
+    steps, A = sample["params"]
+    for _, _, Bu, gy in sample["passes"]:
+        st = steps.clone().requires_grad_(True)
+        a = A.clone().requires_grad_(True)
+        b = Bu.clone().requires_grad_(True)
+        y2 = olin.linoss_scan_fused("IMEX", st, a, None, b)
+        (y2.real * gy.real + y2.imag * gy.imag).sum().backward()
+
+
+# ------------------------------------------------------------- selective-LRU SISO workload
+SLRU_S, SLRU_L, SLRU_C, SLRU_N = 404, 321, 256, 16
+
+
+class SlruPass:
+    """The real selective-LRU scan (Mamba gain) over S x L x C channels x N modes with
+    resident buffers and prebuilt argument structs for semx_selective_lru_fwd / _bwd."""
+
+    kernels = ("slru_fwd_kernel", "slru_bwd_kernel")
+
+    def __init__(self, S, L, seed, device, chunk):
+        from semambaxlinoss_b200 import _lib
+
+        C, N = SLRU_C, SLRU_N
+        self.lib, self._lib = _lib.load(), _lib
+        self.fwd_bytes_per_unit = 4 * (3 * C + 2 * N)
+        self.bwd_bytes_per_unit = 4 * (5 * C + 4 * N)
+        g = torch.Generator(device=device).manual_seed(seed)
+        f = torch.float32
+        self.x = torch.randn(S, L, C, generator=g, device=device)
+        self.dnu = torch.nn.functional.softplus(torch.randn(S, L, C, generator=g, device=device) * 0.5 - 2.0)
+        self.a = torch.rand(C, N, generator=g, device=device) * 15.0 + 1.0
+        self.B = torch.randn(S, L, N, generator=g, device=device) * 0.25
+        self.Cr = torch.randn(S, L, N, generator=g, device=device) * 0.25
+        self.D = torch.randn(C, generator=g, device=device)
+        self.dy = torch.randn(S, L, C, generator=g, device=device)
+        self.y = torch.empty(S, L, C, dtype=f, device=device)
+        self.d_dnu, self.dx = torch.empty_like(self.y), torch.empty_like(self.y)
+        self.dB, self.dC = torch.empty_like(self.B), torch.empty_like(self.B)
+        self.da, self.dD = torch.empty(C, N, device=device), torch.empty(C, device=device)
+        a = _lib.new_args(_lib.SemxSelectiveLruArgs)
+        a.real, a.input_gain, a.chunk = 1, _lib.GAIN_CODES["mamba"], chunk
+        a.S, a.L, a.C, a.N = S, L, C, N
+        for name, t in (("delta_nu", self.dnu), ("a", self.a), ("B_re", self.B), ("C_re", self.Cr),
+                        ("x", self.x), ("D", self.D), ("y", self.y), ("dy", self.dy),
+                        ("d_delta_nu", self.d_dnu), ("dx", self.dx), ("dB_re", self.dB),
+                        ("dC_re", self.dC), ("da", self.da), ("dD", self.dD)):
+            setattr(a, name, t.data_ptr())
+        self.ckpt = _lib.empty_f32(self.lib.semx_selective_lru_ckpt_bytes(ctypes.byref(a)), device)
+        a.ckpt = self.ckpt.data_ptr()
+        self.ws = _lib.empty_f32(self.lib.semx_selective_lru_workspace_bytes(ctypes.byref(a)), device)
+        a.workspace = self.ws.data_ptr()
+        self.args = a
+        self.units = S * L
+        self.S, self.L = S, L
+        self.inputs = [self.x, self.dnu, self.B, self.Cr, self.dy]
+        self.outputs = [self.y, self.d_dnu, self.dx, self.dB, self.dC, self.da, self.dD]
+
+    def fwd(self, sh):
+        self._lib.check("semx_selective_lru_fwd", self.lib.semx_selective_lru_fwd(ctypes.byref(self.args), sh))
+
+    def bwd(self, sh):
+        self._lib.check("semx_selective_lru_bwd", self.lib.semx_selective_lru_bwd(ctypes.byref(self.args), sh))
+
+
+def _slru_cpu_sample(frac, seed=0):
+    C, N = SLRU_C, SLRU_N
+    g = torch.Generator().manual_seed(seed)
+    s = max(1, int(round(SLRU_S * frac)))
+    L = SLRU_L
+    t = {"dnu": torch.nn.functional.softplus(torch.randn(s, L, C, generator=g) * 0.5 - 2.0),
+         "a": torch.rand(C, N, generator=g) * 15.0 + 1.0,
+         "B": torch.randn(s, L, N, generator=g) * 0.25, "C": torch.randn(s, L, N, generator=g) * 0.25,
+         "x": torch.randn(s, L, C, generator=g), "D": torch.randn(C, generator=g)}
+    gy = torch.randn(s, L, C, generator=g)
+    return {"t": t, "gy": gy, "bytes": s * L * 4 * (8 * C + 6 * N), "desc": f"{s}x{L}", "frac": s / SLRU_S}
+
+
+def _slru_cpu_step(sample):
+    """The reference's CPU path (oracle port of the materialised SelectiveLRU path,
+    models/selective_lru/selective_lru.py:242-276 with _selective_recurrence), fwd + bwd."""
+    from oracle import selective_lru as oslru
+
+    t = {k: v.clone().requires_grad_(True) for k, v in sample["t"].items()}
+    y = oslru.selective_lru_real_op(t["dnu"], t["a"], t["B"], t["C"], t["x"], t["D"], "mamba")
+    (y * sample["gy"]).sum().backward()
+
+
+# -------------------------------------------------------------------- MIMO layer workload
+MIMO_F, MIMO_STATE, MIMO_HEADS, MIMO_RANK = 256, 128, 8, 4
+MIMO_PASSES = (("time", 404, 321), ("freq", 1284, 101))
+
+
+def _mimo_layer(device, seed):
+    from semambaxlinoss_b200.selective_lru import SelectiveLRUMIMO
+
+    torch.manual_seed(seed)
+    m = SelectiveLRUMIMO(MIMO_F, MIMO_STATE, n_heads=MIMO_HEADS, rank=MIMO_RANK)
+    g = torch.Generator().manual_seed(seed)
+    with torch.no_grad():
+        # Token-level operands of the workload: dt = softplus(N(-2, 0.5)) per (token, head)
+        # and b_t, c_t ~ N(0, 1/4) for x ~ N(0, 1/4); static B, C, D ~ N(0, 1/4).
+        for lin in (m.dt_nu_proj, m.dt_theta_proj, m.b_dir, m.c_read, m.b_coef, m.c_coef):
+            lin.weight.copy_(torch.randn(lin.weight.shape, generator=g) / 16.0)
+        m.dt_nu_proj.bias.fill_(-2.0)
+        for p in (m.B, m.C, m.D):
+            p.copy_(torch.randn(p.shape, generator=g) * 0.5)
+    return m.to(device)
+
+
+class MimoPass:
+    """One SelectiveLRUMIMO layer pass (bf16 input, fp32 state): forward builds the graph,
+    backward runs it against a fixed upstream gradient."""
+
+    fwd_bytes_per_unit = 4768
+    bwd_bytes_per_unit = 8512
+    kernels = ("mimo_fwd_kernel", "mimo_bwd_kernel")
+
+    def __init__(self, layer, S, L, seed, device):
+        g = torch.Generator(device=device).manual_seed(seed)
+        self.layer = layer
+        self.x = (torch.randn(S, L, MIMO_F, generator=g, device=device) * 0.5).to(torch.bfloat16)
+        self.gy = torch.randn(S, L, MIMO_F, generator=g, device=device)
+        self.units = S * L
+        self.S, self.L = S, L
+        self.inputs = [self.x, self.gy]
+        self.xg = None
+        self.y = None
+        self.outputs = []
+
+    def fwd(self, sh):
+        self.xg = self.x.detach().requires_grad_(True)
+        self.y = self.layer(self.xg)
+
+    def bwd(self, sh):
+        self.y.backward(self.gy)
+        self.outputs = [self.y.detach(), self.xg.grad]
+
+
+class MimoKernelPass:
+    """The fused MIMO scan + readout kernels alone (semx_mimo_fwd / _bwd) on resident
+    poles, drive, readout and input, for the kernel roofline of the MIMO workload."""
+
+    kernels = ("mimo_fwd_kernel", "mimo_bwd_kernel")
+
+    def __init__(self, S, L, seed, device):
+        from semambaxlinoss_b200 import _lib
+
+        H, Nh, Fh = MIMO_HEADS, MIMO_STATE // MIMO_HEADS, MIMO_F // MIMO_HEADS
+        N, Fd = MIMO_STATE, MIMO_F
+        self.lib, self._lib = _lib.load(), _lib
+        self.fwd_bytes_per_unit = 4 * (4 * N + Fd) + 4 * (Fd + 2 * N)       # lam, Bu, x in; y, h out
+        self.bwd_bytes_per_unit = 4 * (4 * N + 2 * Fd) + 4 * (4 * N + Fd)   # lam, h, dy, x in; dlam, dBu, dx out
+        g = torch.Generator(device=device).manual_seed(seed)
+        r = lambda *s: torch.randn(*s, generator=g, device=device)  # noqa: E731
+        nu = torch.rand(S, L, N, generator=g, device=device) * 0.98
+        th = r(S, L, N)
+        self.t = {"lam_re": nu * torch.cos(th), "lam_im": nu * torch.sin(th), "Bu_re": r(S, L, N),
+                  "Bu_im": r(S, L, N), "C_re": r(H, Fh, Nh) * 0.25, "C_im": r(H, Fh, Nh) * 0.25,
+                  "x": r(S, L, Fd), "D": r(Fd), "dy": r(S, L, Fd)}
+        for k in ("y", "dx"):
+            self.t[k] = torch.empty(S, L, Fd, device=device)
+        for k in ("h_re", "h_im", "dlam_re", "dlam_im", "dBu_re", "dBu_im"):
+            self.t[k] = torch.empty(S, L, N, device=device)
+        self.t["dC_re"], self.t["dC_im"] = torch.empty(H, Fh, Nh, device=device), torch.empty(H, Fh, Nh, device=device)
+        self.t["dD"] = torch.empty(Fd, device=device)
+        a = _lib.new_args(_lib.SemxMimoArgs)
+        a.S, a.L, a.H, a.Nh, a.Fh = S, L, H, Nh, Fh
+        for k, v in self.t.items():
+            setattr(a, k, v.data_ptr())
+        self.ws = _lib.empty_f32(self.lib.semx_mimo_workspace_bytes(ctypes.byref(a)), device)
+        a.workspace = self.ws.data_ptr()
+        self.args = a
+        self.units = S * L
+        self.S, self.L = S, L
+
+    def fwd(self, sh):
+        self._lib.check("semx_mimo_fwd", self.lib.semx_mimo_fwd(ctypes.byref(self.args), sh))
+
+    def bwd(self, sh):
+        self._lib.check("semx_mimo_bwd", self.lib.semx_mimo_bwd(ctypes.byref(self.args), sh))
+
+
+def _mimo_cpu_sample(frac, seed=0):
+    from oracle import selective_lru as oslru  # noqa: F401  (import check before timing)
+
+    layer = _mimo_layer("cpu", seed)
+    params = {k: v.detach().clone() for k, v in layer.state_dict().items()}
+    cfg = {"in_features": MIMO_F, "state_dim": MIMO_STATE, "n_heads": MIMO_HEADS, "rank": MIMO_RANK,
+           "input_gain": "gamma"}
+    g = torch.Generator().manual_seed(seed + 1)
+    passes = []
+    for _, S, L in MIMO_PASSES:
+        s = max(1, int(round(S * frac)))
+        x = (torch.randn(s, L, MIMO_F, generator=g) * 0.5).to(torch.bfloat16).float()
+        passes.append((s, L, x, torch.randn(s, L, MIMO_F, generator=g)))
+    return {"params": params, "cfg": cfg, "passes": passes, "frac": passes[0][0] / MIMO_PASSES[0][1],
+            "bytes": sum(s * L * (4768 + 8512) for s, L, _, _ in passes),
+            "desc": " + ".join(f"{s}x{L}" for s, L, _, _ in passes)}
+
+
+def _mimo_cpu_step(sample):
+    """The reference's CPU path for the layer (oracle port of SelectiveLRUMIMO's PyTorch
+    path, models/selective_lru/selective_lru.py:488-587 with _selective_recurrence)."""
+    from oracle import selective_lru as oslru
+
+    for _, _, x, gy in sample["passes"]:
+        p = {k: v.clone().requires_grad_(v.is_floating_point()) for k, v in sample["params"].items()}
+        xx = x.clone().requires_grad_(True)
+        y = oslru.selective_lru_mimo_forward(p, xx, sample["cfg"])
+        (y * gy).sum().backward()
+
+
+# ------------------------------------------------------------------------ scan workloads
+WORKLOADS = {
+    "linoss": {
+        "metric": "LinOSS-IMEX scan fwd+bwd, algorithmic HBM GB/s (time 404x321 + freq 1284x101, P=256)",
+        "describe": "LinOSS-IMEX scan fwd+bwd at the scan boundary, time 404x321 + freq 1284x101, "
+                    "P=256 oscillators, H=64",
+        "data": "synthetic, seeded: A = relu(N(0,1)), dt = sigmoid(N(0,1)), B ~ N(0, 1/sqrt(64)), u ~ N(0,1)",
+        "dtype": "f32",
+        "chunk": 64, "cpu_frac": 0.125, "ref_frac": 1.0 / 16,
+        "l2": "no flush: every operand is 265 MB, larger than the 126 MB L2",
+        "cpu_sample": _linoss_cpu_sample, "cpu_step": _linoss_cpu_step,
+    },
+    "slru": {
+        "metric": "Selective-LRU real diagonal scan fwd+bwd, algorithmic HBM GB/s (404x321, C=256, N=16)",
+        "describe": "real selective-LRU scan (Mamba gain) fwd+bwd, 404 sequences x 321 steps, "
+                    "C=256 channels, N=16 modes",
+        "data": "synthetic, seeded: x ~ N(0,1), dt = softplus(N(-2,0.5)), a ~ U(1,16), B, C ~ N(0,1/16)",
+        "dtype": "f32",
+        "chunk": 64, "cpu_frac": 8.0 / 404, "ref_frac": 4.0 / 404,
+        "l2": "no flush: x, dt, dy, y and each gradient are 133 MB, larger than the 126 MB L2",
+        "cpu_sample": _slru_cpu_sample, "cpu_step": _slru_cpu_step,
+    },
+    "mimo": {
+        "metric": "Selective-LRU MIMO layer fwd+bwd, algorithmic HBM GB/s (time 404x321 + freq 1284x101, "
+                  "8 heads x 32, state 128, rank 4)",
+        "describe": "SelectiveLRUMIMO layer fwd+bwd (bf16 input, fp32 state), 256 features = 8 heads x 32, "
+                    "state 128, rank 4, time 404x321 + freq 1284x101",
+        "data": "synthetic, seeded: x ~ N(0,1/4) bf16, dt = softplus(N(-2,0.5)), b_t, c_t, B, C, D ~ N(0,1/4)",
+        "dtype": "bf16 in / f32 state",
+        "chunk": 0, "cpu_frac": 16.0 / 404, "ref_frac": 8.0 / 404,
+        "l2": "no flush: the layer's activations per pass are GBs, far beyond the 126 MB L2",
+        "cpu_sample": _mimo_cpu_sample, "cpu_step": _mimo_cpu_step,
+    },
+}
+
+
+def _make_passes(name, rank, device, chunk):
+    if name == "linoss":
+        return [LinossPass(S, L, seed=1000 * rank + i, device=device, chunk=chunk)
+                for i, (_, S, L) in enumerate(LIN_PASSES)]
+    if name == "slru":
+        return [SlruPass(SLRU_S, SLRU_L, seed=1000 * rank, device=device, chunk=chunk)]
+    layer = _mimo_layer(device, seed=7)
+    return [MimoPass(layer, S, L, seed=1000 * rank + i, device=device)
+            for i, (_, S, L) in enumerate(MIMO_PASSES)]
+
+
+def _time_passes(passes, steps, stream):
+    """Runs `steps` fwd+bwd sweeps over `passes`; returns (total ms, per-pass fwd / bwd ms)."""
+    sh = stream.cuda_stream
+    ev = [[[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in passes] for _ in range(steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for k in range(steps):
+        for i, p in enumerate(passes):
+            ev[k][i][0].record(stream)
+            p.fwd(sh)
+            ev[k][i][1].record(stream)
+            p.bwd(sh)
+            ev[k][i][2].record(stream)
+    end.record(stream)
+    return start, end, ev
+
+
+def run_scan(args, rank, local_rank, world):
+    from semambaxlinoss_b200 import _lib
+
+    spec = WORKLOADS[args.workload]
+    chunk = args.chunk or spec["chunk"]
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
-    if world > 1:
-        import torch.distributed as dist
-        from datetime import timedelta
-
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
-    passes = [LinossPass(S, L, seed=1000 * rank + i, device=device, chunk=args.chunk)
-              for i, (_, S, L) in enumerate(PASSES)]
+    _init_dist(world, device)
+    passes = _make_passes(args.workload, rank, device, chunk)
     stream = torch.cuda.current_stream(device)
     sh = stream.cuda_stream
-    step_bytes = sum(p.units * (FWD_BYTES_PER_STEP + BWD_BYTES_PER_STEP) for p in passes)
-    launches_per_step = 3 * len(passes)  # fwd, bwd, finalize per pass
+    step_bytes = sum(p.units * (p.fwd_bytes_per_unit + p.bwd_bytes_per_unit) for p in passes)
 
-    def step(ev=None):
-        for i, p in enumerate(passes):
-            if ev is not None:
-                ev[i][0].record(stream)
+    def step():
+        for p in passes:
             p.fwd(sh)
-            if ev is not None:
-                ev[i][1].record(stream)
             p.bwd(sh)
-            if ev is not None:
-                ev[i][2].record(stream)
-
-    def barrier():
-        torch.cuda.synchronize(device)
-        if world > 1:
-            import torch.distributed as dist
-
-            dist.barrier()
-        torch.cuda.synchronize(device)
-
-    uuid = None
-    try:
-        uuid = str(torch.cuda.get_device_properties(device).uuid)
-        uuid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
-    except Exception:
-        pass
-    clocks = ClockSampler(uuid, args.clocks_log if rank == 0 else None)
 
     for _ in range(max(args.warmup, 3)):
         step()
+    clocks = ClockSampler(_device_uuid(device), args.clocks_log if rank == 0 else None)
     # Keep the GPU busy ~1.5 s before timing so the clock samples see it under load.
     soak_t0 = time.time()
     torch.cuda.synchronize(device)
     while not args.no_soak and time.time() - soak_t0 < 1.5:
-        for _ in range(20):
+        for _ in range(5):
             step()
         torch.cuda.synchronize(device)
 
-    ev = [[[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in passes]
-          for _ in range(args.steps)]
-    barrier()
-    t_wall0 = time.time()
-    start = torch.cuda.Event(enable_timing=True)
-    end = torch.cuda.Event(enable_timing=True)
-    start.record(stream)
-    for k in range(args.steps):
-        step(ev[k])
-    end.record(stream)
-    barrier()
+    _barrier(world, device)
+    n0 = _lib.launch_count()
+    start, end, ev = _time_passes(passes, args.steps, stream)
+    _barrier(world, device)
+    launches = _lib.launch_count() - n0
     t_wall1 = time.time()
-    elapsed = start.elapsed_time(end)
-    clocks.stop()
-    fwd_ms = [ev[k][i][0].elapsed_time(ev[k][i][1]) for k in range(args.steps) for i in range(len(passes))]
-    bwd_ms = [ev[k][i][1].elapsed_time(ev[k][i][2]) for k in range(args.steps) for i in range(len(passes))]
-
-    t = torch.tensor([elapsed], device=device)
-    if world > 1:
-        import torch.distributed as dist
-
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    elapsed = t.item()
-    ms_per_step = elapsed / args.steps
+    ms_per_step = _max_over_ranks(start.elapsed_time(end), world, device) / args.steps
     value = world * step_bytes / (ms_per_step * 1e-3) / 1e9
+    per_pass = []
+    for i, p in enumerate(passes):
+        f = statistics.mean(ev[k][i][0].elapsed_time(ev[k][i][1]) for k in range(args.steps))
+        b = statistics.mean(ev[k][i][1].elapsed_time(ev[k][i][2]) for k in range(args.steps))
+        per_pass.append((p, f, b))
 
-    e2e = None if args.no_e2e else run_e2e(passes, args, device, stream, step_bytes, world)
-    if world > 1:
-        import torch.distributed as dist
+    # Kernel roofline: for the MIMO layer, the fused scan + readout kernels timed alone.
+    kpasses = per_pass
+    if args.workload == "mimo":
+        kp = [MimoKernelPass(S, L, seed=5000 + i, device=device) for i, (_, S, L) in enumerate(MIMO_PASSES)]
+        for _ in range(3):
+            for p in kp:
+                p.fwd(sh)
+                p.bwd(sh)
+        torch.cuda.synchronize(device)
+        ks, ke, kev = _time_passes(kp, max(3, args.steps // 2), stream)
+        torch.cuda.synchronize(device)
+        kn = max(3, args.steps // 2)
+        kpasses = [(p, statistics.mean(kev[k][i][0].elapsed_time(kev[k][i][1]) for k in range(kn)),
+                    statistics.mean(kev[k][i][1].elapsed_time(kev[k][i][2]) for k in range(kn)))
+                   for i, p in enumerate(kp)]
+        del kp
 
-        dist.barrier()
-        dist.destroy_process_group()
+    e2e = None if args.no_e2e else run_scan_e2e(passes, args, device, stream, step_bytes, world)
+    clocks.stop()
+    _finish_dist(world)
     if rank != 0:
         return
 
     peak, peak_kind = load_peaks()
-    units = passes[0].units  # both passes process S*L = 129,684 (sequence, step) units
-    fwd_avg, bwd_avg = statistics.mean(fwd_ms), statistics.mean(bwd_ms)
-    fwd_gbs = units * FWD_BYTES_PER_STEP / (fwd_avg * 1e-3) / 1e9
-    bwd_gbs = units * BWD_BYTES_PER_STEP / (bwd_avg * 1e-3) / 1e9
-    dom = "linoss_bwd_kernel" if bwd_avg >= fwd_avg else "linoss_fwd_kernel"
-    dom_gbs = bwd_gbs if dom == "linoss_bwd_kernel" else fwd_gbs
+    fwd_ms = sum(f for _, f, _ in kpasses)
+    bwd_ms = sum(b for _, _, b in kpasses)
+    fwd_bytes = sum(p.units * p.fwd_bytes_per_unit for p, _, _ in kpasses)
+    bwd_bytes = sum(p.units * p.bwd_bytes_per_unit for p, _, _ in kpasses)
+    kf, kb = kpasses[0][0].kernels
+    dom, dom_bytes, dom_ms = (kb, bwd_bytes, bwd_ms) if bwd_ms >= fwd_ms else (kf, fwd_bytes, fwd_ms)
+    dom_gbs = dom_bytes / (dom_ms * 1e-3) / 1e9
     traffic = profiled_traffic(dom)
     out = {
-        "metric": METRIC,
+        "metric": spec["metric"],
         "value": round(value, 2),
         "unit": "GB/s",
         "n_gpus": world,
@@ -303,14 +646,14 @@ def run_semx(args, rank, local_rank, world):
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": "f32",
-        "data": "synthetic (seeded; distributions of config 1)",
+        "dtype": spec["dtype"],
+        "data": spec["data"],
         "config": {
-            "workload": "LinOSS-IMEX scan fwd+bwd, time 404x321 + freq 1284x101, P=256, H=64",
-            "passes": [{"axis": n, "sequences": S, "steps": L} for n, S, L in PASSES],
-            "oscillators": P, "chunk": args.chunk,
+            "workload": spec["describe"],
+            "passes": [{"sequences": p.S, "steps": p.L} for p in passes],
+            "chunk": chunk or None,
             "bytes_per_step": step_bytes,
-            "l2": "no flush: every operand is 265 MB, larger than the 126 MB L2",
+            "l2": spec["l2"],
             "parallelism": f"weak dp{world}: each rank scans its own batch, no collective",
         },
         "roofline": {
@@ -322,142 +665,122 @@ def run_semx(args, rank, local_rank, world):
             "frac": round(dom_gbs / peak, 4),
             "peak_kind": peak_kind,
             "traffic": traffic,
-            "note": "event pair around semx_linoss_bwd also covers its finalize launch (a few us)",
+            "algorithmic_bytes_first_launch": kpasses[0][0].units * (
+                kpasses[0][0].bwd_bytes_per_unit if dom == kb else kpasses[0][0].fwd_bytes_per_unit),
+            "note": "achieved = algorithmic bytes / CUDA-event time of the entry point (includes its "
+                    "small reduction launches); traffic = ncu DRAM bytes of one launch of the first pass",
         },
         "kernels": {
-            "linoss_fwd_kernel": {"ms": round(fwd_avg, 4), "GB/s": round(fwd_gbs, 1),
-                                  "bytes_per_launch": units * FWD_BYTES_PER_STEP},
-            "linoss_bwd_kernel+finalize": {"ms": round(bwd_avg, 4), "GB/s": round(bwd_gbs, 1),
-                                           "bytes_per_launch": units * BWD_BYTES_PER_STEP},
+            f"{kf}": {"ms": round(fwd_ms, 4), "GB/s": round(fwd_bytes / (fwd_ms * 1e-3) / 1e9, 1),
+                      "bytes": fwd_bytes},
+            f"{kb}+reductions": {"ms": round(bwd_ms, 4), "GB/s": round(bwd_bytes / (bwd_ms * 1e-3) / 1e9, 1),
+                                 "bytes": bwd_bytes},
         },
         "hbm_frac_of_8tbs": round(value / world / 8000.0, 4),
-        "gpu_launches": launches_per_step * args.steps,
+        "gpu_launches": launches,
         "clocks": clocks.summary(soak_t0, t_wall1),
         "e2e": e2e,
     }
+    if args.workload == "mimo":
+        out["layer_ms"] = {"fwd": round(sum(f for _, f, _ in per_pass), 4),
+                           "bwd": round(sum(b for _, _, b in per_pass), 4)}
+        out["gpu_launches_note"] = "libsemx kernels only; the layer's projections run as torch/cuBLAS kernels"
     if world == 1 and not args.no_cpu_baseline:
-        out["cpu_baseline"] = cpu_baseline(args.cpu_sample_frac, repeats=3)
+        out["cpu_baseline"] = cpu_baseline(args.workload, args.cpu_sample_frac or spec["cpu_frac"], repeats=3)
     print(json.dumps(out), flush=True)
 
 
-def run_e2e(passes, args, device, stream, step_bytes, world):
-    """Same metric through the C ABI with host buffers: every step copies Bu and dY2 from
-    pinned host memory, runs forward and backward, and copies y2, dBu and the parameter
-    gradients back to pinned host memory, all inside the timed region."""
+def run_scan_e2e(passes, args, device, stream, step_bytes, world):
+    """The same metric through the public entry points with host buffers: every step copies
+    the pass inputs from pinned host memory, runs forward and backward, and copies the
+    outputs and gradients back to pinned host memory, all inside the timed region."""
     sh = stream.cuda_stream
-    host = []
-    for p in passes:
-        host.append({
-            "Bu": p.Bu.cpu().pin_memory(), "dY2": p.dY2.cpu().pin_memory(),
-            "Y2": torch.empty(p.Y2.shape, dtype=p.Y2.dtype).pin_memory(),
-            "dBu": torch.empty(p.dBu.shape, dtype=p.dBu.dtype).pin_memory(),
-            "dparams": torch.empty(3, P).pin_memory(),
-        })
-    h2d = sum(h["Bu"].numel() * 8 + h["dY2"].numel() * 8 for h in host)
-    d2h = sum(h["Y2"].numel() * 8 + h["dBu"].numel() * 8 + 3 * P * 4 for h in host)
+    step_passes = passes
+    host_in = [[t.detach().cpu().pin_memory() for t in p.inputs] for p in step_passes]
+    for p in step_passes:  # outputs exist after one step
+        p.fwd(sh)
+        p.bwd(sh)
+    torch.cuda.synchronize(device)
+    host_out = [[torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in p.outputs] for p in step_passes]
+    h2d = sum(t.numel() * t.element_size() for hs in host_in for t in hs)
+    d2h = sum(t.numel() * t.element_size() for hs in host_out for t in hs)
 
     def e2e_step():
-        for p, h in zip(passes, host):
-            p.Bu.copy_(h["Bu"], non_blocking=True)
-            p.dY2.copy_(h["dY2"], non_blocking=True)
+        for p, hi, ho in zip(step_passes, host_in, host_out):
+            for d, h in zip(p.inputs, hi):
+                d.copy_(h, non_blocking=True)
             p.fwd(sh)
             p.bwd(sh)
-            h["Y2"].copy_(p.Y2, non_blocking=True)
-            h["dBu"].copy_(p.dBu, non_blocking=True)
-            h["dparams"].copy_(p.dparams, non_blocking=True)
+            for d, h in zip(p.outputs, ho):
+                h.copy_(d, non_blocking=True)
 
     e2e_step()
-    torch.cuda.synchronize(device)
-    if world > 1:
-        import torch.distributed as dist
-
-        dist.barrier()
+    _barrier(world, device)
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s.record(stream)
     for _ in range(args.e2e_steps):
         e2e_step()
     e.record(stream)
     torch.cuda.synchronize(device)
-    t = torch.tensor([s.elapsed_time(e)], device=device)
-    if world > 1:
-        import torch.distributed as dist
-
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = t.item() / args.e2e_steps
+    ms = _max_over_ranks(s.elapsed_time(e), world, device) / args.e2e_steps
     return {"value": round(world * step_bytes / (ms * 1e-3) / 1e9, 3), "unit": "GB/s",
             "ms_per_step": round(ms, 3), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-            "path": "C ABI (semx_linoss_fwd/bwd) with pinned host buffers, one stream"}
+            "path": "public entry points with pinned host buffers, one stream"}
 
 
 # ----------------------------------------------------------------------------- CPU legs
-def _cpu_sample(frac, seed=0):
-    g = torch.Generator().manual_seed(seed)
-    steps = torch.randn(P, generator=g)
-    A = torch.randn(P, generator=g)
-    sample = []
-    for _, S, L in PASSES:
-        s = max(1, int(round(S * frac)))
-        Bw = torch.randn(P, H, 2, generator=g) / H**0.5
-        u = torch.randn(s, L, H, generator=g)
-        Bu = torch.complex(u @ Bw[..., 0].t(), u @ Bw[..., 1].t())
-        gy = torch.complex(torch.randn(s, L, P, generator=g), torch.randn(s, L, P, generator=g))
-        sample.append((s, L, Bu, gy))
-    return steps, A, sample
-
-
-def _cpu_step(steps, A, sample):
-    """The reference's CPU path for this scan (oracle port of models/linoss/linoss.py:
-    constraints, IMEX discretisation and the sequential _linoss_recurrence), fwd + bwd."""
-    from oracle import linoss as olin
-
-    for s, L, Bu, gy in sample:
-        st = steps.clone().requires_grad_(True)
-        a = A.clone().requires_grad_(True)
-        b = Bu.clone().requires_grad_(True)
-        y2 = olin.linoss_scan_fused("IMEX", st, a, None, b)
-        (y2.real * gy.real + y2.imag * gy.imag).sum().backward()
-
-
-def _sample_bytes(sample):
-    return sum(s * L * (FWD_BYTES_PER_STEP + BWD_BYTES_PER_STEP) for s, L, _, _ in sample)
-
-
-def cpu_baseline(frac, repeats=3):
+def cpu_baseline(workload, frac, repeats=3):
+    spec = WORKLOADS[workload]
     torch.set_num_threads(os.cpu_count())
-    steps, A, sample = _cpu_sample(frac)
-    _cpu_step(steps, A, sample)
+    sample = spec["cpu_sample"](frac)
+    spec["cpu_step"](sample)
     times = []
     for _ in range(repeats):
         t0 = time.perf_counter()
-        _cpu_step(steps, A, sample)
+        spec["cpu_step"](sample)
         times.append(time.perf_counter() - t0)
     t = statistics.median(times)
-    desc = " + ".join(f"{s}x{L}" for s, L, _, _ in sample)
-    return {"value": round(_sample_bytes(sample) / t / 1e9, 4), "unit": "GB/s",
+    return {"value": round(sample["bytes"] / t / 1e9, 5), "unit": "GB/s",
             "cores": torch.get_num_threads(), "kind": "port",
-            "sample": f"{frac:.4g} of each pass's sequences ({desc}), fwd+bwd float32, median of {repeats}",
+            "sample": f"{frac:.4g} of each pass's sequences ({sample['desc']}), fwd+bwd float32, "
+                      f"median of {repeats}",
             "seconds": round(t, 3)}
 
 
 def run_reference(args, rank):
     if rank != 0:
         return
+    if args.workload not in WORKLOADS:
+        print(json.dumps({"impl": "reference", "unavailable": "the reference generator needs the "
+                          "third-party mamba_ssm package, which the reference does not ship"}))
+        return
+    spec = WORKLOADS[args.workload]
     torch.set_num_threads(os.cpu_count())
-    steps, A, sample = _cpu_sample(args.ref_sample_frac)
+    frac = args.ref_sample_frac
+    if frac is None:
+        # Size the per-step sample so that warm-up + timed steps end within about two
+        # minutes on this host: time one step of a small sample, then scale (never above
+        # the workload's default fraction).
+        f0 = spec["ref_frac"] / 8
+        probe = spec["cpu_sample"](f0)
+        t0 = time.perf_counter()
+        spec["cpu_step"](probe)
+        t_probe = max(time.perf_counter() - t0, 1e-3)
+        frac = min(spec["ref_frac"], probe["frac"] * 120.0 / ((args.steps + args.warmup) * t_probe))
+    sample = spec["cpu_sample"](frac)
     for _ in range(args.warmup):
-        _cpu_step(steps, A, sample)
+        spec["cpu_step"](sample)
     times = []
     for _ in range(args.steps):
         t0 = time.perf_counter()
-        _cpu_step(steps, A, sample)
+        spec["cpu_step"](sample)
         times.append(time.perf_counter() - t0)
     ms = 1e3 * sum(times) / len(times)
-    value = _sample_bytes(sample) / (ms * 1e-3) / 1e9
-    desc = " + ".join(f"{s}x{L}" for s, L, _, _ in sample)
+    value = sample["bytes"] / (ms * 1e-3) / 1e9
     print(json.dumps({
         "impl": "reference",
-        "metric": METRIC,
-        "value": round(value, 4),
+        "metric": spec["metric"],
+        "value": round(value, 5),
         "unit": "GB/s",
         "n_gpus": 0,
         "steps": args.steps,
@@ -466,49 +789,23 @@ def run_reference(args, rank):
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": "f32",
-        "data": "synthetic (seeded; distributions of config 1)",
-        "config": {"workload": "LinOSS-IMEX scan fwd+bwd, time 404x321 + freq 1284x101, P=256, H=64",
-                   "sample": desc},
-        "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": torch.get_num_threads(),
+        "dtype": spec["dtype"],
+        "data": spec["data"],
+        "config": {"workload": spec["describe"], "sample": sample["desc"]},
+        "cpu_baseline": {"value": round(value, 5), "unit": "GB/s", "cores": torch.get_num_threads(),
                          "kind": "port",
-                         "sample": f"{args.ref_sample_frac:.4g} of each pass's sequences ({desc}) per step"},
-        "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                         "sample": f"{frac:.4g} of each pass's sequences ({sample['desc']}) per step"},
+        "e2e": {"value": round(value, 5), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }), flush=True)
 
 
 # ----------------------------------------------------------------- generator workloads
-def _barrier(world, device):
-    torch.cuda.synchronize(device)
-    if world > 1:
-        import torch.distributed as dist
-
-        dist.barrier()
-    torch.cuda.synchronize(device)
-
-
-def _max_over_ranks(ms, world, device):
-    t = torch.tensor([ms], device=device)
-    if world > 1:
-        import torch.distributed as dist
-
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return t.item()
-
-
-def _init_dist(world, device):
-    if world > 1:
-        import torch.distributed as dist
-        from datetime import timedelta
-
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
-
-
 def run_generator(args, rank, local_rank, world):
-    """Config 3: SEMamba generator training step (forward + generator losses + backward +
-    DDP gradient all-reduce + AdamW), bf16 autocast around fp32 scans, `--batch`
-    two-second utterances per GPU. Metric: frames/s over all GPUs."""
+    """SEMamba generator training step (forward + generator losses + backward + DDP
+    gradient all-reduce + AdamW), bf16 autocast around fp32 scans, `--batch` two-second
+    utterances per GPU. Metric: frames/s over all GPUs."""
+    from semambaxlinoss_b200 import _lib
     from semambaxlinoss_b200.generator import SEMamba, config3_cfg, generator_loss, mag_phase_stft
 
     device = torch.device("cuda", local_rank)
@@ -550,16 +847,17 @@ def run_generator(args, rank, local_rank, world):
     stream = torch.cuda.current_stream(device)
     for _ in range(max(args.warmup, 3)):
         step(clean_d, noisy_d)
-    uuid = _device_uuid(device)
-    clocks = ClockSampler(uuid, args.clocks_log if rank == 0 else None)
+    clocks = ClockSampler(_device_uuid(device), args.clocks_log if rank == 0 else None)
     soak_t0 = time.time()
     _barrier(world, device)
+    n0 = _lib.launch_count()
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s.record(stream)
     for _ in range(args.steps):
         loss = step(clean_d, noisy_d)
     e.record(stream)
     _barrier(world, device)
+    launches = _lib.launch_count() - n0
     t_end = time.time()
     ms = _max_over_ranks(s.elapsed_time(e), world, device) / args.steps
     # End to end: audio copied in from pinned host memory and the loss read back, every step.
@@ -581,12 +879,12 @@ def run_generator(args, rank, local_rank, world):
         return
     fps = world * B * frames / (ms * 1e-3)
     print(json.dumps({
-        "metric": "SEMamba generator training step, frames/s (config 3: 2 s utterances, batch 16 per GPU)",
+        "metric": "SEMamba generator training step, frames/s (2 s utterances, batch 16 per GPU)",
         "value": round(fps, 1), "unit": "frames/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16 autocast, fp32 scans",
         "data": "synthetic (clean ~ N(0, 0.1), noise ~ N(0, 0.05), seeded per rank)",
-        "config": {"workload": "config 3: generator fwd + losses + bwd + AdamW, 4 TF-blocks (time: selective-LRU "
+        "config": {"workload": "generator fwd + losses + bwd + AdamW, 4 TF-blocks (time: selective-LRU "
                                "d_inner 256 N 16; freq: damped-IMEX LinOSS P 16), hid 64",
                    "global_batch": world * B, "seq_len": frames, "parallelism": f"ddp{world}",
                    "parameters": n_params,
@@ -594,14 +892,18 @@ def run_generator(args, rank, local_rank, world):
         "e2e": {"value": round(world * B * frames / (ms_e2e * 1e-3), 1), "unit": "frames/s",
                 "ms_per_step": round(ms_e2e, 3), "h2d_bytes_per_step": 2 * B * seg * 4,
                 "d2h_bytes_per_step": 4},
+        "gpu_launches": launches,
+        "gpu_launches_note": "libsemx kernels only (scans, their reductions); convolutions, GEMMs and "
+                             "the optimizer run as torch/cuDNN/cuBLAS kernels",
         "clocks": clocks.summary(soak_t0, t_end),
     }), flush=True)
 
 
 def run_inference(args, rank, local_rank, world):
-    """Config 4: 64 sixty-second utterances (T = 9601 frames) enhanced end to end (STFT ->
-    generator -> iSTFT) under no_grad with bf16 autocast, sharded over the GPUs,
-    `--micro-batch` utterances per forward. Metric: frames/s over all GPUs."""
+    """64 sixty-second utterances (T = 9601 frames) enhanced end to end (STFT -> generator
+    -> iSTFT) under no_grad with bf16 autocast, sharded over the GPUs, `--micro-batch`
+    utterances per forward. Metric: frames/s over all GPUs."""
+    from semambaxlinoss_b200 import _lib
     from semambaxlinoss_b200.generator import SEMamba, config3_cfg, mag_phase_istft, mag_phase_stft
 
     device = torch.device("cuda", local_rank)
@@ -633,16 +935,17 @@ def run_inference(args, rank, local_rank, world):
 
     stream = torch.cuda.current_stream(device)
     run_all()  # warm-up pass over the shard
-    uuid = _device_uuid(device)
-    clocks = ClockSampler(uuid, args.clocks_log if rank == 0 else None)
+    clocks = ClockSampler(_device_uuid(device), args.clocks_log if rank == 0 else None)
     t0 = time.time()
     _barrier(world, device)
+    n0 = _lib.launch_count()
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s.record(stream)
     for _ in range(args.steps):
         run_all()
     e.record(stream)
     _barrier(world, device)
+    launches = _lib.launch_count() - n0
     t1 = time.time()
     clocks.stop()
     ms = _max_over_ranks(s.elapsed_time(e), world, device) / args.steps
@@ -654,36 +957,25 @@ def run_inference(args, rank, local_rank, world):
         return
     fps = total * frames / (ms * 1e-3)
     print(json.dumps({
-        "metric": "SEMamba long-utterance inference, frames/s (config 4: 64 x 60 s, sharded)",
+        "metric": "SEMamba long-utterance inference, frames/s (64 x 60 s utterances, sharded)",
         "value": round(fps, 1), "unit": "frames/s", "n_gpus": world, "steps": args.steps, "warmup": 1,
         "ms_per_step": round(ms, 2), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "bf16 autocast, fp32 scans", "data": "synthetic (audio ~ N(0, 0.1), seeded per rank)",
-        "config": {"workload": "config 4: STFT -> generator -> iSTFT, no_grad", "global_batch": total,
-                   "seq_len": frames, "micro_batch": mb, "parallelism": f"sharded over {world} GPUs"},
+        "config": {"workload": "STFT -> generator -> iSTFT, no_grad, 64 utterances of 60 s",
+                   "global_batch": total, "seq_len": frames, "micro_batch": mb,
+                   "parallelism": f"sharded over {world} GPUs"},
         "e2e": {"value": round(fps, 1), "unit": "frames/s", "h2d_bytes_per_step": total * seg * 4 // world,
                 "d2h_bytes_per_step": total * seg * 4 // world,
                 "note": "every step copies its audio in from pinned host memory and the enhanced audio out"},
+        "gpu_launches": launches,
         "clocks": clocks.summary(t0, t1),
     }), flush=True)
-
-
-def _device_uuid(device):
-    try:
-        u = str(torch.cuda.get_device_properties(device).uuid)
-        return u if u.startswith("GPU-") else "GPU-" + u
-    except Exception:
-        return None
 
 
 def main():
     args = parse_args()
     rank, local_rank, world = dist_env()
     if args.impl == "reference":
-        if args.workload != "linoss":
-            if rank == 0:
-                print(json.dumps({"impl": "reference", "unavailable": "the reference generator needs the "
-                                  "third-party mamba_ssm package, which the reference does not ship"}))
-            return
         run_reference(args, rank)
         return
     if args.workload == "generator":
@@ -691,7 +983,7 @@ def main():
     elif args.workload == "inference":
         run_inference(args, rank, local_rank, world)
     else:
-        run_semx(args, rank, local_rank, world)
+        run_scan(args, rank, local_rank, world)
 
 
 if __name__ == "__main__":

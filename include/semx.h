@@ -60,6 +60,10 @@ int semx_abi_version(void);
 const char* semx_status_string(int status);
 /* Message describing the last failing call made from this host thread ("" if none). */
 const char* semx_last_error(void);
+/* Number of kernels this library has launched successfully in this process, all host
+ * threads and devices together (a monotonically increasing counter). No counterpart in
+ * the reference; it lets a caller count the device launches of a region of its own. */
+uint64_t semx_launch_count(void);
 
 /* ------------------------------------------------------------------------------------
  * LinOSS oscillatory scan.

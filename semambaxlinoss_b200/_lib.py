@@ -143,6 +143,7 @@ _SIGNATURES = {
     "semx_abi_version": (ctypes.c_int, []),
     "semx_status_string": (ctypes.c_char_p, [ctypes.c_int]),
     "semx_last_error": (ctypes.c_char_p, []),
+    "semx_launch_count": (ctypes.c_uint64, []),
     "semx_linoss_args_size": (ctypes.c_size_t, []),
     "semx_linoss_ckpt_bytes": (
         ctypes.c_size_t,
@@ -245,3 +246,8 @@ def new_args(cls):
     a = cls()
     a.struct_size = ctypes.sizeof(cls)
     return a
+
+
+def launch_count() -> int:
+    """Kernels the library has launched in this process so far (all threads, devices)."""
+    return int(load().semx_launch_count())

@@ -1,4 +1,5 @@
 // ABI bookkeeping: version, status strings and the per-host-thread error message.
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -8,6 +9,7 @@
 namespace semx {
 
 thread_local char g_last_error[512] = {0};
+std::atomic<uint64_t> g_launches{0};
 
 int fail(int code, const char* fmt, ...) {
   va_list ap;
@@ -48,6 +50,7 @@ int bind_device(std::initializer_list<const void*> ptrs) {
 int check_launch(const char* what) {
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(SEMX_ERR_LAUNCH, "%s: %s", what, cudaGetErrorString(e));
+  g_launches.fetch_add(1, std::memory_order_relaxed);
   return SEMX_OK;
 }
 
@@ -73,5 +76,7 @@ const char* semx_status_string(int status) {
 }
 
 const char* semx_last_error(void) { return semx::g_last_error; }
+
+uint64_t semx_launch_count(void) { return semx::g_launches.load(std::memory_order_relaxed); }
 
 }  // extern "C"

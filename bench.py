@@ -514,7 +514,7 @@ WORKLOADS = {
                     "C=256 channels, N=16 modes",
         "data": "synthetic, seeded: x ~ N(0,1), dt = softplus(N(-2,0.5)), a ~ U(1,16), B, C ~ N(0,1/16)",
         "dtype": "f32",
-        "chunk": 64, "cpu_frac": 8.0 / 404, "ref_frac": 4.0 / 404,
+        "chunk": 16, "cpu_frac": 8.0 / 404, "ref_frac": 4.0 / 404,
         "l2": "no flush: x, dt, dy, y and each gradient are 133 MB, larger than the 126 MB L2",
         "cpu_sample": _slru_cpu_sample, "cpu_step": _slru_cpu_step,
     },

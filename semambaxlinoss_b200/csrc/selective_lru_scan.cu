@@ -8,23 +8,24 @@
 // Thread layout. A thread owns (sequence s, channel c, group g of kGM = 4 modes): lane
 // = cl * NG + g, where NG = ceil(N / 4) lanes share a channel and a warp covers 32 / NG
 // channels of the same sequence. A CTA of kThreads covers CB = kThreads / NG channels;
-// grid = (channel blocks, sequences). The time loop is sequential with one step of
-// register prefetch; the pole, drive and gain of every (t, c, n) are computed in
-// registers from delta_nu / delta_theta and never touch HBM.
+// grid = (channel blocks, sequences). The operands of a block of consecutive steps for the
+// CTA's channels (delta_nu, x, delta_theta, dy; B_t, C_t) are staged in shared memory by
+// all threads together with cp.async, double-buffered; the pole, drive and gain of every
+// (t, c, n) are computed in registers and never touch HBM.
 //
 // Forward: y_t = sum over modes (reduced over the NG lanes of a channel by shuffles).
 // Training forwards also store the state entering every `chunk`-step block.
 //
-// Backward, per chunk (last first):
+// Backward, per chunk (last first), on the chunk's staged operands:
 //   pass 1  re-runs the chunk from its checkpoint, dropping the state every kR steps
 //           into shared memory;
-//   pass 2  walks kTT-step tiles backwards; inside a tile, kR-step sub-blocks backwards:
-//           recompute the kR states into registers, then run the adjoint
-//           G_t = g_t + conj(lam_{t+1}) G_{t+1} through them. Per-(t, c) gradients are
-//           reduced over the NG lanes by shuffles; per-(t, n) gradients dB / dC are
-//           reduced over channels in a fixed order: transposed shuffles inside the
-//           warp, then shared memory across warps, then DSMEM across the CTAs of a
-//           thread-block cluster that spans all channel blocks of the sequence.
+//   pass 2  walks kR-step sub-blocks backwards: recompute the kR states into registers,
+//           then run the adjoint through them in carry form, c_t = conj(lam_t) G_t,
+//           G_t = g_t + c_{t+1}. Per-(t, c) gradients are reduced over the NG lanes by
+//           shuffles; per-(t, n) gradients dB / dC are reduced over channels in a fixed
+//           order: transposed shuffles inside the warp, then shared memory across warps,
+//           then DSMEM across the CTAs of a thread-block cluster that spans all channel
+//           blocks of the sequence, every kFlush steps.
 // Per-(c, n) parameter gradients are summed per thread over time, written per sequence,
 // and reduced over sequences by a two-stage fixed-order column sum.
 #include <cooperative_groups.h>
@@ -37,9 +38,11 @@ namespace cg = cooperative_groups;
 namespace {
 
 constexpr int kThreads = 128;
-constexpr int kGM = 4;   // modes per thread
-constexpr int kR = 4;    // steps per register-resident sub-block (backward)
-constexpr int kTT = 16;  // steps per dB/dC reduction tile (backward)
+constexpr int kGM = 4;      // modes per thread
+constexpr int kR = 4;       // steps per register-resident sub-block (backward)
+constexpr int kFlush = 8;   // steps per dB/dC cluster reduction (backward)
+constexpr int kTileF = 32;  // steps per staged tile, forward
+constexpr int kTileB = 16;  // steps per staged tile, backward
 constexpr int kMaxClusterCTAs = 8;
 constexpr float kLog2e = 1.4426950408889634f;
 
@@ -83,8 +86,8 @@ struct SParams {
   float* dbc_part;  // (S*L, nclusters, narr*N) when nclusters > 1
 };
 
-// Per-element transcendentals on the special-function unit (PTX ex2 / sin / cos / sqrt
-// .approx: one MUFU instruction each instead of a libm call). sin and cos take their
+// Per-element transcendentals on the special-function unit (PTX ex2 / sin / cos / rsqrt /
+// rcp .approx: one MUFU instruction each instead of a libm call). sin and cos take their
 // argument reduced to [-pi, pi] first: r = x - k * 2pi with k = rint(x / 2pi) and 2pi
 // split Cody-Waite style into hi = 6.28125 (exact: k * hi has no rounding for |k| < 2^16)
 // plus lo = 2pi - hi, so r carries no reduction error worth speaking of.
@@ -93,31 +96,46 @@ __device__ __forceinline__ float ex2_approx(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
-__device__ __forceinline__ float sqrt_approx(float x) {
+__device__ __forceinline__ float rsqrt_approx(float x) {
   float y;
-  asm("sqrt.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  asm("rsqrt.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
-__device__ __forceinline__ void sincos_reduced(float x, float* s, float* c) {
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float reduce_2pi(float x) {
   constexpr float kInv2Pi = 0.15915494f;
   constexpr float k2PiHi = 6.28125f;
   constexpr float k2PiLo = 0.0019353072f;
   const float k = rintf(x * kInv2Pi);
-  const float r = fmaf(-k, k2PiLo, fmaf(-k, k2PiHi, x));
+  return fmaf(-k, k2PiLo, fmaf(-k, k2PiHi, x));
+}
+__device__ __forceinline__ void sincos_reduced(float x, float* s, float* c) {
+  const float r = reduce_2pi(x);
   asm("sin.approx.f32 %0, %1;" : "=f"(*s) : "f"(r));
   asm("cos.approx.f32 %0, %1;" : "=f"(*c) : "f"(r));
 }
+__device__ __forceinline__ float sin_reduced(float x) {
+  const float r = reduce_2pi(x);
+  float s;
+  asm("sin.approx.f32 %0, %1;" : "=f"(s) : "f"(r));
+  return s;
+}
 
-// Pole, drive gain and their intermediates for one (t, c, n).
+// Pole, drive gain and their intermediates for one (t, c, n): lam = nu (cs + j sn),
+// gain = gr + j gi; rs = 1 / gr for the gamma gain, inv_den = 1 / |A_c|^2 for ZOH.
 struct Disc {
-  float nu, cs, sn, base, lre, lim, gr, gi, den;
+  float nu, cs, sn, base, lre, lim, gr, gi, rs, inv_den;
 };
 
 template <bool REAL, int GAIN>
-__device__ __forceinline__ Disc discretise(float a, float a2, float om, float sd, bool detune,
+__device__ __forceinline__ Disc discretise(float a, float om, float sd, bool detune,
                                            float dnu, float dth) {
   Disc d;
-  d.nu = ex2_approx(-dnu * a2);
+  d.nu = ex2_approx(-dnu * (a * kLog2e));
   if (REAL) {
     d.cs = 1.f;
     d.sn = 0.f;
@@ -131,24 +149,27 @@ __device__ __forceinline__ Disc discretise(float a, float a2, float om, float sd
     d.lim = d.nu * d.sn;
   }
   d.gi = 0.f;
-  d.den = 1.f;
+  d.rs = 1.f;
+  d.inv_den = 1.f;
   if (GAIN == SEMX_GAIN_GAMMA) {
-    d.gr = sqrt_approx(fmaxf(1.f - d.nu * d.nu, 1e-6f));
+    // sqrt(max(1 - nu^2, 1e-6)) as q * rsqrt(q): the reciprocal serves the backward.
+    const float q = fmaxf(1.f - d.nu * d.nu, 1e-6f);
+    d.rs = rsqrt_approx(q);
+    d.gr = q * d.rs;
   } else if (GAIN == SEMX_GAIN_MAMBA) {
     d.gr = dnu;
   } else {  // ZOH: (lam - 1) / A_c, A_c = -a + j base, with lam - 1 from expm1
     const float em1 = expm1f(-dnu * a);
     if (REAL) {
-      d.den = fmaxf(a * a, 1e-8f);
-      d.gr = -(a * em1) / d.den;
+      d.inv_den = rcp_approx(fmaxf(a * a, 1e-8f));
+      d.gr = -(a * em1) * d.inv_den;
     } else {
-      float sh, ch;
-      sincos_reduced(0.5f * (dnu * d.base), &sh, &ch);
+      const float sh = sin_reduced(0.5f * (dnu * d.base));
       const float lm1r = em1 * d.cs - 2.f * sh * sh;
       const float lm1i = d.lim;
-      d.den = fmaxf(a * a + d.base * d.base, 1e-8f);
-      d.gr = (d.base * lm1i - a * lm1r) / d.den;
-      d.gi = -(a * lm1i + d.base * lm1r) / d.den;
+      d.inv_den = rcp_approx(fmaxf(a * a + d.base * d.base, 1e-8f));
+      d.gr = (d.base * lm1i - a * lm1r) * d.inv_den;
+      d.gi = -(a * lm1i + d.base * lm1r) * d.inv_den;
     }
   }
   return d;
@@ -156,70 +177,16 @@ __device__ __forceinline__ Disc discretise(float a, float a2, float om, float sd
 
 template <bool REAL>
 struct StepIn {
-  float dnu, dth, x;
+  float dnu, dth, x, dy;
   float bre[kGM], bim[kGM], cre[kGM], cim[kGM];
 };
-
-// Loads the operands of step t for this thread's channel and modes (zeros when invalid).
-template <bool REAL, bool WITH_C>
-__device__ __forceinline__ void load_step(const SParams& p, int64_t s, int t, int c, int g,
-                                          bool cval, bool vec4, StepIn<REAL>& in) {
-  const int64_t row = s * p.L + t;
-  if (cval) {
-    const int64_t ic = row * p.C + c;
-    in.dnu = __ldg(p.dnu + ic);
-    in.dth = REAL ? 0.f : __ldg(p.dth + ic);
-    in.x = __ldg(p.x + ic);
-  } else {
-    in.dnu = in.dth = in.x = 0.f;
-  }
-  const int64_t in0 = row * p.N + g * kGM;
-  if (vec4 && g * kGM >= p.N) {
-    // Whole group beyond N (N a multiple of 4 but not of 4 * NG): no modes to load.
-#pragma unroll
-    for (int j = 0; j < kGM; ++j) in.bre[j] = in.bim[j] = in.cre[j] = in.cim[j] = 0.f;
-  } else if (vec4) {
-    const float4 br = __ldg(reinterpret_cast<const float4*>(p.Bre + in0));
-    in.bre[0] = br.x; in.bre[1] = br.y; in.bre[2] = br.z; in.bre[3] = br.w;
-    if (!REAL) {
-      const float4 bi = __ldg(reinterpret_cast<const float4*>(p.Bim + in0));
-      in.bim[0] = bi.x; in.bim[1] = bi.y; in.bim[2] = bi.z; in.bim[3] = bi.w;
-    }
-    if (WITH_C) {
-      const float4 cr = __ldg(reinterpret_cast<const float4*>(p.Cre + in0));
-      in.cre[0] = cr.x; in.cre[1] = cr.y; in.cre[2] = cr.z; in.cre[3] = cr.w;
-      if (!REAL) {
-        const float4 ci = __ldg(reinterpret_cast<const float4*>(p.Cim + in0));
-        in.cim[0] = ci.x; in.cim[1] = ci.y; in.cim[2] = ci.z; in.cim[3] = ci.w;
-      }
-    }
-  } else {
-#pragma unroll
-    for (int j = 0; j < kGM; ++j) {
-      const bool ok = g * kGM + j < p.N;
-      in.bre[j] = ok ? __ldg(p.Bre + in0 + j) : 0.f;
-      if (!REAL) in.bim[j] = ok ? __ldg(p.Bim + in0 + j) : 0.f;
-      if (WITH_C) {
-        in.cre[j] = ok ? __ldg(p.Cre + in0 + j) : 0.f;
-        if (!REAL) in.cim[j] = ok ? __ldg(p.Cim + in0 + j) : 0.f;
-      }
-    }
-  }
-  if (REAL) {
-#pragma unroll
-    for (int j = 0; j < kGM; ++j) {
-      in.bim[j] = 0.f;
-      in.cim[j] = 0.f;
-    }
-  }
-}
 
 __device__ __forceinline__ bool semx_aligned16(const void* ptr) {
   return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0;
 }
 
 struct ModeParams {
-  float a[kGM], a2[kGM], om[kGM], sd[kGM], ge[kGM];
+  float a[kGM], om[kGM], sd[kGM], ge[kGM];
   bool ok[kGM];
 };
 
@@ -231,7 +198,6 @@ __device__ __forceinline__ void load_params(const SParams& p, int c, int g, bool
     mp.ok[j] = cval && n < p.N;
     const int64_t i = (int64_t)c * p.N + n;
     mp.a[j] = mp.ok[j] ? p.a[i] : 0.f;
-    mp.a2[j] = mp.a[j] * kLog2e;
     mp.om[j] = (mp.ok[j] && !p.real) ? p.om[i] : 0.f;
     mp.sd[j] = (mp.ok[j] && p.detune) ? p.sdet[i] : 1.f;
     mp.ge[j] = (mp.ok[j] && p.envelope) ? p.g[i] : 0.f;
@@ -271,26 +237,28 @@ __device__ __forceinline__ void lane_reduce(float (&v)[V], int cl) {
 }
 
 // ------------------------------------------------------------------- staged operand tiles
-// The operands of kTile consecutive steps for a CTA's channel block are copied into
-// shared memory by all of the CTA's threads together (cp.async, 16 B per copy when the
-// rows are 16-byte aligned), double-buffered so the next tile is in flight while the
-// current one is consumed. Per buffer:
-//   channel rows [kRowC][kTile][CB]: delta_nu, x, delta_theta (complex only)
-//   mode rows    [kRowN][kTile][NP]: B_re, C_re, B_im, C_im (imaginary rows complex only)
+// The operands of TT consecutive steps for a CTA's channel block are copied into shared
+// memory by all of the CTA's threads together (cp.async, 16 B per copy when the rows are
+// 16-byte aligned), double-buffered so the next tile is in flight while the current one
+// is consumed. Per buffer:
+//   channel rows [kRowC][TT][CB]: delta_nu, x, delta_theta (complex only), dy (backward)
+//   mode rows    [kRowN][TT][NP]: B_re, C_re, B_im, C_im (imaginary rows complex only)
 // with CB = channels per CTA and NP = NG * kGM padded modes. Slots for channels >= C or
-// modes >= N are zeroed once and never written by the copies.
-constexpr int kTile = 32;
-
-template <bool REAL, int NG>
+// modes >= N are zeroed once and never written by the copies, so those lanes compute on
+// zeros: their state stays exactly zero and they contribute nothing.
+template <bool REAL, int NG, int TT, bool DY>
 struct Tiles {
+  static constexpr int kTT = TT;
   static constexpr int CB = kThreads / NG;
   static constexpr int NP = NG * kGM;
-  static constexpr int kRowC = REAL ? 2 : 3;
+  static constexpr int kRowTh = REAL ? -1 : 2;
+  static constexpr int kRowDy = DY ? (REAL ? 2 : 3) : -1;
+  static constexpr int kRowC = (REAL ? 2 : 3) + (DY ? 1 : 0);
   static constexpr int kRowN = REAL ? 2 : 4;
-  static constexpr int kBuf = kTile * (kRowC * CB + kRowN * NP);  // floats per buffer
-  static constexpr size_t bytes() { return (size_t)2 * kBuf * sizeof(float); }
-  __device__ static float* chan(float* buf, int row) { return buf + row * kTile * CB; }
-  __device__ static float* mode(float* buf, int row) { return buf + kRowC * kTile * CB + row * kTile * NP; }
+  static constexpr int kBuf = TT * (kRowC * CB + kRowN * NP);  // floats per buffer
+  __host__ __device__ static constexpr size_t bytes() { return (size_t)2 * kBuf * sizeof(float); }
+  __device__ static float* chan(float* buf, int row) { return buf + row * TT * CB; }
+  __device__ static float* mode(float* buf, int row) { return buf + kRowC * TT * CB + row * TT * NP; }
 };
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
@@ -305,40 +273,47 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;\n" ::: "memory"); }
 
 // Zeroes the padding slots of both buffers (channels >= nc, modes >= N).
-template <bool REAL, int NG>
+template <class T>
 __device__ void tile_zero_padding(float* smem, int nc, int N) {
-  using T = Tiles<REAL, NG>;
   for (int b = 0; b < 2; ++b) {
     float* buf = smem + b * T::kBuf;
-    for (int i = threadIdx.x; i < T::kRowC * kTile * T::CB; i += kThreads)
+    for (int i = threadIdx.x; i < T::kRowC * T::kTT * T::CB; i += kThreads)
       if (i % T::CB >= nc) buf[i] = 0.f;
     float* mb = T::mode(buf, 0);
-    for (int i = threadIdx.x; i < T::kRowN * kTile * T::NP; i += kThreads)
+    for (int i = threadIdx.x; i < T::kRowN * T::kTT * T::NP; i += kThreads)
       if (i % T::NP >= N) mb[i] = 0.f;
   }
 }
 
+template <class T>
+__device__ __forceinline__ const float* chan_src(const SParams& p, int row) {
+  if (row == 0) return p.dnu;
+  if (row == 1) return p.x;
+  if (row == T::kRowTh) return p.dth;
+  return p.dy;
+}
+__device__ __forceinline__ const float* mode_src(const SParams& p, int row) {
+  return row == 0 ? p.Bre : (row == 1 ? p.Cre : (row == 2 ? p.Bim : p.Cim));
+}
+
 // Issues the copies of steps [t0, t0 + nt) of sequence s into `buf` (does not commit).
-template <bool REAL, int NG>
+template <class T>
 __device__ void tile_load(const SParams& p, float* buf, int64_t s, int t0, int nt, int c0, int nc,
                           bool vecC, bool vecN) {
-  using T = Tiles<REAL, NG>;
-  auto chan_src = [&](int a) { return a == 0 ? p.dnu : (a == 1 ? p.x : p.dth); };
-  auto mode_src = [&](int a) { return a == 0 ? p.Bre : (a == 1 ? p.Cre : (a == 2 ? p.Bim : p.Cim)); };
   const int N = (int)p.N;
   if (vecC) {
     const int q = nc >> 2;  // 16-byte chunks per channel row
     const int items = T::kRowC * nt * q;
     for (int it = threadIdx.x; it < items; it += kThreads) {
       const int a = it / (nt * q), rem = it % (nt * q), i = rem / q, j = rem % q;
-      const float* src = chan_src(a) + ((s * p.L + t0 + i) * p.C + c0) + 4 * j;
+      const float* src = chan_src<T>(p, a) + ((s * p.L + t0 + i) * p.C + c0) + 4 * j;
       cp_async16(T::chan(buf, a) + i * T::CB + 4 * j, src);
     }
   } else {
     const int items = T::kRowC * nt * nc;
     for (int it = threadIdx.x; it < items; it += kThreads) {
       const int a = it / (nt * nc), rem = it % (nt * nc), i = rem / nc, j = rem % nc;
-      cp_async4(T::chan(buf, a) + i * T::CB + j, chan_src(a) + ((s * p.L + t0 + i) * p.C + c0) + j);
+      cp_async4(T::chan(buf, a) + i * T::CB + j, chan_src<T>(p, a) + ((s * p.L + t0 + i) * p.C + c0) + j);
     }
   }
   if (vecN) {
@@ -346,24 +321,24 @@ __device__ void tile_load(const SParams& p, float* buf, int64_t s, int t0, int n
     const int items = T::kRowN * nt * q;
     for (int it = threadIdx.x; it < items; it += kThreads) {
       const int a = it / (nt * q), rem = it % (nt * q), i = rem / q, j = rem % q;
-      cp_async16(T::mode(buf, a) + i * T::NP + 4 * j, mode_src(a) + (s * p.L + t0 + i) * p.N + 4 * j);
+      cp_async16(T::mode(buf, a) + i * T::NP + 4 * j, mode_src(p, a) + (s * p.L + t0 + i) * p.N + 4 * j);
     }
   } else {
     const int items = T::kRowN * nt * N;
     for (int it = threadIdx.x; it < items; it += kThreads) {
       const int a = it / (nt * N), rem = it % (nt * N), i = rem / N, j = rem % N;
-      cp_async4(T::mode(buf, a) + i * T::NP + j, mode_src(a) + (s * p.L + t0 + i) * p.N + j);
+      cp_async4(T::mode(buf, a) + i * T::NP + j, mode_src(p, a) + (s * p.L + t0 + i) * p.N + j);
     }
   }
 }
 
 // Reads step i of a staged tile for this thread's channel and modes.
-template <bool REAL, int NG, bool WITH_C>
+template <bool REAL, class T, bool WITH_C>
 __device__ __forceinline__ void tile_step(float* buf, int i, int cl, int g, StepIn<REAL>& in) {
-  using T = Tiles<REAL, NG>;
   in.dnu = T::chan(buf, 0)[i * T::CB + cl];
   in.x = T::chan(buf, 1)[i * T::CB + cl];
-  in.dth = REAL ? 0.f : T::chan(buf, 2)[i * T::CB + cl];
+  in.dth = REAL ? 0.f : T::chan(buf, T::kRowTh < 0 ? 0 : T::kRowTh)[i * T::CB + cl];
+  in.dy = T::kRowDy < 0 ? 0.f : T::chan(buf, T::kRowDy < 0 ? 0 : T::kRowDy)[i * T::CB + cl];
   const float4 br = *reinterpret_cast<const float4*>(T::mode(buf, 0) + i * T::NP + g * kGM);
   in.bre[0] = br.x; in.bre[1] = br.y; in.bre[2] = br.z; in.bre[3] = br.w;
   if (WITH_C) {
@@ -383,10 +358,32 @@ __device__ __forceinline__ void tile_step(float* buf, int i, int cl, int g, Step
   }
 }
 
+// One step of the recurrence for this thread's modes: h = lam h + gain x B.
+template <bool REAL, int GAIN>
+__device__ __forceinline__ void advance(const ModeParams& mp, bool detune, const StepIn<REAL>& in,
+                                        float (&hr)[kGM], float (&hi)[kGM]) {
+#pragma unroll
+  for (int j = 0; j < kGM; ++j) {
+    const Disc d = discretise<REAL, GAIN>(mp.a[j], mp.om[j], mp.sd[j], detune, in.dnu, in.dth);
+    const float gxr = d.gr * in.x;
+    if (REAL) {
+      hr[j] = d.lre * hr[j] + gxr * in.bre[j];
+    } else {
+      const float gxi = d.gi * in.x;
+      const float ur = gxr * in.bre[j] - gxi * in.bim[j];
+      const float ui = gxr * in.bim[j] + gxi * in.bre[j];
+      const float nr = d.lre * hr[j] - d.lim * hi[j] + ur;
+      const float ni = d.lre * hi[j] + d.lim * hr[j] + ui;
+      hr[j] = nr;
+      hi[j] = ni;
+    }
+  }
+}
+
 // ----------------------------------------------------------------------------- forward
 template <bool REAL, int GAIN, int NG>
 __global__ void __launch_bounds__(kThreads) slru_fwd_kernel(const SParams p) {
-  using T = Tiles<REAL, NG>;
+  using T = Tiles<REAL, NG, kTileF, false>;
   constexpr int CW = 32 / NG;
   extern __shared__ float4 fwd_smem4[];
   float* smem = reinterpret_cast<float*>(fwd_smem4);
@@ -415,9 +412,9 @@ __global__ void __launch_bounds__(kThreads) slru_fwd_kernel(const SParams p) {
     hi[j] = (mp.ok[j] && p.h0i && !REAL) ? p.h0i[i] : 0.f;
   }
 
-  tile_zero_padding<REAL, NG>(smem, nc, (int)p.N);
-  const int ntiles = (L + kTile - 1) / kTile;
-  if (ntiles > 0) tile_load<REAL, NG>(p, smem, s, 0, min(kTile, L), c0, nc, vecC, vecN);
+  tile_zero_padding<T>(smem, nc, (int)p.N);
+  const int ntiles = (L + kTileF - 1) / kTileF;
+  if (ntiles > 0) tile_load<T>(p, smem, s, 0, min(kTileF, L), c0, nc, vecC, vecN);
   cp_async_commit();
   int next_ck = 0;
   float* yrow = p.y + s * p.L * p.C + c;
@@ -425,11 +422,11 @@ __global__ void __launch_bounds__(kThreads) slru_fwd_kernel(const SParams p) {
     cp_async_wait_all();
     __syncthreads();
     if (k + 1 < ntiles)
-      tile_load<REAL, NG>(p, smem + ((k + 1) & 1) * T::kBuf, s, (k + 1) * kTile,
-                          min(kTile, L - (k + 1) * kTile), c0, nc, vecC, vecN);
+      tile_load<T>(p, smem + ((k + 1) & 1) * T::kBuf, s, (k + 1) * kTileF,
+                   min(kTileF, L - (k + 1) * kTileF), c0, nc, vecC, vecN);
     cp_async_commit();
     float* buf = smem + (k & 1) * T::kBuf;
-    const int t0 = k * kTile, nt = min(kTile, L - t0);
+    const int t0 = k * kTileF, nt = min(kTileF, L - t0);
     for (int i = 0; i < nt; ++i) {
       const int t = t0 + i;
       if (p.ckpt != nullptr && t == next_ck) {
@@ -444,28 +441,13 @@ __global__ void __launch_bounds__(kThreads) slru_fwd_kernel(const SParams p) {
         next_ck += p.chunk;
       }
       StepIn<REAL> cur;
-      tile_step<REAL, NG, true>(buf, i, c_local, g, cur);
-      // Modes beyond N and channels beyond C need no masking here: their parameters and
-      // staged operands are zero, so their state stays exactly zero and adds nothing.
+      tile_step<REAL, T, true>(buf, i, c_local, g, cur);
+      advance<REAL, GAIN>(mp, p.detune, cur, hr, hi);
       float yp = 0.f;
 #pragma unroll
       for (int j = 0; j < kGM; ++j) {
-        const Disc d = discretise<REAL, GAIN>(mp.a[j], mp.a2[j], mp.om[j], mp.sd[j], p.detune,
-                                              cur.dnu, cur.dth);
-        const float gxr = d.gr * cur.x;
-        if (REAL) {
-          hr[j] = d.lre * hr[j] + gxr * cur.bre[j];
-          yp += cur.cre[j] * hr[j];
-        } else {
-          const float gxi = d.gi * cur.x;
-          const float ur = gxr * cur.bre[j] - gxi * cur.bim[j];
-          const float ui = gxr * cur.bim[j] + gxi * cur.bre[j];
-          const float nr = d.lre * hr[j] - d.lim * hi[j] + ur;
-          const float ni = d.lre * hi[j] + d.lim * hr[j] + ui;
-          hr[j] = nr;
-          hi[j] = ni;
-          yp += cur.cre[j] * hr[j] - cur.cim[j] * hi[j];
-        }
+        yp += cur.cre[j] * hr[j];
+        if (!REAL) yp -= cur.cim[j] * hi[j];
       }
       if (p.envelope) {
 #pragma unroll
@@ -490,65 +472,122 @@ __global__ void __launch_bounds__(kThreads) slru_fwd_kernel(const SParams p) {
 // ---------------------------------------------------------------------------- backward
 template <bool REAL, int NG>
 struct BwdLayout {
-  static constexpr int kHS = REAL ? 1 : 2;         // floats per mode of state
-  static constexpr int kNArr = REAL ? 2 : 4;       // dB(re, im), dC(re, im)
-  static constexpr int kV = kNArr * kGM;           // dB/dC values per thread per step
-  static constexpr int kNV = NG * kV;              // values per warp per step
+  using T = Tiles<REAL, NG, kTileB, true>;
+  static constexpr int kHS = REAL ? 1 : 2;    // float4 groups per sub-checkpoint (re [, im])
+  static constexpr int kNArr = REAL ? 2 : 4;  // dB(re [, im]), dC(re [, im])
+  static constexpr int kV = kNArr * kGM;      // dB/dC values per thread per step
+  static constexpr int kNV = NG * kV;         // values per warp per step
   static constexpr int kNW = kThreads / 32;
-  __host__ __device__ static size_t sub_floats(int chunk) { return (size_t)(chunk / kR) * kThreads * kGM * kHS; }
-  __host__ __device__ static size_t red_floats() { return (size_t)2 * kTT * kNW * kNV; }
-  __host__ __device__ static size_t bytes(int chunk) { return (sub_floats(chunk) + red_floats()) * sizeof(float); }
+  __host__ __device__ static constexpr size_t tile_floats() { return 2 * (size_t)T::kBuf; }
+  __host__ __device__ static constexpr size_t red_floats() { return (size_t)2 * kFlush * kNW * kNV; }
+  __host__ __device__ static size_t sub_floats(int chunk) {
+    return (size_t)(chunk / kR) * kHS * kThreads * kGM;
+  }
+  __host__ __device__ static size_t bytes(int chunk) {
+    return (tile_floats() + red_floats() + sub_floats(chunk)) * sizeof(float);
+  }
 };
+
+// The backward visits each chunk's staged tiles in this order: a chunk of one tile once
+// (pass 1 and pass 2 on the same tile); a longer chunk's tiles forwards for pass 1, then
+// backwards for pass 2.
+struct TileEntry {
+  int t0, nt;
+  bool p1, p2;
+};
+__device__ __forceinline__ int tiles_in_chunk(int k, int K, int L) {
+  const int t0 = k * K, t1 = min(t0 + K, L);
+  return (t1 - t0 + kTileB - 1) / kTileB;
+}
+__device__ __forceinline__ int entries_of(int k, int K, int L) {
+  const int nq = tiles_in_chunk(k, K, L);
+  return nq == 1 ? 1 : 2 * nq;
+}
+__device__ __forceinline__ TileEntry entry_of(int k, int e, int K, int L) {
+  const int t0 = k * K, t1 = min(t0 + K, L);
+  const int nq = tiles_in_chunk(k, K, L);
+  TileEntry E;
+  int q;
+  if (nq == 1) {
+    q = 0;
+    E.p1 = E.p2 = true;
+  } else if (e < nq) {
+    q = e;
+    E.p1 = true;
+    E.p2 = false;
+  } else {
+    q = 2 * nq - 1 - e;
+    E.p1 = false;
+    E.p2 = true;
+  }
+  E.t0 = t0 + q * kTileB;
+  E.nt = min(kTileB, t1 - E.t0);
+  return E;
+}
 
 template <bool REAL, int GAIN, int NG>
 __global__ void __launch_bounds__(kThreads) slru_bwd_kernel(const SParams p) {
   using Lay = BwdLayout<REAL, NG>;
+  using T = typename Lay::T;
   constexpr int CW = 32 / NG;
-  constexpr int CB = kThreads / NG;
   constexpr int V = Lay::kV;
   constexpr int NV = Lay::kNV;
   constexpr int NW = Lay::kNW;
   constexpr int HS = Lay::kHS;
-  extern __shared__ float smem[];
-  float* sub = smem;                                 // [chunk/kR][kThreads][kGM*HS]
-  float* red = smem + Lay::sub_floats(p.chunk);      // [2][kTT][NW][NV]
+  extern __shared__ float4 bwd_smem4[];
+  float* tiles = reinterpret_cast<float*>(bwd_smem4);
+  float* red = tiles + Lay::tile_floats();                                  // [2][kFlush][NW][NV]
+  float4* sub = reinterpret_cast<float4*>(red + Lay::red_floats());         // [chunk/kR][HS][kThreads]
   cg::cluster_group cluster = cg::this_cluster();
   const int crank = (int)cluster.block_rank();
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int cl = lane / NG, g = lane % NG;
-  const int c = blockIdx.x * CB + warp * CW + cl;
+  const int c_local = warp * CW + cl;
+  const int c0 = blockIdx.x * T::CB;
+  const int c = c0 + c_local;
   const int64_t s = blockIdx.y;
   const bool cval = c < p.C;
-  const bool vec4 = (p.N % 4) == 0 && p.N > 0;
+  const int nc = (int)max((int64_t)0, min((int64_t)T::CB, p.C - c0));
   const int L = (int)p.L;
   const int N = (int)p.N;
+  const int K = p.chunk;
+  const bool vecC = (p.C % 4) == 0 && semx_aligned16(p.dnu) && semx_aligned16(p.x) &&
+                    semx_aligned16(p.dy) && (REAL || semx_aligned16(p.dth));
+  const bool vecN = (p.N % 4) == 0 && semx_aligned16(p.Bre) && semx_aligned16(p.Cre) &&
+                    (REAL || (semx_aligned16(p.Bim) && semx_aligned16(p.Cim)));
 
   ModeParams mp;
   load_params(p, c, g, cval, mp);
   const float Dc = cval ? p.D[c] : 0.f;
 
-  float Gr[kGM], Gi[kGM], lnr[kGM], lni[kGM];
+  // Carry c_{t+1} = conj(lam_{t+1}) G_{t+1}; it starts as the final-state gradient.
+  float cr[kGM], ci[kGM];
   float acc_a[kGM], acc_om[kGM], acc_s[kGM], acc_g[kGM];
   float acc_D = 0.f;
 #pragma unroll
   for (int j = 0; j < kGM; ++j) {
     const int64_t i = (s * p.C + c) * p.N + g * kGM + j;
     const bool has = mp.ok[j] && p.dhfr != nullptr;
-    Gr[j] = has ? p.dhfr[i] : 0.f;
-    Gi[j] = (has && !REAL && p.dhfi) ? p.dhfi[i] : 0.f;
-    lnr[j] = has ? 1.f : 0.f;
-    lni[j] = 0.f;
+    cr[j] = has ? p.dhfr[i] : 0.f;
+    ci[j] = (has && !REAL && p.dhfi) ? p.dhfi[i] : 0.f;
     acc_a[j] = acc_om[j] = acc_s[j] = acc_g[j] = 0.f;
   }
 
-  int tile_count = 0;
+  tile_zero_padding<T>(tiles, nc, N);
+  if (p.nchunks > 0) {
+    const TileEntry E = entry_of(p.nchunks - 1, 0, K, L);
+    tile_load<T>(p, tiles, s, E.t0, E.nt, c0, nc, vecC, vecN);
+  }
+  cp_async_commit();
+  int bsel = 0;
+
   for (int k = p.nchunks - 1; k >= 0; --k) {
-    const int t0 = k * p.chunk;
-    const int t1 = min(t0 + p.chunk, L);
-    // Pass 1: recurrence from the checkpoint, state every kR steps to shared memory.
+    const int t0c = k * K;
+    const int nE = entries_of(k, K, L);
+    // Pass-1 state: the checkpoint stored by the forward at the start of chunk k.
+    float hr[kGM], hi[kGM];
     {
-      float hr[kGM], hi[kGM];
       const int64_t cb = ((s * p.nchunks + k) * p.C + c) * p.N + g * kGM;
 #pragma unroll
       for (int j = 0; j < kGM; ++j) {
@@ -562,230 +601,227 @@ __global__ void __launch_bounds__(kThreads) slru_bwd_kernel(const SParams p) {
           hi[j] = v.y;
         }
       }
-      StepIn<REAL> cur, nxt;
-      load_step<REAL, false>(p, s, t0, c, g, cval, vec4, cur);
-      for (int t = t0; t < t1; ++t) {
-        if (t + 1 < t1) load_step<REAL, false>(p, s, t + 1, c, g, cval, vec4, nxt);
-        if (((t - t0) % kR) == 0) {
-          float* dst = sub + ((size_t)((t - t0) / kR) * kThreads + tid) * kGM * HS;
-#pragma unroll
-          for (int j = 0; j < kGM; ++j) {
-            dst[j * HS] = hr[j];
-            if (!REAL) dst[j * HS + 1] = hi[j];
-          }
-        }
-#pragma unroll
-        for (int j = 0; j < kGM; ++j) {
-          const Disc d = discretise<REAL, GAIN>(mp.a[j], mp.a2[j], mp.om[j], mp.sd[j], p.detune,
-                                                cur.dnu, cur.dth);
-          const float gxr = d.gr * cur.x, gxi = d.gi * cur.x;
-          const float ur = gxr * cur.bre[j] - gxi * cur.bim[j];
-          const float ui = gxr * cur.bim[j] + gxi * cur.bre[j];
-          const float nr = d.lre * hr[j] - d.lim * hi[j] + ur;
-          const float ni = d.lre * hi[j] + d.lim * hr[j] + ui;
-          hr[j] = mp.ok[j] ? nr : 0.f;
-          hi[j] = mp.ok[j] ? ni : 0.f;
-        }
-        cur = nxt;
-      }
     }
-
-    // Pass 2: tiles backwards, sub-blocks backwards inside each tile.
-    const int ntile = (t1 - t0 + kTT - 1) / kTT;
-    for (int q = ntile - 1; q >= 0; --q, ++tile_count) {
-      const int tt0 = t0 + q * kTT;
-      const int tt1 = min(tt0 + kTT, t1);
-      const int buf = tile_count & 1;
-      float* redb = red + (size_t)buf * kTT * NW * NV;
-      const int nsubt = (tt1 - tt0 + kR - 1) / kR;
-      for (int r = nsubt - 1; r >= 0; --r) {
-        const int ta = tt0 + r * kR;
-        const int tb = min(ta + kR, tt1);
-        float Hr[kR][kGM], Hi[kR][kGM], H0r[kGM], H0i[kGM];
-        {
-          const float* src = sub + ((size_t)((ta - t0) / kR) * kThreads + tid) * kGM * HS;
-#pragma unroll
-          for (int j = 0; j < kGM; ++j) {
-            H0r[j] = src[j * HS];
-            H0i[j] = REAL ? 0.f : src[j * HS + 1];
-          }
-        }
-        // Recompute kR states.
-#pragma unroll
-        for (int i = 0; i < kR; ++i) {
-          if (ta + i < tb) {
-            StepIn<REAL> in;
-            load_step<REAL, false>(p, s, ta + i, c, g, cval, vec4, in);
-#pragma unroll
-            for (int j = 0; j < kGM; ++j) {
-              const float pr = i == 0 ? H0r[j] : Hr[i > 0 ? i - 1 : 0][j];
-              const float pi = i == 0 ? H0i[j] : Hi[i > 0 ? i - 1 : 0][j];
-              const Disc d = discretise<REAL, GAIN>(mp.a[j], mp.a2[j], mp.om[j], mp.sd[j],
-                                                    p.detune, in.dnu, in.dth);
-              const float gxr = d.gr * in.x, gxi = d.gi * in.x;
-              const float ur = gxr * in.bre[j] - gxi * in.bim[j];
-              const float ui = gxr * in.bim[j] + gxi * in.bre[j];
-              const float nr = d.lre * pr - d.lim * pi + ur;
-              const float ni = d.lre * pi + d.lim * pr + ui;
-              Hr[i][j] = mp.ok[j] ? nr : 0.f;
-              Hi[i][j] = mp.ok[j] ? ni : 0.f;
-            }
-          }
-        }
-        // Adjoint through the sub-block.
-#pragma unroll
-        for (int i = kR - 1; i >= 0; --i) {
-          if (ta + i < tb) {
-            const int t = ta + i;
-            StepIn<REAL> in;
-            load_step<REAL, true>(p, s, t, c, g, cval, vec4, in);
-            const float dyv = cval ? __ldg(p.dy + (s * p.L + t) * p.C + c) : 0.f;
-            float sum_dnu = 0.f, sum_dth = 0.f, sum_dx = 0.f;
-            float vals[V];
-#pragma unroll
-            for (int j = 0; j < kGM; ++j) {
-              const float hr = Hr[i][j], hi = Hi[i][j];
-              const float hpr = i == 0 ? H0r[j] : Hr[i > 0 ? i - 1 : 0][j];
-              const float hpi = i == 0 ? H0i[j] : Hi[i > 0 ? i - 1 : 0][j];
-              const Disc d = discretise<REAL, GAIN>(mp.a[j], mp.a2[j], mp.om[j], mp.sd[j],
-                                                    p.detune, in.dnu, in.dth);
-              // Local adjoint from the readout (and the envelope term).
-              float gre = dyv * in.cre[j];
-              float gim = -dyv * in.cim[j];
-              if (p.envelope) {
-                gre += 2.f * dyv * mp.ge[j] * hr;
-                gim += 2.f * dyv * mp.ge[j] * hi;
-                acc_g[j] += dyv * (hr * hr + hi * hi);
-              }
-              // G_t = g_t + conj(lam_{t+1}) G_{t+1}
-              const float gr_ = gre + lnr[j] * Gr[j] + lni[j] * Gi[j];
-              const float gi_ = REAL ? 0.f : gim + lnr[j] * Gi[j] - lni[j] * Gr[j];
-              const float Gtr = mp.ok[j] ? gr_ : 0.f;
-              const float Gti = mp.ok[j] ? gi_ : 0.f;
-              // Input map Bu = (gain x) B.
-              const float gxr = d.gr * in.x, gxi = d.gi * in.x;
-              const float vBr = gxr * Gtr + gxi * Gti;
-              const float vBi = gxr * Gti - gxi * Gtr;
-              const float wre = d.gr * in.bre[j] - d.gi * in.bim[j];
-              const float wim = d.gr * in.bim[j] + d.gi * in.bre[j];
-              sum_dx += wre * Gtr + wim * Gti;
-              const float dgr = in.x * (in.bre[j] * Gtr + in.bim[j] * Gti);
-              const float dgi = in.x * (in.bre[j] * Gti - in.bim[j] * Gtr);
-              float d_nu_tot = 0.f, d_dnu = 0.f, da_extra = 0.f, dbase_extra = 0.f;
-              if (GAIN == SEMX_GAIN_GAMMA) {
-                const bool live = (1.f - d.nu * d.nu) >= 1e-6f;
-                d_nu_tot += live ? -dgr * d.nu / d.gr : 0.f;
-              } else if (GAIN == SEMX_GAIN_MAMBA) {
-                d_dnu += dgr;
-              } else {
-                // d gain / d delta_nu = lam; d gain / d A_c = (dnu lam - gain) / A_c = q.
-                d_dnu += dgr * d.lre + dgi * d.lim;
-                const float pr = in.dnu * d.lre - d.gr;
-                const float pi = in.dnu * d.lim - d.gi;
-                const float qr = (d.base * pi - mp.a[j] * pr) / d.den;
-                const float qi = -(mp.a[j] * pi + d.base * pr) / d.den;
-                da_extra = -(dgr * qr + dgi * qi);
-                dbase_extra = dgi * qr - dgr * qi;
-              }
-              // d lam = G_t conj(h_{t-1}).
-              const float dlre = Gtr * hpr + Gti * hpi;
-              const float dlim = Gti * hpr - Gtr * hpi;
-              float d_th = 0.f;
-              if (REAL) {
-                d_nu_tot += dlre;
-              } else {
-                d_nu_tot += dlre * d.cs + dlim * d.sn;
-                d_th = d.nu * (dlim * d.cs - dlre * d.sn);
-              }
-              d_dnu += d_nu_tot * (-mp.a[j]) * d.nu;
-              acc_a[j] += d_nu_tot * (-in.dnu) * d.nu + da_extra;
-              if (!REAL) {
-                d_dnu += d_th * d.base;
-                const float dbase = d_th * in.dnu + dbase_extra;
-                acc_om[j] += dbase;
-                sum_dth += dbase * mp.sd[j];
-                if (p.detune) acc_s[j] += dbase * in.dth;
-              }
-              sum_dnu += mp.ok[j] ? d_dnu : 0.f;
-              // dB, dC values for the cross-channel reduction.
-              vals[0 * kGM + j] = mp.ok[j] ? vBr : 0.f;
-              if (REAL) {
-                vals[1 * kGM + j] = mp.ok[j] ? dyv * hr : 0.f;
-              } else {
-                vals[1 * kGM + j] = mp.ok[j] ? vBi : 0.f;
-                vals[2 * kGM + j] = mp.ok[j] ? dyv * hr : 0.f;
-                vals[3 * kGM + j] = mp.ok[j] ? -dyv * hi : 0.f;
-              }
-              Gr[j] = Gtr;
-              Gi[j] = Gti;
-              lnr[j] = d.lre;
-              lni[j] = d.lim;
-            }
-            if (g == 0) acc_D += dyv * in.x;
-            sum_dnu = sum_lanes<NG>(sum_dnu);
-            sum_dx = sum_lanes<NG>(sum_dx);
-            if (!REAL) sum_dth = sum_lanes<NG>(sum_dth);
-            if (g == 0 && cval) {
-              const int64_t ic = (s * p.L + t) * p.C + c;
-              if (p.d_dnu) p.d_dnu[ic] = sum_dnu;
-              if (!REAL && p.d_dth) p.d_dth[ic] = sum_dth;
-              if (p.dx) p.dx[ic] = sum_dx + dyv * Dc;
-            }
-            lane_reduce<V, CW, NG>(vals, cl);
-            float* dst = redb + ((size_t)(t - tt0) * NW + warp) * NV + g * V;
-            if (V >= CW) {
-#pragma unroll
-              for (int m = 0; m < (V >= CW ? V / CW : 1); ++m) dst[cl * (V / CW) + m] = vals[m];
-            } else if ((cl % (V < CW ? CW / V : 1)) == 0) {
-              dst[cl / (V < CW ? CW / V : 1)] = vals[0];
-            }
-          }
-        }
-      }
-      // Tile complete: sum dB / dC over warps and over the cluster's CTAs (fixed order).
+    for (int e = 0; e < nE; ++e) {
+      const TileEntry E = entry_of(k, e, K, L);
+      cp_async_wait_all();
       __syncthreads();
-      cluster.sync();
-      const int nitems = (tt1 - tt0) * NV;
-      const int stride = p.ncl * kThreads;
-      for (int it = crank * kThreads + tid; it < nitems; it += stride) {
-        const int tl = it / NV, kk = it % NV;
-        const int gg = kk / V, vv = kk % V;
-        const int arr = vv / kGM, n = gg * kGM + (vv % kGM);
-        if (n >= N) continue;
-        float acc = 0.f;
-        for (int qr = 0; qr < p.ncl; ++qr) {
-          const float* peer = cluster.map_shared_rank(redb, qr);
-#pragma unroll
-          for (int w = 0; w < NW; ++w) acc += peer[((size_t)tl * NW + w) * NV + kk];
+      {
+        const int kn = (e + 1 < nE) ? k : k - 1;
+        const int en = (e + 1 < nE) ? e + 1 : 0;
+        if (kn >= 0) {
+          const TileEntry En = entry_of(kn, en, K, L);
+          tile_load<T>(p, tiles + (bsel ^ 1) * T::kBuf, s, En.t0, En.nt, c0, nc, vecC, vecN);
         }
-        const int64_t row = s * p.L + tt0 + tl;
-        if (p.nclusters > 1) {
-          const int clid = blockIdx.x / p.ncl;
-          p.dbc_part[(row * p.nclusters + clid) * (Lay::kNArr * N) + arr * N + n] = acc;
-        } else {
-          float* outp = REAL ? (arr == 0 ? p.dBre : p.dCre)
-                             : (arr == 0 ? p.dBre : arr == 1 ? p.dBim : arr == 2 ? p.dCre : p.dCim);
-          if (outp) outp[row * N + n] = acc;
+        cp_async_commit();
+      }
+      float* buf = tiles + bsel * T::kBuf;
+
+      if (E.p1) {  // Pass 1: recurrence from the checkpoint, state every kR steps kept.
+        for (int i = 0; i < E.nt; ++i) {
+          const int t = E.t0 + i;
+          if (((t - t0c) % kR) == 0) {
+            const int si = (t - t0c) / kR;
+            sub[(si * HS) * kThreads + tid] = make_float4(hr[0], hr[1], hr[2], hr[3]);
+            if (!REAL) sub[(si * HS + 1) * kThreads + tid] = make_float4(hi[0], hi[1], hi[2], hi[3]);
+          }
+          StepIn<REAL> in;
+          tile_step<REAL, T, false>(buf, i, c_local, g, in);
+          advance<REAL, GAIN>(mp, p.detune, in, hr, hi);
         }
       }
+
+      if (E.p2) {  // Pass 2: kR-step sub-blocks, last first.
+        const int nsb = (E.nt + kR - 1) / kR;
+        for (int r = nsb - 1; r >= 0; --r) {
+          const int ta = E.t0 + r * kR;
+          const int nr = min(kR, E.t0 + E.nt - ta);
+          const int si = (ta - t0c) / kR;
+          float H0r[kGM], H0i[kGM], Hr[kR][kGM], Hi[kR][kGM];
+          {
+            const float4 v = sub[(si * HS) * kThreads + tid];
+            H0r[0] = v.x; H0r[1] = v.y; H0r[2] = v.z; H0r[3] = v.w;
+            if (!REAL) {
+              const float4 w = sub[(si * HS + 1) * kThreads + tid];
+              H0i[0] = w.x; H0i[1] = w.y; H0i[2] = w.z; H0i[3] = w.w;
+            } else {
+#pragma unroll
+              for (int j = 0; j < kGM; ++j) H0i[j] = 0.f;
+            }
+          }
+          // Recompute the sub-block's states.
+#pragma unroll
+          for (int i = 0; i < kR; ++i) {
+#pragma unroll
+            for (int j = 0; j < kGM; ++j) {
+              Hr[i][j] = i == 0 ? H0r[j] : Hr[i > 0 ? i - 1 : 0][j];
+              Hi[i][j] = i == 0 ? H0i[j] : Hi[i > 0 ? i - 1 : 0][j];
+            }
+            if (i < nr) {
+              StepIn<REAL> in;
+              tile_step<REAL, T, false>(buf, ta - E.t0 + i, c_local, g, in);
+              advance<REAL, GAIN>(mp, p.detune, in, Hr[i], Hi[i]);
+            }
+          }
+          // Adjoint through the sub-block.
+#pragma unroll
+          for (int i = kR - 1; i >= 0; --i) {
+            if (i < nr) {
+              const int t = ta + i;
+              StepIn<REAL> in;
+              tile_step<REAL, T, true>(buf, t - E.t0, c_local, g, in);
+              const float dyv = in.dy;
+              float sum_dnu = 0.f, sum_dth = 0.f, sum_dx = 0.f;
+              float vals[V];
+#pragma unroll
+              for (int j = 0; j < kGM; ++j) {
+                const float hrt = Hr[i][j], hit = Hi[i][j];
+                const float hpr = i == 0 ? H0r[j] : Hr[i > 0 ? i - 1 : 0][j];
+                const float hpi = i == 0 ? H0i[j] : Hi[i > 0 ? i - 1 : 0][j];
+                const Disc d = discretise<REAL, GAIN>(mp.a[j], mp.om[j], mp.sd[j], p.detune,
+                                                      in.dnu, in.dth);
+                // Local adjoint from the readout (and the envelope term).
+                float gre = dyv * in.cre[j];
+                float gim = REAL ? 0.f : -dyv * in.cim[j];
+                if (p.envelope) {
+                  const float w = 2.f * dyv * mp.ge[j];
+                  gre += w * hrt;
+                  if (!REAL) gim += w * hit;
+                  acc_g[j] += dyv * (hrt * hrt + (REAL ? 0.f : hit * hit));
+                }
+                const float Gr = gre + cr[j];
+                const float Gi = REAL ? 0.f : gim + ci[j];
+                cr[j] = REAL ? d.lre * Gr : d.lre * Gr + d.lim * Gi;
+                ci[j] = REAL ? 0.f : d.lre * Gi - d.lim * Gr;
+                // Input map Bu = (gain x) B: dB = conj(gain x) G, d(gain) = x conj(B) G.
+                const float gxr = d.gr * in.x, gxi = d.gi * in.x;
+                const float vBr = REAL ? gxr * Gr : gxr * Gr + gxi * Gi;
+                const float vBi = REAL ? 0.f : gxr * Gi - gxi * Gr;
+                if (REAL) {
+                  sum_dx += d.gr * in.bre[j] * Gr;
+                } else {
+                  const float wre = d.gr * in.bre[j] - d.gi * in.bim[j];
+                  const float wim = d.gr * in.bim[j] + d.gi * in.bre[j];
+                  sum_dx += wre * Gr + wim * Gi;
+                }
+                const float dgr = REAL ? in.x * (in.bre[j] * Gr) : in.x * (in.bre[j] * Gr + in.bim[j] * Gi);
+                const float dgi = REAL ? 0.f : in.x * (in.bre[j] * Gi - in.bim[j] * Gr);
+                float d_nu_tot = 0.f, d_dnu = 0.f, da_extra = 0.f, dbase_extra = 0.f;
+                if (GAIN == SEMX_GAIN_GAMMA) {
+                  // gain = sqrt(max(1 - nu^2, 1e-6)): d gain / d nu = -nu / gain where live.
+                  const bool live = (1.f - d.nu * d.nu) >= 1e-6f;
+                  d_nu_tot = live ? -dgr * d.nu * d.rs : 0.f;
+                } else if (GAIN == SEMX_GAIN_MAMBA) {
+                  d_dnu = dgr;
+                } else {
+                  // d gain / d delta_nu = lam; d gain / d A_c = (dnu lam - gain) / A_c = q.
+                  d_dnu = dgr * d.lre + dgi * d.lim;
+                  const float pr = in.dnu * d.lre - d.gr;
+                  const float pi = in.dnu * d.lim - d.gi;
+                  const float qr = (d.base * pi - mp.a[j] * pr) * d.inv_den;
+                  const float qi = -(mp.a[j] * pi + d.base * pr) * d.inv_den;
+                  da_extra = -(dgr * qr + dgi * qi);
+                  dbase_extra = dgi * qr - dgr * qi;
+                }
+                // d lam = G_t conj(h_{t-1}).
+                const float dlre = REAL ? Gr * hpr : Gr * hpr + Gi * hpi;
+                float d_th = 0.f;
+                if (REAL) {
+                  d_nu_tot += dlre;
+                } else {
+                  const float dlim = Gi * hpr - Gr * hpi;
+                  d_nu_tot += dlre * d.cs + dlim * d.sn;
+                  d_th = d.nu * (dlim * d.cs - dlre * d.sn);
+                }
+                d_dnu += d_nu_tot * (-mp.a[j]) * d.nu;
+                acc_a[j] += d_nu_tot * (-in.dnu) * d.nu + da_extra;
+                if (!REAL) {
+                  d_dnu += d_th * d.base;
+                  const float dbase = d_th * in.dnu + dbase_extra;
+                  acc_om[j] += dbase;
+                  sum_dth += dbase * mp.sd[j];
+                  if (p.detune) acc_s[j] += dbase * in.dth;
+                }
+                sum_dnu += d_dnu;
+                vals[0 * kGM + j] = vBr;
+                if (REAL) {
+                  vals[1 * kGM + j] = dyv * hrt;
+                } else {
+                  vals[1 * kGM + j] = vBi;
+                  vals[2 * kGM + j] = dyv * hrt;
+                  vals[3 * kGM + j] = -dyv * hit;
+                }
+              }
+              if (g == 0) acc_D += dyv * in.x;
+              sum_dnu = sum_lanes<NG>(sum_dnu);
+              sum_dx = sum_lanes<NG>(sum_dx);
+              if (!REAL) sum_dth = sum_lanes<NG>(sum_dth);
+              if (g == 0 && cval) {
+                const int64_t ic = (s * p.L + t) * p.C + c;
+                if (p.d_dnu) p.d_dnu[ic] = sum_dnu;
+                if (!REAL && p.d_dth) p.d_dth[ic] = sum_dth;
+                if (p.dx) p.dx[ic] = sum_dx + dyv * Dc;
+              }
+              lane_reduce<V, CW, NG>(vals, cl);
+              float* dst = red + ((size_t)(((t / kFlush) & 1) * kFlush + (t % kFlush)) * NW + warp) * NV + g * V;
+              if (V >= CW) {
+#pragma unroll
+                for (int m = 0; m < (V >= CW ? V / CW : 1); ++m) dst[cl * (V / CW) + m] = vals[m];
+              } else if ((cl % (V < CW ? CW / V : 1)) == 0) {
+                dst[cl / (V < CW ? CW / V : 1)] = vals[0];
+              }
+            }
+          }
+          if ((ta % kFlush) == 0) {
+            // Steps [ta, ta + kFlush) complete on every CTA of the cluster: sum dB / dC over
+            // warps and over the cluster's CTAs in a fixed order.
+            cluster.sync();
+            const float* redb = red + (size_t)((ta / kFlush) & 1) * kFlush * NW * NV;
+            const int nitems = min(kFlush, L - ta) * NV;
+            const int stride = p.ncl * kThreads;
+            for (int it = crank * kThreads + tid; it < nitems; it += stride) {
+              const int tl = it / NV, kk = it % NV;
+              const int gg = kk / V, vv = kk % V;
+              const int arr = vv / kGM, n = gg * kGM + (vv % kGM);
+              if (n >= N) continue;
+              float acc = 0.f;
+              for (int q = 0; q < p.ncl; ++q) {
+                const float* peer = cluster.map_shared_rank(redb, q);
+#pragma unroll
+                for (int w = 0; w < NW; ++w) acc += peer[((size_t)tl * NW + w) * NV + kk];
+              }
+              const int64_t row = s * p.L + ta + tl;
+              if (p.nclusters > 1) {
+                const int clid = blockIdx.x / p.ncl;
+                p.dbc_part[(row * p.nclusters + clid) * (Lay::kNArr * N) + arr * N + n] = acc;
+              } else {
+                float* outp = REAL ? (arr == 0 ? p.dBre : p.dCre)
+                                   : (arr == 0 ? p.dBre : arr == 1 ? p.dBim : arr == 2 ? p.dCre : p.dCim);
+                if (outp) outp[row * N + n] = acc;
+              }
+            }
+          }
+        }
+      }
+      bsel ^= 1;
     }
   }
 
-  // Initial-state gradient: dh0 = conj(lam_0) G_0.
+  // Initial-state gradient: dh0 = conj(lam_0) G_0, the final carry.
   if (p.dh0r != nullptr) {
 #pragma unroll
     for (int j = 0; j < kGM; ++j) {
       if (mp.ok[j]) {
         const int64_t i = (s * p.C + c) * p.N + g * kGM + j;
-        p.dh0r[i] = lnr[j] * Gr[j] + lni[j] * Gi[j];
-        if (!REAL && p.dh0i) p.dh0i[i] = lnr[j] * Gi[j] - lni[j] * Gr[j];
+        p.dh0r[i] = cr[j];
+        if (!REAL && p.dh0i) p.dh0i[i] = ci[j];
       }
     }
   }
   // Per-sequence parameter-gradient partials: [da | domega | ds | dg] (C, N) each, dD (C).
   {
-    const int64_t K = 4 * p.C * p.N + p.C;
-    float* row = p.part + s * K;
+    const int64_t Kp = 4 * p.C * p.N + p.C;
+    float* row = p.part + s * Kp;
     const int64_t CN = p.C * p.N;
 #pragma unroll
     for (int j = 0; j < kGM; ++j) {
@@ -973,7 +1009,7 @@ size_t dbc_floats(const SemxSelectiveLruArgs* a) {
 template <bool REAL, int GAIN, int NG>
 int launch_fwd(const SParams& p, const Geometry& g, cudaStream_t st) {
   const dim3 grid((unsigned)g.nblocks, (unsigned)p.S);
-  const size_t smem = Tiles<REAL, NG>::bytes();
+  const size_t smem = Tiles<REAL, NG, kTileF, false>::bytes();
   if (!semx::allow_smem(slru_fwd_kernel<REAL, GAIN, NG>, smem)) return SEMX_ERR_LAUNCH;
   slru_fwd_kernel<REAL, GAIN, NG><<<grid, kThreads, smem, st>>>(p);
   return semx::check_launch("slru_fwd_kernel");

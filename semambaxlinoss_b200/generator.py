@@ -37,7 +37,7 @@ def config3_cfg(num_tfmamba: int = 4) -> dict:
             hid_feature=64, dense_stride=2, compress_factor=0.3, num_tfmamba=num_tfmamba, beta=2.0,
             input_channel=2, output_channel=1, use_transpose=True,
             time_mixer=dict(mixer, ssm="selective_lru", d_state=16,
-                            ssm_params=dict(input_gain="gamma", chunk_size=64)),
+                            ssm_params=dict(input_gain="gamma", chunk_size=16)),
             freq_mixer=dict(mixer, ssm="linoss", d_state=16,
                             ssm_params=dict(discretization="IMEX", damping=True)),
         ),

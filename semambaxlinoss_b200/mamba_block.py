@@ -173,7 +173,7 @@ def _build_mixer_cls(d_model, model_cfg, layer_idx=0):
             rate_scale=ssm_params.get("rate_scale", 1.0),
             input_gain=ssm_params.get("input_gain", "gamma"),
             use_triton=ssm_params.get("use_triton", False),
-            chunk_size=ssm_params.get("chunk_size", 64),
+            chunk_size=ssm_params.get("chunk_size", 16),
             block_c=ssm_params.get("block_c", 32),
         )
     elif ssm in _OUT_OF_SCOPE:

@@ -20,7 +20,7 @@ import torch
 
 from .. import _lib
 
-DEFAULT_CHUNK = 64
+DEFAULT_CHUNK = 16
 
 
 def _f32(t):

@@ -64,7 +64,7 @@ class SelectiveLRU(nn.Module):
         rate_scale: float = 1.0,
         input_gain: str = "gamma",
         use_triton: bool = False,
-        chunk_size: int = 64,
+        chunk_size: int = 16,
         block_c: int = 32,
         device=None,
         dtype=None,

@@ -105,6 +105,8 @@ def test_fused_op_options(gain, opts):
     (2, 12, 20, 32, 12),    # N = 32 (NG = 8)
     (1, 17, 300, 16, 16),   # 10 channel blocks: two clusters, cross-cluster sum
     (2, 1, 5, 4, 4),        # single step
+    (2, 70, 24, 16, 48),    # chunk of three staged tiles (pass 1 forwards, pass 2 backwards)
+    (1, 45, 9, 8, 20),      # chunk of a full and a partial tile, ragged last chunk
 ])
 def test_fused_op_edge_shapes(B, T, C, N, chunk):
     t, gy, ghf = _inputs(B, T, C, N, 1000 + C + N, ("env", "detune", "h0", "hf"))

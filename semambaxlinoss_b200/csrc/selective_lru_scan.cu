@@ -381,7 +381,7 @@ __device__ __forceinline__ void advance(const ModeParams& mp, bool detune, const
 }
 
 // ----------------------------------------------------------------------------- forward
-template <bool REAL, int GAIN, int NG>
+template <bool REAL, int GAIN, int NG, bool EXTRA>
 __global__ void __launch_bounds__(kThreads) slru_fwd_kernel(const SParams p) {
   using T = Tiles<REAL, NG, kTileF, false>;
   constexpr int CW = 32 / NG;
@@ -398,6 +398,9 @@ __global__ void __launch_bounds__(kThreads) slru_fwd_kernel(const SParams p) {
   const int L = (int)p.L;
   const bool vecC = (p.C % 4) == 0 && semx_aligned16(p.dnu) && semx_aligned16(p.x) &&
                     (REAL || semx_aligned16(p.dth));
+  // Per-mode detune (complex only) and envelope readout exist only in the EXTRA build.
+  const bool detune = EXTRA && !REAL && p.detune;
+  const bool envelope = EXTRA && p.envelope;
   const bool vecN = (p.N % 4) == 0 && semx_aligned16(p.Bre) && semx_aligned16(p.Cre) &&
                     (REAL || (semx_aligned16(p.Bim) && semx_aligned16(p.Cim)));
 
@@ -442,14 +445,14 @@ __global__ void __launch_bounds__(kThreads) slru_fwd_kernel(const SParams p) {
       }
       StepIn<REAL> cur;
       tile_step<REAL, T, true>(buf, i, c_local, g, cur);
-      advance<REAL, GAIN>(mp, p.detune, cur, hr, hi);
+      advance<REAL, GAIN>(mp, detune, cur, hr, hi);
       float yp = 0.f;
 #pragma unroll
       for (int j = 0; j < kGM; ++j) {
         yp += cur.cre[j] * hr[j];
         if (!REAL) yp -= cur.cim[j] * hi[j];
       }
-      if (p.envelope) {
+      if (envelope) {
 #pragma unroll
         for (int j = 0; j < kGM; ++j) yp += mp.ge[j] * (hr[j] * hr[j] + (REAL ? 0.f : hi[j] * hi[j]));
       }
@@ -525,7 +528,7 @@ __device__ __forceinline__ TileEntry entry_of(int k, int e, int K, int L) {
   return E;
 }
 
-template <bool REAL, int GAIN, int NG>
+template <bool REAL, int GAIN, int NG, bool EXTRA>
 __global__ void __launch_bounds__(kThreads) slru_bwd_kernel(const SParams p) {
   using Lay = BwdLayout<REAL, NG>;
   using T = typename Lay::T;
@@ -554,6 +557,8 @@ __global__ void __launch_bounds__(kThreads) slru_bwd_kernel(const SParams p) {
   const int K = p.chunk;
   const bool vecC = (p.C % 4) == 0 && semx_aligned16(p.dnu) && semx_aligned16(p.x) &&
                     semx_aligned16(p.dy) && (REAL || semx_aligned16(p.dth));
+  const bool detune = EXTRA && !REAL && p.detune;
+  const bool envelope = EXTRA && p.envelope;
   const bool vecN = (p.N % 4) == 0 && semx_aligned16(p.Bre) && semx_aligned16(p.Cre) &&
                     (REAL || (semx_aligned16(p.Bim) && semx_aligned16(p.Cim)));
 
@@ -627,7 +632,7 @@ __global__ void __launch_bounds__(kThreads) slru_bwd_kernel(const SParams p) {
           }
           StepIn<REAL> in;
           tile_step<REAL, T, false>(buf, i, c_local, g, in);
-          advance<REAL, GAIN>(mp, p.detune, in, hr, hi);
+          advance<REAL, GAIN>(mp, detune, in, hr, hi);
         }
       }
 
@@ -660,7 +665,7 @@ __global__ void __launch_bounds__(kThreads) slru_bwd_kernel(const SParams p) {
             if (i < nr) {
               StepIn<REAL> in;
               tile_step<REAL, T, false>(buf, ta - E.t0 + i, c_local, g, in);
-              advance<REAL, GAIN>(mp, p.detune, in, Hr[i], Hi[i]);
+              advance<REAL, GAIN>(mp, detune, in, Hr[i], Hi[i]);
             }
           }
           // Adjoint through the sub-block.
@@ -678,12 +683,12 @@ __global__ void __launch_bounds__(kThreads) slru_bwd_kernel(const SParams p) {
                 const float hrt = Hr[i][j], hit = Hi[i][j];
                 const float hpr = i == 0 ? H0r[j] : Hr[i > 0 ? i - 1 : 0][j];
                 const float hpi = i == 0 ? H0i[j] : Hi[i > 0 ? i - 1 : 0][j];
-                const Disc d = discretise<REAL, GAIN>(mp.a[j], mp.om[j], mp.sd[j], p.detune,
+                const Disc d = discretise<REAL, GAIN>(mp.a[j], mp.om[j], mp.sd[j], detune,
                                                       in.dnu, in.dth);
                 // Local adjoint from the readout (and the envelope term).
                 float gre = dyv * in.cre[j];
                 float gim = REAL ? 0.f : -dyv * in.cim[j];
-                if (p.envelope) {
+                if (envelope) {
                   const float w = 2.f * dyv * mp.ge[j];
                   gre += w * hrt;
                   if (!REAL) gim += w * hit;
@@ -693,24 +698,28 @@ __global__ void __launch_bounds__(kThreads) slru_bwd_kernel(const SParams p) {
                 const float Gi = REAL ? 0.f : gim + ci[j];
                 cr[j] = REAL ? d.lre * Gr : d.lre * Gr + d.lim * Gi;
                 ci[j] = REAL ? 0.f : d.lre * Gi - d.lim * Gr;
-                // Input map Bu = (gain x) B: dB = conj(gain x) G, d(gain) = x conj(B) G.
+                // Drive Bu = gain x B. With bG = conj(B) G: dB = conj(gain x) G,
+                // dx += Re(conj(gain) bG), d(gain) = x bG.
+                const float bGr = REAL ? in.bre[j] * Gr : in.bre[j] * Gr + in.bim[j] * Gi;
+                const float bGi = REAL ? 0.f : in.bre[j] * Gi - in.bim[j] * Gr;
                 const float gxr = d.gr * in.x, gxi = d.gi * in.x;
                 const float vBr = REAL ? gxr * Gr : gxr * Gr + gxi * Gi;
                 const float vBi = REAL ? 0.f : gxr * Gi - gxi * Gr;
-                if (REAL) {
-                  sum_dx += d.gr * in.bre[j] * Gr;
-                } else {
-                  const float wre = d.gr * in.bre[j] - d.gi * in.bim[j];
-                  const float wim = d.gr * in.bim[j] + d.gi * in.bre[j];
-                  sum_dx += wre * Gr + wim * Gi;
-                }
-                const float dgr = REAL ? in.x * (in.bre[j] * Gr) : in.x * (in.bre[j] * Gr + in.bim[j] * Gi);
-                const float dgi = REAL ? 0.f : in.x * (in.bre[j] * Gi - in.bim[j] * Gr);
-                float d_nu_tot = 0.f, d_dnu = 0.f, da_extra = 0.f, dbase_extra = 0.f;
+                sum_dx += (GAIN == SEMX_GAIN_ZOH && !REAL) ? d.gr * bGr + d.gi * bGi : d.gr * bGr;
+                const float dgr = in.x * bGr;
+                const float dgi = in.x * bGi;
+                // P = nu * dL/dnu and d_th = dL/d(angle), from d lam = G conj(h_{t-1}):
+                // nu (dlre cs + dlim sn) = dlre lre + dlim lim, nu (dlim cs - dlre sn) =
+                // dlim lre - dlre lim.
+                const float dlre = REAL ? Gr * hpr : Gr * hpr + Gi * hpi;
+                const float dlim = REAL ? 0.f : Gi * hpr - Gr * hpi;
+                float P = REAL ? dlre * d.lre : dlre * d.lre + dlim * d.lim;
+                const float d_th = REAL ? 0.f : dlim * d.lre - dlre * d.lim;
+                float d_dnu = 0.f, da_extra = 0.f, dbase_extra = 0.f;
                 if (GAIN == SEMX_GAIN_GAMMA) {
-                  // gain = sqrt(max(1 - nu^2, 1e-6)): d gain / d nu = -nu / gain where live.
-                  const bool live = (1.f - d.nu * d.nu) >= 1e-6f;
-                  d_nu_tot = live ? -dgr * d.nu * d.rs : 0.f;
+                  // gain = sqrt(max(1 - nu^2, 1e-6)): nu d gain / d nu = -nu^2 / gain where live.
+                  const float nu2 = d.nu * d.nu;
+                  P -= ((1.f - nu2) >= 1e-6f) ? dgr * nu2 * d.rs : 0.f;
                 } else if (GAIN == SEMX_GAIN_MAMBA) {
                   d_dnu = dgr;
                 } else {
@@ -723,24 +732,15 @@ __global__ void __launch_bounds__(kThreads) slru_bwd_kernel(const SParams p) {
                   da_extra = -(dgr * qr + dgi * qi);
                   dbase_extra = dgi * qr - dgr * qi;
                 }
-                // d lam = G_t conj(h_{t-1}).
-                const float dlre = REAL ? Gr * hpr : Gr * hpr + Gi * hpi;
-                float d_th = 0.f;
-                if (REAL) {
-                  d_nu_tot += dlre;
-                } else {
-                  const float dlim = Gi * hpr - Gr * hpi;
-                  d_nu_tot += dlre * d.cs + dlim * d.sn;
-                  d_th = d.nu * (dlim * d.cs - dlre * d.sn);
-                }
-                d_dnu += d_nu_tot * (-mp.a[j]) * d.nu;
-                acc_a[j] += d_nu_tot * (-in.dnu) * d.nu + da_extra;
+                // nu = exp(-dnu a): d nu / d dnu = -a nu, d nu / d a = -dnu nu.
+                d_dnu -= mp.a[j] * P;
+                acc_a[j] += da_extra - in.dnu * P;
                 if (!REAL) {
                   d_dnu += d_th * d.base;
                   const float dbase = d_th * in.dnu + dbase_extra;
                   acc_om[j] += dbase;
-                  sum_dth += dbase * mp.sd[j];
-                  if (p.detune) acc_s[j] += dbase * in.dth;
+                  sum_dth += detune ? dbase * mp.sd[j] : dbase;
+                  if (detune) acc_s[j] += dbase * in.dth;
                 }
                 sum_dnu += d_dnu;
                 vals[0 * kGM + j] = vBr;
@@ -1006,18 +1006,19 @@ size_t dbc_floats(const SemxSelectiveLruArgs* a) {
   return (size_t)a->S * a->L * g.nclusters * (a->real ? 2 : 4) * a->N;
 }
 
-template <bool REAL, int GAIN, int NG>
+template <bool REAL, int GAIN, int NG, bool EXTRA>
 int launch_fwd(const SParams& p, const Geometry& g, cudaStream_t st) {
   const dim3 grid((unsigned)g.nblocks, (unsigned)p.S);
   const size_t smem = Tiles<REAL, NG, kTileF, false>::bytes();
-  if (!semx::allow_smem(slru_fwd_kernel<REAL, GAIN, NG>, smem)) return SEMX_ERR_LAUNCH;
-  slru_fwd_kernel<REAL, GAIN, NG><<<grid, kThreads, smem, st>>>(p);
+  auto kern = slru_fwd_kernel<REAL, GAIN, NG, EXTRA>;
+  if (!semx::allow_smem(kern, smem)) return SEMX_ERR_LAUNCH;
+  kern<<<grid, kThreads, smem, st>>>(p);
   return semx::check_launch("slru_fwd_kernel");
 }
 
-template <bool REAL, int GAIN, int NG>
+template <bool REAL, int GAIN, int NG, bool EXTRA>
 int launch_bwd(const SParams& p, const Geometry& g, size_t smem, cudaStream_t st) {
-  auto kern = slru_bwd_kernel<REAL, GAIN, NG>;
+  auto kern = slru_bwd_kernel<REAL, GAIN, NG, EXTRA>;
   if (!semx::allow_smem(kern, smem)) return SEMX_ERR_LAUNCH;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)g.grid_x, (unsigned)p.S);
@@ -1037,12 +1038,13 @@ int launch_bwd(const SParams& p, const Geometry& g, size_t smem, cudaStream_t st
   return semx::check_launch("slru_bwd_kernel");
 }
 
-template <bool REAL, int GAIN>
+template <bool REAL, int GAIN, bool EXTRA>
 int dispatch_ng(bool bwd, const SParams& p, const Geometry& g, size_t smem, cudaStream_t st) {
   switch (g.ng) {
 #define SEMX_CASE(NGV) \
   case NGV:            \
-    return bwd ? launch_bwd<REAL, GAIN, NGV>(p, g, smem, st) : launch_fwd<REAL, GAIN, NGV>(p, g, st);
+    return bwd ? launch_bwd<REAL, GAIN, NGV, EXTRA>(p, g, smem, st)  \
+               : launch_fwd<REAL, GAIN, NGV, EXTRA>(p, g, st);
     SEMX_CASE(1)
     SEMX_CASE(2)
     SEMX_CASE(4)
@@ -1052,19 +1054,29 @@ int dispatch_ng(bool bwd, const SParams& p, const Geometry& g, size_t smem, cuda
   return semx::fail(SEMX_ERR_UNSUPPORTED, "selective_lru: no kernel for NG=%d", g.ng);
 }
 
+template <int GAIN, bool EXTRA>
+int dispatch_real(bool bwd, bool real, const SParams& p, const Geometry& g, size_t smem,
+                  cudaStream_t st) {
+  return real ? dispatch_ng<true, GAIN, EXTRA>(bwd, p, g, smem, st)
+              : dispatch_ng<false, GAIN, EXTRA>(bwd, p, g, smem, st);
+}
+
+// Kernels are specialised on the element type, the input gain, the lanes per channel and
+// whether the per-mode detune or the envelope readout is on (EXTRA).
 int dispatch(bool bwd, const SemxSelectiveLruArgs* a, const SParams& p, const Geometry& g,
              size_t smem, cudaStream_t st) {
   const bool real = a->real != 0;
+  const bool extra = p.detune || p.envelope;
   switch (a->input_gain) {
     case SEMX_GAIN_GAMMA:
-      return real ? dispatch_ng<true, SEMX_GAIN_GAMMA>(bwd, p, g, smem, st)
-                  : dispatch_ng<false, SEMX_GAIN_GAMMA>(bwd, p, g, smem, st);
+      return extra ? dispatch_real<SEMX_GAIN_GAMMA, true>(bwd, real, p, g, smem, st)
+                   : dispatch_real<SEMX_GAIN_GAMMA, false>(bwd, real, p, g, smem, st);
     case SEMX_GAIN_MAMBA:
-      return real ? dispatch_ng<true, SEMX_GAIN_MAMBA>(bwd, p, g, smem, st)
-                  : dispatch_ng<false, SEMX_GAIN_MAMBA>(bwd, p, g, smem, st);
+      return extra ? dispatch_real<SEMX_GAIN_MAMBA, true>(bwd, real, p, g, smem, st)
+                   : dispatch_real<SEMX_GAIN_MAMBA, false>(bwd, real, p, g, smem, st);
     default:
-      return real ? dispatch_ng<true, SEMX_GAIN_ZOH>(bwd, p, g, smem, st)
-                  : dispatch_ng<false, SEMX_GAIN_ZOH>(bwd, p, g, smem, st);
+      return extra ? dispatch_real<SEMX_GAIN_ZOH, true>(bwd, real, p, g, smem, st)
+                   : dispatch_real<SEMX_GAIN_ZOH, false>(bwd, real, p, g, smem, st);
   }
 }
 

@@ -314,6 +314,72 @@ size_t semx_mimo_workspace_bytes(const SemxMimoArgs* args);
 int semx_mimo_fwd(const SemxMimoArgs* args, semx_stream_t stream);
 int semx_mimo_bwd(const SemxMimoArgs* args, semx_stream_t stream);
 
+/* ------------------------------------------------------------------------------------
+ * Fused SelectiveLRUMIMO layer after its token projections: for every head h of H heads
+ * (Nh modes, Fh channels, rank R) and token t, from the projection row `proj` and the
+ * input x,
+ *   dnu = softplus(proj[dnu_h]) * rate_scale,  dth = proj[dth_h]
+ *   lam[n] = exp(dnu (-a[n] + j (omega[n] + (detune ? s[n] dth : dth)))),  a = exp(A_log)
+ *   Bu[n]  = gain[n] (sum_f B[h,n,f] x[h*Fh+f] + sum_r s_b[r] b_t[r,n])   (B complex,
+ *            the rank write real), gain per input_gain (GAMMA / MAMBA / ZOH / NONE)
+ *   h_t    = lam h_{t-1} + Bu,  h_{-1} = 0
+ *   y[f]   = sum_n Re(C[h,f,n] h[n]) + D[h*Fh+f] x[h*Fh+f]
+ *            + sum_n env[h,f,n] |h[n]|^2                              (envelope only)
+ *            + sum_r s_c[r] Re(sum_n c_t[r,n] h[n]) c_out[h*R+r, f]  (R > 0)
+ * proj (S,L,P) columns: [dnu (H) | dth (H) | s_b (H*R) | b_t (H*R*Nh) | s_c (H*R) |
+ * c_t (H*R*2Nh, per (h, r) Nh real parts then Nh imaginary parts)], P = 2H when R = 0.
+ * x: (S,L,H*Fh); x and proj are fp32, or bf16 when `bf16` is set; y, dy, dx fp32; dproj
+ * has the dtype of proj. Parameters fp32: A_log, omega, detune_gain (H,Nh); B (H,Nh,Fh,2);
+ * C (H,Fh,Nh,2); D (H*Fh); c_out (H*R,Fh); env_gain (H,Fh,Nh).
+ * Replaces SelectiveLRUMIMO.forward after its projections
+ * (models/selective_lru/selective_lru.py:488-587): poles, drive, gain, scan, readout and
+ * feedthrough in one pass per (sequence, head). Training forwards store the state at
+ * every 32-step block in ckpt (semx_mimo_layer_ckpt_bytes()). Backward recomputes from
+ * ckpt and writes dx (the input-map and skip part), dproj and the parameter gradients
+ * (reduced over sequences in a fixed order; dA_log is with respect to A_log).
+ * ---------------------------------------------------------------------------------- */
+typedef struct SemxMimoLayerArgs {
+  uint32_t struct_size;
+  int32_t input_gain; /* enum semx_input_gain                               */
+  int32_t rank;       /* R >= 0                                             */
+  int32_t detune;     /* 1: detune_gain given                               */
+  int32_t envelope;   /* 1: env_gain given                                  */
+  int32_t bf16;       /* 1: x, proj, dproj are bf16                         */
+  float rate_scale;
+  int32_t reserved;
+  int64_t S, L, H, Nh, Fh;
+  const void* x;
+  const void* proj;
+  const float* A_log;
+  const float* omega;
+  const float* detune_gain;
+  const float* B;
+  const float* C;
+  const float* D;
+  const float* c_out;
+  const float* env_gain;
+  float* y;
+  float* ckpt; /* optional in the forward; required by the backward */
+  const float* dy;
+  float* dx;
+  void* dproj;
+  float* dA_log;
+  float* domega;
+  float* ddetune;
+  float* dB;
+  float* dC;
+  float* dD;
+  float* dc_out;
+  float* denv;
+  void* workspace; /* semx_mimo_layer_workspace_bytes(), backward only */
+} SemxMimoLayerArgs;
+
+size_t semx_mimo_layer_args_size(void);
+size_t semx_mimo_layer_ckpt_bytes(const SemxMimoLayerArgs* args);
+size_t semx_mimo_layer_workspace_bytes(const SemxMimoLayerArgs* args);
+int semx_mimo_layer_fwd(const SemxMimoLayerArgs* args, semx_stream_t stream);
+int semx_mimo_layer_bwd(const SemxMimoLayerArgs* args, semx_stream_t stream);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

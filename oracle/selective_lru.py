@@ -132,11 +132,12 @@ def mimo_scan_readout(lam_re, lam_im, Bu_re, Bu_im, C_re, C_im, x, D, H, Nh, Fh)
     return y, h.real, h.imag
 
 
-def mimo_discretise(delta_nu, delta_theta, x, params: dict, cfg: dict):
+def mimo_discretise(delta_nu, delta_theta, x, params: dict, cfg: dict, s_b=None, b_t=None):
     """Pole, drive and gain of ``SelectiveLRUMIMO.forward`` (selective_lru.py:502-546).
 
-    delta_nu, delta_theta: (B,T,H) after softplus / rate scale. Returns (lam_re, lam_im,
-    Bu_re, Bu_im) each (B,T,N)."""
+    delta_nu, delta_theta: (B,T,H) after softplus / rate scale; s_b (B,T,H,r) and b_t
+    (B,T,H,r,Nh) the rank-write projections (computed from x when not given). Returns
+    (lam_re, lam_im, Bu_re, Bu_im) each (B,T,N)."""
     Bsz, T, Fdim = x.shape
     H, rank = cfg["n_heads"], cfg.get("rank", 0)
     Nh, Fh = cfg["state_dim"] // H, Fdim // H
@@ -153,8 +154,9 @@ def mimo_discretise(delta_nu, delta_theta, x, params: dict, cfg: dict):
     Bu_re = torch.einsum("hnf,bthf->bthn", params["B"][..., 0], xh)
     Bu_im = torch.einsum("hnf,bthf->bthn", params["B"][..., 1], xh)
     if rank > 0:
-        s_b = (x @ params["b_coef.weight"].t()).view(Bsz, T, H, rank)
-        b_t = (x @ params["b_dir.weight"].t()).view(Bsz, T, H, rank, Nh)
+        if s_b is None:
+            s_b = (x @ params["b_coef.weight"].t()).view(Bsz, T, H, rank)
+            b_t = (x @ params["b_dir.weight"].t()).view(Bsz, T, H, rank, Nh)
         Bu_re = Bu_re + torch.einsum("bthr,bthrn->bthn", s_b, b_t)
     gain_mode = cfg.get("input_gain", "gamma")
     if gain_mode == "gamma":
@@ -175,19 +177,43 @@ def mimo_discretise(delta_nu, delta_theta, x, params: dict, cfg: dict):
     return lam_re, lam_im, Bu_re.reshape(Bsz, T, N), Bu_im.reshape(Bsz, T, N)
 
 
-def selective_lru_mimo_forward(params: dict, x, cfg: dict, rate_scale=None):
-    """``SelectiveLRUMIMO.forward`` (selective_lru.py:488-587) from a parameter dict with
-    the reference's names. cfg: n_heads, state_dim, rank, rate_scale, input_gain,
-    envelope_readout, mode_detune."""
+def mimo_projection(params: dict, x, cfg: dict):
+    """All token projections of ``SelectiveLRUMIMO`` as one row per token, in the column
+    order [dnu_raw (H) | dth (H) | s_b (H r) | b_t (H r Nh) | s_c (H r) | c_t (H r 2Nh)]
+    (dt_nu_proj / dt_theta_proj / b_coef / b_dir / c_coef / c_read of selective_lru.py:
+    494-498, 528-530, 578-579)."""
+    ws = [params["dt_nu_proj.weight"], params["dt_theta_proj.weight"]]
+    bs = [params["dt_nu_proj.bias"], params["dt_theta_proj.bias"]]
+    if cfg.get("rank", 0) > 0:
+        for k in ("b_coef", "b_dir", "c_coef", "c_read"):
+            w = params[k + ".weight"]
+            ws.append(w)
+            bs.append(w.new_zeros(w.shape[0]))
+    return x @ torch.cat(ws, 0).t() + torch.cat(bs)
+
+
+def selective_lru_mimo_from_projection(proj, params: dict, x, cfg: dict, rate_scale=None):
+    """``SelectiveLRUMIMO.forward`` (selective_lru.py:488-587) given the projection rows
+    of :func:`mimo_projection` (so a caller can fix their rounding, e.g. to bf16)."""
     Bsz, T, Fdim = x.shape
     H, rank = cfg["n_heads"], cfg.get("rank", 0)
     Nh, Fh = cfg["state_dim"] // H, Fdim // H
-    delta_nu = F.softplus(x @ params["dt_nu_proj.weight"].t() + params["dt_nu_proj.bias"])
+    delta_nu = F.softplus(proj[..., :H])
     rs = cfg.get("rate_scale", 1.0) if rate_scale is None else float(rate_scale)
     if rs != 1.0:
         delta_nu = delta_nu * rs
-    delta_theta = x @ params["dt_theta_proj.weight"].t() + params["dt_theta_proj.bias"]
-    lam_re, lam_im, Bu_re, Bu_im = mimo_discretise(delta_nu, delta_theta, x, params, cfg)
+    delta_theta = proj[..., H:2 * H]
+    s_b = b_t = s_c = cr = None
+    if rank > 0:
+        o = 2 * H
+        s_b = proj[..., o:o + H * rank].reshape(Bsz, T, H, rank)
+        o += H * rank
+        b_t = proj[..., o:o + H * rank * Nh].reshape(Bsz, T, H, rank, Nh)
+        o += H * rank * Nh
+        s_c = proj[..., o:o + H * rank].reshape(Bsz, T, H, rank)
+        o += H * rank
+        cr = proj[..., o:o + 2 * H * rank * Nh].reshape(Bsz, T, H, rank, 2 * Nh)
+    lam_re, lam_im, Bu_re, Bu_im = mimo_discretise(delta_nu, delta_theta, x, params, cfg, s_b, b_t)
     y, h_re, h_im = mimo_scan_readout(
         lam_re, lam_im, Bu_re, Bu_im, params["C"][..., 0], params["C"][..., 1], x,
         params["D"], H, Nh, Fh,
@@ -197,10 +223,16 @@ def selective_lru_mimo_forward(params: dict, x, cfg: dict, rate_scale=None):
         p = hh.real**2 + hh.imag**2
         y = y + torch.einsum("hfn,bthn->bthf", params["env_gain"], p).reshape(Bsz, T, Fdim)
     if rank > 0:
-        s_c = (x @ params["c_coef.weight"].t()).view(Bsz, T, H, rank)
-        cr = (x @ params["c_read.weight"].t()).view(Bsz, T, H, rank, 2 * Nh)
         c_t = torch.complex(cr[..., :Nh], cr[..., Nh:])
         read = torch.einsum("bthrn,bthn->bthr", c_t, hh).real
         c_out = params["c_out"].view(H, rank, Fh)
         y = y + torch.einsum("bthr,hrf->bthf", s_c * read, c_out).reshape(Bsz, T, Fdim)
     return y
+
+
+def selective_lru_mimo_forward(params: dict, x, cfg: dict, rate_scale=None):
+    """``SelectiveLRUMIMO.forward`` (selective_lru.py:488-587) from a parameter dict with
+    the reference's names. cfg: n_heads, state_dim, rank, rate_scale, input_gain,
+    envelope_readout, mode_detune."""
+    return selective_lru_mimo_from_projection(mimo_projection(params, x, cfg), params, x, cfg,
+                                              rate_scale)

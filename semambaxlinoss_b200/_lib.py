@@ -130,12 +130,35 @@ class SemxMimoArgs(ctypes.Structure):
     )]
 
 
+class SemxMimoLayerArgs(ctypes.Structure):
+    _fields_ = [
+        ("struct_size", ctypes.c_uint32),
+        ("input_gain", ctypes.c_int32),
+        ("rank", ctypes.c_int32),
+        ("detune", ctypes.c_int32),
+        ("envelope", ctypes.c_int32),
+        ("bf16", ctypes.c_int32),
+        ("rate_scale", ctypes.c_float),
+        ("reserved", ctypes.c_int32),
+        ("S", ctypes.c_int64),
+        ("L", ctypes.c_int64),
+        ("H", ctypes.c_int64),
+        ("Nh", ctypes.c_int64),
+        ("Fh", ctypes.c_int64),
+    ] + [(name, ctypes.c_void_p) for name in (
+        "x", "proj", "A_log", "omega", "detune_gain", "B", "C", "D", "c_out", "env_gain", "y",
+        "ckpt", "dy", "dx", "dproj", "dA_log", "domega", "ddetune", "dB", "dC", "dD", "dc_out",
+        "denv", "workspace",
+    )]
+
+
 # (python struct, C size query) for every argument struct in semx.h.
 STRUCTS = {
     "SemxLinossArgs": (SemxLinossArgs, "semx_linoss_args_size"),
     "SemxSelectiveLruArgs": (SemxSelectiveLruArgs, "semx_selective_lru_args_size"),
     "SemxComplexScanArgs": (SemxComplexScanArgs, "semx_complex_scan_args_size"),
     "SemxMimoArgs": (SemxMimoArgs, "semx_mimo_args_size"),
+    "SemxMimoLayerArgs": (SemxMimoLayerArgs, "semx_mimo_layer_args_size"),
 }
 
 # Every symbol semx.h declares, with its ctypes signature.
@@ -170,6 +193,11 @@ _SIGNATURES = {
     "semx_mimo_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(SemxMimoArgs)]),
     "semx_mimo_fwd": (ctypes.c_int, [ctypes.POINTER(SemxMimoArgs), ctypes.c_void_p]),
     "semx_mimo_bwd": (ctypes.c_int, [ctypes.POINTER(SemxMimoArgs), ctypes.c_void_p]),
+    "semx_mimo_layer_args_size": (ctypes.c_size_t, []),
+    "semx_mimo_layer_ckpt_bytes": (ctypes.c_size_t, [ctypes.POINTER(SemxMimoLayerArgs)]),
+    "semx_mimo_layer_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(SemxMimoLayerArgs)]),
+    "semx_mimo_layer_fwd": (ctypes.c_int, [ctypes.POINTER(SemxMimoLayerArgs), ctypes.c_void_p]),
+    "semx_mimo_layer_bwd": (ctypes.c_int, [ctypes.POINTER(SemxMimoLayerArgs), ctypes.c_void_p]),
 }
 
 _lib = None

@@ -31,9 +31,15 @@
 #include <cooperative_groups.h>
 
 #include "semx_common.cuh"
+#include "semx_math.cuh"
 #include "semx_reduce.cuh"
 
 namespace cg = cooperative_groups;
+using semx::ex2_approx;
+using semx::rcp_approx;
+using semx::rsqrt_approx;
+using semx::sin_reduced;
+using semx::sincos_reduced;
 
 namespace {
 
@@ -85,45 +91,6 @@ struct SParams {
   float* part;      // (S, 4*C*N + C) per-sequence parameter-gradient partials
   float* dbc_part;  // (S*L, nclusters, narr*N) when nclusters > 1
 };
-
-// Per-element transcendentals on the special-function unit (PTX ex2 / sin / cos / rsqrt /
-// rcp .approx: one MUFU instruction each instead of a libm call). sin and cos take their
-// argument reduced to [-pi, pi] first: r = x - k * 2pi with k = rint(x / 2pi) and 2pi
-// split Cody-Waite style into hi = 6.28125 (exact: k * hi has no rounding for |k| < 2^16)
-// plus lo = 2pi - hi, so r carries no reduction error worth speaking of.
-__device__ __forceinline__ float ex2_approx(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-__device__ __forceinline__ float rsqrt_approx(float x) {
-  float y;
-  asm("rsqrt.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-__device__ __forceinline__ float rcp_approx(float x) {
-  float y;
-  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-__device__ __forceinline__ float reduce_2pi(float x) {
-  constexpr float kInv2Pi = 0.15915494f;
-  constexpr float k2PiHi = 6.28125f;
-  constexpr float k2PiLo = 0.0019353072f;
-  const float k = rintf(x * kInv2Pi);
-  return fmaf(-k, k2PiLo, fmaf(-k, k2PiHi, x));
-}
-__device__ __forceinline__ void sincos_reduced(float x, float* s, float* c) {
-  const float r = reduce_2pi(x);
-  asm("sin.approx.f32 %0, %1;" : "=f"(*s) : "f"(r));
-  asm("cos.approx.f32 %0, %1;" : "=f"(*c) : "f"(r));
-}
-__device__ __forceinline__ float sin_reduced(float x) {
-  const float r = reduce_2pi(x);
-  float s;
-  asm("sin.approx.f32 %0, %1;" : "=f"(s) : "f"(r));
-  return s;
-}
 
 // Pole, drive gain and their intermediates for one (t, c, n): lam = nu (cs + j sn),
 // gain = gr + j gi; rs = 1 / gr for the gamma gain, inv_den = 1 / |A_c|^2 for ZOH.

@@ -1,0 +1,49 @@
+// Transcendentals on the special-function unit for the scan kernels.
+#pragma once
+
+namespace semx {
+
+// Per-element transcendentals on the special-function unit (PTX ex2 / sin / cos / rsqrt /
+// rcp .approx: one MUFU instruction each instead of a libm call). sin and cos take their
+// argument reduced to [-pi, pi] first: r = x - k * 2pi with k = rint(x / 2pi) and 2pi
+// split Cody-Waite style into hi = 6.28125 (exact: k * hi has no rounding for |k| < 2^16)
+// plus lo = 2pi - hi, so r carries no reduction error worth speaking of.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float rsqrt_approx(float x) {
+  float y;
+  asm("rsqrt.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float reduce_2pi(float x) {
+  constexpr float kInv2Pi = 0.15915494f;
+  constexpr float k2PiHi = 6.28125f;
+  constexpr float k2PiLo = 0.0019353072f;
+  const float k = rintf(x * kInv2Pi);
+  return fmaf(-k, k2PiLo, fmaf(-k, k2PiHi, x));
+}
+__device__ __forceinline__ void sincos_reduced(float x, float* s, float* c) {
+  const float r = reduce_2pi(x);
+  asm("sin.approx.f32 %0, %1;" : "=f"(*s) : "f"(r));
+  asm("cos.approx.f32 %0, %1;" : "=f"(*c) : "f"(r));
+}
+__device__ __forceinline__ float sin_reduced(float x) {
+  const float r = reduce_2pi(x);
+  float s;
+  asm("sin.approx.f32 %0, %1;" : "=f"(s) : "f"(r));
+  return s;
+}
+
+// torch.nn.functional.softplus (beta 1, threshold 20) and its derivative.
+__device__ __forceinline__ float softplus(float x) { return x > 20.f ? x : log1pf(expf(x)); }
+__device__ __forceinline__ float softplus_grad(float x) { return x > 20.f ? 1.f : 1.f / (1.f + expf(-x)); }
+
+}  // namespace semx

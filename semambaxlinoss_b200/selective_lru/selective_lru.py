@@ -257,68 +257,38 @@ class SelectiveLRUMIMO(nn.Module):
         self.omega._no_weight_decay = True
         self.D._no_weight_decay = True
 
-    def _poles_and_drive(self, x, delta_nu, delta_theta):
-        """(lam_re, lam_im, Bu_re, Bu_im), each (B, T, N): exact-ZOH poles and the gained
-        drive (static block-diagonal B x plus the rank-r write)."""
-        Bsz, T, _ = x.shape
-        H, Nh, N = self.n_heads, self.n_head, self.state_dim
-        a = torch.exp(self.A_log)
-        dnu = delta_nu.unsqueeze(-1)
-        dth = delta_theta.unsqueeze(-1)
-        nu = torch.exp(-dnu * a)
-        base = self.omega + (self.detune_gain * dth if self.mode_detune else dth)
-        theta = dnu * base
-        cos, sin = torch.cos(theta), torch.sin(theta)
-        lam_re = (nu * cos).reshape(Bsz, T, N)
-        lam_im = (nu * sin).reshape(Bsz, T, N)
-        xh = x.view(Bsz, T, H, self.f_head)
-        Bu_re = torch.einsum("hnf,bthf->bthn", self.B[..., 0], xh)
-        Bu_im = torch.einsum("hnf,bthf->bthn", self.B[..., 1], xh)
+    def _projection(self):
+        """Weight and bias of all token projections as one matrix, rows in the order the
+        fused layer kernel reads them: [dt_nu (H) | dt_theta (H) | b_coef (H r) |
+        b_dir (H r Nh) | c_coef (H r) | c_read (2 H r Nh)]."""
+        ws = [self.dt_nu_proj.weight, self.dt_theta_proj.weight]
         if self.rank > 0:
-            s_b = self.b_coef(x).view(Bsz, T, H, self.rank)
-            b_t = self.b_dir(x).view(Bsz, T, H, self.rank, Nh)
-            Bu_re = Bu_re + torch.einsum("bthr,bthrn->bthn", s_b, b_t)
-        if self.input_gain == "gamma":
-            gain = torch.sqrt((1.0 - nu * nu).clamp_min(1e-6))
-            Bu_re, Bu_im = Bu_re * gain, Bu_im * gain
-        elif self.input_gain == "mamba":
-            Bu_re, Bu_im = Bu_re * dnu, Bu_im * dnu
-        elif self.input_gain == "zoh":
-            lm1_re = torch.expm1(-dnu * a) * cos - 2.0 * torch.sin(0.5 * theta).square()
-            lm1_im = nu * sin
-            den = (a * a + base * base).clamp_min(1e-8)
-            g_re = (base * lm1_im - a * lm1_re) / den
-            g_im = -(a * lm1_im + base * lm1_re) / den
-            Bu_re, Bu_im = g_re * Bu_re - g_im * Bu_im, g_re * Bu_im + g_im * Bu_re
-        return lam_re, lam_im, Bu_re.reshape(Bsz, T, N), Bu_im.reshape(Bsz, T, N)
+            ws += [self.b_coef.weight, self.b_dir.weight, self.c_coef.weight, self.c_read.weight]
+        W = torch.cat(ws, 0)
+        b = torch.cat([self.dt_nu_proj.bias, self.dt_theta_proj.bias,
+                       self.dt_nu_proj.bias.new_zeros(W.shape[0] - 2 * self.n_heads)])
+        return W, b
 
     def forward(self, x: torch.Tensor, rate_scale: float | None = None) -> torch.Tensor:
-        from .mimo import fused_selective_lru_mimo
+        """Float32 input runs in float32; bfloat16 input (or float32 input under CUDA bf16
+        autocast) runs the projections and the kernel's operand reads in bfloat16 with
+        float32 state, accumulation and output."""
+        from .mimo import mimo_layer
 
-        x = x.float()
-        Bsz, T, Fdim = x.shape
-        H, Nh = self.n_heads, self.n_head
-        delta_nu = F.softplus(self.dt_nu_proj(x))
-        rs = self.rate_scale if rate_scale is None else float(rate_scale)
-        if rs != 1.0:
-            delta_nu = delta_nu * rs
-        delta_theta = self.dt_theta_proj(x)
-        lam_re, lam_im, Bu_re, Bu_im = self._poles_and_drive(x, delta_nu, delta_theta)
-        y, h_re, h_im = fused_selective_lru_mimo(
-            lam_re, lam_im, Bu_re, Bu_im, self.C[..., 0], self.C[..., 1], x, self.D,
-            H, Nh, self.f_head,
-        )
-        if self.envelope_readout or self.rank > 0:
-            hr = h_re.view(Bsz, T, H, Nh)
-            hi = h_im.view(Bsz, T, H, Nh)
-            if self.envelope_readout:
-                power = hr * hr + hi * hi
-                y = y + torch.einsum("hfn,bthn->bthf", self.env_gain, power).reshape(Bsz, T, Fdim)
-            if self.rank > 0:
-                s_c = self.c_coef(x).view(Bsz, T, H, self.rank)
-                cr = self.c_read(x).view(Bsz, T, H, self.rank, 2 * Nh)
-                read = (torch.einsum("bthrn,bthn->bthr", cr[..., :Nh], hr)
-                        - torch.einsum("bthrn,bthn->bthr", cr[..., Nh:], hi))
-                c_out = self.c_out.view(H, self.rank, self.f_head)
-                y = y + torch.einsum("bthr,hrf->bthf", s_c * read, c_out).reshape(Bsz, T, Fdim)
-        return y
+        bf16 = x.dtype == torch.bfloat16 or (
+            x.is_cuda and torch.is_autocast_enabled("cuda")
+            and torch.get_autocast_dtype("cuda") == torch.bfloat16)
+        W, b = self._projection()
+        with torch.autocast("cuda", enabled=False):
+            if bf16:
+                x = x.to(torch.bfloat16)
+                proj = F.linear(x, W.to(torch.bfloat16), b.to(torch.bfloat16))
+            else:
+                x = x.float()
+                proj = F.linear(x, W, b)
+            rs = self.rate_scale if rate_scale is None else float(rate_scale)
+            return mimo_layer(
+                x, proj, self.A_log, self.omega, self.detune_gain if self.mode_detune else None,
+                self.B, self.C, self.D, self.c_out if self.rank > 0 else None,
+                self.env_gain if self.envelope_readout else None, self.n_heads, self.n_head,
+                self.f_head, self.rank, self.input_gain, rs)

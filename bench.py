@@ -68,6 +68,9 @@ def parse_args():
     ap.add_argument("--batch", type=int, default=16, help="generator: utterances per GPU")
     ap.add_argument("--micro-batch", type=int, default=4, help="inference: utterances per forward")
     ap.add_argument("--chunk", type=int, default=None, help="checkpoint interval of the scan")
+    ap.add_argument("--slru-complex", action="store_true",
+                    help="slru: the complex scan with the gamma gain (the generator's time scans)")
+    ap.add_argument("--sequences", type=int, default=None, help="slru: sequences (default 404)")
     ap.add_argument("--cpu-sample-frac", type=float, default=None)
     ap.add_argument("--ref-sample-frac", type=float, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -298,18 +301,24 @@ SLRU_S, SLRU_L, SLRU_C, SLRU_N = 404, 321, 256, 16
 
 
 class SlruPass:
-    """The real selective-LRU scan (Mamba gain) over S x L x C channels x N modes with
-    resident buffers and prebuilt argument structs for semx_selective_lru_fwd / _bwd."""
+    """The selective-LRU scan over S x L x C channels x N modes with resident buffers and
+    prebuilt argument structs for semx_selective_lru_fwd / _bwd: the real scan with the
+    Mamba gain, or (`complex_`) the generator's complex scan with the gamma gain
+    (delta_theta ~ N(0, 0.1^2), omega ~ N(0, 1), B_im, C_im ~ N(0, 1/16))."""
 
     kernels = ("slru_fwd_kernel", "slru_bwd_kernel")
 
-    def __init__(self, S, L, seed, device, chunk):
+    def __init__(self, S, L, seed, device, chunk, complex_=False):
         from semambaxlinoss_b200 import _lib
 
         C, N = SLRU_C, SLRU_N
         self.lib, self._lib = _lib.load(), _lib
-        self.fwd_bytes_per_unit = 4 * (3 * C + 2 * N)
-        self.bwd_bytes_per_unit = 4 * (5 * C + 4 * N)
+        if complex_:  # x, dt, dth, B, C (re, im) in, y out / + dy in, 3 channel + 4 mode grads out
+            self.fwd_bytes_per_unit = 4 * (4 * C + 4 * N)
+            self.bwd_bytes_per_unit = 4 * (7 * C + 8 * N)
+        else:
+            self.fwd_bytes_per_unit = 4 * (3 * C + 2 * N)
+            self.bwd_bytes_per_unit = 4 * (5 * C + 4 * N)
         g = torch.Generator(device=device).manual_seed(seed)
         f = torch.float32
         self.x = torch.randn(S, L, C, generator=g, device=device)
@@ -324,12 +333,27 @@ class SlruPass:
         self.dB, self.dC = torch.empty_like(self.B), torch.empty_like(self.B)
         self.da, self.dD = torch.empty(C, N, device=device), torch.empty(C, device=device)
         a = _lib.new_args(_lib.SemxSelectiveLruArgs)
-        a.real, a.input_gain, a.chunk = 1, _lib.GAIN_CODES["mamba"], chunk
+        a.real, a.input_gain, a.chunk = int(not complex_), _lib.GAIN_CODES["gamma" if complex_ else "mamba"], chunk
         a.S, a.L, a.C, a.N = S, L, C, N
-        for name, t in (("delta_nu", self.dnu), ("a", self.a), ("B_re", self.B), ("C_re", self.Cr),
-                        ("x", self.x), ("D", self.D), ("y", self.y), ("dy", self.dy),
-                        ("d_delta_nu", self.d_dnu), ("dx", self.dx), ("dB_re", self.dB),
-                        ("dC_re", self.dC), ("da", self.da), ("dD", self.dD)):
+        named = [("delta_nu", self.dnu), ("a", self.a), ("B_re", self.B), ("C_re", self.Cr),
+                 ("x", self.x), ("D", self.D), ("y", self.y), ("dy", self.dy),
+                 ("d_delta_nu", self.d_dnu), ("dx", self.dx), ("dB_re", self.dB),
+                 ("dC_re", self.dC), ("da", self.da), ("dD", self.dD)]
+        extra_in, extra_out = [], []
+        if complex_:
+            self.dth = torch.randn(S, L, C, generator=g, device=device) * 0.1
+            self.om = torch.randn(C, N, generator=g, device=device)
+            self.Bi = torch.randn(S, L, N, generator=g, device=device) * 0.25
+            self.Ci = torch.randn(S, L, N, generator=g, device=device) * 0.25
+            self.d_dth = torch.empty_like(self.y)
+            self.dBi, self.dCi = torch.empty_like(self.B), torch.empty_like(self.B)
+            self.dom = torch.empty(C, N, device=device)
+            named += [("delta_theta", self.dth), ("omega", self.om), ("B_im", self.Bi), ("C_im", self.Ci),
+                      ("d_delta_theta", self.d_dth), ("dB_im", self.dBi), ("dC_im", self.dCi),
+                      ("domega", self.dom)]
+            extra_in = [self.dth, self.Bi, self.Ci]
+            extra_out = [self.d_dth, self.dBi, self.dCi, self.dom]
+        for name, t in named:
             setattr(a, name, t.data_ptr())
         self.ckpt = _lib.empty_f32(self.lib.semx_selective_lru_ckpt_bytes(ctypes.byref(a)), device)
         a.ckpt = self.ckpt.data_ptr()
@@ -338,8 +362,8 @@ class SlruPass:
         self.args = a
         self.units = S * L
         self.S, self.L = S, L
-        self.inputs = [self.x, self.dnu, self.B, self.Cr, self.dy]
-        self.outputs = [self.y, self.d_dnu, self.dx, self.dB, self.dC, self.da, self.dD]
+        self.inputs = [self.x, self.dnu, self.B, self.Cr, self.dy] + extra_in
+        self.outputs = [self.y, self.d_dnu, self.dx, self.dB, self.dC, self.da, self.dD] + extra_out
 
     def fwd(self, sh):
         self._lib.check("semx_selective_lru_fwd", self.lib.semx_selective_lru_fwd(ctypes.byref(self.args), sh))
@@ -348,17 +372,24 @@ class SlruPass:
         self._lib.check("semx_selective_lru_bwd", self.lib.semx_selective_lru_bwd(ctypes.byref(self.args), sh))
 
 
-def _slru_cpu_sample(frac, seed=0):
+def _slru_cpu_sample(frac, seed=0, complex_=False, S=None):
     C, N = SLRU_C, SLRU_N
+    S = S or SLRU_S
     g = torch.Generator().manual_seed(seed)
-    s = max(1, int(round(SLRU_S * frac)))
+    s = max(1, int(round(S * frac)))
     L = SLRU_L
     t = {"dnu": torch.nn.functional.softplus(torch.randn(s, L, C, generator=g) * 0.5 - 2.0),
          "a": torch.rand(C, N, generator=g) * 15.0 + 1.0,
          "B": torch.randn(s, L, N, generator=g) * 0.25, "C": torch.randn(s, L, N, generator=g) * 0.25,
          "x": torch.randn(s, L, C, generator=g), "D": torch.randn(C, generator=g)}
+    per_unit = 4 * (8 * C + 6 * N)
+    if complex_:
+        t.update(dth=torch.randn(s, L, C, generator=g) * 0.1, om=torch.randn(C, N, generator=g),
+                 Bi=torch.randn(s, L, N, generator=g) * 0.25, Ci=torch.randn(s, L, N, generator=g) * 0.25)
+        per_unit = 4 * (11 * C + 12 * N)
     gy = torch.randn(s, L, C, generator=g)
-    return {"t": t, "gy": gy, "bytes": s * L * 4 * (8 * C + 6 * N), "desc": f"{s}x{L}", "frac": s / SLRU_S}
+    return {"t": t, "gy": gy, "bytes": s * L * per_unit, "desc": f"{s}x{L}", "frac": s / S,
+            "complex": complex_}
 
 
 def _slru_cpu_step(sample):
@@ -367,7 +398,11 @@ def _slru_cpu_step(sample):
     from oracle import selective_lru as oslru
 
     t = {k: v.clone().requires_grad_(True) for k, v in sample["t"].items()}
-    y = oslru.selective_lru_real_op(t["dnu"], t["a"], t["B"], t["C"], t["x"], t["D"], "mamba")
+    if sample["complex"]:
+        y = oslru.selective_lru_op(t["dnu"], t["dth"], t["a"], t["om"], t["B"], t["Bi"], t["C"],
+                                   t["Ci"], t["x"], t["D"], input_gain="gamma")
+    else:
+        y = oslru.selective_lru_real_op(t["dnu"], t["a"], t["B"], t["C"], t["x"], t["D"], "mamba")
     (y * sample["gy"]).sum().backward()
 
 
@@ -423,47 +458,54 @@ class MimoPass:
 
 
 class MimoKernelPass:
-    """The fused MIMO scan + readout kernels alone (semx_mimo_fwd / _bwd) on resident
-    poles, drive, readout and input, for the kernel roofline of the MIMO workload."""
+    """The fused MIMO layer kernels alone (semx_mimo_layer_fwd / _bwd) on resident bf16
+    token operands (x and the projection rows), for the kernel roofline of the MIMO
+    workload. Bytes per token: fwd x + proj (bf16) in, y (fp32) out = 4768; bwd x, proj
+    (bf16), dy (fp32) in, dx (fp32), dproj (bf16) out = 9024."""
 
-    kernels = ("mimo_fwd_kernel", "mimo_bwd_kernel")
+    kernels = ("mimo_layer_fwd_kernel", "mimo_layer_bwd_kernel")
 
-    def __init__(self, S, L, seed, device):
+    def __init__(self, layer, S, L, seed, device):
         from semambaxlinoss_b200 import _lib
 
-        H, Nh, Fh = MIMO_HEADS, MIMO_STATE // MIMO_HEADS, MIMO_F // MIMO_HEADS
-        N, Fd = MIMO_STATE, MIMO_F
+        H, Nh, Fh, R = MIMO_HEADS, MIMO_STATE // MIMO_HEADS, MIMO_F // MIMO_HEADS, MIMO_RANK
         self.lib, self._lib = _lib.load(), _lib
-        self.fwd_bytes_per_unit = 4 * (4 * N + Fd) + 4 * (Fd + 2 * N)       # lam, Bu, x in; y, h out
-        self.bwd_bytes_per_unit = 4 * (4 * N + 2 * Fd) + 4 * (4 * N + Fd)   # lam, h, dy, x in; dlam, dBu, dx out
         g = torch.Generator(device=device).manual_seed(seed)
-        r = lambda *s: torch.randn(*s, generator=g, device=device)  # noqa: E731
-        nu = torch.rand(S, L, N, generator=g, device=device) * 0.98
-        th = r(S, L, N)
-        self.t = {"lam_re": nu * torch.cos(th), "lam_im": nu * torch.sin(th), "Bu_re": r(S, L, N),
-                  "Bu_im": r(S, L, N), "C_re": r(H, Fh, Nh) * 0.25, "C_im": r(H, Fh, Nh) * 0.25,
-                  "x": r(S, L, Fd), "D": r(Fd), "dy": r(S, L, Fd)}
-        for k in ("y", "dx"):
-            self.t[k] = torch.empty(S, L, Fd, device=device)
-        for k in ("h_re", "h_im", "dlam_re", "dlam_im", "dBu_re", "dBu_im"):
-            self.t[k] = torch.empty(S, L, N, device=device)
-        self.t["dC_re"], self.t["dC_im"] = torch.empty(H, Fh, Nh, device=device), torch.empty(H, Fh, Nh, device=device)
-        self.t["dD"] = torch.empty(Fd, device=device)
-        a = _lib.new_args(_lib.SemxMimoArgs)
+        bf = torch.bfloat16
+        self.x = (torch.randn(S, L, MIMO_F, generator=g, device=device) * 0.5).to(bf)
+        with torch.no_grad():
+            W, b = layer._projection()
+            self.proj = torch.nn.functional.linear(self.x, W.to(bf), b.to(bf))
+        P = self.proj.shape[-1]
+        self.fwd_bytes_per_unit = 2 * MIMO_F + 2 * P + 4 * MIMO_F
+        self.bwd_bytes_per_unit = (2 * MIMO_F + 2 * P + 4 * MIMO_F) + (4 * MIMO_F + 2 * P)
+        self.y = torch.empty(S, L, MIMO_F, device=device)
+        self.dy = torch.randn(S, L, MIMO_F, generator=g, device=device)
+        self.dx = torch.empty_like(self.y)
+        self.dproj = torch.empty_like(self.proj)
+        self.params = [t.detach().float().contiguous() for t in (
+            layer.A_log, layer.omega, layer.B, layer.C, layer.D, layer.c_out)]
+        self.grads = [torch.empty_like(t) for t in self.params]
+        a = _lib.new_args(_lib.SemxMimoLayerArgs)
+        a.input_gain, a.rank, a.rate_scale, a.bf16 = _lib.GAIN_CODES["gamma"], R, 1.0, 1
         a.S, a.L, a.H, a.Nh, a.Fh = S, L, H, Nh, Fh
-        for k, v in self.t.items():
-            setattr(a, k, v.data_ptr())
-        self.ws = _lib.empty_f32(self.lib.semx_mimo_workspace_bytes(ctypes.byref(a)), device)
+        a.x, a.proj, a.y, a.dy, a.dx, a.dproj = [t.data_ptr() for t in (
+            self.x, self.proj, self.y, self.dy, self.dx, self.dproj)]
+        a.A_log, a.omega, a.B, a.C, a.D, a.c_out = [t.data_ptr() for t in self.params]
+        a.dA_log, a.domega, a.dB, a.dC, a.dD, a.dc_out = [t.data_ptr() for t in self.grads]
+        self.ckpt = _lib.empty_f32(self.lib.semx_mimo_layer_ckpt_bytes(ctypes.byref(a)), device)
+        a.ckpt = self.ckpt.data_ptr()
+        self.ws = _lib.empty_f32(self.lib.semx_mimo_layer_workspace_bytes(ctypes.byref(a)), device)
         a.workspace = self.ws.data_ptr()
         self.args = a
         self.units = S * L
         self.S, self.L = S, L
 
     def fwd(self, sh):
-        self._lib.check("semx_mimo_fwd", self.lib.semx_mimo_fwd(ctypes.byref(self.args), sh))
+        self._lib.check("semx_mimo_layer_fwd", self.lib.semx_mimo_layer_fwd(ctypes.byref(self.args), sh))
 
     def bwd(self, sh):
-        self._lib.check("semx_mimo_bwd", self.lib.semx_mimo_bwd(ctypes.byref(self.args), sh))
+        self._lib.check("semx_mimo_layer_bwd", self.lib.semx_mimo_layer_bwd(ctypes.byref(self.args), sh))
 
 
 def _mimo_cpu_sample(frac, seed=0):
@@ -532,12 +574,32 @@ WORKLOADS = {
 }
 
 
-def _make_passes(name, rank, device, chunk):
+def workload_spec(args):
+    """The workload table entry, adapted to the SISO variant options."""
+    import functools
+
+    spec = dict(WORKLOADS[args.workload])
+    if args.workload == "slru" and (args.slru_complex or args.sequences):
+        S = args.sequences or SLRU_S
+        kind = "complex selective-LRU scan (gamma gain)" if args.slru_complex else spec["describe"].split(" fwd")[0]
+        spec["metric"] = (f"Selective-LRU {'complex' if args.slru_complex else 'real'} diagonal scan fwd+bwd, "
+                          f"algorithmic HBM GB/s ({S}x321, C=256, N=16)")
+        spec["describe"] = f"{kind} fwd+bwd, {S} sequences x 321 steps, C=256 channels, N=16 modes"
+        if args.slru_complex:
+            spec["data"] += ", dth ~ N(0, 0.01), omega ~ N(0,1)"
+        spec["cpu_sample"] = functools.partial(_slru_cpu_sample, complex_=args.slru_complex, S=S)
+        spec["cpu_frac"] = 8.0 / S
+        spec["ref_frac"] = 4.0 / S
+    return spec
+
+
+def _make_passes(name, rank, device, chunk, args):
     if name == "linoss":
         return [LinossPass(S, L, seed=1000 * rank + i, device=device, chunk=chunk)
                 for i, (_, S, L) in enumerate(LIN_PASSES)]
     if name == "slru":
-        return [SlruPass(SLRU_S, SLRU_L, seed=1000 * rank, device=device, chunk=chunk)]
+        return [SlruPass(args.sequences or SLRU_S, SLRU_L, seed=1000 * rank, device=device, chunk=chunk,
+                         complex_=args.slru_complex)]
     layer = _mimo_layer(device, seed=7)
     return [MimoPass(layer, S, L, seed=1000 * rank + i, device=device)
             for i, (_, S, L) in enumerate(MIMO_PASSES)]
@@ -563,12 +625,12 @@ def _time_passes(passes, steps, stream):
 def run_scan(args, rank, local_rank, world):
     from semambaxlinoss_b200 import _lib
 
-    spec = WORKLOADS[args.workload]
+    spec = workload_spec(args)
     chunk = args.chunk or spec["chunk"]
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
     _init_dist(world, device)
-    passes = _make_passes(args.workload, rank, device, chunk)
+    passes = _make_passes(args.workload, rank, device, chunk, args)
     stream = torch.cuda.current_stream(device)
     sh = stream.cuda_stream
     step_bytes = sum(p.units * (p.fwd_bytes_per_unit + p.bwd_bytes_per_unit) for p in passes)
@@ -606,7 +668,8 @@ def run_scan(args, rank, local_rank, world):
     # Kernel roofline: for the MIMO layer, the fused scan + readout kernels timed alone.
     kpasses = per_pass
     if args.workload == "mimo":
-        kp = [MimoKernelPass(S, L, seed=5000 + i, device=device) for i, (_, S, L) in enumerate(MIMO_PASSES)]
+        kp = [MimoKernelPass(passes[0].layer, S, L, seed=5000 + i, device=device)
+              for i, (_, S, L) in enumerate(MIMO_PASSES)]
         for _ in range(3):
             for p in kp:
                 p.fwd(sh)
@@ -684,9 +747,10 @@ def run_scan(args, rank, local_rank, world):
     if args.workload == "mimo":
         out["layer_ms"] = {"fwd": round(sum(f for _, f, _ in per_pass), 4),
                            "bwd": round(sum(b for _, _, b in per_pass), 4)}
-        out["gpu_launches_note"] = "libsemx kernels only; the layer's projections run as torch/cuBLAS kernels"
+        out["gpu_launches_note"] = ("libsemx kernels only; the layer's token projections (one GEMM "
+                                    "forward, two backward) run as cuBLAS kernels")
     if world == 1 and not args.no_cpu_baseline:
-        out["cpu_baseline"] = cpu_baseline(args.workload, args.cpu_sample_frac or spec["cpu_frac"], repeats=3)
+        out["cpu_baseline"] = cpu_baseline(spec, args.cpu_sample_frac or spec["cpu_frac"], repeats=3)
     print(json.dumps(out), flush=True)
 
 
@@ -729,8 +793,7 @@ def run_scan_e2e(passes, args, device, stream, step_bytes, world):
 
 
 # ----------------------------------------------------------------------------- CPU legs
-def cpu_baseline(workload, frac, repeats=3):
-    spec = WORKLOADS[workload]
+def cpu_baseline(spec, frac, repeats=3):
     torch.set_num_threads(os.cpu_count())
     sample = spec["cpu_sample"](frac)
     spec["cpu_step"](sample)
@@ -754,7 +817,7 @@ def run_reference(args, rank):
         print(json.dumps({"impl": "reference", "unavailable": "the reference generator needs the "
                           "third-party mamba_ssm package, which the reference does not ship"}))
         return
-    spec = WORKLOADS[args.workload]
+    spec = workload_spec(args)
     torch.set_num_threads(os.cpu_count())
     frac = args.ref_sample_frac
     if frac is None:

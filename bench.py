@@ -99,13 +99,16 @@ def load_peaks():
     return 6650.0, "fallback"
 
 
-def profiled_traffic(kernel: str):
-    """Per-launch DRAM bytes of `kernel` recorded by an ncu capture in profiles/*.md
-    (a line `traffic_bytes_per_launch[<kernel>]: <int>`), or None."""
+def profiled_traffic(kernel: str, workload: str, units: int):
+    """DRAM bytes of one launch of `kernel` over `units` (sequence, step) units, from an
+    ncu capture recorded in profiles/*.md as `traffic_bytes_per_launch[<kernel>|<workload>|
+    <units>]: <bytes>`; a capture of a different size is scaled by the units processed
+    (the traffic of these scans grows in proportion). None if no capture is recorded."""
+    pat = re.compile(rf"traffic_bytes_per_launch\[{re.escape(kernel)}\|{re.escape(workload)}\|(\d+)\]:\s*(\d+)")
     for f in sorted((ROOT / "profiles").glob("*.md")):
-        m = re.search(rf"traffic_bytes_per_launch\[{re.escape(kernel)}\]:\s*([0-9.e+]+)", f.read_text())
+        m = pat.search(f.read_text())
         if m:
-            return float(m.group(1))
+            return float(m.group(2)) * units / int(m.group(1))
     return None
 
 
@@ -697,7 +700,8 @@ def run_scan(args, rank, local_rank, world):
     kf, kb = kpasses[0][0].kernels
     dom, dom_bytes, dom_ms = (kb, bwd_bytes, bwd_ms) if bwd_ms >= fwd_ms else (kf, fwd_bytes, fwd_ms)
     dom_gbs = dom_bytes / (dom_ms * 1e-3) / 1e9
-    traffic = profiled_traffic(dom)
+    tag = args.workload if args.workload != "slru" else ("slru complex" if args.slru_complex else "slru real")
+    traffic = profiled_traffic(dom, tag, kpasses[0][0].units)
     out = {
         "metric": spec["metric"],
         "value": round(value, 2),
@@ -731,7 +735,8 @@ def run_scan(args, rank, local_rank, world):
             "algorithmic_bytes_first_launch": kpasses[0][0].units * (
                 kpasses[0][0].bwd_bytes_per_unit if dom == kb else kpasses[0][0].fwd_bytes_per_unit),
             "note": "achieved = algorithmic bytes / CUDA-event time of the entry point (includes its "
-                    "small reduction launches); traffic = ncu DRAM bytes of one launch of the first pass",
+                    "small reduction launches); traffic = ncu DRAM bytes of one launch of the first pass "
+                    "(profiles/*.md; scaled by units when the capture was a smaller case)",
         },
         "kernels": {
             f"{kf}": {"ms": round(fwd_ms, 4), "GB/s": round(fwd_bytes / (fwd_ms * 1e-3) / 1e9, 1),

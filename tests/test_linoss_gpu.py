@@ -3,7 +3,7 @@
 Mirrors the reference's tests/test_linoss.py (parity of forward and all gradients at the
 reference's shapes and tolerances, causality, batch independence, zero input) and adds
 chunk-boundary edge cases, every constraint branch, determinism, and full-size
-property checks at the config-1 shape (B*F = 404 sequences x 321 steps, P = 256).
+property checks at the 404-sequence x 321-step, P = 256 shape.
 """
 from __future__ import annotations
 
@@ -215,8 +215,8 @@ def test_empty_and_errors():
         linoss_scan(A, A, A, A, F, F, chunk=12)
 
 
-def test_full_size_config1_properties():
-    """Config-1 shapes (time pass 404 x 321, frequency pass 1284 x 101, P = 256):
+def test_full_size_linoss_workload_properties():
+    """The LinOSS-IMEX workload shapes (time pass 404 x 321, frequency pass 1284 x 101, P = 256):
     a sequence slice agrees with the float64 oracle, the forward is linear in Bu, and
     forward + backward are bitwise deterministic."""
     from semambaxlinoss_b200.linoss import linoss_scan_fused

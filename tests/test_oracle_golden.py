@@ -108,7 +108,7 @@ def test_selective_recurrence_matches_reference(golden):
 
 
 def test_real_special_case_equals_complex_op():
-    """The real (config-0) form is the complex op with omega = dtheta = B_im = C_im = 0."""
+    """The real form is the complex op with omega = dtheta = B_im = C_im = 0."""
     g = torch.Generator().manual_seed(3)
     B, T, C, N = 2, 11, 5, 4
     dnu = torch.nn.functional.softplus(torch.randn(B, T, C, generator=g, dtype=torch.float64))

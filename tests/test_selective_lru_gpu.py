@@ -4,9 +4,9 @@ reference's materialised path).
 Mirrors the reference's tests/test_selective_lru.py (direct fused-op parity of forward and
 all input gradients at its (B, T, C, N, chunk) shapes, module parity, causality, batch
 independence, zero input) for every input gain and option, and adds: the real
-specialisation (config 0), N not a multiple of 4, N = 32, channel counts that need one
+specialisation, N not a multiple of 4, N = 32, channel counts that need one
 and several thread-block clusters, final-state gradients, determinism, and full-size
-config-0 property checks.
+property checks on the 404 x 321, C = 256, N = 16 real scan.
 """
 from __future__ import annotations
 
@@ -210,8 +210,8 @@ def test_module_properties(gain):
         assert torch.equal(a_, b_), "backward is not bitwise deterministic"
 
 
-def test_full_size_config0_properties():
-    """Config 0 (404 x 321, C = 256, N = 16, real, mamba gain): a sequence slice agrees
+def test_full_size_real_scan_properties():
+    """The real scan at 404 x 321, C = 256, N = 16 with the mamba gain: a sequence slice agrees
     with the float64 oracle and forward + backward are bitwise deterministic."""
     from semambaxlinoss_b200.selective_lru import fused_selective_lru_real
 

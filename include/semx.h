@@ -374,6 +374,54 @@ typedef struct SemxMimoLayerArgs {
   void* workspace; /* semx_mimo_layer_workspace_bytes(), backward only */
 } SemxMimoLayerArgs;
 
+/* ------------------------------------------------------------------------------------
+ * Mixer surround, channels-last (replaces the depthwise Conv1d + SiLU and the SiLU gate
+ * of MambaStyleMixer.forward, models/mixer.py:82-99). `xz` is the in_proj output with
+ * rows of `ld` elements: u = columns [0, C), z = columns [C, 2C).
+ *   conv_silu: v[s,t,c] = silu(b[c] + sum_k w[c,k] u[s, t - left + k, c]), u = 0 outside
+ *              [0, L) (left = K-1: causal; (K-1)/2: centred, as the reference's padding).
+ *              Backward writes du into columns [0, C) of dxz and reduces dw, db over
+ *              (S, L) in a fixed order (workspace: semx_conv_silu_workspace_bytes()).
+ *   gate_silu: o = y * silu(z); backward writes dy and dz (into columns [C, 2C) of dxz).
+ * xz, dxz, o, dout are bf16 when `bf16` is set, else fp32; v, dv, y, dy are fp32.
+ * ---------------------------------------------------------------------------------- */
+typedef struct SemxConvSiluArgs {
+  uint32_t struct_size;
+  int32_t K;    /* kernel width, 1..8                          */
+  int32_t left; /* taps before t                               */
+  int32_t bf16; /* xz / dxz dtype                              */
+  int64_t S, L, C, ld;
+  const void* xz;
+  const float* w;  /* (C, K)          */
+  const float* b;  /* (C), may be NULL */
+  float* v;        /* (S, L, C)       */
+  const float* dv; /* (S, L, C)       */
+  void* dxz;
+  float* dw; /* (C, K) */
+  float* db; /* (C), may be NULL */
+  void* workspace;
+} SemxConvSiluArgs;
+
+typedef struct SemxGateSiluArgs {
+  uint32_t struct_size;
+  int32_t bf16; /* xz, o, dout, dxz dtype */
+  int64_t n, C, ld; /* n = S*L rows */
+  const float* y;   /* (n, C) */
+  const void* xz;
+  void* o;          /* (n, C) */
+  const void* dout; /* (n, C) */
+  float* dy;        /* (n, C) */
+  void* dxz;
+} SemxGateSiluArgs;
+
+size_t semx_conv_silu_args_size(void);
+size_t semx_conv_silu_workspace_bytes(const SemxConvSiluArgs* args);
+int semx_conv_silu_fwd(const SemxConvSiluArgs* args, semx_stream_t stream);
+int semx_conv_silu_bwd(const SemxConvSiluArgs* args, semx_stream_t stream);
+size_t semx_gate_silu_args_size(void);
+int semx_gate_silu_fwd(const SemxGateSiluArgs* args, semx_stream_t stream);
+int semx_gate_silu_bwd(const SemxGateSiluArgs* args, semx_stream_t stream);
+
 size_t semx_mimo_layer_args_size(void);
 size_t semx_mimo_layer_ckpt_bytes(const SemxMimoLayerArgs* args);
 size_t semx_mimo_layer_workspace_bytes(const SemxMimoLayerArgs* args);

@@ -152,6 +152,29 @@ class SemxMimoLayerArgs(ctypes.Structure):
     )]
 
 
+class SemxConvSiluArgs(ctypes.Structure):
+    _fields_ = [
+        ("struct_size", ctypes.c_uint32),
+        ("K", ctypes.c_int32),
+        ("left", ctypes.c_int32),
+        ("bf16", ctypes.c_int32),
+        ("S", ctypes.c_int64),
+        ("L", ctypes.c_int64),
+        ("C", ctypes.c_int64),
+        ("ld", ctypes.c_int64),
+    ] + [(name, ctypes.c_void_p) for name in ("xz", "w", "b", "v", "dv", "dxz", "dw", "db", "workspace")]
+
+
+class SemxGateSiluArgs(ctypes.Structure):
+    _fields_ = [
+        ("struct_size", ctypes.c_uint32),
+        ("bf16", ctypes.c_int32),
+        ("n", ctypes.c_int64),
+        ("C", ctypes.c_int64),
+        ("ld", ctypes.c_int64),
+    ] + [(name, ctypes.c_void_p) for name in ("y", "xz", "o", "dout", "dy", "dxz")]
+
+
 # (python struct, C size query) for every argument struct in semx.h.
 STRUCTS = {
     "SemxLinossArgs": (SemxLinossArgs, "semx_linoss_args_size"),
@@ -159,6 +182,8 @@ STRUCTS = {
     "SemxComplexScanArgs": (SemxComplexScanArgs, "semx_complex_scan_args_size"),
     "SemxMimoArgs": (SemxMimoArgs, "semx_mimo_args_size"),
     "SemxMimoLayerArgs": (SemxMimoLayerArgs, "semx_mimo_layer_args_size"),
+    "SemxConvSiluArgs": (SemxConvSiluArgs, "semx_conv_silu_args_size"),
+    "SemxGateSiluArgs": (SemxGateSiluArgs, "semx_gate_silu_args_size"),
 }
 
 # Every symbol semx.h declares, with its ctypes signature.
@@ -193,6 +218,13 @@ _SIGNATURES = {
     "semx_mimo_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(SemxMimoArgs)]),
     "semx_mimo_fwd": (ctypes.c_int, [ctypes.POINTER(SemxMimoArgs), ctypes.c_void_p]),
     "semx_mimo_bwd": (ctypes.c_int, [ctypes.POINTER(SemxMimoArgs), ctypes.c_void_p]),
+    "semx_conv_silu_args_size": (ctypes.c_size_t, []),
+    "semx_conv_silu_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(SemxConvSiluArgs)]),
+    "semx_conv_silu_fwd": (ctypes.c_int, [ctypes.POINTER(SemxConvSiluArgs), ctypes.c_void_p]),
+    "semx_conv_silu_bwd": (ctypes.c_int, [ctypes.POINTER(SemxConvSiluArgs), ctypes.c_void_p]),
+    "semx_gate_silu_args_size": (ctypes.c_size_t, []),
+    "semx_gate_silu_fwd": (ctypes.c_int, [ctypes.POINTER(SemxGateSiluArgs), ctypes.c_void_p]),
+    "semx_gate_silu_bwd": (ctypes.c_int, [ctypes.POINTER(SemxGateSiluArgs), ctypes.c_void_p]),
     "semx_mimo_layer_args_size": (ctypes.c_size_t, []),
     "semx_mimo_layer_ckpt_bytes": (ctypes.c_size_t, [ctypes.POINTER(SemxMimoLayerArgs)]),
     "semx_mimo_layer_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(SemxMimoLayerArgs)]),

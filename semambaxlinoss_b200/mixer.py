@@ -5,14 +5,108 @@
     y = ssm(u) * SiLU(z) -> out_proj (expand * C -> C)
 
 Same constructor, parameter names and forward contract as the reference. The projections
-and the depthwise convolution are cuDNN / cuBLAS calls; the scan layer (``ssm``) is one
-of this package's CUDA layers.
+are cuBLAS GEMMs; the convolution + SiLU and the SiLU gate are this package's
+channels-last kernels (``semx_conv_silu``, ``semx_gate_silu``), which read u and z in
+place from the in_proj output, so the transposes, padding and split copies of the
+reference formulation never materialise; the scan layer (``ssm``) is one of this
+package's CUDA layers.
 """
 from __future__ import annotations
 
 import torch
 import torch.nn as nn
-import torch.nn.functional as F
+
+from . import _lib
+
+
+class _DxzLink:
+    """Gradient buffer of the in_proj output shared by the gate and the convolution of one
+    forward call: the gate's backward (which always runs first, since the convolution's
+    output gradient flows back through the scan from the gate) writes dz into columns
+    [C, 2C); the convolution's backward writes du into columns [0, C) and returns it."""
+
+    __slots__ = ("dxz",)
+
+    def __init__(self):
+        self.dxz = None
+
+
+def _check_xz(xz):
+    if not xz.is_cuda:
+        raise RuntimeError("MambaStyleMixer requires CUDA tensors.")
+    if xz.dtype not in (torch.float32, torch.bfloat16):
+        raise ValueError(f"MambaStyleMixer: unsupported dtype {xz.dtype}")
+
+
+class _ConvSiLU(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, xz, weight, bias, C, K, left, link):
+        S, L, _ = xz.shape
+        w = weight.detach().reshape(C, K).float().contiguous()
+        b = None if bias is None else bias.detach().float().contiguous()
+        v = torch.empty((S, L, C), dtype=torch.float32, device=xz.device)
+        a = _lib.new_args(_lib.SemxConvSiluArgs)
+        a.K, a.left, a.bf16 = K, left, int(xz.dtype == torch.bfloat16)
+        a.S, a.L, a.C, a.ld = S, L, C, xz.shape[2]
+        a.xz, a.w, a.b, a.v = xz.data_ptr(), w.data_ptr(), _lib.ptr(b), v.data_ptr()
+        _lib.call("semx_conv_silu_fwd", a, xz.device)
+        ctx.save_for_backward(xz, w, b if b is not None else w.new_empty(0))
+        ctx.cfg = (C, K, left, bias is not None, weight.shape, link)
+        return v
+
+    @staticmethod
+    def backward(ctx, dv):
+        xz, w, b = ctx.saved_tensors
+        C, K, left, has_bias, wshape, link = ctx.cfg
+        S, L, ld = xz.shape
+        dxz = link.dxz
+        if dxz is None:  # no gradient reached the gate: the z half is zero
+            dxz = torch.zeros_like(xz)
+        link.dxz = None
+        dv = dv.float().contiguous()
+        dw = torch.empty((C, K), dtype=torch.float32, device=xz.device)
+        db = torch.empty(C, dtype=torch.float32, device=xz.device) if has_bias else None
+        a = _lib.new_args(_lib.SemxConvSiluArgs)
+        a.K, a.left, a.bf16 = K, left, int(xz.dtype == torch.bfloat16)
+        a.S, a.L, a.C, a.ld = S, L, C, ld
+        a.xz, a.w, a.b = xz.data_ptr(), w.data_ptr(), (b.data_ptr() if has_bias else None)
+        a.dv, a.dxz, a.dw, a.db = dv.data_ptr(), dxz.data_ptr(), dw.data_ptr(), _lib.ptr(db)
+        ws = _lib.empty_f32(_lib.load().semx_conv_silu_workspace_bytes(a), xz.device)
+        a.workspace = ws.data_ptr()
+        _lib.call("semx_conv_silu_bwd", a, xz.device)
+        return dxz, dw.reshape(wshape), db, None, None, None, None
+
+
+class _GateSiLU(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, y, xz, C, link):
+        S, L, ld = xz.shape
+        y = y.float().contiguous()
+        o = torch.empty((S, L, C), dtype=xz.dtype, device=xz.device)
+        a = _lib.new_args(_lib.SemxGateSiluArgs)
+        a.bf16 = int(xz.dtype == torch.bfloat16)
+        a.n, a.C, a.ld = S * L, C, ld
+        a.y, a.xz, a.o = y.data_ptr(), xz.data_ptr(), o.data_ptr()
+        _lib.call("semx_gate_silu_fwd", a, xz.device)
+        ctx.save_for_backward(y, xz)
+        ctx.cfg = (C, link)
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        y, xz = ctx.saved_tensors
+        C, link = ctx.cfg
+        S, L, ld = xz.shape
+        do = do.to(xz.dtype).contiguous()
+        dy = torch.empty_like(y)
+        dxz = torch.empty_like(xz)  # columns [0, C) are written by the convolution's backward
+        a = _lib.new_args(_lib.SemxGateSiluArgs)
+        a.bf16 = int(xz.dtype == torch.bfloat16)
+        a.n, a.C, a.ld = S * L, C, ld
+        a.y, a.xz, a.dout, a.dy, a.dxz = y.data_ptr(), xz.data_ptr(), do.data_ptr(), dy.data_ptr(), dxz.data_ptr()
+        _lib.call("semx_gate_silu_bwd", a, xz.device)
+        link.dxz = dxz
+        return dy, None, None, None
 
 
 class MambaStyleMixer(nn.Module):
@@ -43,14 +137,11 @@ class MambaStyleMixer(nn.Module):
         # ``inference_params`` is accepted for the prenorm Block calling convention; the
         # scan layers have no single-step decoding state here.
         del inference_params
-        u, z = self.in_proj(x).chunk(2, dim=-1)
-        if self.causal_conv:
-            pad = (self.d_conv - 1, 0)
-        else:
-            left = (self.d_conv - 1) // 2
-            pad = (left, self.d_conv - 1 - left)
-        u = self.conv(F.pad(u.transpose(1, 2), pad)).transpose(1, 2)
-        u = F.silu(u)
+        xz = self.in_proj(x)
+        _check_xz(xz)
+        xz = xz.contiguous()
+        left = self.d_conv - 1 if self.causal_conv else (self.d_conv - 1) // 2
+        link = _DxzLink()
+        u = _ConvSiLU.apply(xz, self.conv.weight, self.conv.bias, self.inner_dim, self.d_conv, left, link)
         y = self.ssm(u)
-        y = y * F.silu(z)
-        return self.out_proj(y)
+        return self.out_proj(_GateSiLU.apply(y, xz, self.inner_dim, link))

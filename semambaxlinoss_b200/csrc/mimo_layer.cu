@@ -23,6 +23,8 @@
 // env_gain are kept where both access orders occur).
 #include <cuda_bf16.h>
 
+#include <type_traits>
+
 #include "semx_common.cuh"
 #include "semx_math.cuh"
 #include "semx_reduce.cuh"
@@ -39,6 +41,7 @@ constexpr float kLog2e = 1.4426950408889634f;
 struct LParams {
   int64_t S, L, H, Nh, Fh, R, P;  // P = projection row width
   int gain, detune, envelope, nchunks;
+  int vec;  // bit 0: x rows 16-byte aligned; bit 1: b_t / c_t rows 16-byte aligned
   float rs;
   const void* x;
   const void* proj;
@@ -267,66 +270,394 @@ __device__ void poles_and_drive(const LParams& p, const Lay& l, float* sm, int n
 }
 
 // ----------------------------------------------------------------------------- forward
+// Shared-memory layout of the forward (floats; staging buffers hold the input dtype).
+struct FLay {
+  int Btr, Bti, Cr, Ci, En, Co, Dp, prm, cin;
+  int stg[2], sml[2];  // staged x | b_t | c_t (input dtype); small operands (fp32)
+  int lam, bu, hs, sr;
+  int xw, btw, ctw;    // staged row widths in elements, padded so rows two tokens apart
+                       // fall in different shared-memory banks
+  int hw;              // row width of lam / bu / hs in float2 (Nh + 1, same reason)
+  int total;
+};
+
+__host__ __device__ inline FLay make_flay(int Nh, int Fh, int R, bool env, int es) {
+  FLay l = {};
+  int o = 0;
+  auto take = [&](int n) {
+    const int at = o;
+    o += al4(n);
+    return at;
+  };
+  l.Btr = take(Fh * Nh);
+  l.Bti = take(Fh * Nh);
+  l.Cr = take(Nh * Fh);
+  l.Ci = take(Nh * Fh);
+  l.En = env ? take(Nh * Fh) : -1;
+  l.Co = take(R * Fh);
+  l.Dp = take(Fh);
+  l.prm = take(3 * Nh);
+  l.cin = take(Nh * 2);
+  const int pad = 16 / es;
+  l.xw = ((Fh * es + 15) / 16) * 16 / es + pad;
+  l.btw = R > 0 ? ((R * Nh * es + 15) / 16) * 16 / es + pad : 0;
+  l.ctw = R > 0 ? ((2 * R * Nh * es + 15) / 16) * 16 / es + pad : 0;
+  const int stg_elems = kTC * (l.xw + l.btw + l.ctw);
+  for (int b = 0; b < 2; ++b) l.stg[b] = take((stg_elems * es + 3) / 4);
+  for (int b = 0; b < 2; ++b) l.sml[b] = take(kTC * (3 + 2 * R));
+  l.hw = Nh + 1;
+  l.lam = take(kTC * l.hw * 2);
+  l.bu = take(kTC * l.hw * 2);
+  l.hs = take(kTC * l.hw * 2);
+  l.sr = take(kTC * R);
+  l.total = o;
+  return l;
+}
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const unsigned sa = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(sa), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;\n" ::: "memory"); }
+
+// Issues the staging of chunk [t0, t0 + nt) of head h: x [kTC][Fh], b_t [kTC][R Nh],
+// c_t [kTC][2 R Nh] in the input dtype; 16-byte cp.async where the host found the rows
+// aligned (p.vec bit 0: x, bit 1: b_t and c_t), otherwise plain loads.
 template <bool BF16>
+__device__ void stage_bulk(const LParams& p, const FLay& l, void* dst, int64_t s, int h, int t0, int nt) {
+  using T = typename std::conditional<BF16, __nv_bfloat16, float>::type;
+  constexpr int kPer = 16 / sizeof(T);
+  const int Nh = (int)p.Nh, Fh = (int)p.Fh, R = (int)p.R;
+  T* xs = reinterpret_cast<T*>(dst);
+  T* bts = xs + kTC * l.xw;
+  T* cts = bts + kTC * l.btw;
+  const T* X = reinterpret_cast<const T*>(p.x);
+  const T* Pj = reinterpret_cast<const T*>(p.proj);
+  const Cols c = cols_of(p, h);
+  const int64_t Fd = p.H * p.Fh;
+  auto seg = [&](T* d, int dw, const T* src, int64_t row_stride, int64_t col, int width, bool vec) {
+    if (vec) {
+      const int q = width / kPer;
+      for (int i = threadIdx.x; i < nt * q; i += kT) {
+        const int t = i / q, j = i % q;
+        cp_async16(d + t * dw + j * kPer, src + (s * p.L + t0 + t) * row_stride + col + j * kPer);
+      }
+    } else {
+      for (int i = threadIdx.x; i < nt * width; i += kT) {
+        const int t = i / width, j = i % width;
+        d[t * dw + j] = src[(s * p.L + t0 + t) * row_stride + col + j];
+      }
+    }
+  };
+  seg(xs, l.xw, X, Fd, (int64_t)h * Fh, Fh, (p.vec & 1) != 0);
+  if (R > 0) {
+    seg(bts, l.btw, Pj, p.P, c.bt, R * Nh, (p.vec & 2) != 0);
+    seg(cts, l.ctw, Pj, p.P, c.ct, 2 * R * Nh, (p.vec & 2) != 0);
+  }
+}
+
+// Small per-token operands [dnu_raw, dth, s_b (R), s_c (R)] of chunk [t0, t0 + nt): item q
+// of this thread is i = tid + q kT over nt (2 + 2R) values.
+constexpr int kPre = 9;
+template <bool BF16>
+__device__ __forceinline__ void load_small(const LParams& p, int64_t s, int h, int t0, int nt,
+                                           float (&pre)[kPre]) {
+  const int R = (int)p.R, w = 2 + 2 * R;
+  const Cols c = cols_of(p, h);
+#pragma unroll
+  for (int q = 0; q < kPre; ++q) {
+    const int i = threadIdx.x + q * kT;
+    if (i < nt * w) {
+      const int t = i / w, j = i % w;
+      const int64_t col = j == 0 ? c.dnu : j == 1 ? c.dth : j < 2 + R ? c.sb + (j - 2) : c.sc + (j - 2 - R);
+      pre[q] = ld<BF16>(p.proj, (s * p.L + t0 + t) * p.P + col);
+    }
+  }
+}
+// Writes them as [raw (kTC) | dnu (kTC) | dth (kTC) | s_b (kTC R) | s_c (kTC R)].
+__device__ __forceinline__ void store_small(const LParams& p, float* sml, int nt, const float (&pre)[kPre]) {
+  const int R = (int)p.R, w = 2 + 2 * R;
+#pragma unroll
+  for (int q = 0; q < kPre; ++q) {
+    const int i = threadIdx.x + q * kT;
+    if (i < nt * w) {
+      const int t = i / w, j = i % w;
+      if (j == 0) {
+        sml[t] = pre[q];
+        sml[kTC + t] = semx::softplus(pre[q]) * p.rs;
+      } else if (j == 1) {
+        sml[2 * kTC + t] = pre[q];
+      } else if (j < 2 + R) {
+        sml[3 * kTC + t * R + (j - 2)] = pre[q];
+      } else {
+        sml[3 * kTC + kTC * R + t * R + (j - 2 - R)] = pre[q];
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ float2 cmul(float2 a, float2 b) {
+  return make_float2(a.x * b.x - a.y * b.y, a.x * b.y + a.y * b.x);
+}
+
+// Scan of the chunk: h_t = lam_t h_{t-1} + bu_t from cin[n]; writes hs[t][n] and the
+// chunk's final state back to cin[n]. With SEG > 1 (Nh * SEG == kT), thread (n, seg)
+// composes kTC / SEG steps, the segments are combined by an inclusive shuffle scan of the
+// affine maps, and each segment is replayed from its entry state; SEG == 1 runs one
+// thread per mode over the whole chunk.
+// Rows of lam / bu / hs are hw float2 apart. Lanes are segment-major inside a warp
+// (lane = seg * (32 / SEG) + mode), so the shuffles step by 32 / SEG lanes and the
+// shared-memory rows touched by one instruction fall in distinct banks.
+template <int SEG>
+__device__ __forceinline__ void chunk_scan(const float2* lam, const float2* bu, float2* hs, float2* cin,
+                                           int Nh, int hw, int nt) {
+  if (SEG == 1) {
+    const int n = threadIdx.x;
+    if (n < Nh) {
+      float2 st = cin[n];
+      for (int t = 0; t < nt; ++t) {
+        st = cmul(lam[t * hw + n], st);
+        st.x += bu[t * hw + n].x;
+        st.y += bu[t * hw + n].y;
+        hs[t * hw + n] = st;
+      }
+      cin[n] = st;
+    }
+    return;
+  }
+  constexpr int TS = kTC / SEG;
+  constexpr int MPW = 32 / SEG;  // modes per warp
+  const int lane = threadIdx.x & 31;
+  const int n = (threadIdx.x >> 5) * MPW + lane % MPW, seg = lane / MPW;
+  const int t0 = seg * TS;
+  float2 A = make_float2(1.f, 0.f), b = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int i = 0; i < TS; ++i) {
+    const int t = t0 + i;
+    if (t < nt) {
+      const float2 a = lam[t * hw + n];
+      b = cmul(a, b);
+      b.x += bu[t * hw + n].x;
+      b.y += bu[t * hw + n].y;
+      A = cmul(a, A);
+    }
+  }
+  // Inclusive scan over the segments of mode n: (A, b) after (Ap, bp) = (A Ap, A bp + b).
+#pragma unroll
+  for (int off = 1; off < SEG; off <<= 1) {
+    const float apr = __shfl_up_sync(0xffffffffu, A.x, off * MPW);
+    const float api = __shfl_up_sync(0xffffffffu, A.y, off * MPW);
+    const float bpr = __shfl_up_sync(0xffffffffu, b.x, off * MPW);
+    const float bpi = __shfl_up_sync(0xffffffffu, b.y, off * MPW);
+    if (seg >= off) {
+      const float2 nb = cmul(A, make_float2(bpr, bpi));
+      b = make_float2(nb.x + b.x, nb.y + b.y);
+      A = cmul(A, make_float2(apr, api));
+    }
+  }
+  const float2 c0 = cin[n];
+  // Entry state of this segment: the inclusive map of the previous segment applied to c0.
+  const float epr = __shfl_up_sync(0xffffffffu, A.x, MPW);
+  const float epi = __shfl_up_sync(0xffffffffu, A.y, MPW);
+  const float ebr = __shfl_up_sync(0xffffffffu, b.x, MPW);
+  const float ebi = __shfl_up_sync(0xffffffffu, b.y, MPW);
+  float2 st = c0;
+  if (seg > 0) {
+    st = cmul(make_float2(epr, epi), c0);
+    st.x += ebr;
+    st.y += ebi;
+  }
+#pragma unroll
+  for (int i = 0; i < TS; ++i) {
+    const int t = t0 + i;
+    if (t < nt) {
+      st = cmul(lam[t * hw + n], st);
+      st.x += bu[t * hw + n].x;
+      st.y += bu[t * hw + n].y;
+      hs[t * hw + n] = st;
+    }
+  }
+  __syncwarp();
+  if (seg == SEG - 1) {  // final state of the chunk: the last segment's map applied to c0
+    const float2 e = cmul(A, c0);
+    cin[n] = make_float2(e.x + b.x, e.y + b.y);
+  }
+}
+
+template <bool BF16, int SEG>
 __global__ void __launch_bounds__(kT) mimo_layer_fwd_kernel(const LParams p) {
+  using T = typename std::conditional<BF16, __nv_bfloat16, float>::type;
   extern __shared__ float4 smem4[];
   float* sm = reinterpret_cast<float*>(smem4);
   const int Nh = (int)p.Nh, Fh = (int)p.Fh, R = (int)p.R, L = (int)p.L;
-  const Lay l = make_lay(Nh, Fh, R, false, p.envelope != 0);
+  const bool env = p.envelope != 0;
+  const FLay l = make_flay(Nh, Fh, R, env, (int)sizeof(T));
   const int64_t s = blockIdx.x / p.H;
   const int h = (int)(blockIdx.x % p.H);
   const int tid = threadIdx.x;
   const int64_t Fd = p.H * p.Fh;
-  load_head_params(p, l, sm, h, false);
+  // Head parameters.
+  for (int i = tid; i < Nh * Fh; i += kT) {
+    const int n = i / Fh, f = i % Fh;
+    const float2 bv = reinterpret_cast<const float2*>(p.B)[((int64_t)h * Nh + n) * Fh + f];
+    sm[l.Btr + f * Nh + n] = bv.x;
+    sm[l.Bti + f * Nh + n] = bv.y;
+    const int f2 = i / Nh, n2 = i % Nh;
+    const float2 cv = reinterpret_cast<const float2*>(p.C)[((int64_t)h * Fh + f2) * Nh + n2];
+    sm[l.Cr + n2 * Fh + f2] = cv.x;
+    sm[l.Ci + n2 * Fh + f2] = cv.y;
+    if (env) sm[l.En + n2 * Fh + f2] = p.env[((int64_t)h * Fh + f2) * Nh + n2];
+  }
+  for (int i = tid; i < R * Fh; i += kT) sm[l.Co + i] = p.cout[(int64_t)h * R * Fh + i];
+  for (int i = tid; i < Fh; i += kT) sm[l.Dp + i] = p.D[(int64_t)h * Fh + i];
+  for (int n = tid; n < Nh; n += kT) {
+    sm[l.prm + n] = expf(p.A_log[(int64_t)h * Nh + n]);
+    sm[l.prm + Nh + n] = p.omega[(int64_t)h * Nh + n];
+    sm[l.prm + 2 * Nh + n] = p.detune ? p.sdet[(int64_t)h * Nh + n] : 1.f;
+    reinterpret_cast<float2*>(sm + l.cin)[n] = make_float2(0.f, 0.f);
+  }
+  float2* lam = reinterpret_cast<float2*>(sm + l.lam);
+  float2* bu = reinterpret_cast<float2*>(sm + l.bu);
   float2* hs = reinterpret_cast<float2*>(sm + l.hs);
-  float2 state = make_float2(0.f, 0.f);  // thread n < Nh: the mode's state
+  float2* cin = reinterpret_cast<float2*>(sm + l.cin);
+  const float* Btr = sm + l.Btr;
+  const float* Bti = sm + l.Bti;
+  const float* Cr = sm + l.Cr;
+  const float* Ci = sm + l.Ci;
+  const int hw = l.hw;
+  float pre[kPre];
+  if (p.nchunks > 0) {
+    const int nt0 = min(kTC, L);
+    stage_bulk<BF16>(p, l, sm + l.stg[0], s, h, 0, nt0);
+    load_small<BF16>(p, s, h, 0, nt0, pre);
+    store_small(p, sm + l.sml[0], nt0, pre);
+  }
+  cp_async_commit();
   for (int k = 0; k < p.nchunks; ++k) {
+    const int b = k & 1;
     const int t0 = k * kTC, nt = min(kTC, L - t0);
+    const int t0n = t0 + kTC, ntn = min(kTC, L - t0n);
+    cp_async_wait_all();
     __syncthreads();
-    stage_chunk<BF16>(p, l, sm, s, h, t0, nt, false);
-    __syncthreads();
-    poles_and_drive(p, l, sm, nt, true);
-    __syncthreads();
-    if (tid < Nh) {
-      if (p.ckpt) reinterpret_cast<float2*>(p.ckpt)[((s * p.nchunks + k) * p.H + h) * Nh + tid] = state;
-      hs[tid] = state;
-      const float2* lam = reinterpret_cast<const float2*>(sm + l.lam);
-      const float2* bu = reinterpret_cast<const float2*>(sm + l.bu);
-      for (int t = 0; t < nt; ++t) {
-        const float2 a = lam[t * Nh + tid], u = bu[t * Nh + tid];
-        const float nr = fmaf(a.x, state.x, fmaf(-a.y, state.y, u.x));
-        const float ni = fmaf(a.x, state.y, fmaf(a.y, state.x, u.y));
-        state = make_float2(nr, ni);
-        hs[(t + 1) * Nh + tid] = state;
+    if (k + 1 < p.nchunks) {
+      stage_bulk<BF16>(p, l, sm + l.stg[b ^ 1], s, h, t0n, ntn);
+      load_small<BF16>(p, s, h, t0n, ntn, pre);
+    }
+    cp_async_commit();
+    const T* xs = reinterpret_cast<const T*>(sm + l.stg[b]);
+    const T* bts = xs + kTC * l.xw;
+    const T* cts = bts + kTC * l.btw;
+    const int xw = l.xw, btw = l.btw, ctw = l.ctw;
+    const float* sml = sm + l.sml[b];
+    const float* dnus = sml + kTC;
+    const float* dths = sml + 2 * kTC;
+    const float* sbs = sml + 3 * kTC;
+    const float* scs = sbs + kTC * R;
+    // Poles and gained drive, 2 tokens x 2 modes per item.
+    const int np = (Nh + 1) / 2;
+    for (int it = tid; it < (kTC / 2) * np; it += kT) {
+      const int ta = (it / np) * 2, na = (it % np) * 2;
+      if (ta >= nt) continue;
+      float br[2][2] = {}, bi[2][2] = {};
+      const bool t1ok = ta + 1 < nt, n1ok = na + 1 < Nh;
+      for (int f = 0; f < Fh; ++f) {
+        const float x0 = static_cast<float>(xs[ta * xw + f]);
+        const float x1 = t1ok ? static_cast<float>(xs[(ta + 1) * xw + f]) : 0.f;
+        const float b0r = Btr[f * Nh + na], b0i = Bti[f * Nh + na];
+        const float b1r = n1ok ? Btr[f * Nh + na + 1] : 0.f, b1i = n1ok ? Bti[f * Nh + na + 1] : 0.f;
+        br[0][0] = fmaf(b0r, x0, br[0][0]); bi[0][0] = fmaf(b0i, x0, bi[0][0]);
+        br[0][1] = fmaf(b1r, x0, br[0][1]); bi[0][1] = fmaf(b1i, x0, bi[0][1]);
+        br[1][0] = fmaf(b0r, x1, br[1][0]); bi[1][0] = fmaf(b0i, x1, bi[1][0]);
+        br[1][1] = fmaf(b1r, x1, br[1][1]); bi[1][1] = fmaf(b1i, x1, bi[1][1]);
+      }
+#pragma unroll
+      for (int dt = 0; dt < 2; ++dt) {
+        const int t = ta + dt;
+        if (t >= nt) continue;
+#pragma unroll
+        for (int dn = 0; dn < 2; ++dn) {
+          const int n = na + dn;
+          if (n >= Nh) continue;
+          float rr = br[dt][dn];
+          for (int r = 0; r < R; ++r) rr = fmaf(sbs[t * R + r], static_cast<float>(bts[t * btw + r * Nh + n]), rr);
+          const MDisc d = mdisc(p.gain, sm[l.prm + n], sm[l.prm + Nh + n], sm[l.prm + 2 * Nh + n],
+                                p.detune != 0, dnus[t], dths[t]);
+          lam[t * hw + n] = make_float2(d.lre, d.lim);
+          bu[t * hw + n] = make_float2(d.gr * rr - d.gi * bi[dt][dn], d.gr * bi[dt][dn] + d.gi * rr);
+        }
       }
     }
+    __syncthreads();
+    if (p.ckpt != nullptr && tid < Nh)
+      reinterpret_cast<float2*>(p.ckpt)[((s * p.nchunks + k) * p.H + h) * Nh + tid] = cin[tid];
+    __syncthreads();
+    chunk_scan<SEG>(lam, bu, hs, cin, Nh, hw, nt);
     __syncthreads();
     if (R > 0) {
       for (int i = tid; i < nt * R; i += kT) {
         const int t = i / R, r = i % R;
-        const float* cr = sm + l.ct + (t * R + r) * 2 * Nh;
+        const T* cr = cts + t * ctw + r * 2 * Nh;
         float acc = 0.f;
         for (int n = 0; n < Nh; ++n) {
-          const float2 hv = hs[(t + 1) * Nh + n];
-          acc = fmaf(cr[n], hv.x, fmaf(-cr[Nh + n], hv.y, acc));
+          const float2 hv = hs[t * hw + n];
+          acc = fmaf(static_cast<float>(cr[n]), hv.x, fmaf(-static_cast<float>(cr[Nh + n]), hv.y, acc));
         }
-        sm[l.sr + i] = sm[l.sc + i] * acc;
+        sm[l.sr + i] = scs[i] * acc;
       }
       __syncthreads();
     }
-    const float2* Cn = reinterpret_cast<const float2*>(sm + l.Cn);
-    for (int i = tid; i < nt * Fh; i += kT) {
-      const int t = i / Fh, f = i % Fh;
-      float acc = sm[l.Dp + f] * sm[l.xs + i];
+    // Readout, 2 tokens x 4 channels per item.
+    const int fq = (Fh + 3) / 4;
+    for (int it = tid; it < (kTC / 2) * fq; it += kT) {
+      const int ta = (it / fq) * 2, fa = (it % fq) * 4;
+      if (ta >= nt) continue;
+      const bool t1ok = ta + 1 < nt;
+      float acc[2][4];
+#pragma unroll
+      for (int dt = 0; dt < 2; ++dt)
+#pragma unroll
+        for (int df = 0; df < 4; ++df) {
+          const int f = min(fa + df, Fh - 1);
+          const int t = min(ta + dt, nt - 1);
+          acc[dt][df] = sm[l.Dp + f] * static_cast<float>(xs[t * xw + f]);
+        }
       for (int n = 0; n < Nh; ++n) {
-        const float2 hv = hs[(t + 1) * Nh + n];
-        const float2 c = Cn[n * Fh + f];
-        acc = fmaf(c.x, hv.x, fmaf(-c.y, hv.y, acc));
-        if (p.envelope) acc = fmaf(sm[l.En + n * Fh + f], hv.x * hv.x + hv.y * hv.y, acc);
+        const float2 h0 = hs[ta * hw + n];
+        const float2 h1 = t1ok ? hs[(ta + 1) * hw + n] : make_float2(0.f, 0.f);
+        const float p0 = h0.x * h0.x + h0.y * h0.y, p1 = h1.x * h1.x + h1.y * h1.y;
+#pragma unroll
+        for (int df = 0; df < 4; ++df) {
+          const int f = min(fa + df, Fh - 1);
+          const float cre = Cr[n * Fh + f], cim = Ci[n * Fh + f];
+          acc[0][df] = fmaf(cre, h0.x, fmaf(-cim, h0.y, acc[0][df]));
+          acc[1][df] = fmaf(cre, h1.x, fmaf(-cim, h1.y, acc[1][df]));
+          if (env) {
+            const float e = sm[l.En + n * Fh + f];
+            acc[0][df] = fmaf(e, p0, acc[0][df]);
+            acc[1][df] = fmaf(e, p1, acc[1][df]);
+          }
+        }
       }
-      for (int r = 0; r < R; ++r) acc = fmaf(sm[l.sr + t * R + r], sm[l.Co + r * Fh + f], acc);
-      p.y[(s * p.L + t0 + t) * Fd + (int64_t)h * Fh + f] = acc;
+      for (int r = 0; r < R; ++r) {
+        const float s0 = sm[l.sr + ta * R + r], s1 = t1ok ? sm[l.sr + (ta + 1) * R + r] : 0.f;
+#pragma unroll
+        for (int df = 0; df < 4; ++df) {
+          const float co = sm[l.Co + r * Fh + min(fa + df, Fh - 1)];
+          acc[0][df] = fmaf(s0, co, acc[0][df]);
+          acc[1][df] = fmaf(s1, co, acc[1][df]);
+        }
+      }
+#pragma unroll
+      for (int dt = 0; dt < 2; ++dt) {
+        if (dt == 1 && !t1ok) continue;
+        float* yr = p.y + (s * p.L + t0 + ta + dt) * Fd + (int64_t)h * Fh + fa;
+#pragma unroll
+        for (int df = 0; df < 4; ++df)
+          if (fa + df < Fh) yr[df] = acc[dt][df];
+      }
     }
+    if (k + 1 < p.nchunks) store_small(p, sm + l.sml[b ^ 1], ntn, pre);
   }
 }
 
@@ -602,7 +933,27 @@ int64_t part_row(const SemxMimoLayerArgs* a) {
 }
 
 size_t layer_smem(const SemxMimoLayerArgs* a, bool bwd) {
+  if (!bwd)
+    return (size_t)make_flay((int)a->Nh, (int)a->Fh, a->rank, a->envelope != 0, a->bf16 ? 2 : 4).total *
+           sizeof(float);
   return (size_t)make_lay((int)a->Nh, (int)a->Fh, a->rank, bwd, a->envelope != 0).total * sizeof(float);
+}
+
+// Which operand rows allow 16-byte staging copies (LParams::vec).
+int vec_flags(const SemxMimoLayerArgs* a) {
+  const int64_t es = a->bf16 ? 2 : 4, H = a->H, R = a->rank, Nh = a->Nh, Fh = a->Fh;
+  const int64_t P = proj_width(a);
+  const bool vx = semx::aligned(a->x, 16) && (H * Fh * es) % 16 == 0 && (Fh * es) % 16 == 0;
+  const bool vp = semx::aligned(a->proj, 16) && (P * es) % 16 == 0 && ((2 * H + H * R) * es) % 16 == 0 &&
+                  ((R * Nh * es) % 16) == 0 && ((2 * H + 2 * H * R + H * R * Nh) * es) % 16 == 0;
+  return (vx ? 1 : 0) | (vp ? 2 : 0);
+}
+
+// Segments per mode of the forward's parallel chunk scan (1: one thread per mode).
+int scan_segments(int64_t Nh) {
+  if (Nh <= 0 || kT % Nh != 0) return 1;
+  const int seg = kT / (int)Nh;
+  return (seg <= 32 && kTC % seg == 0) ? seg : 1;
 }
 
 int layer_validate(const SemxMimoLayerArgs* a, bool bwd) {
@@ -653,6 +1004,7 @@ LParams to_lparams(const SemxMimoLayerArgs* a) {
   p.cout = a->c_out; p.env = a->env_gain;
   p.y = a->y; p.ckpt = a->ckpt; p.dy = a->dy; p.dx = a->dx; p.dproj = a->dproj;
   p.K = part_row(a);
+  p.vec = vec_flags(a);
   return p;
 }
 
@@ -690,8 +1042,21 @@ int semx_mimo_layer_fwd(const SemxMimoLayerArgs* a, semx_stream_t stream) {
   const LParams p = to_lparams(a);
   const size_t smem = layer_smem(a, false);
   cudaStream_t st = semx::as_stream(stream);
-  return a->bf16 ? launch_layer(mimo_layer_fwd_kernel<true>, p, smem, st, "mimo_layer_fwd_kernel")
-                 : launch_layer(mimo_layer_fwd_kernel<false>, p, smem, st, "mimo_layer_fwd_kernel");
+  switch (scan_segments(a->Nh)) {
+#define SEMX_SEG(SV)                                                                                     \
+  case SV:                                                                                               \
+    return a->bf16 ? launch_layer(mimo_layer_fwd_kernel<true, SV>, p, smem, st, "mimo_layer_fwd_kernel") \
+                   : launch_layer(mimo_layer_fwd_kernel<false, SV>, p, smem, st, "mimo_layer_fwd_kernel");
+    SEMX_SEG(2)
+    SEMX_SEG(4)
+    SEMX_SEG(8)
+    SEMX_SEG(16)
+    SEMX_SEG(32)
+#undef SEMX_SEG
+    default:
+      return a->bf16 ? launch_layer(mimo_layer_fwd_kernel<true, 1>, p, smem, st, "mimo_layer_fwd_kernel")
+                     : launch_layer(mimo_layer_fwd_kernel<false, 1>, p, smem, st, "mimo_layer_fwd_kernel");
+  }
 }
 
 int semx_mimo_layer_bwd(const SemxMimoLayerArgs* a, semx_stream_t stream) {

@@ -321,49 +321,56 @@ __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;\n" ::: "memory"); }
 
-// Issues the staging of chunk [t0, t0 + nt) of head h: x [kTC][Fh], b_t [kTC][R Nh],
-// c_t [kTC][2 R Nh] in the input dtype; 16-byte cp.async where the host found the rows
-// aligned (p.vec bit 0: x, bit 1: b_t and c_t), otherwise plain loads.
-template <bool BF16>
-__device__ void stage_bulk(const LParams& p, const FLay& l, void* dst, int64_t s, int h, int t0, int nt) {
-  using T = typename std::conditional<BF16, __nv_bfloat16, float>::type;
+// Copies rows [t0, t0 + nt) of one column segment (width elements at column col of rows
+// row_stride apart) into d (rows dw elements apart).
+template <typename T>
+__device__ __forceinline__ void stage_segment(T* d, int dw, const T* src, int64_t row0, int64_t row_stride,
+                                              int64_t col, int width, int nt, bool vec) {
   constexpr int kPer = 16 / sizeof(T);
-  const int Nh = (int)p.Nh, Fh = (int)p.Fh, R = (int)p.R;
+  if (vec) {
+    const int q = width / kPer;
+    for (int i = threadIdx.x; i < nt * q; i += kT) {
+      const int t = i / q, j = i - (i / q) * q;
+      cp_async16(d + t * dw + j * kPer, src + (row0 + t) * row_stride + col + j * kPer);
+    }
+  } else {
+    for (int i = threadIdx.x; i < nt * width; i += kT) {
+      const int t = i / width, j = i - (i / width) * width;
+      d[t * dw + j] = src[(row0 + t) * row_stride + col + j];
+    }
+  }
+}
+
+// Issues the staging of chunk [t0, t0 + nt) of head h: x [kTC][Fh], b_t [kTC][R Nh],
+// c_t [kTC][2 R Nh] in the input dtype, rows padded to l.xw / l.btw / l.ctw; 16-byte
+// cp.async where the host found the rows aligned (p.vec bit 0: x, bit 1: b_t and c_t),
+// otherwise plain loads.
+template <bool BF16, int NH, int FH, int RK>
+__device__ __forceinline__ void stage_bulk(const LParams& p, const FLay& l, void* dst, int64_t s, int h,
+                                           int t0, int nt) {
+  using T = typename std::conditional<BF16, __nv_bfloat16, float>::type;
+  const int Nh = NH > 0 ? NH : (int)p.Nh, Fh = FH > 0 ? FH : (int)p.Fh, R = RK >= 0 ? RK : (int)p.R;
   T* xs = reinterpret_cast<T*>(dst);
   T* bts = xs + kTC * l.xw;
   T* cts = bts + kTC * l.btw;
   const T* X = reinterpret_cast<const T*>(p.x);
   const T* Pj = reinterpret_cast<const T*>(p.proj);
-  const Cols c = cols_of(p, h);
-  const int64_t Fd = p.H * p.Fh;
-  auto seg = [&](T* d, int dw, const T* src, int64_t row_stride, int64_t col, int width, bool vec) {
-    if (vec) {
-      const int q = width / kPer;
-      for (int i = threadIdx.x; i < nt * q; i += kT) {
-        const int t = i / q, j = i % q;
-        cp_async16(d + t * dw + j * kPer, src + (s * p.L + t0 + t) * row_stride + col + j * kPer);
-      }
-    } else {
-      for (int i = threadIdx.x; i < nt * width; i += kT) {
-        const int t = i / width, j = i % width;
-        d[t * dw + j] = src[(s * p.L + t0 + t) * row_stride + col + j];
-      }
-    }
-  };
-  seg(xs, l.xw, X, Fd, (int64_t)h * Fh, Fh, (p.vec & 1) != 0);
+  const int64_t row0 = s * p.L + t0;
+  stage_segment<T>(xs, l.xw, X, row0, p.H * p.Fh, (int64_t)h * Fh, Fh, nt, (p.vec & 1) != 0);
   if (R > 0) {
-    seg(bts, l.btw, Pj, p.P, c.bt, R * Nh, (p.vec & 2) != 0);
-    seg(cts, l.ctw, Pj, p.P, c.ct, 2 * R * Nh, (p.vec & 2) != 0);
+    const Cols c = cols_of(p, h);
+    stage_segment<T>(bts, l.btw, Pj, row0, p.P, c.bt, R * Nh, nt, (p.vec & 2) != 0);
+    stage_segment<T>(cts, l.ctw, Pj, row0, p.P, c.ct, 2 * R * Nh, nt, (p.vec & 2) != 0);
   }
 }
 
 // Small per-token operands [dnu_raw, dth, s_b (R), s_c (R)] of chunk [t0, t0 + nt): item q
 // of this thread is i = tid + q kT over nt (2 + 2R) values.
 constexpr int kPre = 9;
-template <bool BF16>
+template <bool BF16, int RK>
 __device__ __forceinline__ void load_small(const LParams& p, int64_t s, int h, int t0, int nt,
                                            float (&pre)[kPre]) {
-  const int R = (int)p.R, w = 2 + 2 * R;
+  const int R = RK >= 0 ? RK : (int)p.R, w = 2 + 2 * R;
   const Cols c = cols_of(p, h);
 #pragma unroll
   for (int q = 0; q < kPre; ++q) {
@@ -376,8 +383,9 @@ __device__ __forceinline__ void load_small(const LParams& p, int64_t s, int h, i
   }
 }
 // Writes them as [raw (kTC) | dnu (kTC) | dth (kTC) | s_b (kTC R) | s_c (kTC R)].
+template <int RK>
 __device__ __forceinline__ void store_small(const LParams& p, float* sml, int nt, const float (&pre)[kPre]) {
-  const int R = (int)p.R, w = 2 + 2 * R;
+  const int R = RK >= 0 ? RK : (int)p.R, w = 2 + 2 * R;
 #pragma unroll
   for (int q = 0; q < kPre; ++q) {
     const int i = threadIdx.x + q * kT;
@@ -485,12 +493,15 @@ __device__ __forceinline__ void chunk_scan(const float2* lam, const float2* bu, 
   }
 }
 
-template <bool BF16, int SEG>
+// NH, FH, RK > 0 (RK >= 0) fix the head's modes, channels and rank at compile time;
+// 0 (-1) takes them from the parameters.
+template <bool BF16, int SEG, int NH, int FH, int RK>
 __global__ void __launch_bounds__(kT) mimo_layer_fwd_kernel(const LParams p) {
   using T = typename std::conditional<BF16, __nv_bfloat16, float>::type;
   extern __shared__ float4 smem4[];
   float* sm = reinterpret_cast<float*>(smem4);
-  const int Nh = (int)p.Nh, Fh = (int)p.Fh, R = (int)p.R, L = (int)p.L;
+  const int Nh = NH > 0 ? NH : (int)p.Nh, Fh = FH > 0 ? FH : (int)p.Fh, R = RK >= 0 ? RK : (int)p.R;
+  const int L = (int)p.L;
   const bool env = p.envelope != 0;
   const FLay l = make_flay(Nh, Fh, R, env, (int)sizeof(T));
   const int64_t s = blockIdx.x / p.H;
@@ -529,9 +540,9 @@ __global__ void __launch_bounds__(kT) mimo_layer_fwd_kernel(const LParams p) {
   float pre[kPre];
   if (p.nchunks > 0) {
     const int nt0 = min(kTC, L);
-    stage_bulk<BF16>(p, l, sm + l.stg[0], s, h, 0, nt0);
-    load_small<BF16>(p, s, h, 0, nt0, pre);
-    store_small(p, sm + l.sml[0], nt0, pre);
+    stage_bulk<BF16, NH, FH, RK>(p, l, sm + l.stg[0], s, h, 0, nt0);
+    load_small<BF16, RK>(p, s, h, 0, nt0, pre);
+    store_small<RK>(p, sm + l.sml[0], nt0, pre);
   }
   cp_async_commit();
   for (int k = 0; k < p.nchunks; ++k) {
@@ -541,8 +552,8 @@ __global__ void __launch_bounds__(kT) mimo_layer_fwd_kernel(const LParams p) {
     cp_async_wait_all();
     __syncthreads();
     if (k + 1 < p.nchunks) {
-      stage_bulk<BF16>(p, l, sm + l.stg[b ^ 1], s, h, t0n, ntn);
-      load_small<BF16>(p, s, h, t0n, ntn, pre);
+      stage_bulk<BF16, NH, FH, RK>(p, l, sm + l.stg[b ^ 1], s, h, t0n, ntn);
+      load_small<BF16, RK>(p, s, h, t0n, ntn, pre);
     }
     cp_async_commit();
     const T* xs = reinterpret_cast<const T*>(sm + l.stg[b]);
@@ -561,6 +572,7 @@ __global__ void __launch_bounds__(kT) mimo_layer_fwd_kernel(const LParams p) {
       if (ta >= nt) continue;
       float br[2][2] = {}, bi[2][2] = {};
       const bool t1ok = ta + 1 < nt, n1ok = na + 1 < Nh;
+#pragma unroll 8
       for (int f = 0; f < Fh; ++f) {
         const float x0 = static_cast<float>(xs[ta * xw + f]);
         const float x1 = t1ok ? static_cast<float>(xs[(ta + 1) * xw + f]) : 0.f;
@@ -622,6 +634,7 @@ __global__ void __launch_bounds__(kT) mimo_layer_fwd_kernel(const LParams p) {
           const int t = min(ta + dt, nt - 1);
           acc[dt][df] = sm[l.Dp + f] * static_cast<float>(xs[t * xw + f]);
         }
+#pragma unroll 4
       for (int n = 0; n < Nh; ++n) {
         const float2 h0 = hs[ta * hw + n];
         const float2 h1 = t1ok ? hs[(ta + 1) * hw + n] : make_float2(0.f, 0.f);
@@ -657,7 +670,7 @@ __global__ void __launch_bounds__(kT) mimo_layer_fwd_kernel(const LParams p) {
           if (fa + df < Fh) yr[df] = acc[dt][df];
       }
     }
-    if (k + 1 < p.nchunks) store_small(p, sm + l.sml[b ^ 1], ntn, pre);
+    if (k + 1 < p.nchunks) store_small<RK>(p, sm + l.sml[b ^ 1], ntn, pre);
   }
 }
 
@@ -1042,11 +1055,21 @@ int semx_mimo_layer_fwd(const SemxMimoLayerArgs* a, semx_stream_t stream) {
   const LParams p = to_lparams(a);
   const size_t smem = layer_smem(a, false);
   cudaStream_t st = semx::as_stream(stream);
-  switch (scan_segments(a->Nh)) {
-#define SEMX_SEG(SV)                                                                                     \
-  case SV:                                                                                               \
-    return a->bf16 ? launch_layer(mimo_layer_fwd_kernel<true, SV>, p, smem, st, "mimo_layer_fwd_kernel") \
-                   : launch_layer(mimo_layer_fwd_kernel<false, SV>, p, smem, st, "mimo_layer_fwd_kernel");
+  const int seg = scan_segments(a->Nh);
+  if (seg == 8 && a->Nh == 16 && a->Fh == 32 && (a->rank == 4 || a->rank == 0)) {
+    // The 8-head x 32 / 16-mode layers, specialised at compile time.
+    if (a->rank == 4)
+      return a->bf16 ? launch_layer(mimo_layer_fwd_kernel<true, 8, 16, 32, 4>, p, smem, st, "mimo_layer_fwd_kernel")
+                     : launch_layer(mimo_layer_fwd_kernel<false, 8, 16, 32, 4>, p, smem, st, "mimo_layer_fwd_kernel");
+    return a->bf16 ? launch_layer(mimo_layer_fwd_kernel<true, 8, 16, 32, 0>, p, smem, st, "mimo_layer_fwd_kernel")
+                   : launch_layer(mimo_layer_fwd_kernel<false, 8, 16, 32, 0>, p, smem, st, "mimo_layer_fwd_kernel");
+  }
+  switch (seg) {
+#define SEMX_SEG(SV)                                                                                  \
+  case SV:                                                                                            \
+    return a->bf16                                                                                    \
+               ? launch_layer(mimo_layer_fwd_kernel<true, SV, 0, 0, -1>, p, smem, st, "mimo_layer_fwd_kernel") \
+               : launch_layer(mimo_layer_fwd_kernel<false, SV, 0, 0, -1>, p, smem, st, "mimo_layer_fwd_kernel");
     SEMX_SEG(2)
     SEMX_SEG(4)
     SEMX_SEG(8)
@@ -1054,8 +1077,8 @@ int semx_mimo_layer_fwd(const SemxMimoLayerArgs* a, semx_stream_t stream) {
     SEMX_SEG(32)
 #undef SEMX_SEG
     default:
-      return a->bf16 ? launch_layer(mimo_layer_fwd_kernel<true, 1>, p, smem, st, "mimo_layer_fwd_kernel")
-                     : launch_layer(mimo_layer_fwd_kernel<false, 1>, p, smem, st, "mimo_layer_fwd_kernel");
+      return a->bf16 ? launch_layer(mimo_layer_fwd_kernel<true, 1, 0, 0, -1>, p, smem, st, "mimo_layer_fwd_kernel")
+                     : launch_layer(mimo_layer_fwd_kernel<false, 1, 0, 0, -1>, p, smem, st, "mimo_layer_fwd_kernel");
   }
 }
 

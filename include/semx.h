@@ -334,7 +334,7 @@ int semx_mimo_bwd(const SemxMimoArgs* args, semx_stream_t stream);
  * Replaces SelectiveLRUMIMO.forward after its projections
  * (models/selective_lru/selective_lru.py:488-587): poles, drive, gain, scan, readout and
  * feedthrough in one pass per (sequence, head). Training forwards store the state at
- * every 32-step block in ckpt (semx_mimo_layer_ckpt_bytes()). Backward recomputes from
+ * every 16-step block in ckpt (semx_mimo_layer_ckpt_bytes()). Backward recomputes from
  * ckpt and writes dx (the input-map and skip part), dproj and the parameter gradients
  * (reduced over sequences in a fixed order; dA_log is with respect to A_log).
  * ---------------------------------------------------------------------------------- */

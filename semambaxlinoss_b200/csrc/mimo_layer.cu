@@ -33,6 +33,7 @@ namespace {
 
 constexpr int kT = 128;   // threads per CTA
 constexpr int kTC = 32;   // tokens per chunk
+constexpr int kCk = 16;   // tokens per checkpoint
 constexpr int kMaxNh = 64;
 constexpr int kMaxFh = 256;
 constexpr int kMaxR = 16;
@@ -41,7 +42,8 @@ constexpr float kLog2e = 1.4426950408889634f;
 struct LParams {
   int64_t S, L, H, Nh, Fh, R, P;  // P = projection row width
   int gain, detune, envelope, nchunks;
-  int vec;  // bit 0: x rows 16-byte aligned; bit 1: b_t / c_t rows 16-byte aligned
+  int nck;  // checkpoints: one per kCk tokens
+  int vec;  // 16-byte aligned rows: bit 0 x, bit 1 b_t / c_t, bit 2 dy, bit 3 dx
   float rs;
   const void* x;
   const void* proj;
@@ -382,8 +384,9 @@ __device__ __forceinline__ void load_small(const LParams& p, int64_t s, int h, i
     }
   }
 }
-// Writes them as [raw (kTC) | dnu (kTC) | dth (kTC) | s_b (kTC R) | s_c (kTC R)].
-template <int RK>
+// Writes them as [raw (CT) | dnu (CT) | dth (CT) | s_b (CT R) | s_c (CT R)] for a chunk of
+// CT tokens.
+template <int RK, int CT = kTC>
 __device__ __forceinline__ void store_small(const LParams& p, float* sml, int nt, const float (&pre)[kPre]) {
   const int R = RK >= 0 ? RK : (int)p.R, w = 2 + 2 * R;
 #pragma unroll
@@ -393,13 +396,13 @@ __device__ __forceinline__ void store_small(const LParams& p, float* sml, int nt
       const int t = i / w, j = i % w;
       if (j == 0) {
         sml[t] = pre[q];
-        sml[kTC + t] = semx::softplus(pre[q]) * p.rs;
+        sml[CT + t] = semx::softplus(pre[q]) * p.rs;
       } else if (j == 1) {
-        sml[2 * kTC + t] = pre[q];
+        sml[2 * CT + t] = pre[q];
       } else if (j < 2 + R) {
-        sml[3 * kTC + t * R + (j - 2)] = pre[q];
+        sml[3 * CT + t * R + (j - 2)] = pre[q];
       } else {
-        sml[3 * kTC + kTC * R + t * R + (j - 2 - R)] = pre[q];
+        sml[3 * CT + CT * R + t * R + (j - 2 - R)] = pre[q];
       }
     }
   }
@@ -417,7 +420,7 @@ __device__ __forceinline__ float2 cmul(float2 a, float2 b) {
 // Rows of lam / bu / hs are hw float2 apart. Lanes are segment-major inside a warp
 // (lane = seg * (32 / SEG) + mode), so the shuffles step by 32 / SEG lanes and the
 // shared-memory rows touched by one instruction fall in distinct banks.
-template <int SEG>
+template <int SEG, int CT = kTC>
 __device__ __forceinline__ void chunk_scan(const float2* lam, const float2* bu, float2* hs, float2* cin,
                                            int Nh, int hw, int nt) {
   if (SEG == 1) {
@@ -434,7 +437,7 @@ __device__ __forceinline__ void chunk_scan(const float2* lam, const float2* bu, 
     }
     return;
   }
-  constexpr int TS = kTC / SEG;
+  constexpr int TS = CT / SEG;
   constexpr int MPW = 32 / SEG;  // modes per warp
   const int lane = threadIdx.x & 31;
   const int n = (threadIdx.x >> 5) * MPW + lane % MPW, seg = lane / MPW;
@@ -602,10 +605,12 @@ __global__ void __launch_bounds__(kT) mimo_layer_fwd_kernel(const LParams p) {
     }
     __syncthreads();
     if (p.ckpt != nullptr && tid < Nh)
-      reinterpret_cast<float2*>(p.ckpt)[((s * p.nchunks + k) * p.H + h) * Nh + tid] = cin[tid];
+      reinterpret_cast<float2*>(p.ckpt)[((s * p.nck + 2 * k) * p.H + h) * Nh + tid] = cin[tid];
     __syncthreads();
     chunk_scan<SEG>(lam, bu, hs, cin, Nh, hw, nt);
     __syncthreads();
+    if (p.ckpt != nullptr && tid < Nh && t0 + kCk < L)  // the state entering token t0 + 16
+      reinterpret_cast<float2*>(p.ckpt)[((s * p.nck + 2 * k + 1) * p.H + h) * Nh + tid] = hs[(kCk - 1) * hw + tid];
     if (R > 0) {
       for (int i = tid; i < nt * R; i += kT) {
         const int t = i / R, r = i % R;
@@ -715,7 +720,7 @@ __global__ void __launch_bounds__(kT) mimo_layer_bwd_kernel(const LParams p) {
     __syncthreads();
     // Recompute the chunk's states from its checkpoint (row 0 = state entering it).
     if (tid < Nh) {
-      float2 hv = reinterpret_cast<const float2*>(p.ckpt)[((s * p.nchunks + k) * p.H + h) * Nh + tid];
+      float2 hv = reinterpret_cast<const float2*>(p.ckpt)[((s * p.nck + 2 * k) * p.H + h) * Nh + tid];
       hs[tid] = hv;
       for (int t = 0; t < nt; ++t) {
         const float2 a = lam[t * Nh + tid], g = gn[t * Nh + tid], b = braw[t * Nh + tid];
@@ -935,6 +940,505 @@ __global__ void __launch_bounds__(kT) mimo_layer_bwd_kernel(const LParams p) {
   }
 }
 
+// ------------------------------------------------------------- backward, 16 x 32 heads
+// The backward of the 16-mode, 32-channel heads (rank RK = 0 or 4), 16-token chunks:
+// everything a thread sums over time lives in its registers with a fixed ownership, so
+// the shared-memory footprint (about 52 KB) leaves room for 4 CTAs per SM.
+constexpr int kB_NH = 16, kB_FH = 32, kB_CT = 16, kB_SEG = 8;
+constexpr int kB_HW = kB_NH + 2;  // float2 row width of lam / gain / drive / h / G / db
+
+// Reverse adjoint scan of a chunk: G_t = g_t + c_{t+1}, c_t = conj(lam_t) G_t, starting
+// from cadj[n] (the carry of the token after the chunk); writes G over g and the carry at
+// the chunk start back to cadj[n]. Thread (mode, segment) as in chunk_scan; segments are
+// combined by an inclusive scan from the last segment down.
+template <int SEG, int CT>
+__device__ __forceinline__ void chunk_scan_rev(const float2* lam, float2* gs, float2* cadj, int hw, int nt) {
+  constexpr int TS = CT / SEG, MPW = 32 / SEG;
+  const int lane = threadIdx.x & 31;
+  const int n = (threadIdx.x >> 5) * MPW + lane % MPW, seg = lane / MPW;
+  const int t0 = seg * TS;
+  float2 A = make_float2(1.f, 0.f), b = make_float2(0.f, 0.f);  // c_start = A c_end + b
+#pragma unroll
+  for (int i = TS - 1; i >= 0; --i) {
+    const int t = t0 + i;
+    if (t < nt) {
+      const float2 l = lam[t * hw + n];
+      const float2 g = gs[t * hw + n];
+      const float2 G = make_float2(g.x + b.x, g.y + b.y);
+      b = make_float2(l.x * G.x + l.y * G.y, l.x * G.y - l.y * G.x);
+      A = make_float2(l.x * A.x + l.y * A.y, l.x * A.y - l.y * A.x);
+    }
+  }
+  // Inclusive maps over segments seg .. SEG-1: (A, b) o (An, bn) = (A An, A bn + b).
+#pragma unroll
+  for (int off = 1; off < SEG; off <<= 1) {
+    const float anr = __shfl_down_sync(0xffffffffu, A.x, off * MPW);
+    const float ani = __shfl_down_sync(0xffffffffu, A.y, off * MPW);
+    const float bnr = __shfl_down_sync(0xffffffffu, b.x, off * MPW);
+    const float bni = __shfl_down_sync(0xffffffffu, b.y, off * MPW);
+    if (seg + off < SEG) {
+      const float2 nb = cmul(A, make_float2(bnr, bni));
+      b = make_float2(nb.x + b.x, nb.y + b.y);
+      A = cmul(A, make_float2(anr, ani));
+    }
+  }
+  const float2 c0 = cadj[n];
+  const float enr = __shfl_down_sync(0xffffffffu, A.x, MPW);
+  const float eni = __shfl_down_sync(0xffffffffu, A.y, MPW);
+  const float ebr = __shfl_down_sync(0xffffffffu, b.x, MPW);
+  const float ebi = __shfl_down_sync(0xffffffffu, b.y, MPW);
+  float2 c = c0;
+  if (seg < SEG - 1) {
+    c = cmul(make_float2(enr, eni), c0);
+    c.x += ebr;
+    c.y += ebi;
+  }
+#pragma unroll
+  for (int i = TS - 1; i >= 0; --i) {
+    const int t = t0 + i;
+    if (t < nt) {
+      const float2 l = lam[t * hw + n];
+      const float2 g = gs[t * hw + n];
+      const float2 G = make_float2(g.x + c.x, g.y + c.y);
+      gs[t * hw + n] = G;
+      c = make_float2(l.x * G.x + l.y * G.y, l.x * G.y - l.y * G.x);
+    }
+  }
+  __syncwarp();
+  if (seg == 0) {
+    const float2 e = cmul(A, c0);
+    cadj[n] = make_float2(e.x + b.x, e.y + b.y);
+  }
+}
+
+struct BLay {
+  int Btr, Bti, Bnr, Bni, Cfr, Cfi, Ef, Co, Dp, prm, cin, cadj;
+  int stg[2], dys[2], sml[2];
+  int lam, gn, braw, hs, gs, db, sr, dr, red;
+  int xw, btw, ctw, dyw;
+  int total;
+};
+
+__host__ __device__ inline BLay make_blay(int R, bool env, int es) {
+  constexpr int NH = kB_NH, FH = kB_FH, CT = kB_CT, HW = kB_HW;
+  BLay l = {};
+  int o = 0;
+  auto take = [&](int n) {
+    const int at = o;
+    o += al4(n);
+    return at;
+  };
+  l.Btr = take(FH * NH);
+  l.Bti = take(FH * NH);
+  l.Bnr = take(NH * FH);
+  l.Bni = take(NH * FH);
+  l.Cfr = take(FH * NH);
+  l.Cfi = take(FH * NH);
+  l.Ef = env ? take(FH * NH) : -1;
+  l.Co = take(R * FH);
+  l.Dp = take(FH);
+  l.prm = take(3 * NH);
+  l.cin = take(2 * NH);
+  l.cadj = take(2 * NH);
+  const int pad = 16 / es;
+  l.xw = FH + pad;
+  l.btw = R > 0 ? R * NH + pad : 0;
+  l.ctw = R > 0 ? 2 * R * NH + pad : 0;
+  l.dyw = FH + 4;
+  for (int b = 0; b < 2; ++b) l.stg[b] = take((CT * (l.xw + l.btw + l.ctw) * es + 3) / 4);
+  for (int b = 0; b < 2; ++b) l.dys[b] = take(CT * l.dyw);
+  for (int b = 0; b < 2; ++b) l.sml[b] = take(CT * (3 + 2 * R));
+  l.lam = take(CT * HW * 2);
+  l.gn = take(CT * HW * 2);
+  l.braw = take(CT * HW * 2);
+  l.hs = take((CT + 1) * HW * 2);
+  l.gs = take(CT * HW * 2);
+  l.db = take(CT * HW * 2);
+  l.sr = take(CT * R);
+  l.dr = take(CT * R);
+  l.red = take(3 * NH * (kT / 8));
+  l.total = o;
+  return l;
+}
+
+template <bool BF16, int RK>
+__global__ void __launch_bounds__(kT) mimo_layer_bwd16_kernel(const LParams p) {
+  using T = typename std::conditional<BF16, __nv_bfloat16, float>::type;
+  constexpr int NH = kB_NH, FH = kB_FH, CT = kB_CT, HW = kB_HW, R = RK;
+  extern __shared__ float4 smem4[];
+  float* sm = reinterpret_cast<float*>(smem4);
+  const bool env = p.envelope != 0, det = p.detune != 0;
+  const BLay l = make_blay(R, env, (int)sizeof(T));
+  const int64_t s = blockIdx.x / p.H;
+  const int h = (int)(blockIdx.x % p.H);
+  const int tid = threadIdx.x;
+  const int L = (int)p.L;
+  const int64_t Fd = p.H * p.Fh;
+  const Cols cols = cols_of(p, h);
+  // Head parameters in the storage orders the loops read.
+  for (int i = tid; i < NH * FH; i += kT) {
+    const int n = i / FH, f = i % FH;
+    const float2 bv = reinterpret_cast<const float2*>(p.B)[((int64_t)h * NH + n) * FH + f];
+    sm[l.Btr + f * NH + n] = bv.x;
+    sm[l.Bti + f * NH + n] = bv.y;
+    sm[l.Bnr + n * FH + f] = bv.x;
+    sm[l.Bni + n * FH + f] = bv.y;
+    const int f2 = i / NH, n2 = i % NH;
+    const float2 cv = reinterpret_cast<const float2*>(p.C)[((int64_t)h * FH + f2) * NH + n2];
+    sm[l.Cfr + f2 * NH + n2] = cv.x;
+    sm[l.Cfi + f2 * NH + n2] = cv.y;
+    if (env) sm[l.Ef + f2 * NH + n2] = p.env[((int64_t)h * FH + f2) * NH + n2];
+  }
+  for (int i = tid; i < R * FH; i += kT) sm[l.Co + i] = p.cout[(int64_t)h * R * FH + i];
+  for (int i = tid; i < FH; i += kT) sm[l.Dp + i] = p.D[(int64_t)h * FH + i];
+  for (int n = tid; n < NH; n += kT) {
+    sm[l.prm + n] = expf(p.A_log[(int64_t)h * NH + n]);
+    sm[l.prm + NH + n] = p.omega[(int64_t)h * NH + n];
+    sm[l.prm + 2 * NH + n] = det ? p.sdet[(int64_t)h * NH + n] : 1.f;
+    reinterpret_cast<float2*>(sm + l.cadj)[n] = make_float2(0.f, 0.f);
+  }
+  float2* lam = reinterpret_cast<float2*>(sm + l.lam);
+  float2* gn = reinterpret_cast<float2*>(sm + l.gn);
+  float2* braw = reinterpret_cast<float2*>(sm + l.braw);
+  float2* hs = reinterpret_cast<float2*>(sm + l.hs);
+  float2* gs = reinterpret_cast<float2*>(sm + l.gs);
+  float2* db = reinterpret_cast<float2*>(sm + l.db);
+  float2* cin = reinterpret_cast<float2*>(sm + l.cin);
+  float2* cadj = reinterpret_cast<float2*>(sm + l.cadj);
+
+  // Thread roles (fixed for the whole kernel).
+  const int tA = tid / 8, npA = tid % 8;        // (token, mode pair) items
+  const int nB = tid / 8, fqB = tid % 8;        // dB items (mode, 4 channels)
+  const int fC = tid / 4, nqC = tid % 4;        // dC / denv items (channel, 4 modes)
+  const int rO = tid / FH, fO = tid % FH;       // dcout items (rank, channel) when R = 4
+  float acc_a[2] = {0.f, 0.f}, acc_om[2] = {0.f, 0.f}, acc_sd[2] = {0.f, 0.f};
+  float aBr[4] = {}, aBi[4] = {}, aCr[4] = {}, aCi[4] = {}, aE[4] = {};
+  float aO = 0.f, aD = 0.f;
+
+  const int nck = p.nck;
+  float pre[kPre];
+  auto stage = [&](int k, int b) {
+    const int t0 = k * CT, nt = min(CT, L - t0);
+    T* xs = reinterpret_cast<T*>(sm + l.stg[b]);
+    const int64_t row0 = s * p.L + t0;
+    stage_segment<T>(xs, l.xw, reinterpret_cast<const T*>(p.x), row0, Fd, (int64_t)h * FH, FH, nt,
+                     (p.vec & 1) != 0);
+    if (R > 0) {
+      stage_segment<T>(xs + CT * l.xw, l.btw, reinterpret_cast<const T*>(p.proj), row0, p.P, cols.bt,
+                       R * NH, nt, (p.vec & 2) != 0);
+      stage_segment<T>(xs + CT * (l.xw + l.btw), l.ctw, reinterpret_cast<const T*>(p.proj), row0, p.P,
+                       cols.ct, 2 * R * NH, nt, (p.vec & 2) != 0);
+    }
+    stage_segment<float>(sm + l.dys[b], l.dyw, p.dy, row0, Fd, (int64_t)h * FH, FH, nt, (p.vec & 4) != 0);
+  };
+  if (nck > 0) {
+    const int k = nck - 1, nt = min(CT, L - k * CT);
+    stage(k, 0);
+    load_small<BF16, RK>(p, s, h, k * CT, nt, pre);
+    store_small<RK, CT>(p, sm + l.sml[0], nt, pre);
+  }
+  cp_async_commit();
+  int b = 0;
+  for (int k = nck - 1; k >= 0; --k, b ^= 1) {
+    const int t0 = k * CT, nt = min(CT, L - t0);
+    cp_async_wait_all();
+    __syncthreads();
+    if (k > 0) {
+      stage(k - 1, b ^ 1);
+      load_small<BF16, RK>(p, s, h, (k - 1) * CT, CT, pre);
+    }
+    cp_async_commit();
+    const T* xs = reinterpret_cast<const T*>(sm + l.stg[b]);
+    const T* bts = xs + CT * l.xw;
+    const T* cts = bts + CT * l.btw;
+    const float* dys = sm + l.dys[b];
+    const float* sml = sm + l.sml[b];
+    const float* raws = sml;
+    const float* dnus = sml + CT;
+    const float* dths = sml + 2 * CT;
+    const float* sbs = sml + 3 * CT;
+    const float* scs = sbs + CT * R;
+    const int xw = l.xw, btw = l.btw, ctw = l.ctw, dyw = l.dyw;
+
+    // A. Poles, gains, raw and gained drive per (token, mode pair); entry state.
+    if (tid < NH) {
+      const float2 c = reinterpret_cast<const float2*>(p.ckpt)[((s * nck + k) * p.H + h) * NH + tid];
+      cin[tid] = c;
+      hs[tid] = c;
+    }
+    if (tA < nt) {
+      const int t = tA, na = 2 * npA;
+      float br0 = 0.f, bi0 = 0.f, br1 = 0.f, bi1 = 0.f;
+#pragma unroll 8
+      for (int f = 0; f < FH; ++f) {
+        const float xv = static_cast<float>(xs[t * xw + f]);
+        const float2 brp = *reinterpret_cast<const float2*>(sm + l.Btr + f * NH + na);
+        const float2 bip = *reinterpret_cast<const float2*>(sm + l.Bti + f * NH + na);
+        br0 = fmaf(brp.x, xv, br0);
+        bi0 = fmaf(bip.x, xv, bi0);
+        br1 = fmaf(brp.y, xv, br1);
+        bi1 = fmaf(bip.y, xv, bi1);
+      }
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        const float sbv = sbs[t * R + r];
+        br0 = fmaf(sbv, static_cast<float>(bts[t * btw + r * NH + na]), br0);
+        br1 = fmaf(sbv, static_cast<float>(bts[t * btw + r * NH + na + 1]), br1);
+      }
+#pragma unroll
+      for (int dn = 0; dn < 2; ++dn) {
+        const int n = na + dn;
+        const float brv = dn ? br1 : br0, biv = dn ? bi1 : bi0;
+        const MDisc d = mdisc(p.gain, sm[l.prm + n], sm[l.prm + NH + n], sm[l.prm + 2 * NH + n], det,
+                              dnus[t], dths[t]);
+        lam[t * HW + n] = make_float2(d.lre, d.lim);
+        gn[t * HW + n] = make_float2(d.gr, d.gi);
+        braw[t * HW + n] = make_float2(brv, biv);
+        gs[t * HW + n] = make_float2(d.gr * brv - d.gi * biv, d.gr * biv + d.gi * brv);
+      }
+    }
+    __syncthreads();
+    // B. States of the chunk (rows 1..nt of hs) from the checkpoint.
+    chunk_scan<kB_SEG, CT>(lam, gs, hs + HW, cin, NH, HW, nt);
+    __syncthreads();
+    // C. Rank read and its adjoint per (token, rank).
+    if (R > 0) {
+      if (tid < nt * R) {
+        const int t = tid / R, r = tid % R;
+        const T* cr = cts + t * ctw + r * 2 * NH;
+        float rd = 0.f;
+#pragma unroll
+        for (int n = 0; n < NH; ++n) {
+          const float2 hv = hs[(t + 1) * HW + n];
+          rd = fmaf(static_cast<float>(cr[n]), hv.x, fmaf(-static_cast<float>(cr[NH + n]), hv.y, rd));
+        }
+        float dyc = 0.f;
+#pragma unroll 8
+        for (int f = 0; f < FH; ++f) dyc = fmaf(dys[t * dyw + f], sm[l.Co + r * FH + f], dyc);
+        const float scv = scs[t * R + r];
+        sm[l.sr + tid] = scv * rd;
+        sm[l.dr + tid] = scv * dyc;
+        st<BF16>(p.dproj, (s * p.L + t0 + t) * p.P + cols.sc + r, rd * dyc);
+      }
+      __syncthreads();
+    }
+    // D. Readout adjoint g per (token, mode pair), and the c_t gradient.
+    if (tA < nt) {
+      const int t = tA, na = 2 * npA;
+      float g0r = 0.f, g0i = 0.f, g1r = 0.f, g1i = 0.f, e0 = 0.f, e1 = 0.f;
+#pragma unroll 8
+      for (int f = 0; f < FH; ++f) {
+        const float dv = dys[t * dyw + f];
+        const float2 cr = *reinterpret_cast<const float2*>(sm + l.Cfr + f * NH + na);
+        const float2 ci = *reinterpret_cast<const float2*>(sm + l.Cfi + f * NH + na);
+        g0r = fmaf(dv, cr.x, g0r);
+        g0i = fmaf(-dv, ci.x, g0i);
+        g1r = fmaf(dv, cr.y, g1r);
+        g1i = fmaf(-dv, ci.y, g1i);
+        if (env) {
+          const float2 ev = *reinterpret_cast<const float2*>(sm + l.Ef + f * NH + na);
+          e0 = fmaf(dv, ev.x, e0);
+          e1 = fmaf(dv, ev.y, e1);
+        }
+      }
+      const float2 h0 = hs[(t + 1) * HW + na], h1 = hs[(t + 1) * HW + na + 1];
+      if (env) {
+        g0r = fmaf(2.f * e0, h0.x, g0r);
+        g0i = fmaf(2.f * e0, h0.y, g0i);
+        g1r = fmaf(2.f * e1, h1.x, g1r);
+        g1i = fmaf(2.f * e1, h1.y, g1i);
+      }
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        const float drv = sm[l.dr + t * R + r];
+        const T* cr = cts + t * ctw + r * 2 * NH;
+        g0r = fmaf(drv, static_cast<float>(cr[na]), g0r);
+        g1r = fmaf(drv, static_cast<float>(cr[na + 1]), g1r);
+        g0i = fmaf(-drv, static_cast<float>(cr[NH + na]), g0i);
+        g1i = fmaf(-drv, static_cast<float>(cr[NH + na + 1]), g1i);
+        const int64_t row = (s * p.L + t0 + t) * p.P + cols.ct + (int64_t)r * 2 * NH;
+        st<BF16>(p.dproj, row + na, drv * h0.x);
+        st<BF16>(p.dproj, row + na + 1, drv * h1.x);
+        st<BF16>(p.dproj, row + NH + na, -drv * h0.y);
+        st<BF16>(p.dproj, row + NH + na + 1, -drv * h1.y);
+      }
+      gs[t * HW + na] = make_float2(g0r, g0i);
+      gs[t * HW + na + 1] = make_float2(g1r, g1i);
+    }
+    __syncthreads();
+    // E. Adjoint scan: G over g, carry across chunks in cadj.
+    chunk_scan_rev<kB_SEG, CT>(lam, gs, cadj, HW, nt);
+    __syncthreads();
+    // F. Through the gain and the pole per (token, mode pair).
+    {
+      float sdnu = 0.f, sdth = 0.f;
+      if (tA < nt) {
+        const int t = tA;
+#pragma unroll
+        for (int dn = 0; dn < 2; ++dn) {
+          const int n = 2 * npA + dn;
+          const float a = sm[l.prm + n], om = sm[l.prm + NH + n], sd = sm[l.prm + 2 * NH + n];
+          const float dnu = dnus[t], dth = dths[t];
+          const MDisc d = mdisc(p.gain, a, om, sd, det, dnu, dth);
+          const float2 G = gs[t * HW + n], bv = braw[t * HW + n], hp = hs[t * HW + n];
+          db[t * HW + n] = make_float2(d.gr * G.x + d.gi * G.y, d.gr * G.y - d.gi * G.x);
+          const float dgr = bv.x * G.x + bv.y * G.y, dgi = bv.x * G.y - bv.y * G.x;
+          const float dlre = G.x * hp.x + G.y * hp.y, dlim = G.y * hp.x - G.x * hp.y;
+          float P = dlre * d.lre + dlim * d.lim;
+          const float d_th = dlim * d.lre - dlre * d.lim;
+          float d_dnu = 0.f, da_extra = 0.f, dbase_extra = 0.f;
+          if (p.gain == SEMX_GAIN_GAMMA) {
+            const float nu2 = d.nu * d.nu;
+            P -= ((1.f - nu2) >= 1e-6f) ? dgr * nu2 * d.rs : 0.f;
+          } else if (p.gain == SEMX_GAIN_MAMBA) {
+            d_dnu = dgr;
+          } else if (p.gain == SEMX_GAIN_ZOH) {
+            d_dnu = dgr * d.lre + dgi * d.lim;
+            const float pr = dnu * d.lre - d.gr, pi = dnu * d.lim - d.gi;
+            const float qr = (d.base * pi - a * pr) * d.inv_den;
+            const float qi = -(a * pi + d.base * pr) * d.inv_den;
+            da_extra = -(dgr * qr + dgi * qi);
+            dbase_extra = dgi * qr - dgr * qi;
+          }
+          d_dnu += d_th * d.base - a * P;
+          const float dbase = d_th * dnu + dbase_extra;
+          sdnu += d_dnu;
+          sdth += det ? dbase * sd : dbase;
+          acc_a[dn] += da_extra - dnu * P;
+          acc_om[dn] += dbase;
+          acc_sd[dn] += det ? dbase * dth : 0.f;
+        }
+      }
+      // Per-token sums over the 8 mode pairs (consecutive lanes), fixed order.
+#pragma unroll
+      for (int m = 1; m < 8; m <<= 1) {
+        sdnu += __shfl_xor_sync(0xffffffffu, sdnu, m);
+        sdth += __shfl_xor_sync(0xffffffffu, sdth, m);
+      }
+      if (npA == 0 && tA < nt) {
+        const int64_t row = (s * p.L + t0 + tA) * p.P;
+        st<BF16>(p.dproj, row + cols.dnu, sdnu * p.rs * semx::softplus_grad(raws[tA]));
+        st<BF16>(p.dproj, row + cols.dth, sdth);
+      }
+    }
+    __syncthreads();
+    // G. dx = B^H d(raw drive) + D dy per (token, 4 channels).
+    if (tA < nt) {
+      const int t = tA, f0 = 4 * npA;
+      float4 acc;
+      acc.x = sm[l.Dp + f0] * dys[t * dyw + f0];
+      acc.y = sm[l.Dp + f0 + 1] * dys[t * dyw + f0 + 1];
+      acc.z = sm[l.Dp + f0 + 2] * dys[t * dyw + f0 + 2];
+      acc.w = sm[l.Dp + f0 + 3] * dys[t * dyw + f0 + 3];
+#pragma unroll 4
+      for (int n = 0; n < NH; ++n) {
+        const float2 g = db[t * HW + n];
+        const float4 br = *reinterpret_cast<const float4*>(sm + l.Bnr + n * FH + f0);
+        const float4 bi = *reinterpret_cast<const float4*>(sm + l.Bni + n * FH + f0);
+        acc.x = fmaf(br.x, g.x, fmaf(bi.x, g.y, acc.x));
+        acc.y = fmaf(br.y, g.x, fmaf(bi.y, g.y, acc.y));
+        acc.z = fmaf(br.z, g.x, fmaf(bi.z, g.y, acc.z));
+        acc.w = fmaf(br.w, g.x, fmaf(bi.w, g.y, acc.w));
+      }
+      float* dxr = p.dx + (s * p.L + t0 + t) * Fd + (int64_t)h * FH + f0;
+      if ((p.vec & 8) != 0) {
+        *reinterpret_cast<float4*>(dxr) = acc;
+      } else {
+        dxr[0] = acc.x; dxr[1] = acc.y; dxr[2] = acc.z; dxr[3] = acc.w;
+      }
+    }
+    // H. Rank write: d s_b, d b_t.
+    if (R > 0 && tid < nt * R) {
+      const int t = tid / R, r = tid % R;
+      const float sbv = sbs[t * R + r];
+      const int64_t row = (s * p.L + t0 + t) * p.P;
+      float acc = 0.f;
+#pragma unroll
+      for (int n = 0; n < NH; ++n) {
+        const float g = db[t * HW + n].x;
+        acc = fmaf(static_cast<float>(bts[t * btw + r * NH + n]), g, acc);
+        st<BF16>(p.dproj, row + cols.bt + r * NH + n, sbv * g);
+      }
+      st<BF16>(p.dproj, row + cols.sb + r, acc);
+    }
+    // I. Parameter sums over the chunk, fixed ownership.
+    for (int t = 0; t < nt; ++t) {
+      {  // dB[nB, 4 fqB .. +3] += x[t, f] conj-free d(raw drive)[t, nB]
+        const float2 g = db[t * HW + nB];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float xv = static_cast<float>(xs[t * xw + 4 * fqB + j]);
+          aBr[j] = fmaf(xv, g.x, aBr[j]);
+          aBi[j] = fmaf(xv, g.y, aBi[j]);
+        }
+      }
+      {  // dC[fC, 4 nqC .. +3] += dy (h_re, -h_im); denv += dy |h|^2
+        const float dv = dys[t * dyw + fC];
+        const float4 ha = *reinterpret_cast<const float4*>(hs + (t + 1) * HW + 4 * nqC);
+        const float4 hb = *reinterpret_cast<const float4*>(hs + (t + 1) * HW + 4 * nqC + 2);
+        const float hr[4] = {ha.x, ha.z, hb.x, hb.z}, hi[4] = {ha.y, ha.w, hb.y, hb.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          aCr[j] = fmaf(dv, hr[j], aCr[j]);
+          aCi[j] = fmaf(-dv, hi[j], aCi[j]);
+          if (env) aE[j] = fmaf(dv, hr[j] * hr[j] + hi[j] * hi[j], aE[j]);
+        }
+      }
+      if (R > 0) aO = fmaf(sm[l.sr + t * R + rO], dys[t * dyw + fO], aO);
+      if (tid < FH) aD = fmaf(dys[t * dyw + tid], static_cast<float>(xs[t * xw + tid]), aD);
+    }
+    // Small operands of the next chunk (its buffer was last read two chunks ago).
+    if (k > 0) store_small<RK, CT>(p, sm + l.sml[b ^ 1], CT, pre);
+  }
+  __syncthreads();
+  // Per-mode sums over the 16 token lanes that share a mode pair, fixed order.
+  float* red = sm + l.red;  // [3][NH][kT / 8]
+#pragma unroll
+  for (int dn = 0; dn < 2; ++dn) {
+    const int n = 2 * npA + dn;
+    red[(0 * NH + n) * (kT / 8) + tA] = acc_a[dn];
+    red[(1 * NH + n) * (kT / 8) + tA] = acc_om[dn];
+    red[(2 * NH + n) * (kT / 8) + tA] = acc_sd[dn];
+  }
+  __syncthreads();
+  // Partial row of sequence s: [dB | dC | denv | dcout | dD | dA_log | domega | ddetune].
+  const int64_t H = p.H;
+  float* row = p.part + s * p.K;
+  int64_t off = 0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int64_t i = ((int64_t)h * NH + nB) * FH + 4 * fqB + j;
+    row[off + 2 * i] = aBr[j];
+    row[off + 2 * i + 1] = aBi[j];
+  }
+  off += H * NH * FH * 2;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int64_t i = ((int64_t)h * FH + fC) * NH + 4 * nqC + j;
+    row[off + 2 * i] = aCr[j];
+    row[off + 2 * i + 1] = aCi[j];
+  }
+  off += H * FH * NH * 2;
+  if (env) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) row[off + ((int64_t)h * FH + fC) * NH + 4 * nqC + j] = aE[j];
+    off += H * FH * NH;
+  }
+  if (R > 0) {
+    row[off + (int64_t)h * R * FH + rO * FH + fO] = aO;
+    off += H * R * FH;
+  }
+  if (tid < FH) row[off + (int64_t)h * FH + tid] = aD;
+  off += H * FH;
+  if (tid < 3 * NH) {
+    const int which = tid / NH, n = tid % NH;
+    float acc = 0.f;
+    for (int q = 0; q < kT / 8; ++q) acc += red[(which * NH + n) * (kT / 8) + q];
+    if (which == 0) acc *= sm[l.prm + n];  // d/dA_log = a d/da
+    row[off + which * H * NH + (int64_t)h * NH + n] = acc;
+  }
+}
+
 // ------------------------------------------------------------------------ host side
 int64_t proj_width(const SemxMimoLayerArgs* a) {
   return 2 * a->H + (a->rank > 0 ? 2 * a->H * a->rank + 3 * a->H * a->rank * a->Nh : 0);
@@ -945,7 +1449,11 @@ int64_t part_row(const SemxMimoLayerArgs* a) {
   return H * (4 * Nh * Fh + (a->envelope ? Fh * Nh : 0) + R * Fh + Fh + 3 * Nh);
 }
 
+// The backward of 16-mode, 32-channel heads of rank 0 or 4 has its own kernel.
+bool bwd16(const SemxMimoLayerArgs* a) { return a->Nh == 16 && a->Fh == 32 && (a->rank == 0 || a->rank == 4); }
+
 size_t layer_smem(const SemxMimoLayerArgs* a, bool bwd) {
+  if (bwd && bwd16(a)) return (size_t)make_blay(a->rank, a->envelope != 0, a->bf16 ? 2 : 4).total * sizeof(float);
   if (!bwd)
     return (size_t)make_flay((int)a->Nh, (int)a->Fh, a->rank, a->envelope != 0, a->bf16 ? 2 : 4).total *
            sizeof(float);
@@ -959,7 +1467,9 @@ int vec_flags(const SemxMimoLayerArgs* a) {
   const bool vx = semx::aligned(a->x, 16) && (H * Fh * es) % 16 == 0 && (Fh * es) % 16 == 0;
   const bool vp = semx::aligned(a->proj, 16) && (P * es) % 16 == 0 && ((2 * H + H * R) * es) % 16 == 0 &&
                   ((R * Nh * es) % 16) == 0 && ((2 * H + 2 * H * R + H * R * Nh) * es) % 16 == 0;
-  return (vx ? 1 : 0) | (vp ? 2 : 0);
+  const bool vdy = semx::aligned(a->dy, 16) && (H * Fh * 4) % 16 == 0 && (Fh * 4) % 16 == 0;
+  const bool vdx = semx::aligned(a->dx, 16) && (H * Fh * 4) % 16 == 0 && (Fh * 4) % 16 == 0;
+  return (vx ? 1 : 0) | (vp ? 2 : 0) | (vdy ? 4 : 0) | (vdx ? 8 : 0);
 }
 
 // Segments per mode of the forward's parallel chunk scan (1: one thread per mode).
@@ -1011,6 +1521,7 @@ LParams to_lparams(const SemxMimoLayerArgs* a) {
   p.detune = a->detune ? 1 : 0;
   p.envelope = a->envelope ? 1 : 0;
   p.nchunks = (int)semx::cdiv(a->L, kTC);
+  p.nck = (int)semx::cdiv(a->L, kCk);
   p.rs = a->rate_scale;
   p.x = a->x; p.proj = a->proj;
   p.A_log = a->A_log; p.omega = a->omega; p.sdet = a->detune_gain; p.B = a->B; p.C = a->C; p.D = a->D;
@@ -1036,7 +1547,7 @@ size_t semx_mimo_layer_args_size(void) { return sizeof(SemxMimoLayerArgs); }
 
 size_t semx_mimo_layer_ckpt_bytes(const SemxMimoLayerArgs* a) {
   if (a == nullptr || a->S < 0 || a->L < 0 || a->H < 0 || a->Nh < 0) return 0;
-  return (size_t)a->S * (size_t)semx::cdiv(a->L, kTC) * (size_t)(a->H * a->Nh) * 2 * sizeof(float);
+  return (size_t)a->S * (size_t)semx::cdiv(a->L, kCk) * (size_t)(a->H * a->Nh) * 2 * sizeof(float);
 }
 
 size_t semx_mimo_layer_workspace_bytes(const SemxMimoLayerArgs* a) {
@@ -1096,8 +1607,17 @@ int semx_mimo_layer_bwd(const SemxMimoLayerArgs* a, semx_stream_t stream) {
   p.part = ws;
   if (a->L > 0) {
     const size_t smem = layer_smem(a, true);
-    rc = a->bf16 ? launch_layer(mimo_layer_bwd_kernel<true>, p, smem, st, "mimo_layer_bwd_kernel")
-                 : launch_layer(mimo_layer_bwd_kernel<false>, p, smem, st, "mimo_layer_bwd_kernel");
+    if (bwd16(a)) {
+      if (a->rank == 4)
+        rc = a->bf16 ? launch_layer(mimo_layer_bwd16_kernel<true, 4>, p, smem, st, "mimo_layer_bwd16_kernel")
+                     : launch_layer(mimo_layer_bwd16_kernel<false, 4>, p, smem, st, "mimo_layer_bwd16_kernel");
+      else
+        rc = a->bf16 ? launch_layer(mimo_layer_bwd16_kernel<true, 0>, p, smem, st, "mimo_layer_bwd16_kernel")
+                     : launch_layer(mimo_layer_bwd16_kernel<false, 0>, p, smem, st, "mimo_layer_bwd16_kernel");
+    } else {
+      rc = a->bf16 ? launch_layer(mimo_layer_bwd_kernel<true>, p, smem, st, "mimo_layer_bwd_kernel")
+                   : launch_layer(mimo_layer_bwd_kernel<false>, p, smem, st, "mimo_layer_bwd_kernel");
+    }
     if (rc != SEMX_OK) return rc;
   } else {
     cudaMemsetAsync(ws, 0, (size_t)a->S * p.K * sizeof(float), st);

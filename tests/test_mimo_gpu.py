@@ -137,6 +137,9 @@ _LAYER_CASES = [
     (dict(in_features=16, state_dim=32, n_heads=2, rank=4, input_gain="mamba", envelope_readout=True), 1, 40),
     (dict(in_features=8, state_dim=8, n_heads=1, rank=1, input_gain="none", envelope_readout=True,
           mode_detune=True, n_real_modes=2), 3, 5),
+    (dict(in_features=64, state_dim=32, n_heads=2, rank=0, input_gain="zoh", envelope_readout=True,
+          mode_detune=True), 2, 37),
+    (dict(in_features=64, state_dim=32, n_heads=2, rank=4, input_gain="mamba", envelope_readout=True), 1, 50),
     (dict(in_features=256, state_dim=128, n_heads=8, rank=4, input_gain="gamma"), 2, 37),
 ]
 

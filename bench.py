@@ -437,7 +437,7 @@ class MimoPass:
 
     fwd_bytes_per_unit = 4768
     bwd_bytes_per_unit = 8512
-    kernels = ("mimo_fwd_kernel", "mimo_bwd_kernel")
+    kernels = ("mimo_layer_fwd_kernel", "mimo_layer_bwd16_kernel")
 
     def __init__(self, layer, S, L, seed, device):
         g = torch.Generator(device=device).manual_seed(seed)
@@ -466,7 +466,7 @@ class MimoKernelPass:
     workload. Bytes per token: fwd x + proj (bf16) in, y (fp32) out = 4768; bwd x, proj
     (bf16), dy (fp32) in, dx (fp32), dproj (bf16) out = 9024."""
 
-    kernels = ("mimo_layer_fwd_kernel", "mimo_layer_bwd_kernel")
+    kernels = ("mimo_layer_fwd_kernel", "mimo_layer_bwd16_kernel")
 
     def __init__(self, layer, S, L, seed, device):
         from semambaxlinoss_b200 import _lib

@@ -589,7 +589,10 @@ __global__ void __launch_bounds__(kThreads) slru_bwd_kernel(const SParams p) {
       }
       float* buf = tiles + bsel * T::kBuf;
 
-      if (E.p1) {  // Pass 1: recurrence from the checkpoint, state every kR steps kept.
+      if (E.p1 && K == kR) {  // the checkpoint is the chunk's only sub-block start
+        sub[tid] = make_float4(hr[0], hr[1], hr[2], hr[3]);
+        if (!REAL) sub[kThreads + tid] = make_float4(hi[0], hi[1], hi[2], hi[3]);
+      } else if (E.p1) {  // Pass 1: recurrence from the checkpoint, state every kR steps kept.
         for (int i = 0; i < E.nt; ++i) {
           const int t = E.t0 + i;
           if (((t - t0c) % kR) == 0) {

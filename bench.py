@@ -433,7 +433,11 @@ def _mimo_layer(device, seed):
 
 class MimoPass:
     """One SelectiveLRUMIMO layer pass (bf16 input, fp32 state): forward builds the graph,
-    backward runs it against a fixed upstream gradient."""
+    backward runs it against a fixed upstream gradient. Algorithmic bytes per token are
+    the layer's token I/O with the reference's 1616 projection columns (8 heads, rank 4):
+    fwd x + projections (bf16) in, y (fp32) out = 4768; bwd x, projections (bf16), dy
+    (fp32) in, dx, d projections (bf16) out = 8512. The static drive columns this
+    package adds to the projection GEMM are an implementation choice and not counted."""
 
     fwd_bytes_per_unit = 4768
     bwd_bytes_per_unit = 8512
@@ -462,9 +466,10 @@ class MimoPass:
 
 class MimoKernelPass:
     """The fused MIMO layer kernels alone (semx_mimo_layer_fwd / _bwd) on resident bf16
-    token operands (x and the projection rows), for the kernel roofline of the MIMO
-    workload. Bytes per token: fwd x + proj (bf16) in, y (fp32) out = 4768; bwd x, proj
-    (bf16), dy (fp32) in, dx (fp32), dproj (bf16) out = 9024."""
+    token operands (x and the projection rows, 1872 columns including the static drive),
+    for the kernel roofline of the MIMO workload. Bytes per token: fwd x + proj (bf16) in,
+    y (fp32) out = 5280; bwd x, proj (bf16), dy (fp32) in, dx (fp32), dproj (bf16) out =
+    10048."""
 
     kernels = ("mimo_layer_fwd_kernel", "mimo_layer_bwd16_kernel")
 
@@ -487,15 +492,15 @@ class MimoKernelPass:
         self.dx = torch.empty_like(self.y)
         self.dproj = torch.empty_like(self.proj)
         self.params = [t.detach().float().contiguous() for t in (
-            layer.A_log, layer.omega, layer.B, layer.C, layer.D, layer.c_out)]
+            layer.A_log, layer.omega, layer.C, layer.D, layer.c_out)]
         self.grads = [torch.empty_like(t) for t in self.params]
         a = _lib.new_args(_lib.SemxMimoLayerArgs)
         a.input_gain, a.rank, a.rate_scale, a.bf16 = _lib.GAIN_CODES["gamma"], R, 1.0, 1
         a.S, a.L, a.H, a.Nh, a.Fh = S, L, H, Nh, Fh
         a.x, a.proj, a.y, a.dy, a.dx, a.dproj = [t.data_ptr() for t in (
             self.x, self.proj, self.y, self.dy, self.dx, self.dproj)]
-        a.A_log, a.omega, a.B, a.C, a.D, a.c_out = [t.data_ptr() for t in self.params]
-        a.dA_log, a.domega, a.dB, a.dC, a.dD, a.dc_out = [t.data_ptr() for t in self.grads]
+        a.A_log, a.omega, a.C, a.D, a.c_out = [t.data_ptr() for t in self.params]
+        a.dA_log, a.domega, a.dC, a.dD, a.dc_out = [t.data_ptr() for t in self.grads]
         self.ckpt = _lib.empty_f32(self.lib.semx_mimo_layer_ckpt_bytes(ctypes.byref(a)), device)
         a.ckpt = self.ckpt.data_ptr()
         self.ws = _lib.empty_f32(self.lib.semx_mimo_layer_workspace_bytes(ctypes.byref(a)), device)

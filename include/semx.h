@@ -320,22 +320,28 @@ int semx_mimo_bwd(const SemxMimoArgs* args, semx_stream_t stream);
  * input x,
  *   dnu = softplus(proj[dnu_h]) * rate_scale,  dth = proj[dth_h]
  *   lam[n] = exp(dnu (-a[n] + j (omega[n] + (detune ? s[n] dth : dth)))),  a = exp(A_log)
- *   Bu[n]  = gain[n] (sum_f B[h,n,f] x[h*Fh+f] + sum_r s_b[r] b_t[r,n])   (B complex,
- *            the rank write real), gain per input_gain (GAMMA / MAMBA / ZOH / NONE)
+ *   Bu[n]  = gain[n] (bx[n] + sum_r s_b[r] b_t[r,n])   (bx complex: the static drive
+ *            sum_f B[h,n,f] x[h*Fh+f]; the rank write real), gain per input_gain
+ *            (GAMMA / MAMBA / ZOH / NONE)
  *   h_t    = lam h_{t-1} + Bu,  h_{-1} = 0
  *   y[f]   = sum_n Re(C[h,f,n] h[n]) + D[h*Fh+f] x[h*Fh+f]
  *            + sum_n env[h,f,n] |h[n]|^2                              (envelope only)
  *            + sum_r s_c[r] Re(sum_n c_t[r,n] h[n]) c_out[h*R+r, f]  (R > 0)
  * proj (S,L,P) columns: [dnu (H) | dth (H) | s_b (H*R) | b_t (H*R*Nh) | s_c (H*R) |
- * c_t (H*R*2Nh, per (h, r) Nh real parts then Nh imaginary parts)], P = 2H when R = 0.
+ * c_t (H*R*2Nh, per (h, r) Nh real parts then Nh imaginary parts) | bx (H*2Nh, per (h, n)
+ * the real then the imaginary part)], P = 2H + 2H*R + 3H*R*Nh + 2H*Nh. The static input
+ * map B (H,Nh,Fh,2) of the reference is therefore a block-diagonal part of the caller's
+ * projection weight (rows h*2Nh + 2n + {0: re, 1: im}, columns h*Fh .. h*Fh+Fh-1), and its
+ * gradients (dB, and B^H d(bx) in dx) come from the projection's backward: dproj's bx
+ * columns hold d(loss)/d(bx).
  * x: (S,L,H*Fh); x and proj are fp32, or bf16 when `bf16` is set; y, dy, dx fp32; dproj
- * has the dtype of proj. Parameters fp32: A_log, omega, detune_gain (H,Nh); B (H,Nh,Fh,2);
+ * has the dtype of proj. Parameters fp32: A_log, omega, detune_gain (H,Nh);
  * C (H,Fh,Nh,2); D (H*Fh); c_out (H*R,Fh); env_gain (H,Fh,Nh).
  * Replaces SelectiveLRUMIMO.forward after its projections
  * (models/selective_lru/selective_lru.py:488-587): poles, drive, gain, scan, readout and
  * feedthrough in one pass per (sequence, head). Training forwards store the state at
  * every 16-step block in ckpt (semx_mimo_layer_ckpt_bytes()). Backward recomputes from
- * ckpt and writes dx (the input-map and skip part), dproj and the parameter gradients
+ * ckpt and writes dx (the skip part D dy), dproj and the parameter gradients
  * (reduced over sequences in a fixed order; dA_log is with respect to A_log).
  * ---------------------------------------------------------------------------------- */
 typedef struct SemxMimoLayerArgs {
@@ -353,7 +359,6 @@ typedef struct SemxMimoLayerArgs {
   const float* A_log;
   const float* omega;
   const float* detune_gain;
-  const float* B;
   const float* C;
   const float* D;
   const float* c_out;
@@ -366,7 +371,6 @@ typedef struct SemxMimoLayerArgs {
   float* dA_log;
   float* domega;
   float* ddetune;
-  float* dB;
   float* dC;
   float* dD;
   float* dc_out;

@@ -132,11 +132,12 @@ def mimo_scan_readout(lam_re, lam_im, Bu_re, Bu_im, C_re, C_im, x, D, H, Nh, Fh)
     return y, h.real, h.imag
 
 
-def mimo_discretise(delta_nu, delta_theta, x, params: dict, cfg: dict, s_b=None, b_t=None):
+def mimo_discretise(delta_nu, delta_theta, x, params: dict, cfg: dict, s_b=None, b_t=None, bx=None):
     """Pole, drive and gain of ``SelectiveLRUMIMO.forward`` (selective_lru.py:502-546).
 
     delta_nu, delta_theta: (B,T,H) after softplus / rate scale; s_b (B,T,H,r) and b_t
-    (B,T,H,r,Nh) the rank-write projections (computed from x when not given). Returns
+    (B,T,H,r,Nh) the rank-write projections (computed from x when not given); bx
+    (B,T,H,Nh,2) the static drive B x (computed from x and B when not given). Returns
     (lam_re, lam_im, Bu_re, Bu_im) each (B,T,N)."""
     Bsz, T, Fdim = x.shape
     H, rank = cfg["n_heads"], cfg.get("rank", 0)
@@ -150,9 +151,12 @@ def mimo_discretise(delta_nu, delta_theta, x, params: dict, cfg: dict, s_b=None,
     theta = dnu_n * base
     lam_re = (nu * torch.cos(theta)).reshape(Bsz, T, N)
     lam_im = (nu * torch.sin(theta)).reshape(Bsz, T, N)
-    xh = x.view(Bsz, T, H, Fh)
-    Bu_re = torch.einsum("hnf,bthf->bthn", params["B"][..., 0], xh)
-    Bu_im = torch.einsum("hnf,bthf->bthn", params["B"][..., 1], xh)
+    if bx is None:
+        xh = x.view(Bsz, T, H, Fh)
+        Bu_re = torch.einsum("hnf,bthf->bthn", params["B"][..., 0], xh)
+        Bu_im = torch.einsum("hnf,bthf->bthn", params["B"][..., 1], xh)
+    else:
+        Bu_re, Bu_im = bx[..., 0], bx[..., 1]
     if rank > 0:
         if s_b is None:
             s_b = (x @ params["b_coef.weight"].t()).view(Bsz, T, H, rank)
@@ -177,11 +181,12 @@ def mimo_discretise(delta_nu, delta_theta, x, params: dict, cfg: dict, s_b=None,
     return lam_re, lam_im, Bu_re.reshape(Bsz, T, N), Bu_im.reshape(Bsz, T, N)
 
 
-def mimo_projection(params: dict, x, cfg: dict):
+def mimo_projection(params: dict, x, cfg: dict, drive: bool = False):
     """All token projections of ``SelectiveLRUMIMO`` as one row per token, in the column
     order [dnu_raw (H) | dth (H) | s_b (H r) | b_t (H r Nh) | s_c (H r) | c_t (H r 2Nh)]
     (dt_nu_proj / dt_theta_proj / b_coef / b_dir / c_coef / c_read of selective_lru.py:
-    494-498, 528-530, 578-579)."""
+    494-498, 528-530, 578-579), followed with ``drive`` by the static drive B x per
+    (head, mode) as [re, im] pairs (H 2Nh columns; selective_lru.py:516-517)."""
     ws = [params["dt_nu_proj.weight"], params["dt_theta_proj.weight"]]
     bs = [params["dt_nu_proj.bias"], params["dt_theta_proj.bias"]]
     if cfg.get("rank", 0) > 0:
@@ -189,12 +194,20 @@ def mimo_projection(params: dict, x, cfg: dict):
             w = params[k + ".weight"]
             ws.append(w)
             bs.append(w.new_zeros(w.shape[0]))
-    return x @ torch.cat(ws, 0).t() + torch.cat(bs)
+    proj = x @ torch.cat(ws, 0).t() + torch.cat(bs)
+    if not drive:
+        return proj
+    Bsz, T, Fdim = x.shape
+    H = cfg["n_heads"]
+    Nh, Fh = cfg["state_dim"] // H, Fdim // H
+    bx = torch.einsum("hnfc,bthf->bthnc", params["B"], x.view(Bsz, T, H, Fh))
+    return torch.cat([proj, bx.reshape(Bsz, T, 2 * H * Nh)], -1)
 
 
 def selective_lru_mimo_from_projection(proj, params: dict, x, cfg: dict, rate_scale=None):
     """``SelectiveLRUMIMO.forward`` (selective_lru.py:488-587) given the projection rows
-    of :func:`mimo_projection` (so a caller can fix their rounding, e.g. to bf16)."""
+    of :func:`mimo_projection` (so a caller can fix their rounding, e.g. to bf16); rows
+    that carry the drive columns use them in place of B x."""
     Bsz, T, Fdim = x.shape
     H, rank = cfg["n_heads"], cfg.get("rank", 0)
     Nh, Fh = cfg["state_dim"] // H, Fdim // H
@@ -213,7 +226,13 @@ def selective_lru_mimo_from_projection(proj, params: dict, x, cfg: dict, rate_sc
         s_c = proj[..., o:o + H * rank].reshape(Bsz, T, H, rank)
         o += H * rank
         cr = proj[..., o:o + 2 * H * rank * Nh].reshape(Bsz, T, H, rank, 2 * Nh)
-    lam_re, lam_im, Bu_re, Bu_im = mimo_discretise(delta_nu, delta_theta, x, params, cfg, s_b, b_t)
+    o = 2 * H + 2 * H * rank + 3 * H * rank * Nh
+    bx = None
+    if proj.shape[-1] == o + 2 * H * Nh:
+        bx = proj[..., o:].reshape(Bsz, T, H, Nh, 2)
+    elif proj.shape[-1] != o:
+        raise ValueError(f"projection rows of width {proj.shape[-1]}: expected {o} or {o + 2 * H * Nh}")
+    lam_re, lam_im, Bu_re, Bu_im = mimo_discretise(delta_nu, delta_theta, x, params, cfg, s_b, b_t, bx)
     y, h_re, h_im = mimo_scan_readout(
         lam_re, lam_im, Bu_re, Bu_im, params["C"][..., 0], params["C"][..., 1], x,
         params["D"], H, Nh, Fh,

@@ -8,7 +8,7 @@
 // head's token operands (x, the projection columns of the head) are staged in shared
 // memory, then:
 //   forward  1. per (t, n): pole lam and gain from (delta_nu, delta_theta), raw drive
-//               sum_f B[n,f] x[f] + sum_r s_b[r] b_t[r,n], gained drive;
+//               (B x)[n] + sum_r s_b[r] b_t[r,n], gained drive;
 //            2. per mode n (one thread each): h_t = lam h_{t-1} + Bu over the chunk;
 //            3. per (t, r): the rank read s_c Re(<c_t, h>);
 //            4. per (t, f): y = Re(C h) + D x + <env, |h|^2> + rank feedthrough.
@@ -18,9 +18,14 @@
 //            gradients (dx, dproj) are written directly; parameter gradients are summed
 //            per CTA in a fixed order, written as per-sequence partial rows and reduced
 //            over sequences by the two-stage column sum.
+// The static drive (B x)[n] of every head is a column pair of the projection rows: the
+// block-diagonal B is part of the input projection GEMM, so its forward product, its
+// x-gradient B^H d(drive) and its weight gradient run on the tensor cores in that GEMM
+// and its backward, and the layer kernels read and write the drive columns like the
+// other token operands (dproj of the drive = d(raw drive)).
 // Every parallel loop distributes (t, n) or (t, f) items so that a warp's shared-memory
-// reads of the per-head matrices are consecutive (both storage orders of B, C and
-// env_gain are kept where both access orders occur).
+// reads of the per-head matrices are consecutive (both storage orders of C and env_gain
+// are kept where both access orders occur).
 #include <cuda_bf16.h>
 
 #include <type_traits>
@@ -43,14 +48,14 @@ struct LParams {
   int64_t S, L, H, Nh, Fh, R, P;  // P = projection row width
   int gain, detune, envelope, nchunks;
   int nck;  // checkpoints: one per kCk tokens
-  int vec;  // 16-byte aligned rows: bit 0 x, bit 1 b_t / c_t, bit 2 dy, bit 3 dx
+  int vec;  // 16-byte aligned rows: bit 0 x, bit 1 b_t / c_t, bit 2 dy, bit 3 dx,
+            // bit 4 the drive columns (proj and dproj)
   float rs;
   const void* x;
   const void* proj;
   const float* A_log;
   const float* omega;
   const float* sdet;
-  const float* B;
   const float* C;
   const float* D;
   const float* cout;
@@ -66,8 +71,8 @@ struct LParams {
 
 // Shared-memory layout in floats (every offset a multiple of 4).
 struct Lay {
-  int Bt, Bn, Cn, Cf, En, Ef, Co, Dp, prm;
-  int xs, raw, dnu, dth, sb, bt, sc, ct;
+  int Cn, Cf, En, Ef, Co, Dp, prm;
+  int xs, bx, raw, dnu, dth, sb, bt, sc, ct;
   int lam, gn, bu, hs, sr;
   int dys, dr, gs, db, tn, acc;
   int total;
@@ -83,8 +88,6 @@ __host__ __device__ inline Lay make_lay(int Nh, int Fh, int R, bool bwd, bool en
     o += al4(n);
     return at;
   };
-  l.Bt = take(Fh * Nh * 2);
-  l.Bn = bwd ? take(Nh * Fh * 2) : -1;
   l.Cn = take(Nh * Fh * 2);
   l.Cf = bwd ? take(Fh * Nh * 2) : -1;
   l.En = env ? take(Nh * Fh) : -1;
@@ -93,6 +96,7 @@ __host__ __device__ inline Lay make_lay(int Nh, int Fh, int R, bool bwd, bool en
   l.Dp = take(Fh);
   l.prm = take(3 * Nh);
   l.xs = take(kTC * Fh);
+  l.bx = take(kTC * Nh * 2);
   l.raw = take(kTC);
   l.dnu = take(kTC);
   l.dth = take(kTC);
@@ -111,7 +115,7 @@ __host__ __device__ inline Lay make_lay(int Nh, int Fh, int R, bool bwd, bool en
     l.gs = take(kTC * Nh * 2);
     l.db = take(kTC * Nh * 2);
     l.tn = take(5 * kTC * Nh);
-    l.acc = take(Nh * Fh * 2 + Fh * Nh * 2 + (env ? Fh * Nh : 0) + R * Fh + Fh);
+    l.acc = take(Fh * Nh * 2 + (env ? Fh * Nh : 0) + R * Fh + Fh);
   } else {
     l.dys = l.dr = l.gs = l.db = l.tn = l.acc = -1;
   }
@@ -121,7 +125,7 @@ __host__ __device__ inline Lay make_lay(int Nh, int Fh, int R, bool bwd, bool en
 
 // Column offsets of head h's operands in a projection row.
 struct Cols {
-  int64_t dnu, dth, sb, bt, sc, ct;
+  int64_t dnu, dth, sb, bt, sc, ct, bx;
 };
 __device__ __forceinline__ Cols cols_of(const LParams& p, int h) {
   const int64_t H = p.H, R = p.R, Nh = p.Nh;
@@ -132,6 +136,7 @@ __device__ __forceinline__ Cols cols_of(const LParams& p, int h) {
   c.bt = 2 * H + H * R + (int64_t)h * R * Nh;
   c.sc = 2 * H + H * R + H * R * Nh + (int64_t)h * R;
   c.ct = 2 * H + 2 * H * R + H * R * Nh + (int64_t)h * R * 2 * Nh;
+  c.bx = 2 * H + 2 * H * R + 3 * H * R * Nh + (int64_t)h * 2 * Nh;
   return c;
 }
 
@@ -185,10 +190,6 @@ __device__ __forceinline__ MDisc mdisc(int gain, float a, float om, float sd, bo
 __device__ void load_head_params(const LParams& p, const Lay& l, float* sm, int h, bool bwd) {
   const int Nh = (int)p.Nh, Fh = (int)p.Fh, R = (int)p.R;
   for (int i = threadIdx.x; i < Nh * Fh; i += kT) {
-    const int n = i / Fh, f = i % Fh;
-    const float2 b = reinterpret_cast<const float2*>(p.B)[((int64_t)h * Nh + n) * Fh + f];
-    reinterpret_cast<float2*>(sm + l.Bt)[f * Nh + n] = b;
-    if (bwd) reinterpret_cast<float2*>(sm + l.Bn)[n * Fh + f] = b;
     const int f2 = i / Nh, n2 = i % Nh;
     const float2 c = reinterpret_cast<const float2*>(p.C)[((int64_t)h * Fh + f2) * Nh + n2];
     reinterpret_cast<float2*>(sm + l.Cn)[n2 * Fh + f2] = c;
@@ -228,6 +229,10 @@ __device__ void stage_chunk(const LParams& p, const Lay& l, float* sm, int64_t s
     sm[l.dnu + t] = semx::softplus(raw) * p.rs;
     sm[l.dth + t] = ld<BF16>(p.proj, row + c.dth);
   }
+  for (int i = threadIdx.x; i < nt * 2 * Nh; i += kT) {
+    const int t = i / (2 * Nh), j = i % (2 * Nh);
+    sm[l.bx + i] = ld<BF16>(p.proj, (s * p.L + t0 + t) * p.P + c.bx + j);
+  }
   if (R > 0) {
     for (int i = threadIdx.x; i < nt * R; i += kT) {
       const int t = i / R, r = i % R;
@@ -250,19 +255,14 @@ __device__ void stage_chunk(const LParams& p, const Lay& l, float* sm, int64_t s
 
 // Pole, gain and raw drive per (t, n) of the chunk; `gained` stores gain * drive.
 __device__ void poles_and_drive(const LParams& p, const Lay& l, float* sm, int nt, bool gained) {
-  const int Nh = (int)p.Nh, Fh = (int)p.Fh, R = (int)p.R;
-  const float2* Bt = reinterpret_cast<const float2*>(sm + l.Bt);
+  const int Nh = (int)p.Nh, R = (int)p.R;
+  const float2* bx = reinterpret_cast<const float2*>(sm + l.bx);
   for (int i = threadIdx.x; i < nt * Nh; i += kT) {
     const int t = i / Nh, n = i % Nh;
     const MDisc d = mdisc(p.gain, sm[l.prm + n], sm[l.prm + Nh + n], sm[l.prm + 2 * Nh + n],
                           p.detune != 0, sm[l.dnu + t], sm[l.dth + t]);
-    float br = 0.f, bi = 0.f;
-    const float* xr = sm + l.xs + t * Fh;
-    for (int f = 0; f < Fh; ++f) {
-      const float2 b = Bt[f * Nh + n];
-      br = fmaf(b.x, xr[f], br);
-      bi = fmaf(b.y, xr[f], bi);
-    }
+    float br = bx[i].x;
+    const float bi = bx[i].y;
     for (int r = 0; r < R; ++r) br = fmaf(sm[l.sb + t * R + r], sm[l.bt + (t * R + r) * Nh + n], br);
     reinterpret_cast<float2*>(sm + l.lam)[i] = make_float2(d.lre, d.lim);
     reinterpret_cast<float2*>(sm + l.gn)[i] = make_float2(d.gr, d.gi);
@@ -274,11 +274,13 @@ __device__ void poles_and_drive(const LParams& p, const Lay& l, float* sm, int n
 // ----------------------------------------------------------------------------- forward
 // Shared-memory layout of the forward (floats; staging buffers hold the input dtype).
 struct FLay {
-  int Btr, Bti, Cr, Ci, En, Co, Dp, prm, cin;
-  int stg[2], sml[2];  // staged x | b_t | c_t (input dtype); small operands (fp32)
+  int Cr, Ci, En, Co, Dp, prm, cin;
+  int stg[2], sml[2];  // staged x | drive | b_t | c_t (input dtype); small operands (fp32)
   int lam, bu, hs, sr;
-  int xw, btw, ctw;    // staged row widths in elements, padded so rows two tokens apart
-                       // fall in different shared-memory banks
+  int xw, bxw, btw, ctw;  // staged row widths in elements; x, b_t and c_t rows are padded
+                          // so rows two tokens apart fall in different shared-memory banks
+                          // (drive rows are read two consecutive tokens per warp and are
+                          // not padded)
   int hw;              // row width of lam / bu / hs in float2 (Nh + 1, same reason)
   int total;
 };
@@ -291,8 +293,6 @@ __host__ __device__ inline FLay make_flay(int Nh, int Fh, int R, bool env, int e
     o += al4(n);
     return at;
   };
-  l.Btr = take(Fh * Nh);
-  l.Bti = take(Fh * Nh);
   l.Cr = take(Nh * Fh);
   l.Ci = take(Nh * Fh);
   l.En = env ? take(Nh * Fh) : -1;
@@ -302,9 +302,10 @@ __host__ __device__ inline FLay make_flay(int Nh, int Fh, int R, bool env, int e
   l.cin = take(Nh * 2);
   const int pad = 16 / es;
   l.xw = ((Fh * es + 15) / 16) * 16 / es + pad;
+  l.bxw = ((2 * Nh * es + 15) / 16) * 16 / es;
   l.btw = R > 0 ? ((R * Nh * es + 15) / 16) * 16 / es + pad : 0;
   l.ctw = R > 0 ? ((2 * R * Nh * es + 15) / 16) * 16 / es + pad : 0;
-  const int stg_elems = kTC * (l.xw + l.btw + l.ctw);
+  const int stg_elems = kTC * (l.xw + l.bxw + l.btw + l.ctw);
   for (int b = 0; b < 2; ++b) l.stg[b] = take((stg_elems * es + 3) / 4);
   for (int b = 0; b < 2; ++b) l.sml[b] = take(kTC * (3 + 2 * R));
   l.hw = Nh + 1;
@@ -343,24 +344,26 @@ __device__ __forceinline__ void stage_segment(T* d, int dw, const T* src, int64_
   }
 }
 
-// Issues the staging of chunk [t0, t0 + nt) of head h: x [kTC][Fh], b_t [kTC][R Nh],
-// c_t [kTC][2 R Nh] in the input dtype, rows padded to l.xw / l.btw / l.ctw; 16-byte
-// cp.async where the host found the rows aligned (p.vec bit 0: x, bit 1: b_t and c_t),
-// otherwise plain loads.
+// Issues the staging of chunk [t0, t0 + nt) of head h: x [kTC][Fh], drive [kTC][2 Nh],
+// b_t [kTC][R Nh], c_t [kTC][2 R Nh] in the input dtype, rows l.xw / l.bxw / l.btw /
+// l.ctw apart; 16-byte cp.async where the host found the rows aligned (p.vec bit 0: x,
+// bit 1: b_t and c_t, bit 4: drive), otherwise plain loads.
 template <bool BF16, int NH, int FH, int RK>
 __device__ __forceinline__ void stage_bulk(const LParams& p, const FLay& l, void* dst, int64_t s, int h,
                                            int t0, int nt) {
   using T = typename std::conditional<BF16, __nv_bfloat16, float>::type;
   const int Nh = NH > 0 ? NH : (int)p.Nh, Fh = FH > 0 ? FH : (int)p.Fh, R = RK >= 0 ? RK : (int)p.R;
   T* xs = reinterpret_cast<T*>(dst);
-  T* bts = xs + kTC * l.xw;
+  T* bxs = xs + kTC * l.xw;
+  T* bts = bxs + kTC * l.bxw;
   T* cts = bts + kTC * l.btw;
   const T* X = reinterpret_cast<const T*>(p.x);
   const T* Pj = reinterpret_cast<const T*>(p.proj);
   const int64_t row0 = s * p.L + t0;
+  const Cols c = cols_of(p, h);
   stage_segment<T>(xs, l.xw, X, row0, p.H * p.Fh, (int64_t)h * Fh, Fh, nt, (p.vec & 1) != 0);
+  stage_segment<T>(bxs, l.bxw, Pj, row0, p.P, c.bx, 2 * Nh, nt, (p.vec & 16) != 0);
   if (R > 0) {
-    const Cols c = cols_of(p, h);
     stage_segment<T>(bts, l.btw, Pj, row0, p.P, c.bt, R * Nh, nt, (p.vec & 2) != 0);
     stage_segment<T>(cts, l.ctw, Pj, row0, p.P, c.ct, 2 * R * Nh, nt, (p.vec & 2) != 0);
   }
@@ -407,6 +410,20 @@ __device__ __forceinline__ void store_small(const LParams& p, float* sml, int nt
     }
   }
 }
+
+// Four consecutive staged values (8-byte aligned for bf16, 16-byte aligned for fp32).
+__device__ __forceinline__ float4 ld4(const __nv_bfloat16* q) {
+  const uint2 u = *reinterpret_cast<const uint2*>(q);
+  const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+  const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+  return make_float4(a.x, a.y, b.x, b.y);
+}
+__device__ __forceinline__ float4 ld4(const float* q) { return *reinterpret_cast<const float4*>(q); }
+// Two consecutive staged values (4-byte aligned for bf16, 8-byte aligned for fp32).
+__device__ __forceinline__ float2 ld2(const __nv_bfloat16* q) {
+  return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(q));
+}
+__device__ __forceinline__ float2 ld2(const float* q) { return *reinterpret_cast<const float2*>(q); }
 
 __device__ __forceinline__ float2 cmul(float2 a, float2 b) {
   return make_float2(a.x * b.x - a.y * b.y, a.x * b.y + a.y * b.x);
@@ -513,10 +530,6 @@ __global__ void __launch_bounds__(kT) mimo_layer_fwd_kernel(const LParams p) {
   const int64_t Fd = p.H * p.Fh;
   // Head parameters.
   for (int i = tid; i < Nh * Fh; i += kT) {
-    const int n = i / Fh, f = i % Fh;
-    const float2 bv = reinterpret_cast<const float2*>(p.B)[((int64_t)h * Nh + n) * Fh + f];
-    sm[l.Btr + f * Nh + n] = bv.x;
-    sm[l.Bti + f * Nh + n] = bv.y;
     const int f2 = i / Nh, n2 = i % Nh;
     const float2 cv = reinterpret_cast<const float2*>(p.C)[((int64_t)h * Fh + f2) * Nh + n2];
     sm[l.Cr + n2 * Fh + f2] = cv.x;
@@ -535,8 +548,6 @@ __global__ void __launch_bounds__(kT) mimo_layer_fwd_kernel(const LParams p) {
   float2* bu = reinterpret_cast<float2*>(sm + l.bu);
   float2* hs = reinterpret_cast<float2*>(sm + l.hs);
   float2* cin = reinterpret_cast<float2*>(sm + l.cin);
-  const float* Btr = sm + l.Btr;
-  const float* Bti = sm + l.Bti;
   const float* Cr = sm + l.Cr;
   const float* Ci = sm + l.Ci;
   const int hw = l.hw;
@@ -560,48 +571,26 @@ __global__ void __launch_bounds__(kT) mimo_layer_fwd_kernel(const LParams p) {
     }
     cp_async_commit();
     const T* xs = reinterpret_cast<const T*>(sm + l.stg[b]);
-    const T* bts = xs + kTC * l.xw;
+    const T* bxs = xs + kTC * l.xw;
+    const T* bts = bxs + kTC * l.bxw;
     const T* cts = bts + kTC * l.btw;
-    const int xw = l.xw, btw = l.btw, ctw = l.ctw;
+    const int xw = l.xw, bxw = l.bxw, btw = l.btw, ctw = l.ctw;
     const float* sml = sm + l.sml[b];
     const float* dnus = sml + kTC;
     const float* dths = sml + 2 * kTC;
     const float* sbs = sml + 3 * kTC;
     const float* scs = sbs + kTC * R;
-    // Poles and gained drive, 2 tokens x 2 modes per item.
-    const int np = (Nh + 1) / 2;
-    for (int it = tid; it < (kTC / 2) * np; it += kT) {
-      const int ta = (it / np) * 2, na = (it % np) * 2;
-      if (ta >= nt) continue;
-      float br[2][2] = {}, bi[2][2] = {};
-      const bool t1ok = ta + 1 < nt, n1ok = na + 1 < Nh;
-#pragma unroll 8
-      for (int f = 0; f < Fh; ++f) {
-        const float x0 = static_cast<float>(xs[ta * xw + f]);
-        const float x1 = t1ok ? static_cast<float>(xs[(ta + 1) * xw + f]) : 0.f;
-        const float b0r = Btr[f * Nh + na], b0i = Bti[f * Nh + na];
-        const float b1r = n1ok ? Btr[f * Nh + na + 1] : 0.f, b1i = n1ok ? Bti[f * Nh + na + 1] : 0.f;
-        br[0][0] = fmaf(b0r, x0, br[0][0]); bi[0][0] = fmaf(b0i, x0, bi[0][0]);
-        br[0][1] = fmaf(b1r, x0, br[0][1]); bi[0][1] = fmaf(b1i, x0, bi[0][1]);
-        br[1][0] = fmaf(b0r, x1, br[1][0]); bi[1][0] = fmaf(b0i, x1, bi[1][0]);
-        br[1][1] = fmaf(b1r, x1, br[1][1]); bi[1][1] = fmaf(b1i, x1, bi[1][1]);
-      }
-#pragma unroll
-      for (int dt = 0; dt < 2; ++dt) {
-        const int t = ta + dt;
-        if (t >= nt) continue;
-#pragma unroll
-        for (int dn = 0; dn < 2; ++dn) {
-          const int n = na + dn;
-          if (n >= Nh) continue;
-          float rr = br[dt][dn];
-          for (int r = 0; r < R; ++r) rr = fmaf(sbs[t * R + r], static_cast<float>(bts[t * btw + r * Nh + n]), rr);
-          const MDisc d = mdisc(p.gain, sm[l.prm + n], sm[l.prm + Nh + n], sm[l.prm + 2 * Nh + n],
-                                p.detune != 0, dnus[t], dths[t]);
-          lam[t * hw + n] = make_float2(d.lre, d.lim);
-          bu[t * hw + n] = make_float2(d.gr * rr - d.gi * bi[dt][dn], d.gr * bi[dt][dn] + d.gi * rr);
-        }
-      }
+    // Poles and gained drive per (token, mode).
+    for (int i = tid; i < nt * Nh; i += kT) {
+      const int t = i / Nh, n = i - (i / Nh) * Nh;
+      const float2 bq = ld2(bxs + t * bxw + 2 * n);
+      float rr = bq.x;
+      const float bi = bq.y;
+      for (int r = 0; r < R; ++r) rr = fmaf(sbs[t * R + r], static_cast<float>(bts[t * btw + r * Nh + n]), rr);
+      const MDisc d = mdisc(p.gain, sm[l.prm + n], sm[l.prm + Nh + n], sm[l.prm + 2 * Nh + n],
+                            p.detune != 0, dnus[t], dths[t]);
+      lam[t * hw + n] = make_float2(d.lre, d.lim);
+      bu[t * hw + n] = make_float2(d.gr * rr - d.gi * bi, d.gr * bi + d.gi * rr);
     }
     __syncthreads();
     if (p.ckpt != nullptr && tid < Nh)
@@ -693,9 +682,8 @@ __global__ void __launch_bounds__(kT) mimo_layer_bwd_kernel(const LParams p) {
   const int64_t Fd = p.H * p.Fh;
   const Cols cols = cols_of(p, h);
   load_head_params(p, l, sm, h, true);
-  // Parameter accumulators: [dB (Nh,Fh,2) | dC (Fh,Nh,2) | denv (Fh,Nh) | dcout (R,Fh) | dD (Fh)]
-  const int oB = 0, oC = oB + Nh * Fh * 2, oE = oC + Fh * Nh * 2, oO = oE + (env ? Fh * Nh : 0),
-            oD = oO + R * Fh, nacc = oD + Fh;
+  // Parameter accumulators: [dC (Fh,Nh,2) | denv (Fh,Nh) | dcout (R,Fh) | dD (Fh)]
+  const int oC = 0, oE = oC + Fh * Nh * 2, oO = oE + (env ? Fh * Nh : 0), oD = oO + R * Fh, nacc = oD + Fh;
   for (int i = tid; i < nacc; i += kT) sm[l.acc + i] = 0.f;
   float2* hs = reinterpret_cast<float2*>(sm + l.hs);
   float2* gs = reinterpret_cast<float2*>(sm + l.gs);
@@ -847,18 +835,15 @@ __global__ void __launch_bounds__(kT) mimo_layer_bwd_kernel(const LParams p) {
         acc_sd += tn[4 * kTC * Nh + t * Nh + nthr];
       }
     }
-    // dx = B^H d(raw drive) + D dy per (t, f).
-    {
-      const float2* Bn = reinterpret_cast<const float2*>(sm + l.Bn);
-      for (int i = tid; i < nt * Fh; i += kT) {
-        const int t = i / Fh, f = i % Fh;
-        float acc = sm[l.Dp + f] * sm[l.dys + i];
-        for (int n = 0; n < Nh; ++n) {
-          const float2 b = Bn[n * Fh + f], g = db[t * Nh + n];
-          acc = fmaf(b.x, g.x, fmaf(b.y, g.y, acc));
-        }
-        p.dx[(s * p.L + t0 + t) * Fd + (int64_t)h * Fh + f] = acc;
-      }
+    // dx = D dy per (t, f) (the drive's part B^H d(raw drive) reaches x through the
+    // projection's backward); d(drive columns) = d(raw drive) per (t, n).
+    for (int i = tid; i < nt * Fh; i += kT) {
+      const int t = i / Fh, f = i % Fh;
+      p.dx[(s * p.L + t0 + t) * Fd + (int64_t)h * Fh + f] = sm[l.Dp + f] * sm[l.dys + i];
+    }
+    for (int i = tid; i < nt * 2 * Nh; i += kT) {
+      const int t = i / (2 * Nh), j = i % (2 * Nh);
+      st<BF16>(p.dproj, (s * p.L + t0 + t) * p.P + cols.bx + j, sm[l.db + t * 2 * Nh + j]);
     }
     // Rank write: d s_b, d b_t.
     if (R > 0) {
@@ -876,18 +861,6 @@ __global__ void __launch_bounds__(kT) mimo_layer_bwd_kernel(const LParams p) {
     }
     // Parameter sums over the chunk (each item owned by one thread, fixed order in t).
     for (int i = tid; i < Nh * Fh; i += kT) {
-      {  // dB[n, f] += x[t, f] d(raw drive)[t, n]
-        const int n = i / Fh, f = i % Fh;
-        float ar = 0.f, ai = 0.f;
-        for (int t = 0; t < nt; ++t) {
-          const float xv = sm[l.xs + t * Fh + f];
-          const float2 g = db[t * Nh + n];
-          ar = fmaf(xv, g.x, ar);
-          ai = fmaf(xv, g.y, ai);
-        }
-        sm[l.acc + oB + 2 * i] += ar;
-        sm[l.acc + oB + 2 * i + 1] += ai;
-      }
       {  // dC[f, n] += dy[t, f] (h_re, -h_im)[t, n]; denv[f, n] += dy |h|^2
         const int f = i / Nh, n = i % Nh;
         float ar = 0.f, ai = 0.f, ae = 0.f;
@@ -918,7 +891,7 @@ __global__ void __launch_bounds__(kT) mimo_layer_bwd_kernel(const LParams p) {
   }
   __syncthreads();
   // Partial row of sequence s, parameter-major so every segment is in output order:
-  // [dB | dC | denv | dcout | dD | dA_log | domega | ddetune], each over all heads.
+  // [dC | denv | dcout | dD | dA_log | domega | ddetune], each over all heads.
   {
     const int64_t H = p.H;
     float* row = p.part + s * p.K;
@@ -927,7 +900,6 @@ __global__ void __launch_bounds__(kT) mimo_layer_bwd_kernel(const LParams p) {
       for (int i = tid; i < cnt; i += kT) row[off + (int64_t)h * seg_per_head + i] = sm[l.acc + src + i];
       off += H * seg_per_head;
     };
-    put(Nh * Fh * 2, oB, Nh * Fh * 2);
     put(Fh * Nh * 2, oC, Fh * Nh * 2);
     if (env) put(Fh * Nh, oE, Fh * Nh);
     if (R > 0) put(R * Fh, oO, R * Fh);
@@ -1012,10 +984,10 @@ __device__ __forceinline__ void chunk_scan_rev(const float2* lam, float2* gs, fl
 }
 
 struct BLay {
-  int Btr, Bti, Bnr, Bni, Cfr, Cfi, Ef, Co, Dp, prm, cin, cadj;
+  int Cfr, Cfi, Ef, Co, Dp, prm, cin, cadj;
   int stg[2], dys[2], sml[2];
   int lam, gn, braw, hs, gs, db, sr, dr, red;
-  int xw, btw, ctw, dyw;
+  int xw, bxw, btw, ctw, dyw;
   int total;
 };
 
@@ -1028,10 +1000,6 @@ __host__ __device__ inline BLay make_blay(int R, bool env, int es) {
     o += al4(n);
     return at;
   };
-  l.Btr = take(FH * NH);
-  l.Bti = take(FH * NH);
-  l.Bnr = take(NH * FH);
-  l.Bni = take(NH * FH);
   l.Cfr = take(FH * NH);
   l.Cfi = take(FH * NH);
   l.Ef = env ? take(FH * NH) : -1;
@@ -1042,10 +1010,11 @@ __host__ __device__ inline BLay make_blay(int R, bool env, int es) {
   l.cadj = take(2 * NH);
   const int pad = 16 / es;
   l.xw = FH + pad;
+  l.bxw = 2 * NH;
   l.btw = R > 0 ? R * NH + pad : 0;
   l.ctw = R > 0 ? 2 * R * NH + pad : 0;
   l.dyw = FH + 4;
-  for (int b = 0; b < 2; ++b) l.stg[b] = take((CT * (l.xw + l.btw + l.ctw) * es + 3) / 4);
+  for (int b = 0; b < 2; ++b) l.stg[b] = take((CT * (l.xw + l.bxw + l.btw + l.ctw) * es + 3) / 4);
   for (int b = 0; b < 2; ++b) l.dys[b] = take(CT * l.dyw);
   for (int b = 0; b < 2; ++b) l.sml[b] = take(CT * (3 + 2 * R));
   l.lam = take(CT * HW * 2);
@@ -1077,12 +1046,6 @@ __global__ void __launch_bounds__(kT) mimo_layer_bwd16_kernel(const LParams p) {
   const Cols cols = cols_of(p, h);
   // Head parameters in the storage orders the loops read.
   for (int i = tid; i < NH * FH; i += kT) {
-    const int n = i / FH, f = i % FH;
-    const float2 bv = reinterpret_cast<const float2*>(p.B)[((int64_t)h * NH + n) * FH + f];
-    sm[l.Btr + f * NH + n] = bv.x;
-    sm[l.Bti + f * NH + n] = bv.y;
-    sm[l.Bnr + n * FH + f] = bv.x;
-    sm[l.Bni + n * FH + f] = bv.y;
     const int f2 = i / NH, n2 = i % NH;
     const float2 cv = reinterpret_cast<const float2*>(p.C)[((int64_t)h * FH + f2) * NH + n2];
     sm[l.Cfr + f2 * NH + n2] = cv.x;
@@ -1108,11 +1071,10 @@ __global__ void __launch_bounds__(kT) mimo_layer_bwd16_kernel(const LParams p) {
 
   // Thread roles (fixed for the whole kernel).
   const int tA = tid / 8, npA = tid % 8;        // (token, mode pair) items
-  const int nB = tid / 8, fqB = tid % 8;        // dB items (mode, 4 channels)
   const int fC = tid / 4, nqC = tid % 4;        // dC / denv items (channel, 4 modes)
   const int rO = tid / FH, fO = tid % FH;       // dcout items (rank, channel) when R = 4
   float acc_a[2] = {0.f, 0.f}, acc_om[2] = {0.f, 0.f}, acc_sd[2] = {0.f, 0.f};
-  float aBr[4] = {}, aBi[4] = {}, aCr[4] = {}, aCi[4] = {}, aE[4] = {};
+  float aCr[4] = {}, aCi[4] = {}, aE[4] = {};
   float aO = 0.f, aD = 0.f;
 
   const int nck = p.nck;
@@ -1121,13 +1083,14 @@ __global__ void __launch_bounds__(kT) mimo_layer_bwd16_kernel(const LParams p) {
     const int t0 = k * CT, nt = min(CT, L - t0);
     T* xs = reinterpret_cast<T*>(sm + l.stg[b]);
     const int64_t row0 = s * p.L + t0;
+    const T* Pj = reinterpret_cast<const T*>(p.proj);
     stage_segment<T>(xs, l.xw, reinterpret_cast<const T*>(p.x), row0, Fd, (int64_t)h * FH, FH, nt,
                      (p.vec & 1) != 0);
+    stage_segment<T>(xs + CT * l.xw, l.bxw, Pj, row0, p.P, cols.bx, 2 * NH, nt, (p.vec & 16) != 0);
     if (R > 0) {
-      stage_segment<T>(xs + CT * l.xw, l.btw, reinterpret_cast<const T*>(p.proj), row0, p.P, cols.bt,
-                       R * NH, nt, (p.vec & 2) != 0);
-      stage_segment<T>(xs + CT * (l.xw + l.btw), l.ctw, reinterpret_cast<const T*>(p.proj), row0, p.P,
-                       cols.ct, 2 * R * NH, nt, (p.vec & 2) != 0);
+      stage_segment<T>(xs + CT * (l.xw + l.bxw), l.btw, Pj, row0, p.P, cols.bt, R * NH, nt, (p.vec & 2) != 0);
+      stage_segment<T>(xs + CT * (l.xw + l.bxw + l.btw), l.ctw, Pj, row0, p.P, cols.ct, 2 * R * NH, nt,
+                       (p.vec & 2) != 0);
     }
     stage_segment<float>(sm + l.dys[b], l.dyw, p.dy, row0, Fd, (int64_t)h * FH, FH, nt, (p.vec & 4) != 0);
   };
@@ -1149,7 +1112,8 @@ __global__ void __launch_bounds__(kT) mimo_layer_bwd16_kernel(const LParams p) {
     }
     cp_async_commit();
     const T* xs = reinterpret_cast<const T*>(sm + l.stg[b]);
-    const T* bts = xs + CT * l.xw;
+    const T* bxs = xs + CT * l.xw;
+    const T* bts = bxs + CT * l.bxw;
     const T* cts = bts + CT * l.btw;
     const float* dys = sm + l.dys[b];
     const float* sml = sm + l.sml[b];
@@ -1158,7 +1122,7 @@ __global__ void __launch_bounds__(kT) mimo_layer_bwd16_kernel(const LParams p) {
     const float* dths = sml + 2 * CT;
     const float* sbs = sml + 3 * CT;
     const float* scs = sbs + CT * R;
-    const int xw = l.xw, btw = l.btw, ctw = l.ctw, dyw = l.dyw;
+    const int xw = l.xw, bxw = l.bxw, btw = l.btw, ctw = l.ctw, dyw = l.dyw;
 
     // A. Poles, gains, raw and gained drive per (token, mode pair); entry state.
     if (tid < NH) {
@@ -1168,17 +1132,8 @@ __global__ void __launch_bounds__(kT) mimo_layer_bwd16_kernel(const LParams p) {
     }
     if (tA < nt) {
       const int t = tA, na = 2 * npA;
-      float br0 = 0.f, bi0 = 0.f, br1 = 0.f, bi1 = 0.f;
-#pragma unroll 8
-      for (int f = 0; f < FH; ++f) {
-        const float xv = static_cast<float>(xs[t * xw + f]);
-        const float2 brp = *reinterpret_cast<const float2*>(sm + l.Btr + f * NH + na);
-        const float2 bip = *reinterpret_cast<const float2*>(sm + l.Bti + f * NH + na);
-        br0 = fmaf(brp.x, xv, br0);
-        bi0 = fmaf(bip.x, xv, bi0);
-        br1 = fmaf(brp.y, xv, br1);
-        bi1 = fmaf(bip.y, xv, bi1);
-      }
+      const float4 bq = ld4(bxs + t * bxw + 2 * na);
+      float br0 = bq.x, bi0 = bq.y, br1 = bq.z, bi1 = bq.w;
 #pragma unroll
       for (int r = 0; r < R; ++r) {
         const float sbv = sbs[t * R + r];
@@ -1322,23 +1277,31 @@ __global__ void __launch_bounds__(kT) mimo_layer_bwd16_kernel(const LParams p) {
       }
     }
     __syncthreads();
-    // G. dx = B^H d(raw drive) + D dy per (token, 4 channels).
+    // G. dx = D dy per (token, 4 channels); the drive's part B^H d(raw drive) reaches x
+    // through the projection's backward. d(drive columns) = d(raw drive) of the token's
+    // mode pair.
     if (tA < nt) {
-      const int t = tA, f0 = 4 * npA;
+      const int t = tA, f0 = 4 * npA, na = 2 * npA;
       float4 acc;
       acc.x = sm[l.Dp + f0] * dys[t * dyw + f0];
       acc.y = sm[l.Dp + f0 + 1] * dys[t * dyw + f0 + 1];
       acc.z = sm[l.Dp + f0 + 2] * dys[t * dyw + f0 + 2];
       acc.w = sm[l.Dp + f0 + 3] * dys[t * dyw + f0 + 3];
-#pragma unroll 4
-      for (int n = 0; n < NH; ++n) {
-        const float2 g = db[t * HW + n];
-        const float4 br = *reinterpret_cast<const float4*>(sm + l.Bnr + n * FH + f0);
-        const float4 bi = *reinterpret_cast<const float4*>(sm + l.Bni + n * FH + f0);
-        acc.x = fmaf(br.x, g.x, fmaf(bi.x, g.y, acc.x));
-        acc.y = fmaf(br.y, g.x, fmaf(bi.y, g.y, acc.y));
-        acc.z = fmaf(br.z, g.x, fmaf(bi.z, g.y, acc.z));
-        acc.w = fmaf(br.w, g.x, fmaf(bi.w, g.y, acc.w));
+      const float2 g0 = db[t * HW + na], g1 = db[t * HW + na + 1];
+      const int64_t drow = (s * p.L + t0 + t) * p.P + cols.bx + 2 * na;
+      if ((p.vec & 16) != 0) {
+        if (BF16) {
+          __nv_bfloat162 q[2] = {__floats2bfloat162_rn(g0.x, g0.y), __floats2bfloat162_rn(g1.x, g1.y)};
+          *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(p.dproj) + drow) =
+              *reinterpret_cast<const uint2*>(q);
+        } else {
+          *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.dproj) + drow) = make_float4(g0.x, g0.y, g1.x, g1.y);
+        }
+      } else {
+        st<BF16>(p.dproj, drow, g0.x);
+        st<BF16>(p.dproj, drow + 1, g0.y);
+        st<BF16>(p.dproj, drow + 2, g1.x);
+        st<BF16>(p.dproj, drow + 3, g1.y);
       }
       float* dxr = p.dx + (s * p.L + t0 + t) * Fd + (int64_t)h * FH + f0;
       if ((p.vec & 8) != 0) {
@@ -1363,15 +1326,6 @@ __global__ void __launch_bounds__(kT) mimo_layer_bwd16_kernel(const LParams p) {
     }
     // I. Parameter sums over the chunk, fixed ownership.
     for (int t = 0; t < nt; ++t) {
-      {  // dB[nB, 4 fqB .. +3] += x[t, f] conj-free d(raw drive)[t, nB]
-        const float2 g = db[t * HW + nB];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float xv = static_cast<float>(xs[t * xw + 4 * fqB + j]);
-          aBr[j] = fmaf(xv, g.x, aBr[j]);
-          aBi[j] = fmaf(xv, g.y, aBi[j]);
-        }
-      }
       {  // dC[fC, 4 nqC .. +3] += dy (h_re, -h_im); denv += dy |h|^2
         const float dv = dys[t * dyw + fC];
         const float4 ha = *reinterpret_cast<const float4*>(hs + (t + 1) * HW + 4 * nqC);
@@ -1401,17 +1355,10 @@ __global__ void __launch_bounds__(kT) mimo_layer_bwd16_kernel(const LParams p) {
     red[(2 * NH + n) * (kT / 8) + tA] = acc_sd[dn];
   }
   __syncthreads();
-  // Partial row of sequence s: [dB | dC | denv | dcout | dD | dA_log | domega | ddetune].
+  // Partial row of sequence s: [dC | denv | dcout | dD | dA_log | domega | ddetune].
   const int64_t H = p.H;
   float* row = p.part + s * p.K;
   int64_t off = 0;
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int64_t i = ((int64_t)h * NH + nB) * FH + 4 * fqB + j;
-    row[off + 2 * i] = aBr[j];
-    row[off + 2 * i + 1] = aBi[j];
-  }
-  off += H * NH * FH * 2;
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     const int64_t i = ((int64_t)h * FH + fC) * NH + 4 * nqC + j;
@@ -1441,12 +1388,12 @@ __global__ void __launch_bounds__(kT) mimo_layer_bwd16_kernel(const LParams p) {
 
 // ------------------------------------------------------------------------ host side
 int64_t proj_width(const SemxMimoLayerArgs* a) {
-  return 2 * a->H + (a->rank > 0 ? 2 * a->H * a->rank + 3 * a->H * a->rank * a->Nh : 0);
+  return 2 * a->H + (a->rank > 0 ? 2 * a->H * a->rank + 3 * a->H * a->rank * a->Nh : 0) + 2 * a->H * a->Nh;
 }
 
 int64_t part_row(const SemxMimoLayerArgs* a) {
   const int64_t H = a->H, Nh = a->Nh, Fh = a->Fh, R = a->rank;
-  return H * (4 * Nh * Fh + (a->envelope ? Fh * Nh : 0) + R * Fh + Fh + 3 * Nh);
+  return H * (2 * Nh * Fh + (a->envelope ? Fh * Nh : 0) + R * Fh + Fh + 3 * Nh);
 }
 
 // The backward of 16-mode, 32-channel heads of rank 0 or 4 has its own kernel.
@@ -1469,7 +1416,10 @@ int vec_flags(const SemxMimoLayerArgs* a) {
                   ((R * Nh * es) % 16) == 0 && ((2 * H + 2 * H * R + H * R * Nh) * es) % 16 == 0;
   const bool vdy = semx::aligned(a->dy, 16) && (H * Fh * 4) % 16 == 0 && (Fh * 4) % 16 == 0;
   const bool vdx = semx::aligned(a->dx, 16) && (H * Fh * 4) % 16 == 0 && (Fh * 4) % 16 == 0;
-  return (vx ? 1 : 0) | (vp ? 2 : 0) | (vdy ? 4 : 0) | (vdx ? 8 : 0);
+  const int64_t bx0 = 2 * H + 2 * H * R + 3 * H * R * Nh;
+  const bool vbx = semx::aligned(a->proj, 16) && (a->dproj == nullptr || semx::aligned(a->dproj, 16)) &&
+                   (P * es) % 16 == 0 && (bx0 * es) % 16 == 0 && (2 * Nh * es) % 16 == 0;
+  return (vx ? 1 : 0) | (vp ? 2 : 0) | (vdy ? 4 : 0) | (vdx ? 8 : 0) | (vbx ? 16 : 0);
 }
 
 // Segments per mode of the forward's parallel chunk scan (1: one thread per mode).
@@ -1493,13 +1443,11 @@ int layer_validate(const SemxMimoLayerArgs* a, bool bwd) {
                "mimo_layer: head of Nh=%lld, Fh=%lld, rank=%d needs %zu B of shared memory",
                (long long)a->Nh, (long long)a->Fh, a->rank, smem);
   if (a->S * a->H > 0) {
-    SEMX_REQUIRE(a->A_log && a->omega && a->B && a->C && a->D, SEMX_ERR_NULL,
-                 "mimo_layer: NULL parameter");
+    SEMX_REQUIRE(a->A_log && a->omega && a->C && a->D, SEMX_ERR_NULL, "mimo_layer: NULL parameter");
     SEMX_REQUIRE(!a->detune || a->detune_gain, SEMX_ERR_NULL, "mimo_layer: detune_gain is NULL");
     SEMX_REQUIRE(!a->envelope || a->env_gain, SEMX_ERR_NULL, "mimo_layer: env_gain is NULL");
     SEMX_REQUIRE(a->rank == 0 || a->c_out, SEMX_ERR_NULL, "mimo_layer: c_out is NULL");
-    SEMX_REQUIRE(semx::aligned(a->B, 8) && semx::aligned(a->C, 8), SEMX_ERR_ALIGN,
-                 "mimo_layer: B and C must be 8-byte aligned");
+    SEMX_REQUIRE(semx::aligned(a->C, 8), SEMX_ERR_ALIGN, "mimo_layer: C must be 8-byte aligned");
   }
   if (a->S * a->L * a->H > 0) {
     SEMX_REQUIRE(a->x && a->proj, SEMX_ERR_NULL, "mimo_layer: x/proj is NULL");
@@ -1524,7 +1472,7 @@ LParams to_lparams(const SemxMimoLayerArgs* a) {
   p.nck = (int)semx::cdiv(a->L, kCk);
   p.rs = a->rate_scale;
   p.x = a->x; p.proj = a->proj;
-  p.A_log = a->A_log; p.omega = a->omega; p.sdet = a->detune_gain; p.B = a->B; p.C = a->C; p.D = a->D;
+  p.A_log = a->A_log; p.omega = a->omega; p.sdet = a->detune_gain; p.C = a->C; p.D = a->D;
   p.cout = a->c_out; p.env = a->env_gain;
   p.y = a->y; p.ckpt = a->ckpt; p.dy = a->dy; p.dx = a->dx; p.dproj = a->dproj;
   p.K = part_row(a);
@@ -1630,7 +1578,6 @@ int semx_mimo_layer_bwd(const SemxMimoLayerArgs* a, semx_stream_t stream) {
     seg.len[n] = len;
     ++n;
   };
-  add(a->dB, H * Nh * Fh * 2);
   add(a->dC, H * Fh * Nh * 2);
   if (a->envelope) add(a->denv, H * Fh * Nh);
   if (R > 0) add(a->dc_out, H * R * Fh);

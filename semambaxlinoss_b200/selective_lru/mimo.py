@@ -134,22 +134,22 @@ def fused_selective_lru_mimo(lam_re, lam_im, Bu_re, Bu_im, C_re, C_im, x, D, n_h
 
 class _MimoLayer(torch.autograd.Function):
     """The SelectiveLRUMIMO layer after its token projections (semx_mimo_layer_fwd/bwd):
-    poles, gain, drive, scan, readout and feedthrough in one kernel per direction."""
+    poles, gain, scan, readout and feedthrough in one kernel per direction."""
 
     @staticmethod
-    def forward(ctx, x, proj, A_log, omega, detune_gain, B, C, D, c_out, env_gain, dims):
+    def forward(ctx, x, proj, A_log, omega, detune_gain, C, D, c_out, env_gain, dims):
         H, Nh, Fh, rank, gain_code, rate_scale = dims
-        for t in (x, proj, A_log, omega, B, C, D):
+        for t in (x, proj, A_log, omega, C, D):
             if not t.is_cuda:
                 raise RuntimeError("SelectiveLRUMIMO requires CUDA tensors.")
         if x.dtype != proj.dtype or x.dtype not in (torch.float32, torch.bfloat16):
             raise ValueError("x and proj must both be float32 or both bfloat16")
         S, L, Fd = x.shape
-        if Fd != H * Fh or B.shape != (H, Nh, Fh, 2) or C.shape != (H, Fh, Nh, 2):
+        if Fd != H * Fh or C.shape != (H, Fh, Nh, 2) or proj.shape != (S, L, proj_width(H, Nh, rank)):
             raise ValueError("SelectiveLRUMIMO operand shapes do not agree")
         x = x.contiguous()
         proj = proj.contiguous()
-        params = [_f32(t) for t in (A_log, omega, detune_gain, B, C, D, c_out, env_gain)]
+        params = [_f32(t) for t in (A_log, omega, detune_gain, C, D, c_out, env_gain)]
         y = torch.empty((S, L, Fd), dtype=torch.float32, device=x.device)
         a = _lib.new_args(_lib.SemxMimoLayerArgs)
         a.input_gain, a.rank, a.rate_scale = gain_code, rank, float(rate_scale)
@@ -157,7 +157,7 @@ class _MimoLayer(torch.autograd.Function):
         a.bf16 = int(x.dtype == torch.bfloat16)
         a.S, a.L, a.H, a.Nh, a.Fh = S, L, H, Nh, Fh
         a.x, a.proj, a.y = x.data_ptr(), proj.data_ptr(), y.data_ptr()
-        (a.A_log, a.omega, a.detune_gain, a.B, a.C, a.D, a.c_out, a.env_gain) = [_lib.ptr(t) for t in params]
+        (a.A_log, a.omega, a.detune_gain, a.C, a.D, a.c_out, a.env_gain) = [_lib.ptr(t) for t in params]
         ckpt = None
         if any(ctx.needs_input_grad):
             ckpt = _lib.empty_f32(_lib.load().semx_mimo_layer_ckpt_bytes(a), x.device)
@@ -171,7 +171,7 @@ class _MimoLayer(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, dy):
-        x, proj, ckpt, A_log, omega, det, B, C, D, c_out, env = ctx.saved_tensors
+        x, proj, ckpt, A_log, omega, det, C, D, c_out, env = ctx.saved_tensors
         H, Nh, Fh, rank, gain_code, rate_scale = ctx.dims
         detune, envelope = ctx.flags
         S, L, Fd = x.shape
@@ -179,8 +179,7 @@ class _MimoLayer(torch.autograd.Function):
         dy = _f32(dy)
         dx = torch.empty((S, L, Fd), dtype=torch.float32, device=dev)
         dproj = torch.empty_like(proj)
-        g = {k: torch.empty_like(v) for k, v in (("dA_log", A_log), ("domega", omega), ("dB", B),
-                                                  ("dC", C), ("dD", D))}
+        g = {k: torch.empty_like(v) for k, v in (("dA_log", A_log), ("domega", omega), ("dC", C), ("dD", D))}
         g["ddetune"] = torch.empty_like(det) if detune else None
         g["dc_out"] = torch.empty_like(c_out) if rank > 0 else None
         g["denv"] = torch.empty_like(env) if envelope else None
@@ -190,24 +189,42 @@ class _MimoLayer(torch.autograd.Function):
         a.bf16 = int(x.dtype == torch.bfloat16)
         a.S, a.L, a.H, a.Nh, a.Fh = S, L, H, Nh, Fh
         a.x, a.proj, a.ckpt, a.dy, a.dx, a.dproj = [t.data_ptr() for t in (x, proj, ckpt, dy, dx, dproj)]
-        (a.A_log, a.omega, a.detune_gain, a.B, a.C, a.D, a.c_out, a.env_gain) = [
-            _lib.ptr(t) for t in (A_log, omega, det, B, C, D, c_out, env)]
+        (a.A_log, a.omega, a.detune_gain, a.C, a.D, a.c_out, a.env_gain) = [
+            _lib.ptr(t) for t in (A_log, omega, det, C, D, c_out, env)]
         for k, v in g.items():
             setattr(a, k, _lib.ptr(v))
         ws = _lib.empty_f32(_lib.load().semx_mimo_layer_workspace_bytes(a), dev)
         a.workspace = ws.data_ptr()
         _lib.call("semx_mimo_layer_bwd", a, dev)
-        return (dx.to(x.dtype), dproj, g["dA_log"], g["domega"], g["ddetune"], g["dB"], g["dC"],
+        return (dx.to(x.dtype), dproj, g["dA_log"], g["domega"], g["ddetune"], g["dC"],
                 g["dD"], g["dc_out"], g["denv"], None)
 
 
-def mimo_layer(x, proj, A_log, omega, detune_gain, B, C, D, c_out, env_gain, n_heads, n_head,
+def proj_width(n_heads, n_head, rank):
+    """Columns of the projection row the layer kernels read (see :func:`mimo_layer`)."""
+    H, Nh, r = int(n_heads), int(n_head), int(rank)
+    return 2 * H + 2 * H * r + 3 * H * r * Nh + 2 * H * Nh
+
+
+def drive_weight(B):
+    """The static input map B (H, Nh, Fh, 2) as the block-diagonal rows of the projection
+    weight that produce the drive columns: row h*2Nh + 2n + c, column h*Fh + f holds
+    B[h, n, f, c] (c = 0 real, 1 imaginary part)."""
+    H, Nh, Fh, _ = B.shape
+    return torch.block_diag(*B.permute(0, 1, 3, 2).reshape(H, 2 * Nh, Fh).unbind(0))
+
+
+def mimo_layer(x, proj, A_log, omega, detune_gain, C, D, c_out, env_gain, n_heads, n_head,
                f_head, rank, input_gain="gamma", rate_scale=1.0):
     """SelectiveLRUMIMO after its token projections. ``proj`` (B, T, P) holds, per token,
-    [dnu_raw (H) | dth (H) | s_b (H r) | b_t (H r Nh) | s_c (H r) | c_t (H r 2Nh)] with
-    dnu = softplus(dnu_raw) * rate_scale; ``x`` (B, T, H Fh) and ``proj`` are both float32
-    or both bfloat16 (state and outputs are float32). Returns y (B, T, H Fh) float32."""
+    [dnu_raw (H) | dth (H) | s_b (H r) | b_t (H r Nh) | s_c (H r) | c_t (H r 2Nh) |
+    bx (H 2Nh)] with dnu = softplus(dnu_raw) * rate_scale and bx the static drive
+    (sum_f B[h, n, f] x[h Fh + f], real and imaginary part per mode; :func:`drive_weight`
+    gives its weight rows); ``x`` (B, T, H Fh) and ``proj`` are both float32 or both
+    bfloat16 (state and outputs are float32). Returns y (B, T, H Fh) float32; the
+    gradient reaching x directly is the skip part D dy, the drive's part flows through
+    ``proj``."""
     if input_gain not in _lib.GAIN_CODES:
         raise ValueError(f"input_gain must be 'gamma', 'mamba', 'zoh', or 'none', got {input_gain!r}")
     dims = (int(n_heads), int(n_head), int(f_head), int(rank), _lib.GAIN_CODES[input_gain], float(rate_scale))
-    return _MimoLayer.apply(x, proj, A_log, omega, detune_gain, B, C, D, c_out, env_gain, dims)
+    return _MimoLayer.apply(x, proj, A_log, omega, detune_gain, C, D, c_out, env_gain, dims)

@@ -165,9 +165,10 @@ class SelectiveLRUMIMO(nn.Module):
     readout ``Re(C h) [+ <g, |h|^2>] + D x [+ rank-r read]``.
 
     Same constructor, parameter names, registration order, initial values and tags as the
-    reference. The scan + readout + D skip run in the sm_100a MIMO kernel
-    (:func:`fused_selective_lru_mimo`); the pole / drive construction and the rank /
-    envelope feedthrough terms are evaluated around it.
+    reference. All token projections, the static drive B x included, are one GEMM (its
+    weight from :meth:`_projection`); poles, gain, scan, readout, D skip and the rank /
+    envelope feedthrough run in the sm_100a layer kernels (:func:`mimo_layer`), one per
+    direction.
     """
 
     def __init__(
@@ -260,10 +261,15 @@ class SelectiveLRUMIMO(nn.Module):
     def _projection(self):
         """Weight and bias of all token projections as one matrix, rows in the order the
         fused layer kernel reads them: [dt_nu (H) | dt_theta (H) | b_coef (H r) |
-        b_dir (H r Nh) | c_coef (H r) | c_read (2 H r Nh)]."""
+        b_dir (H r Nh) | c_coef (H r) | c_read (2 H r Nh) | static drive B (2 H Nh,
+        block-diagonal)]. The static drive B x is computed (and back-propagated) in the
+        projection GEMM, so dB comes from the GEMM's weight gradient."""
+        from .mimo import drive_weight
+
         ws = [self.dt_nu_proj.weight, self.dt_theta_proj.weight]
         if self.rank > 0:
             ws += [self.b_coef.weight, self.b_dir.weight, self.c_coef.weight, self.c_read.weight]
+        ws.append(drive_weight(self.B))
         W = torch.cat(ws, 0)
         b = torch.cat([self.dt_nu_proj.bias, self.dt_theta_proj.bias,
                        self.dt_nu_proj.bias.new_zeros(W.shape[0] - 2 * self.n_heads)])
@@ -289,6 +295,6 @@ class SelectiveLRUMIMO(nn.Module):
             rs = self.rate_scale if rate_scale is None else float(rate_scale)
             return mimo_layer(
                 x, proj, self.A_log, self.omega, self.detune_gain if self.mode_detune else None,
-                self.B, self.C, self.D, self.c_out if self.rank > 0 else None,
+                self.C, self.D, self.c_out if self.rank > 0 else None,
                 self.env_gain if self.envelope_readout else None, self.n_heads, self.n_head,
                 self.f_head, self.rank, self.input_gain, rs)

@@ -186,10 +186,10 @@ def _layer_gpu(m, x, gy, dtype):
 
 @pytest.mark.parametrize("case", range(len(_LAYER_CASES)))
 def test_fused_layer_matches_oracle(case):
-    """The fused layer kernel (token projections -> poles, gain, drive, scan, readout,
-    envelope, rank feedthrough) against the float64 oracle: output, input gradient and
-    every parameter gradient, for every gain, rank 0-4, detune, envelope, rate scale,
-    Nh not a power of two and ragged 32-token chunks."""
+    """The fused layer (token projections incl. the static drive -> poles, gain, scan,
+    readout, envelope, rank feedthrough) against the float64 oracle: output, input
+    gradient and every parameter gradient, for every gain, rank 0-4, detune, envelope,
+    rate scale, Nh not a power of two and ragged 32-token chunks."""
     cfg, B, T = _LAYER_CASES[case]
     m, x, gy = _layer_case(cfg, B, T, 40 + case)
     ref = _layer_oracle(m, cfg, x, gy, torch.float64)
@@ -252,6 +252,10 @@ def test_fused_layer_bf16_inputs():
         if name.startswith("dt_"):
             ref[f"d{name}.bias"] = dproj[..., o:o + rows].sum((0, 1))
         o += rows
+    # The static input map B is the block-diagonal drive block of the projection weight.
+    Fh = 256 // H
+    ref["dB"] = torch.stack([dW[o + h * 2 * Nh:o + (h + 1) * 2 * Nh, h * Fh:(h + 1) * Fh]
+                             .reshape(Nh, 2, Fh).permute(0, 2, 1) for h in range(H)])
     for k in ref:
         assert_close(out[k], ref[k], BF16_TOL, k)
 

@@ -95,3 +95,22 @@ def test_layer_spec_matches():
     assert _layer_spec_matches([-1], 3, 4)
     assert _layer_spec_matches(["1-2"], 2, 4)
     assert not _layer_spec_matches(["1-2", 0], 3, 4)
+
+
+def test_mimo_drive_weight_layout():
+    """drive_weight(B) holds B block-diagonally: F.linear(x, drive_weight(B)) is the static
+    drive sum_f B[h, n, f, c] x[h Fh + f] at column h 2Nh + 2n + c, and the projection of
+    SelectiveLRUMIMO is proj_width() columns wide with the drive block last."""
+    from semambaxlinoss_b200.selective_lru import drive_weight, proj_width
+
+    g = torch.Generator().manual_seed(3)
+    H, Nh, Fh = 3, 5, 4
+    B = torch.randn(H, Nh, Fh, 2, generator=g, dtype=torch.float64)
+    x = torch.randn(2, 7, H * Fh, generator=g, dtype=torch.float64)
+    bx = torch.nn.functional.linear(x, drive_weight(B))
+    want = torch.einsum("hnfc,bthf->bthnc", B, x.view(2, 7, H, Fh)).reshape(2, 7, 2 * H * Nh)
+    assert torch.allclose(bx, want, rtol=0, atol=1e-12)
+    m = SelectiveLRUMIMO(24, 16, n_heads=2, rank=3)
+    W, b = m._projection()
+    assert W.shape == (proj_width(2, 8, 3), 24) and b.shape == (W.shape[0],)
+    assert torch.equal(W[-2 * 16:], drive_weight(m.B.detach()))

@@ -96,6 +96,23 @@ def test_mimo_layers_match_reference(golden, idx):
     _module_case(rec, lambda p, x: oslru.selective_lru_mimo_forward(p, x, cfg))
 
 
+@pytest.mark.parametrize("idx", range(5))
+def test_mimo_drive_columns_match_reference(golden, idx):
+    """The layer kernels' input contract: projection rows that carry the static drive
+    B x as extra columns give the reference's outputs and gradients (B's gradient then
+    flows through those columns)."""
+    cases = golden("mimo")
+    name = sorted(cases)[idx]
+    rec = cases[name]
+    cfg = dict(rec["config"])
+
+    def fwd(p, x):
+        proj = oslru.mimo_projection(p, x, cfg, drive=True)
+        return oslru.selective_lru_mimo_from_projection(proj, p, x, cfg)
+
+    _module_case(rec, fwd)
+
+
 def test_selective_recurrence_matches_reference(golden):
     rec = golden("recurrence")["selective_recurrence"]
     ins = [t.clone().requires_grad_(True) for t in (rec["lam"], rec["Bu"], rec["h0"])]

@@ -468,8 +468,7 @@ class MimoKernelPass:
     """The fused MIMO layer kernels alone (semx_mimo_layer_fwd / _bwd) on resident bf16
     token operands (x and the projection rows, 1872 columns including the static drive),
     for the kernel roofline of the MIMO workload. Bytes per token: fwd x + proj (bf16) in,
-    y (fp32) out = 5280; bwd x, proj (bf16), dy (fp32) in, dx (fp32), dproj (bf16) out =
-    10048."""
+    y (fp32) out = 5280; bwd x, proj (bf16), dy (fp32) in, dx, dproj (bf16) out = 9536."""
 
     kernels = ("mimo_layer_fwd_kernel", "mimo_layer_bwd16_kernel")
 
@@ -483,13 +482,15 @@ class MimoKernelPass:
         self.x = (torch.randn(S, L, MIMO_F, generator=g, device=device) * 0.5).to(bf)
         with torch.no_grad():
             W, b = layer._projection()
-            self.proj = torch.nn.functional.linear(self.x, W.to(bf), b.to(bf))
+            self.proj = torch.nn.functional.linear(self.x, W.to(bf))
+        self.dt_bias = b.detach().float().contiguous()
+        self.d_dt_bias = torch.empty_like(self.dt_bias)
         P = self.proj.shape[-1]
         self.fwd_bytes_per_unit = 2 * MIMO_F + 2 * P + 4 * MIMO_F
-        self.bwd_bytes_per_unit = (2 * MIMO_F + 2 * P + 4 * MIMO_F) + (4 * MIMO_F + 2 * P)
+        self.bwd_bytes_per_unit = (2 * MIMO_F + 2 * P + 4 * MIMO_F) + (2 * MIMO_F + 2 * P)
         self.y = torch.empty(S, L, MIMO_F, device=device)
         self.dy = torch.randn(S, L, MIMO_F, generator=g, device=device)
-        self.dx = torch.empty_like(self.y)
+        self.dx = torch.empty_like(self.x)
         self.dproj = torch.empty_like(self.proj)
         self.params = [t.detach().float().contiguous() for t in (
             layer.A_log, layer.omega, layer.C, layer.D, layer.c_out)]
@@ -501,6 +502,7 @@ class MimoKernelPass:
             self.x, self.proj, self.y, self.dy, self.dx, self.dproj)]
         a.A_log, a.omega, a.C, a.D, a.c_out = [t.data_ptr() for t in self.params]
         a.dA_log, a.domega, a.dC, a.dD, a.dc_out = [t.data_ptr() for t in self.grads]
+        a.dt_bias, a.d_dt_bias = self.dt_bias.data_ptr(), self.d_dt_bias.data_ptr()
         self.ckpt = _lib.empty_f32(self.lib.semx_mimo_layer_ckpt_bytes(ctypes.byref(a)), device)
         a.ckpt = self.ckpt.data_ptr()
         self.ws = _lib.empty_f32(self.lib.semx_mimo_layer_workspace_bytes(ctypes.byref(a)), device)

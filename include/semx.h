@@ -318,7 +318,8 @@ int semx_mimo_bwd(const SemxMimoArgs* args, semx_stream_t stream);
  * Fused SelectiveLRUMIMO layer after its token projections: for every head h of H heads
  * (Nh modes, Fh channels, rank R) and token t, from the projection row `proj` and the
  * input x,
- *   dnu = softplus(proj[dnu_h]) * rate_scale,  dth = proj[dth_h]
+ *   dnu = softplus(proj[dnu_h] + b_nu[h]) * rate_scale,  dth = proj[dth_h] + b_th[h]
+ *          (dt_bias = [b_nu (H) | b_th (H)], optional: zero when NULL)
  *   lam[n] = exp(dnu (-a[n] + j (omega[n] + (detune ? s[n] dth : dth)))),  a = exp(A_log)
  *   Bu[n]  = gain[n] (bx[n] + sum_r s_b[r] b_t[r,n])   (bx complex: the static drive
  *            sum_f B[h,n,f] x[h*Fh+f]; the rank write real), gain per input_gain
@@ -334,14 +335,15 @@ int semx_mimo_bwd(const SemxMimoArgs* args, semx_stream_t stream);
  * projection weight (rows h*2Nh + 2n + {0: re, 1: im}, columns h*Fh .. h*Fh+Fh-1), and its
  * gradients (dB, and B^H d(bx) in dx) come from the projection's backward: dproj's bx
  * columns hold d(loss)/d(bx).
- * x: (S,L,H*Fh); x and proj are fp32, or bf16 when `bf16` is set; y, dy, dx fp32; dproj
- * has the dtype of proj. Parameters fp32: A_log, omega, detune_gain (H,Nh);
- * C (H,Fh,Nh,2); D (H*Fh); c_out (H*R,Fh); env_gain (H,Fh,Nh).
+ * x: (S,L,H*Fh); x and proj are fp32, or bf16 when `bf16` is set; y, dy fp32; dx and
+ * dproj have the dtype of x. Parameters fp32: A_log, omega, detune_gain (H,Nh);
+ * C (H,Fh,Nh,2); D (H*Fh); c_out (H*R,Fh); env_gain (H,Fh,Nh); dt_bias (2H).
  * Replaces SelectiveLRUMIMO.forward after its projections
  * (models/selective_lru/selective_lru.py:488-587): poles, drive, gain, scan, readout and
  * feedthrough in one pass per (sequence, head). Training forwards store the state at
  * every 16-step block in ckpt (semx_mimo_layer_ckpt_bytes()). Backward recomputes from
- * ckpt and writes dx (the skip part D dy), dproj and the parameter gradients
+ * ckpt and writes dx (the skip part D dy), dproj (for the dt columns the gradient
+ * with respect to the biased value, which is also the bias's) and the parameter gradients
  * (reduced over sequences in a fixed order; dA_log is with respect to A_log).
  * ---------------------------------------------------------------------------------- */
 typedef struct SemxMimoLayerArgs {
@@ -363,10 +365,11 @@ typedef struct SemxMimoLayerArgs {
   const float* D;
   const float* c_out;
   const float* env_gain;
+  const float* dt_bias; /* optional */
   float* y;
   float* ckpt; /* optional in the forward; required by the backward */
   const float* dy;
-  float* dx;
+  void* dx;
   void* dproj;
   float* dA_log;
   float* domega;
@@ -375,7 +378,8 @@ typedef struct SemxMimoLayerArgs {
   float* dD;
   float* dc_out;
   float* denv;
-  void* workspace; /* semx_mimo_layer_workspace_bytes(), backward only */
+  float* d_dt_bias; /* written when dt_bias is given */
+  void* workspace;  /* semx_mimo_layer_workspace_bytes(), backward only */
 } SemxMimoLayerArgs;
 
 /* ------------------------------------------------------------------------------------

@@ -146,9 +146,9 @@ class SemxMimoLayerArgs(ctypes.Structure):
         ("Nh", ctypes.c_int64),
         ("Fh", ctypes.c_int64),
     ] + [(name, ctypes.c_void_p) for name in (
-        "x", "proj", "A_log", "omega", "detune_gain", "C", "D", "c_out", "env_gain", "y",
-        "ckpt", "dy", "dx", "dproj", "dA_log", "domega", "ddetune", "dC", "dD", "dc_out",
-        "denv", "workspace",
+        "x", "proj", "A_log", "omega", "detune_gain", "C", "D", "c_out", "env_gain", "dt_bias",
+        "y", "ckpt", "dy", "dx", "dproj", "dA_log", "domega", "ddetune", "dC", "dD", "dc_out",
+        "denv", "d_dt_bias", "workspace",
     )]
 
 

@@ -60,10 +60,11 @@ struct LParams {
   const float* D;
   const float* cout;
   const float* env;
+  const float* dtb;  // [b_nu (H) | b_th (H)] added to the dnu_raw / dth columns, or null
   float* y;
   float* ckpt;
   const float* dy;
-  float* dx;
+  void* dx;          // the dtype of x
   void* dproj;
   float* part;  // (S, K) partial parameter-gradient rows
   int64_t K;
@@ -74,7 +75,7 @@ struct Lay {
   int Cn, Cf, En, Ef, Co, Dp, prm;
   int xs, bx, raw, dnu, dth, sb, bt, sc, ct;
   int lam, gn, bu, hs, sr;
-  int dys, dr, gs, db, tn, acc;
+  int dys, dr, gs, db, tn, acc, rb;
   int total;
 };
 
@@ -116,8 +117,9 @@ __host__ __device__ inline Lay make_lay(int Nh, int Fh, int R, bool bwd, bool en
     l.db = take(kTC * Nh * 2);
     l.tn = take(5 * kTC * Nh);
     l.acc = take(Fh * Nh * 2 + (env ? Fh * Nh : 0) + R * Fh + Fh);
+    l.rb = take(2 * kTC);
   } else {
-    l.dys = l.dr = l.gs = l.db = l.tn = l.acc = -1;
+    l.dys = l.dr = l.gs = l.db = l.tn = l.acc = l.rb = -1;
   }
   l.total = o;
   return l;
@@ -138,6 +140,11 @@ __device__ __forceinline__ Cols cols_of(const LParams& p, int h) {
   c.ct = 2 * H + 2 * H * R + H * R * Nh + (int64_t)h * R * 2 * Nh;
   c.bx = 2 * H + 2 * H * R + 3 * H * R * Nh + (int64_t)h * 2 * Nh;
   return c;
+}
+
+// The dt_nu / dt_theta biases of head h (zero without them).
+__device__ __forceinline__ float2 dt_bias(const LParams& p, int h) {
+  return p.dtb ? make_float2(p.dtb[h], p.dtb[p.H + h]) : make_float2(0.f, 0.f);
 }
 
 template <bool BF16>
@@ -222,12 +229,13 @@ __device__ void stage_chunk(const LParams& p, const Lay& l, float* sm, int64_t s
     sm[l.xs + i] = ld<BF16>(p.x, row * Fd + (int64_t)h * Fh + f);
     if (bwd) sm[l.dys + i] = p.dy[row * Fd + (int64_t)h * Fh + f];
   }
+  const float2 bias = dt_bias(p, h);
   for (int t = threadIdx.x; t < nt; t += kT) {
     const int64_t row = (s * p.L + t0 + t) * p.P;
-    const float raw = ld<BF16>(p.proj, row + c.dnu);
+    const float raw = ld<BF16>(p.proj, row + c.dnu) + bias.x;
     sm[l.raw + t] = raw;
     sm[l.dnu + t] = semx::softplus(raw) * p.rs;
-    sm[l.dth + t] = ld<BF16>(p.proj, row + c.dth);
+    sm[l.dth + t] = ld<BF16>(p.proj, row + c.dth) + bias.y;
   }
   for (int i = threadIdx.x; i < nt * 2 * Nh; i += kT) {
     const int t = i / (2 * Nh), j = i % (2 * Nh);
@@ -373,7 +381,7 @@ __device__ __forceinline__ void stage_bulk(const LParams& p, const FLay& l, void
 // of this thread is i = tid + q kT over nt (2 + 2R) values.
 constexpr int kPre = 9;
 template <bool BF16, int RK>
-__device__ __forceinline__ void load_small(const LParams& p, int64_t s, int h, int t0, int nt,
+__device__ __forceinline__ void load_small(const LParams& p, int64_t s, int h, int t0, int nt, float2 bias,
                                            float (&pre)[kPre]) {
   const int R = RK >= 0 ? RK : (int)p.R, w = 2 + 2 * R;
   const Cols c = cols_of(p, h);
@@ -383,7 +391,7 @@ __device__ __forceinline__ void load_small(const LParams& p, int64_t s, int h, i
     if (i < nt * w) {
       const int t = i / w, j = i % w;
       const int64_t col = j == 0 ? c.dnu : j == 1 ? c.dth : j < 2 + R ? c.sb + (j - 2) : c.sc + (j - 2 - R);
-      pre[q] = ld<BF16>(p.proj, (s * p.L + t0 + t) * p.P + col);
+      pre[q] = ld<BF16>(p.proj, (s * p.L + t0 + t) * p.P + col) + (j == 0 ? bias.x : j == 1 ? bias.y : 0.f);
     }
   }
 }
@@ -551,11 +559,12 @@ __global__ void __launch_bounds__(kT) mimo_layer_fwd_kernel(const LParams p) {
   const float* Cr = sm + l.Cr;
   const float* Ci = sm + l.Ci;
   const int hw = l.hw;
+  const float2 bias = dt_bias(p, h);
   float pre[kPre];
   if (p.nchunks > 0) {
     const int nt0 = min(kTC, L);
     stage_bulk<BF16, NH, FH, RK>(p, l, sm + l.stg[0], s, h, 0, nt0);
-    load_small<BF16, RK>(p, s, h, 0, nt0, pre);
+    load_small<BF16, RK>(p, s, h, 0, nt0, bias, pre);
     store_small<RK>(p, sm + l.sml[0], nt0, pre);
   }
   cp_async_commit();
@@ -567,7 +576,7 @@ __global__ void __launch_bounds__(kT) mimo_layer_fwd_kernel(const LParams p) {
     __syncthreads();
     if (k + 1 < p.nchunks) {
       stage_bulk<BF16, NH, FH, RK>(p, l, sm + l.stg[b ^ 1], s, h, t0n, ntn);
-      load_small<BF16, RK>(p, s, h, t0n, ntn, pre);
+      load_small<BF16, RK>(p, s, h, t0n, ntn, bias, pre);
     }
     cp_async_commit();
     const T* xs = reinterpret_cast<const T*>(sm + l.stg[b]);
@@ -698,6 +707,7 @@ __global__ void __launch_bounds__(kT) mimo_layer_bwd_kernel(const LParams p) {
   const bool mode_thr = nthr >= 0 && nthr < Nh;
   float2 carry = make_float2(0.f, 0.f);
   float acc_a = 0.f, acc_om = 0.f, acc_sd = 0.f;
+  float acc_bnu = 0.f, acc_bth = 0.f;  // dt bias sums of token lane tid < kTC
 
   for (int k = p.nchunks - 1; k >= 0; --k) {
     const int t0 = k * kTC, nt = min(kTC, L - t0);
@@ -825,8 +835,11 @@ __global__ void __launch_bounds__(kT) mimo_layer_bwd_kernel(const LParams p) {
         st_ += tn[kTC * Nh + tid * Nh + n];
       }
       const int64_t row = (s * p.L + t0 + tid) * p.P;
-      st<BF16>(p.dproj, row + cols.dnu, sn * p.rs * semx::softplus_grad(sm[l.raw + tid]));
+      const float draw = sn * p.rs * semx::softplus_grad(sm[l.raw + tid]);
+      st<BF16>(p.dproj, row + cols.dnu, draw);
       st<BF16>(p.dproj, row + cols.dth, st_);
+      acc_bnu += draw;
+      acc_bth += st_;
     }
     if (mode_thr) {
       for (int t = nt - 1; t >= 0; --t) {
@@ -839,7 +852,7 @@ __global__ void __launch_bounds__(kT) mimo_layer_bwd_kernel(const LParams p) {
     // projection's backward); d(drive columns) = d(raw drive) per (t, n).
     for (int i = tid; i < nt * Fh; i += kT) {
       const int t = i / Fh, f = i % Fh;
-      p.dx[(s * p.L + t0 + t) * Fd + (int64_t)h * Fh + f] = sm[l.Dp + f] * sm[l.dys + i];
+      st<BF16>(p.dx, (s * p.L + t0 + t) * Fd + (int64_t)h * Fh + f, sm[l.Dp + f] * sm[l.dys + i]);
     }
     for (int i = tid; i < nt * 2 * Nh; i += kT) {
       const int t = i / (2 * Nh), j = i % (2 * Nh);
@@ -889,9 +902,13 @@ __global__ void __launch_bounds__(kT) mimo_layer_bwd_kernel(const LParams p) {
       }
     }
   }
+  if (tid < kTC) {
+    sm[l.rb + tid] = acc_bnu;
+    sm[l.rb + kTC + tid] = acc_bth;
+  }
   __syncthreads();
   // Partial row of sequence s, parameter-major so every segment is in output order:
-  // [dC | denv | dcout | dD | dA_log | domega | ddetune], each over all heads.
+  // [dC | denv | dcout | dD | dA_log | domega | ddetune | d dt bias], each over all heads.
   {
     const int64_t H = p.H;
     float* row = p.part + s * p.K;
@@ -908,6 +925,12 @@ __global__ void __launch_bounds__(kT) mimo_layer_bwd_kernel(const LParams p) {
       row[off + (int64_t)h * Nh + nthr] = acc_a * sm[l.prm + nthr];  // d/dA_log = a d/da
       row[off + H * Nh + (int64_t)h * Nh + nthr] = acc_om;
       row[off + 2 * H * Nh + (int64_t)h * Nh + nthr] = acc_sd;
+    }
+    off += 3 * H * Nh;
+    if (tid < 2) {  // over the token lanes in a fixed order
+      float acc = 0.f;
+      for (int q = 0; q < kTC; ++q) acc += sm[l.rb + tid * kTC + q];
+      row[off + tid * H + h] = acc;
     }
   }
 }
@@ -986,7 +1009,7 @@ __device__ __forceinline__ void chunk_scan_rev(const float2* lam, float2* gs, fl
 struct BLay {
   int Cfr, Cfi, Ef, Co, Dp, prm, cin, cadj;
   int stg[2], dys[2], sml[2];
-  int lam, gn, braw, hs, gs, db, sr, dr, red;
+  int lam, gn, braw, hs, gs, db, sr, dr, red, rb;
   int xw, bxw, btw, ctw, dyw;
   int total;
 };
@@ -1026,6 +1049,7 @@ __host__ __device__ inline BLay make_blay(int R, bool env, int es) {
   l.sr = take(CT * R);
   l.dr = take(CT * R);
   l.red = take(3 * NH * (kT / 8));
+  l.rb = take(2 * (kT / 8));
   l.total = o;
   return l;
 }
@@ -1076,6 +1100,8 @@ __global__ void __launch_bounds__(kT) mimo_layer_bwd16_kernel(const LParams p) {
   float acc_a[2] = {0.f, 0.f}, acc_om[2] = {0.f, 0.f}, acc_sd[2] = {0.f, 0.f};
   float aCr[4] = {}, aCi[4] = {}, aE[4] = {};
   float aO = 0.f, aD = 0.f;
+  float aBnu = 0.f, aBth = 0.f;  // dt bias sums of token lane tA (threads with npA == 0)
+  const float2 bias = dt_bias(p, h);
 
   const int nck = p.nck;
   float pre[kPre];
@@ -1097,7 +1123,7 @@ __global__ void __launch_bounds__(kT) mimo_layer_bwd16_kernel(const LParams p) {
   if (nck > 0) {
     const int k = nck - 1, nt = min(CT, L - k * CT);
     stage(k, 0);
-    load_small<BF16, RK>(p, s, h, k * CT, nt, pre);
+    load_small<BF16, RK>(p, s, h, k * CT, nt, bias, pre);
     store_small<RK, CT>(p, sm + l.sml[0], nt, pre);
   }
   cp_async_commit();
@@ -1108,7 +1134,7 @@ __global__ void __launch_bounds__(kT) mimo_layer_bwd16_kernel(const LParams p) {
     __syncthreads();
     if (k > 0) {
       stage(k - 1, b ^ 1);
-      load_small<BF16, RK>(p, s, h, (k - 1) * CT, CT, pre);
+      load_small<BF16, RK>(p, s, h, (k - 1) * CT, CT, bias, pre);
     }
     cp_async_commit();
     const T* xs = reinterpret_cast<const T*>(sm + l.stg[b]);
@@ -1272,8 +1298,11 @@ __global__ void __launch_bounds__(kT) mimo_layer_bwd16_kernel(const LParams p) {
       }
       if (npA == 0 && tA < nt) {
         const int64_t row = (s * p.L + t0 + tA) * p.P;
-        st<BF16>(p.dproj, row + cols.dnu, sdnu * p.rs * semx::softplus_grad(raws[tA]));
+        const float draw = sdnu * p.rs * semx::softplus_grad(raws[tA]);
+        st<BF16>(p.dproj, row + cols.dnu, draw);
         st<BF16>(p.dproj, row + cols.dth, sdth);
+        aBnu += draw;
+        aBth += sdth;
       }
     }
     __syncthreads();
@@ -1303,11 +1332,19 @@ __global__ void __launch_bounds__(kT) mimo_layer_bwd16_kernel(const LParams p) {
         st<BF16>(p.dproj, drow + 2, g1.x);
         st<BF16>(p.dproj, drow + 3, g1.y);
       }
-      float* dxr = p.dx + (s * p.L + t0 + t) * Fd + (int64_t)h * FH + f0;
+      const int64_t xo = (s * p.L + t0 + t) * Fd + (int64_t)h * FH + f0;
       if ((p.vec & 8) != 0) {
-        *reinterpret_cast<float4*>(dxr) = acc;
+        if (BF16) {
+          __nv_bfloat162 q[2] = {__floats2bfloat162_rn(acc.x, acc.y), __floats2bfloat162_rn(acc.z, acc.w)};
+          *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(p.dx) + xo) = *reinterpret_cast<const uint2*>(q);
+        } else {
+          *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.dx) + xo) = acc;
+        }
       } else {
-        dxr[0] = acc.x; dxr[1] = acc.y; dxr[2] = acc.z; dxr[3] = acc.w;
+        st<BF16>(p.dx, xo, acc.x);
+        st<BF16>(p.dx, xo + 1, acc.y);
+        st<BF16>(p.dx, xo + 2, acc.z);
+        st<BF16>(p.dx, xo + 3, acc.w);
       }
     }
     // H. Rank write: d s_b, d b_t.
@@ -1354,8 +1391,12 @@ __global__ void __launch_bounds__(kT) mimo_layer_bwd16_kernel(const LParams p) {
     red[(1 * NH + n) * (kT / 8) + tA] = acc_om[dn];
     red[(2 * NH + n) * (kT / 8) + tA] = acc_sd[dn];
   }
+  if (npA == 0) {
+    sm[l.rb + tA] = aBnu;
+    sm[l.rb + kT / 8 + tA] = aBth;
+  }
   __syncthreads();
-  // Partial row of sequence s: [dC | denv | dcout | dD | dA_log | domega | ddetune].
+  // Partial row of sequence s: [dC | denv | dcout | dD | dA_log | domega | ddetune | d dt bias].
   const int64_t H = p.H;
   float* row = p.part + s * p.K;
   int64_t off = 0;
@@ -1384,6 +1425,12 @@ __global__ void __launch_bounds__(kT) mimo_layer_bwd16_kernel(const LParams p) {
     if (which == 0) acc *= sm[l.prm + n];  // d/dA_log = a d/da
     row[off + which * H * NH + (int64_t)h * NH + n] = acc;
   }
+  off += 3 * H * NH;
+  if (tid < 2) {  // dt bias: over the token lanes in a fixed order
+    float acc = 0.f;
+    for (int q = 0; q < kT / 8; ++q) acc += sm[l.rb + tid * (kT / 8) + q];
+    row[off + tid * H + h] = acc;
+  }
 }
 
 // ------------------------------------------------------------------------ host side
@@ -1393,7 +1440,7 @@ int64_t proj_width(const SemxMimoLayerArgs* a) {
 
 int64_t part_row(const SemxMimoLayerArgs* a) {
   const int64_t H = a->H, Nh = a->Nh, Fh = a->Fh, R = a->rank;
-  return H * (2 * Nh * Fh + (a->envelope ? Fh * Nh : 0) + R * Fh + Fh + 3 * Nh);
+  return H * (2 * Nh * Fh + (a->envelope ? Fh * Nh : 0) + R * Fh + Fh + 3 * Nh + 2);
 }
 
 // The backward of 16-mode, 32-channel heads of rank 0 or 4 has its own kernel.
@@ -1415,7 +1462,7 @@ int vec_flags(const SemxMimoLayerArgs* a) {
   const bool vp = semx::aligned(a->proj, 16) && (P * es) % 16 == 0 && ((2 * H + H * R) * es) % 16 == 0 &&
                   ((R * Nh * es) % 16) == 0 && ((2 * H + 2 * H * R + H * R * Nh) * es) % 16 == 0;
   const bool vdy = semx::aligned(a->dy, 16) && (H * Fh * 4) % 16 == 0 && (Fh * 4) % 16 == 0;
-  const bool vdx = semx::aligned(a->dx, 16) && (H * Fh * 4) % 16 == 0 && (Fh * 4) % 16 == 0;
+  const bool vdx = semx::aligned(a->dx, 16) && Fh % 4 == 0;
   const int64_t bx0 = 2 * H + 2 * H * R + 3 * H * R * Nh;
   const bool vbx = semx::aligned(a->proj, 16) && (a->dproj == nullptr || semx::aligned(a->dproj, 16)) &&
                    (P * es) % 16 == 0 && (bx0 * es) % 16 == 0 && (2 * Nh * es) % 16 == 0;
@@ -1473,7 +1520,7 @@ LParams to_lparams(const SemxMimoLayerArgs* a) {
   p.rs = a->rate_scale;
   p.x = a->x; p.proj = a->proj;
   p.A_log = a->A_log; p.omega = a->omega; p.sdet = a->detune_gain; p.C = a->C; p.D = a->D;
-  p.cout = a->c_out; p.env = a->env_gain;
+  p.cout = a->c_out; p.env = a->env_gain; p.dtb = a->dt_bias;
   p.y = a->y; p.ckpt = a->ckpt; p.dy = a->dy; p.dx = a->dx; p.dproj = a->dproj;
   p.K = part_row(a);
   p.vec = vec_flags(a);
@@ -1585,6 +1632,7 @@ int semx_mimo_layer_bwd(const SemxMimoLayerArgs* a, semx_stream_t stream) {
   add(a->dA_log, H * Nh);
   add(a->domega, H * Nh);
   add(a->detune ? a->ddetune : nullptr, H * Nh);
+  add(a->dt_bias ? a->d_dt_bias : nullptr, 2 * H);
   seg.n = n;
   return semx::colsum(ws, a->S, p.K, ws + (size_t)a->S * p.K, seg, st);
 }

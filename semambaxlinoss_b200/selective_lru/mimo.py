@@ -132,72 +132,125 @@ def fused_selective_lru_mimo(lam_re, lam_im, Bu_re, Bu_im, C_re, C_im, x, D, n_h
                             int(n_heads), int(n_head), int(f_head))
 
 
+def _layer_fwd(x, proj, dt_bias, params, dims, want_ckpt):
+    """semx_mimo_layer_fwd on contiguous x / proj (same dtype) and fp32 parameters
+    (A_log, omega, detune_gain, C, D, c_out, env_gain). Returns (y, ckpt or None)."""
+    H, Nh, Fh, rank, gain_code, rate_scale = dims
+    S, L, Fd = x.shape
+    y = torch.empty((S, L, Fd), dtype=torch.float32, device=x.device)
+    a = _lib.new_args(_lib.SemxMimoLayerArgs)
+    a.input_gain, a.rank, a.rate_scale = gain_code, rank, float(rate_scale)
+    a.detune, a.envelope = int(params[2] is not None), int(params[6] is not None)
+    a.bf16 = int(x.dtype == torch.bfloat16)
+    a.S, a.L, a.H, a.Nh, a.Fh = S, L, H, Nh, Fh
+    a.x, a.proj, a.y, a.dt_bias = x.data_ptr(), proj.data_ptr(), y.data_ptr(), _lib.ptr(dt_bias)
+    (a.A_log, a.omega, a.detune_gain, a.C, a.D, a.c_out, a.env_gain) = [_lib.ptr(t) for t in params]
+    ckpt = None
+    if want_ckpt:
+        ckpt = _lib.empty_f32(_lib.load().semx_mimo_layer_ckpt_bytes(a), x.device)
+        a.ckpt = ckpt.data_ptr()
+    _lib.call("semx_mimo_layer_fwd", a, x.device)
+    return y, ckpt
+
+
+def _layer_bwd(x, proj, ckpt, dt_bias, params, dims, dy):
+    """semx_mimo_layer_bwd. Returns dx (the skip part D dy, dtype of x), dproj and the
+    parameter gradients as a dict (dA_log, domega, ddetune, dC, dD, dc_out, denv,
+    d_dt_bias; None where the operand is absent)."""
+    A_log, omega, det, C, D, c_out, env = params
+    H, Nh, Fh, rank, gain_code, rate_scale = dims
+    S, L, Fd = x.shape
+    dev = x.device
+    dx = torch.empty_like(x)
+    dproj = torch.empty_like(proj)
+    g = {k: torch.empty_like(v) for k, v in (("dA_log", A_log), ("domega", omega), ("dC", C), ("dD", D))}
+    g["ddetune"] = torch.empty_like(det) if det is not None else None
+    g["dc_out"] = torch.empty_like(c_out) if rank > 0 else None
+    g["denv"] = torch.empty_like(env) if env is not None else None
+    g["d_dt_bias"] = torch.empty_like(dt_bias) if dt_bias is not None else None
+    a = _lib.new_args(_lib.SemxMimoLayerArgs)
+    a.input_gain, a.rank, a.rate_scale = gain_code, rank, float(rate_scale)
+    a.detune, a.envelope = int(det is not None), int(env is not None)
+    a.bf16 = int(x.dtype == torch.bfloat16)
+    a.S, a.L, a.H, a.Nh, a.Fh = S, L, H, Nh, Fh
+    a.x, a.proj, a.ckpt, a.dy, a.dx, a.dproj = [t.data_ptr() for t in (x, proj, ckpt, dy, dx, dproj)]
+    a.dt_bias = _lib.ptr(dt_bias)
+    (a.A_log, a.omega, a.detune_gain, a.C, a.D, a.c_out, a.env_gain) = [_lib.ptr(t) for t in params]
+    for k, v in g.items():
+        setattr(a, k, _lib.ptr(v))
+    ws = _lib.empty_f32(_lib.load().semx_mimo_layer_workspace_bytes(a), dev)
+    a.workspace = ws.data_ptr()
+    _lib.call("semx_mimo_layer_bwd", a, dev)
+    return dx, dproj, g
+
+
+def _check_layer(x, proj_cols, C, dims, tensors):
+    H, Nh, Fh, rank = dims[:4]
+    for t in tensors:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError("SelectiveLRUMIMO requires CUDA tensors.")
+    if x.dtype not in (torch.float32, torch.bfloat16):
+        raise ValueError(f"SelectiveLRUMIMO: unsupported dtype {x.dtype}")
+    if x.dim() != 3 or x.shape[2] != H * Fh or C.shape != (H, Fh, Nh, 2) or proj_cols != proj_width(H, Nh, rank):
+        raise ValueError("SelectiveLRUMIMO operand shapes do not agree")
+
+
 class _MimoLayer(torch.autograd.Function):
     """The SelectiveLRUMIMO layer after its token projections (semx_mimo_layer_fwd/bwd):
     poles, gain, scan, readout and feedthrough in one kernel per direction."""
 
     @staticmethod
-    def forward(ctx, x, proj, A_log, omega, detune_gain, C, D, c_out, env_gain, dims):
-        H, Nh, Fh, rank, gain_code, rate_scale = dims
-        for t in (x, proj, A_log, omega, C, D):
-            if not t.is_cuda:
-                raise RuntimeError("SelectiveLRUMIMO requires CUDA tensors.")
-        if x.dtype != proj.dtype or x.dtype not in (torch.float32, torch.bfloat16):
-            raise ValueError("x and proj must both be float32 or both bfloat16")
-        S, L, Fd = x.shape
-        if Fd != H * Fh or C.shape != (H, Fh, Nh, 2) or proj.shape != (S, L, proj_width(H, Nh, rank)):
-            raise ValueError("SelectiveLRUMIMO operand shapes do not agree")
-        x = x.contiguous()
-        proj = proj.contiguous()
+    def forward(ctx, x, proj, dt_bias, A_log, omega, detune_gain, C, D, c_out, env_gain, dims):
+        _check_layer(x, proj.shape[-1], C, dims, (x, proj, A_log, omega, C, D))
+        if x.dtype != proj.dtype or proj.shape[:2] != x.shape[:2]:
+            raise ValueError("x and proj must have the same dtype and leading shape")
+        x, proj = x.contiguous(), proj.contiguous()
         params = [_f32(t) for t in (A_log, omega, detune_gain, C, D, c_out, env_gain)]
-        y = torch.empty((S, L, Fd), dtype=torch.float32, device=x.device)
-        a = _lib.new_args(_lib.SemxMimoLayerArgs)
-        a.input_gain, a.rank, a.rate_scale = gain_code, rank, float(rate_scale)
-        a.detune, a.envelope = int(detune_gain is not None), int(env_gain is not None)
-        a.bf16 = int(x.dtype == torch.bfloat16)
-        a.S, a.L, a.H, a.Nh, a.Fh = S, L, H, Nh, Fh
-        a.x, a.proj, a.y = x.data_ptr(), proj.data_ptr(), y.data_ptr()
-        (a.A_log, a.omega, a.detune_gain, a.C, a.D, a.c_out, a.env_gain) = [_lib.ptr(t) for t in params]
-        ckpt = None
-        if any(ctx.needs_input_grad):
-            ckpt = _lib.empty_f32(_lib.load().semx_mimo_layer_ckpt_bytes(a), x.device)
-            a.ckpt = ckpt.data_ptr()
-        _lib.call("semx_mimo_layer_fwd", a, x.device)
+        dtb = _f32(dt_bias)
+        y, ckpt = _layer_fwd(x, proj, dtb, params, dims, any(ctx.needs_input_grad))
         if ckpt is not None:
-            ctx.save_for_backward(x, proj, ckpt, *params)
+            ctx.save_for_backward(x, proj, ckpt, dtb, *params)
             ctx.dims = dims
-            ctx.flags = (a.detune, a.envelope)
         return y
 
     @staticmethod
     def backward(ctx, dy):
-        x, proj, ckpt, A_log, omega, det, C, D, c_out, env = ctx.saved_tensors
-        H, Nh, Fh, rank, gain_code, rate_scale = ctx.dims
-        detune, envelope = ctx.flags
-        S, L, Fd = x.shape
-        dev = x.device
-        dy = _f32(dy)
-        dx = torch.empty((S, L, Fd), dtype=torch.float32, device=dev)
-        dproj = torch.empty_like(proj)
-        g = {k: torch.empty_like(v) for k, v in (("dA_log", A_log), ("domega", omega), ("dC", C), ("dD", D))}
-        g["ddetune"] = torch.empty_like(det) if detune else None
-        g["dc_out"] = torch.empty_like(c_out) if rank > 0 else None
-        g["denv"] = torch.empty_like(env) if envelope else None
-        a = _lib.new_args(_lib.SemxMimoLayerArgs)
-        a.input_gain, a.rank, a.rate_scale = gain_code, rank, float(rate_scale)
-        a.detune, a.envelope = detune, envelope
-        a.bf16 = int(x.dtype == torch.bfloat16)
-        a.S, a.L, a.H, a.Nh, a.Fh = S, L, H, Nh, Fh
-        a.x, a.proj, a.ckpt, a.dy, a.dx, a.dproj = [t.data_ptr() for t in (x, proj, ckpt, dy, dx, dproj)]
-        (a.A_log, a.omega, a.detune_gain, a.C, a.D, a.c_out, a.env_gain) = [
-            _lib.ptr(t) for t in (A_log, omega, det, C, D, c_out, env)]
-        for k, v in g.items():
-            setattr(a, k, _lib.ptr(v))
-        ws = _lib.empty_f32(_lib.load().semx_mimo_layer_workspace_bytes(a), dev)
-        a.workspace = ws.data_ptr()
-        _lib.call("semx_mimo_layer_bwd", a, dev)
-        return (dx.to(x.dtype), dproj, g["dA_log"], g["domega"], g["ddetune"], g["dC"],
-                g["dD"], g["dc_out"], g["denv"], None)
+        x, proj, ckpt, dtb, *params = ctx.saved_tensors
+        dx, dproj, g = _layer_bwd(x, proj, ckpt, dtb, params, ctx.dims, _f32(dy))
+        return (dx, dproj, g["d_dt_bias"], g["dA_log"], g["domega"], g["ddetune"], g["dC"], g["dD"],
+                g["dc_out"], g["denv"], None)
+
+
+class _MimoLayerProjected(torch.autograd.Function):
+    """The whole SelectiveLRUMIMO layer from its concatenated projection weight W
+    (P, H Fh): proj = x W^T (one GEMM), then the layer kernels. The backward's input
+    gradient is one accumulating GEMM, dx = D dy + dproj W, and dW = dproj^T x."""
+
+    @staticmethod
+    def forward(ctx, x, W, dt_bias, A_log, omega, detune_gain, C, D, c_out, env_gain, dims):
+        _check_layer(x, W.shape[0], C, dims, (x, W, A_log, omega, C, D))
+        if W.dtype != x.dtype or W.shape[1] != x.shape[2]:
+            raise ValueError("W must be (P, in_features) in the dtype of x")
+        x, W = x.contiguous(), W.contiguous()
+        proj = torch.matmul(x, W.t())
+        params = [_f32(t) for t in (A_log, omega, detune_gain, C, D, c_out, env_gain)]
+        dtb = _f32(dt_bias)
+        y, ckpt = _layer_fwd(x, proj, dtb, params, dims, any(ctx.needs_input_grad))
+        if ckpt is not None:
+            ctx.save_for_backward(x, W, proj, ckpt, dtb, *params)
+            ctx.dims = dims
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, W, proj, ckpt, dtb, *params = ctx.saved_tensors
+        dx, dproj, g = _layer_bwd(x, proj, ckpt, dtb, params, ctx.dims, _f32(dy))
+        P, Fd = W.shape
+        dproj2 = dproj.view(-1, P)
+        dx.view(-1, Fd).addmm_(dproj2, W)
+        dW = dproj2.t().mm(x.view(-1, Fd)) if ctx.needs_input_grad[1] else None
+        return (dx, dW, g["d_dt_bias"], g["dA_log"], g["domega"], g["ddetune"], g["dC"], g["dD"],
+                g["dc_out"], g["denv"], None)
 
 
 def proj_width(n_heads, n_head, rank):
@@ -215,16 +268,31 @@ def drive_weight(B):
 
 
 def mimo_layer(x, proj, A_log, omega, detune_gain, C, D, c_out, env_gain, n_heads, n_head,
-               f_head, rank, input_gain="gamma", rate_scale=1.0):
+               f_head, rank, input_gain="gamma", rate_scale=1.0, dt_bias=None):
     """SelectiveLRUMIMO after its token projections. ``proj`` (B, T, P) holds, per token,
     [dnu_raw (H) | dth (H) | s_b (H r) | b_t (H r Nh) | s_c (H r) | c_t (H r 2Nh) |
-    bx (H 2Nh)] with dnu = softplus(dnu_raw) * rate_scale and bx the static drive
+    bx (H 2Nh)] with dnu = softplus(dnu_raw + b_nu) * rate_scale, dth = dth + b_th
+    (``dt_bias`` = [b_nu (H) | b_th (H)], optional) and bx the static drive
     (sum_f B[h, n, f] x[h Fh + f], real and imaginary part per mode; :func:`drive_weight`
     gives its weight rows); ``x`` (B, T, H Fh) and ``proj`` are both float32 or both
     bfloat16 (state and outputs are float32). Returns y (B, T, H Fh) float32; the
     gradient reaching x directly is the skip part D dy, the drive's part flows through
     ``proj``."""
+    return _MimoLayer.apply(x, proj, dt_bias, A_log, omega, detune_gain, C, D, c_out, env_gain,
+                            _dims(n_heads, n_head, f_head, rank, input_gain, rate_scale))
+
+
+def mimo_layer_projected(x, W, dt_bias, A_log, omega, detune_gain, C, D, c_out, env_gain, n_heads,
+                         n_head, f_head, rank, input_gain="gamma", rate_scale=1.0):
+    """The whole SelectiveLRUMIMO layer: :func:`mimo_layer` on ``proj = x W^T`` with the
+    projection GEMM inside the operator (``W`` (P, H Fh) in the dtype of ``x``, rows in
+    the column order of :func:`mimo_layer`), so its backward forms the input gradient in
+    one accumulating GEMM."""
+    return _MimoLayerProjected.apply(x, W, dt_bias, A_log, omega, detune_gain, C, D, c_out, env_gain,
+                                     _dims(n_heads, n_head, f_head, rank, input_gain, rate_scale))
+
+
+def _dims(n_heads, n_head, f_head, rank, input_gain, rate_scale):
     if input_gain not in _lib.GAIN_CODES:
         raise ValueError(f"input_gain must be 'gamma', 'mamba', 'zoh', or 'none', got {input_gain!r}")
-    dims = (int(n_heads), int(n_head), int(f_head), int(rank), _lib.GAIN_CODES[input_gain], float(rate_scale))
-    return _MimoLayer.apply(x, proj, A_log, omega, detune_gain, C, D, c_out, env_gain, dims)
+    return (int(n_heads), int(n_head), int(f_head), int(rank), _lib.GAIN_CODES[input_gain], float(rate_scale))

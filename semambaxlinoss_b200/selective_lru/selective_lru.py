@@ -259,42 +259,36 @@ class SelectiveLRUMIMO(nn.Module):
         self.D._no_weight_decay = True
 
     def _projection(self):
-        """Weight and bias of all token projections as one matrix, rows in the order the
-        fused layer kernel reads them: [dt_nu (H) | dt_theta (H) | b_coef (H r) |
-        b_dir (H r Nh) | c_coef (H r) | c_read (2 H r Nh) | static drive B (2 H Nh,
-        block-diagonal)]. The static drive B x is computed (and back-propagated) in the
-        projection GEMM, so dB comes from the GEMM's weight gradient."""
+        """All token projections as one weight matrix, rows in the order the fused layer
+        kernels read them: [dt_nu (H) | dt_theta (H) | b_coef (H r) | b_dir (H r Nh) |
+        c_coef (H r) | c_read (2 H r Nh) | static drive B (2 H Nh, block-diagonal)], and
+        the dt biases [dt_nu (H) | dt_theta (H)], which the kernels add themselves (the
+        other projections have none). The static drive B x is computed (and
+        back-propagated) in the projection GEMM, so dB comes from its weight gradient."""
         from .mimo import drive_weight
 
         ws = [self.dt_nu_proj.weight, self.dt_theta_proj.weight]
         if self.rank > 0:
             ws += [self.b_coef.weight, self.b_dir.weight, self.c_coef.weight, self.c_read.weight]
         ws.append(drive_weight(self.B))
-        W = torch.cat(ws, 0)
-        b = torch.cat([self.dt_nu_proj.bias, self.dt_theta_proj.bias,
-                       self.dt_nu_proj.bias.new_zeros(W.shape[0] - 2 * self.n_heads)])
-        return W, b
+        return torch.cat(ws, 0), torch.cat([self.dt_nu_proj.bias, self.dt_theta_proj.bias])
 
     def forward(self, x: torch.Tensor, rate_scale: float | None = None) -> torch.Tensor:
         """Float32 input runs in float32; bfloat16 input (or float32 input under CUDA bf16
         autocast) runs the projections and the kernel's operand reads in bfloat16 with
         float32 state, accumulation and output."""
-        from .mimo import mimo_layer
+        from .mimo import mimo_layer_projected
 
         bf16 = x.dtype == torch.bfloat16 or (
             x.is_cuda and torch.is_autocast_enabled("cuda")
             and torch.get_autocast_dtype("cuda") == torch.bfloat16)
-        W, b = self._projection()
+        W, dt_bias = self._projection()
         with torch.autocast("cuda", enabled=False):
-            if bf16:
-                x = x.to(torch.bfloat16)
-                proj = F.linear(x, W.to(torch.bfloat16), b.to(torch.bfloat16))
-            else:
-                x = x.float()
-                proj = F.linear(x, W, b)
+            dt = torch.bfloat16 if bf16 else torch.float32
             rs = self.rate_scale if rate_scale is None else float(rate_scale)
-            return mimo_layer(
-                x, proj, self.A_log, self.omega, self.detune_gain if self.mode_detune else None,
+            return mimo_layer_projected(
+                x.to(dt), W.to(dt), dt_bias, self.A_log, self.omega,
+                self.detune_gain if self.mode_detune else None,
                 self.C, self.D, self.c_out if self.rank > 0 else None,
                 self.env_gain if self.envelope_readout else None, self.n_heads, self.n_head,
                 self.f_head, self.rank, self.input_gain, rs)

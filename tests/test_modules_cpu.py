@@ -112,5 +112,5 @@ def test_mimo_drive_weight_layout():
     assert torch.allclose(bx, want, rtol=0, atol=1e-12)
     m = SelectiveLRUMIMO(24, 16, n_heads=2, rank=3)
     W, b = m._projection()
-    assert W.shape == (proj_width(2, 8, 3), 24) and b.shape == (W.shape[0],)
+    assert W.shape == (proj_width(2, 8, 3), 24) and b.shape == (2 * 2,)
     assert torch.equal(W[-2 * 16:], drive_weight(m.B.detach()))

@@ -81,9 +81,11 @@ uint64_t semx_launch_count(void);
  *   _apply_damped_linoss_imex (models/linoss/linoss.py:183-232). Input is Bu (S,L,P)
  *   complex, the projected input of _project_input (models/linoss/linoss.py:148-152).
  *
- * Forward writes Y2 and, if ckpt != NULL, the state entering every `chunk`-step block:
- *   ckpt (S, ceil(L/chunk), P, 4) fp32 = (y1.re, y1.im, y2.re, y2.im).
- * Backward (needs the forward's ckpt) recomputes the states chunk by chunk and writes
+ * Forward writes Y2 and, if ckpt != NULL, the state entering every `chunk`-step block
+ * and the final state: ckpt (S, ceil(L/chunk) + 1, P, 4) fp32 = (y1.re, y1.im, y2.re,
+ * y2.im). Backward (needs the forward's ckpt) rebuilds the states chunk by chunk (IMEX:
+ * running the symplectic recurrence backwards from each chunk's end; otherwise, or for
+ * oscillators with step^2 A near or above 4, re-running it from the chunk start) and writes
  *   GENERIC: dF1, dF2 (S,L,P) complex and dM (4,P) = dM11, dM12, dM21, dM22;
  *   fused:   dBu (S,L,P) complex and dparams (3,P) = d steps, d A_diag, d G_diag
  *            (d G_diag row written only for DAMPED_IMEX).
@@ -117,7 +119,7 @@ typedef struct SemxLinossArgs {
   const float* Bu;     /* (S,L,P) complex            */
   /* forward outputs */
   float* Y2;   /* (S,L,P) complex */
-  float* ckpt; /* (S, ceil(L/chunk), P, 4) or NULL */
+  float* ckpt; /* (S, ceil(L/chunk) + 1, P, 4) or NULL */
   /* backward */
   const float* dY2; /* (S,L,P) complex */
   float* dF1;       /* GENERIC (S,L,P) complex */
@@ -131,7 +133,8 @@ typedef struct SemxLinossArgs {
 size_t semx_linoss_args_size(void);
 /* Size of ckpt in bytes for (S, L, P, chunk). */
 size_t semx_linoss_ckpt_bytes(int64_t S, int64_t L, int64_t P, int32_t chunk);
-/* Scratch the backward needs (per-sequence partial reductions). */
+/* Scratch the backward needs (per-sequence partial reductions, and for IMEX the list
+ * of thread blocks the reversal backward hands to the recompute backward). */
 size_t semx_linoss_workspace_bytes(const SemxLinossArgs* args);
 int semx_linoss_fwd(const SemxLinossArgs* args, semx_stream_t stream);
 int semx_linoss_bwd(const SemxLinossArgs* args, semx_stream_t stream);

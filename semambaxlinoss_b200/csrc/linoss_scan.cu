@@ -13,15 +13,25 @@
 // every thread keeps 8 loads in flight.
 //
 // Forward (training) additionally stores the state entering every `chunk`-step block
-// (16 B per chunk and chain). Backward walks the chunks in reverse. For each chunk it
-// re-runs the recurrence once from the checkpoint, dropping the state every kSub steps
-// into shared memory; then for each kSub-step sub-block (last first) it recomputes the
-// kSub states into registers and runs the adjoint
-//   a_t = (0, dY2_t) + M^T a_{t+1},  dF_t = a_t,  dM_ij += Re(a_i,t conj(s_j,t-1)),
-// so no per-step state ever goes to HBM. Per-oscillator parameter gradients are summed
-// per chain in registers, written once per chain, and reduced over sequences by
-// linoss_finalize_kernel in a fixed order (bitwise deterministic), which also applies
-// the chain rule from (M, f) back to the raw parameters.
+// and the final state (16 B per chunk and chain). The backward runs the adjoint
+//   a_t = (0, dY2_t) + M^T a_{t+1},  dF_t = a_t,  dM_ij += Re(a_i,t conj(s_j,t-1))
+// backwards in time and needs the forward states s_{t-1}; no per-step state goes to HBM.
+//   * IMEX (linoss_bwd_rev_kernel): M has determinant 1 (the scheme is symplectic), so
+//     the state is run backwards with the adjoint, s_{t-1} = M^-1 (s_t - F_t), from each
+//     chunk's end state and reset to the exact checkpoint at every chunk start. With both
+//     eigenvalues on the unit circle (trace > -2) this is as accurate as re-running the
+//     recurrence; a CTA holding an oscillator outside that range (step^2 A near or
+//     above 4, where the reversal amplifies rounding) does not run it and is listed for
+//     the recompute kernel instead.
+//   * otherwise (linoss_bwd_kernel): for each chunk, re-run the recurrence once from the
+//     checkpoint, dropping the state every kSub steps into shared memory; then for each
+//     kSub-step sub-block (last first) recompute the kSub states into registers and run
+//     the adjoint through them.
+// Per-oscillator parameter gradients are summed per chain in registers, written once per
+// chain, and reduced over sequences by linoss_finalize_kernel in a fixed order (bitwise
+// deterministic), which also applies the chain rule from (M, f) back to the raw
+// parameters.
+#include <algorithm>
 #include <mutex>
 
 #include "semx_common.cuh"
@@ -32,6 +42,11 @@ constexpr int kBlock = 128;  // threads per CTA (scan kernels)
 constexpr int kSub = 8;      // steps per register-resident sub-block
 constexpr int kMaxChunk = 256;
 constexpr int kPartials = 6;  // dM11, dM12, dM21, dM22, df1, df2
+constexpr int kLook = 8;      // steps per staged batch of the reversal backward
+constexpr int kStages = 3;    // staged batches in flight (reversal backward)
+static_assert(kSub % kLook == 0, "chunk (a multiple of kSub) must be a multiple of kLook");
+// Reversal backward only for transitions with trace above this (IMEX: step^2 A < 3.99).
+constexpr float kRevTraceMin = -1.99f;
 
 struct Coef {
   float m11, m12, m21, m22;  // transition
@@ -60,7 +75,13 @@ struct Params {
   float* dM;
   float* dparams;
   float* part;  // (S, kPartials, P)
+  // Checkpoint slot j of chain (s, o) at ckpt[(s * (nchunks + 1) + j) * P + o]: the state
+  // entering chunk j; slot nchunks is the final state.
 };
+
+__host__ __device__ inline int64_t ckpt_index(const Params& p, int64_t s, int j, int o) {
+  return (s * (p.nchunks + 1) + j) * p.P + o;
+}
 
 __device__ __forceinline__ float sigmoid_f(float x) { return 1.0f / (1.0f + expf(-x)); }
 __device__ __forceinline__ float relu_f(float x) { return x > 0.0f ? x : 0.0f; }
@@ -199,8 +220,7 @@ __global__ void __launch_bounds__(kBlock) linoss_fwd_kernel(const Params p) {
   for (int t0 = 0; t0 < L; t0 += kSub) {
     float2 n1[kSub], n2[kSub];
     load_batch<GENERIC>(src1, src2, P, t0 + kSub, L, n1, n2);
-    if (p.ckpt != nullptr && (t0 % p.chunk) == 0)
-      p.ckpt[(s * p.nchunks + t0 / p.chunk) * p.P + o] = st;
+    if (p.ckpt != nullptr && (t0 % p.chunk) == 0) p.ckpt[ckpt_index(p, s, t0 / p.chunk, o)] = st;
 #pragma unroll
     for (int i = 0; i < kSub; ++i) {
       if (t0 + i < L) {
@@ -216,6 +236,7 @@ __global__ void __launch_bounds__(kBlock) linoss_fwd_kernel(const Params p) {
       c2[i] = n2[i];
     }
   }
+  if (p.ckpt != nullptr) p.ckpt[ckpt_index(p, s, p.nchunks, o)] = st;
 }
 
 // Shared memory of the backward kernel, per thread (kBlock threads, slot = threadIdx.x):
@@ -238,9 +259,9 @@ __device__ __forceinline__ void prefetch_sub(float2* in_buf, float2* dy_buf,
   }
 }
 
+// The chains of thread block `blk` (kBlock consecutive chains).
 template <bool GENERIC>
-__global__ void __launch_bounds__(kBlock, 4) linoss_bwd_kernel(const Params p) {
-  extern __shared__ float4 smem4[];
+__device__ __forceinline__ void bwd_block(const Params& p, int blk, float4* smem4) {
   constexpr int kIn = GENERIC ? 2 : 1;
   const int nsub_max = p.chunk / kSub;
   float4* sub_ckpt = smem4;                                            // [nsub_max][kBlock]
@@ -248,7 +269,7 @@ __global__ void __launch_bounds__(kBlock, 4) linoss_bwd_kernel(const Params p) {
   float2* dy_base = in_base + 2 * kIn * kSub * kBlock;                     // [2][kSub][kBlock]
   const int tid = threadIdx.x;
 
-  const int64_t gid = (int64_t)blockIdx.x * kBlock + tid;
+  const int64_t gid = (int64_t)blk * kBlock + tid;
   if (gid >= p.S * p.P) return;
   const int64_t s = gid / p.P;
   const int o = (int)(gid - s * p.P);
@@ -276,7 +297,7 @@ __global__ void __launch_bounds__(kBlock, 4) linoss_bwd_kernel(const Params p) {
 
     // Pass 1: recurrence over the chunk, keeping the state every kSub steps on chip.
     {
-      float4 st = p.ckpt[(s * p.nchunks + c) * p.P + o];
+      float4 st = p.ckpt[ckpt_index(p, s, c, o)];
       float2 c1[kSub], c2[kSub];
       load_batch<GENERIC>(src1, src2, P, t0, t1, c1, c2);
       for (int tb = t0; tb < t1; tb += kSub) {
@@ -368,9 +389,151 @@ __global__ void __launch_bounds__(kBlock, 4) linoss_bwd_kernel(const Params p) {
   part[5 * p.P] = gf2;
 }
 
+// Without `list`, CTA b processes block b. With `list` (the reversal kernel's fallback
+// list: a count, then block indices), the CTAs walk the listed blocks grid-stride; every
+// block's copies are complete when bwd_block returns, so shared memory is reused safely.
+template <bool GENERIC>
+__global__ void __launch_bounds__(kBlock, 4) linoss_bwd_kernel(const Params p, const int* list) {
+  extern __shared__ float4 smem4[];
+  if (GENERIC || list == nullptr) {  // the generic operator never has a list
+    bwd_block<GENERIC>(p, (int)blockIdx.x, smem4);
+    return;
+  }
+  const int n = list[0];
+  for (int i = (int)blockIdx.x; i < n; i += (int)gridDim.x) bwd_block<GENERIC>(p, list[1 + i], smem4);
+}
+
 __host__ __device__ inline size_t bwd_smem_bytes(int chunk, bool generic) {
   return (size_t)(chunk / kSub) * kBlock * sizeof(float4) +
          (size_t)2 * ((generic ? 2 : 1) + 1) * kSub * kBlock * sizeof(float2);
+}
+
+// Stages the Bu and dY2 values of steps [tb, te) of this thread's chain into its slots of
+// one stage buffer (slot i of a buffer at i * kBlock).
+__device__ __forceinline__ void stage_batch(float2* in_buf, float2* dy_buf, const float2* bu,
+                                            const float2* dys, int P, int tb, int te) {
+#pragma unroll
+  for (int i = 0; i < kLook; ++i) {
+    if (tb + i < te) {
+      cp_async8(in_buf + i * kBlock, bu + (tb + i) * P);
+      cp_async8(dy_buf + i * kBlock, dys + (tb + i) * P);
+    }
+  }
+}
+
+__host__ __device__ inline size_t rev_smem_bytes() { return (size_t)2 * kStages * kLook * kBlock * sizeof(float2); }
+
+// IMEX backward with the state run backwards in time (see the file comment). Batches of
+// kLook steps, last first; Bu and dY2 of batch b - (kStages - 1) are staged by cp.async
+// while batch b runs, so every load is issued two batches (16 steps) before its use.
+// That lookahead, not the warp count, is what keeps HBM busy: measured against 2 stages
+// at 6 CTAs/SM and register prefetch variants, 3 stages at 4 CTAs/SM is fastest.
+// chunk is a multiple of kLook, so every chunk starts a batch.
+// Shared memory: in[kStages][kLook][kBlock], dy[kStages][kLook][kBlock] float2, per-thread
+// slots (no block barrier after the stability vote; a stage is refilled only by the
+// thread that consumed it in the previous batch).
+__global__ void __launch_bounds__(kBlock, 4) linoss_bwd_rev_kernel(const Params p, int* fallback) {
+  extern __shared__ float4 smem4[];
+  float2* in_base = reinterpret_cast<float2*>(smem4);
+  float2* dy_base = in_base + kStages * kLook * kBlock;
+  const int tid = threadIdx.x;
+  const int64_t gid = (int64_t)blockIdx.x * kBlock + tid;
+  const bool active = gid < p.S * p.P;
+  const int64_t s = active ? gid / p.P : 0;
+  const int o = active ? (int)(gid - s * p.P) : 0;
+  const Coef k = load_coef(p, o);
+  // Every thread votes (NaN parameters vote unstable): one unstable chain sends the whole
+  // CTA to the recompute kernel.
+  const bool stable = !active || (k.m11 + k.m22 > kRevTraceMin);
+  if (!__syncthreads_and(stable)) {
+    if (tid == 0) fallback[1 + atomicAdd(fallback, 1)] = (int)blockIdx.x;
+    return;
+  }
+  if (!active) return;
+  const int L = (int)p.L;
+  const int P = (int)p.P;
+  const int64_t base = s * p.L * p.P + o;
+  const float2* bu = p.Bu + base;
+  const float2* dys = p.dY2 + base;
+  float2* out = p.dBu + base;
+  const float rdet = 1.0f / (k.m11 * k.m22 - k.m12 * k.m21);
+  const float i11 = k.m22 * rdet, i12 = -k.m12 * rdet, i21 = -k.m21 * rdet, i22 = k.m11 * rdet;
+
+  float a1r = 0.f, a1i = 0.f, a2r = 0.f, a2i = 0.f;  // adjoint a_{t+1}
+  float g11 = 0.f, g12 = 0.f, g21 = 0.f, g22 = 0.f, gf1 = 0.f, gf2 = 0.f;
+  const int nb = (L + kLook - 1) / kLook;
+  // Batch b lives in stage (nb - 1 - b) % kStages. One commit group per batch (empty
+  // groups past the first batch keep the count uniform).
+  auto stage_of = [&](int b) { return (nb - 1 - b) % kStages; };
+#pragma unroll
+  for (int q = 0; q < kStages - 1; ++q) {
+    const int b = nb - 1 - q;
+    if (b >= 0) {
+      const int sg = stage_of(b);
+      stage_batch(in_base + sg * kLook * kBlock + tid, dy_base + sg * kLook * kBlock + tid, bu, dys, P, b * kLook,
+                  min(b * kLook + kLook, L));
+    }
+    cp_async_commit();
+  }
+  float4 st = p.ckpt[ckpt_index(p, s, p.nchunks, o)];  // state after the last step
+  for (int b = nb - 1; b >= 0; --b) {
+    const int bn = b - (kStages - 1);
+    if (bn >= 0) {  // refills the stage consumed by batch b + 1 (full batch: bn < b)
+      const int sg = stage_of(bn);
+      stage_batch(in_base + sg * kLook * kBlock + tid, dy_base + sg * kLook * kBlock + tid, bu, dys, P, bn * kLook,
+                  bn * kLook + kLook);
+    }
+    cp_async_commit();
+    cp_async_wait<kStages - 1>();
+    const int tb = b * kLook, te = min(tb + kLook, L);
+    const bool chunk_start = (tb % p.chunk) == 0;
+    float4 s_begin = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (chunk_start) s_begin = p.ckpt[ckpt_index(p, s, tb / p.chunk, o)];  // state before step tb
+    const int sg = stage_of(b);
+    const float2* inb = in_base + sg * kLook * kBlock + tid;
+    const float2* dyb = dy_base + sg * kLook * kBlock + tid;
+#pragma unroll
+    for (int i = kLook - 1; i >= 0; --i) {
+      if (tb + i < te) {
+        const float2 dy = dyb[i * kBlock];
+        const float2 u = inb[i * kBlock];
+        const float n1r = k.m11 * a1r + k.m21 * a2r;
+        const float n1i = k.m11 * a1i + k.m21 * a2i;
+        const float n2r = dy.x + k.m12 * a1r + k.m22 * a2r;
+        const float n2i = dy.y + k.m12 * a1i + k.m22 * a2i;
+        a1r = n1r;
+        a1i = n1i;
+        a2r = n2r;
+        a2i = n2i;
+        __stcs(out + (tb + i) * P, make_float2(k.f1 * a1r + k.f2 * a2r, k.f1 * a1i + k.f2 * a2i));
+        gf1 += a1r * u.x + a1i * u.y;
+        gf2 += a2r * u.x + a2i * u.y;
+        float4 sp;
+        if (i == 0 && chunk_start) {
+          sp = s_begin;
+        } else {  // s_{t-1} = M^-1 (s_t - F_t)
+          const float v1r = st.x - k.f1 * u.x, v1i = st.y - k.f1 * u.y;
+          const float v2r = st.z - k.f2 * u.x, v2i = st.w - k.f2 * u.y;
+          sp = make_float4(i11 * v1r + i12 * v2r, i11 * v1i + i12 * v2i, i21 * v1r + i22 * v2r,
+                           i21 * v1i + i22 * v2i);
+        }
+        g11 += a1r * sp.x + a1i * sp.y;
+        g12 += a1r * sp.z + a1i * sp.w;
+        g21 += a2r * sp.x + a2i * sp.y;
+        g22 += a2r * sp.z + a2i * sp.w;
+        st = sp;
+      }
+    }
+  }
+  cp_async_wait<0>();
+
+  float* part = p.part + s * kPartials * p.P + o;
+  part[0 * p.P] = g11;
+  part[1 * p.P] = g12;
+  part[2 * p.P] = g21;
+  part[3 * p.P] = g22;
+  part[4 * p.P] = gf1;
+  part[5 * p.P] = gf2;
 }
 
 // d(loss)/d(raw parameters) from the summed gradients of (M11, M12, M21, M22, f1, f2),
@@ -658,13 +821,14 @@ size_t semx_linoss_args_size(void) { return sizeof(SemxLinossArgs); }
 
 size_t semx_linoss_ckpt_bytes(int64_t S, int64_t L, int64_t P, int32_t chunk) {
   if (chunk <= 0 || S < 0 || L < 0 || P < 0) return 0;
-  return (size_t)S * (size_t)semx::cdiv(L, chunk) * (size_t)P * 4 * sizeof(float);
+  return (size_t)S * (size_t)(semx::cdiv(L, chunk) + 1) * (size_t)P * 4 * sizeof(float);
 }
 
 size_t semx_linoss_workspace_bytes(const SemxLinossArgs* a) {
   if (a == nullptr || a->S < 0 || a->P < 0) return 0;
   const size_t groups = (size_t)semx::cdiv(a->S, kRowsPerGroup);
-  return ((size_t)a->S + groups) * kPartials * (size_t)a->P * sizeof(float);
+  const size_t blocks = (size_t)semx::cdiv(a->S * a->P, kBlock);
+  return ((size_t)a->S + groups) * kPartials * (size_t)a->P * sizeof(float) + (1 + blocks) * sizeof(int);
 }
 
 int semx_linoss_fwd(const SemxLinossArgs* a, semx_stream_t stream) {
@@ -699,10 +863,24 @@ int semx_linoss_bwd(const SemxLinossArgs* a, semx_stream_t stream) {
     const dim3 grid((unsigned)semx::cdiv(n, kBlock));
     if (generic) {
       if (!semx::allow_smem(linoss_bwd_kernel<true>, smem)) return SEMX_ERR_LAUNCH;
-      linoss_bwd_kernel<true><<<grid, kBlock, smem, st>>>(p);
+      linoss_bwd_kernel<true><<<grid, kBlock, smem, st>>>(p, nullptr);
+    } else if (a->variant == SEMX_LINOSS_IMEX) {
+      // Reversal backward; CTAs it cannot take are listed for the recompute kernel.
+      int* fallback = reinterpret_cast<int*>(p.part + (a->S + semx::cdiv(a->S, kRowsPerGroup)) * kPartials * a->P);
+      cudaMemsetAsync(fallback, 0, sizeof(int), st);
+      if (!semx::allow_smem(linoss_bwd_rev_kernel, rev_smem_bytes())) return SEMX_ERR_LAUNCH;
+      linoss_bwd_rev_kernel<<<grid, kBlock, rev_smem_bytes(), st>>>(p, fallback);
+      rc = semx::check_launch("linoss_bwd_rev_kernel");
+      if (rc != SEMX_OK) return rc;
+      // The recompute kernel over the listed blocks (usually none): at most one wave.
+      int dev = 0, nsm = 148;
+      if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+      const unsigned fgrid = (unsigned)std::min<int64_t>(semx::cdiv(n, kBlock), (int64_t)nsm * 4);
+      if (!semx::allow_smem(linoss_bwd_kernel<false>, smem)) return SEMX_ERR_LAUNCH;
+      linoss_bwd_kernel<false><<<fgrid, kBlock, smem, st>>>(p, fallback);
     } else {
       if (!semx::allow_smem(linoss_bwd_kernel<false>, smem)) return SEMX_ERR_LAUNCH;
-      linoss_bwd_kernel<false><<<grid, kBlock, smem, st>>>(p);
+      linoss_bwd_kernel<false><<<grid, kBlock, smem, st>>>(p, nullptr);
     }
     rc = semx::check_launch("linoss_bwd_kernel");
     if (rc != SEMX_OK) return rc;

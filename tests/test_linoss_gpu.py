@@ -86,6 +86,37 @@ def test_fused_scan_matches_oracle(disc, damp, afg, S, L, P, chunk):
         assert_close(g_gpu[k], g_ref[k], tol[k], f"d{k}")
 
 
+@pytest.mark.parametrize("S,L,P,chunk", [(3, 45, 256, 16), (2, 70, 16, 64)])
+def test_imex_unstable_oscillators_take_the_recompute_backward(S, L, P, chunk):
+    """The IMEX backward runs the state backwards in time only for oscillators whose
+    transition has both eigenvalues on the unit circle; a thread block holding one with
+    step^2 A above 4 (growing forward) goes to the recompute backward. P = 256: of the two
+    128-oscillator blocks per sequence, the first (stable, one oscillator at step^2 A =
+    3.95) takes the reversal, the second (one at step^2 A = 4.05) the recompute; P = 16:
+    every block falls back. Each block's oscillators are compared on their own, since the
+    growing one dominates any norm over all of them."""
+    variant = _variant("IMEX", False)
+    g = gen(4242 + P)
+    steps, A, _ = _params(P, g, variant)
+    A = A.abs().clamp(max=2.0)  # step^2 A <= 2 elsewhere
+    s9 = torch.logit(torch.tensor(0.9, dtype=torch.float64))
+    bad = P - 3
+    steps[bad], A[bad] = s9, 4.05 / 0.81
+    if P > 128:
+        steps[5], A[5] = s9, 3.95 / 0.81
+    Bu = crandn((S, L, P), g)
+    gy = crandn((S, L, P), g)
+    y_ref, g_ref = _oracle_fused(variant, steps, A, None, Bu, gy, True)
+    y32, g32 = _oracle_fused(variant, steps, A, None, Bu, gy, True, dtype=torch.float32)
+    y_gpu, g_gpu = _gpu_fused(variant, steps, A, None, Bu, gy, True, chunk)
+    for lo, hi in ((0, min(P, 128)), (128, P)) if P > 128 else ((0, P),):
+        sl = (..., slice(lo, hi))
+        assert_close(y_gpu[sl], y_ref[sl], floor_tol(rel_err(y32[sl], y_ref[sl])), f"y2[{lo}:{hi}]")
+        for k in g_ref:
+            tol = floor_tol(rel_err(g32[k][sl], g_ref[k][sl]))
+            assert_close(g_gpu[k][sl], g_ref[k][sl], tol, f"d{k}[{lo}:{hi}]")
+
+
 @pytest.mark.parametrize("S,L,P,chunk", [(3, 17, 16, 8), (2, 29, 64, 16), (1, 100, 7, 64)])
 def test_generic_scan_matches_oracle(S, L, P, chunk):
     from semambaxlinoss_b200.linoss import linoss_scan

@@ -133,8 +133,7 @@ typedef struct SemxLinossArgs {
 size_t semx_linoss_args_size(void);
 /* Size of ckpt in bytes for (S, L, P, chunk). */
 size_t semx_linoss_ckpt_bytes(int64_t S, int64_t L, int64_t P, int32_t chunk);
-/* Scratch the backward needs (per-sequence partial reductions, and for IMEX the list
- * of thread blocks the reversal backward hands to the recompute backward). */
+/* Scratch the backward needs (per-sequence partial reductions). */
 size_t semx_linoss_workspace_bytes(const SemxLinossArgs* args);
 int semx_linoss_fwd(const SemxLinossArgs* args, semx_stream_t stream);
 int semx_linoss_bwd(const SemxLinossArgs* args, semx_stream_t stream);

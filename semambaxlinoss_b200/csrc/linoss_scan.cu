@@ -16,17 +16,19 @@
 // and the final state (16 B per chunk and chain). The backward runs the adjoint
 //   a_t = (0, dY2_t) + M^T a_{t+1},  dF_t = a_t,  dM_ij += Re(a_i,t conj(s_j,t-1))
 // backwards in time and needs the forward states s_{t-1}; no per-step state goes to HBM.
-//   * IMEX (linoss_bwd_rev_kernel): M has determinant 1 (the scheme is symplectic), so
-//     the state is run backwards with the adjoint, s_{t-1} = M^-1 (s_t - F_t), from each
-//     chunk's end state and reset to the exact checkpoint at every chunk start. With both
-//     eigenvalues on the unit circle (trace > -2) this is as accurate as re-running the
-//     recurrence; a CTA holding an oscillator outside that range (step^2 A near or
-//     above 4, where the reversal amplifies rounding) does not run it and is listed for
-//     the recompute kernel instead.
-//   * otherwise (linoss_bwd_kernel): for each chunk, re-run the recurrence once from the
+// linoss_bwd_kernel takes one of two paths per thread block:
+//   * IMEX (rev_block): M has determinant 1 (the scheme is symplectic), so the state is
+//     run backwards with the adjoint, s_{t-1} = M^-1 (s_t - F_t), from each chunk's end
+//     state and reset to the exact checkpoint at every chunk start. With both eigenvalues
+//     on the unit circle (trace > -2) this is as accurate as re-running the recurrence; a
+//     block holding an oscillator outside that range (step^2 A near or above 4, where the
+//     reversal amplifies rounding) takes the other path.
+//   * otherwise (bwd_block): for each chunk, re-run the recurrence once from the
 //     checkpoint, dropping the state every kSub steps into shared memory; then for each
 //     kSub-step sub-block (last first) recompute the kSub states into registers and run
 //     the adjoint through them.
+// Both paths need the same 48 KB of shared memory at the default chunk of 64 steps, and 4
+// blocks of 128 threads fit an SM either way.
 // Per-oscillator parameter gradients are summed per chain in registers, written once per
 // chain, and reduced over sequences by linoss_finalize_kernel in a fixed order (bitwise
 // deterministic), which also applies the chain rule from (M, f) back to the raw
@@ -389,20 +391,6 @@ __device__ __forceinline__ void bwd_block(const Params& p, int blk, float4* smem
   part[5 * p.P] = gf2;
 }
 
-// Without `list`, CTA b processes block b. With `list` (the reversal kernel's fallback
-// list: a count, then block indices), the CTAs walk the listed blocks grid-stride; every
-// block's copies are complete when bwd_block returns, so shared memory is reused safely.
-template <bool GENERIC>
-__global__ void __launch_bounds__(kBlock, 4) linoss_bwd_kernel(const Params p, const int* list) {
-  extern __shared__ float4 smem4[];
-  if (GENERIC || list == nullptr) {  // the generic operator never has a list
-    bwd_block<GENERIC>(p, (int)blockIdx.x, smem4);
-    return;
-  }
-  const int n = list[0];
-  for (int i = (int)blockIdx.x; i < n; i += (int)gridDim.x) bwd_block<GENERIC>(p, list[1 + i], smem4);
-}
-
 __host__ __device__ inline size_t bwd_smem_bytes(int chunk, bool generic) {
   return (size_t)(chunk / kSub) * kBlock * sizeof(float4) +
          (size_t)2 * ((generic ? 2 : 1) + 1) * kSub * kBlock * sizeof(float2);
@@ -423,17 +411,17 @@ __device__ __forceinline__ void stage_batch(float2* in_buf, float2* dy_buf, cons
 
 __host__ __device__ inline size_t rev_smem_bytes() { return (size_t)2 * kStages * kLook * kBlock * sizeof(float2); }
 
-// IMEX backward with the state run backwards in time (see the file comment). Batches of
-// kLook steps, last first; Bu and dY2 of batch b - (kStages - 1) are staged by cp.async
-// while batch b runs, so every load is issued two batches (16 steps) before its use.
-// That lookahead, not the warp count, is what keeps HBM busy: measured against 2 stages
-// at 6 CTAs/SM and register prefetch variants, 3 stages at 4 CTAs/SM is fastest.
-// chunk is a multiple of kLook, so every chunk starts a batch.
+// IMEX backward of this thread block with the state run backwards in time (see the file
+// comment); returns false, having done nothing, when one of the block's oscillators does
+// not allow it. Batches of kLook steps, last first; Bu and dY2 of batch b - (kStages - 1)
+// are staged by cp.async while batch b runs, so every load is issued two batches (16
+// steps) before its use. That lookahead, not the warp count, is what keeps HBM busy:
+// measured against 2 stages at 6 blocks/SM and register prefetch variants, 3 stages at 4
+// blocks/SM is fastest. chunk is a multiple of kLook, so every chunk starts a batch.
 // Shared memory: in[kStages][kLook][kBlock], dy[kStages][kLook][kBlock] float2, per-thread
 // slots (no block barrier after the stability vote; a stage is refilled only by the
 // thread that consumed it in the previous batch).
-__global__ void __launch_bounds__(kBlock, 4) linoss_bwd_rev_kernel(const Params p, int* fallback) {
-  extern __shared__ float4 smem4[];
+__device__ __forceinline__ bool rev_block(const Params& p, float4* smem4) {
   float2* in_base = reinterpret_cast<float2*>(smem4);
   float2* dy_base = in_base + kStages * kLook * kBlock;
   const int tid = threadIdx.x;
@@ -443,13 +431,10 @@ __global__ void __launch_bounds__(kBlock, 4) linoss_bwd_rev_kernel(const Params 
   const int o = active ? (int)(gid - s * p.P) : 0;
   const Coef k = load_coef(p, o);
   // Every thread votes (NaN parameters vote unstable): one unstable chain sends the whole
-  // CTA to the recompute kernel.
+  // block to the recompute path.
   const bool stable = !active || (k.m11 + k.m22 > kRevTraceMin);
-  if (!__syncthreads_and(stable)) {
-    if (tid == 0) fallback[1 + atomicAdd(fallback, 1)] = (int)blockIdx.x;
-    return;
-  }
-  if (!active) return;
+  if (!__syncthreads_and(stable)) return false;
+  if (!active) return true;
   const int L = (int)p.L;
   const int P = (int)p.P;
   const int64_t base = s * p.L * p.P + o;
@@ -534,6 +519,15 @@ __global__ void __launch_bounds__(kBlock, 4) linoss_bwd_rev_kernel(const Params 
   part[3 * p.P] = g22;
   part[4 * p.P] = gf1;
   part[5 * p.P] = gf2;
+  return true;
+}
+
+// One backward kernel for every variant (see the file comment).
+template <bool GENERIC>
+__global__ void __launch_bounds__(kBlock, 4) linoss_bwd_kernel(const Params p) {
+  extern __shared__ float4 smem4[];
+  if (!GENERIC && p.variant == SEMX_LINOSS_IMEX && rev_block(p, smem4)) return;
+  bwd_block<GENERIC>(p, (int)blockIdx.x, smem4);
 }
 
 // d(loss)/d(raw parameters) from the summed gradients of (M11, M12, M21, M22, f1, f2),
@@ -827,8 +821,7 @@ size_t semx_linoss_ckpt_bytes(int64_t S, int64_t L, int64_t P, int32_t chunk) {
 size_t semx_linoss_workspace_bytes(const SemxLinossArgs* a) {
   if (a == nullptr || a->S < 0 || a->P < 0) return 0;
   const size_t groups = (size_t)semx::cdiv(a->S, kRowsPerGroup);
-  const size_t blocks = (size_t)semx::cdiv(a->S * a->P, kBlock);
-  return ((size_t)a->S + groups) * kPartials * (size_t)a->P * sizeof(float) + (1 + blocks) * sizeof(int);
+  return ((size_t)a->S + groups) * kPartials * (size_t)a->P * sizeof(float);
 }
 
 int semx_linoss_fwd(const SemxLinossArgs* a, semx_stream_t stream) {
@@ -859,28 +852,15 @@ int semx_linoss_bwd(const SemxLinossArgs* a, semx_stream_t stream) {
   const int64_t n = a->S * a->P;
   if (n > 0 && a->L > 0) {
     const bool generic = a->variant == SEMX_LINOSS_GENERIC;
-    const size_t smem = bwd_smem_bytes(a->chunk, generic);
+    const size_t smem = std::max(bwd_smem_bytes(a->chunk, generic),
+                                 a->variant == SEMX_LINOSS_IMEX ? rev_smem_bytes() : (size_t)0);
     const dim3 grid((unsigned)semx::cdiv(n, kBlock));
     if (generic) {
       if (!semx::allow_smem(linoss_bwd_kernel<true>, smem)) return SEMX_ERR_LAUNCH;
-      linoss_bwd_kernel<true><<<grid, kBlock, smem, st>>>(p, nullptr);
-    } else if (a->variant == SEMX_LINOSS_IMEX) {
-      // Reversal backward; CTAs it cannot take are listed for the recompute kernel.
-      int* fallback = reinterpret_cast<int*>(p.part + (a->S + semx::cdiv(a->S, kRowsPerGroup)) * kPartials * a->P);
-      cudaMemsetAsync(fallback, 0, sizeof(int), st);
-      if (!semx::allow_smem(linoss_bwd_rev_kernel, rev_smem_bytes())) return SEMX_ERR_LAUNCH;
-      linoss_bwd_rev_kernel<<<grid, kBlock, rev_smem_bytes(), st>>>(p, fallback);
-      rc = semx::check_launch("linoss_bwd_rev_kernel");
-      if (rc != SEMX_OK) return rc;
-      // The recompute kernel over the listed blocks (usually none): at most one wave.
-      int dev = 0, nsm = 148;
-      if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
-      const unsigned fgrid = (unsigned)std::min<int64_t>(semx::cdiv(n, kBlock), (int64_t)nsm * 4);
-      if (!semx::allow_smem(linoss_bwd_kernel<false>, smem)) return SEMX_ERR_LAUNCH;
-      linoss_bwd_kernel<false><<<fgrid, kBlock, smem, st>>>(p, fallback);
+      linoss_bwd_kernel<true><<<grid, kBlock, smem, st>>>(p);
     } else {
       if (!semx::allow_smem(linoss_bwd_kernel<false>, smem)) return SEMX_ERR_LAUNCH;
-      linoss_bwd_kernel<false><<<grid, kBlock, smem, st>>>(p, nullptr);
+      linoss_bwd_kernel<false><<<grid, kBlock, smem, st>>>(p);
     }
     rc = semx::check_launch("linoss_bwd_kernel");
     if (rc != SEMX_OK) return rc;

@@ -63,9 +63,8 @@ def test_size_queries():
     assert lib.semx_linoss_ckpt_bytes(404, 321, 256, 64) == 404 * (6 + 1) * 256 * 16
     a = _lib.new_args(_lib.SemxLinossArgs)
     a.S, a.P = 3, 10
-    # per-sequence partial rows + one row per group of 32 sequences, 6 sums per oscillator,
-    # then the reversal backward's fallback list (a count and one slot per 128-chain block)
-    assert lib.semx_linoss_workspace_bytes(ctypes.byref(a)) == (3 + 1) * 6 * 10 * 4 + (1 + 1) * 4
+    # per-sequence partial rows + one row per group of 32 sequences, 6 sums per oscillator
+    assert lib.semx_linoss_workspace_bytes(ctypes.byref(a)) == (3 + 1) * 6 * 10 * 4
     b = _lib.new_args(_lib.SemxSelectiveLruArgs)
     b.S, b.L, b.C, b.N, b.chunk, b.real = 4, 10, 8, 4, 4, 0
     assert lib.semx_selective_lru_ckpt_bytes(ctypes.byref(b)) == 4 * 3 * 8 * 4 * 2 * 4

@@ -1048,8 +1048,12 @@ __host__ __device__ inline BLay make_blay(int R, bool env, int es) {
   l.db = take(CT * HW * 2);
   l.sr = take(CT * R);
   l.dr = take(CT * R);
-  l.red = take(3 * NH * (kT / 8));
-  l.rb = take(2 * (kT / 8));
+  // The end-of-kernel sums reuse lam and gn (contiguous, 2 CT HW 2 >= 3 NH kT/8 + 2 kT/8
+  // floats), which are dead after the last chunk: 3 KB less per CTA is what lets 5 CTAs
+  // share an SM.
+  l.red = l.lam;
+  l.rb = l.lam + 3 * NH * (kT / 8);
+  static_assert(2 * kB_CT * kB_HW * 2 >= 3 * kB_NH * (kT / 8) + 2 * (kT / 8), "red / rb must fit in lam + gn");
   l.total = o;
   return l;
 }

@@ -556,7 +556,7 @@ WORKLOADS = {
                     "P=256 oscillators, H=64",
         "data": "synthetic, seeded: A = relu(N(0,1)), dt = sigmoid(N(0,1)), B ~ N(0, 1/sqrt(64)), u ~ N(0,1)",
         "dtype": "f32",
-        "chunk": 64, "cpu_frac": 1.0, "ref_frac": 1.0 / 16,
+        "chunk": 64, "cpu_frac": 0.5, "ref_frac": 1.0 / 16,
         "l2": "no flush: every operand is 265 MB, larger than the 126 MB L2",
         "cpu_sample": _linoss_cpu_sample, "cpu_step": _linoss_cpu_step,
     },
@@ -577,7 +577,7 @@ WORKLOADS = {
                     "state 128, rank 4, time 404x321 + freq 1284x101",
         "data": "synthetic, seeded: x ~ N(0,1/4) bf16, dt = softplus(N(-2,0.5)), b_t, c_t, B, C, D ~ N(0,1/4)",
         "dtype": "bf16 in / f32 state",
-        "chunk": 0, "cpu_frac": 1.0, "ref_frac": 8.0 / 404,
+        "chunk": 0, "cpu_frac": 0.5, "ref_frac": 8.0 / 404,
         "l2": "no flush: the layer's activations per pass are GBs, far beyond the 126 MB L2",
         "cpu_sample": _mimo_cpu_sample, "cpu_step": _mimo_cpu_step,
     },

@@ -290,11 +290,13 @@ struct FLay {
                           // (drive rows are read two consecutive tokens per warp and are
                           // not padded)
   int hw;              // row width of lam / bu / hs in float2 (Nh + 1, same reason)
+  int tc;              // tokens per chunk
   int total;
 };
 
-__host__ __device__ inline FLay make_flay(int Nh, int Fh, int R, bool env, int es) {
+__host__ __device__ inline FLay make_flay(int Nh, int Fh, int R, bool env, int es, int tc = kTC) {
   FLay l = {};
+  l.tc = tc;
   int o = 0;
   auto take = [&](int n) {
     const int at = o;
@@ -313,14 +315,14 @@ __host__ __device__ inline FLay make_flay(int Nh, int Fh, int R, bool env, int e
   l.bxw = ((2 * Nh * es + 15) / 16) * 16 / es;
   l.btw = R > 0 ? ((R * Nh * es + 15) / 16) * 16 / es + pad : 0;
   l.ctw = R > 0 ? ((2 * R * Nh * es + 15) / 16) * 16 / es + pad : 0;
-  const int stg_elems = kTC * (l.xw + l.bxw + l.btw + l.ctw);
+  const int stg_elems = tc * (l.xw + l.bxw + l.btw + l.ctw);
   for (int b = 0; b < 2; ++b) l.stg[b] = take((stg_elems * es + 3) / 4);
-  for (int b = 0; b < 2; ++b) l.sml[b] = take(kTC * (3 + 2 * R));
+  for (int b = 0; b < 2; ++b) l.sml[b] = take(tc * (3 + 2 * R));
   l.hw = Nh + 1;
-  l.lam = take(kTC * l.hw * 2);
-  l.bu = take(kTC * l.hw * 2);
-  l.hs = take(kTC * l.hw * 2);
-  l.sr = take(kTC * R);
+  l.lam = take(tc * l.hw * 2);
+  l.bu = take(tc * l.hw * 2);
+  l.hs = take(tc * l.hw * 2);
+  l.sr = take(tc * R);
   l.total = o;
   return l;
 }
@@ -352,8 +354,8 @@ __device__ __forceinline__ void stage_segment(T* d, int dw, const T* src, int64_
   }
 }
 
-// Issues the staging of chunk [t0, t0 + nt) of head h: x [kTC][Fh], drive [kTC][2 Nh],
-// b_t [kTC][R Nh], c_t [kTC][2 R Nh] in the input dtype, rows l.xw / l.bxw / l.btw /
+// Issues the staging of chunk [t0, t0 + nt) of head h: x [tc][Fh], drive [tc][2 Nh],
+// b_t [tc][R Nh], c_t [tc][2 R Nh] in the input dtype, rows l.xw / l.bxw / l.btw /
 // l.ctw apart; 16-byte cp.async where the host found the rows aligned (p.vec bit 0: x,
 // bit 1: b_t and c_t, bit 4: drive), otherwise plain loads.
 template <bool BF16, int NH, int FH, int RK>
@@ -362,9 +364,9 @@ __device__ __forceinline__ void stage_bulk(const LParams& p, const FLay& l, void
   using T = typename std::conditional<BF16, __nv_bfloat16, float>::type;
   const int Nh = NH > 0 ? NH : (int)p.Nh, Fh = FH > 0 ? FH : (int)p.Fh, R = RK >= 0 ? RK : (int)p.R;
   T* xs = reinterpret_cast<T*>(dst);
-  T* bxs = xs + kTC * l.xw;
-  T* bts = bxs + kTC * l.bxw;
-  T* cts = bts + kTC * l.btw;
+  T* bxs = xs + l.tc * l.xw;
+  T* bts = bxs + l.tc * l.bxw;
+  T* cts = bts + l.tc * l.btw;
   const T* X = reinterpret_cast<const T*>(p.x);
   const T* Pj = reinterpret_cast<const T*>(p.proj);
   const int64_t row0 = s * p.L + t0;
@@ -522,8 +524,10 @@ __device__ __forceinline__ void chunk_scan(const float2* lam, const float2* bu, 
 }
 
 // NH, FH, RK > 0 (RK >= 0) fix the head's modes, channels and rank at compile time;
-// 0 (-1) takes them from the parameters.
-template <bool BF16, int SEG, int NH, int FH, int RK>
+// 0 (-1) takes them from the parameters. CT tokens per chunk (a multiple of the 16-token
+// checkpoint interval): 16 for the 16-mode, 32-channel heads, whose 31 KB of shared memory
+// then lets 7 CTAs share an SM; 32 otherwise.
+template <bool BF16, int SEG, int NH, int FH, int RK, int CT = kTC>
 __global__ void __launch_bounds__(kT) mimo_layer_fwd_kernel(const LParams p) {
   using T = typename std::conditional<BF16, __nv_bfloat16, float>::type;
   extern __shared__ float4 smem4[];
@@ -531,7 +535,10 @@ __global__ void __launch_bounds__(kT) mimo_layer_fwd_kernel(const LParams p) {
   const int Nh = NH > 0 ? NH : (int)p.Nh, Fh = FH > 0 ? FH : (int)p.Fh, R = RK >= 0 ? RK : (int)p.R;
   const int L = (int)p.L;
   const bool env = p.envelope != 0;
-  const FLay l = make_flay(Nh, Fh, R, env, (int)sizeof(T));
+  static_assert(CT % kCk == 0 && CT % SEG == 0, "chunk must hold whole checkpoint blocks and segments");
+  constexpr int CPC = CT / kCk;  // checkpoints per chunk
+  const FLay l = make_flay(Nh, Fh, R, env, (int)sizeof(T), CT);
+  const int nchunks = (L + CT - 1) / CT;
   const int64_t s = blockIdx.x / p.H;
   const int h = (int)(blockIdx.x % p.H);
   const int tid = threadIdx.x;
@@ -561,34 +568,34 @@ __global__ void __launch_bounds__(kT) mimo_layer_fwd_kernel(const LParams p) {
   const int hw = l.hw;
   const float2 bias = dt_bias(p, h);
   float pre[kPre];
-  if (p.nchunks > 0) {
-    const int nt0 = min(kTC, L);
+  if (nchunks > 0) {
+    const int nt0 = min(CT, L);
     stage_bulk<BF16, NH, FH, RK>(p, l, sm + l.stg[0], s, h, 0, nt0);
     load_small<BF16, RK>(p, s, h, 0, nt0, bias, pre);
-    store_small<RK>(p, sm + l.sml[0], nt0, pre);
+    store_small<RK, CT>(p, sm + l.sml[0], nt0, pre);
   }
   cp_async_commit();
-  for (int k = 0; k < p.nchunks; ++k) {
+  for (int k = 0; k < nchunks; ++k) {
     const int b = k & 1;
-    const int t0 = k * kTC, nt = min(kTC, L - t0);
-    const int t0n = t0 + kTC, ntn = min(kTC, L - t0n);
+    const int t0 = k * CT, nt = min(CT, L - t0);
+    const int t0n = t0 + CT, ntn = min(CT, L - t0n);
     cp_async_wait_all();
     __syncthreads();
-    if (k + 1 < p.nchunks) {
+    if (k + 1 < nchunks) {
       stage_bulk<BF16, NH, FH, RK>(p, l, sm + l.stg[b ^ 1], s, h, t0n, ntn);
       load_small<BF16, RK>(p, s, h, t0n, ntn, bias, pre);
     }
     cp_async_commit();
     const T* xs = reinterpret_cast<const T*>(sm + l.stg[b]);
-    const T* bxs = xs + kTC * l.xw;
-    const T* bts = bxs + kTC * l.bxw;
-    const T* cts = bts + kTC * l.btw;
+    const T* bxs = xs + CT * l.xw;
+    const T* bts = bxs + CT * l.bxw;
+    const T* cts = bts + CT * l.btw;
     const int xw = l.xw, bxw = l.bxw, btw = l.btw, ctw = l.ctw;
     const float* sml = sm + l.sml[b];
-    const float* dnus = sml + kTC;
-    const float* dths = sml + 2 * kTC;
-    const float* sbs = sml + 3 * kTC;
-    const float* scs = sbs + kTC * R;
+    const float* dnus = sml + CT;
+    const float* dths = sml + 2 * CT;
+    const float* sbs = sml + 3 * CT;
+    const float* scs = sbs + CT * R;
     // Poles and gained drive per (token, mode).
     for (int i = tid; i < nt * Nh; i += kT) {
       const int t = i / Nh, n = i - (i / Nh) * Nh;
@@ -603,12 +610,15 @@ __global__ void __launch_bounds__(kT) mimo_layer_fwd_kernel(const LParams p) {
     }
     __syncthreads();
     if (p.ckpt != nullptr && tid < Nh)
-      reinterpret_cast<float2*>(p.ckpt)[((s * p.nck + 2 * k) * p.H + h) * Nh + tid] = cin[tid];
+      reinterpret_cast<float2*>(p.ckpt)[((s * p.nck + CPC * k) * p.H + h) * Nh + tid] = cin[tid];
     __syncthreads();
-    chunk_scan<SEG>(lam, bu, hs, cin, Nh, hw, nt);
+    chunk_scan<SEG, CT>(lam, bu, hs, cin, Nh, hw, nt);
     __syncthreads();
-    if (p.ckpt != nullptr && tid < Nh && t0 + kCk < L)  // the state entering token t0 + 16
-      reinterpret_cast<float2*>(p.ckpt)[((s * p.nck + 2 * k + 1) * p.H + h) * Nh + tid] = hs[(kCk - 1) * hw + tid];
+#pragma unroll
+    for (int m = 1; m < CPC; ++m)  // the state entering token t0 + 16 m
+      if (p.ckpt != nullptr && tid < Nh && t0 + m * kCk < L)
+        reinterpret_cast<float2*>(p.ckpt)[((s * p.nck + CPC * k + m) * p.H + h) * Nh + tid] =
+            hs[(m * kCk - 1) * hw + tid];
     if (R > 0) {
       for (int i = tid; i < nt * R; i += kT) {
         const int t = i / R, r = i % R;
@@ -622,15 +632,18 @@ __global__ void __launch_bounds__(kT) mimo_layer_fwd_kernel(const LParams p) {
       }
       __syncthreads();
     }
-    // Readout, 2 tokens x 4 channels per item.
+    // Readout, TPI tokens x 4 channels per item (one item per thread for 16 x 32 heads).
+    constexpr int TPI = CT >= 32 ? 2 : 1;
     const int fq = (Fh + 3) / 4;
-    for (int it = tid; it < (kTC / 2) * fq; it += kT) {
-      const int ta = (it / fq) * 2, fa = (it % fq) * 4;
+    for (int it = tid; it < (CT / TPI) * fq; it += kT) {
+      const int ta = (it / fq) * TPI, fa = (it % fq) * 4;
       if (ta >= nt) continue;
-      const bool t1ok = ta + 1 < nt;
-      float acc[2][4];
+      bool tok[TPI];
 #pragma unroll
-      for (int dt = 0; dt < 2; ++dt)
+      for (int dt = 0; dt < TPI; ++dt) tok[dt] = ta + dt < nt;
+      float acc[TPI][4];
+#pragma unroll
+      for (int dt = 0; dt < TPI; ++dt)
 #pragma unroll
         for (int df = 0; df < 4; ++df) {
           const int f = min(fa + df, Fh - 1);
@@ -639,41 +652,47 @@ __global__ void __launch_bounds__(kT) mimo_layer_fwd_kernel(const LParams p) {
         }
 #pragma unroll 4
       for (int n = 0; n < Nh; ++n) {
-        const float2 h0 = hs[ta * hw + n];
-        const float2 h1 = t1ok ? hs[(ta + 1) * hw + n] : make_float2(0.f, 0.f);
-        const float p0 = h0.x * h0.x + h0.y * h0.y, p1 = h1.x * h1.x + h1.y * h1.y;
+        float2 hv[TPI];
+        float pw[TPI];
+#pragma unroll
+        for (int dt = 0; dt < TPI; ++dt) {
+          hv[dt] = tok[dt] ? hs[(ta + dt) * hw + n] : make_float2(0.f, 0.f);
+          pw[dt] = hv[dt].x * hv[dt].x + hv[dt].y * hv[dt].y;
+        }
 #pragma unroll
         for (int df = 0; df < 4; ++df) {
           const int f = min(fa + df, Fh - 1);
           const float cre = Cr[n * Fh + f], cim = Ci[n * Fh + f];
-          acc[0][df] = fmaf(cre, h0.x, fmaf(-cim, h0.y, acc[0][df]));
-          acc[1][df] = fmaf(cre, h1.x, fmaf(-cim, h1.y, acc[1][df]));
+#pragma unroll
+          for (int dt = 0; dt < TPI; ++dt) acc[dt][df] = fmaf(cre, hv[dt].x, fmaf(-cim, hv[dt].y, acc[dt][df]));
           if (env) {
             const float e = sm[l.En + n * Fh + f];
-            acc[0][df] = fmaf(e, p0, acc[0][df]);
-            acc[1][df] = fmaf(e, p1, acc[1][df]);
+#pragma unroll
+            for (int dt = 0; dt < TPI; ++dt) acc[dt][df] = fmaf(e, pw[dt], acc[dt][df]);
           }
         }
       }
       for (int r = 0; r < R; ++r) {
-        const float s0 = sm[l.sr + ta * R + r], s1 = t1ok ? sm[l.sr + (ta + 1) * R + r] : 0.f;
+        float sv[TPI];
+#pragma unroll
+        for (int dt = 0; dt < TPI; ++dt) sv[dt] = tok[dt] ? sm[l.sr + (ta + dt) * R + r] : 0.f;
 #pragma unroll
         for (int df = 0; df < 4; ++df) {
           const float co = sm[l.Co + r * Fh + min(fa + df, Fh - 1)];
-          acc[0][df] = fmaf(s0, co, acc[0][df]);
-          acc[1][df] = fmaf(s1, co, acc[1][df]);
+#pragma unroll
+          for (int dt = 0; dt < TPI; ++dt) acc[dt][df] = fmaf(sv[dt], co, acc[dt][df]);
         }
       }
 #pragma unroll
-      for (int dt = 0; dt < 2; ++dt) {
-        if (dt == 1 && !t1ok) continue;
+      for (int dt = 0; dt < TPI; ++dt) {
+        if (!tok[dt]) continue;
         float* yr = p.y + (s * p.L + t0 + ta + dt) * Fd + (int64_t)h * Fh + fa;
 #pragma unroll
         for (int df = 0; df < 4; ++df)
           if (fa + df < Fh) yr[df] = acc[dt][df];
       }
     }
-    if (k + 1 < p.nchunks) store_small<RK>(p, sm + l.sml[b ^ 1], ntn, pre);
+    if (k + 1 < nchunks) store_small<RK, CT>(p, sm + l.sml[b ^ 1], ntn, pre);
   }
 }
 
@@ -1450,11 +1469,14 @@ int64_t part_row(const SemxMimoLayerArgs* a) {
 // The backward of 16-mode, 32-channel heads of rank 0 or 4 has its own kernel.
 bool bwd16(const SemxMimoLayerArgs* a) { return a->Nh == 16 && a->Fh == 32 && (a->rank == 0 || a->rank == 4); }
 
+// The forward of 16-mode, 32-channel heads (rank 0 or 4) runs 16-token chunks.
+int fwd_chunk(const SemxMimoLayerArgs* a) { return bwd16(a) ? kCk : kTC; }
+
 size_t layer_smem(const SemxMimoLayerArgs* a, bool bwd) {
   if (bwd && bwd16(a)) return (size_t)make_blay(a->rank, a->envelope != 0, a->bf16 ? 2 : 4).total * sizeof(float);
   if (!bwd)
-    return (size_t)make_flay((int)a->Nh, (int)a->Fh, a->rank, a->envelope != 0, a->bf16 ? 2 : 4).total *
-           sizeof(float);
+    return (size_t)make_flay((int)a->Nh, (int)a->Fh, a->rank, a->envelope != 0, a->bf16 ? 2 : 4, fwd_chunk(a))
+               .total * sizeof(float);
   return (size_t)make_lay((int)a->Nh, (int)a->Fh, a->rank, bwd, a->envelope != 0).total * sizeof(float);
 }
 
@@ -1566,13 +1588,14 @@ int semx_mimo_layer_fwd(const SemxMimoLayerArgs* a, semx_stream_t stream) {
   const size_t smem = layer_smem(a, false);
   cudaStream_t st = semx::as_stream(stream);
   const int seg = scan_segments(a->Nh);
-  if (seg == 8 && a->Nh == 16 && a->Fh == 32 && (a->rank == 4 || a->rank == 0)) {
-    // The 8-head x 32 / 16-mode layers, specialised at compile time.
+  if (bwd16(a)) {
+    // The 16-mode, 32-channel heads, specialised at compile time, 16-token chunks.
+    static_assert(kCk % 8 == 0, "16-token chunks hold whole 8-segment scans");
     if (a->rank == 4)
-      return a->bf16 ? launch_layer(mimo_layer_fwd_kernel<true, 8, 16, 32, 4>, p, smem, st, "mimo_layer_fwd_kernel")
-                     : launch_layer(mimo_layer_fwd_kernel<false, 8, 16, 32, 4>, p, smem, st, "mimo_layer_fwd_kernel");
-    return a->bf16 ? launch_layer(mimo_layer_fwd_kernel<true, 8, 16, 32, 0>, p, smem, st, "mimo_layer_fwd_kernel")
-                   : launch_layer(mimo_layer_fwd_kernel<false, 8, 16, 32, 0>, p, smem, st, "mimo_layer_fwd_kernel");
+      return a->bf16 ? launch_layer(mimo_layer_fwd_kernel<true, 8, 16, 32, 4, kCk>, p, smem, st, "mimo_layer_fwd_kernel")
+                     : launch_layer(mimo_layer_fwd_kernel<false, 8, 16, 32, 4, kCk>, p, smem, st, "mimo_layer_fwd_kernel");
+    return a->bf16 ? launch_layer(mimo_layer_fwd_kernel<true, 8, 16, 32, 0, kCk>, p, smem, st, "mimo_layer_fwd_kernel")
+                   : launch_layer(mimo_layer_fwd_kernel<false, 8, 16, 32, 0, kCk>, p, smem, st, "mimo_layer_fwd_kernel");
   }
   switch (seg) {
 #define SEMX_SEG(SV)                                                                                  \

@@ -432,6 +432,37 @@ size_t semx_gate_silu_args_size(void);
 int semx_gate_silu_fwd(const SemxGateSiluArgs* args, semx_stream_t stream);
 int semx_gate_silu_bwd(const SemxGateSiluArgs* args, semx_stream_t stream);
 
+/* ------------------------------------------------------------------------------------
+ * RMS normalisation over the last dimension with a learned gain (replaces the pre-norm
+ * Block's RMSNorm, built by create_block with rms_norm=True, models/mamba_block.py:
+ * 335-342; the reference takes the class from mamba_ssm):
+ *   y[r, j] = x[r, j] / sqrt(mean_j(x[r, j]^2) + eps) * weight[j]
+ * computed in fp32; x, y, dy, dx are bf16 when `bf16` is set, else fp32; weight, rstd
+ * (n, the 1 / rms of each row, written by the forward when non-NULL, read by the
+ * backward), dweight fp32. Rows of d <= 1024 elements. Backward writes dx and dweight,
+ * reduced over rows in a fixed order (workspace: semx_rms_norm_workspace_bytes()).
+ * ---------------------------------------------------------------------------------- */
+typedef struct SemxRmsNormArgs {
+  uint32_t struct_size;
+  int32_t bf16;
+  float eps;
+  int32_t reserved;
+  int64_t n, d; /* rows, elements per row */
+  const void* x;
+  const float* weight;
+  void* y;
+  float* rstd;
+  const void* dy;
+  void* dx;
+  float* dweight;
+  void* workspace;
+} SemxRmsNormArgs;
+
+size_t semx_rms_norm_args_size(void);
+size_t semx_rms_norm_workspace_bytes(const SemxRmsNormArgs* args);
+int semx_rms_norm_fwd(const SemxRmsNormArgs* args, semx_stream_t stream);
+int semx_rms_norm_bwd(const SemxRmsNormArgs* args, semx_stream_t stream);
+
 size_t semx_mimo_layer_args_size(void);
 size_t semx_mimo_layer_ckpt_bytes(const SemxMimoLayerArgs* args);
 size_t semx_mimo_layer_workspace_bytes(const SemxMimoLayerArgs* args);

@@ -175,6 +175,17 @@ class SemxGateSiluArgs(ctypes.Structure):
     ] + [(name, ctypes.c_void_p) for name in ("y", "xz", "o", "dout", "dy", "dxz")]
 
 
+class SemxRmsNormArgs(ctypes.Structure):
+    _fields_ = [
+        ("struct_size", ctypes.c_uint32),
+        ("bf16", ctypes.c_int32),
+        ("eps", ctypes.c_float),
+        ("reserved", ctypes.c_int32),
+        ("n", ctypes.c_int64),
+        ("d", ctypes.c_int64),
+    ] + [(name, ctypes.c_void_p) for name in ("x", "weight", "y", "rstd", "dy", "dx", "dweight", "workspace")]
+
+
 # (python struct, C size query) for every argument struct in semx.h.
 STRUCTS = {
     "SemxLinossArgs": (SemxLinossArgs, "semx_linoss_args_size"),
@@ -184,6 +195,7 @@ STRUCTS = {
     "SemxMimoLayerArgs": (SemxMimoLayerArgs, "semx_mimo_layer_args_size"),
     "SemxConvSiluArgs": (SemxConvSiluArgs, "semx_conv_silu_args_size"),
     "SemxGateSiluArgs": (SemxGateSiluArgs, "semx_gate_silu_args_size"),
+    "SemxRmsNormArgs": (SemxRmsNormArgs, "semx_rms_norm_args_size"),
 }
 
 # Every symbol semx.h declares, with its ctypes signature.
@@ -225,6 +237,10 @@ _SIGNATURES = {
     "semx_gate_silu_args_size": (ctypes.c_size_t, []),
     "semx_gate_silu_fwd": (ctypes.c_int, [ctypes.POINTER(SemxGateSiluArgs), ctypes.c_void_p]),
     "semx_gate_silu_bwd": (ctypes.c_int, [ctypes.POINTER(SemxGateSiluArgs), ctypes.c_void_p]),
+    "semx_rms_norm_args_size": (ctypes.c_size_t, []),
+    "semx_rms_norm_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(SemxRmsNormArgs)]),
+    "semx_rms_norm_fwd": (ctypes.c_int, [ctypes.POINTER(SemxRmsNormArgs), ctypes.c_void_p]),
+    "semx_rms_norm_bwd": (ctypes.c_int, [ctypes.POINTER(SemxRmsNormArgs), ctypes.c_void_p]),
     "semx_mimo_layer_args_size": (ctypes.c_size_t, []),
     "semx_mimo_layer_ckpt_bytes": (ctypes.c_size_t, [ctypes.POINTER(SemxMimoLayerArgs)]),
     "semx_mimo_layer_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(SemxMimoLayerArgs)]),

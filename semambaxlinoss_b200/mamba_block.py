@@ -30,13 +30,56 @@ from typing import Literal
 import torch
 from torch import nn
 
+from . import _lib
 from .linoss import LinOSS
 from .mixer import MambaStyleMixer
 from .selective_lru import SelectiveLRU, SelectiveLRUMIMO
 
 
+class _RmsNorm(torch.autograd.Function):
+    """semx_rms_norm_fwd / _bwd: one kernel per direction (fp32 arithmetic, output in the
+    input's dtype, fp32 or bf16)."""
+
+    @staticmethod
+    def forward(ctx, x, weight, eps):
+        if not x.is_cuda:
+            raise RuntimeError("RMSNorm requires CUDA tensors.")
+        if x.dtype not in (torch.float32, torch.bfloat16):
+            raise ValueError(f"RMSNorm: unsupported dtype {x.dtype}")
+        shape = x.shape
+        x2 = x.contiguous().view(-1, shape[-1])
+        w = weight.detach().float().contiguous()
+        y = torch.empty_like(x2)
+        rstd = torch.empty(x2.shape[0], dtype=torch.float32, device=x.device)
+        a = _lib.new_args(_lib.SemxRmsNormArgs)
+        a.bf16, a.eps, a.n, a.d = int(x.dtype == torch.bfloat16), float(eps), x2.shape[0], x2.shape[1]
+        a.x, a.weight, a.y, a.rstd = x2.data_ptr(), w.data_ptr(), y.data_ptr(), rstd.data_ptr()
+        _lib.call("semx_rms_norm_fwd", a, x.device)
+        ctx.save_for_backward(x2, w, rstd)
+        ctx.meta = (shape, float(eps), weight.dtype)
+        return y.view(shape)
+
+    @staticmethod
+    def backward(ctx, dy):
+        x2, w, rstd = ctx.saved_tensors
+        shape, eps, wdtype = ctx.meta
+        dy2 = dy.to(x2.dtype).contiguous().view(-1, shape[-1])
+        dx = torch.empty_like(x2)
+        dw = torch.empty_like(w)
+        a = _lib.new_args(_lib.SemxRmsNormArgs)
+        a.bf16, a.eps, a.n, a.d = int(x2.dtype == torch.bfloat16), eps, x2.shape[0], x2.shape[1]
+        a.x, a.weight, a.rstd = x2.data_ptr(), w.data_ptr(), rstd.data_ptr()
+        a.dy, a.dx, a.dweight = dy2.data_ptr(), dx.data_ptr(), dw.data_ptr()
+        ws = _lib.empty_f32(_lib.load().semx_rms_norm_workspace_bytes(a), x2.device)
+        a.workspace = ws.data_ptr()
+        _lib.call("semx_rms_norm_bwd", a, x2.device)
+        return dx.view(shape), dw.to(wdtype), None
+
+
 class RMSNorm(nn.Module):
-    """Root-mean-square normalisation over the last dimension with a learned gain."""
+    """Root-mean-square normalisation over the last dimension with a learned gain:
+    y = x / sqrt(mean(x^2) + eps) * weight, in fp32, returned in x's dtype. Runs the
+    semx_rms_norm kernels (CUDA tensors only)."""
 
     def __init__(self, hidden_size: int, eps: float = 1e-5, device=None, dtype=None):
         super().__init__()
@@ -45,9 +88,7 @@ class RMSNorm(nn.Module):
         self.register_parameter("bias", None)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        xf = x.float()
-        y = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.eps)
-        return (y * self.weight.float()).to(x.dtype)
+        return _RmsNorm.apply(x, self.weight, self.eps)
 
 
 class Block(nn.Module):

@@ -353,6 +353,50 @@ __device__ __forceinline__ void advance(const ModeParams& mp, bool detune, const
   }
 }
 
+// The complex gamma-gain Disc of a step from its kept pole: nu^2 = |lam|^2, the gain
+// sqrt(max(1 - nu^2, 1e-6)) as q rsqrt(q); nu itself is not needed (nu2 is returned).
+__device__ __forceinline__ Disc kept_pole(float lre, float lim, float om, float sd, bool detune, float dth,
+                                          float& nu2) {
+  Disc d;
+  d.lre = lre;
+  d.lim = lim;
+  d.base = om + (detune ? sd * dth : dth);
+  nu2 = fmaf(lre, lre, lim * lim);
+  const float q = fmaxf(1.f - nu2, 1e-6f);
+  d.rs = rsqrt_approx(q);
+  d.gr = q * d.rs;
+  d.gi = 0.f;
+  d.nu = 0.f;
+  d.cs = d.sn = 0.f;
+  d.inv_den = 1.f;
+  return d;
+}
+
+// advance(), also returning each mode's pole (lre, lim) for the adjoint of the same step.
+template <bool REAL, int GAIN>
+__device__ __forceinline__ void advance_keep(const ModeParams& mp, bool detune, const StepIn<REAL>& in,
+                                             float (&hr)[kGM], float (&hi)[kGM], float (&lr)[kGM],
+                                             float (&li)[kGM]) {
+#pragma unroll
+  for (int j = 0; j < kGM; ++j) {
+    const Disc d = discretise<REAL, GAIN>(mp.a[j], mp.om[j], mp.sd[j], detune, in.dnu, in.dth);
+    lr[j] = d.lre;
+    li[j] = d.lim;
+    const float gxr = d.gr * in.x;
+    if (REAL) {
+      hr[j] = d.lre * hr[j] + gxr * in.bre[j];
+    } else {
+      const float gxi = d.gi * in.x;
+      const float ur = gxr * in.bre[j] - gxi * in.bim[j];
+      const float ui = gxr * in.bim[j] + gxi * in.bre[j];
+      const float nr = d.lre * hr[j] - d.lim * hi[j] + ur;
+      const float ni = d.lre * hi[j] + d.lim * hr[j] + ui;
+      hr[j] = nr;
+      hi[j] = ni;
+    }
+  }
+}
+
 // ----------------------------------------------------------------------------- forward
 template <bool REAL, int GAIN, int NG, bool EXTRA>
 __global__ void __launch_bounds__(kThreads) slru_fwd_kernel(const SParams p) {
@@ -502,7 +546,7 @@ __device__ __forceinline__ TileEntry entry_of(int k, int e, int K, int L) {
 }
 
 template <bool REAL, int GAIN, int NG, bool EXTRA>
-__global__ void __launch_bounds__(kThreads) slru_bwd_kernel(const SParams p) {
+__global__ void __launch_bounds__(kThreads, REAL ? 0 : ((GAIN == SEMX_GAIN_GAMMA && EXTRA) ? 3 : 4)) slru_bwd_kernel(const SParams p) {
   using Lay = BwdLayout<REAL, NG>;
   using T = typename Lay::T;
   constexpr int CW = 32 / NG;
@@ -619,6 +663,10 @@ __global__ void __launch_bounds__(kThreads) slru_bwd_kernel(const SParams p) {
           const int nr = min(kR, E.t0 + E.nt - ta);
           const int si = (ta - t0c) / kR;
           float H0r[kGM], H0i[kGM], Hr[kR][kGM], Hi[kR][kGM];
+          // Complex gamma gain: the recompute keeps each step's pole for the adjoint, which
+          // then evaluates only the gain's rsqrt (nu^2 = |lam|^2) instead of ex2, sin and cos.
+          constexpr bool KEEP = !REAL && GAIN == SEMX_GAIN_GAMMA;
+          float Lr[kR][kGM], Li[kR][kGM];
           {
             const float4 v = sub[(si * HS) * kThreads + tid];
             H0r[0] = v.x; H0r[1] = v.y; H0r[2] = v.z; H0r[3] = v.w;
@@ -641,7 +689,8 @@ __global__ void __launch_bounds__(kThreads) slru_bwd_kernel(const SParams p) {
             if (i < nr) {
               StepIn<REAL> in;
               tile_step<REAL, T, false>(buf, ta - E.t0 + i, c_local, g, in);
-              advance<REAL, GAIN>(mp, detune, in, Hr[i], Hi[i]);
+              if (KEEP) advance_keep<REAL, GAIN>(mp, detune, in, Hr[i], Hi[i], Lr[i], Li[i]);
+              else advance<REAL, GAIN>(mp, detune, in, Hr[i], Hi[i]);
             }
           }
           // Adjoint through the sub-block.
@@ -659,8 +708,10 @@ __global__ void __launch_bounds__(kThreads) slru_bwd_kernel(const SParams p) {
                 const float hrt = Hr[i][j], hit = Hi[i][j];
                 const float hpr = i == 0 ? H0r[j] : Hr[i > 0 ? i - 1 : 0][j];
                 const float hpi = i == 0 ? H0i[j] : Hi[i > 0 ? i - 1 : 0][j];
-                const Disc d = discretise<REAL, GAIN>(mp.a[j], mp.om[j], mp.sd[j], detune,
-                                                      in.dnu, in.dth);
+                float nu2k = 0.f;
+                const Disc d = KEEP ? kept_pole(Lr[i][j], Li[i][j], mp.om[j], mp.sd[j], detune, in.dth, nu2k)
+                                    : discretise<REAL, GAIN>(mp.a[j], mp.om[j], mp.sd[j], detune,
+                                                             in.dnu, in.dth);
                 // Local adjoint from the readout (and the envelope term).
                 float gre = dyv * in.cre[j];
                 float gim = REAL ? 0.f : -dyv * in.cim[j];
@@ -694,7 +745,7 @@ __global__ void __launch_bounds__(kThreads) slru_bwd_kernel(const SParams p) {
                 float d_dnu = 0.f, da_extra = 0.f, dbase_extra = 0.f;
                 if (GAIN == SEMX_GAIN_GAMMA) {
                   // gain = sqrt(max(1 - nu^2, 1e-6)): nu d gain / d nu = -nu^2 / gain where live.
-                  const float nu2 = d.nu * d.nu;
+                  const float nu2 = KEEP ? nu2k : d.nu * d.nu;
                   P -= ((1.f - nu2) >= 1e-6f) ? dgr * nu2 * d.rs : 0.f;
                 } else if (GAIN == SEMX_GAIN_MAMBA) {
                   d_dnu = dgr;

@@ -29,6 +29,7 @@ from typing import Literal
 
 import torch
 from torch import nn
+import torch.nn.functional as F
 
 from . import _lib
 from .linoss import LinOSS
@@ -296,6 +297,14 @@ def _layer_spec_matches(spec, layer_idx, num_layers):
     return False
 
 
+def _pointwise_transpose(conv: nn.ConvTranspose1d, y: torch.Tensor) -> torch.Tensor:
+    """``conv(y.permute(0, 2, 1)).permute(0, 2, 1)`` for a kernel-1, stride-1
+    ConvTranspose1d, evaluated channels-last: out = y W[:, :, 0] + b, one GEMM on the
+    (N, L, C_in) rows with no layout conversion or transposed copies."""
+    assert conv.kernel_size == (1,) and conv.stride == (1,) and conv.groups == 1
+    return F.linear(y, conv.weight[:, :, 0].t(), conv.bias)
+
+
 class TFMambaBlock(nn.Module):
     """Time-frequency block: a MambaBlock along time over (B*F) sequences, then along
     frequency over (B*T) sequences, each followed by a channel projection and a residual.
@@ -339,9 +348,9 @@ class TFMambaBlock(nn.Module):
             x = x + self.freq_emb.t().unsqueeze(0).unsqueeze(2)
         x = x.permute(0, 3, 2, 1).contiguous().view(b * f, t, c)
         if self.use_transpose:
-            x = self.tlinear(self.time_mamba(x).permute(0, 2, 1)).permute(0, 2, 1) + x
+            x = _pointwise_transpose(self.tlinear, self.time_mamba(x)) + x
             x = x.view(b, f, t, c).permute(0, 2, 1, 3).contiguous().view(b * t, f, c)
-            x = self.flinear(self.freq_mamba(x).permute(0, 2, 1)).permute(0, 2, 1) + x
+            x = _pointwise_transpose(self.flinear, self.freq_mamba(x)) + x
         else:
             x = self.tlinear(self.time_mamba(x)) + x
             x = x.view(b, f, t, c).permute(0, 2, 1, 3).contiguous().view(b * t, f, c)

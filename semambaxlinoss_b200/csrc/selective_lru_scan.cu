@@ -270,10 +270,37 @@ __device__ __forceinline__ const float* mode_src(const SParams& p, int row) {
 }
 
 // Issues the copies of steps [t0, t0 + nt) of sequence s into `buf` (does not commit).
+// A full tile (TT steps, CB channels, N = NP modes, 16-byte rows) takes the first branch,
+// whose item -> (row, step, chunk) split uses compile-time shapes (shifts instead of the
+// general branch's runtime divisions: the copy loop is a tenth of the kernels' issue slots
+// otherwise); ragged tiles take the general branch.
 template <class T>
 __device__ void tile_load(const SParams& p, float* buf, int64_t s, int t0, int nt, int c0, int nc,
                           bool vecC, bool vecN) {
   const int N = (int)p.N;
+  if (vecC && vecN && nt == T::kTT && nc == T::CB && N == T::NP) {
+    constexpr int qc = T::CB / 4, per_c = T::kTT * qc, items_c = T::kRowC * per_c;
+#pragma unroll
+    for (int it0 = 0; it0 < items_c; it0 += kThreads) {
+      const unsigned it = it0 + threadIdx.x;
+      if (items_c % kThreads == 0 || it < (unsigned)items_c) {
+        const unsigned a = it / per_c, rem = it % per_c, i = rem / qc, j = rem % qc;
+        cp_async16(T::chan(buf, a) + i * T::CB + 4 * j,
+                   chan_src<T>(p, a) + ((s * p.L + t0 + i) * p.C + c0) + 4 * j);
+      }
+    }
+    constexpr int qn = T::NP / 4, per_n = T::kTT * qn, items_n = T::kRowN * per_n;
+#pragma unroll
+    for (int it0 = 0; it0 < items_n; it0 += kThreads) {
+      const unsigned it = it0 + threadIdx.x;
+      if (items_n % kThreads == 0 || it < (unsigned)items_n) {
+        const unsigned a = it / per_n, rem = it % per_n, i = rem / qn, j = rem % qn;
+        cp_async16(T::mode(buf, a) + i * T::NP + 4 * j,
+                   mode_src(p, a) + (s * p.L + t0 + i) * T::NP + 4 * j);
+      }
+    }
+    return;
+  }
   if (vecC) {
     const int q = nc >> 2;  // 16-byte chunks per channel row
     const int items = T::kRowC * nt * q;
@@ -447,6 +474,9 @@ __global__ void __launch_bounds__(kThreads) slru_fwd_kernel(const SParams p) {
     cp_async_commit();
     float* buf = smem + (k & 1) * T::kBuf;
     const int t0 = k * kTileF, nt = min(kTileF, L - t0);
+    // Unrolled so the poles of later steps (which do not depend on the state) issue
+    // between the state updates: real 404 x 321 forward 0.38 -> 0.30 ms.
+#pragma unroll 8
     for (int i = 0; i < nt; ++i) {
       const int t = t0 + i;
       if (p.ckpt != nullptr && t == next_ck) {
@@ -643,6 +673,7 @@ __global__ void __launch_bounds__(kThreads, REAL ? 0 : ((GAIN == SEMX_GAIN_GAMMA
         sub[tid] = make_float4(hr[0], hr[1], hr[2], hr[3]);
         if (!REAL) sub[kThreads + tid] = make_float4(hi[0], hi[1], hi[2], hi[3]);
       } else if (E.p1) {  // Pass 1: recurrence from the checkpoint, state every kR steps kept.
+#pragma unroll 4
         for (int i = 0; i < E.nt; ++i) {
           const int t = E.t0 + i;
           if (((t - t0c) % kR) == 0) {

@@ -49,7 +49,10 @@ constexpr int kThreads = 128;
 constexpr int kGM = 4;      // modes per thread
 constexpr int kR = 4;       // steps per register-resident sub-block (backward)
 constexpr int kFlush = 8;   // steps per dB/dC cluster reduction (backward)
-constexpr int kTileF = 32;  // steps per staged tile, forward
+constexpr int kTileF = 32;  // steps per staged tile, forward (real)
+// Complex forwards stage 16 steps: their 40 KB of double-buffered 32-step tiles held 5 CTAs
+// per SM where registers allow 7 (404 x 321 gamma forward 0.852 -> 0.824 ms).
+template <bool REAL> constexpr int tile_f() { return REAL ? kTileF : 16; }
 constexpr int kTileB = 16;  // steps per staged tile, backward
 // Two CTAs per cluster: measured faster than 8 (which spans a 256-channel sequence and
 // needs no cluster sums in HBM) on every shape tried — real 404 x 321 backward 1.53 ->
@@ -427,7 +430,8 @@ __device__ __forceinline__ void advance_keep(const ModeParams& mp, bool detune, 
 // ----------------------------------------------------------------------------- forward
 template <bool REAL, int GAIN, int NG, bool EXTRA>
 __global__ void __launch_bounds__(kThreads) slru_fwd_kernel(const SParams p) {
-  using T = Tiles<REAL, NG, kTileF, false>;
+  constexpr int TF = tile_f<REAL>();
+  using T = Tiles<REAL, NG, TF, false>;
   constexpr int CW = 32 / NG;
   extern __shared__ float4 fwd_smem4[];
   float* smem = reinterpret_cast<float*>(fwd_smem4);
@@ -460,8 +464,8 @@ __global__ void __launch_bounds__(kThreads) slru_fwd_kernel(const SParams p) {
   }
 
   tile_zero_padding<T>(smem, nc, (int)p.N);
-  const int ntiles = (L + kTileF - 1) / kTileF;
-  if (ntiles > 0) tile_load<T>(p, smem, s, 0, min(kTileF, L), c0, nc, vecC, vecN);
+  const int ntiles = (L + TF - 1) / TF;
+  if (ntiles > 0) tile_load<T>(p, smem, s, 0, min(TF, L), c0, nc, vecC, vecN);
   cp_async_commit();
   int next_ck = 0;
   float* yrow = p.y + s * p.L * p.C + c;
@@ -469,11 +473,11 @@ __global__ void __launch_bounds__(kThreads) slru_fwd_kernel(const SParams p) {
     cp_async_wait_all();
     __syncthreads();
     if (k + 1 < ntiles)
-      tile_load<T>(p, smem + ((k + 1) & 1) * T::kBuf, s, (k + 1) * kTileF,
-                   min(kTileF, L - (k + 1) * kTileF), c0, nc, vecC, vecN);
+      tile_load<T>(p, smem + ((k + 1) & 1) * T::kBuf, s, (k + 1) * TF,
+                   min(TF, L - (k + 1) * TF), c0, nc, vecC, vecN);
     cp_async_commit();
     float* buf = smem + (k & 1) * T::kBuf;
-    const int t0 = k * kTileF, nt = min(kTileF, L - t0);
+    const int t0 = k * TF, nt = min(TF, L - t0);
     // Unrolled so the poles of later steps (which do not depend on the state) issue
     // between the state updates: real 404 x 321 forward 0.38 -> 0.30 ms.
 #pragma unroll 8
@@ -1088,7 +1092,7 @@ size_t dbc_floats(const SemxSelectiveLruArgs* a) {
 template <bool REAL, int GAIN, int NG, bool EXTRA>
 int launch_fwd(const SParams& p, const Geometry& g, cudaStream_t st) {
   const dim3 grid((unsigned)g.nblocks, (unsigned)p.S);
-  const size_t smem = Tiles<REAL, NG, kTileF, false>::bytes();
+  const size_t smem = Tiles<REAL, NG, tile_f<REAL>(), false>::bytes();
   auto kern = slru_fwd_kernel<REAL, GAIN, NG, EXTRA>;
   if (!semx::allow_smem(kern, smem)) return SEMX_ERR_LAUNCH;
   kern<<<grid, kThreads, smem, st>>>(p);

@@ -579,8 +579,10 @@ __device__ __forceinline__ TileEntry entry_of(int k, int e, int K, int L) {
   return E;
 }
 
+// Complex gamma kernels run 3 CTAs per SM: with the kept poles they need more than the 128
+// registers of 4 CTAs (which spilled; 404 x 321 backward 3.233 -> 3.203 ms at 164).
 template <bool REAL, int GAIN, int NG, bool EXTRA>
-__global__ void __launch_bounds__(kThreads, REAL ? 0 : ((GAIN == SEMX_GAIN_GAMMA && EXTRA) ? 3 : 4)) slru_bwd_kernel(const SParams p) {
+__global__ void __launch_bounds__(kThreads, REAL ? 0 : (GAIN == SEMX_GAIN_GAMMA ? 3 : 4)) slru_bwd_kernel(const SParams p) {
   using Lay = BwdLayout<REAL, NG>;
   using T = typename Lay::T;
   constexpr int CW = 32 / NG;

@@ -29,6 +29,25 @@ def _inv_softplus(x: torch.Tensor) -> torch.Tensor:
     return x + torch.log(-torch.expm1(-x))
 
 
+def _step_projection(lin: nn.Linear, z: torch.Tensor) -> torch.Tensor:
+    """``lin(z)`` for a rank-r step projection (r -> d_model) as one fp32 GEMM, with the
+    bias as the weight row of an appended column of ones.
+
+    The result is the (batch, time, d_model) fp32 tensor the scan reads. Under bf16
+    autocast, ``nn.Linear`` on the non-contiguous split of the x_proj output runs a bf16
+    matmul plus a separate bias add, and the scan then casts the result to fp32. Each of
+    those passes is a full (batch, time, d_model) read and write. Outside autocast the
+    value is the same as ``lin(z)`` up to rounding order.
+    """
+    shp = z.shape
+    with torch.autocast(device_type=z.device.type, enabled=False):
+        z2 = z.reshape(-1, shp[-1]).float()
+        z1 = torch.cat([z2, z2.new_ones(z2.shape[0], 1)], dim=1)
+        w1 = torch.cat([lin.weight.t(), lin.bias.unsqueeze(0)], dim=0).float()
+        out = torch.mm(z1, w1)
+    return out.reshape(*shp[:-1], lin.out_features)
+
+
 def _phase_grid(n_modes: int, n_real_modes: int, theta_max: float) -> torch.Tensor:
     """``n_real_modes`` zero phases, then oscillators evenly spaced on (0, theta_max]."""
     n_osc = n_modes - n_real_modes
@@ -126,11 +145,11 @@ class SelectiveLRU(nn.Module):
         r, N = self.dt_rank, self.d_state
         x = x.float()
         dnu_r, dth_r, B_sel, C_sel = torch.split(self.x_proj(x), [r, r, 2 * N, 2 * N], dim=-1)
-        delta_nu = F.softplus(self.dt_nu_up(dnu_r))
+        delta_nu = F.softplus(_step_projection(self.dt_nu_up, dnu_r))
         rs = self.rate_scale if rate_scale is None else float(rate_scale)
         if rs != 1.0:
             delta_nu = delta_nu * rs
-        delta_theta = self.dt_theta_up(dth_r)
+        delta_theta = _step_projection(self.dt_theta_up, dth_r)
         a = torch.exp(self.A_log)
         g = self.env_gain if self.envelope_readout else None
         s = self.detune_gain if self.mode_detune else None

@@ -114,3 +114,30 @@ def test_mimo_drive_weight_layout():
     W, b = m._projection()
     assert W.shape == (proj_width(2, 8, 3), 24) and b.shape == (2 * 2,)
     assert torch.equal(W[-2 * 16:], drive_weight(m.B.detach()))
+
+
+def test_step_projection_matches_linear():
+    """The rank-r step projections (one GEMM with the bias as a row of the weight) give
+    nn.Linear's value and gradients, on the non-contiguous split the layer feeds them,
+    and stay fp32 under bf16 autocast (the scan reads fp32)."""
+    from semambaxlinoss_b200.selective_lru.selective_lru import _step_projection
+
+    torch.manual_seed(0)
+    lin = torch.nn.Linear(4, 32)
+    rows = torch.randn(3, 11, 20)
+    z_ref = rows[..., 2:6].clone().requires_grad_(True)
+    z = rows[..., 2:6].detach().requires_grad_(True)
+    ref = lin(z_ref)
+    g = torch.randn_like(ref)
+    (ref * g).sum().backward()
+    w_ref, b_ref = lin.weight.grad.clone(), lin.bias.grad.clone()
+    lin.zero_grad()
+    out = _step_projection(lin, z)
+    (out * g).sum().backward()
+    assert out.shape == ref.shape and out.dtype == torch.float32
+    torch.testing.assert_close(out, ref, rtol=1e-5, atol=1e-6)
+    torch.testing.assert_close(z.grad, z_ref.grad, rtol=1e-5, atol=1e-6)
+    torch.testing.assert_close(lin.weight.grad, w_ref, rtol=1e-5, atol=1e-6)
+    torch.testing.assert_close(lin.bias.grad, b_ref, rtol=1e-5, atol=1e-6)
+    with torch.autocast(device_type="cpu", dtype=torch.bfloat16):
+        assert _step_projection(lin, z.detach().to(torch.bfloat16)).dtype == torch.float32

@@ -31,9 +31,9 @@ __device__ __forceinline__ float reduce_2pi(float x) {
   constexpr float k2PiHi = 6.28125f;
   constexpr float k2PiLo = 0.0019353072f;
   // k = rint(x / 2pi) by the 1.5 * 2^23 rounding constant on the FMA pipe (exact for
-  // |x / 2pi| < 2^22, far beyond the 2^16 the Cody-Waite split allows): rintf's rounding
-  // instruction competed with ex2 / sin / cos / rsqrt for the special-function pipe
-  // (complex selective-LRU forward 404 x 321 0.827 -> 0.779 ms).
+  // |x / 2pi| < 2^22, far beyond the 2^16 the Cody-Waite split allows): with rintf the
+  // rounding instruction apparently shared the special-function pipe with ex2 / sin / cos /
+  // rsqrt (complex selective-LRU forward 404 x 321 0.827 -> 0.779 ms without it).
   const float k = fmaf(x, kInv2Pi, 12582912.f) - 12582912.f;
   return fmaf(-k, k2PiLo, fmaf(-k, k2PiHi, x));
 }

@@ -3,37 +3,44 @@
 
 Workloads (`--workload`; one "step" = one forward + backward of every pass listed):
 
-  linoss (default)  LinOSS-IMEX oscillatory scan, P = 256 oscillators, H = 64 inputs, at the
-                    scan boundary (Bu in, y2 out; dY2 in, dBu + parameter gradients out):
-                    time pass 404 sequences x 321 steps, frequency pass 1284 x 101.
+  scans (default)   configs 0, 1 and 2 below in one step (slru, then linoss, then mimo);
+                    `value` = their algorithmic bytes / the step's time, with a per-config
+                    table and a per-kernel roofline table. Also measures the generator
+                    training step (config 3) as the `generator` sub-line, and at N > 1 the
+                    named shapes split over the ranks (`sharded`, strong scaling).
+  slru              Config 0. Real selective-LRU diagonal scan (fused discretisation + readout
+                    + D skip), 404 sequences x 321 steps, C = 256 channels, N = 16 modes, Mamba
+                    gain: x ~ N(0,1), dt = softplus(N(-2, 0.5)), a = exp(A_log) with A_log ~
+                    log U(1,16), B_t, C_t ~ N(0, 1/16), D ~ N(0,1). Algorithmic bytes per
+                    (sequence, step): fwd 4 (3C + 2N) = 3200 (x, dt, B, C in; y out), bwd
+                    4 (5C + 4N) = 5376 (x, dt, dy, B, C in; d_dt, dx, dB, dC out).
+  linoss            Config 1. LinOSS-IMEX oscillatory scan, P = 256 oscillators, H = 64 inputs,
+                    at the scan boundary (Bu in, y2 out; dY2 in, dBu + parameter gradients
+                    out): time pass 404 sequences x 321 steps, frequency pass 1284 x 101.
                     A = relu(N(0,1)), dt = sigmoid(N(0,1)), complex B entries N(0, 1/sqrt(H)),
                     u ~ N(0,1), Bu = B u, upstream gradient N(0,1).
                     Algorithmic bytes per (sequence, step): fwd 16 P, bwd 24 P.
-  slru              Real selective-LRU diagonal scan (fused discretisation + readout + D skip),
-                    404 sequences x 321 steps, C = 256 channels, N = 16 modes, Mamba gain:
-                    x ~ N(0,1), dt = softplus(N(-2, 0.5)), a = exp(A_log) with A_log ~ log U(1,16),
-                    B_t, C_t ~ N(0, 1/16), D ~ N(0,1). Algorithmic bytes per (sequence, step):
-                    fwd 4 (3C + 2N) = 3200 (x, dt, B, C in; y out), bwd 4 (5C + 4N) = 5376
-                    (x, dt, dy, B, C in; d_dt, dx, dB, dC out).
-  mimo              SelectiveLRUMIMO layer, 256 features = 8 heads x 32, 128 state (16 per
-                    head), rank 4, bf16 input, fp32 state: time pass 404 x 321, frequency
-                    pass 1284 x 101. Algorithmic bytes per (sequence, step) of the layer's
-                    token-level operands: fwd 4768, bwd 8512.
-  generator         SEMamba generator training step (STFT, forward, losses, backward, AdamW),
-                    2 s utterances, batch 16 per GPU, DDP over NCCL; frames/s.
-  inference         64 sixty-second utterances enhanced end to end, sharded; frames/s.
+  mimo              Config 2. SelectiveLRUMIMO layer, 256 features = 8 heads x 32, 128 state
+                    (16 per head), rank 4, bf16 input, fp32 state: time pass 404 x 321,
+                    frequency pass 1284 x 101. Algorithmic bytes per (sequence, step) of the
+                    layer's token-level operands: fwd 4768, bwd 8512.
+  generator         Config 3. SEMamba generator training step (STFT, forward, losses, backward,
+                    AdamW), 2 s utterances, batch 16 per GPU, DDP over NCCL; frames/s.
+  inference         Config 4. 64 sixty-second utterances enhanced end to end, sharded; frames/s.
 
 Scan workloads report algorithmic GB/s (`value`, inputs resident in HBM), `e2e` (the same
 metric with host buffers and the copies inside the timed region), the roofline of the
-dominant kernel, clocks sampled during the timed region, the kernel launch count and a
-CPU baseline (the reference algorithm on the host cores, on a bounded sample). Every scan
-operand is larger than the 126 MB L2 except where `config.l2` says otherwise.
+dominant kernel (and the table of every kernel), clocks sampled during the timed region,
+the kernel launch count and a CPU baseline (the reference algorithm on the host cores, on a
+fixed sample per config). Every scan operand is larger than the 126 MB L2 except where
+`config.l2` says otherwise.
 
 `--impl reference` times the reference's CPU implementation of the path (the oracle port)
-on the host cores, on a bounded sample of the same workload.
+on the host cores, on the same fixed sample of the same workload.
 
-Multi-GPU (torchrun, one process per GPU): weak scaling for the scans (each rank scans its
-own batch, no collective on the data path) and the training step (DDP); time = max over
+Multi-GPU (torchrun, one process per GPU): weak scaling for the scans (the global batch is
+N times the named shapes; rank r scans its contiguous slice r, no collective on the data
+path) plus the strong-scaling `sharded` run, and the training step (DDP); time = max over
 ranks, measured with CUDA events.
 """
 from __future__ import annotations
@@ -63,16 +70,22 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=None, help="timed steps (default per workload)")
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["semx", "reference"], default="semx")
-    ap.add_argument("--workload", choices=["linoss", "slru", "mimo", "generator", "inference"],
-                    default="linoss")
+    ap.add_argument("--workload", choices=["scans", "linoss", "slru", "mimo", "generator", "inference"],
+                    default="scans")
     ap.add_argument("--batch", type=int, default=16, help="generator: utterances per GPU")
     ap.add_argument("--micro-batch", type=int, default=4, help="inference: utterances per forward")
     ap.add_argument("--chunk", type=int, default=None, help="checkpoint interval of the scan")
     ap.add_argument("--slru-complex", action="store_true",
                     help="slru: the complex scan with the gamma gain (the generator's time scans)")
     ap.add_argument("--sequences", type=int, default=None, help="slru: sequences (default 404)")
-    ap.add_argument("--cpu-sample-frac", type=float, default=None)
-    ap.add_argument("--ref-sample-frac", type=float, default=None)
+    ap.add_argument("--ref-sample-frac", type=float, default=None,
+                    help="reference arm: fraction of each pass's sequences per step (default: the "
+                         "workload's fixed sample)")
+    ap.add_argument("--no-sharded", action="store_true",
+                    help="N > 1: skip the strong-scaling run over the named shapes")
+    ap.add_argument("--no-generator", action="store_true",
+                    help="scans: skip the generator training-step sub-measurement")
+    ap.add_argument("--gen-steps", type=int, default=10, help="timed generator steps (scans workload)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=10)
@@ -81,7 +94,8 @@ def parse_args():
                     help="skip the 1.5 s busy period before timing (for profiler runs)")
     args = ap.parse_args()
     if args.steps is None:
-        args.steps = {"linoss": 200, "slru": 20, "mimo": 20, "generator": 10, "inference": 1}[args.workload]
+        args.steps = {"scans": 20, "linoss": 200, "slru": 20, "mimo": 20, "generator": 10,
+                      "inference": 1}[args.workload]
     return args
 
 
@@ -103,13 +117,16 @@ def profiled_traffic(kernel: str, workload: str, units: int):
     """DRAM bytes of one launch of `kernel` over `units` (sequence, step) units, from an
     ncu capture recorded in profiles/*.md as `traffic_bytes_per_launch[<kernel>|<workload>|
     <units>]: <bytes>`; a capture of a different size is scaled by the units processed
-    (the traffic of these scans grows in proportion). None if no capture is recorded."""
+    (the traffic of these scans grows in proportion). Returns (bytes, source) with source
+    naming the profile file and the capture's size, or (None, None) if none is recorded."""
     pat = re.compile(rf"traffic_bytes_per_launch\[{re.escape(kernel)}\|{re.escape(workload)}\|(\d+)\]:\s*(\d+)")
     for f in sorted((ROOT / "profiles").glob("*.md")):
         m = pat.search(f.read_text())
         if m:
-            return float(m.group(2)) * units / int(m.group(1))
-    return None
+            return (float(m.group(2)) * units / int(m.group(1)),
+                    f"profiles/{f.name} (ncu capture of {m.group(1)} units"
+                    + (", scaled by units)" if int(m.group(1)) != units else ")"))
+    return None, None
 
 
 class ClockSampler:
@@ -316,6 +333,7 @@ class SlruPass:
 
         C, N = SLRU_C, SLRU_N
         self.lib, self._lib = _lib.load(), _lib
+        self.complex_ = complex_
         if complex_:  # x, dt, dth, B, C (re, im) in, y out / + dy in, 3 channel + 4 mode grads out
             self.fwd_bytes_per_unit = 4 * (4 * C + 4 * N)
             self.bwd_bytes_per_unit = 4 * (7 * C + 8 * N)
@@ -551,36 +569,69 @@ def _mimo_cpu_step(sample):
 # ------------------------------------------------------------------------ scan workloads
 WORKLOADS = {
     "linoss": {
+        "config": "1",
         "metric": "LinOSS-IMEX scan fwd+bwd, algorithmic HBM GB/s (time 404x321 + freq 1284x101, P=256)",
         "describe": "LinOSS-IMEX scan fwd+bwd at the scan boundary, time 404x321 + freq 1284x101, "
                     "P=256 oscillators, H=64",
         "data": "synthetic, seeded: A = relu(N(0,1)), dt = sigmoid(N(0,1)), B ~ N(0, 1/sqrt(64)), u ~ N(0,1)",
         "dtype": "f32",
-        "chunk": 64, "cpu_frac": 0.5, "ref_frac": 1.0 / 16,
+        "chunk": 64, "sample_frac": 1.0 / 32,
         "l2": "no flush: every operand is 265 MB, larger than the 126 MB L2",
         "cpu_sample": _linoss_cpu_sample, "cpu_step": _linoss_cpu_step,
     },
     "slru": {
+        "config": "0",
         "metric": "Selective-LRU real diagonal scan fwd+bwd, algorithmic HBM GB/s (404x321, C=256, N=16)",
         "describe": "real selective-LRU scan (Mamba gain) fwd+bwd, 404 sequences x 321 steps, "
                     "C=256 channels, N=16 modes",
         "data": "synthetic, seeded: x ~ N(0,1), dt = softplus(N(-2,0.5)), a ~ U(1,16), B, C ~ N(0,1/16)",
         "dtype": "f32",
-        "chunk": 16, "cpu_frac": 8.0 / 404, "ref_frac": 4.0 / 404,
+        "chunk": 16, "sample_frac": 1.0 / 404,
         "l2": "no flush: x, dt, dy, y and each gradient are 133 MB, larger than the 126 MB L2",
         "cpu_sample": _slru_cpu_sample, "cpu_step": _slru_cpu_step,
     },
     "mimo": {
+        "config": "2",
         "metric": "Selective-LRU MIMO layer fwd+bwd, algorithmic HBM GB/s (time 404x321 + freq 1284x101, "
                   "8 heads x 32, state 128, rank 4)",
         "describe": "SelectiveLRUMIMO layer fwd+bwd (bf16 input, fp32 state), 256 features = 8 heads x 32, "
                     "state 128, rank 4, time 404x321 + freq 1284x101",
         "data": "synthetic, seeded: x ~ N(0,1/4) bf16, dt = softplus(N(-2,0.5)), b_t, c_t, B, C, D ~ N(0,1/4)",
         "dtype": "bf16 in / f32 state",
-        "chunk": 0, "cpu_frac": 0.5, "ref_frac": 8.0 / 404,
+        "chunk": 0, "sample_frac": 0.01,
         "l2": "no flush: the layer's activations per pass are GBs, far beyond the 126 MB L2",
         "cpu_sample": _mimo_cpu_sample, "cpu_step": _mimo_cpu_step,
     },
+}
+# The default workload: configs 0, 1 and 2 in one step, in this order.
+SCAN_SET = ("slru", "linoss", "mimo")
+
+
+def _scans_cpu_sample(frac=None):
+    """One fixed sample per config (each workload's own `sample_frac`)."""
+    parts = {k: WORKLOADS[k]["cpu_sample"](WORKLOADS[k]["sample_frac"]) for k in SCAN_SET}
+    return {"parts": parts, "bytes": sum(p["bytes"] for p in parts.values()),
+            "desc": "; ".join(f"config {WORKLOADS[k]['config']}: {p['desc']}" for k, p in parts.items())}
+
+
+def _scans_cpu_step(sample):
+    for k, part in sample["parts"].items():
+        WORKLOADS[k]["cpu_step"](part)
+
+
+WORKLOADS["scans"] = {
+    "config": "0+1+2",
+    "metric": "scan fwd+bwd, algorithmic HBM GB/s over BASELINE configs 0-2 (selective-LRU SISO real 404x321 "
+              "C=256 N=16; LinOSS-IMEX P=256 time 404x321 + freq 1284x101; SelectiveLRUMIMO 8x32 heads, "
+              "state 128, rank 4, bf16, time 404x321 + freq 1284x101)",
+    "describe": "configs 0, 1 and 2 fwd+bwd in one step: " + "; ".join(
+        f"config {WORKLOADS[k]['config']}: {WORKLOADS[k]['describe']}" for k in SCAN_SET),
+    "data": "synthetic, seeded: " + "; ".join(
+        f"config {WORKLOADS[k]['config']}: {WORKLOADS[k]['data'].split(': ', 1)[1]}" for k in SCAN_SET),
+    "dtype": "f32 (configs 0, 1); bf16 in / f32 state (config 2)",
+    "chunk": None, "sample_frac": None,
+    "l2": "no flush: every operand of every pass is larger than the 126 MB L2 (133 MB - GBs)",
+    "cpu_sample": _scans_cpu_sample, "cpu_step": _scans_cpu_step,
 }
 
 
@@ -598,25 +649,55 @@ def workload_spec(args):
         if args.slru_complex:
             spec["data"] += ", dth ~ N(0, 0.01), omega ~ N(0,1)"
         spec["cpu_sample"] = functools.partial(_slru_cpu_sample, complex_=args.slru_complex, S=S)
-        spec["cpu_frac"] = 8.0 / S
-        spec["ref_frac"] = 4.0 / S
+        spec["sample_frac"] = 1.0 / S
     return spec
 
 
-def _make_passes(name, rank, device, chunk, args):
+def _shard(S, rank, world):
+    """Rank `rank`'s contiguous slice [floor(r S / W), floor((r + 1) S / W)) of S sequences."""
+    return (rank + 1) * S // world - rank * S // world
+
+
+def _make_passes(name, rank, device, chunk, args, world=1, sharded=False):
+    """The passes of one step. `sharded`: each pass holds this rank's contiguous slice of the
+    named shape's sequences (strong scaling); otherwise the full named shape (every rank
+    its own batch: weak scaling)."""
+    if name == "scans":
+        return [p for sub in SCAN_SET for p in _make_passes(sub, rank, device, None, args, world, sharded)]
+    chunk = chunk or WORKLOADS[name]["chunk"]
+    size = (lambda S: _shard(S, rank, world)) if sharded else (lambda S: S)
     if name == "linoss":
-        return [LinossPass(S, L, seed=1000 * rank + i, device=device, chunk=chunk)
-                for i, (_, S, L) in enumerate(LIN_PASSES)]
-    if name == "slru":
-        return [SlruPass(args.sequences or SLRU_S, SLRU_L, seed=1000 * rank, device=device, chunk=chunk,
-                         complex_=args.slru_complex)]
-    layer = _mimo_layer(device, seed=7)
-    return [MimoPass(layer, S, L, seed=1000 * rank + i, device=device)
-            for i, (_, S, L) in enumerate(MIMO_PASSES)]
+        ps = [LinossPass(size(S), L, seed=1000 * rank + i, device=device, chunk=chunk)
+              for i, (_, S, L) in enumerate(LIN_PASSES)]
+    elif name == "slru":
+        ps = [SlruPass(size(args.sequences or SLRU_S), SLRU_L, seed=1000 * rank, device=device, chunk=chunk,
+                       complex_=args.slru_complex)]
+    else:
+        layer = _mimo_layer(device, seed=7)
+        ps = [MimoPass(layer, size(S), L, seed=1000 * rank + i, device=device)
+              for i, (_, S, L) in enumerate(MIMO_PASSES)]
+    for p in ps:
+        p.workload = name
+        p.chunk = chunk
+    return ps
+
+
+def _kernel_passes(passes, device):
+    """The passes whose kernels carry the roofline: the scan passes themselves, and for the
+    MIMO layer the fused layer kernels alone on resident bf16 operands (MimoKernelPass)."""
+    out = []
+    for i, p in enumerate(passes):
+        if isinstance(p, MimoPass):
+            k = MimoKernelPass(p.layer, p.S, p.L, seed=5000 + i, device=device)
+            k.workload = p.workload
+            out.append(k)
+        else:
+            out.append(p)
+    return out
 
 
 def _time_passes(passes, steps, stream):
-    """Runs `steps` fwd+bwd sweeps over `passes`; returns (total ms, per-pass fwd / bwd ms)."""
+    """Runs `steps` fwd+bwd sweeps over `passes`; returns (start, end, per-pass events)."""
     sh = stream.cuda_stream
     ev = [[[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in passes] for _ in range(steps)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -632,85 +713,135 @@ def _time_passes(passes, steps, stream):
     return start, end, ev
 
 
-def run_scan(args, rank, local_rank, world):
+def _per_pass_ms(passes, ev, steps):
+    return [(p, statistics.mean(ev[k][i][0].elapsed_time(ev[k][i][1]) for k in range(steps)),
+             statistics.mean(ev[k][i][1].elapsed_time(ev[k][i][2]) for k in range(steps)))
+            for i, p in enumerate(passes)]
+
+
+def _traffic_tag(p):
+    if p.workload == "slru":
+        return "slru complex" if getattr(p, "complex_", False) else "slru real"
+    return p.workload
+
+
+def _kernel_table(kpasses, peak):
+    """Per workload and direction: kernel, ms per step (all its passes), algorithmic bytes,
+    achieved GB/s, fraction of the peak, ncu traffic of one launch of its first pass."""
+    rows = []
+    for w in dict.fromkeys(p.workload for p, _, _ in kpasses):
+        group = [(p, f, b) for p, f, b in kpasses if p.workload == w]
+        for d, name in ((1, "fwd"), (2, "bwd")):
+            p0 = group[0][0]
+            kernel = p0.kernels[d - 1]
+            ms = sum(x[d] for x in group)
+            by = sum(p.units * (p.fwd_bytes_per_unit if d == 1 else p.bwd_bytes_per_unit) for p, _, _ in group)
+            gbs = by / (ms * 1e-3) / 1e9
+            traffic, source = profiled_traffic(kernel, _traffic_tag(p0), p0.units)
+            rows.append({"config": WORKLOADS[w]["config"], "workload": w, "dir": name, "kernel": kernel,
+                         "ms": round(ms, 4), "bytes": by, "achieved": round(gbs, 1),
+                         "frac": round(gbs / peak, 4), "traffic": traffic, "traffic_source": source,
+                         "algorithmic_bytes_first_launch": p0.units * (
+                             p0.fwd_bytes_per_unit if d == 1 else p0.bwd_bytes_per_unit)})
+    return rows
+
+
+def _timed_scan(passes, args, device, stream, world, steps):
+    """Warm-up, then `steps` timed steps between barriers; returns (ms per step as the max
+    over ranks, per-pass (pass, fwd ms, bwd ms), kernel launches)."""
     from semambaxlinoss_b200 import _lib
 
+    sh = stream.cuda_stream
+    for _ in range(max(args.warmup, 3)):
+        for p in passes:
+            p.fwd(sh)
+            p.bwd(sh)
+    _barrier(world, device)
+    n0 = _lib.launch_count()
+    start, end, ev = _time_passes(passes, steps, stream)
+    _barrier(world, device)
+    launches = _lib.launch_count() - n0
+    ms = _max_over_ranks(start.elapsed_time(end), world, device) / steps
+    return ms, _per_pass_ms(passes, ev, steps), launches
+
+
+def run_scan(args, rank, local_rank, world):
     spec = workload_spec(args)
-    chunk = args.chunk or spec["chunk"]
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
     _init_dist(world, device)
-    passes = _make_passes(args.workload, rank, device, chunk, args)
+    passes = _make_passes(args.workload, rank, device, args.chunk, args)
     stream = torch.cuda.current_stream(device)
     sh = stream.cuda_stream
     step_bytes = sum(p.units * (p.fwd_bytes_per_unit + p.bwd_bytes_per_unit) for p in passes)
 
-    def step():
+    for _ in range(max(args.warmup, 3)):
         for p in passes:
             p.fwd(sh)
             p.bwd(sh)
-
-    for _ in range(max(args.warmup, 3)):
-        step()
     clocks = ClockSampler(_device_uuid(device), args.clocks_log if rank == 0 else None)
     # Keep the GPU busy ~1.5 s before timing so the clock samples see it under load.
     soak_t0 = time.time()
     torch.cuda.synchronize(device)
     while not args.no_soak and time.time() - soak_t0 < 1.5:
         for _ in range(5):
-            step()
-        torch.cuda.synchronize(device)
-
-    _barrier(world, device)
-    n0 = _lib.launch_count()
-    start, end, ev = _time_passes(passes, args.steps, stream)
-    _barrier(world, device)
-    launches = _lib.launch_count() - n0
-    t_wall1 = time.time()
-    ms_per_step = _max_over_ranks(start.elapsed_time(end), world, device) / args.steps
-    value = world * step_bytes / (ms_per_step * 1e-3) / 1e9
-    per_pass = []
-    for i, p in enumerate(passes):
-        f = statistics.mean(ev[k][i][0].elapsed_time(ev[k][i][1]) for k in range(args.steps))
-        b = statistics.mean(ev[k][i][1].elapsed_time(ev[k][i][2]) for k in range(args.steps))
-        per_pass.append((p, f, b))
-
-    # Kernel roofline: for the MIMO layer, the fused scan + readout kernels timed alone.
-    kpasses = per_pass
-    if args.workload == "mimo":
-        kp = [MimoKernelPass(passes[0].layer, S, L, seed=5000 + i, device=device)
-              for i, (_, S, L) in enumerate(MIMO_PASSES)]
-        for _ in range(3):
-            for p in kp:
+            for p in passes:
                 p.fwd(sh)
                 p.bwd(sh)
         torch.cuda.synchronize(device)
-        ks, ke, kev = _time_passes(kp, max(3, args.steps // 2), stream)
-        torch.cuda.synchronize(device)
+
+    ms_per_step, per_pass, launches = _timed_scan(passes, args, device, stream, world, args.steps)
+    t_wall1 = time.time()
+    value = world * step_bytes / (ms_per_step * 1e-3) / 1e9
+
+    # Kernel rooflines (the MIMO layer's fused kernels timed alone).
+    kp = _kernel_passes(passes, device)
+    if any(k is not p for k, p in zip(kp, passes)):
         kn = max(3, args.steps // 2)
-        kpasses = [(p, statistics.mean(kev[k][i][0].elapsed_time(kev[k][i][1]) for k in range(kn)),
-                    statistics.mean(kev[k][i][1].elapsed_time(kev[k][i][2]) for k in range(kn)))
-                   for i, p in enumerate(kp)]
-        del kp
+        _, kpasses, _ = _timed_scan(kp, args, device, stream, 1, kn)
+    else:
+        kpasses = per_pass
+    del kp
 
     e2e = None if args.no_e2e else run_scan_e2e(
         passes, args, device, stream, step_bytes, world,
-        lambda: _make_passes(args.workload, rank, device, chunk, args))
+        lambda: _make_passes(args.workload, rank, device, args.chunk, args))
+
+    # Strong scaling over the named shapes: rank r scans its contiguous slice of every pass.
+    sharded = None
+    if world > 1 and not args.no_sharded:
+        sp = _make_passes(args.workload, rank, device, args.chunk, args, world, sharded=True)
+        full_bytes = step_bytes  # the named shapes' bytes (every rank's full batch is one named set)
+        ms_sh, _, _ = _timed_scan(sp, args, device, stream, world, args.steps)
+        sharded = {"value": round(full_bytes / (ms_sh * 1e-3) / 1e9, 2), "unit": "GB/s",
+                   "ms_per_step": round(ms_sh, 4), "scaling": "strong",
+                   "sequences_rank0": [p.S for p in sp] if rank == 0 else None,
+                   "note": "the named shapes split into contiguous per-rank sequence slices "
+                           "[floor(r S / W), floor((r+1) S / W)); time = max over ranks"}
+        del sp
+    gen = None
+    if args.workload == "scans" and not args.no_generator:
+        gen = measure_generator(args, rank, local_rank, world, device, args.gen_steps, clocks=False)
     clocks.stop()
     _finish_dist(world)
     if rank != 0:
         return
 
     peak, peak_kind = load_peaks()
-    fwd_ms = sum(f for _, f, _ in kpasses)
-    bwd_ms = sum(b for _, _, b in kpasses)
-    fwd_bytes = sum(p.units * p.fwd_bytes_per_unit for p, _, _ in kpasses)
-    bwd_bytes = sum(p.units * p.bwd_bytes_per_unit for p, _, _ in kpasses)
-    kf, kb = kpasses[0][0].kernels
-    dom, dom_bytes, dom_ms = (kb, bwd_bytes, bwd_ms) if bwd_ms >= fwd_ms else (kf, fwd_bytes, fwd_ms)
-    dom_gbs = dom_bytes / (dom_ms * 1e-3) / 1e9
-    tag = args.workload if args.workload != "slru" else ("slru complex" if args.slru_complex else "slru real")
-    traffic = profiled_traffic(dom, tag, kpasses[0][0].units)
+    table = _kernel_table(kpasses, peak)
+    dom = max(table, key=lambda r: r["ms"])
+    slow = min(table, key=lambda r: r["frac"])
+    configs = {}
+    for w in dict.fromkeys(p.workload for p in passes):
+        group = [(p, f, b) for p, f, b in per_pass if p.workload == w]
+        by = sum(p.units * (p.fwd_bytes_per_unit + p.bwd_bytes_per_unit) for p, _, _ in group)
+        ms = sum(f + b for _, f, b in group)
+        configs[WORKLOADS[w]["config"]] = {
+            "workload": w, "fwd_ms": round(sum(f for _, f, _ in group), 4),
+            "bwd_ms": round(sum(b for _, _, b in group), 4), "bytes": by,
+            "GB/s": round(by / (ms * 1e-3) / 1e9, 1), "frac": round(by / (ms * 1e-3) / 1e9 / peak, 4),
+            "passes": [{"sequences": p.S, "steps": p.L} for p, _, _ in group],
+            "chunk": group[0][0].chunk or None}
     out = {
         "metric": spec["metric"],
         "value": round(value, 2),
@@ -726,45 +857,45 @@ def run_scan(args, rank, local_rank, world):
         "data": spec["data"],
         "config": {
             "workload": spec["describe"],
-            "passes": [{"sequences": p.S, "steps": p.L} for p in passes],
-            "chunk": chunk or None,
             "bytes_per_step": step_bytes,
             "l2": spec["l2"],
-            "parallelism": f"weak dp{world}: each rank scans its own batch, no collective",
+            "parallelism": f"weak dp{world}: the global batch is {world}x the named shapes, rank r scans "
+                           "its contiguous slice r (one named set), no collective",
         },
         "roofline": {
             "bound": "hbm",
-            "kernel": dom,
-            "achieved": round(dom_gbs, 1),
+            "kernel": dom["kernel"],
+            "config": dom["config"],
+            "achieved": dom["achieved"],
             "peak": peak,
             "unit": "GB/s",
-            "frac": round(dom_gbs / peak, 4),
+            "frac": dom["frac"],
             "peak_kind": peak_kind,
-            "traffic": traffic,
-            "algorithmic_bytes_first_launch": kpasses[0][0].units * (
-                kpasses[0][0].bwd_bytes_per_unit if dom == kb else kpasses[0][0].fwd_bytes_per_unit),
-            "note": "achieved = algorithmic bytes / CUDA-event time of the entry point (includes its "
-                    "small reduction launches); traffic = ncu DRAM bytes of one launch of the first pass "
-                    "(profiles/*.md; scaled by units when the capture was a smaller case)",
+            "traffic": dom["traffic"],
+            "traffic_source": dom["traffic_source"],
+            "algorithmic_bytes_first_launch": dom["algorithmic_bytes_first_launch"],
+            "slowest_frac_kernel": {k: slow[k] for k in ("config", "kernel", "dir", "achieved", "frac")},
+            "note": "the dominant kernel = the largest share of the step's kernel time; achieved = "
+                    "algorithmic bytes / CUDA-event time of the entry point (includes its small reduction "
+                    "launches); traffic = ncu DRAM bytes of one launch of the first pass, recorded in the "
+                    "named profile (not measured in this run)",
         },
-        "kernels": {
-            f"{kf}": {"ms": round(fwd_ms, 4), "GB/s": round(fwd_bytes / (fwd_ms * 1e-3) / 1e9, 1),
-                      "bytes": fwd_bytes},
-            f"{kb}+reductions": {"ms": round(bwd_ms, 4), "GB/s": round(bwd_bytes / (bwd_ms * 1e-3) / 1e9, 1),
-                                 "bytes": bwd_bytes},
-        },
+        "kernels": table,
+        "configs": configs,
         "hbm_frac_of_8tbs": round(value / world / 8000.0, 4),
         "gpu_launches": launches,
         "clocks": clocks.summary(soak_t0, t_wall1),
         "e2e": e2e,
     }
-    if args.workload == "mimo":
-        out["layer_ms"] = {"fwd": round(sum(f for _, f, _ in per_pass), 4),
-                           "bwd": round(sum(b for _, _, b in per_pass), 4)}
-        out["gpu_launches_note"] = ("libsemx kernels only; the layer's token projections (one GEMM "
+    if sharded is not None:
+        out["sharded"] = sharded
+    if gen is not None:
+        out["generator"] = gen
+    if any(p.workload == "mimo" for p in passes):
+        out["gpu_launches_note"] = ("libsemx kernels only; the MIMO layer's token projections (one GEMM "
                                     "forward, two backward) run as cuBLAS kernels")
     if world == 1 and not args.no_cpu_baseline:
-        out["cpu_baseline"] = cpu_baseline(spec, args.cpu_sample_frac or spec["cpu_frac"], repeats=3)
+        out["cpu_baseline"] = cpu_baseline(spec, repeats=3)
     print(json.dumps(out), flush=True)
 
 
@@ -826,6 +957,7 @@ def run_scan_e2e(passes, args, device, stream, step_bytes, world, make_set):
     end.record(stream)
     torch.cuda.synchronize(device)
     ms = _max_over_ranks(start.elapsed_time(end), world, device) / args.e2e_steps
+    del sets[1]
     return {"value": round(world * step_bytes / (ms * 1e-3) / 1e9, 3), "unit": "GB/s",
             "ms_per_step": round(ms, 3), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
             "path": "public entry points with pinned host buffers; copies in and out on two "
@@ -833,9 +965,9 @@ def run_scan_e2e(passes, args, device, stream, step_bytes, world, make_set):
 
 
 # ----------------------------------------------------------------------------- CPU legs
-def cpu_baseline(spec, frac, repeats=3):
+def cpu_baseline(spec, repeats=3, frac=None):
     torch.set_num_threads(os.cpu_count())
-    sample = spec["cpu_sample"](frac)
+    sample = spec["cpu_sample"](frac if frac is not None else spec["sample_frac"])
     spec["cpu_step"](sample)
     times = []
     for _ in range(repeats):
@@ -845,8 +977,7 @@ def cpu_baseline(spec, frac, repeats=3):
     t = statistics.median(times)
     return {"value": round(sample["bytes"] / t / 1e9, 5), "unit": "GB/s",
             "cores": torch.get_num_threads(), "kind": "port",
-            "sample": f"{frac:.4g} of each pass's sequences ({sample['desc']}), fwd+bwd float32, "
-                      f"median of {repeats}",
+            "sample": f"fixed sample ({sample['desc']}), fwd+bwd float32, median of {repeats}",
             "seconds": round(t, 3)}
 
 
@@ -859,18 +990,9 @@ def run_reference(args, rank):
         return
     spec = workload_spec(args)
     torch.set_num_threads(os.cpu_count())
-    frac = args.ref_sample_frac
-    if frac is None:
-        # Size the per-step sample so that warm-up + timed steps end within about two
-        # minutes on this host: time one step of a small sample, then scale (never above
-        # the workload's default fraction).
-        f0 = spec["ref_frac"] / 8
-        probe = spec["cpu_sample"](f0)
-        t0 = time.perf_counter()
-        spec["cpu_step"](probe)
-        t_probe = max(time.perf_counter() - t0, 1e-3)
-        frac = min(spec["ref_frac"], probe["frac"] * 120.0 / ((args.steps + args.warmup) * t_probe))
-    sample = spec["cpu_sample"](frac)
+    # A fixed, stated sample per config (the same one the GPU arm's cpu_baseline times), so
+    # the ratio to the GPU arm does not depend on this host's speed.
+    sample = spec["cpu_sample"](args.ref_sample_frac if args.ref_sample_frac is not None else spec["sample_frac"])
     for _ in range(args.warmup):
         spec["cpu_step"](sample)
     times = []
@@ -897,23 +1019,23 @@ def run_reference(args, rank):
         "config": {"workload": spec["describe"], "sample": sample["desc"]},
         "cpu_baseline": {"value": round(value, 5), "unit": "GB/s", "cores": torch.get_num_threads(),
                          "kind": "port",
-                         "sample": f"{frac:.4g} of each pass's sequences ({sample['desc']}) per step"},
+                         "sample": f"fixed sample per step ({sample['desc']}), fwd+bwd float32"},
         "e2e": {"value": round(value, 5), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }), flush=True)
 
 
 # ----------------------------------------------------------------- generator workloads
-def run_generator(args, rank, local_rank, world):
+def measure_generator(args, rank, local_rank, world, device, steps, clocks=True):
     """SEMamba generator training step (forward + generator losses + backward + DDP
     gradient all-reduce + AdamW), bf16 autocast around fp32 scans, `--batch` two-second
-    utterances per GPU. Metric: frames/s over all GPUs."""
+    utterances per GPU, on an initialised process group when world > 1. Returns, on rank 0,
+    the measurement as a dict (frames/s over all GPUs, device time = max over ranks, an
+    end-to-end figure with the audio copied in from pinned host memory and the loss read
+    back every step); None on other ranks."""
     from semambaxlinoss_b200 import _lib
     from semambaxlinoss_b200.generator import SEMamba, config3_cfg, generator_loss, mag_phase_stft
 
-    device = torch.device("cuda", local_rank)
-    torch.cuda.set_device(device)
-    _init_dist(world, device)
     cfg = config3_cfg()
     sc, cf = cfg["stft_cfg"], cfg["model_cfg"]["compress_factor"]
     torch.manual_seed(1234)
@@ -950,19 +1072,19 @@ def run_generator(args, rank, local_rank, world):
     stream = torch.cuda.current_stream(device)
     for _ in range(max(args.warmup, 3)):
         step(clean_d, noisy_d)
-    clocks = ClockSampler(_device_uuid(device), args.clocks_log if rank == 0 else None)
+    sampler = ClockSampler(_device_uuid(device), args.clocks_log if rank == 0 else None) if clocks else None
     soak_t0 = time.time()
     _barrier(world, device)
     n0 = _lib.launch_count()
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s.record(stream)
-    for _ in range(args.steps):
+    for _ in range(steps):
         loss = step(clean_d, noisy_d)
     e.record(stream)
     _barrier(world, device)
     launches = _lib.launch_count() - n0
     t_end = time.time()
-    ms = _max_over_ranks(s.elapsed_time(e), world, device) / args.steps
+    ms = _max_over_ranks(s.elapsed_time(e), world, device) / steps
     # End to end: audio copied in from pinned host memory and the loss read back, every step.
     _barrier(world, device)
     s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -973,20 +1095,17 @@ def run_generator(args, rank, local_rank, world):
     e2.record(stream)
     _barrier(world, device)
     ms_e2e = _max_over_ranks(s2.elapsed_time(e2), world, device) / args.e2e_steps
-    clocks.stop()
-    if world > 1:
-        import torch.distributed as dist
-
-        dist.destroy_process_group()
+    if sampler is not None:
+        sampler.stop()
+    del model, opt
     if rank != 0:
-        return
-    fps = world * B * frames / (ms * 1e-3)
-    print(json.dumps({
+        return None
+    out = {
         "metric": "SEMamba generator training step, frames/s (2 s utterances, batch 16 per GPU)",
-        "value": round(fps, 1), "unit": "frames/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "bf16 autocast, fp32 scans",
-        "data": "synthetic (clean ~ N(0, 0.1), noise ~ N(0, 0.05), seeded per rank)",
+        "value": round(world * B * frames / (ms * 1e-3), 1), "unit": "frames/s", "n_gpus": world,
+        "steps": steps, "ms_per_step": round(ms, 3), "scaling": "weak",
+        "dtype": "bf16 autocast, fp32 scans",
+        "data": "synthetic (clean ~ N(0, 0.1), noise ~ N(0, 0.05), seeded per rank), random-init weights",
         "config": {"workload": "generator fwd + losses + bwd + AdamW, 4 TF-blocks (time: selective-LRU "
                                "d_inner 256 N 16; freq: damped-IMEX LinOSS P 16), hid 64",
                    "global_batch": world * B, "seq_len": frames, "parallelism": f"ddp{world}",
@@ -996,10 +1115,28 @@ def run_generator(args, rank, local_rank, world):
                 "ms_per_step": round(ms_e2e, 3), "h2d_bytes_per_step": 2 * B * seg * 4,
                 "d2h_bytes_per_step": 4},
         "gpu_launches": launches,
-        "gpu_launches_note": "libsemx kernels only (scans, their reductions); convolutions, GEMMs and "
-                             "the optimizer run as torch/cuDNN/cuBLAS kernels",
-        "clocks": clocks.summary(soak_t0, t_end),
-    }), flush=True)
+        "gpu_launches_note": "libsemx kernels only (scans, their reductions, mixer and norm kernels); "
+                             "convolutions, GEMMs and the optimizer run as torch/cuDNN/cuBLAS kernels",
+    }
+    if sampler is not None:
+        out["clocks"] = sampler.summary(soak_t0, t_end)
+    return out
+
+
+def run_generator(args, rank, local_rank, world):
+    """The generator training step as the bench line (`--workload generator`)."""
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    _init_dist(world, device)
+    out = measure_generator(args, rank, local_rank, world, device, args.steps)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    if out is None:
+        return
+    out.update(warmup=args.warmup, higher_is_better=True, vs_baseline=None)
+    print(json.dumps(out), flush=True)
 
 
 def run_inference(args, rank, local_rank, world):

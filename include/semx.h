@@ -18,9 +18,12 @@
  *   - Work runs on the GPU that owns the operands (found from the first operand pointer
  *     and made current for the call) and is enqueued on `stream`, a cudaStream_t of that
  *     GPU passed as an opaque pointer; nothing synchronises the host.
- *   - The library keeps no state between calls and allocates no device memory: scratch
- *     comes from the caller through `workspace`, sized by the matching
- *     *_workspace_bytes() query.
+ *   - The library allocates no device memory at run time: scratch comes from the caller
+ *     through `workspace`, sized by the matching *_workspace_bytes() query. The one
+ *     exception is semx_linoss_bwd_noalloc, which takes no workspace and instead uses an
+ *     8 MiB scratch pool compiled into the library (held by every GPU that loads it);
+ *     apart from that pool's per-device address, the library keeps no state between
+ *     calls.
  *   - The return value is SEMX_OK or one of the SEMX_ERR_* codes; no exception crosses
  *     the ABI. semx_last_error() returns a message for the calling host thread.
  *
@@ -148,10 +151,13 @@ int semx_linoss_bwd(const SemxLinossArgs* args, semx_stream_t stream);
  * A call whose semx_linoss_workspace_bytes() exceeds the pool returns SEMX_ERR_SHAPE
  * without launching. The caller still passes every input and output (ckpt included).
  * The first call on a device looks up the pool's device address (cudaGetSymbolAddress,
- * once per device); make that first call before any stream capture. Every call shares
- * the one pool and nothing in it needs to start at zero (each call overwrites what it
- * reads), but calls whose work overlaps on the GPU (different streams, or several host
- * threads) race on it: serialise them. */
+ * once per device) and keeps it for the life of the process; make that first call before
+ * any stream capture, and make no call after a cudaDeviceReset of that device in the same
+ * process (the reset re-loads the library's device code, and the kept address would no
+ * longer be the pool's). Every call shares the one pool and nothing in it needs to start
+ * at zero (each call overwrites what it reads, or clears it when L == 0), but calls whose
+ * work overlaps on the GPU (different streams, or several host threads) race on it:
+ * serialise them. */
 #define SEMX_LINOSS_NOALLOC_SCRATCH_BYTES ((size_t)8 << 20)
 int semx_linoss_bwd_noalloc(const SemxLinossArgs* args, semx_stream_t stream);
 

@@ -3,7 +3,8 @@
 Every ``csrc/*.cu`` file is compiled separately (in parallel) for
 ``-gencode arch=compute_100a,code=sm_100a`` and linked into one shared library next to
 this file, so the library travels with the source tree. Rebuilds only when a source or
-header is newer than the library. The CUDA runtime is linked statically; the driver is
+header is newer than the library, and recompiles only the sources whose object is older
+than the source or any header. The CUDA runtime is linked statically; the driver is
 resolved at first use, so the library also loads on machines without a GPU (for ABI
 checks).
 """
@@ -60,6 +61,10 @@ def up_to_date() -> bool:
 
 def _compile(src: Path, verbose_ptxas: bool) -> tuple[Path, str]:
     obj = BUILD_DIR / (src.stem + ".o")
+    if not verbose_ptxas and obj.exists():
+        obj_m = obj.stat().st_mtime
+        if all(p.stat().st_mtime <= obj_m for p in [src] + _headers()):
+            return obj, ""
     cmd = [_nvcc(), *ARCH_FLAGS, *COMMON_FLAGS, "-c", str(src), "-o", str(obj)]
     if verbose_ptxas:
         cmd += ["-Xptxas", "-v"]

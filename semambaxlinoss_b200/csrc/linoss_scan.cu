@@ -924,6 +924,14 @@ int noalloc_scratch(void** out) {
 
 extern "C" int semx_linoss_bwd_noalloc(const SemxLinossArgs* a, semx_stream_t stream) {
   SEMX_CHECK_ARGS(a, SemxLinossArgs);
+  // Bound S and P before the size query multiplies them, so that a huge S*P cannot wrap
+  // the byte count into something that fits the pool.
+  constexpr int64_t kPoolFloats = (int64_t)(SEMX_LINOSS_NOALLOC_SCRATCH_BYTES / sizeof(float));
+  SEMX_REQUIRE(a->S >= 0 && a->P >= 0 && (a->P == 0 || a->S <= kPoolFloats / (kPartials * a->P)),
+               SEMX_ERR_SHAPE,
+               "linoss noalloc: S=%lld, P=%lld need more scratch than the built-in pool holds (%zu B; "
+               "use semx_linoss_bwd with a workspace instead)",
+               (long long)a->S, (long long)a->P, (size_t)SEMX_LINOSS_NOALLOC_SCRATCH_BYTES);
   const size_t need = semx_linoss_workspace_bytes(a);
   SEMX_REQUIRE(need <= SEMX_LINOSS_NOALLOC_SCRATCH_BYTES, SEMX_ERR_SHAPE,
                "linoss noalloc: S=%lld, P=%lld need %zu B of scratch; the built-in pool holds %zu B "

@@ -1,7 +1,7 @@
 """Generates the golden fixtures in this folder by running the reference implementation.
 
-Runs on a machine that has the reference checkout (default /root/reference, override
-with SEMX_REFERENCE). Nothing else reads the reference: the committed ``*.pt`` fixtures
+Runs on a machine that has the reference checkout: set SEMX_REFERENCE to its root
+directory (the script refuses to run without it). Nothing else reads the reference: the committed ``*.pt`` fixtures
 carry seeded inputs, parameters and the reference's float64 outputs and gradients, and
 ``tests/test_oracle_golden.py`` checks the oracle restatement against them.
 
@@ -11,7 +11,7 @@ What runs (all on CPU, float64, through the reference's own modules and function
   SelectiveLRUMIMO (every gain / option, rank > 0) and _selective_recurrence
 * models/mixer.py                  MambaStyleMixer around SelectiveLRU and LinOSS
 
-Usage: python tests/golden/make_golden.py
+Usage: SEMX_REFERENCE=<reference checkout> python tests/golden/make_golden.py
 """
 from __future__ import annotations
 
@@ -23,10 +23,12 @@ from pathlib import Path
 import torch
 
 OUT = Path(__file__).resolve().parent
-REF = Path(os.environ.get("SEMX_REFERENCE", "/root/reference"))
+REF = Path(os.environ["SEMX_REFERENCE"]) if "SEMX_REFERENCE" in os.environ else None
 
 
 def _import_reference():
+    if REF is None or not (REF / "models").is_dir():
+        raise SystemExit("set SEMX_REFERENCE to the root of the reference checkout")
     sys.path.insert(0, str(REF))
     from models.selective_lru.selective_lru import (  # noqa: E402
         SelectiveLRU,

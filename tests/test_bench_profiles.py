@@ -39,7 +39,8 @@ def bench():
 
 @pytest.mark.parametrize("kernel,workload,bytes_per_unit", CASES)
 def test_profiled_traffic_resolves(bench, kernel, workload, bytes_per_unit):
-    traffic = bench.profiled_traffic(kernel, workload, UNITS)
+    traffic, source = bench.profiled_traffic(kernel, workload, UNITS)
+    assert source and source.startswith("profiles/")
     assert traffic is not None, f"no traffic_bytes_per_launch entry for {kernel} / {workload}"
     ratio = traffic / (bytes_per_unit * UNITS)
     assert 0.5 < ratio < 2.0, f"{kernel} / {workload}: traffic {ratio:.2f}x algorithmic"

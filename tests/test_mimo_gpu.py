@@ -199,43 +199,42 @@ def test_fused_layer_matches_oracle(case):
         assert_close(out[k], ref[k], floor_tol(rel_err(r32[k], ref[k])), k)
 
 
-def test_fused_layer_bf16_inputs():
-    """bf16 input on the 8-head x 32, state 128, rank 4 layer with the workload's
-    distributions (x, b_t, c_t, B, C, D ~ N(0, 1/4), delta_nu = softplus(N(-2, 0.5))): the
-    projections and the kernel's operand reads are bf16, state and accumulation fp32.
-    Checked against the float64 oracle given the same bf16 projection rows (the layer's
-    default omega, up to pi / dt_min, makes the pole phase far more sensitive to a rounding
-    of delta_nu than the 2e-2 bound, so the oracle must see the same rounded rows): output,
-    input gradient and every parameter gradient within the bf16-input tolerance."""
-    import torch.nn.functional as F
-
+def _bf16_workload_layer(seed, omega_std=None):
+    """The 8-head x 32, state 128, rank 4 layer with the MIMO workload's distributions
+    (projection weights N(0, 1/256) held at bf16 values, so that x ~ N(0, 1/4) gives
+    b_t, c_t ~ N(0, 1/4); dt_nu bias -2; B, C, D ~ N(0, 1/4)). ``omega_std`` replaces the
+    default omega (up to pi / dt_min) by N(0, omega_std^2)."""
     from semambaxlinoss_b200.selective_lru import SelectiveLRUMIMO
 
     cfg = dict(in_features=256, state_dim=128, n_heads=8, rank=4, input_gain="gamma")
-    torch.manual_seed(11)
+    torch.manual_seed(seed)
     m = SelectiveLRUMIMO(**cfg)
-    g = gen(12)
+    g = gen(seed + 1)
     with torch.no_grad():
         for lin in (m.dt_nu_proj, m.dt_theta_proj, m.b_dir, m.c_read, m.b_coef, m.c_coef):
             lin.weight.copy_((torch.randn(lin.weight.shape, generator=g) / 16.0).bfloat16().float())
         m.dt_nu_proj.bias.fill_(-2.0)
         for p_ in (m.B, m.C, m.D):
             p_.copy_(torch.randn(p_.shape, generator=g) * 0.5)
-    x = randn((2, 45, 256), g, scale=0.5).to(torch.bfloat16)
-    gy = randn((2, 45, 256), g)
-    out = _layer_gpu(m, x, gy, torch.bfloat16)
-    # Oracle on the same bf16 projection rows.
-    dev = cuda()
-    with torch.no_grad():
-        W, b = m._projection()
-        proj = F.linear(x.to(dev), W.to(torch.bfloat16)).double().cpu()
-        proj[..., :2 * 8] += b.double().cpu()  # the layer adds the dt biases in fp32
+        if omega_std is not None:
+            m.omega.copy_(torch.randn(m.omega.shape, generator=g) * omega_std)
+    return m, cfg
+
+
+def _bf16_layer_reference(m, cfg, x, gy, proj):
+    """Float64 oracle of the bf16 layer given its projection rows ``proj`` (float64,
+    without the dt biases; the layer adds those in fp32): output, input gradient and
+    every parameter gradient, the projection weights' through the projection rows."""
     names = [n for n, _ in m.named_parameters()]
+    W, b = m._projection()
+    proj = proj.clone()
+    H, r, Nh, Fd = cfg["n_heads"], cfg["rank"], cfg["state_dim"] // cfg["n_heads"], cfg["in_features"]
+    proj[..., :2 * H] += b.detach().double().cpu()
     params = {k: v.detach().double().cpu().clone().requires_grad_(True) for k, v in m.state_dict().items()}
-    x64 = x.double().clone().requires_grad_(True)
-    proj64 = proj.clone().requires_grad_(True)
+    x64 = x.double().cpu().clone().requires_grad_(True)
+    proj64 = proj.requires_grad_(True)
     y = oslru.selective_lru_mimo_from_projection(proj64, params, x64, dict(cfg, rate_scale=m.rate_scale))
-    grads = torch.autograd.grad((y * gy.double()).sum(), [x64, proj64] + [params[n] for n in names],
+    grads = torch.autograd.grad((y * gy.double().cpu()).sum(), [x64, proj64] + [params[n] for n in names],
                                 allow_unused=True)
     dproj = grads[1]
     W64 = W.detach().double().cpu()
@@ -243,8 +242,7 @@ def test_fused_layer_bf16_inputs():
     for n, g_ in zip(names, grads[2:]):
         ref["d" + n] = torch.zeros_like(params[n]) if g_ is None else g_
     # Projection weights / biases get their gradient through the projection rows.
-    dW = dproj.reshape(-1, dproj.shape[-1]).t() @ x64.detach().reshape(-1, 256)
-    H, r, Nh = 8, 4, 16
+    dW = dproj.reshape(-1, dproj.shape[-1]).t() @ x64.detach().reshape(-1, Fd)
     blocks = [("dt_nu_proj", H), ("dt_theta_proj", H), ("b_coef", H * r), ("b_dir", H * r * Nh),
               ("c_coef", H * r), ("c_read", 2 * H * r * Nh)]
     o = 0
@@ -254,11 +252,70 @@ def test_fused_layer_bf16_inputs():
             ref[f"d{name}.bias"] = dproj[..., o:o + rows].sum((0, 1))
         o += rows
     # The static input map B is the block-diagonal drive block of the projection weight.
-    Fh = 256 // H
+    Fh = Fd // H
     ref["dB"] = torch.stack([dW[o + h * 2 * Nh:o + (h + 1) * 2 * Nh, h * Fh:(h + 1) * Fh]
                              .reshape(Nh, 2, Fh).permute(0, 2, 1) for h in range(H)])
+    return ref
+
+
+def test_fused_layer_bf16_inputs():
+    """bf16 input on the 8-head x 32, state 128, rank 4 layer with the workload's
+    distributions and the layer's default omega: the projections and the kernel's operand
+    reads are bf16, state and accumulation fp32. Checked against the float64 oracle given
+    the same bf16 projection rows the GPU produced (the default omega, up to pi / dt_min,
+    makes the pole phase far more sensitive to a one-ulp difference in the bf16 rounding
+    of delta_nu than the 2e-2 bound, so this case isolates the layer kernels): output,
+    input gradient and every parameter gradient within the bf16-input tolerance.
+    test_bf16_layer_full_size_slices covers the projection GEMM with independently
+    computed rows."""
+    import torch.nn.functional as F
+
+    m, cfg = _bf16_workload_layer(11)
+    g = gen(12)
+    x = randn((2, 45, 256), g, scale=0.5).to(torch.bfloat16)
+    gy = randn((2, 45, 256), g)
+    out = _layer_gpu(m, x, gy, torch.bfloat16)
+    dev = cuda()
+    with torch.no_grad():
+        W, _ = m._projection()
+        proj = F.linear(x.to(dev), W.to(torch.bfloat16)).double().cpu()
+    ref = _bf16_layer_reference(m, cfg, x, gy, proj)
     for k in ref:
         assert_close(out[k], ref[k], BF16_TOL, k)
+
+
+@pytest.mark.parametrize("S,L", [(404, 321), (1284, 101)])
+def test_bf16_layer_full_size_slices(S, L):
+    """The MIMO workload layer (256 features = 8 heads x 32, state 128, rank 4, bf16 input,
+    fp32 state) at its full pass shapes, time 404 x 321 and frequency 1284 x 101. The
+    upstream gradient is zero outside four sequences (first, two inner, last), so every
+    gradient, the parameter sums included, comes from those sequences alone and can be
+    checked against the float64 oracle run on them; the oracle's projection rows are
+    computed on the CPU from the same bf16 x and bf16 weights and rounded to bf16, as the
+    layer's bf16 GEMM rounds its output. Omega is drawn N(0, 3^2): the layer's default
+    (up to pi / dt_min) makes a one-ulp difference in the bf16 rounding of delta_nu (the
+    GPU GEMM accumulates in a different order) turn the pole phase by radians, in the
+    reference under bf16 autocast as much as here."""
+    m, cfg = _bf16_workload_layer(21, omega_std=3.0)
+    dev = cuda()
+    gd = torch.Generator(device=dev).manual_seed(S)
+    x = (torch.randn(S, L, 256, generator=gd, device=dev) * 0.5).to(torch.bfloat16)
+    sl = [0, S // 3, (2 * S) // 3 + 1, S - 1]
+    mask = torch.zeros(S, 1, 1, device=dev)
+    mask[sl] = 1.0
+    gy = torch.randn(S, L, 256, generator=gd, device=dev) * mask
+    out = _layer_gpu(m, x, gy, torch.bfloat16)
+    # Sequences outside the slice got a zero upstream gradient: their input gradient is zero.
+    rest = torch.ones(S, dtype=torch.bool)
+    rest[sl] = False
+    assert out["dx"][rest.to(dev)].abs().max().item() == 0.0
+    xs = x[sl].cpu()
+    W, _ = m._projection()
+    proj = (xs.double() @ W.detach().to(torch.bfloat16).double().cpu().t()).to(torch.bfloat16).double()
+    ref = _bf16_layer_reference(m, cfg, xs, gy[sl].cpu(), proj)
+    for k in ref:
+        got = out[k][sl] if k in ("y", "dx") else out[k]
+        assert_close(got, ref[k], BF16_TOL, k)
 
 
 def test_fused_layer_deterministic():

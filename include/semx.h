@@ -67,6 +67,10 @@ const char* semx_last_error(void);
  * threads and devices together (a monotonically increasing counter). No counterpart in
  * the reference; it lets a caller count the device launches of a region of its own. */
 uint64_t semx_launch_count(void);
+/* Number of tensor-core completion waits, on the current GPU, that ran out of time in this
+ * process (the kernel then stops and leaves the rest of its outputs unwritten); 0 in a
+ * healthy run. Synchronises with that GPU. No counterpart in the reference. */
+int semx_tc_timeouts(uint32_t* count);
 
 /* ------------------------------------------------------------------------------------
  * LinOSS oscillatory scan.

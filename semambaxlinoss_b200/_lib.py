@@ -204,6 +204,7 @@ _SIGNATURES = {
     "semx_status_string": (ctypes.c_char_p, [ctypes.c_int]),
     "semx_last_error": (ctypes.c_char_p, []),
     "semx_launch_count": (ctypes.c_uint64, []),
+    "semx_tc_timeouts": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint32)]),
     "semx_linoss_args_size": (ctypes.c_size_t, []),
     "semx_linoss_ckpt_bytes": (
         ctypes.c_size_t,
@@ -327,3 +328,13 @@ def new_args(cls):
 def launch_count() -> int:
     """Kernels the library has launched in this process so far (all threads, devices)."""
     return int(load().semx_launch_count())
+
+
+def tc_timeouts(device=None) -> int:
+    """Tensor-core completion waits that ran out of time on `device` (default: current) in
+    this process; 0 in a healthy run."""
+    if device is not None:
+        torch.cuda.set_device(device)
+    n = ctypes.c_uint32(0)
+    check("semx_tc_timeouts", load().semx_tc_timeouts(ctypes.byref(n)))
+    return int(n.value)

@@ -33,6 +33,7 @@
 #include "semx_common.cuh"
 #include "semx_math.cuh"
 #include "semx_reduce.cuh"
+#include "semx_tc.cuh"
 
 namespace {
 
@@ -447,9 +448,20 @@ __device__ __forceinline__ float2 cmul(float2 a, float2 b) {
 // Rows of lam / bu / hs are hw float2 apart. Lanes are segment-major inside a warp
 // (lane = seg * (32 / SEG) + mode), so the shuffles step by 32 / SEG lanes and the
 // shared-memory rows touched by one instruction fall in distinct banks.
+// chunk_scan_to: the same scan with each state h_t of mode n handed to store(t, n, h_t).
+template <int SEG, int CT, typename Store>
+__device__ __forceinline__ void chunk_scan_to(const float2* lam, const float2* bu, float2* cin, int Nh, int hw,
+                                              int nt, Store store);
+
 template <int SEG, int CT = kTC>
 __device__ __forceinline__ void chunk_scan(const float2* lam, const float2* bu, float2* hs, float2* cin,
                                            int Nh, int hw, int nt) {
+  chunk_scan_to<SEG, CT>(lam, bu, cin, Nh, hw, nt, [&](int t, int n, float2 v) { hs[t * hw + n] = v; });
+}
+
+template <int SEG, int CT, typename Store>
+__device__ __forceinline__ void chunk_scan_to(const float2* lam, const float2* bu, float2* cin, int Nh, int hw,
+                                              int nt, Store store) {
   if (SEG == 1) {
     const int n = threadIdx.x;
     if (n < Nh) {
@@ -458,7 +470,7 @@ __device__ __forceinline__ void chunk_scan(const float2* lam, const float2* bu, 
         st = cmul(lam[t * hw + n], st);
         st.x += bu[t * hw + n].x;
         st.y += bu[t * hw + n].y;
-        hs[t * hw + n] = st;
+        store(t, n, st);
       }
       cin[n] = st;
     }
@@ -513,7 +525,7 @@ __device__ __forceinline__ void chunk_scan(const float2* lam, const float2* bu, 
       st = cmul(lam[t * hw + n], st);
       st.x += bu[t * hw + n].x;
       st.y += bu[t * hw + n].y;
-      hs[t * hw + n] = st;
+      store(t, n, st);
     }
   }
   __syncwarp();
@@ -694,6 +706,273 @@ __global__ void __launch_bounds__(kT) mimo_layer_fwd_kernel(const LParams p) {
     }
     if (k + 1 < nchunks) store_small<RK, CT>(p, sm + l.sml[b ^ 1], ntn, pre);
   }
+}
+
+// ------------------------------------------------- forward, tensor-core readout (bf16)
+// The forward of 16-mode, 32-channel heads with bf16 operands and no envelope readout,
+// with the readout Re(C h) on the tensor cores: the chunk scan writes each state straight
+// into a 64-token A tile [h_re (16) | h_im (16)] (fp32, 128-byte swizzled, K-major); once
+// four 16-token chunks are in, one thread issues four kind::tf32 MMAs (M 64, N 32, K 8
+// each) against the B tile [C_re | -C_im] of the head, accumulating in tensor memory. The
+// epilogue (D skip and rank feedthrough added, y stored) of a tile runs during the next
+// chunk, after its poles, so the MMA never stalls the CTA. tf32 operands (10-bit mantissa)
+// keep the readout well inside the bf16-input tolerance; the fp32 layer keeps the fp32
+// CUDA-core readout of mimo_layer_fwd_kernel.
+//
+// Shared memory (floats, from a 1024-byte aligned base): A tile, B tile, head parameters,
+// double-buffered unpadded staging of x / drive / b_t / c_t and of the small operands,
+// poles and gained drive of a chunk, rank reads of a tile, the mbarrier and the
+// tensor-memory address: 35.6 KB, 6 CTAs per SM.
+constexpr int kTcM = 64;                    // tokens per tensor-core tile (the MMA's M)
+constexpr uint32_t kTcWaitLimit = 1u << 22;  // mbarrier polls before a wait gives up
+__device__ unsigned int g_tc_timeouts;       // waits that gave up (semx_tc_timeouts)
+
+struct TcLay {
+  static constexpr int at = 0;                        // 64 x 32 fp32, swizzled
+  static constexpr int bt2 = at + kTcM * 32;          // 32 x 32 fp32, swizzled
+  static constexpr int Co = bt2 + 32 * 32;            // c_out (4 x 32)
+  static constexpr int Dp = Co + 4 * 32;              // D (32)
+  static constexpr int prm = Dp + 32;                 // a, omega, detune (3 x 16)
+  static constexpr int cin = prm + 48;                // chunk entry state (16 float2)
+  static constexpr int stg_floats = 16 * (32 + 32 + 64 + 128) / 2;  // bf16 x | drive | b_t | c_t
+  static constexpr int stg0 = cin + 32;
+  static constexpr int stg1 = stg0 + stg_floats;
+  static constexpr int sml_floats = 16 * (3 + 2 * 4);
+  static constexpr int sml0 = stg1 + stg_floats;
+  static constexpr int sml1 = sml0 + sml_floats;
+  static constexpr int hw = 17;                       // lam / bu rows (float2)
+  static constexpr int lam = sml1 + sml_floats;
+  static constexpr int bu = lam + 16 * hw * 2;
+  static constexpr int srk = bu + 16 * hw * 2;        // rank reads of the tile (64 x 4)
+  static constexpr int bar = srk + kTcM * 4;          // 8-byte mbarrier
+  static constexpr int tslot = bar + 2;               // tensor-memory address
+  static constexpr int total = tslot + 2;
+};
+static_assert(TcLay::bt2 % 256 == 0 && TcLay::bar % 2 == 0, "tile / mbarrier alignment");
+
+// Epilogue of the tile whose MMA was committed: lanes 0..15 of warp w <= last hold the rows
+// of its chunk w (tensor-memory lanes 32 w + i); y = acc + D x + sum_r rank read_r c_out_r.
+template <int RK>
+__device__ __forceinline__ void tc_epilogue(const LParams& p, const float* sm, uint32_t taddr, int64_t s,
+                                            int h, int tile_t0, int last, int L) {
+  const int tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
+  if (w > last) return;  // warp-uniform
+  const int64_t Fd = p.H * 32;
+  const int j = 16 * w + lane, tg = tile_t0 + j;
+  const bool live = lane < 16 && tg < L;
+  uint4 xu[4];
+  if (live) {
+    const uint4* xg = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(p.x) +
+                                                     (s * p.L + tg) * Fd + (int64_t)h * 32);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) xu[c] = __ldg(xg + c);
+  }
+  float acc[32];
+  semx::tc::tmem_ld32(taddr + ((uint32_t)(32 * w) << 16), acc);
+  if (!live) return;
+  const __nv_bfloat16* xr = reinterpret_cast<const __nv_bfloat16*>(xu);
+  float sv[RK > 0 ? RK : 1];
+#pragma unroll
+  for (int r = 0; r < RK; ++r) sv[r] = sm[TcLay::srk + j * 4 + r];
+  float* yr = p.y + (s * p.L + tg) * Fd + (int64_t)h * 32;
+#pragma unroll
+  for (int f4 = 0; f4 < 8; ++f4) {
+    const float4 xv = ld4(xr + 4 * f4);
+    const float xa[4] = {xv.x, xv.y, xv.z, xv.w};
+    float o[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int f = 4 * f4 + e;
+      o[e] = fmaf(sm[TcLay::Dp + f], xa[e], acc[f]);
+#pragma unroll
+      for (int r = 0; r < RK; ++r) o[e] = fmaf(sv[r], sm[TcLay::Co + r * 32 + f], o[e]);
+    }
+    *reinterpret_cast<float4*>(yr + 4 * f4) = make_float4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+template <int RK>
+__global__ void __launch_bounds__(kT, 6) mimo_layer_fwd_tc_kernel(const LParams p) {
+  using T = __nv_bfloat16;
+  constexpr int NH = 16, FH = 32, CT = 16, SEG = 8, R = RK, hw = TcLay::hw;
+  extern __shared__ __align__(1024) float4 smem4[];
+  float* sm = reinterpret_cast<float*>(smem4);
+  const int L = (int)p.L;
+  const int nchunks = (L + CT - 1) / CT;
+  const int64_t s = blockIdx.x / p.H;
+  const int h = (int)(blockIdx.x % p.H);
+  const int tid = threadIdx.x;
+  // The staging helpers read the row widths of an FLay: unpadded rows here.
+  FLay l = {};
+  l.tc = CT;
+  l.xw = FH;
+  l.bxw = 2 * NH;
+  l.btw = R * NH;
+  l.ctw = 2 * R * NH;
+  // The tiles' swizzle pattern assumes a 1024-byte aligned base (declared above); a
+  // misaligned base is counted like a timed-out wait and the CTA writes nothing.
+  if ((semx::tc::smem_addr(smem4) & 1023u) != 0) {
+    if (tid == 0) atomicAdd(&g_tc_timeouts, 1u);
+    return;
+  }
+  // Head parameters; B tile row f = [C_re[f, 0..15] | -C_im[f, 0..15]].
+  for (int i = tid; i < 32 * 8; i += kT) {
+    const int f2 = i >> 3, c = i & 7;
+    const float2* cr = reinterpret_cast<const float2*>(p.C) + ((int64_t)h * FH + f2) * NH + (c & 3) * 4;
+    const float2 c0 = cr[0], c1 = cr[1], c2 = cr[2], c3 = cr[3];
+    const float4 v = c < 4 ? make_float4(c0.x, c1.x, c2.x, c3.x) : make_float4(-c0.y, -c1.y, -c2.y, -c3.y);
+    *reinterpret_cast<float4*>(reinterpret_cast<char*>(sm + TcLay::bt2) + semx::tc::sw128(f2, c)) = v;
+  }
+  for (int i = tid; i < R * FH; i += kT) sm[TcLay::Co + i] = p.cout[(int64_t)h * R * FH + i];
+  for (int i = tid; i < FH; i += kT) sm[TcLay::Dp + i] = p.D[(int64_t)h * FH + i];
+  if (tid < NH) {
+    sm[TcLay::prm + tid] = expf(p.A_log[(int64_t)h * NH + tid]);
+    sm[TcLay::prm + NH + tid] = p.omega[(int64_t)h * NH + tid];
+    sm[TcLay::prm + 2 * NH + tid] = p.detune ? p.sdet[(int64_t)h * NH + tid] : 1.f;
+    reinterpret_cast<float2*>(sm + TcLay::cin)[tid] = make_float2(0.f, 0.f);
+  }
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + TcLay::bar);
+  if (tid < 32) semx::tc::tmem_alloc(reinterpret_cast<uint32_t*>(sm + TcLay::tslot), 32);
+  if (tid == 0) semx::tc::mbar_init(bar, 1);
+  semx::tc::fence_smem_to_async();
+  semx::tc::fence_before_sync();
+  __syncthreads();
+  semx::tc::fence_after_sync();
+  const uint32_t taddr = *reinterpret_cast<const uint32_t*>(sm + TcLay::tslot);
+
+  float2* lam = reinterpret_cast<float2*>(sm + TcLay::lam);
+  float2* bu = reinterpret_cast<float2*>(sm + TcLay::bu);
+  float2* cin = reinterpret_cast<float2*>(sm + TcLay::cin);
+  char* atile = reinterpret_cast<char*>(sm + TcLay::at);
+  const int stg[2] = {TcLay::stg0, TcLay::stg1}, sml_off[2] = {TcLay::sml0, TcLay::sml1};
+  const float2 bias = dt_bias(p, h);
+  float pre[kPre];
+  uint32_t phase = 0;
+  int pending = -1;     // chunk index of the last chunk of a committed, not yet read-out tile
+  bool bail = false;
+  if (nchunks > 0) {
+    const int nt0 = min(CT, L);
+    stage_bulk<true, NH, FH, RK>(p, l, sm + stg[0], s, h, 0, nt0);
+    load_small<true, RK>(p, s, h, 0, nt0, bias, pre);
+    store_small<RK, CT>(p, sm + sml_off[0], nt0, pre);
+  }
+  cp_async_commit();
+  for (int k = 0; k < nchunks; ++k) {
+    const int b = k & 1, q = k & 3;
+    const int t0 = k * CT, nt = min(CT, L - t0);
+    const int t0n = t0 + CT, ntn = min(CT, L - t0n);
+    cp_async_wait_all();
+    __syncthreads();
+    if (k + 1 < nchunks) {
+      stage_bulk<true, NH, FH, RK>(p, l, sm + stg[b ^ 1], s, h, t0n, ntn);
+      load_small<true, RK>(p, s, h, t0n, ntn, bias, pre);
+    }
+    cp_async_commit();
+    const T* xs = reinterpret_cast<const T*>(sm + stg[b]);
+    const T* bxs = xs + CT * l.xw;
+    const T* bts = bxs + CT * l.bxw;
+    const T* cts = bts + CT * l.btw;
+    const float* sml = sm + sml_off[b];
+    const float* dnus = sml + CT;
+    const float* dths = sml + 2 * CT;
+    const float* sbs = sml + 3 * CT;
+    const float* scs = sbs + CT * R;
+    // Poles and gained drive per (token, mode).
+    for (int i = tid; i < nt * NH; i += kT) {
+      const int t = i >> 4, n = i & 15;
+      const float2 bq = ld2(bxs + t * l.bxw + 2 * n);
+      float rr = bq.x;
+      const float bi = bq.y;
+#pragma unroll
+      for (int r = 0; r < R; ++r) rr = fmaf(sbs[t * R + r], static_cast<float>(bts[t * l.btw + r * NH + n]), rr);
+      const MDisc d = mdisc(p.gain, sm[TcLay::prm + n], sm[TcLay::prm + NH + n], sm[TcLay::prm + 2 * NH + n],
+                            p.detune != 0, dnus[t], dths[t]);
+      lam[t * hw + n] = make_float2(d.lre, d.lim);
+      bu[t * hw + n] = make_float2(d.gr * rr - d.gi * bi, d.gr * bi + d.gi * rr);
+    }
+    if (p.ckpt != nullptr && tid < NH)
+      reinterpret_cast<float2*>(p.ckpt)[((s * p.nck + k) * p.H + h) * NH + tid] = cin[tid];
+    __syncthreads();
+    if (q == 0 && pending >= 0) {
+      // The previous tile: its MMA was committed a whole chunk ago; read it out before
+      // this chunk's states overwrite the A rows 0..15 and its rank reads.
+      const bool ok = semx::tc::mbar_wait(bar, phase, kTcWaitLimit);
+      phase ^= 1u;
+      if (__syncthreads_or(!ok)) {
+        if (tid == 0) atomicAdd(&g_tc_timeouts, 1u);
+        bail = true;
+        break;
+      }
+      semx::tc::fence_after_sync();
+      tc_epilogue<RK>(p, sm, taddr, s, h, (pending - 3) * CT, 3, L);
+      semx::tc::fence_before_sync();
+      pending = -1;
+    }
+    // The chunk's states, straight into A rows 16 q + t.
+    const int row0 = 16 * q;
+    chunk_scan_to<SEG, CT>(lam, bu, cin, NH, hw, nt, [&](int t, int n, float2 v) {
+      const int row = row0 + t;
+      char* base = atile + row * 128 + 4 * (n & 3);
+      *reinterpret_cast<float*>(base + (((n >> 2) ^ (row & 7)) << 4)) = v.x;
+      *reinterpret_cast<float*>(base + ((((n >> 2) + 4) ^ (row & 7)) << 4)) = v.y;
+    });
+    __syncthreads();
+    // Rank reads s_c Re(<c_t, h_t>) per (token, rank), from the A rows.
+    if (R > 0 && tid < nt * R) {
+      const int t = tid / (R > 0 ? R : 1), r = tid % (R > 0 ? R : 1);
+      const int row = row0 + t;
+      const T* cr = cts + t * l.ctw + r * 2 * NH;
+      float acc = 0.f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const float4 hre = *reinterpret_cast<const float4*>(atile + semx::tc::sw128(row, c));
+        const float4 him = *reinterpret_cast<const float4*>(atile + semx::tc::sw128(row, c + 4));
+        const float4 cre = ld4(cr + 4 * c), cim = ld4(cr + NH + 4 * c);
+        acc = fmaf(cre.x, hre.x, fmaf(-cim.x, him.x, acc));
+        acc = fmaf(cre.y, hre.y, fmaf(-cim.y, him.y, acc));
+        acc = fmaf(cre.z, hre.z, fmaf(-cim.z, him.z, acc));
+        acc = fmaf(cre.w, hre.w, fmaf(-cim.w, him.w, acc));
+      }
+      sm[TcLay::srk + row * 4 + r] = scs[tid] * acc;
+    }
+    if (q == 3 || k == nchunks - 1) {
+      // The tile is complete: one thread issues its MMAs (the accumulator is free: the
+      // previous tile was read out before this tile's first chunk).
+      semx::tc::fence_smem_to_async();
+      semx::tc::fence_before_sync();
+      __syncthreads();
+      semx::tc::fence_after_sync();
+      if (tid == 0) {
+        constexpr uint32_t idesc = semx::tc::idesc_tf32(kTcM, 32);
+        const uint32_t a0 = semx::tc::smem_addr(atile), b0 = semx::tc::smem_addr(sm + TcLay::bt2);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          semx::tc::mma_tf32(taddr, semx::tc::desc_sw128_kmajor(a0 + 32 * kk),
+                             semx::tc::desc_sw128_kmajor(b0 + 32 * kk), idesc, kk > 0);
+        semx::tc::mma_commit(bar);
+      }
+      pending = k;
+    }
+    if (k + 1 < nchunks) store_small<RK, CT>(p, sm + sml_off[b ^ 1], ntn, pre);
+  }
+  if (!bail && pending >= 0) {  // the last tile (possibly partial)
+    const bool ok = semx::tc::mbar_wait(bar, phase, kTcWaitLimit);
+    phase ^= 1u;
+    if (__syncthreads_or(!ok)) {
+      if (tid == 0) atomicAdd(&g_tc_timeouts, 1u);
+      bail = true;
+    } else {
+      semx::tc::fence_after_sync();
+      tc_epilogue<RK>(p, sm, taddr, s, h, (pending & ~3) * CT, pending & 3, L);
+    }
+  }
+  cp_async_wait_all();
+  // After a give-up, one more bounded wait for the outstanding MMA before its tensor
+  // memory is released.
+  if (bail) semx::tc::mbar_wait(bar, phase ^ 1u, kTcWaitLimit);
+  semx::tc::fence_before_sync();
+  __syncthreads();
+  if (tid < 32) semx::tc::tmem_dealloc(taddr, 32);
 }
 
 // ---------------------------------------------------------------------------- backward
@@ -1472,8 +1751,15 @@ bool bwd16(const SemxMimoLayerArgs* a) { return a->Nh == 16 && a->Fh == 32 && (a
 // The forward of 16-mode, 32-channel heads (rank 0 or 4) runs 16-token chunks.
 int fwd_chunk(const SemxMimoLayerArgs* a) { return bwd16(a) ? kCk : kTC; }
 
+// The bf16 forward of those heads without the envelope readout reads out on the tensor
+// cores (mimo_layer_fwd_tc_kernel: 16-byte aligned x and y rows).
+bool fwd_tc(const SemxMimoLayerArgs* a) {
+  return bwd16(a) && a->bf16 && !a->envelope && semx::aligned(a->y, 16) && semx::aligned(a->x, 16);
+}
+
 size_t layer_smem(const SemxMimoLayerArgs* a, bool bwd) {
   if (bwd && bwd16(a)) return (size_t)make_blay(a->rank, a->envelope != 0, a->bf16 ? 2 : 4).total * sizeof(float);
+  if (!bwd && fwd_tc(a)) return (size_t)TcLay::total * sizeof(float);
   if (!bwd)
     return (size_t)make_flay((int)a->Nh, (int)a->Fh, a->rank, a->envelope != 0, a->bf16 ? 2 : 4, fwd_chunk(a))
                .total * sizeof(float);
@@ -1564,6 +1850,15 @@ int launch_layer(K kern, const LParams& p, size_t smem, cudaStream_t st, const c
 
 extern "C" {
 
+int semx_tc_timeouts(uint32_t* count) {
+  SEMX_REQUIRE(count != nullptr, SEMX_ERR_NULL, "semx_tc_timeouts: count is NULL");
+  unsigned int v = 0;
+  const cudaError_t e = cudaMemcpyFromSymbol(&v, g_tc_timeouts, sizeof(v));
+  if (e != cudaSuccess) return semx::fail(SEMX_ERR_LAUNCH, "semx_tc_timeouts: %s", cudaGetErrorString(e));
+  *count = v;
+  return SEMX_OK;
+}
+
 size_t semx_mimo_layer_args_size(void) { return sizeof(SemxMimoLayerArgs); }
 
 size_t semx_mimo_layer_ckpt_bytes(const SemxMimoLayerArgs* a) {
@@ -1588,6 +1883,11 @@ int semx_mimo_layer_fwd(const SemxMimoLayerArgs* a, semx_stream_t stream) {
   const size_t smem = layer_smem(a, false);
   cudaStream_t st = semx::as_stream(stream);
   const int seg = scan_segments(a->Nh);
+  if (fwd_tc(a)) {
+    static_assert(kCk == 16, "the tensor-core forward writes one checkpoint per 16-token chunk");
+    return a->rank == 4 ? launch_layer(mimo_layer_fwd_tc_kernel<4>, p, smem, st, "mimo_layer_fwd_tc_kernel")
+                        : launch_layer(mimo_layer_fwd_tc_kernel<0>, p, smem, st, "mimo_layer_fwd_tc_kernel");
+  }
   if (bwd16(a)) {
     // The 16-mode, 32-channel heads, specialised at compile time, 16-token chunks.
     static_assert(kCk % 8 == 0, "16-token chunks hold whole 8-segment scans");

@@ -12,6 +12,7 @@ import pytest
 import torch
 
 from oracle import selective_lru as oslru
+from semambaxlinoss_b200 import _lib
 from tests.parity import BF16_TOL, FP32_TOL, assert_close, crandn, cuda, floor_tol, gen, randn, rel_err, to32
 
 pytestmark = pytest.mark.gpu
@@ -282,6 +283,7 @@ def test_fused_layer_bf16_inputs():
     ref = _bf16_layer_reference(m, cfg, x, gy, proj)
     for k in ref:
         assert_close(out[k], ref[k], BF16_TOL, k)
+    assert _lib.tc_timeouts() == 0
 
 
 @pytest.mark.parametrize("S,L", [(404, 321), (1284, 101)])
@@ -316,6 +318,7 @@ def test_bf16_layer_full_size_slices(S, L):
     for k in ref:
         got = out[k][sl] if k in ("y", "dx") else out[k]
         assert_close(got, ref[k], BF16_TOL, k)
+    assert _lib.tc_timeouts() == 0
 
 
 def test_fused_layer_deterministic():

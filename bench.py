@@ -70,10 +70,13 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=None, help="timed steps (default per workload)")
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["semx", "reference"], default="semx")
-    ap.add_argument("--workload", choices=["scans", "linoss", "slru", "mimo", "generator", "inference"],
+    ap.add_argument("--workload", choices=["scans", "linoss", "slru", "mimo", "ops", "generator", "inference"],
                     default="scans")
     ap.add_argument("--batch", type=int, default=16, help="generator: utterances per GPU")
-    ap.add_argument("--micro-batch", type=int, default=4, help="inference: utterances per forward")
+    ap.add_argument("--micro-batch", type=int, default=8, help="inference: utterances per forward")
+    ap.add_argument("--stream-chunk", type=int, default=0,
+                    help="inference: time-scan pieces of this many frames carrying the scan state "
+                         "(SelectiveLRU.stream_chunk; 0 = one piece)")
     ap.add_argument("--chunk", type=int, default=None, help="checkpoint interval of the scan")
     ap.add_argument("--slru-complex", action="store_true",
                     help="slru: the complex scan with the gamma gain (the generator's time scans)")
@@ -86,6 +89,8 @@ def parse_args():
     ap.add_argument("--no-generator", action="store_true",
                     help="scans: skip the generator training-step sub-measurement")
     ap.add_argument("--gen-steps", type=int, default=10, help="timed generator steps (scans workload)")
+    ap.add_argument("--no-inference", action="store_true",
+                    help="scans: skip the long-utterance inference sub-measurement")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=10)
@@ -94,7 +99,7 @@ def parse_args():
                     help="skip the 1.5 s busy period before timing (for profiler runs)")
     args = ap.parse_args()
     if args.steps is None:
-        args.steps = {"scans": 20, "linoss": 200, "slru": 20, "mimo": 20, "generator": 10,
+        args.steps = {"scans": 20, "linoss": 200, "slru": 20, "mimo": 20, "ops": 20, "generator": 10,
                       "inference": 1}[args.workload]
     return args
 
@@ -334,6 +339,8 @@ class SlruPass:
         C, N = SLRU_C, SLRU_N
         self.lib, self._lib = _lib.load(), _lib
         self.complex_ = complex_
+        # The real forward with N <= 16 modes runs slru_fwd_real16_kernel.
+        self.kernels = ("slru_fwd_kernel" if complex_ else "slru_fwd_real16_kernel", "slru_bwd_kernel")
         if complex_:  # x, dt, dth, B, C (re, im) in, y out / + dy in, 3 channel + 4 mode grads out
             self.fwd_bytes_per_unit = 4 * (4 * C + 4 * N)
             self.bwd_bytes_per_unit = 4 * (7 * C + 8 * N)
@@ -566,6 +573,117 @@ def _mimo_cpu_step(sample):
         (y * gy).sum().backward()
 
 
+# ------------------------------------------------------------- operator-level workloads
+OPS_S, OPS_L, OPS_H, OPS_NH, OPS_FH = 404, 321, 8, 16, 32
+
+
+class CscanPass:
+    """The plain complex diagonal scan (selective_scan_triton_real's replacement) over the
+    MIMO workload's state, 404 sequences x 321 steps x 128 modes, fwd + bwd with an
+    upstream gradient on h. Bytes per (sequence, step): fwd lam, Bu in + h out (complex
+    fp32) = 24 N; bwd lam, h, dh in + dlam, dBu out = 40 N."""
+
+    kernels = ("cscan_fwd_kernel", "cscan_bwd_kernel")
+
+    def __init__(self, S, L, seed, device):
+        N = OPS_H * OPS_NH
+        g = torch.Generator(device=device).manual_seed(seed)
+        mag = torch.rand(S, L, N, generator=g, device=device) * 0.98
+        ph = torch.randn(S, L, N, generator=g, device=device)
+        self.ins = [(mag * torch.cos(ph)).contiguous(), (mag * torch.sin(ph)).contiguous(),
+                    torch.randn(S, L, N, generator=g, device=device),
+                    torch.randn(S, L, N, generator=g, device=device)]
+        self.gh = [torch.randn(S, L, N, generator=g, device=device) for _ in range(2)]
+        self.fwd_bytes_per_unit = 24 * N
+        self.bwd_bytes_per_unit = 40 * N
+        self.units, self.S, self.L = S * L, S, L
+        self.inputs = self.ins + self.gh
+        self.outputs = []
+
+    def fwd(self, sh):
+        from semambaxlinoss_b200.selective_lru import selective_scan_triton_real
+
+        self.leaf = [t.detach().requires_grad_(True) for t in self.ins]
+        self.h = selective_scan_triton_real(*self.leaf)
+
+    def bwd(self, sh):
+        torch.autograd.backward(self.h, self.gh)
+        self.outputs = [self.h[0].detach(), self.h[1].detach()] + [t.grad for t in self.leaf]
+
+
+class MimoOpPass:
+    """The fused MIMO scan + block-diagonal readout operator (fused_selective_lru_mimo's
+    replacement) on given poles and drive, 8 heads x 16 modes, 32 channels per head,
+    404 sequences x 321 steps, fwd + bwd with upstream gradients on y and h. Bytes per
+    (sequence, step): fwd lam, Bu (complex fp32), x in + y, h out = 24 N + 8 Fd; bwd lam,
+    h, dh, dy, x in + dlam, dBu, dx out = 40 N + 12 Fd."""
+
+    kernels = ("mimo_fwd_kernel", "mimo_bwd_kernel")
+
+    def __init__(self, S, L, seed, device):
+        H, Nh, Fh = OPS_H, OPS_NH, OPS_FH
+        N, Fd = H * Nh, H * Fh
+        g = torch.Generator(device=device).manual_seed(seed)
+        mag = torch.rand(S, L, N, generator=g, device=device) * 0.98
+        ph = torch.randn(S, L, N, generator=g, device=device)
+        self.ins = [(mag * torch.cos(ph)).contiguous(), (mag * torch.sin(ph)).contiguous(),
+                    torch.randn(S, L, N, generator=g, device=device),
+                    torch.randn(S, L, N, generator=g, device=device),
+                    torch.randn(H, Fh, Nh, generator=g, device=device) * 0.3,
+                    torch.randn(H, Fh, Nh, generator=g, device=device) * 0.3,
+                    torch.randn(S, L, Fd, generator=g, device=device),
+                    torch.randn(Fd, generator=g, device=device)]
+        self.gy = torch.randn(S, L, Fd, generator=g, device=device)
+        self.gh = [torch.randn(S, L, N, generator=g, device=device) for _ in range(2)]
+        self.fwd_bytes_per_unit = 24 * N + 8 * Fd
+        self.bwd_bytes_per_unit = 40 * N + 12 * Fd
+        self.units, self.S, self.L = S * L, S, L
+        self.inputs = self.ins[:4] + self.ins[6:7] + [self.gy] + self.gh
+        self.outputs = []
+
+    def fwd(self, sh):
+        from semambaxlinoss_b200.selective_lru import fused_selective_lru_mimo
+
+        self.leaf = [t.detach().requires_grad_(True) for t in self.ins]
+        self.out = fused_selective_lru_mimo(*self.leaf, OPS_H, OPS_NH, OPS_FH)
+
+    def bwd(self, sh):
+        torch.autograd.backward(self.out, [self.gy] + self.gh)
+        self.outputs = [self.out[0].detach()] + [self.leaf[i].grad for i in (0, 1, 2, 3, 6)]
+
+
+def _ops_cpu_sample(frac, seed=0):
+    N, Fd = OPS_H * OPS_NH, OPS_H * OPS_FH
+    g = torch.Generator().manual_seed(seed)
+    s = max(1, int(round(OPS_S * frac)))
+    L = OPS_L
+    mag = torch.rand(s, L, N, generator=g) * 0.98
+    ph = torch.randn(s, L, N, generator=g)
+    t = {"lr": mag * torch.cos(ph), "li": mag * torch.sin(ph), "br": torch.randn(s, L, N, generator=g),
+         "bi": torch.randn(s, L, N, generator=g), "cr": torch.randn(OPS_H, OPS_FH, OPS_NH, generator=g) * 0.3,
+         "ci": torch.randn(OPS_H, OPS_FH, OPS_NH, generator=g) * 0.3, "x": torch.randn(s, L, Fd, generator=g),
+         "D": torch.randn(Fd, generator=g)}
+    gy = torch.randn(s, L, Fd, generator=g)
+    gh = (torch.randn(s, L, N, generator=g), torch.randn(s, L, N, generator=g))
+    return {"t": t, "gy": gy, "gh": gh, "desc": f"{s}x{L} (both operators)",
+            "bytes": s * L * ((24 + 40) * N + (24 * N + 8 * Fd) + (40 * N + 12 * Fd))}
+
+
+def _ops_cpu_step(sample):
+    """The reference's PyTorch equivalents (oracle port of the sequential complex scan and
+    the MIMO scan + readout, models/selective_lru/selective_lru.py:550-574, 590-599), fwd + bwd."""
+    from oracle import selective_lru as oslru
+
+    t = {k: v.clone().requires_grad_(True) for k, v in sample["t"].items()}
+    h = oslru.selective_recurrence(torch.complex(t["lr"], t["li"]), torch.complex(t["br"], t["bi"]))
+    gh = sample["gh"]
+    (h.real * gh[0] + h.imag * gh[1]).sum().backward()
+    t = {k: v.clone().requires_grad_(True) for k, v in sample["t"].items()}
+    y, hr, hi = oslru.mimo_scan_readout(t["lr"], t["li"], t["br"], t["bi"], t["cr"], t["ci"], t["x"], t["D"],
+                                        OPS_H, OPS_NH, OPS_FH)
+    ((y * sample["gy"]).sum() + (hr * gh[0] + hi * gh[1]).sum()).backward()
+
+
 # ------------------------------------------------------------------------ scan workloads
 WORKLOADS = {
     "linoss": {
@@ -602,6 +720,20 @@ WORKLOADS = {
         "l2": "no flush: the layer's activations per pass are GBs, far beyond the 126 MB L2",
         "cpu_sample": _mimo_cpu_sample, "cpu_step": _mimo_cpu_step,
     },
+}
+WORKLOADS["ops"] = {
+    "config": "ops",
+    "metric": "Selective-LRU MIMO operator + plain complex scan fwd+bwd, algorithmic HBM GB/s "
+              "(404x321, 8 heads x 16 modes, 32 channels per head)",
+    "describe": "fused_selective_lru_mimo (scan + block-diagonal readout + D skip on given poles and drive) "
+                "and selective_scan_triton_real (plain complex diagonal scan), 404 sequences x 321 steps, "
+                "128 modes, 256 channels",
+    "data": "synthetic, seeded: |lam| ~ U(0, 0.98), phase ~ N(0,1), Bu, x, D ~ N(0,1), C ~ N(0, 0.09)",
+    "dtype": "f32",
+    "chunk": 0, "sample_frac": 2.0 / 404,
+    "l2": "no flush: every (404, 321, 128) operand is 66 MB and (404, 321, 256) 133 MB; a step moves "
+          "6.7 GB, far beyond the 126 MB L2",
+    "cpu_sample": _ops_cpu_sample, "cpu_step": _ops_cpu_step,
 }
 # The default workload: configs 0, 1 and 2 in one step, in this order.
 SCAN_SET = ("slru", "linoss", "mimo")
@@ -666,6 +798,13 @@ def _make_passes(name, rank, device, chunk, args, world=1, sharded=False):
         return [p for sub in SCAN_SET for p in _make_passes(sub, rank, device, None, args, world, sharded)]
     chunk = chunk or WORKLOADS[name]["chunk"]
     size = (lambda S: _shard(S, rank, world)) if sharded else (lambda S: S)
+    if name == "ops":
+        ps = [MimoOpPass(size(OPS_S), OPS_L, seed=1000 * rank, device=device),
+              CscanPass(size(OPS_S), OPS_L, seed=1000 * rank + 1, device=device)]
+        ps[0].workload, ps[1].workload = "ops", "ops_cscan"
+        for p in ps:
+            p.chunk = chunk
+        return ps
     if name == "linoss":
         ps = [LinossPass(size(S), L, seed=1000 * rank + i, device=device, chunk=chunk)
               for i, (_, S, L) in enumerate(LIN_PASSES)]
@@ -719,6 +858,11 @@ def _per_pass_ms(passes, ev, steps):
             for i, p in enumerate(passes)]
 
 
+def _cfg_of(workload):
+    """The BASELINE config a pass group belongs to (its workload name where it has none)."""
+    return WORKLOADS[workload]["config"] if workload in WORKLOADS else workload
+
+
 def _traffic_tag(p):
     if p.workload == "slru":
         return "slru complex" if getattr(p, "complex_", False) else "slru real"
@@ -738,7 +882,7 @@ def _kernel_table(kpasses, peak):
             by = sum(p.units * (p.fwd_bytes_per_unit if d == 1 else p.bwd_bytes_per_unit) for p, _, _ in group)
             gbs = by / (ms * 1e-3) / 1e9
             traffic, source = profiled_traffic(kernel, _traffic_tag(p0), p0.units)
-            rows.append({"config": WORKLOADS[w]["config"], "workload": w, "dir": name, "kernel": kernel,
+            rows.append({"config": _cfg_of(w), "workload": w, "dir": name, "kernel": kernel,
                          "ms": round(ms, 4), "bytes": by, "achieved": round(gbs, 1),
                          "frac": round(gbs / peak, 4), "traffic": traffic, "traffic_source": source,
                          "algorithmic_bytes_first_launch": p0.units * (
@@ -819,9 +963,12 @@ def run_scan(args, rank, local_rank, world):
                    "note": "the named shapes split into contiguous per-rank sequence slices "
                            "[floor(r S / W), floor((r+1) S / W)); time = max over ranks"}
         del sp
-    gen = None
+    gen = inf = None
     if args.workload == "scans" and not args.no_generator:
         gen = measure_generator(args, rank, local_rank, world, device, args.gen_steps, clocks=False)
+        torch.cuda.empty_cache()
+    if args.workload == "scans" and not args.no_inference:
+        inf = measure_inference(args, rank, local_rank, world, device, 1, clocks=False)
     clocks.stop()
     _finish_dist(world)
     if rank != 0:
@@ -836,7 +983,7 @@ def run_scan(args, rank, local_rank, world):
         group = [(p, f, b) for p, f, b in per_pass if p.workload == w]
         by = sum(p.units * (p.fwd_bytes_per_unit + p.bwd_bytes_per_unit) for p, _, _ in group)
         ms = sum(f + b for _, f, b in group)
-        configs[WORKLOADS[w]["config"]] = {
+        configs[_cfg_of(w)] = {
             "workload": w, "fwd_ms": round(sum(f for _, f, _ in group), 4),
             "bwd_ms": round(sum(b for _, _, b in group), 4), "bytes": by,
             "GB/s": round(by / (ms * 1e-3) / 1e9, 1), "frac": round(by / (ms * 1e-3) / 1e9 / peak, 4),
@@ -891,6 +1038,8 @@ def run_scan(args, rank, local_rank, world):
         out["sharded"] = sharded
     if gen is not None:
         out["generator"] = gen
+    if inf is not None:
+        out["inference"] = inf
     if any(p.workload == "mimo" for p in passes):
         out["gpu_launches_note"] = ("libsemx kernels only; the MIMO layer's token projections (one GEMM "
                                     "forward, two backward) run as cuBLAS kernels")
@@ -1139,20 +1288,26 @@ def run_generator(args, rank, local_rank, world):
     print(json.dumps(out), flush=True)
 
 
-def run_inference(args, rank, local_rank, world):
+def measure_inference(args, rank, local_rank, world, device, steps, clocks=True):
     """64 sixty-second utterances (T = 9601 frames) enhanced end to end (STFT -> generator
-    -> iSTFT) under no_grad with bf16 autocast, sharded over the GPUs, `--micro-batch`
-    utterances per forward. Metric: frames/s over all GPUs."""
+    -> iSTFT) under no_grad with bf16 autocast, sharded over the GPUs (rank r takes
+    utterances r, r + W, ...), `--micro-batch` utterances per forward, the time scans
+    streamed in `--stream-chunk`-frame pieces. Every step copies its audio in from pinned
+    host memory and the enhanced audio out. Returns, on rank 0, the measurement (frames/s
+    over all GPUs, device time = max over ranks); None on other ranks."""
     from semambaxlinoss_b200 import _lib
     from semambaxlinoss_b200.generator import SEMamba, config3_cfg, mag_phase_istft, mag_phase_stft
 
-    device = torch.device("cuda", local_rank)
-    torch.cuda.set_device(device)
-    _init_dist(world, device)
     cfg = config3_cfg()
     sc, cf = cfg["stft_cfg"], cfg["model_cfg"]["compress_factor"]
     torch.manual_seed(1234)
     model = SEMamba(cfg).to(device).eval()
+    if args.stream_chunk > 0:
+        from semambaxlinoss_b200.selective_lru import SelectiveLRU
+
+        for m in model.modules():
+            if isinstance(m, SelectiveLRU):
+                m.stream_chunk = args.stream_chunk
     total, seg = 64, 960000
     per_rank = [len(range(r, total, world)) for r in range(world)][rank]
     mb = args.micro_batch
@@ -1175,41 +1330,60 @@ def run_inference(args, rank, local_rank, world):
 
     stream = torch.cuda.current_stream(device)
     run_all()  # warm-up pass over the shard
-    clocks = ClockSampler(_device_uuid(device), args.clocks_log if rank == 0 else None)
+    sampler = ClockSampler(_device_uuid(device), args.clocks_log if rank == 0 else None) if clocks else None
     t0 = time.time()
     _barrier(world, device)
     n0 = _lib.launch_count()
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s.record(stream)
-    for _ in range(args.steps):
+    for _ in range(steps):
         run_all()
     e.record(stream)
     _barrier(world, device)
     launches = _lib.launch_count() - n0
     t1 = time.time()
-    clocks.stop()
-    ms = _max_over_ranks(s.elapsed_time(e), world, device) / args.steps
-    if world > 1:
-        import torch.distributed as dist
-
-        dist.destroy_process_group()
+    if sampler is not None:
+        sampler.stop()
+    ms = _max_over_ranks(s.elapsed_time(e), world, device) / steps
+    del model, buf
+    torch.cuda.empty_cache()
     if rank != 0:
-        return
+        return None
     fps = total * frames / (ms * 1e-3)
-    print(json.dumps({
+    out = {
         "metric": "SEMamba long-utterance inference, frames/s (64 x 60 s utterances, sharded)",
-        "value": round(fps, 1), "unit": "frames/s", "n_gpus": world, "steps": args.steps, "warmup": 1,
-        "ms_per_step": round(ms, 2), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-        "dtype": "bf16 autocast, fp32 scans", "data": "synthetic (audio ~ N(0, 0.1), seeded per rank)",
+        "value": round(fps, 1), "unit": "frames/s", "n_gpus": world, "steps": steps, "warmup": 1,
+        "ms_per_step": round(ms, 2), "scaling": "strong",
+        "dtype": "bf16 autocast, fp32 scans", "data": "synthetic (audio ~ N(0, 0.1), seeded per rank), "
+                                                     "random-init weights",
         "config": {"workload": "STFT -> generator -> iSTFT, no_grad, 64 utterances of 60 s",
                    "global_batch": total, "seq_len": frames, "micro_batch": mb,
+                   "stream_chunk": args.stream_chunk or None,
                    "parallelism": f"sharded over {world} GPUs"},
         "e2e": {"value": round(fps, 1), "unit": "frames/s", "h2d_bytes_per_step": total * seg * 4 // world,
                 "d2h_bytes_per_step": total * seg * 4 // world,
                 "note": "every step copies its audio in from pinned host memory and the enhanced audio out"},
         "gpu_launches": launches,
-        "clocks": clocks.summary(t0, t1),
-    }), flush=True)
+    }
+    if sampler is not None:
+        out["clocks"] = sampler.summary(t0, t1)
+    return out
+
+
+def run_inference(args, rank, local_rank, world):
+    """The long-utterance inference as the bench line (`--workload inference`)."""
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    _init_dist(world, device)
+    out = measure_inference(args, rank, local_rank, world, device, args.steps)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    if out is None:
+        return
+    out.update(higher_is_better=True, vs_baseline=None)
+    print(json.dumps(out), flush=True)
 
 
 def main():

@@ -523,6 +523,128 @@ __global__ void __launch_bounds__(kThreads) slru_fwd_kernel(const SParams p) {
   }
 }
 
+// ------------------------------------------------- forward, real, modes in registers
+// The real scan with N <= 16 modes: one thread per (sequence, channel) holding all of the
+// channel's modes in registers, so y_t = D x_t + sum_n C_t[n] h_t[n] is summed inside the
+// thread (no lane shuffles) and each staged dnu / x value is read once per step instead
+// of once per 4-mode group. A CTA covers kRmCB channels of one sequence; operand tiles of
+// kRmTT steps are staged by cp.async (dnu, x per channel; B_t, C_t per mode, padded to 16
+// with zeros: a padded mode keeps a zero state and adds nothing). Checkpoints hold the same
+// (S, nchunks, C, N) layout as slru_fwd_kernel's, so the backward is shared.
+constexpr int kRmCB = 128;  // channels per CTA
+constexpr int kRmTT = 16;   // steps per staged tile
+constexpr int kRmNM = 16;   // modes held per thread
+
+struct TilesRM {
+  static constexpr int kTT = kRmTT;
+  static constexpr int CB = kRmCB;
+  static constexpr int NP = kRmNM;
+  static constexpr int kRowTh = -1;
+  static constexpr int kRowDy = -1;
+  static constexpr int kRowC = 2;  // delta_nu, x
+  static constexpr int kRowN = 2;  // B, C
+  static constexpr int kBuf = kTT * (kRowC * CB + kRowN * NP);
+  __host__ __device__ static constexpr size_t bytes() { return (size_t)2 * kBuf * sizeof(float); }
+  __device__ static float* chan(float* buf, int row) { return buf + row * kTT * CB; }
+  __device__ static float* mode(float* buf, int row) { return buf + kRowC * kTT * CB + row * kTT * NP; }
+};
+
+template <int GAIN, bool EXTRA>
+__global__ void __launch_bounds__(kRmCB, 6) slru_fwd_real16_kernel(const SParams p) {
+  using T = TilesRM;
+  constexpr int NM = kRmNM, TT = kRmTT;
+  extern __shared__ float4 rm_smem4[];
+  float* smem = reinterpret_cast<float*>(rm_smem4);
+  const int tid = threadIdx.x;
+  const int c0 = blockIdx.x * T::CB;
+  const int c = c0 + tid;
+  const int64_t s = blockIdx.y;
+  const bool cval = c < p.C;
+  const int nc = (int)min((int64_t)T::CB, p.C - c0);
+  const int L = (int)p.L, N = (int)p.N;
+  const bool vecC = (p.C % 4) == 0 && semx_aligned16(p.dnu) && semx_aligned16(p.x);
+  const bool vecN = (p.N % 4) == 0 && semx_aligned16(p.Bre) && semx_aligned16(p.Cre);
+  const bool envelope = EXTRA && p.envelope;
+
+  float a[NM], ge[NM], h[NM];
+#pragma unroll
+  for (int n = 0; n < NM; ++n) {
+    const bool ok = cval && n < N;
+    const int64_t i = (int64_t)c * N + n;
+    a[n] = ok ? p.a[i] : 0.f;
+    ge[n] = (ok && envelope) ? p.g[i] : 0.f;
+    h[n] = (ok && p.h0r) ? p.h0r[(s * p.C + c) * N + n] : 0.f;
+  }
+  const float Dc = cval ? p.D[c] : 0.f;
+
+  tile_zero_padding<T>(smem, nc, N);
+  const int ntiles = (L + TT - 1) / TT;
+  if (ntiles > 0) tile_load<T>(p, smem, s, 0, min(TT, L), c0, nc, vecC, vecN);
+  cp_async_commit();
+  int next_ck = 0;
+  float* yrow = p.y + s * p.L * p.C + c;
+  const bool ck16 = N == NM && semx_aligned16(p.ckpt);
+  for (int k = 0; k < ntiles; ++k) {
+    cp_async_wait_all();
+    __syncthreads();
+    if (k + 1 < ntiles)
+      tile_load<T>(p, smem + ((k + 1) & 1) * T::kBuf, s, (k + 1) * TT, min(TT, L - (k + 1) * TT), c0, nc,
+                   vecC, vecN);
+    cp_async_commit();
+    const float* buf = smem + (k & 1) * T::kBuf;
+    const float* dnus = buf;
+    const float* xs = buf + TT * T::CB;
+    const float* Bs = buf + T::kRowC * TT * T::CB;
+    const float* Cs = Bs + TT * T::NP;
+    const int t0 = k * TT, nt = min(TT, L - t0);
+#pragma unroll 2
+    for (int i = 0; i < nt; ++i) {
+      const int t = t0 + i;
+      if (p.ckpt != nullptr && t == next_ck) {
+        if (cval) {
+          float* ck = p.ckpt + ((s * p.nchunks + t / p.chunk) * p.C + c) * N;
+          if (ck16) {
+#pragma unroll
+            for (int n = 0; n < NM; n += 4)
+              *reinterpret_cast<float4*>(ck + n) = make_float4(h[n], h[n + 1], h[n + 2], h[n + 3]);
+          } else {
+#pragma unroll
+            for (int n = 0; n < NM; ++n)
+              if (n < N) ck[n] = h[n];
+          }
+        }
+        next_ck += p.chunk;
+      }
+      const float dnu = dnus[i * T::CB + tid], x = xs[i * T::CB + tid];
+      const float dx_m = dnu * x;  // the Mamba gain's drive scale
+      // Four partial readout sums (one per mode of a float4 group), so the readout is four
+      // chains of four FMAs instead of one chain of sixteen.
+      float yq[4] = {Dc * x, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int n4 = 0; n4 < NM; n4 += 4) {
+        const float4 b4 = *reinterpret_cast<const float4*>(Bs + i * T::NP + n4);
+        const float4 c4 = *reinterpret_cast<const float4*>(Cs + i * T::NP + n4);
+        const float bb[4] = {b4.x, b4.y, b4.z, b4.w}, cc[4] = {c4.x, c4.y, c4.z, c4.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int n = n4 + j;
+          const Disc d = discretise<true, GAIN>(a[n], 0.f, 1.f, false, dnu, 0.f);
+          const float gx = GAIN == SEMX_GAIN_MAMBA ? dx_m : d.gr * x;
+          h[n] = fmaf(d.lre, h[n], gx * bb[j]);
+          yq[j] = fmaf(cc[j], h[n], yq[j]);
+          if (envelope) yq[j] = fmaf(ge[n], h[n] * h[n], yq[j]);
+        }
+      }
+      if (cval) yrow[(int64_t)t * p.C] = (yq[0] + yq[1]) + (yq[2] + yq[3]);
+    }
+  }
+  if (p.hfr != nullptr && cval) {
+#pragma unroll
+    for (int n = 0; n < NM; ++n)
+      if (n < N) p.hfr[(s * p.C + c) * N + n] = h[n];
+  }
+}
+
 // ---------------------------------------------------------------------------- backward
 template <bool REAL, int NG>
 struct BwdLayout {
@@ -1101,6 +1223,30 @@ int launch_fwd(const SParams& p, const Geometry& g, cudaStream_t st) {
   return semx::check_launch("slru_fwd_kernel");
 }
 
+template <int GAIN, bool EXTRA>
+int launch_fwd_rm(const SParams& p, cudaStream_t st) {
+  const dim3 grid((unsigned)semx::cdiv(p.C, kRmCB), (unsigned)p.S);
+  const size_t smem = TilesRM::bytes();
+  auto kern = slru_fwd_real16_kernel<GAIN, EXTRA>;
+  if (!semx::allow_smem(kern, smem)) return SEMX_ERR_LAUNCH;
+  kern<<<grid, kRmCB, smem, st>>>(p);
+  return semx::check_launch("slru_fwd_real16_kernel");
+}
+
+// The real forward with N <= 16 modes (slru_fwd_real16_kernel), specialised on the gain
+// and the envelope readout.
+int launch_fwd_real16(const SemxSelectiveLruArgs* a, const SParams& p, cudaStream_t st) {
+  const bool env = p.envelope != 0;
+  switch (a->input_gain) {
+    case SEMX_GAIN_GAMMA:
+      return env ? launch_fwd_rm<SEMX_GAIN_GAMMA, true>(p, st) : launch_fwd_rm<SEMX_GAIN_GAMMA, false>(p, st);
+    case SEMX_GAIN_MAMBA:
+      return env ? launch_fwd_rm<SEMX_GAIN_MAMBA, true>(p, st) : launch_fwd_rm<SEMX_GAIN_MAMBA, false>(p, st);
+    default:
+      return env ? launch_fwd_rm<SEMX_GAIN_ZOH, true>(p, st) : launch_fwd_rm<SEMX_GAIN_ZOH, false>(p, st);
+  }
+}
+
 template <bool REAL, int GAIN, int NG, bool EXTRA>
 int launch_bwd(const SParams& p, const Geometry& g, size_t smem, cudaStream_t st) {
   auto kern = slru_bwd_kernel<REAL, GAIN, NG, EXTRA>;
@@ -1190,6 +1336,7 @@ int semx_selective_lru_fwd(const SemxSelectiveLruArgs* a, semx_stream_t stream) 
   rc = semx::bind_device({a->y, a->delta_nu, a->D});
   if (rc != SEMX_OK) return rc;
   const SParams p = to_params(a);
+  if (a->real && a->N <= kRmNM) return launch_fwd_real16(a, p, semx::as_stream(stream));
   const Geometry g = geometry(a);
   return dispatch(false, a, p, g, 0, semx::as_stream(stream));
 }

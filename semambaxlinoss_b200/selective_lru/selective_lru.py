@@ -137,11 +137,30 @@ class SelectiveLRU(nn.Module):
         self.omega._no_weight_decay = True
         self.D._no_weight_decay = True
 
+    #: Streaming: when set to a step count K, forward() runs sequences longer than K as
+    #: consecutive K-step pieces, each starting from the previous piece's final state (the
+    #: h_init / return_final_state path), so the layer's (batch, time, d_model) step
+    #: tensors exist for one piece at a time. The result equals the unsplit scan's (the
+    #: recurrence is the same; only the projection GEMMs' row blocking changes). None: one
+    #: piece. Gradients flow through the carried states.
+    stream_chunk: int | None = None
+
     def forward(self, x: torch.Tensor, h_init: torch.Tensor | None = None,
                 rate_scale: float | None = None, return_final_state: bool = False):
         """``h_init``: optional complex (B, C, N) initial state; ``rate_scale``: per-call
         frame-rate factor on the selective step; ``return_final_state``: also return
         h_{T-1} as complex (B, C, N) (gradients flow through it)."""
+        K = self.stream_chunk
+        if K is not None and x.shape[1] > K:
+            h, ys = h_init, []
+            for t0 in range(0, x.shape[1], K):
+                y, h = self._forward_piece(x[:, t0:t0 + K], h, rate_scale, True)
+                ys.append(y)
+            y = torch.cat(ys, 1)
+            return (y, h) if return_final_state else y
+        return self._forward_piece(x, h_init, rate_scale, return_final_state)
+
+    def _forward_piece(self, x, h_init, rate_scale, return_final_state):
         r, N = self.dt_rank, self.d_state
         x = x.float()
         dnu_r, dth_r, B_sel, C_sel = torch.split(self.x_proj(x), [r, r, 2 * N, 2 * N], dim=-1)

@@ -16,7 +16,8 @@ UNITS = 129_684  # sequence-steps of one op-level pass (404 x 321 = 1284 x 101)
 
 # (kernel, bench workload tag, algorithmic bytes per sequence-step) for the kernels
 # bench.py names: LinOSS P = 256; SISO C = 256, N = 16 (real / complex gamma); MIMO
-# 8 heads x 32, state 128, rank 4 (bf16 input, 1872-column projection).
+# 8 heads x 32, state 128, rank 4 (bf16 input, 1872-column projection); the MIMO operator and
+# the plain complex scan at 404 x 321, 8 heads x 16 modes, 32 channels per head.
 CASES = [
     ("linoss_fwd_kernel", "linoss", 16 * 256),
     ("linoss_bwd_kernel", "linoss", 24 * 256),
@@ -25,7 +26,12 @@ CASES = [
     ("slru_fwd_kernel", "slru complex", 4 * (4 * 256 + 4 * 16)),
     ("slru_bwd_kernel", "slru complex", 4 * (7 * 256 + 8 * 16)),
     ("mimo_layer_fwd_kernel", "mimo", 5280),
+    ("mimo_layer_fwd_tc_kernel", "mimo", 5280),
     ("mimo_layer_bwd16_kernel", "mimo", 9536),
+    ("mimo_fwd_kernel", "ops", 24 * 128 + 8 * 256),
+    ("mimo_bwd_kernel", "ops", 40 * 128 + 12 * 256),
+    ("cscan_fwd_kernel", "ops_cscan", 24 * 128),
+    ("cscan_bwd_kernel", "ops_cscan", 40 * 128),
 ]
 
 

@@ -290,3 +290,32 @@ def test_full_size_complex_gamma_scan_slices():
     for k, ref in g_ref.items():
         got = ins[k].grad[sl] if k in per_seq else ins[k].grad
         assert_close(got, ref, floor_tol(rel_err(g32[k], ref)), f"d{k}")
+
+
+@pytest.mark.parametrize("gain", ["gamma", "mamba"])
+def test_streamed_layer_matches_one_piece(gain):
+    """SelectiveLRU.stream_chunk: the sequence run as 32-step pieces that carry the state
+    (h_init / return_final_state) gives the unsplit layer's output, final state and every
+    gradient (only the projection GEMMs' row blocking differs)."""
+    from semambaxlinoss_b200.selective_lru import SelectiveLRU
+
+    torch.manual_seed(3)
+    m = SelectiveLRU(d_model=64, d_state=16, input_gain=gain, envelope_readout=True).to(cuda())
+    with torch.no_grad():
+        for p_ in m.parameters():
+            p_.add_(0.05 * torch.randn_like(p_))
+    x = torch.randn(3, 101, 64, device="cuda")
+    gy = torch.randn(3, 101, 64, device="cuda")
+    h0 = torch.randn(3, 64, 16, dtype=torch.complex64, device="cuda")
+    outs = []
+    for K in (None, 32):
+        m.stream_chunk = K
+        m.zero_grad(set_to_none=True)
+        xx = x.clone().requires_grad_(True)
+        hh = h0.clone().requires_grad_(True)
+        y, hf = m(xx, h_init=hh, return_final_state=True)
+        ((y * gy).sum() + hf.real.sum() - hf.imag.sum()).backward()
+        outs.append([y.detach(), hf.detach(), xx.grad, hh.grad] + [p_.grad.clone() for p_ in m.parameters()])
+    m.stream_chunk = None
+    for i, (a_, b_) in enumerate(zip(*outs)):
+        assert_close(b_, a_, 1e-5, f"tensor {i}")

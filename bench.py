@@ -466,7 +466,7 @@ class MimoPass:
 
     fwd_bytes_per_unit = 4768
     bwd_bytes_per_unit = 8512
-    kernels = ("mimo_layer_fwd_tc_kernel", "mimo_layer_bwd16_kernel")
+    kernels = ("mimo_layer_fwd_tc_kernel", "mimo_layer_bwd_tc_kernel")
 
     def __init__(self, layer, S, L, seed, device):
         g = torch.Generator(device=device).manual_seed(seed)
@@ -495,7 +495,7 @@ class MimoKernelPass:
     for the kernel roofline of the MIMO workload. Bytes per token: fwd x + proj (bf16) in,
     y (fp32) out = 5280; bwd x, proj (bf16), dy (fp32) in, dx, dproj (bf16) out = 9536."""
 
-    kernels = ("mimo_layer_fwd_tc_kernel", "mimo_layer_bwd16_kernel")
+    kernels = ("mimo_layer_fwd_tc_kernel", "mimo_layer_bwd_tc_kernel")
 
     def __init__(self, layer, S, L, seed, device):
         from semambaxlinoss_b200 import _lib

@@ -1735,6 +1735,518 @@ __global__ void __launch_bounds__(kT) mimo_layer_bwd16_kernel(const LParams p) {
   }
 }
 
+// ------------------------------------------------ backward, tensor-core readout adjoint (bf16)
+// mimo_layer_bwd16_kernel with the readout adjoint on the tensor cores (bf16 operands,
+// 16 x 32 heads, no envelope readout): per 64-token tile, one thread issues four
+// kind::tf32 MMAs, D (64 x 32, tensor memory) = dy tile (K-major, rows = tokens) x
+// [C_re | -C_im]^T (K-major, rows = modes), i.e. g[t, n] = sum_f dy[t, f] conj(C[f, n]);
+// warp q moves the rows of chunk q into shared memory when the backward reaches that
+// chunk. The dy tile holds the current 64-token tile; each chunk's 16 rows are refilled
+// with the previous tile's (cp.async) as soon as the chunk is done. The chunk's states
+// live in a swizzled h tile ([h_re | -h_im], rows = tokens) plus the entry state. dC stays
+// a per-thread register sum: the tf32 MMA with an MN-major operand (the token-major h and
+// dy tiles read as K = tokens) returned zeros in the 128-byte-swizzled layout used here.
+// 43 KB of shared memory, at most 96 registers: 5 CTAs per SM, as for bwd16.
+struct TcBLay {
+  static constexpr int dyt = 0;                          // 64 x 32 fp32, swizzled
+  static constexpr int bwt = dyt + 64 * 32;              // 32 x 32 fp32, swizzled
+  static constexpr int ht = bwt + 32 * 32;               // 16 x 32 fp32, swizzled
+  static constexpr int Co = ht + 16 * 32;                // c_out (4 x 32)
+  static constexpr int Dp = Co + 4 * 32;
+  static constexpr int prm = Dp + 32;                    // a, omega, detune (3 x 16)
+  static constexpr int cin = prm + 48;                   // scan carry (16 float2)
+  static constexpr int cadj = cin + 32;                  // adjoint carry (16 float2)
+  static constexpr int hent = cadj + 32;                 // chunk entry state (16 float2)
+  static constexpr int stg_floats = 16 * (32 + 32 + 64 + 128) / 2;
+  static constexpr int stg0 = hent + 32;
+  static constexpr int stg1 = stg0 + stg_floats;
+  static constexpr int sml_floats = 16 * (3 + 2 * 4);
+  static constexpr int sml0 = stg1 + stg_floats;
+  static constexpr int sml1 = sml0 + sml_floats;
+  static constexpr int lam = sml1 + sml_floats;          // 16 x kB_HW float2 each
+  static constexpr int braw = lam + 16 * kB_HW * 2;
+  static constexpr int gs = braw + 16 * kB_HW * 2;
+  static constexpr int db = gs + 16 * kB_HW * 2;
+  static constexpr int sr = db + 16 * kB_HW * 2;
+  static constexpr int dr = sr + 64;
+  static constexpr int bar = dr + 64;                    // the adjoint MMA's 8-byte mbarrier
+  static constexpr int tslot = bar + 4;
+  static constexpr int total = tslot + 4;
+  static constexpr int red = lam;                        // end-of-kernel sums reuse lam + braw
+  static constexpr int rb = lam + 3 * 16 * (kT / 8);
+};
+static_assert(TcBLay::bwt % 256 == 0 && TcBLay::ht % 256 == 0 && TcBLay::stg0 % 4 == 0 &&
+                  TcBLay::bar % 2 == 0 && TcBLay::rb + 2 * (kT / 8) <= TcBLay::gs,
+              "tensor-core backward layout");
+
+// Copies dy rows [t0g, t0g + nt) of head h into dy-tile rows row0.. (zeros for rows
+// nt..15 of a partial chunk).
+__device__ __forceinline__ void tcb_load_dy(const LParams& p, float* sm, int64_t s, int h, int row0, int t0g,
+                                            int nt) {
+  char* dyt = reinterpret_cast<char*>(sm + TcBLay::dyt);
+  const int64_t Fd = p.H * 32;
+  for (int i = threadIdx.x; i < 16 * 8; i += kT) {
+    const int r = i >> 3, c = i & 7;
+    float* dst = reinterpret_cast<float*>(dyt + semx::tc::sw128(row0 + r, c));
+    if (r < nt) {
+      const float* src = p.dy + (s * p.L + t0g + r) * Fd + (int64_t)h * 32 + 4 * c;
+      if ((p.vec & 4) != 0) {
+        cp_async16(dst, src);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) dst[e] = src[e];
+      }
+    } else {
+      *reinterpret_cast<float4*>(dst) = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
+}
+
+// dy[t, f] and a float4 of it from the dy tile (row = tile row of token t).
+__device__ __forceinline__ float tcb_dy(const float* sm, int row, int f) {
+  return *reinterpret_cast<const float*>(reinterpret_cast<const char*>(sm + TcBLay::dyt) +
+                                         semx::tc::sw128(row, f >> 2) + 4 * (f & 3));
+}
+// h_t[n] from the h tile, which stores [h_re | -h_im].
+__device__ __forceinline__ float2 tcb_h(const float* sm, int t, int n) {
+  const char* ht = reinterpret_cast<const char*>(sm + TcBLay::ht);
+  const float re = *reinterpret_cast<const float*>(ht + semx::tc::sw128(t, n >> 2) + 4 * (n & 3));
+  const float nim = *reinterpret_cast<const float*>(ht + semx::tc::sw128(t, (n >> 2) + 4) + 4 * (n & 3));
+  return make_float2(re, -nim);
+}
+
+template <int RK>
+__global__ void __launch_bounds__(kT, 5) mimo_layer_bwd_tc_kernel(const LParams p) {
+  using T = __nv_bfloat16;
+  constexpr int NH = kB_NH, FH = kB_FH, CT = kB_CT, HW = kB_HW, R = RK;
+  extern __shared__ __align__(1024) float4 smem4[];
+  float* sm = reinterpret_cast<float*>(smem4);
+  const bool det = p.detune != 0;
+  const int64_t s = blockIdx.x / p.H;
+  const int h = (int)(blockIdx.x % p.H);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int L = (int)p.L;
+  const int64_t Fd = p.H * p.Fh;
+  const Cols cols = cols_of(p, h);
+  // Unpadded staging rows (the staging helpers read these widths).
+  FLay fl = {};
+  fl.tc = CT;
+  fl.xw = FH;
+  fl.bxw = 2 * NH;
+  fl.btw = R * NH;
+  fl.ctw = 2 * R * NH;
+  if ((semx::tc::smem_addr(smem4) & 1023u) != 0) {  // the swizzled tiles need a 1 KB base
+    if (tid == 0) atomicAdd(&g_tc_timeouts, 1u);
+    return;
+  }
+  // Head parameters; B tile row n = [C_re[0..31, n]] (n < 16) or [-C_im[0..31, n - 16]].
+  for (int i = tid; i < 32 * 8; i += kT) {
+    const int n2 = i >> 3, c = i & 7;
+    const float2* cp = reinterpret_cast<const float2*>(p.C) + ((int64_t)h * FH + 4 * c) * NH + (n2 & 15);
+    float v[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 cv = cp[e * NH];
+      v[e] = n2 < 16 ? cv.x : -cv.y;
+    }
+    *reinterpret_cast<float4*>(reinterpret_cast<char*>(sm + TcBLay::bwt) + semx::tc::sw128(n2, c)) =
+        make_float4(v[0], v[1], v[2], v[3]);
+  }
+  for (int i = tid; i < 16 * 32; i += kT) sm[TcBLay::ht + i] = 0.f;  // rows past a partial chunk stay 0
+  for (int i = tid; i < R * FH; i += kT) sm[TcBLay::Co + i] = p.cout[(int64_t)h * R * FH + i];
+  for (int i = tid; i < FH; i += kT) sm[TcBLay::Dp + i] = p.D[(int64_t)h * FH + i];
+  if (tid < NH) {
+    sm[TcBLay::prm + tid] = expf(p.A_log[(int64_t)h * NH + tid]);
+    sm[TcBLay::prm + NH + tid] = p.omega[(int64_t)h * NH + tid];
+    sm[TcBLay::prm + 2 * NH + tid] = det ? p.sdet[(int64_t)h * NH + tid] : 1.f;
+    reinterpret_cast<float2*>(sm + TcBLay::cadj)[tid] = make_float2(0.f, 0.f);
+  }
+  uint64_t* bar_adj = reinterpret_cast<uint64_t*>(sm + TcBLay::bar);
+  if (tid < 32) semx::tc::tmem_alloc(reinterpret_cast<uint32_t*>(sm + TcBLay::tslot), 32);
+  if (tid == 0) semx::tc::mbar_init(bar_adj, 1);
+  semx::tc::fence_before_sync();
+  __syncthreads();
+  semx::tc::fence_after_sync();
+  const uint32_t taddr = *reinterpret_cast<const uint32_t*>(sm + TcBLay::tslot);
+
+  float2* lam = reinterpret_cast<float2*>(sm + TcBLay::lam);
+  float2* braw = reinterpret_cast<float2*>(sm + TcBLay::braw);
+  float2* gs = reinterpret_cast<float2*>(sm + TcBLay::gs);
+  float2* db = reinterpret_cast<float2*>(sm + TcBLay::db);
+  float2* cin = reinterpret_cast<float2*>(sm + TcBLay::cin);
+  float2* cadj = reinterpret_cast<float2*>(sm + TcBLay::cadj);
+  float2* hent = reinterpret_cast<float2*>(sm + TcBLay::hent);
+  char* htile = reinterpret_cast<char*>(sm + TcBLay::ht);
+  const int stg[2] = {TcBLay::stg0, TcBLay::stg1}, smlo[2] = {TcBLay::sml0, TcBLay::sml1};
+
+  // Thread roles (fixed for the whole kernel).
+  const int tA = tid / 8, npA = tid % 8;   // (token, mode pair) items
+  const int fC = tid / 4, nqC = tid % 4;   // dC items (channel, 4 modes)
+  const int rO = tid / FH, fO = tid % FH;  // dcout items (rank, channel) when R = 4
+  float acc_a[2] = {0.f, 0.f}, acc_om[2] = {0.f, 0.f}, acc_sd[2] = {0.f, 0.f};
+  float aCr[4] = {}, aCi[4] = {};
+  float aO = 0.f, aD = 0.f;
+  float aBnu = 0.f, aBth = 0.f;
+  const float2 bias = dt_bias(p, h);
+  const int nck = p.nck;
+  uint32_t ph_adj = 0;
+  bool bail = false, adj_pending = false;
+  float pre[kPre];
+  auto stage = [&](int k, int b) {
+    const int t0 = k * CT, nt = min(CT, L - t0);
+    stage_bulk<true, 16, 32, RK>(p, fl, sm + stg[b], s, h, t0, nt);
+  };
+  if (nck > 0) {
+    const int k = nck - 1, nt = min(CT, L - k * CT);
+    stage(k, 0);
+    load_small<true, RK>(p, s, h, k * CT, nt, bias, pre);
+    store_small<RK, CT>(p, sm + smlo[0], nt, pre);
+    // dy of the last tile, and of the previous tile's chunks whose rows the last tile
+    // does not use.
+    const int qlast = k & 3;
+    for (int q = 0; q <= qlast; ++q) {
+      const int kk = k - qlast + q;
+      tcb_load_dy(p, sm, s, h, 16 * q, kk * CT, min(CT, L - kk * CT));
+    }
+    for (int q = qlast + 1; q < 4 && k - qlast - 4 + q >= 0; ++q) tcb_load_dy(p, sm, s, h, 16 * q, (k - qlast - 4 + q) * CT, CT);
+  }
+  cp_async_commit();
+  int b = 0;
+  for (int k = nck - 1; k >= 0; --k, b ^= 1) {
+    const int q = k & 3;
+    const int t0 = k * CT, nt = min(CT, L - t0);
+    const bool tile_start = (k == nck - 1) || q == 3;
+    const int row0 = 16 * q;  // this chunk's rows in the dy tile
+    if (tile_start) cp_async_wait_all();
+    else asm volatile("cp.async.wait_group 1;\n" ::: "memory");
+    semx::tc::fence_smem_to_async();
+    __syncthreads();
+    if (tile_start && tid == 0) {  // readout adjoint of the tile: dy x [C_re | -C_im]^T
+      constexpr uint32_t idesc = semx::tc::idesc_tf32(64, 32);
+      const uint32_t a0 = semx::tc::smem_addr(sm + TcBLay::dyt), b0 = semx::tc::smem_addr(sm + TcBLay::bwt);
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk)
+        semx::tc::mma_tf32(taddr, semx::tc::desc_sw128_kmajor(a0 + 32 * kk), semx::tc::desc_sw128_kmajor(b0 + 32 * kk),
+                           idesc, kk > 0);
+      semx::tc::mma_commit(bar_adj);
+    }
+    adj_pending = adj_pending || tile_start;
+    if (k > 0) {
+      stage(k - 1, b ^ 1);
+      load_small<true, RK>(p, s, h, (k - 1) * CT, CT, bias, pre);
+    }
+    cp_async_commit();
+    const T* xs = reinterpret_cast<const T*>(sm + stg[b]);
+    const T* bxs = xs + CT * fl.xw;
+    const T* bts = bxs + CT * fl.bxw;
+    const T* cts = bts + CT * fl.btw;
+    const float* sml = sm + smlo[b];
+    const float* raws = sml;
+    const float* dnus = sml + CT;
+    const float* dths = sml + 2 * CT;
+    const float* sbs = sml + 3 * CT;
+    const float* scs = sbs + CT * R;
+    const int xw = fl.xw, bxw = fl.bxw, btw = fl.btw, ctw = fl.ctw;
+
+    // A. Poles, raw and gained drive per (token, mode pair); entry state.
+    if (tid < NH) {
+      const float2 c = reinterpret_cast<const float2*>(p.ckpt)[((s * nck + k) * p.H + h) * NH + tid];
+      cin[tid] = c;
+      hent[tid] = c;
+    }
+    if (tA < nt) {
+      const int t = tA, na = 2 * npA;
+      const float4 bq = ld4(bxs + t * bxw + 2 * na);
+      float br0 = bq.x, bi0 = bq.y, br1 = bq.z, bi1 = bq.w;
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        const float sbv = sbs[t * R + r];
+        br0 = fmaf(sbv, static_cast<float>(bts[t * btw + r * NH + na]), br0);
+        br1 = fmaf(sbv, static_cast<float>(bts[t * btw + r * NH + na + 1]), br1);
+      }
+#pragma unroll
+      for (int dn = 0; dn < 2; ++dn) {
+        const int n = na + dn;
+        const float brv = dn ? br1 : br0, biv = dn ? bi1 : bi0;
+        const MDisc d = mdisc(p.gain, sm[TcBLay::prm + n], sm[TcBLay::prm + NH + n], sm[TcBLay::prm + 2 * NH + n],
+                              det, dnus[t], dths[t]);
+        lam[t * HW + n] = make_float2(d.lre, d.lim);
+        braw[t * HW + n] = make_float2(brv, biv);
+        gs[t * HW + n] = make_float2(d.gr * brv - d.gi * biv, d.gr * biv + d.gi * brv);
+      }
+    }
+    // The readout adjoint rows of this chunk (warp q, lanes 0..15) into db, which is free
+    // until phase F; at a tile start, after its MMA (issued above) completes.
+    if (tile_start) {
+      const bool ok = semx::tc::mbar_wait(bar_adj, ph_adj, kTcWaitLimit);
+      if (__syncthreads_or(!ok)) {
+        if (tid == 0) atomicAdd(&g_tc_timeouts, 1u);
+        bail = true;
+        break;
+      }
+      ph_adj ^= 1u;
+      adj_pending = false;
+      semx::tc::fence_after_sync();
+    }
+    if (warp == q) {
+      float acc[32];
+      semx::tc::tmem_ld32(taddr + ((uint32_t)(32 * q) << 16), acc);
+      if (lane < nt) {
+#pragma unroll
+        for (int n = 0; n < NH; ++n) db[lane * HW + n] = make_float2(acc[n], acc[16 + n]);
+      }
+    }
+    semx::tc::fence_before_sync();
+    __syncthreads();
+    // B. States of the chunk from the checkpoint, into the h tile as [h_re | -h_im].
+    chunk_scan_to<kB_SEG, CT>(lam, gs, cin, NH, HW, nt, [&](int t, int n, float2 v) {
+      char* base = htile + t * 128 + 4 * (n & 3);
+      *reinterpret_cast<float*>(base + (((n >> 2) ^ (t & 7)) << 4)) = v.x;
+      *reinterpret_cast<float*>(base + ((((n >> 2) + 4) ^ (t & 7)) << 4)) = -v.y;
+    });
+    __syncthreads();
+    // C. Rank read and its adjoint per (token, rank).
+    if (R > 0) {
+      if (tid < nt * R) {
+        const int t = tid / (R > 0 ? R : 1), r = tid % (R > 0 ? R : 1);
+        const T* cr = cts + t * ctw + r * 2 * NH;
+        float rd = 0.f;
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4) {
+          const float4 hre = *reinterpret_cast<const float4*>(htile + semx::tc::sw128(t, c4));
+          const float4 hni = *reinterpret_cast<const float4*>(htile + semx::tc::sw128(t, c4 + 4));
+          const float4 cre = ld4(cr + 4 * c4), cim = ld4(cr + NH + 4 * c4);
+          rd = fmaf(cre.x, hre.x, fmaf(cim.x, hni.x, rd));
+          rd = fmaf(cre.y, hre.y, fmaf(cim.y, hni.y, rd));
+          rd = fmaf(cre.z, hre.z, fmaf(cim.z, hni.z, rd));
+          rd = fmaf(cre.w, hre.w, fmaf(cim.w, hni.w, rd));
+        }
+        float dyc = 0.f;
+#pragma unroll
+        for (int c4 = 0; c4 < 8; ++c4) {
+          const float4 dv = *reinterpret_cast<const float4*>(reinterpret_cast<const char*>(sm + TcBLay::dyt) +
+                                                             semx::tc::sw128(row0 + t, c4));
+          const float* co = sm + TcBLay::Co + r * FH + 4 * c4;
+          dyc = fmaf(dv.x, co[0], fmaf(dv.y, co[1], fmaf(dv.z, co[2], fmaf(dv.w, co[3], dyc))));
+        }
+        const float scv = scs[t * R + r];
+        sm[TcBLay::sr + tid] = scv * rd;
+        sm[TcBLay::dr + tid] = scv * dyc;
+        st<true>(p.dproj, (s * p.L + t0 + t) * p.P + cols.sc + r, rd * dyc);
+      }
+    }
+    // D. Readout adjoint (drained into db after phase A) plus the rank terms, and the c_t
+    // gradient, per (token, mode pair).
+    if (R > 0) __syncthreads();
+    if (tA < nt) {
+      const int t = tA, na = 2 * npA;
+      float2 g0 = db[t * HW + na], g1 = db[t * HW + na + 1];
+      const float2 h0 = tcb_h(sm, t, na), h1 = tcb_h(sm, t, na + 1);
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        const float drv = sm[TcBLay::dr + t * R + r];
+        const T* cr = cts + t * ctw + r * 2 * NH;
+        g0.x = fmaf(drv, static_cast<float>(cr[na]), g0.x);
+        g1.x = fmaf(drv, static_cast<float>(cr[na + 1]), g1.x);
+        g0.y = fmaf(-drv, static_cast<float>(cr[NH + na]), g0.y);
+        g1.y = fmaf(-drv, static_cast<float>(cr[NH + na + 1]), g1.y);
+        const int64_t row = (s * p.L + t0 + t) * p.P + cols.ct + (int64_t)r * 2 * NH;
+        st<true>(p.dproj, row + na, drv * h0.x);
+        st<true>(p.dproj, row + na + 1, drv * h1.x);
+        st<true>(p.dproj, row + NH + na, -drv * h0.y);
+        st<true>(p.dproj, row + NH + na + 1, -drv * h1.y);
+      }
+      gs[t * HW + na] = g0;
+      gs[t * HW + na + 1] = g1;
+    }
+    __syncthreads();
+    // E. Adjoint scan: G over g, carry across chunks in cadj.
+    chunk_scan_rev<kB_SEG, CT>(lam, gs, cadj, HW, nt);
+    __syncthreads();
+    // F. Through the gain and the pole per (token, mode pair).
+    {
+      float sdnu = 0.f, sdth = 0.f;
+      if (tA < nt) {
+        const int t = tA;
+#pragma unroll
+        for (int dn = 0; dn < 2; ++dn) {
+          const int n = 2 * npA + dn;
+          const float a = sm[TcBLay::prm + n], om = sm[TcBLay::prm + NH + n], sd = sm[TcBLay::prm + 2 * NH + n];
+          const float dnu = dnus[t], dth = dths[t];
+          const MDisc d = mdisc(p.gain, a, om, sd, det, dnu, dth);
+          const float2 G = gs[t * HW + n], bv = braw[t * HW + n];
+          const float2 hp = t == 0 ? hent[n] : tcb_h(sm, t > 0 ? t - 1 : 0, n);
+          db[t * HW + n] = make_float2(d.gr * G.x + d.gi * G.y, d.gr * G.y - d.gi * G.x);
+          const float dgr = bv.x * G.x + bv.y * G.y, dgi = bv.x * G.y - bv.y * G.x;
+          const float dlre = G.x * hp.x + G.y * hp.y, dlim = G.y * hp.x - G.x * hp.y;
+          float P = dlre * d.lre + dlim * d.lim;
+          const float d_th = dlim * d.lre - dlre * d.lim;
+          float d_dnu = 0.f, da_extra = 0.f, dbase_extra = 0.f;
+          if (p.gain == SEMX_GAIN_GAMMA) {
+            const float nu2 = d.nu * d.nu;
+            P -= ((1.f - nu2) >= 1e-6f) ? dgr * nu2 * d.rs : 0.f;
+          } else if (p.gain == SEMX_GAIN_MAMBA) {
+            d_dnu = dgr;
+          } else if (p.gain == SEMX_GAIN_ZOH) {
+            d_dnu = dgr * d.lre + dgi * d.lim;
+            const float pr = dnu * d.lre - d.gr, pi = dnu * d.lim - d.gi;
+            const float qr = (d.base * pi - a * pr) * d.inv_den;
+            const float qi = -(a * pi + d.base * pr) * d.inv_den;
+            da_extra = -(dgr * qr + dgi * qi);
+            dbase_extra = dgi * qr - dgr * qi;
+          }
+          d_dnu += d_th * d.base - a * P;
+          const float dbase = d_th * dnu + dbase_extra;
+          sdnu += d_dnu;
+          sdth += det ? dbase * sd : dbase;
+          acc_a[dn] += da_extra - dnu * P;
+          acc_om[dn] += dbase;
+          acc_sd[dn] += det ? dbase * dth : 0.f;
+        }
+      }
+#pragma unroll
+      for (int m = 1; m < 8; m <<= 1) {
+        sdnu += __shfl_xor_sync(0xffffffffu, sdnu, m);
+        sdth += __shfl_xor_sync(0xffffffffu, sdth, m);
+      }
+      if (npA == 0 && tA < nt) {
+        const int64_t row = (s * p.L + t0 + tA) * p.P;
+        const float draw = sdnu * p.rs * semx::softplus_grad(raws[tA]);
+        st<true>(p.dproj, row + cols.dnu, draw);
+        st<true>(p.dproj, row + cols.dth, sdth);
+        aBnu += draw;
+        aBth += sdth;
+      }
+    }
+    __syncthreads();
+    // G. dx = D dy per (token, 4 channels); d(drive columns) = d(raw drive) of the token's
+    // mode pair.
+    if (tA < nt) {
+      const int t = tA, f0 = 4 * npA, na = 2 * npA;
+      const float4 dv = *reinterpret_cast<const float4*>(reinterpret_cast<const char*>(sm + TcBLay::dyt) +
+                                                         semx::tc::sw128(row0 + t, npA));
+      float4 acc;
+      acc.x = sm[TcBLay::Dp + f0] * dv.x;
+      acc.y = sm[TcBLay::Dp + f0 + 1] * dv.y;
+      acc.z = sm[TcBLay::Dp + f0 + 2] * dv.z;
+      acc.w = sm[TcBLay::Dp + f0 + 3] * dv.w;
+      const float2 g0 = db[t * HW + na], g1 = db[t * HW + na + 1];
+      const int64_t drow = (s * p.L + t0 + t) * p.P + cols.bx + 2 * na;
+      if ((p.vec & 16) != 0) {
+        __nv_bfloat162 qv[2] = {__floats2bfloat162_rn(g0.x, g0.y), __floats2bfloat162_rn(g1.x, g1.y)};
+        *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(p.dproj) + drow) = *reinterpret_cast<const uint2*>(qv);
+      } else {
+        st<true>(p.dproj, drow, g0.x);
+        st<true>(p.dproj, drow + 1, g0.y);
+        st<true>(p.dproj, drow + 2, g1.x);
+        st<true>(p.dproj, drow + 3, g1.y);
+      }
+      const int64_t xo = (s * p.L + t0 + t) * Fd + (int64_t)h * FH + f0;
+      if ((p.vec & 8) != 0) {
+        __nv_bfloat162 qv[2] = {__floats2bfloat162_rn(acc.x, acc.y), __floats2bfloat162_rn(acc.z, acc.w)};
+        *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(p.dx) + xo) = *reinterpret_cast<const uint2*>(qv);
+      } else {
+        st<true>(p.dx, xo, acc.x);
+        st<true>(p.dx, xo + 1, acc.y);
+        st<true>(p.dx, xo + 2, acc.z);
+        st<true>(p.dx, xo + 3, acc.w);
+      }
+    }
+    // H. Rank write: d s_b, d b_t.
+    if (R > 0 && tid < nt * R) {
+      const int t = tid / (R > 0 ? R : 1), r = tid % (R > 0 ? R : 1);
+      const float sbv = sbs[t * R + r];
+      const int64_t row = (s * p.L + t0 + t) * p.P;
+      float acc = 0.f;
+#pragma unroll
+      for (int n = 0; n < NH; ++n) {
+        const float g = db[t * HW + n].x;
+        acc = fmaf(static_cast<float>(bts[t * btw + r * NH + n]), g, acc);
+        st<true>(p.dproj, row + cols.bt + r * NH + n, sbv * g);
+      }
+      st<true>(p.dproj, row + cols.sb + r, acc);
+    }
+    // I. dC, dc_out and dD sums over the chunk, fixed ownership.
+    for (int t = 0; t < nt; ++t) {
+      {  // dC[fC, 4 nqC .. +3] += dy (h_re, -h_im)
+        const float dv = tcb_dy(sm, row0 + t, fC);
+        const float4 hre = *reinterpret_cast<const float4*>(htile + semx::tc::sw128(t, nqC));
+        const float4 hni = *reinterpret_cast<const float4*>(htile + semx::tc::sw128(t, nqC + 4));
+        aCr[0] = fmaf(dv, hre.x, aCr[0]);
+        aCr[1] = fmaf(dv, hre.y, aCr[1]);
+        aCr[2] = fmaf(dv, hre.z, aCr[2]);
+        aCr[3] = fmaf(dv, hre.w, aCr[3]);
+        aCi[0] = fmaf(dv, hni.x, aCi[0]);
+        aCi[1] = fmaf(dv, hni.y, aCi[1]);
+        aCi[2] = fmaf(dv, hni.z, aCi[2]);
+        aCi[3] = fmaf(dv, hni.w, aCi[3]);
+      }
+      if (R > 0) aO = fmaf(sm[TcBLay::sr + t * R + rO], tcb_dy(sm, row0 + t, fO), aO);
+      if (tid < FH) aD = fmaf(tcb_dy(sm, row0 + t, tid), static_cast<float>(xs[t * xw + tid]), aD);
+    }
+    if (k > 0) store_small<RK, CT>(p, sm + smlo[b ^ 1], CT, pre);
+    // Every thread is past its reads of the chunk's dy rows: refill them with the same
+    // chunk of the previous tile.
+    __syncthreads();
+    if (k >= 4) tcb_load_dy(p, sm, s, h, row0, (k - 4) * CT, CT);
+    cp_async_commit();
+  }
+  cp_async_wait_all();
+  __syncthreads();
+  const int64_t H = p.H;
+  float* row = p.part + s * p.K;
+  if (!bail) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int64_t i = ((int64_t)h * FH + fC) * NH + 4 * nqC + j;
+      row[2 * i] = aCr[j];
+      row[2 * i + 1] = aCi[j];
+    }
+    // Per-mode sums over the 16 token lanes that share a mode pair, fixed order.
+    float* red = sm + TcBLay::red;  // [3][NH][kT / 8]
+#pragma unroll
+    for (int dn = 0; dn < 2; ++dn) {
+      const int n = 2 * npA + dn;
+      red[(0 * NH + n) * (kT / 8) + tA] = acc_a[dn];
+      red[(1 * NH + n) * (kT / 8) + tA] = acc_om[dn];
+      red[(2 * NH + n) * (kT / 8) + tA] = acc_sd[dn];
+    }
+    if (npA == 0) {
+      sm[TcBLay::rb + tA] = aBnu;
+      sm[TcBLay::rb + kT / 8 + tA] = aBth;
+    }
+    __syncthreads();
+    // Partial row of sequence s: [dC | dcout | dD | dA_log | domega | ddetune | d dt bias].
+    int64_t off = H * FH * NH * 2;
+    if (R > 0) {
+      row[off + (int64_t)h * R * FH + rO * FH + fO] = aO;
+      off += H * R * FH;
+    }
+    if (tid < FH) row[off + (int64_t)h * FH + tid] = aD;
+    off += H * FH;
+    if (tid < 3 * NH) {
+      const int which = tid / NH, n = tid % NH;
+      float acc = 0.f;
+      for (int qq = 0; qq < kT / 8; ++qq) acc += red[(which * NH + n) * (kT / 8) + qq];
+      if (which == 0) acc *= sm[TcBLay::prm + n];  // d/dA_log = a d/da
+      row[off + which * H * NH + (int64_t)h * NH + n] = acc;
+    }
+    off += 3 * H * NH;
+    if (tid < 2) {
+      float acc = 0.f;
+      for (int qq = 0; qq < kT / 8; ++qq) acc += sm[TcBLay::rb + tid * (kT / 8) + qq];
+      row[off + tid * H + h] = acc;
+    }
+  } else if (adj_pending) {
+    // After a give-up, let the outstanding MMA finish (bounded) before the tensor memory
+    // it writes is released.
+    semx::tc::mbar_wait(bar_adj, ph_adj, kTcWaitLimit);
+  }
+  semx::tc::fence_before_sync();
+  __syncthreads();
+  if (tid < 32) semx::tc::tmem_dealloc(taddr, 32);
+}
+
 // ------------------------------------------------------------------------ host side
 int64_t proj_width(const SemxMimoLayerArgs* a) {
   return 2 * a->H + (a->rank > 0 ? 2 * a->H * a->rank + 3 * a->H * a->rank * a->Nh : 0) + 2 * a->H * a->Nh;
@@ -1757,7 +2269,12 @@ bool fwd_tc(const SemxMimoLayerArgs* a) {
   return bwd16(a) && a->bf16 && !a->envelope && semx::aligned(a->y, 16) && semx::aligned(a->x, 16);
 }
 
+// The bf16 backward of those heads without the envelope readout runs its contractions on
+// the tensor cores (mimo_layer_bwd_tc_kernel).
+bool bwd_tc(const SemxMimoLayerArgs* a) { return bwd16(a) && a->bf16 && !a->envelope; }
+
 size_t layer_smem(const SemxMimoLayerArgs* a, bool bwd) {
+  if (bwd && bwd_tc(a)) return (size_t)TcBLay::total * sizeof(float);
   if (bwd && bwd16(a)) return (size_t)make_blay(a->rank, a->envelope != 0, a->bf16 ? 2 : 4).total * sizeof(float);
   if (!bwd && fwd_tc(a)) return (size_t)TcLay::total * sizeof(float);
   if (!bwd)
@@ -1929,7 +2446,10 @@ int semx_mimo_layer_bwd(const SemxMimoLayerArgs* a, semx_stream_t stream) {
   p.part = ws;
   if (a->L > 0) {
     const size_t smem = layer_smem(a, true);
-    if (bwd16(a)) {
+    if (bwd_tc(a)) {
+      rc = a->rank == 4 ? launch_layer(mimo_layer_bwd_tc_kernel<4>, p, smem, st, "mimo_layer_bwd_tc_kernel")
+                        : launch_layer(mimo_layer_bwd_tc_kernel<0>, p, smem, st, "mimo_layer_bwd_tc_kernel");
+    } else if (bwd16(a)) {
       if (a->rank == 4)
         rc = a->bf16 ? launch_layer(mimo_layer_bwd16_kernel<true, 4>, p, smem, st, "mimo_layer_bwd16_kernel")
                      : launch_layer(mimo_layer_bwd16_kernel<false, 4>, p, smem, st, "mimo_layer_bwd16_kernel");

@@ -22,12 +22,14 @@ CASES = [
     ("linoss_fwd_kernel", "linoss", 16 * 256),
     ("linoss_bwd_kernel", "linoss", 24 * 256),
     ("slru_fwd_kernel", "slru real", 4 * (3 * 256 + 2 * 16)),
+    ("slru_fwd_real16_kernel", "slru real", 4 * (3 * 256 + 2 * 16)),
     ("slru_bwd_kernel", "slru real", 4 * (5 * 256 + 4 * 16)),
     ("slru_fwd_kernel", "slru complex", 4 * (4 * 256 + 4 * 16)),
     ("slru_bwd_kernel", "slru complex", 4 * (7 * 256 + 8 * 16)),
     ("mimo_layer_fwd_kernel", "mimo", 5280),
     ("mimo_layer_fwd_tc_kernel", "mimo", 5280),
     ("mimo_layer_bwd16_kernel", "mimo", 9536),
+    ("mimo_layer_bwd_tc_kernel", "mimo", 9536),
     ("mimo_fwd_kernel", "ops", 24 * 128 + 8 * 256),
     ("mimo_bwd_kernel", "ops", 40 * 128 + 12 * 256),
     ("cscan_fwd_kernel", "ops_cscan", 24 * 128),

@@ -1406,6 +1406,8 @@ __global__ void __launch_bounds__(kT) mimo_layer_bwd16_kernel(const LParams p) {
   const float2 bias = dt_bias(p, h);
 
   const int nck = p.nck;
+  float2 ck_next = make_float2(0.f, 0.f);  // the next chunk's checkpoint (threads < NH)
+  if (tid < NH && nck > 0) ck_next = reinterpret_cast<const float2*>(p.ckpt)[((s * nck + nck - 1) * p.H + h) * NH + tid];
   float pre[kPre];
   auto stage = [&](int k, int b) {
     const int t0 = k * CT, nt = min(CT, L - t0);
@@ -1452,11 +1454,12 @@ __global__ void __launch_bounds__(kT) mimo_layer_bwd16_kernel(const LParams p) {
     const float* scs = sbs + CT * R;
     const int xw = l.xw, bxw = l.bxw, btw = l.btw, ctw = l.ctw, dyw = l.dyw;
 
-    // A. Poles, gains, raw and gained drive per (token, mode pair); entry state.
+    // A. Poles, gains, raw and gained drive per (token, mode pair); entry state (loaded a
+    // chunk ahead).
     if (tid < NH) {
-      const float2 c = reinterpret_cast<const float2*>(p.ckpt)[((s * nck + k) * p.H + h) * NH + tid];
-      cin[tid] = c;
-      hs[tid] = c;
+      cin[tid] = ck_next;
+      hs[tid] = ck_next;
+      if (k > 0) ck_next = reinterpret_cast<const float2*>(p.ckpt)[((s * nck + k - 1) * p.H + h) * NH + tid];
     }
     if (tA < nt) {
       const int t = tA, na = 2 * npA;
@@ -1891,6 +1894,8 @@ __global__ void __launch_bounds__(kT, 5) mimo_layer_bwd_tc_kernel(const LParams 
   const int nck = p.nck;
   uint32_t ph_adj = 0;
   bool bail = false, adj_pending = false;
+  float2 ck_next = make_float2(0.f, 0.f);  // the next chunk's checkpoint (threads < NH)
+  if (tid < NH && nck > 0) ck_next = reinterpret_cast<const float2*>(p.ckpt)[((s * nck + nck - 1) * p.H + h) * NH + tid];
   float pre[kPre];
   auto stage = [&](int k, int b) {
     const int t0 = k * CT, nt = min(CT, L - t0);
@@ -1948,11 +1953,12 @@ __global__ void __launch_bounds__(kT, 5) mimo_layer_bwd_tc_kernel(const LParams 
     const float* scs = sbs + CT * R;
     const int xw = fl.xw, bxw = fl.bxw, btw = fl.btw, ctw = fl.ctw;
 
-    // A. Poles, raw and gained drive per (token, mode pair); entry state.
+    // A. Poles, raw and gained drive per (token, mode pair); entry state (loaded a chunk
+    // ahead, so the load's latency is not waited for here).
     if (tid < NH) {
-      const float2 c = reinterpret_cast<const float2*>(p.ckpt)[((s * nck + k) * p.H + h) * NH + tid];
-      cin[tid] = c;
-      hent[tid] = c;
+      cin[tid] = ck_next;
+      hent[tid] = ck_next;
+      if (k > 0) ck_next = reinterpret_cast<const float2*>(p.ckpt)[((s * nck + k - 1) * p.H + h) * NH + tid];
     }
     if (tA < nt) {
       const int t = tA, na = 2 * npA;

@@ -244,7 +244,7 @@ __device__ void stage_chunk(const LParams& p, const Lay& l, float* sm, int64_t s
   }
   if (R > 0) {
     for (int i = threadIdx.x; i < nt * R; i += kT) {
-      const int t = i / R, r = i % R;
+      const int t = i / (R > 0 ? R : 1), r = i % (R > 0 ? R : 1);
       const int64_t row = (s * p.L + t0 + t) * p.P;
       sm[l.sb + i] = ld<BF16>(p.proj, row + c.sb + r);
       sm[l.sc + i] = ld<BF16>(p.proj, row + c.sc + r);
@@ -381,15 +381,19 @@ __device__ __forceinline__ void stage_bulk(const LParams& p, const FLay& l, void
 }
 
 // Small per-token operands [dnu_raw, dth, s_b (R), s_c (R)] of chunk [t0, t0 + nt): item q
-// of this thread is i = tid + q kT over nt (2 + 2R) values.
+// of this thread is i = tid + q kT over nt (2 + 2R) values. With the rank known at compile
+// time, the loops run only the ceil(CT (2 + 2R) / kT) items a thread can own.
 constexpr int kPre = 9;
-template <bool BF16, int RK>
+__host__ __device__ constexpr int npre(int CT, int RK) {
+  return RK >= 0 && (CT * (2 + 2 * RK) + kT - 1) / kT < kPre ? (CT * (2 + 2 * RK) + kT - 1) / kT : kPre;
+}
+template <bool BF16, int RK, int CT = kTC>
 __device__ __forceinline__ void load_small(const LParams& p, int64_t s, int h, int t0, int nt, float2 bias,
                                            float (&pre)[kPre]) {
   const int R = RK >= 0 ? RK : (int)p.R, w = 2 + 2 * R;
   const Cols c = cols_of(p, h);
 #pragma unroll
-  for (int q = 0; q < kPre; ++q) {
+  for (int q = 0; q < npre(CT, RK); ++q) {
     const int i = threadIdx.x + q * kT;
     if (i < nt * w) {
       const int t = i / w, j = i % w;
@@ -404,7 +408,7 @@ template <int RK, int CT = kTC>
 __device__ __forceinline__ void store_small(const LParams& p, float* sml, int nt, const float (&pre)[kPre]) {
   const int R = RK >= 0 ? RK : (int)p.R, w = 2 + 2 * R;
 #pragma unroll
-  for (int q = 0; q < kPre; ++q) {
+  for (int q = 0; q < npre(CT, RK); ++q) {
     const int i = threadIdx.x + q * kT;
     if (i < nt * w) {
       const int t = i / w, j = i % w;
@@ -583,7 +587,7 @@ __global__ void __launch_bounds__(kT) mimo_layer_fwd_kernel(const LParams p) {
   if (nchunks > 0) {
     const int nt0 = min(CT, L);
     stage_bulk<BF16, NH, FH, RK>(p, l, sm + l.stg[0], s, h, 0, nt0);
-    load_small<BF16, RK>(p, s, h, 0, nt0, bias, pre);
+    load_small<BF16, RK, CT>(p, s, h, 0, nt0, bias, pre);
     store_small<RK, CT>(p, sm + l.sml[0], nt0, pre);
   }
   cp_async_commit();
@@ -595,7 +599,7 @@ __global__ void __launch_bounds__(kT) mimo_layer_fwd_kernel(const LParams p) {
     __syncthreads();
     if (k + 1 < nchunks) {
       stage_bulk<BF16, NH, FH, RK>(p, l, sm + l.stg[b ^ 1], s, h, t0n, ntn);
-      load_small<BF16, RK>(p, s, h, t0n, ntn, bias, pre);
+      load_small<BF16, RK, CT>(p, s, h, t0n, ntn, bias, pre);
     }
     cp_async_commit();
     const T* xs = reinterpret_cast<const T*>(sm + l.stg[b]);
@@ -633,7 +637,7 @@ __global__ void __launch_bounds__(kT) mimo_layer_fwd_kernel(const LParams p) {
             hs[(m * kCk - 1) * hw + tid];
     if (R > 0) {
       for (int i = tid; i < nt * R; i += kT) {
-        const int t = i / R, r = i % R;
+        const int t = i / (R > 0 ? R : 1), r = i % (R > 0 ? R : 1);
         const T* cr = cts + t * ctw + r * 2 * Nh;
         float acc = 0.f;
         for (int n = 0; n < Nh; ++n) {
@@ -853,7 +857,7 @@ __global__ void __launch_bounds__(kT, 6) mimo_layer_fwd_tc_kernel(const LParams 
   if (nchunks > 0) {
     const int nt0 = min(CT, L);
     stage_bulk<true, NH, FH, RK>(p, l, sm + stg[0], s, h, 0, nt0);
-    load_small<true, RK>(p, s, h, 0, nt0, bias, pre);
+    load_small<true, RK, CT>(p, s, h, 0, nt0, bias, pre);
     store_small<RK, CT>(p, sm + sml_off[0], nt0, pre);
   }
   cp_async_commit();
@@ -865,9 +869,16 @@ __global__ void __launch_bounds__(kT, 6) mimo_layer_fwd_tc_kernel(const LParams 
     __syncthreads();
     if (k + 1 < nchunks) {
       stage_bulk<true, NH, FH, RK>(p, l, sm + stg[b ^ 1], s, h, t0n, ntn);
-      load_small<true, RK>(p, s, h, t0n, ntn, bias, pre);
+      load_small<true, RK, CT>(p, s, h, t0n, ntn, bias, pre);
     }
     cp_async_commit();
+    if (q == 0 && pending >= 0) {
+      // The x rows the pending tile's epilogue reads after this chunk's poles: into L1 now.
+      const int lane = tid & 31, tg = (pending - 3) * CT + 16 * (tid >> 5) + lane;
+      if (lane < 16 && tg < L)
+        asm volatile("prefetch.global.L1 [%0];" ::"l"(reinterpret_cast<const __nv_bfloat16*>(p.x) +
+                                                      (s * p.L + tg) * p.H * 32 + (int64_t)h * 32));
+    }
     const T* xs = reinterpret_cast<const T*>(sm + stg[b]);
     const T* bxs = xs + CT * l.xw;
     const T* bts = bxs + CT * l.bxw;
@@ -1031,7 +1042,7 @@ __global__ void __launch_bounds__(kT) mimo_layer_bwd_kernel(const LParams p) {
     // Rank read and its adjoint per (t, r).
     if (R > 0) {
       for (int i = tid; i < nt * R; i += kT) {
-        const int t = i / R, r = i % R;
+        const int t = i / (R > 0 ? R : 1), r = i % (R > 0 ? R : 1);
         const float* cr = sm + l.ct + (t * R + r) * 2 * Nh;
         float rd = 0.f;
         for (int n = 0; n < Nh; ++n) {
@@ -1159,7 +1170,7 @@ __global__ void __launch_bounds__(kT) mimo_layer_bwd_kernel(const LParams p) {
     // Rank write: d s_b, d b_t.
     if (R > 0) {
       for (int i = tid; i < nt * R; i += kT) {
-        const int t = i / R, r = i % R;
+        const int t = i / (R > 0 ? R : 1), r = i % (R > 0 ? R : 1);
         float acc = 0.f;
         for (int n = 0; n < Nh; ++n) acc = fmaf(sm[l.bt + (t * R + r) * Nh + n], db[t * Nh + n].x, acc);
         st<BF16>(p.dproj, (s * p.L + t0 + t) * p.P + cols.sb + r, acc);
@@ -1357,7 +1368,7 @@ __host__ __device__ inline BLay make_blay(int R, bool env, int es) {
 }
 
 template <bool BF16, int RK>
-__global__ void __launch_bounds__(kT) mimo_layer_bwd16_kernel(const LParams p) {
+__global__ void __launch_bounds__(kT, 5) mimo_layer_bwd16_kernel(const LParams p) {
   using T = typename std::conditional<BF16, __nv_bfloat16, float>::type;
   constexpr int NH = kB_NH, FH = kB_FH, CT = kB_CT, HW = kB_HW, R = RK;
   extern __shared__ float4 smem4[];
@@ -1427,7 +1438,7 @@ __global__ void __launch_bounds__(kT) mimo_layer_bwd16_kernel(const LParams p) {
   if (nck > 0) {
     const int k = nck - 1, nt = min(CT, L - k * CT);
     stage(k, 0);
-    load_small<BF16, RK>(p, s, h, k * CT, nt, bias, pre);
+    load_small<BF16, RK, CT>(p, s, h, k * CT, nt, bias, pre);
     store_small<RK, CT>(p, sm + l.sml[0], nt, pre);
   }
   cp_async_commit();
@@ -1438,7 +1449,7 @@ __global__ void __launch_bounds__(kT) mimo_layer_bwd16_kernel(const LParams p) {
     __syncthreads();
     if (k > 0) {
       stage(k - 1, b ^ 1);
-      load_small<BF16, RK>(p, s, h, (k - 1) * CT, CT, bias, pre);
+      load_small<BF16, RK, CT>(p, s, h, (k - 1) * CT, CT, bias, pre);
     }
     cp_async_commit();
     const T* xs = reinterpret_cast<const T*>(sm + l.stg[b]);
@@ -1490,7 +1501,7 @@ __global__ void __launch_bounds__(kT) mimo_layer_bwd16_kernel(const LParams p) {
     // C. Rank read and its adjoint per (token, rank).
     if (R > 0) {
       if (tid < nt * R) {
-        const int t = tid / R, r = tid % R;
+        const int t = tid / (R > 0 ? R : 1), r = tid % (R > 0 ? R : 1);
         const T* cr = cts + t * ctw + r * 2 * NH;
         float rd = 0.f;
 #pragma unroll
@@ -1654,7 +1665,7 @@ __global__ void __launch_bounds__(kT) mimo_layer_bwd16_kernel(const LParams p) {
     }
     // H. Rank write: d s_b, d b_t.
     if (R > 0 && tid < nt * R) {
-      const int t = tid / R, r = tid % R;
+      const int t = tid / (R > 0 ? R : 1), r = tid % (R > 0 ? R : 1);
       const float sbv = sbs[t * R + r];
       const int64_t row = (s * p.L + t0 + t) * p.P;
       float acc = 0.f;
@@ -1904,7 +1915,7 @@ __global__ void __launch_bounds__(kT, 5) mimo_layer_bwd_tc_kernel(const LParams 
   if (nck > 0) {
     const int k = nck - 1, nt = min(CT, L - k * CT);
     stage(k, 0);
-    load_small<true, RK>(p, s, h, k * CT, nt, bias, pre);
+    load_small<true, RK, CT>(p, s, h, k * CT, nt, bias, pre);
     store_small<RK, CT>(p, sm + smlo[0], nt, pre);
     // dy of the last tile, and of the previous tile's chunks whose rows the last tile
     // does not use.
@@ -1938,7 +1949,7 @@ __global__ void __launch_bounds__(kT, 5) mimo_layer_bwd_tc_kernel(const LParams 
     adj_pending = adj_pending || tile_start;
     if (k > 0) {
       stage(k - 1, b ^ 1);
-      load_small<true, RK>(p, s, h, (k - 1) * CT, CT, bias, pre);
+      load_small<true, RK, CT>(p, s, h, (k - 1) * CT, CT, bias, pre);
     }
     cp_async_commit();
     const T* xs = reinterpret_cast<const T*>(sm + stg[b]);

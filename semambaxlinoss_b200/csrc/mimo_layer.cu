@@ -381,19 +381,15 @@ __device__ __forceinline__ void stage_bulk(const LParams& p, const FLay& l, void
 }
 
 // Small per-token operands [dnu_raw, dth, s_b (R), s_c (R)] of chunk [t0, t0 + nt): item q
-// of this thread is i = tid + q kT over nt (2 + 2R) values. With the rank known at compile
-// time, the loops run only the ceil(CT (2 + 2R) / kT) items a thread can own.
+// of this thread is i = tid + q kT over nt (2 + 2R) values.
 constexpr int kPre = 9;
-__host__ __device__ constexpr int npre(int CT, int RK) {
-  return RK >= 0 && (CT * (2 + 2 * RK) + kT - 1) / kT < kPre ? (CT * (2 + 2 * RK) + kT - 1) / kT : kPre;
-}
-template <bool BF16, int RK, int CT = kTC>
+template <bool BF16, int RK>
 __device__ __forceinline__ void load_small(const LParams& p, int64_t s, int h, int t0, int nt, float2 bias,
                                            float (&pre)[kPre]) {
   const int R = RK >= 0 ? RK : (int)p.R, w = 2 + 2 * R;
   const Cols c = cols_of(p, h);
 #pragma unroll
-  for (int q = 0; q < npre(CT, RK); ++q) {
+  for (int q = 0; q < kPre; ++q) {
     const int i = threadIdx.x + q * kT;
     if (i < nt * w) {
       const int t = i / w, j = i % w;
@@ -408,7 +404,7 @@ template <int RK, int CT = kTC>
 __device__ __forceinline__ void store_small(const LParams& p, float* sml, int nt, const float (&pre)[kPre]) {
   const int R = RK >= 0 ? RK : (int)p.R, w = 2 + 2 * R;
 #pragma unroll
-  for (int q = 0; q < npre(CT, RK); ++q) {
+  for (int q = 0; q < kPre; ++q) {
     const int i = threadIdx.x + q * kT;
     if (i < nt * w) {
       const int t = i / w, j = i % w;
@@ -587,7 +583,7 @@ __global__ void __launch_bounds__(kT) mimo_layer_fwd_kernel(const LParams p) {
   if (nchunks > 0) {
     const int nt0 = min(CT, L);
     stage_bulk<BF16, NH, FH, RK>(p, l, sm + l.stg[0], s, h, 0, nt0);
-    load_small<BF16, RK, CT>(p, s, h, 0, nt0, bias, pre);
+    load_small<BF16, RK>(p, s, h, 0, nt0, bias, pre);
     store_small<RK, CT>(p, sm + l.sml[0], nt0, pre);
   }
   cp_async_commit();
@@ -599,7 +595,7 @@ __global__ void __launch_bounds__(kT) mimo_layer_fwd_kernel(const LParams p) {
     __syncthreads();
     if (k + 1 < nchunks) {
       stage_bulk<BF16, NH, FH, RK>(p, l, sm + l.stg[b ^ 1], s, h, t0n, ntn);
-      load_small<BF16, RK, CT>(p, s, h, t0n, ntn, bias, pre);
+      load_small<BF16, RK>(p, s, h, t0n, ntn, bias, pre);
     }
     cp_async_commit();
     const T* xs = reinterpret_cast<const T*>(sm + l.stg[b]);
@@ -857,7 +853,7 @@ __global__ void __launch_bounds__(kT, 6) mimo_layer_fwd_tc_kernel(const LParams 
   if (nchunks > 0) {
     const int nt0 = min(CT, L);
     stage_bulk<true, NH, FH, RK>(p, l, sm + stg[0], s, h, 0, nt0);
-    load_small<true, RK, CT>(p, s, h, 0, nt0, bias, pre);
+    load_small<true, RK>(p, s, h, 0, nt0, bias, pre);
     store_small<RK, CT>(p, sm + sml_off[0], nt0, pre);
   }
   cp_async_commit();
@@ -869,16 +865,9 @@ __global__ void __launch_bounds__(kT, 6) mimo_layer_fwd_tc_kernel(const LParams 
     __syncthreads();
     if (k + 1 < nchunks) {
       stage_bulk<true, NH, FH, RK>(p, l, sm + stg[b ^ 1], s, h, t0n, ntn);
-      load_small<true, RK, CT>(p, s, h, t0n, ntn, bias, pre);
+      load_small<true, RK>(p, s, h, t0n, ntn, bias, pre);
     }
     cp_async_commit();
-    if (q == 0 && pending >= 0) {
-      // The x rows the pending tile's epilogue reads after this chunk's poles: into L1 now.
-      const int lane = tid & 31, tg = (pending - 3) * CT + 16 * (tid >> 5) + lane;
-      if (lane < 16 && tg < L)
-        asm volatile("prefetch.global.L1 [%0];" ::"l"(reinterpret_cast<const __nv_bfloat16*>(p.x) +
-                                                      (s * p.L + tg) * p.H * 32 + (int64_t)h * 32));
-    }
     const T* xs = reinterpret_cast<const T*>(sm + stg[b]);
     const T* bxs = xs + CT * l.xw;
     const T* bts = bxs + CT * l.bxw;
@@ -1368,7 +1357,7 @@ __host__ __device__ inline BLay make_blay(int R, bool env, int es) {
 }
 
 template <bool BF16, int RK>
-__global__ void __launch_bounds__(kT, 5) mimo_layer_bwd16_kernel(const LParams p) {
+__global__ void __launch_bounds__(kT) mimo_layer_bwd16_kernel(const LParams p) {
   using T = typename std::conditional<BF16, __nv_bfloat16, float>::type;
   constexpr int NH = kB_NH, FH = kB_FH, CT = kB_CT, HW = kB_HW, R = RK;
   extern __shared__ float4 smem4[];
@@ -1417,8 +1406,6 @@ __global__ void __launch_bounds__(kT, 5) mimo_layer_bwd16_kernel(const LParams p
   const float2 bias = dt_bias(p, h);
 
   const int nck = p.nck;
-  float2 ck_next = make_float2(0.f, 0.f);  // the next chunk's checkpoint (threads < NH)
-  if (tid < NH && nck > 0) ck_next = reinterpret_cast<const float2*>(p.ckpt)[((s * nck + nck - 1) * p.H + h) * NH + tid];
   float pre[kPre];
   auto stage = [&](int k, int b) {
     const int t0 = k * CT, nt = min(CT, L - t0);
@@ -1438,7 +1425,7 @@ __global__ void __launch_bounds__(kT, 5) mimo_layer_bwd16_kernel(const LParams p
   if (nck > 0) {
     const int k = nck - 1, nt = min(CT, L - k * CT);
     stage(k, 0);
-    load_small<BF16, RK, CT>(p, s, h, k * CT, nt, bias, pre);
+    load_small<BF16, RK>(p, s, h, k * CT, nt, bias, pre);
     store_small<RK, CT>(p, sm + l.sml[0], nt, pre);
   }
   cp_async_commit();
@@ -1449,7 +1436,7 @@ __global__ void __launch_bounds__(kT, 5) mimo_layer_bwd16_kernel(const LParams p
     __syncthreads();
     if (k > 0) {
       stage(k - 1, b ^ 1);
-      load_small<BF16, RK, CT>(p, s, h, (k - 1) * CT, CT, bias, pre);
+      load_small<BF16, RK>(p, s, h, (k - 1) * CT, CT, bias, pre);
     }
     cp_async_commit();
     const T* xs = reinterpret_cast<const T*>(sm + l.stg[b]);
@@ -1465,12 +1452,11 @@ __global__ void __launch_bounds__(kT, 5) mimo_layer_bwd16_kernel(const LParams p
     const float* scs = sbs + CT * R;
     const int xw = l.xw, bxw = l.bxw, btw = l.btw, ctw = l.ctw, dyw = l.dyw;
 
-    // A. Poles, gains, raw and gained drive per (token, mode pair); entry state (loaded a
-    // chunk ahead).
+    // A. Poles, gains, raw and gained drive per (token, mode pair); entry state.
     if (tid < NH) {
-      cin[tid] = ck_next;
-      hs[tid] = ck_next;
-      if (k > 0) ck_next = reinterpret_cast<const float2*>(p.ckpt)[((s * nck + k - 1) * p.H + h) * NH + tid];
+      const float2 c = reinterpret_cast<const float2*>(p.ckpt)[((s * nck + k) * p.H + h) * NH + tid];
+      cin[tid] = c;
+      hs[tid] = c;
     }
     if (tA < nt) {
       const int t = tA, na = 2 * npA;
@@ -1905,8 +1891,6 @@ __global__ void __launch_bounds__(kT, 5) mimo_layer_bwd_tc_kernel(const LParams 
   const int nck = p.nck;
   uint32_t ph_adj = 0;
   bool bail = false, adj_pending = false;
-  float2 ck_next = make_float2(0.f, 0.f);  // the next chunk's checkpoint (threads < NH)
-  if (tid < NH && nck > 0) ck_next = reinterpret_cast<const float2*>(p.ckpt)[((s * nck + nck - 1) * p.H + h) * NH + tid];
   float pre[kPre];
   auto stage = [&](int k, int b) {
     const int t0 = k * CT, nt = min(CT, L - t0);
@@ -1915,7 +1899,7 @@ __global__ void __launch_bounds__(kT, 5) mimo_layer_bwd_tc_kernel(const LParams 
   if (nck > 0) {
     const int k = nck - 1, nt = min(CT, L - k * CT);
     stage(k, 0);
-    load_small<true, RK, CT>(p, s, h, k * CT, nt, bias, pre);
+    load_small<true, RK>(p, s, h, k * CT, nt, bias, pre);
     store_small<RK, CT>(p, sm + smlo[0], nt, pre);
     // dy of the last tile, and of the previous tile's chunks whose rows the last tile
     // does not use.
@@ -1949,7 +1933,7 @@ __global__ void __launch_bounds__(kT, 5) mimo_layer_bwd_tc_kernel(const LParams 
     adj_pending = adj_pending || tile_start;
     if (k > 0) {
       stage(k - 1, b ^ 1);
-      load_small<true, RK, CT>(p, s, h, (k - 1) * CT, CT, bias, pre);
+      load_small<true, RK>(p, s, h, (k - 1) * CT, CT, bias, pre);
     }
     cp_async_commit();
     const T* xs = reinterpret_cast<const T*>(sm + stg[b]);
@@ -1964,12 +1948,11 @@ __global__ void __launch_bounds__(kT, 5) mimo_layer_bwd_tc_kernel(const LParams 
     const float* scs = sbs + CT * R;
     const int xw = fl.xw, bxw = fl.bxw, btw = fl.btw, ctw = fl.ctw;
 
-    // A. Poles, raw and gained drive per (token, mode pair); entry state (loaded a chunk
-    // ahead, so the load's latency is not waited for here).
+    // A. Poles, raw and gained drive per (token, mode pair); entry state.
     if (tid < NH) {
-      cin[tid] = ck_next;
-      hent[tid] = ck_next;
-      if (k > 0) ck_next = reinterpret_cast<const float2*>(p.ckpt)[((s * nck + k - 1) * p.H + h) * NH + tid];
+      const float2 c = reinterpret_cast<const float2*>(p.ckpt)[((s * nck + k) * p.H + h) * NH + tid];
+      cin[tid] = c;
+      hent[tid] = c;
     }
     if (tA < nt) {
       const int t = tA, na = 2 * npA;

@@ -248,6 +248,8 @@ def _bf16_layer_reference(m, cfg, x, gy, proj):
               ("c_coef", H * r), ("c_read", 2 * H * r * Nh)]
     o = 0
     for name, rows in blocks:
+        if rows == 0:  # rank 0: no rank projections
+            continue
         ref[f"d{name}.weight"] = dW[o:o + rows]
         if name.startswith("dt_"):
             ref[f"d{name}.bias"] = dproj[..., o:o + rows].sum((0, 1))
@@ -280,6 +282,41 @@ def test_fused_layer_bf16_inputs():
     with torch.no_grad():
         W, _ = m._projection()
         proj = F.linear(x.to(dev), W.to(torch.bfloat16)).double().cpu()
+    ref = _bf16_layer_reference(m, cfg, x, gy, proj)
+    for k in ref:
+        assert_close(out[k], ref[k], BF16_TOL, k)
+    assert _lib.tc_timeouts() == 0
+
+
+@pytest.mark.parametrize("extra", [dict(rank=0), dict(rank=4, mode_detune=True), dict(rank=0, mode_detune=True),
+                                   dict(rank=4, envelope_readout=True)])
+def test_bf16_layer_variants(extra):
+    """The bf16 16-mode x 32-channel layer beyond rank 4: rank 0, mode detune and the
+    envelope readout (the tensor-core kernels serve every case but the envelope, which
+    runs the CUDA-core kernels), 2 x 83 tokens (a partial 64-token tile and chunk),
+    against the float64 oracle on the GPU's own projection rows, within the bf16-input
+    tolerance."""
+    import torch.nn.functional as F
+
+    from semambaxlinoss_b200.selective_lru import SelectiveLRUMIMO
+
+    cfg = dict(in_features=256, state_dim=128, n_heads=8, input_gain="gamma", **extra)
+    torch.manual_seed(31)
+    m = SelectiveLRUMIMO(**cfg)
+    g = gen(32)
+    with torch.no_grad():
+        for p_ in m.parameters():
+            p_.add_((0.05 * torch.randn(p_.shape, generator=g)).to(p_.dtype))
+        m.dt_nu_proj.bias.fill_(-2.0)
+        m.omega.copy_(torch.randn(m.omega.shape, generator=g) * 3.0)
+        if extra.get("envelope_readout"):
+            m.env_gain.copy_(torch.randn(m.env_gain.shape, generator=g) * 0.1)
+    x = randn((2, 83, 256), g, scale=0.5).to(torch.bfloat16)
+    gy = randn((2, 83, 256), g)
+    out = _layer_gpu(m, x, gy, torch.bfloat16)
+    with torch.no_grad():
+        W, _ = m._projection()
+        proj = F.linear(x.to(cuda()), W.to(torch.bfloat16)).double().cpu()
     ref = _bf16_layer_reference(m, cfg, x, gy, proj)
     for k in ref:
         assert_close(out[k], ref[k], BF16_TOL, k)

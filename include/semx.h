@@ -41,7 +41,7 @@
 extern "C" {
 #endif
 
-#define SEMX_ABI_VERSION 1
+#define SEMX_ABI_VERSION 2
 
 typedef void* semx_stream_t; /* cudaStream_t */
 
@@ -135,6 +135,9 @@ typedef struct SemxLinossArgs {
   float* dM;        /* GENERIC (4,P)           */
   float* dparams;   /* fused (3,P)             */
   void* workspace;  /* semx_linoss_workspace_bytes() bytes, backward only */
+  int32_t reverse;  /* 1: step t of a sequence is element L-1-t of its (L,P) block, i.e.
+                       the scan runs backwards in time over the stored order (replaces
+                       flipping the input and the output); 0: forward */
 } SemxLinossArgs;
 
 size_t semx_linoss_args_size(void);
@@ -242,6 +245,19 @@ typedef struct SemxSelectiveLruArgs {
   float* dh0_re;
   float* dh0_im;
   void* workspace; /* semx_selective_lru_workspace_bytes(), backward only */
+  /* Token layout (all zero: the documented (S,L,X) layout). Every per-step operand,
+   * output and gradient is a matrix of S*L token rows; step t of sequence s is row
+   *   (s / G) * group_stride + (s % G) * seq_stride + t' * step_stride,
+   * t' = reverse ? L-1-t : t, with G = seq_group (0 = 1), group_stride (0 = L) and
+   * step_stride (0 = 1). Example: activations laid out (B, T, F, X) scanned along T
+   * over the B*F sequences: G = F, group_stride = T*F, seq_stride = 1, step_stride = F
+   * (no transposed copy). The map must send the S*L pairs (s, t) to distinct rows below
+   * S*L (checked: S % G == 0, S and G below 2^31, and the largest row index; a map that
+   * sends two tokens to one row is not detected and gives undefined results, with every
+   * access still inside the rows). Checkpoints and the final state keep their
+   * documented (sequence-major) layouts. */
+  int32_t reverse;
+  int64_t seq_group, group_stride, seq_stride, step_stride;
 } SemxSelectiveLruArgs;
 
 size_t semx_selective_lru_args_size(void);
@@ -420,6 +436,11 @@ typedef struct SemxConvSiluArgs {
   float* dw; /* (C, K) */
   float* db; /* (C), may be NULL */
   void* workspace;
+  /* Token layout of xz, v, dv, dxz: as SemxSelectiveLruArgs (reverse: the convolution's
+   * window looks at the following steps of the stored order, i.e. the causal convolution
+   * of the time-reversed sequence). */
+  int32_t reverse;
+  int64_t seq_group, group_stride, seq_stride, step_stride;
 } SemxConvSiluArgs;
 
 typedef struct SemxGateSiluArgs {

@@ -18,7 +18,7 @@ import os
 # The in-tree library; SEMX_LIB may name another build of the same ABI (e.g. to compare
 # builds side by side).
 LIB_PATH = Path(os.environ.get("SEMX_LIB", Path(__file__).resolve().parent / "libsemx.so"))
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 c_f32p = ctypes.POINTER(ctypes.c_float)
 
@@ -76,11 +76,32 @@ class SemxLinossArgs(ctypes.Structure):
         ("dM", ctypes.c_void_p),
         ("dparams", ctypes.c_void_p),
         ("workspace", ctypes.c_void_p),
+        ("reverse", ctypes.c_int32),
     ]
 
 
 # enum semx_input_gain
 GAIN_CODES = {"gamma": 0, "mamba": 1, "zoh": 2, "none": 3}
+
+
+# Token layout fields shared by the selective-LRU and conv + SiLU argument structs.
+_LAYOUT_FIELDS = [
+    ("reverse", ctypes.c_int32),
+    ("seq_group", ctypes.c_int64),
+    ("group_stride", ctypes.c_int64),
+    ("seq_stride", ctypes.c_int64),
+    ("step_stride", ctypes.c_int64),
+]
+
+
+def set_layout(args, layout) -> None:
+    """Copies a TokenLayout (or None: the default sequence-major layout) into an argument
+    struct's layout fields."""
+    if layout is None:
+        return
+    args.reverse = int(layout.reverse)
+    args.seq_group, args.group_stride = layout.seq_group, layout.group_stride
+    args.seq_stride, args.step_stride = layout.seq_stride, layout.step_stride
 
 
 class SemxSelectiveLruArgs(ctypes.Structure):
@@ -98,7 +119,7 @@ class SemxSelectiveLruArgs(ctypes.Structure):
         "g", "s", "h0_re", "h0_im", "y", "hf_re", "hf_im", "ckpt", "dy", "dhf_re", "dhf_im",
         "d_delta_nu", "d_delta_theta", "dx", "dB_re", "dB_im", "dC_re", "dC_im", "da",
         "domega", "dD", "dg", "ds", "dh0_re", "dh0_im", "workspace",
-    )]
+    )] + _LAYOUT_FIELDS
 
 
 class SemxComplexScanArgs(ctypes.Structure):
@@ -162,7 +183,8 @@ class SemxConvSiluArgs(ctypes.Structure):
         ("L", ctypes.c_int64),
         ("C", ctypes.c_int64),
         ("ld", ctypes.c_int64),
-    ] + [(name, ctypes.c_void_p) for name in ("xz", "w", "b", "v", "dv", "dxz", "dw", "db", "workspace")]
+    ] + [(name, ctypes.c_void_p) for name in ("xz", "w", "b", "v", "dv", "dxz", "dw", "db", "workspace")] + \
+        _LAYOUT_FIELDS
 
 
 class SemxGateSiluArgs(ctypes.Structure):

@@ -77,6 +77,7 @@ struct Params {
   float* dM;
   float* dparams;
   float* part;  // (S, kPartials, P)
+  int rev;      // 1: step t of a chain is row L - 1 - t of its sequence (kernels take it as REV)
   // Checkpoint slot j of chain (s, o) at ckpt[(s * (nchunks + 1) + j) * P + o]: the state
   // entering chunk j; slot nchunks is the final state.
 };
@@ -202,7 +203,7 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
 }
 
-template <bool GENERIC>
+template <bool GENERIC, bool REV>
 __global__ void __launch_bounds__(kBlock) linoss_fwd_kernel(const Params p) {
   const int64_t gid = (int64_t)blockIdx.x * kBlock + threadIdx.x;
   if (gid >= p.S * p.P) return;
@@ -210,8 +211,8 @@ __global__ void __launch_bounds__(kBlock) linoss_fwd_kernel(const Params p) {
   const int o = (int)(gid - s * p.P);
   const Coef k = load_coef(p, o);
   const int L = (int)p.L;
-  const int P = (int)p.P;
-  const int64_t base = s * p.L * p.P + o;
+  const int P = REV ? -(int)p.P : (int)p.P;  // step stride; negative when scanning backwards
+  const int64_t base = s * p.L * p.P + o + (REV ? (p.L - 1) * p.P : 0);
   const float2* src1 = (GENERIC ? p.F1 : p.Bu) + base;
   const float2* src2 = GENERIC ? p.F2 + base : nullptr;
   float2* y2 = p.Y2 + base;
@@ -262,7 +263,7 @@ __device__ __forceinline__ void prefetch_sub(float2* in_buf, float2* dy_buf,
 }
 
 // The chains of thread block `blk` (kBlock consecutive chains).
-template <bool GENERIC>
+template <bool GENERIC, bool REV>
 __device__ __forceinline__ void bwd_block(const Params& p, int blk, float4* smem4) {
   constexpr int kIn = GENERIC ? 2 : 1;
   const int nsub_max = p.chunk / kSub;
@@ -277,8 +278,8 @@ __device__ __forceinline__ void bwd_block(const Params& p, int blk, float4* smem
   const int o = (int)(gid - s * p.P);
   const Coef k = load_coef(p, o);
   const int L = (int)p.L;
-  const int P = (int)p.P;
-  const int64_t base = s * p.L * p.P + o;
+  const int P = REV ? -(int)p.P : (int)p.P;  // step stride; negative when scanning backwards
+  const int64_t base = s * p.L * p.P + o + (REV ? (p.L - 1) * p.P : 0);
   const float2* src1 = (GENERIC ? p.F1 : p.Bu) + base;
   const float2* src2 = GENERIC ? p.F2 + base : nullptr;
   const float2* dys = p.dY2 + base;
@@ -421,6 +422,7 @@ __host__ __device__ inline size_t rev_smem_bytes() { return (size_t)2 * kStages 
 // Shared memory: in[kStages][kLook][kBlock], dy[kStages][kLook][kBlock] float2, per-thread
 // slots (no block barrier after the stability vote; a stage is refilled only by the
 // thread that consumed it in the previous batch).
+template <bool REV>
 __device__ __forceinline__ bool rev_block(const Params& p, float4* smem4) {
   float2* in_base = reinterpret_cast<float2*>(smem4);
   float2* dy_base = in_base + kStages * kLook * kBlock;
@@ -436,8 +438,8 @@ __device__ __forceinline__ bool rev_block(const Params& p, float4* smem4) {
   if (!__syncthreads_and(stable)) return false;
   if (!active) return true;
   const int L = (int)p.L;
-  const int P = (int)p.P;
-  const int64_t base = s * p.L * p.P + o;
+  const int P = REV ? -(int)p.P : (int)p.P;  // step stride; negative when scanning backwards
+  const int64_t base = s * p.L * p.P + o + (REV ? (p.L - 1) * p.P : 0);
   const float2* bu = p.Bu + base;
   const float2* dys = p.dY2 + base;
   float2* out = p.dBu + base;
@@ -523,11 +525,11 @@ __device__ __forceinline__ bool rev_block(const Params& p, float4* smem4) {
 }
 
 // One backward kernel for every variant (see the file comment).
-template <bool GENERIC>
+template <bool GENERIC, bool REV>
 __global__ void __launch_bounds__(kBlock, 4) linoss_bwd_kernel(const Params p) {
   extern __shared__ float4 smem4[];
-  if (!GENERIC && p.variant == SEMX_LINOSS_IMEX && rev_block(p, smem4)) return;
-  bwd_block<GENERIC>(p, (int)blockIdx.x, smem4);
+  if (!GENERIC && p.variant == SEMX_LINOSS_IMEX && rev_block<REV>(p, smem4)) return;
+  bwd_block<GENERIC, REV>(p, (int)blockIdx.x, smem4);
 }
 
 // d(loss)/d(raw parameters) from the summed gradients of (M11, M12, M21, M22, f1, f2),
@@ -781,6 +783,7 @@ Params to_params(const SemxLinossArgs* a) {
   p.variant = a->variant;
   p.a_from_g = a->a_from_g;
   p.chunk = a->chunk;
+  p.rev = a->reverse != 0;
   p.nchunks = (int)semx::cdiv(a->L, a->chunk);
   p.S = a->S;
   p.L = a->L;
@@ -834,10 +837,16 @@ int semx_linoss_fwd(const SemxLinossArgs* a, semx_stream_t stream) {
   const Params p = to_params(a);
   const int64_t n = a->S * a->P;
   const dim3 grid((unsigned)semx::cdiv(n, kBlock));
-  if (a->variant == SEMX_LINOSS_GENERIC)
-    linoss_fwd_kernel<true><<<grid, kBlock, 0, semx::as_stream(stream)>>>(p);
+  cudaStream_t st = semx::as_stream(stream);
+  const bool generic = a->variant == SEMX_LINOSS_GENERIC;
+  if (generic && p.rev)
+    linoss_fwd_kernel<true, true><<<grid, kBlock, 0, st>>>(p);
+  else if (generic)
+    linoss_fwd_kernel<true, false><<<grid, kBlock, 0, st>>>(p);
+  else if (p.rev)
+    linoss_fwd_kernel<false, true><<<grid, kBlock, 0, st>>>(p);
   else
-    linoss_fwd_kernel<false><<<grid, kBlock, 0, semx::as_stream(stream)>>>(p);
+    linoss_fwd_kernel<false, false><<<grid, kBlock, 0, st>>>(p);
   return semx::check_launch("linoss_fwd_kernel");
 }
 
@@ -855,13 +864,10 @@ int semx_linoss_bwd(const SemxLinossArgs* a, semx_stream_t stream) {
     const size_t smem = std::max(bwd_smem_bytes(a->chunk, generic),
                                  a->variant == SEMX_LINOSS_IMEX ? rev_smem_bytes() : (size_t)0);
     const dim3 grid((unsigned)semx::cdiv(n, kBlock));
-    if (generic) {
-      if (!semx::allow_smem(linoss_bwd_kernel<true>, smem)) return SEMX_ERR_LAUNCH;
-      linoss_bwd_kernel<true><<<grid, kBlock, smem, st>>>(p);
-    } else {
-      if (!semx::allow_smem(linoss_bwd_kernel<false>, smem)) return SEMX_ERR_LAUNCH;
-      linoss_bwd_kernel<false><<<grid, kBlock, smem, st>>>(p);
-    }
+    auto kernel = generic ? (p.rev ? linoss_bwd_kernel<true, true> : linoss_bwd_kernel<true, false>)
+                          : (p.rev ? linoss_bwd_kernel<false, true> : linoss_bwd_kernel<false, false>);
+    if (!semx::allow_smem(kernel, smem)) return SEMX_ERR_LAUNCH;
+    kernel<<<grid, kBlock, smem, st>>>(p);
     rc = semx::check_launch("linoss_bwd_kernel");
     if (rc != SEMX_OK) return rc;
   } else if (n > 0) {

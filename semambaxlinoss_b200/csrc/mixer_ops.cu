@@ -84,6 +84,7 @@ __device__ __forceinline__ void st4(void* base, int64_t i, bool vec, const float
 __device__ __forceinline__ float sigmoidf_(float x) { return 1.f / (1.f + __expf(-x)); }
 
 struct ConvParams {
+  semx::RowMap rm;      // token row of (sequence, step)
   int64_t S, L, C, ld;  // ld = row stride of xz / dxz in elements (2C)
   int left;             // taps before t
   const void* xz;       // u = columns [0, C)
@@ -102,6 +103,7 @@ __global__ void __launch_bounds__(kT) conv_silu_fwd_kernel(const ConvParams p) {
   const int64_t gid = (int64_t)blockIdx.x * kT + threadIdx.x;
   if (gid >= p.S * groups) return;
   const int64_t s = gid / groups;
+  const int64_t sb = p.rm.seq(s);  // token row of step t: sb + p.rm.step(t)
   const int c0 = (int)(gid % groups) * kCV;
   const int cn = (int)min((int64_t)kCV, p.C - c0);
   const bool full = cn == kCV;
@@ -125,7 +127,7 @@ __global__ void __launch_bounds__(kT) conv_silu_fwd_kernel(const ConvParams p) {
     for (int j = 0; j < kCV; ++j) win[k][j] = 0.f;
     if (k < K - 1 && tt >= 0 && tt < L) {
       float tmp[kCV];
-      ld4<BF16>(p.xz, (s * p.L + tt) * p.ld + c0, vin, tmp, cn);
+      ld4<BF16>(p.xz, (sb + p.rm.step(tt)) * p.ld + c0, vin, tmp, cn);
 #pragma unroll
       for (int j = 0; j < kCV; ++j) win[k][j] = tmp[j];
     }
@@ -138,7 +140,7 @@ __global__ void __launch_bounds__(kT) conv_silu_fwd_kernel(const ConvParams p) {
       for (int j = 0; j < kCV; ++j) win[K - 1][j] = 0.f;
       if (tt >= 0 && tt < L) {
         float tmp[kCV];
-        ld4<BF16>(p.xz, (s * p.L + tt) * p.ld + c0, vin, tmp, cn);
+        ld4<BF16>(p.xz, (sb + p.rm.step(tt)) * p.ld + c0, vin, tmp, cn);
 #pragma unroll
         for (int j = 0; j < kCV; ++j) win[K - 1][j] = tmp[j];
       }
@@ -151,7 +153,7 @@ __global__ void __launch_bounds__(kT) conv_silu_fwd_kernel(const ConvParams p) {
       for (int k = 0; k < K; ++k) a = fmaf(w[k][j], win[k][j], a);
       out[j] = a * sigmoidf_(a);
     }
-    st4<false>(p.v, (s * p.L + t) * p.C + c0, vout, out, cn);
+    st4<false>(p.v, (sb + p.rm.step(t)) * p.C + c0, vout, out, cn);
 #pragma unroll
     for (int k = 0; k + 1 < K; ++k)
 #pragma unroll
@@ -168,6 +170,7 @@ __global__ void __launch_bounds__(kT) conv_silu_bwd_kernel(const ConvParams p) {
   const int64_t gid = (int64_t)blockIdx.x * kT + threadIdx.x;
   if (gid >= p.S * groups) return;
   const int64_t s = gid / groups;
+  const int64_t sb = p.rm.seq(s);  // token row of step t: sb + p.rm.step(t)
   const int c0 = (int)(gid % groups) * kCV;
   const int cn = (int)min((int64_t)kCV, p.C - c0);
   const bool full = cn == kCV;
@@ -200,7 +203,7 @@ __global__ void __launch_bounds__(kT) conv_silu_bwd_kernel(const ConvParams p) {
     }
     if (k < K - 1 && tt >= 0 && tt < L) {
       float tmp[kCV];
-      ld4<BF16>(p.xz, (s * p.L + tt) * p.ld + c0, vin, tmp, cn);
+      ld4<BF16>(p.xz, (sb + p.rm.step(tt)) * p.ld + c0, vin, tmp, cn);
 #pragma unroll
       for (int j = 0; j < kCV; ++j) win[k][j] = tmp[j];
     }
@@ -217,12 +220,12 @@ __global__ void __launch_bounds__(kT) conv_silu_bwd_kernel(const ConvParams p) {
       for (int j = 0; j < kCV; ++j) win[K - 1][j] = 0.f;
       if (tt >= 0 && tt < L) {
         float tmp[kCV];
-        ld4<BF16>(p.xz, (s * p.L + tt) * p.ld + c0, vin, tmp, cn);
+        ld4<BF16>(p.xz, (sb + p.rm.step(tt)) * p.ld + c0, vin, tmp, cn);
 #pragma unroll
         for (int j = 0; j < kCV; ++j) win[K - 1][j] = tmp[j];
       }
       float g[kCV];
-      ld4<false>(p.dv, (s * p.L + jt) * p.C + c0, vdv, g, cn);
+      ld4<false>(p.dv, (sb + p.rm.step(jt)) * p.C + c0, vdv, g, cn);
 #pragma unroll
       for (int j = 0; j < kCV; ++j) {
         float a = bias[j];
@@ -254,7 +257,7 @@ __global__ void __launch_bounds__(kT) conv_silu_bwd_kernel(const ConvParams p) {
         for (int k = 0; k < K; ++k) a = fmaf(w[k][j], dp[K - 1 - k][j], a);
         du[j] = a;
       }
-      st4<BF16>(p.dxz, (s * p.L + t) * p.ld + c0, vin, du, cn);
+      st4<BF16>(p.dxz, (sb + p.rm.step(t)) * p.ld + c0, vin, du, cn);
     }
   }
   // Per-sequence partials: [dw (C, K) | db (C)].
@@ -308,6 +311,7 @@ __global__ void __launch_bounds__(kT) conv_silu_fwd_split_kernel(const ConvParam
   const Slot q = slot_of<TS>(p);
   if (!q.ok || q.t0 >= q.t1) return;
   const int64_t s = q.s;
+  const int64_t sb = p.rm.seq(s);  // token row of step t: sb + p.rm.step(t)
   const int c0 = q.c0, cn = q.cn;
   const bool full = cn == kCV;
   const bool vin = full && ((p.ld % kCV) == 0) &&
@@ -330,11 +334,16 @@ __global__ void __launch_bounds__(kT) conv_silu_fwd_split_kernel(const ConvParam
     for (int j = 0; j < kCV; ++j) win[k][j] = 0.f;
     if (k < K - 1 && tt >= 0 && tt < L) {
       float tmp[kCV];
-      ld4<BF16>(p.xz, (s * p.L + tt) * p.ld + c0, vin, tmp, cn);
+      ld4<BF16>(p.xz, (sb + p.rm.step(tt)) * p.ld + c0, vin, tmp, cn);
 #pragma unroll
       for (int j = 0; j < kCV; ++j) win[k][j] = tmp[j];
     }
   }
+  // Element offsets of the next input row (step t - left + K - 1) and output row (step t),
+  // advanced by one step stride per step instead of recomputed from the row map.
+  const int64_t din = p.rm.step(1) * p.ld, dout = p.rm.step(1) * p.C;
+  int64_t oin = (sb + p.rm.step(q.t0 - left + K - 1)) * p.ld + c0;
+  int64_t oout = (sb + p.rm.step(q.t0)) * p.C + c0;
   auto step = [&](int t) {
     // Shift in u[t - left + K - 1].
     {
@@ -343,10 +352,11 @@ __global__ void __launch_bounds__(kT) conv_silu_fwd_split_kernel(const ConvParam
       for (int j = 0; j < kCV; ++j) win[K - 1][j] = 0.f;
       if (tt >= 0 && tt < L) {
         float tmp[kCV];
-        ld4<BF16>(p.xz, (s * p.L + tt) * p.ld + c0, vin, tmp, cn);
+        ld4<BF16>(p.xz, oin, vin, tmp, cn);
 #pragma unroll
         for (int j = 0; j < kCV; ++j) win[K - 1][j] = tmp[j];
       }
+      oin += din;
     }
     float out[kCV];
 #pragma unroll
@@ -356,7 +366,8 @@ __global__ void __launch_bounds__(kT) conv_silu_fwd_split_kernel(const ConvParam
       for (int k = 0; k < K; ++k) a = fmaf(w[k][j], win[k][j], a);
       out[j] = a * sigmoidf_(a);
     }
-    st4<false>(p.v, (s * p.L + t) * p.C + c0, vout, out, cn);
+    st4<false>(p.v, oout, vout, out, cn);
+    oout += dout;
 #pragma unroll
     for (int k = 0; k + 1 < K; ++k)
 #pragma unroll
@@ -381,6 +392,7 @@ __global__ void __launch_bounds__(kT) conv_silu_bwd_split_kernel(const ConvParam
   __shared__ float red[TS > 1 ? kT : 1][kCV * (K + 1)];
   const Slot q = slot_of<TS>(p);
   const int64_t s = q.s;
+  const int64_t sb = p.rm.seq(s);  // token row of step t: sb + p.rm.step(t)
   const int c0 = q.c0, cn = q.cn;
   const bool full = cn == kCV;
   const bool vin = full && ((p.ld % kCV) == 0) &&
@@ -414,7 +426,7 @@ __global__ void __launch_bounds__(kT) conv_silu_bwd_split_kernel(const ConvParam
       }
       if (k < K - 1 && tt >= 0 && tt < L) {
         float tmp[kCV];
-        ld4<BF16>(p.xz, (s * p.L + tt) * p.ld + c0, vin, tmp, cn);
+        ld4<BF16>(p.xz, (sb + p.rm.step(tt)) * p.ld + c0, vin, tmp, cn);
 #pragma unroll
         for (int j = 0; j < kCV; ++j) win[k][j] = tmp[j];
       }
@@ -432,13 +444,13 @@ __global__ void __launch_bounds__(kT) conv_silu_bwd_split_kernel(const ConvParam
         for (int j = 0; j < kCV; ++j) win[K - 1][j] = 0.f;
         if (tt >= 0 && tt < L) {
           float tmp[kCV];
-          ld4<BF16>(p.xz, (s * p.L + tt) * p.ld + c0, vin, tmp, cn);
+          ld4<BF16>(p.xz, (sb + p.rm.step(tt)) * p.ld + c0, vin, tmp, cn);
 #pragma unroll
           for (int j = 0; j < kCV; ++j) win[K - 1][j] = tmp[j];
         }
         if (jt >= 0) {
           float g[kCV];
-          ld4<false>(p.dv, (s * p.L + jt) * p.C + c0, vdv, g, cn);
+          ld4<false>(p.dv, (sb + p.rm.step(jt)) * p.C + c0, vdv, g, cn);
           const bool own = jt >= q.t0 && jt < q.t1;
 #pragma unroll
           for (int j = 0; j < kCV; ++j) {
@@ -471,7 +483,7 @@ __global__ void __launch_bounds__(kT) conv_silu_bwd_split_kernel(const ConvParam
           for (int k = 0; k < K; ++k) a = fmaf(w[k][j], dp[K - 1 - k][j], a);
           du[j] = a;
         }
-        st4<BF16>(p.dxz, (s * p.L + t) * p.ld + c0, vin, du, cn);
+        st4<BF16>(p.dxz, (sb + p.rm.step(t)) * p.ld + c0, vin, du, cn);
       }
     };
     // TS > 1: unrolled by 4; TS = 1: the compiler's own unrolling (measured faster there).
@@ -619,6 +631,12 @@ int conv_validate(const SemxConvSiluArgs* a, bool bwd) {
   SEMX_REQUIRE(a->K >= 1 && a->K <= 8, SEMX_ERR_UNSUPPORTED, "conv_silu: kernel width %d (1..8)", a->K);
   SEMX_REQUIRE(a->left >= 0 && a->left < a->K, SEMX_ERR_SHAPE, "conv_silu: left=%d outside [0, K)", a->left);
   SEMX_REQUIRE(a->ld >= a->C, SEMX_ERR_SHAPE, "conv_silu: row stride %lld < C", (long long)a->ld);
+  {
+    semx::RowMap rm;
+    const int rc = semx::make_rowmap(a->S, a->L, a->reverse, a->seq_group, a->group_stride, a->seq_stride,
+                                     a->step_stride, &rm, "conv_silu");
+    if (rc != SEMX_OK) return rc;
+  }
   if (a->S * a->L * a->C > 0) {
     SEMX_REQUIRE(a->xz && a->w, SEMX_ERR_NULL, "conv_silu: xz / w is NULL");
     if (!bwd) SEMX_REQUIRE(a->v, SEMX_ERR_NULL, "conv_silu: v is NULL");
@@ -629,6 +647,8 @@ int conv_validate(const SemxConvSiluArgs* a, bool bwd) {
 
 ConvParams conv_params(const SemxConvSiluArgs* a) {
   ConvParams p = {};
+  semx::make_rowmap(a->S, a->L, a->reverse, a->seq_group, a->group_stride, a->seq_stride, a->step_stride, &p.rm,
+                    "conv_silu");
   p.S = a->S; p.L = a->L; p.C = a->C; p.ld = a->ld; p.left = a->left;
   p.xz = a->xz; p.w = a->w; p.b = a->b; p.v = a->v; p.dv = a->dv; p.dxz = a->dxz;
   return p;

@@ -62,6 +62,7 @@ constexpr int kMaxClusterCTAs = 2;
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct SParams {
+  semx::RowMap rm;  // token row of (sequence, step)
   int real, gain, chunk, nchunks;
   int64_t S, L, C, N;
   int detune, envelope;
@@ -272,13 +273,14 @@ __device__ __forceinline__ const float* mode_src(const SParams& p, int row) {
   return row == 0 ? p.Bre : (row == 1 ? p.Cre : (row == 2 ? p.Bim : p.Cim));
 }
 
-// Issues the copies of steps [t0, t0 + nt) of sequence s into `buf` (does not commit).
+// Issues the copies of steps [t0, t0 + nt) of the sequence whose token rows are
+// sb + p.rm.step(t) into `buf` (does not commit).
 // A full tile (TT steps, CB channels, N = NP modes, 16-byte rows) takes the first branch,
 // whose item -> (row, step, chunk) split uses compile-time shapes (shifts instead of the
 // general branch's runtime divisions: the copy loop is a tenth of the kernels' issue slots
 // otherwise); ragged tiles take the general branch.
 template <class T>
-__device__ void tile_load(const SParams& p, float* buf, int64_t s, int t0, int nt, int c0, int nc,
+__device__ void tile_load(const SParams& p, float* buf, int64_t sb, int t0, int nt, int c0, int nc,
                           bool vecC, bool vecN) {
   const int N = (int)p.N;
   if (vecC && vecN && nt == T::kTT && nc == T::CB && N == T::NP) {
@@ -289,7 +291,7 @@ __device__ void tile_load(const SParams& p, float* buf, int64_t s, int t0, int n
       if (items_c % kThreads == 0 || it < (unsigned)items_c) {
         const unsigned a = it / per_c, rem = it % per_c, i = rem / qc, j = rem % qc;
         cp_async16(T::chan(buf, a) + i * T::CB + 4 * j,
-                   chan_src<T>(p, a) + ((s * p.L + t0 + i) * p.C + c0) + 4 * j);
+                   chan_src<T>(p, a) + ((sb + p.rm.step(t0 + i)) * p.C + c0) + 4 * j);
       }
     }
     constexpr int qn = T::NP / 4, per_n = T::kTT * qn, items_n = T::kRowN * per_n;
@@ -299,7 +301,7 @@ __device__ void tile_load(const SParams& p, float* buf, int64_t s, int t0, int n
       if (items_n % kThreads == 0 || it < (unsigned)items_n) {
         const unsigned a = it / per_n, rem = it % per_n, i = rem / qn, j = rem % qn;
         cp_async16(T::mode(buf, a) + i * T::NP + 4 * j,
-                   mode_src(p, a) + (s * p.L + t0 + i) * T::NP + 4 * j);
+                   mode_src(p, a) + (sb + p.rm.step(t0 + i)) * T::NP + 4 * j);
       }
     }
     return;
@@ -309,14 +311,14 @@ __device__ void tile_load(const SParams& p, float* buf, int64_t s, int t0, int n
     const int items = T::kRowC * nt * q;
     for (int it = threadIdx.x; it < items; it += kThreads) {
       const int a = it / (nt * q), rem = it % (nt * q), i = rem / q, j = rem % q;
-      const float* src = chan_src<T>(p, a) + ((s * p.L + t0 + i) * p.C + c0) + 4 * j;
+      const float* src = chan_src<T>(p, a) + ((sb + p.rm.step(t0 + i)) * p.C + c0) + 4 * j;
       cp_async16(T::chan(buf, a) + i * T::CB + 4 * j, src);
     }
   } else {
     const int items = T::kRowC * nt * nc;
     for (int it = threadIdx.x; it < items; it += kThreads) {
       const int a = it / (nt * nc), rem = it % (nt * nc), i = rem / nc, j = rem % nc;
-      cp_async4(T::chan(buf, a) + i * T::CB + j, chan_src<T>(p, a) + ((s * p.L + t0 + i) * p.C + c0) + j);
+      cp_async4(T::chan(buf, a) + i * T::CB + j, chan_src<T>(p, a) + ((sb + p.rm.step(t0 + i)) * p.C + c0) + j);
     }
   }
   if (vecN) {
@@ -324,13 +326,13 @@ __device__ void tile_load(const SParams& p, float* buf, int64_t s, int t0, int n
     const int items = T::kRowN * nt * q;
     for (int it = threadIdx.x; it < items; it += kThreads) {
       const int a = it / (nt * q), rem = it % (nt * q), i = rem / q, j = rem % q;
-      cp_async16(T::mode(buf, a) + i * T::NP + 4 * j, mode_src(p, a) + (s * p.L + t0 + i) * p.N + 4 * j);
+      cp_async16(T::mode(buf, a) + i * T::NP + 4 * j, mode_src(p, a) + (sb + p.rm.step(t0 + i)) * p.N + 4 * j);
     }
   } else {
     const int items = T::kRowN * nt * N;
     for (int it = threadIdx.x; it < items; it += kThreads) {
       const int a = it / (nt * N), rem = it % (nt * N), i = rem / N, j = rem % N;
-      cp_async4(T::mode(buf, a) + i * T::NP + j, mode_src(p, a) + (s * p.L + t0 + i) * p.N + j);
+      cp_async4(T::mode(buf, a) + i * T::NP + j, mode_src(p, a) + (sb + p.rm.step(t0 + i)) * p.N + j);
     }
   }
 }
@@ -441,6 +443,7 @@ __global__ void __launch_bounds__(kThreads) slru_fwd_kernel(const SParams p) {
   const int c0 = blockIdx.x * T::CB;
   const int c = c0 + c_local;
   const int64_t s = blockIdx.y;
+  const int64_t sb = p.rm.seq(s);  // token row of step t: sb + p.rm.step(t)
   const bool cval = c < p.C;
   const int nc = (int)min((int64_t)T::CB, p.C - c0);
   const int L = (int)p.L;
@@ -465,15 +468,15 @@ __global__ void __launch_bounds__(kThreads) slru_fwd_kernel(const SParams p) {
 
   tile_zero_padding<T>(smem, nc, (int)p.N);
   const int ntiles = (L + TF - 1) / TF;
-  if (ntiles > 0) tile_load<T>(p, smem, s, 0, min(TF, L), c0, nc, vecC, vecN);
+  if (ntiles > 0) tile_load<T>(p, smem, sb, 0, min(TF, L), c0, nc, vecC, vecN);
   cp_async_commit();
   int next_ck = 0;
-  float* yrow = p.y + s * p.L * p.C + c;
+  float* yrow = p.y + sb * p.C + c;  // step t: yrow[p.rm.step(t) * C]
   for (int k = 0; k < ntiles; ++k) {
     cp_async_wait_all();
     __syncthreads();
     if (k + 1 < ntiles)
-      tile_load<T>(p, smem + ((k + 1) & 1) * T::kBuf, s, (k + 1) * TF,
+      tile_load<T>(p, smem + ((k + 1) & 1) * T::kBuf, sb, (k + 1) * TF,
                    min(TF, L - (k + 1) * TF), c0, nc, vecC, vecN);
     cp_async_commit();
     float* buf = smem + (k & 1) * T::kBuf;
@@ -508,7 +511,7 @@ __global__ void __launch_bounds__(kThreads) slru_fwd_kernel(const SParams p) {
         for (int j = 0; j < kGM; ++j) yp += mp.ge[j] * (hr[j] * hr[j] + (REAL ? 0.f : hi[j] * hi[j]));
       }
       yp = sum_lanes<NG>(yp);
-      if (g == 0 && cval) yrow[(int64_t)t * p.C] = yp + Dc * cur.x;
+      if (g == 0 && cval) yrow[p.rm.step(t) * p.C] = yp + Dc * cur.x;
     }
   }
   if (p.hfr != nullptr) {
@@ -559,6 +562,7 @@ __global__ void __launch_bounds__(kRmCB, 6) slru_fwd_real16_kernel(const SParams
   const int c0 = blockIdx.x * T::CB;
   const int c = c0 + tid;
   const int64_t s = blockIdx.y;
+  const int64_t sb = p.rm.seq(s);  // token row of step t: sb + p.rm.step(t)
   const bool cval = c < p.C;
   const int nc = (int)min((int64_t)T::CB, p.C - c0);
   const int L = (int)p.L, N = (int)p.N;
@@ -579,16 +583,16 @@ __global__ void __launch_bounds__(kRmCB, 6) slru_fwd_real16_kernel(const SParams
 
   tile_zero_padding<T>(smem, nc, N);
   const int ntiles = (L + TT - 1) / TT;
-  if (ntiles > 0) tile_load<T>(p, smem, s, 0, min(TT, L), c0, nc, vecC, vecN);
+  if (ntiles > 0) tile_load<T>(p, smem, sb, 0, min(TT, L), c0, nc, vecC, vecN);
   cp_async_commit();
   int next_ck = 0;
-  float* yrow = p.y + s * p.L * p.C + c;
+  float* yrow = p.y + sb * p.C + c;  // step t: yrow[p.rm.step(t) * C]
   const bool ck16 = N == NM && semx_aligned16(p.ckpt);
   for (int k = 0; k < ntiles; ++k) {
     cp_async_wait_all();
     __syncthreads();
     if (k + 1 < ntiles)
-      tile_load<T>(p, smem + ((k + 1) & 1) * T::kBuf, s, (k + 1) * TT, min(TT, L - (k + 1) * TT), c0, nc,
+      tile_load<T>(p, smem + ((k + 1) & 1) * T::kBuf, sb, (k + 1) * TT, min(TT, L - (k + 1) * TT), c0, nc,
                    vecC, vecN);
     cp_async_commit();
     const float* buf = smem + (k & 1) * T::kBuf;
@@ -635,7 +639,7 @@ __global__ void __launch_bounds__(kRmCB, 6) slru_fwd_real16_kernel(const SParams
           if (envelope) yq[j] = fmaf(ge[n], h[n] * h[n], yq[j]);
         }
       }
-      if (cval) yrow[(int64_t)t * p.C] = (yq[0] + yq[1]) + (yq[2] + yq[3]);
+      if (cval) yrow[p.rm.step(t) * p.C] = (yq[0] + yq[1]) + (yq[2] + yq[3]);
     }
   }
   if (p.hfr != nullptr && cval) {
@@ -725,6 +729,7 @@ __global__ void __launch_bounds__(kThreads, REAL ? 0 : (GAIN == SEMX_GAIN_GAMMA 
   const int c0 = blockIdx.x * T::CB;
   const int c = c0 + c_local;
   const int64_t s = blockIdx.y;
+  const int64_t sb = p.rm.seq(s);  // token row of step t: sb + p.rm.step(t)
   const bool cval = c < p.C;
   const int nc = (int)max((int64_t)0, min((int64_t)T::CB, p.C - c0));
   const int L = (int)p.L;
@@ -757,7 +762,7 @@ __global__ void __launch_bounds__(kThreads, REAL ? 0 : (GAIN == SEMX_GAIN_GAMMA 
   tile_zero_padding<T>(tiles, nc, N);
   if (p.nchunks > 0) {
     const TileEntry E = entry_of(p.nchunks - 1, 0, K, L);
-    tile_load<T>(p, tiles, s, E.t0, E.nt, c0, nc, vecC, vecN);
+    tile_load<T>(p, tiles, sb, E.t0, E.nt, c0, nc, vecC, vecN);
   }
   cp_async_commit();
   int bsel = 0;
@@ -791,7 +796,7 @@ __global__ void __launch_bounds__(kThreads, REAL ? 0 : (GAIN == SEMX_GAIN_GAMMA 
         const int en = (e + 1 < nE) ? e + 1 : 0;
         if (kn >= 0) {
           const TileEntry En = entry_of(kn, en, K, L);
-          tile_load<T>(p, tiles + (bsel ^ 1) * T::kBuf, s, En.t0, En.nt, c0, nc, vecC, vecN);
+          tile_load<T>(p, tiles + (bsel ^ 1) * T::kBuf, sb, En.t0, En.nt, c0, nc, vecC, vecN);
         }
         cp_async_commit();
       }
@@ -943,7 +948,7 @@ __global__ void __launch_bounds__(kThreads, REAL ? 0 : (GAIN == SEMX_GAIN_GAMMA 
               sum_dx = sum_lanes<NG>(sum_dx);
               if (!REAL) sum_dth = sum_lanes<NG>(sum_dth);
               if (g == 0 && cval) {
-                const int64_t ic = (s * p.L + t) * p.C + c;
+                const int64_t ic = (sb + p.rm.step(t)) * p.C + c;
                 if (p.d_dnu) p.d_dnu[ic] = sum_dnu;
                 if (!REAL && p.d_dth) p.d_dth[ic] = sum_dth;
                 if (p.dx) p.dx[ic] = sum_dx + dyv * Dc;
@@ -976,7 +981,7 @@ __global__ void __launch_bounds__(kThreads, REAL ? 0 : (GAIN == SEMX_GAIN_GAMMA 
 #pragma unroll
                 for (int w = 0; w < NW; ++w) acc += peer[((size_t)tl * NW + w) * NV + kk];
               }
-              const int64_t row = s * p.L + ta + tl;
+              const int64_t row = sb + p.rm.step(ta + tl);
               if (p.nclusters > 1) {
                 const int clid = blockIdx.x / p.ncl;
                 p.dbc_part[(row * p.nclusters + clid) * (Lay::kNArr * N) + arr * N + n] = acc;
@@ -1112,6 +1117,10 @@ int validate(const SemxSelectiveLruArgs* a, bool bwd) {
                SEMX_ERR_UNSUPPORTED, "selective_lru: input_gain=%d", a->input_gain);
   SEMX_REQUIRE(a->chunk >= kR && a->chunk <= 256 && a->chunk % kR == 0, SEMX_ERR_UNSUPPORTED,
                "selective_lru: chunk=%d must be a multiple of %d in [%d, 256]", a->chunk, kR, kR);
+  semx::RowMap rm;
+  const int rc = semx::make_rowmap(a->S, a->L, a->reverse, a->seq_group, a->group_stride, a->seq_stride,
+                                   a->step_stride, &rm, "selective_lru");
+  if (rc != SEMX_OK) return rc;
   const bool real = a->real != 0;
   const bool any = a->S * a->C > 0;
   if (any && a->N > 0) {
@@ -1155,6 +1164,8 @@ int validate(const SemxSelectiveLruArgs* a, bool bwd) {
 
 SParams to_params(const SemxSelectiveLruArgs* a) {
   SParams p = {};
+  semx::make_rowmap(a->S, a->L, a->reverse, a->seq_group, a->group_stride, a->seq_stride, a->step_stride, &p.rm,
+                    "selective_lru");
   const Geometry g = geometry(a);
   p.real = a->real != 0;
   p.gain = a->input_gain;

@@ -47,6 +47,34 @@ int bind_device(std::initializer_list<const void*> ptrs) {
   return SEMX_OK;
 }
 
+int make_rowmap(int64_t S, int64_t L, int reverse, int64_t G, int64_t A, int64_t B, int64_t Cst, RowMap* m,
+                const char* what) {
+  if (G < 0 || A < 0 || B < 0 || Cst < 0)
+    return fail(SEMX_ERR_SHAPE, "%s: negative token-layout field", what);
+  m->G = G > 0 ? G : 1;
+  m->A = A > 0 ? A : L;
+  m->B = B;
+  const int64_t step = Cst > 0 ? Cst : 1;
+  m->base = reverse && L > 0 ? (L - 1) * step : 0;
+  m->dstep = reverse ? -step : step;
+  if (S <= 0 || L <= 0) return SEMX_OK;
+  if (S >= ((int64_t)1 << 31) || m->G >= ((int64_t)1 << 31))
+    return fail(SEMX_ERR_SHAPE, "%s: token layout with S=%lld or seq_group=%lld >= 2^31", what, (long long)S,
+                (long long)m->G);
+  if (S % m->G != 0)
+    return fail(SEMX_ERR_SHAPE, "%s: S=%lld is not a multiple of seq_group=%lld", what, (long long)S,
+                (long long)m->G);
+  // The largest row index any (s, t) reaches (every coefficient is non-negative, so the
+  // map is monotone in each index), in 128-bit arithmetic so that no field value can wrap
+  // it below the bound. The map is not checked to be one-to-one: a layout that sends two
+  // tokens to one row gives undefined results, but every access stays inside the rows.
+  const __int128 top = (__int128)((S - 1) / m->G) * m->A + (__int128)(m->G - 1 < S - 1 ? m->G - 1 : S - 1) * m->B +
+                       (__int128)(L - 1) * step;
+  if (top >= (__int128)S * L)
+    return fail(SEMX_ERR_SHAPE, "%s: token layout reaches beyond row %lld", what, (long long)(S * L - 1));
+  return SEMX_OK;
+}
+
 int check_launch(const char* what) {
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(SEMX_ERR_LAUNCH, "%s: %s", what, cudaGetErrorString(e));

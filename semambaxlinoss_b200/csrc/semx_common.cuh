@@ -33,6 +33,26 @@ inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
 inline cudaStream_t as_stream(semx_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
 
+// Token row of step t of sequence s: (s / G) * A + (s % G) * B + t' * Cst, t' = L - 1 - t
+// when reversed (the layout fields of the selective-LRU and conv + SiLU structs), split as
+// seq(s) + step(t): the reversal is folded into seq's constant term base = (L - 1) * Cst
+// and a negative step stride dstep = -Cst, so a kernel that hoists seq(s) pays one
+// multiply-add per token row, as for the sequence-major layout.
+struct RowMap {
+  int64_t G, A, B, base, dstep;
+  // s and G below 2^31 (checked on the host): one 32-bit division.
+  __host__ __device__ __forceinline__ int64_t seq(int64_t s) const {
+    if (G == 1) return s * A + base;
+    const int64_t q = (int64_t)((uint32_t)s / (uint32_t)G);
+    return q * A + (s - q * G) * B + base;
+  }
+  __host__ __device__ __forceinline__ int64_t step(int64_t t) const { return t * dstep; }
+};
+// Fills `m` from the layout fields (zeros select the sequence-major layout: G = 1, A = L,
+// Cst = 1) and checks that every (s, t) maps below S * L; returns a semx_status.
+int make_rowmap(int64_t S, int64_t L, int reverse, int64_t G, int64_t A, int64_t B, int64_t Cst, RowMap* m,
+                const char* what);
+
 // Raises the dynamic shared-memory limit of `kernel` when a launch needs more than the
 // 48 KB default. Returns false (with the error recorded) if the attribute is refused.
 template <typename K>

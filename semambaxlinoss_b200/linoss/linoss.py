@@ -21,6 +21,7 @@ from typing import Literal
 import torch
 import torch.nn as nn
 
+from ..layout import TokenLayout
 from .scan import DEFAULT_CHUNK, linoss_scan_fused
 
 
@@ -121,13 +122,28 @@ class LinOSS(nn.Module):
             return "IM"
         return "DAMPED_IMEX" if self.damping else "IMEX"
 
-    def forward(self, x: torch.Tensor) -> torch.Tensor:
+    def accepts_layout(self, layout: TokenLayout) -> bool:
+        """Sequence-major token rows, in either step order (the scan kernels run a chain
+        forwards or backwards through its rows)."""
+        return layout.is_contiguous
+
+    def forward(self, x: torch.Tensor, layout: TokenLayout | None = None) -> torch.Tensor:
+        """``layout`` (not in the reference): x holds layout.rows sequence-major token rows,
+        scanned last step first when layout.reverse (the result is flip(layer(flip(x)))
+        along time, without the flips)."""
         lead = x.shape[:-1]
-        x3 = x.reshape(-1, *x.shape[-2:]) if x.dim() != 3 else x
+        reverse = False
+        if layout is not None:
+            if not layout.is_contiguous:
+                raise ValueError(f"LinOSS reads sequence-major token rows only, got {layout}")
+            x3 = x.reshape(layout.S, layout.L, x.shape[-1])
+            reverse = layout.reverse
+        else:
+            x3 = x.reshape(-1, *x.shape[-2:]) if x.dim() != 3 else x
         Bu = _project_input(self.B.float(), x3.float())
         y2 = linoss_scan_fused(
             self.variant, self.steps, self.A_diag, self.G_diag, Bu,
-            a_from_g=self.A_from_G, chunk=self.chunk_size,
+            a_from_g=self.A_from_G, chunk=self.chunk_size, reverse=reverse,
         )
         y = _readout(self.C.float(), y2) + x3 * self.D
         return y.reshape(*lead, -1) if x.dim() != 3 else y

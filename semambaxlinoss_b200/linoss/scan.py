@@ -14,7 +14,9 @@ Two entry points:
 Conventions follow the reference operators: CUDA tensors only (RuntimeError otherwise),
 ValueError on shape mismatch, inputs made contiguous, outputs freshly allocated. The
 forward keeps one state checkpoint per ``chunk`` steps when a gradient is needed; the
-backward recomputes everything else.
+backward recomputes everything else. ``reverse=True`` (not in the reference) runs every
+chain from its last step to its first, in place: the result is
+``flip(op(flip(inputs)))`` along the time axis without the two copies.
 """
 from __future__ import annotations
 
@@ -65,7 +67,7 @@ def _alloc_ws(args, device):
 
 class _LinOSSScanGeneric(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, M11, M12, M21, M22, F1, F2, chunk):
+    def forward(ctx, M11, M12, M21, M22, F1, F2, chunk, reverse):
         _require_cuda("linoss_scan", M11, M12, M21, M22, F1, F2)
         if F1.shape != F2.shape:
             raise ValueError(f"F1 {tuple(F1.shape)} != F2 {tuple(F2.shape)}")
@@ -82,6 +84,7 @@ class _LinOSSScanGeneric(torch.autograd.Function):
         ckpt = _alloc_ckpt(S, L, P, chunk, F1.device) if need else None
         a = _lib.new_args(_lib.SemxLinossArgs)
         a.variant, a.chunk, a.S, a.L, a.P = _lib.LINOSS_GENERIC, chunk, S, L, P
+        a.reverse = int(reverse)
         a.M11, a.M12, a.M21, a.M22 = [m.data_ptr() for m in Ms]
         a.F1, a.F2 = F1c.data_ptr(), F2c.data_ptr()
         a.Y2 = Y2.data_ptr()
@@ -89,7 +92,7 @@ class _LinOSSScanGeneric(torch.autograd.Function):
         _call("semx_linoss_fwd", a, F1.device)
         if need:
             ctx.save_for_backward(*Ms, F1c, F2c, ckpt)
-            ctx.chunk = chunk
+            ctx.chunk, ctx.reverse = chunk, int(reverse)
         return Y2
 
     @staticmethod
@@ -102,6 +105,7 @@ class _LinOSSScanGeneric(torch.autograd.Function):
         dM = torch.empty((4, P), dtype=torch.float32, device=F1.device)
         a = _lib.new_args(_lib.SemxLinossArgs)
         a.variant, a.chunk, a.S, a.L, a.P = _lib.LINOSS_GENERIC, ctx.chunk, S, L, P
+        a.reverse = ctx.reverse
         a.M11, a.M12, a.M21, a.M22 = [m.data_ptr() for m in (M11, M12, M21, M22)]
         a.F1, a.F2 = F1.data_ptr(), F2.data_ptr()
         a.ckpt, a.dY2 = ckpt.data_ptr(), dY2.data_ptr()
@@ -109,12 +113,12 @@ class _LinOSSScanGeneric(torch.autograd.Function):
         ws = _alloc_ws(a, F1.device)
         a.workspace = ws.data_ptr()
         _call("semx_linoss_bwd", a, F1.device)
-        return dM[0], dM[1], dM[2], dM[3], dF1, dF2, None
+        return dM[0], dM[1], dM[2], dM[3], dF1, dF2, None, None
 
 
 class _LinOSSScanFused(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, steps, A_diag, G_diag, Bu, variant, a_from_g, chunk):
+    def forward(ctx, steps, A_diag, G_diag, Bu, variant, a_from_g, chunk, reverse):
         _require_cuda("linoss_scan_fused", steps, A_diag, G_diag, Bu)
         if Bu.dim() != 3:
             raise ValueError(f"Bu must be (B, T, N), got {tuple(Bu.shape)}")
@@ -134,36 +138,36 @@ class _LinOSSScanFused(torch.autograd.Function):
         ckpt = _alloc_ckpt(S, L, P, chunk, Bu.device) if need else None
         a = _lib.new_args(_lib.SemxLinossArgs)
         a.variant, a.a_from_g, a.chunk = code, int(bool(a_from_g)), chunk
-        a.S, a.L, a.P = S, L, P
+        a.S, a.L, a.P, a.reverse = S, L, P, int(reverse)
         a.steps, a.A_diag, a.G_diag = st.data_ptr(), A.data_ptr(), _lib.ptr(G)
         a.Bu, a.Y2, a.ckpt = Buc.data_ptr(), Y2.data_ptr(), _lib.ptr(ckpt)
         _call("semx_linoss_fwd", a, Bu.device)
         if need:
             ctx.save_for_backward(st, A, G, Buc, ckpt)
-            ctx.cfg = (code, int(bool(a_from_g)), chunk, damped)
+            ctx.cfg = (code, int(bool(a_from_g)), chunk, damped, int(reverse))
         return Y2
 
     @staticmethod
     def backward(ctx, dY2):
         st, A, G, Bu, ckpt = ctx.saved_tensors
-        code, a_from_g, chunk, damped = ctx.cfg
+        code, a_from_g, chunk, damped, reverse = ctx.cfg
         S, L, P = Bu.shape
         dY2 = _c64(dY2)
         dBu = torch.empty_like(Bu)
         dparams = torch.zeros((3, P), dtype=torch.float32, device=Bu.device)
         a = _lib.new_args(_lib.SemxLinossArgs)
         a.variant, a.a_from_g, a.chunk = code, a_from_g, chunk
-        a.S, a.L, a.P = S, L, P
+        a.S, a.L, a.P, a.reverse = S, L, P, reverse
         a.steps, a.A_diag, a.G_diag = st.data_ptr(), A.data_ptr(), _lib.ptr(G)
         a.Bu, a.ckpt, a.dY2 = Bu.data_ptr(), ckpt.data_ptr(), dY2.data_ptr()
         a.dBu, a.dparams = dBu.data_ptr(), dparams.data_ptr()
         ws = _alloc_ws(a, Bu.device)
         a.workspace = ws.data_ptr()
         _call("semx_linoss_bwd", a, Bu.device)
-        return dparams[0], dparams[1], (dparams[2] if damped else None), dBu, None, None, None
+        return dparams[0], dparams[1], (dparams[2] if damped else None), dBu, None, None, None, None
 
 
-def linoss_scan(M_11, M_12, M_21, M_22, F1, F2, chunk: int = DEFAULT_CHUNK):
+def linoss_scan(M_11, M_12, M_21, M_22, F1, F2, chunk: int = DEFAULT_CHUNK, reverse: bool = False):
     """LinOSS scan with a given transition.
 
     Args:
@@ -171,11 +175,12 @@ def linoss_scan(M_11, M_12, M_21, M_22, F1, F2, chunk: int = DEFAULT_CHUNK):
             N independent 2x2 blocks).
         F1, F2: (B, T, N) complex64. Per-step forcings.
         chunk: checkpoint interval / backward recompute block (multiple of 8, <= 256).
+        reverse: scan each chain from its last step to its first.
 
     Returns:
         Y2: (B, T, N) complex64, the y2 component of the state trajectory.
     """
-    return _LinOSSScanGeneric.apply(M_11, M_12, M_21, M_22, F1, F2, int(chunk))
+    return _LinOSSScanGeneric.apply(M_11, M_12, M_21, M_22, F1, F2, int(chunk), bool(reverse))
 
 
 # Drop-in name of the reference operator (models/linoss/triton.py:276).
@@ -183,7 +188,7 @@ linoss_scan_triton = linoss_scan
 
 
 def linoss_scan_fused(variant: str, steps, A_diag, G_diag, Bu, a_from_g: bool = True,
-                      chunk: int = DEFAULT_CHUNK):
+                      chunk: int = DEFAULT_CHUNK, reverse: bool = False):
     """Fused LinOSS scan: raw parameters (P,) and Bu (B, T, P) complex64 -> y2.
 
     ``variant`` is "IM", "IMEX" or "DAMPED_IMEX"; ``G_diag`` is used (and required) only
@@ -192,4 +197,4 @@ def linoss_scan_fused(variant: str, steps, A_diag, G_diag, Bu, a_from_g: bool = 
     """
     if variant not in VARIANTS:
         raise ValueError(f"unknown LinOSS variant {variant!r}")
-    return _LinOSSScanFused.apply(steps, A_diag, G_diag, Bu, variant, a_from_g, int(chunk))
+    return _LinOSSScanFused.apply(steps, A_diag, G_diag, Bu, variant, a_from_g, int(chunk), bool(reverse))

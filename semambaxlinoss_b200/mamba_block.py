@@ -16,6 +16,15 @@ checkout. Their documented behaviour is restated here:
   re-draw every ``out_proj.weight`` / ``fc2.weight`` Kaiming-uniform (a = sqrt(5)) and
   divide it by sqrt(n_layer).
 
+Token layouts (:mod:`semambaxlinoss_b200.layout`): a TF-block keeps its activations as
+one (batch, frames, bins, channels) tensor. The frequency-axis scans read it as
+contiguous sequences and the time-axis scans read it through a strided row grid, and
+the backward branch of a bi-directional block runs its convolution and scan in reverse
+step order over the same rows. This replaces the reference's ``torch.flip`` pair and
+its permute + contiguous copies (models/mamba_block.py:387-396, 496-507) with reads in
+place. A scan layer that cannot read a layout (the MIMO layer; a streamed
+SelectiveLRU for strided layouts) falls back to the reference's copies.
+
 Supported mixers: ``selective_lru``, ``selective_lru_mimo``, ``linoss`` (the layers on
 this package's scan path). The reference's other backbones (``mamba``, ``mamba2``,
 ``mamba3`` from mamba_ssm, ``s4d``, ``s5``, and ``selective_linoss``, whose source the
@@ -32,6 +41,7 @@ from torch import nn
 import torch.nn.functional as F
 
 from . import _lib
+from .layout import TokenLayout
 from .linoss import LinOSS
 from .mixer import MambaStyleMixer
 from .selective_lru import SelectiveLRU, SelectiveLRUMIMO
@@ -160,21 +170,34 @@ class HybridBlock(nn.Module):
             else:
                 self.gate = nn.Sequential(nn.Linear(2 * dim, gate_hidden), nn.SiLU(), nn.Linear(gate_hidden, dim))
 
-    def forward(self, x, residual=None):
+    def accepts_layout(self, layout: TokenLayout) -> bool:
+        return all(_accepts(b, layout) for b in (self.backbone_1, self.backbone_2))
+
+    def forward(self, x, residual=None, layout: TokenLayout | None = None):
+        kw = {} if layout is None else {"layout": layout}
         if self.mode == "sequential":
             x, residual = _apply_layer_norm(x, residual, self.norm1)
-            x = self.backbone_1(x)
+            x = self.backbone_1(x, **kw)
             x, residual = _apply_layer_norm(x, residual, self.norm2)
-            x = self.backbone_2(x)
+            x = self.backbone_2(x, **kw)
         elif self.mode == "parallel":
             x, residual = _apply_layer_norm(x, residual, self.norm1)
-            x1 = self.backbone_1(x)
-            x2 = self.backbone_2(x)
+            x1 = self.backbone_1(x, **kw)
+            x2 = self.backbone_2(x, **kw)
             g = torch.sigmoid(self.gate(torch.cat([x1, x2], dim=-1)))
             x = g * x1 + (1.0 - g) * x2
         else:
             raise ValueError(f"Unknown mode {self.mode}. Has to be either 'sequential' or 'parallel'.")
         return x, residual
+
+
+def _accepts(module, layout: TokenLayout) -> bool:
+    """Whether ``module`` (a mixer, a pre-norm Block or a HybridBlock) reads ``layout``
+    in place."""
+    if isinstance(module, Block):
+        module = module.mixer
+    ok = getattr(module, "accepts_layout", None)
+    return layout.is_default or bool(ok is not None and ok(layout))
 
 
 _OUT_OF_SCOPE = ("mamba", "mamba2", "mamba3", "selective_linoss", "s4d", "s5")
@@ -267,17 +290,41 @@ class MambaBlock(nn.Module):
             self.backward_blocks = nn.ModuleList(create_block(in_channels, cfg) for _ in range(n_layer))
         self.apply(partial(_init_weights, n_layer=n_layer))
 
-    def forward(self, x):
+    def accepts_layout(self, layout: TokenLayout) -> bool:
+        """Whether forward(x, layout=layout) reads x in place: the forward blocks take
+        the layout and the backward blocks its reverse."""
+        if not all(_accepts(b, layout) for b in self.forward_blocks):
+            return False
+        return not self.bidirectional or all(_accepts(b, layout.flipped()) for b in self.backward_blocks)
+
+    def forward(self, x, layout: TokenLayout | None = None):
+        """x: (batch, length, channels), or with ``layout`` (not in the reference) any
+        tensor of layout.rows token rows. The backward branch runs its blocks on the
+        reversed layout of the same rows when they accept it, which equals the flip /
+        blocks / flip of the reference without the copies; otherwise (default layout
+        only) it flips."""
+        if layout is None:
+            layout = TokenLayout.contiguous(x.shape[0], x.shape[1])
+        kw = {} if layout.is_default else {"layout": layout}
         xf, rf = x, None
         for layer in self.forward_blocks:
-            xf, rf = layer(xf, rf)
+            xf, rf = layer(xf, rf, **kw)
         y_forward = xf + rf if rf is not None else xf
         if not self.bidirectional:
             return y_forward
-        xb, rb = torch.flip(x, [1]), None
-        for layer in self.backward_blocks:
-            xb, rb = layer(xb, rb)
-        y_backward = torch.flip(xb + rb, [1]) if rb is not None else torch.flip(xb, [1])
+        back = layout.flipped()
+        if all(_accepts(b, back) for b in self.backward_blocks):
+            xb, rb = x, None
+            for layer in self.backward_blocks:
+                xb, rb = layer(xb, rb, layout=back)
+            y_backward = xb + rb if rb is not None else xb
+        else:
+            if not layout.is_default:
+                raise ValueError(f"the backward blocks read neither {back} nor flipped copies of it")
+            xb, rb = torch.flip(x, [1]), None
+            for layer in self.backward_blocks:
+                xb, rb = layer(xb, rb)
+            y_backward = torch.flip(xb + rb, [1]) if rb is not None else torch.flip(xb, [1])
         return torch.cat([y_forward, y_backward], -1)
 
 
@@ -340,19 +387,29 @@ class TFMambaBlock(nn.Module):
         else:
             self.freq_emb = None
 
+    def _project(self, lin, y):
+        return _pointwise_transpose(lin, y) if self.use_transpose else lin(y)
+
     def forward(self, x):
+        """x: (batch, channels, time, freq) -> the same shape. The activations stay one
+        (batch, time, freq, channels) tensor throughout: the time-axis scans read it
+        through TokenLayout.time_axis, the frequency-axis scans as contiguous sequences.
+        The result is a (b, c, t, f) view of that tensor, so the permute at the start of
+        the next block is free. A time mixer that cannot read the strided layout gets the
+        reference's (b*f, t, c) copy instead."""
         b, c, t, f = x.size()
         if self.freq_emb is not None:
             assert f == self.freq_emb.shape[0], (
                 f"freq_emb_bins={self.freq_emb.shape[0]} but the latent input has {f} bins")
             x = x + self.freq_emb.t().unsqueeze(0).unsqueeze(2)
-        x = x.permute(0, 3, 2, 1).contiguous().view(b * f, t, c)
-        if self.use_transpose:
-            x = _pointwise_transpose(self.tlinear, self.time_mamba(x)) + x
-            x = x.view(b, f, t, c).permute(0, 2, 1, 3).contiguous().view(b * t, f, c)
-            x = _pointwise_transpose(self.flinear, self.freq_mamba(x)) + x
+        tl = TokenLayout.time_axis(b, t, f)
+        if self.time_mamba.accepts_layout(tl):
+            x = x.permute(0, 2, 3, 1).contiguous()  # (b, t, f, c); no copy after a TF-block
+            x = self._project(self.tlinear, self.time_mamba(x, layout=tl)) + x
         else:
-            x = self.tlinear(self.time_mamba(x)) + x
-            x = x.view(b, f, t, c).permute(0, 2, 1, 3).contiguous().view(b * t, f, c)
-            x = self.flinear(self.freq_mamba(x)) + x
+            x = x.permute(0, 3, 2, 1).contiguous().view(b * f, t, c)
+            x = self._project(self.tlinear, self.time_mamba(x)) + x
+            x = x.view(b, f, t, c).permute(0, 2, 1, 3).contiguous()
+        x = x.view(b * t, f, c)
+        x = self._project(self.flinear, self.freq_mamba(x)) + x
         return x.view(b, t, f, c).permute(0, 3, 1, 2)

@@ -13,12 +13,19 @@ contiguous fp32, outputs freshly allocated, unused outputs get ``None`` gradient
 into the adjoint. ``block_t`` is the checkpoint interval of the recompute backward (a
 multiple of 4, at most 256); ``block_c`` is accepted for API compatibility (the channel
 tiling is chosen from N).
+
+``layout`` (a :class:`~semambaxlinoss_b200.layout.TokenLayout`, not in the reference
+signature) lets the per-token tensors be any (rows, width) arrangement the kernels read
+in place: a reversed step order, or a row grid such as the time axis of a
+(batch, frames, bins, width) tensor. The per-token outputs and gradients keep the
+inputs' shapes and row order; ``h0`` and the final state stay (S, C, N).
 """
 from __future__ import annotations
 
 import torch
 
 from .. import _lib
+from ..layout import TokenLayout, check_rows
 
 DEFAULT_CHUNK = 16
 
@@ -35,10 +42,11 @@ def _check_cuda(*tensors):
             raise RuntimeError("fused selective-LRU scan requires CUDA tensors.")
 
 
-def _build_args(real, gain_code, chunk, S, L, C, N, t):
+def _build_args(real, gain_code, chunk, layout, C, N, t):
     a = _lib.new_args(_lib.SemxSelectiveLruArgs)
     a.real, a.input_gain, a.chunk = int(real), gain_code, int(chunk)
-    a.S, a.L, a.C, a.N = S, L, C, N
+    a.S, a.L, a.C, a.N = layout.S, layout.L, C, N
+    _lib.set_layout(a, layout)
     for name, tensor in t.items():
         setattr(a, name, _lib.ptr(tensor))
     return a
@@ -46,19 +54,26 @@ def _build_args(real, gain_code, chunk, S, L, C, N, t):
 
 class _SelectiveLRUScan(torch.autograd.Function):
     # Inputs (in order): delta_nu, delta_theta, a, omega, B_re, B_im, C_re, C_im, x, D, g,
-    # s, h0_re, h0_im; then non-tensor block_t, want_final_state, gain_code, real.
+    # s, h0_re, h0_im; then non-tensor block_t, want_final_state, gain_code, real, layout.
     @staticmethod
     def forward(ctx, delta_nu, delta_theta, a, omega, B_re, B_im, C_re, C_im, x, D, g, s,
-                h0_re, h0_im, block_t, want_final_state, gain_code, real):
+                h0_re, h0_im, block_t, want_final_state, gain_code, real, layout):
         ctx.set_materialize_grads(False)
         _check_cuda(delta_nu, delta_theta, a, omega, B_re, B_im, C_re, C_im, x, D, g, s,
                     h0_re, h0_im)
-        if delta_nu.dim() != 3:
-            raise ValueError(f"delta_nu must be (B, T, C), got {tuple(delta_nu.shape)}")
-        S, L, C = delta_nu.shape
+        if layout is None:
+            if delta_nu.dim() != 3:
+                raise ValueError(f"delta_nu must be (B, T, C), got {tuple(delta_nu.shape)}")
+            layout = TokenLayout.contiguous(delta_nu.shape[0], delta_nu.shape[1])
+        S, L, C = layout.S, layout.L, delta_nu.shape[-1]
         N = a.shape[1]
-        if a.shape != (C, N) or x.shape != (S, L, C) or B_re.shape != (S, L, N):
+        if a.shape != (C, N):
             raise ValueError("selective-LRU operand shapes do not agree")
+        for name, t, w in (("delta_nu", delta_nu, C), ("x", x, C), ("B_re", B_re, N), ("C_re", C_re, N)):
+            check_rows(name, t, layout, w)
+        if not real:
+            for name, t, w in (("delta_theta", delta_theta, C), ("B_im", B_im, N), ("C_im", C_im, N)):
+                check_rows(name, t, layout, w)
         dev = delta_nu.device
         ins = {
             "delta_nu": _f32(delta_nu), "delta_theta": None if real else _f32(delta_theta),
@@ -70,11 +85,11 @@ class _SelectiveLRUScan(torch.autograd.Function):
         }
         need = any(ctx.needs_input_grad[:14])
         save_hf = want_final_state or need
-        y = torch.empty((S, L, C), dtype=torch.float32, device=dev)
+        y = torch.empty(delta_nu.shape, dtype=torch.float32, device=dev)
         hf_re = torch.empty((S, C, N), dtype=torch.float32, device=dev) if save_hf else None
         hf_im = (torch.empty((S, C, N), dtype=torch.float32, device=dev)
                  if save_hf and not real else None)
-        args = _build_args(real, gain_code, block_t, S, L, C, N, dict(ins, y=y, hf_re=hf_re, hf_im=hf_im))
+        args = _build_args(real, gain_code, block_t, layout, C, N, dict(ins, y=y, hf_re=hf_re, hf_im=hf_im))
         ckpt = None
         if need:
             ckpt = _lib.empty_f32(_lib.load().semx_selective_lru_ckpt_bytes(args), dev)
@@ -84,7 +99,7 @@ class _SelectiveLRUScan(torch.autograd.Function):
             ctx.save_for_backward(*[ins[k] for k in (
                 "delta_nu", "delta_theta", "a", "omega", "B_re", "B_im", "C_re", "C_im", "x",
                 "D", "g", "s", "h0_re", "h0_im")], ckpt)
-            ctx.cfg = (S, L, C, N, block_t, gain_code, real)
+            ctx.cfg = (layout, C, N, block_t, gain_code, real, delta_nu.shape, B_re.shape)
         dummy = y.new_zeros(1)
         if not save_hf:
             return y, dummy, dummy
@@ -93,14 +108,15 @@ class _SelectiveLRUScan(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dy, dhf_re, dhf_im):
         (dnu, dth, a, om, Bre, Bim, Cre, Cim, x, D, g, s, h0r, h0i, ckpt) = ctx.saved_tensors
-        S, L, C, N, block_t, gain_code, real = ctx.cfg
+        layout, C, N, block_t, gain_code, real, tok_shape, sel_shape = ctx.cfg
+        S = layout.S
         dev = dnu.device
         if dhf_re is None and dhf_im is not None:
             dhf_re = torch.zeros_like(dhf_im)
         if dhf_im is None and dhf_re is not None:
             dhf_im = torch.zeros_like(dhf_re)
         if dy is None:
-            dy = torch.zeros((S, L, C), dtype=torch.float32, device=dev)
+            dy = torch.zeros(tok_shape, dtype=torch.float32, device=dev)
         need = ctx.needs_input_grad
 
         def out(i, shape):
@@ -110,15 +126,15 @@ class _SelectiveLRUScan(torch.autograd.Function):
             return torch.zeros(shape, dtype=torch.float32, device=dev) if need[i] else None
 
         grads = {
-            "d_delta_nu": out(0, (S, L, C)),
-            "d_delta_theta": None if real else out(1, (S, L, C)),
+            "d_delta_nu": out(0, tok_shape),
+            "d_delta_theta": None if real else out(1, tok_shape),
             "da": zout(2, (C, N)),
             "domega": None if real else zout(3, (C, N)),
-            "dB_re": zout(4, (S, L, N)),
-            "dB_im": None if real else zout(5, (S, L, N)),
-            "dC_re": zout(6, (S, L, N)),
-            "dC_im": None if real else zout(7, (S, L, N)),
-            "dx": out(8, (S, L, C)),
+            "dB_re": zout(4, sel_shape),
+            "dB_im": None if real else zout(5, sel_shape),
+            "dC_re": zout(6, sel_shape),
+            "dC_im": None if real else zout(7, sel_shape),
+            "dx": out(8, tok_shape),
             "dD": zout(9, (C,)),
             "dg": zout(10, (C, N)) if g is not None else None,
             "ds": zout(11, (C, N)) if (s is not None and not real) else None,
@@ -131,13 +147,13 @@ class _SelectiveLRUScan(torch.autograd.Function):
              "dhf_re": None if dhf_re is None else _f32(dhf_re),
              "dhf_im": None if (dhf_im is None or real) else _f32(dhf_im)}
         t.update(grads)
-        args = _build_args(real, gain_code, block_t, S, L, C, N, t)
+        args = _build_args(real, gain_code, block_t, layout, C, N, t)
         ws = _lib.empty_f32(_lib.load().semx_selective_lru_workspace_bytes(args), dev)
         args.workspace = ws.data_ptr()
         _lib.call("semx_selective_lru_bwd", args, dev)
         order = ["d_delta_nu", "d_delta_theta", "da", "domega", "dB_re", "dB_im", "dC_re",
                  "dC_im", "dx", "dD", "dg", "ds", "dh0_re", "dh0_im"]
-        return tuple(grads[k] for k in order) + (None, None, None, None)
+        return tuple(grads[k] for k in order) + (None, None, None, None, None)
 
 
 def fused_selective_lru(
@@ -159,6 +175,7 @@ def fused_selective_lru(
     block_c: int = 32,
     want_final_state: bool = False,
     input_gain: str = "gamma",
+    layout: TokenLayout | None = None,
 ):
     """Fused selective-LRU scan + readout. Returns ``(y, hf_re, hf_im)``: ``y`` (B, T, C)
     and the final state parts (B, C, N) (1-element dummies unless ``want_final_state``
@@ -175,6 +192,7 @@ def fused_selective_lru(
     return _SelectiveLRUScan.apply(
         delta_nu, delta_theta, a, omega, Bsel_re, Bsel_im, Csel_re, Csel_im, x, D, g, s,
         h0_re, h0_im, int(block_t), bool(want_final_state), _lib.GAIN_CODES[input_gain], False,
+        layout,
     )
 
 
@@ -190,6 +208,7 @@ def fused_selective_lru_real(
     g: torch.Tensor | None = None,
     block_t: int = DEFAULT_CHUNK,
     want_final_state: bool = False,
+    layout: TokenLayout | None = None,
 ):
     """Real selective diagonal scan (the ``fused_selective_lru`` special case with
     omega = delta_theta = B_im = C_im = 0). Returns ``(y, hf)``."""
@@ -197,6 +216,6 @@ def fused_selective_lru_real(
         raise ValueError(f"input_gain must be 'gamma', 'mamba', or 'zoh', got {input_gain!r}")
     y, hf, _ = _SelectiveLRUScan.apply(
         delta_nu, None, a, None, B, None, C, None, x, D, g, None, h0, None,
-        int(block_t), bool(want_final_state), _lib.GAIN_CODES[input_gain], True,
+        int(block_t), bool(want_final_state), _lib.GAIN_CODES[input_gain], True, layout,
     )
     return y, hf

@@ -19,6 +19,7 @@ import torch
 import torch.nn.functional as F
 from torch import nn
 
+from ..layout import TokenLayout
 from .scan import fused_selective_lru
 
 GAINS = ("gamma", "mamba", "zoh")
@@ -145,11 +146,25 @@ class SelectiveLRU(nn.Module):
     #: piece. Gradients flow through the carried states.
     stream_chunk: int | None = None
 
+    def accepts_layout(self, layout: TokenLayout) -> bool:
+        """Every token layout is read in place, except that a streamed layer (stream_chunk
+        set) splits (batch, time, d_model) tensors along time and so takes the default one
+        only."""
+        return layout.is_default or self.stream_chunk is None
+
     def forward(self, x: torch.Tensor, h_init: torch.Tensor | None = None,
-                rate_scale: float | None = None, return_final_state: bool = False):
+                rate_scale: float | None = None, return_final_state: bool = False,
+                layout: TokenLayout | None = None):
         """``h_init``: optional complex (B, C, N) initial state; ``rate_scale``: per-call
         frame-rate factor on the selective step; ``return_final_state``: also return
-        h_{T-1} as complex (B, C, N) (gradients flow through it)."""
+        h_{T-1} as complex (B, C, N) (gradients flow through it). ``layout`` (not in the
+        reference): x is any tensor of layout.rows token rows, read in that
+        :class:`TokenLayout` (reversed, or strided); y has x's shape and row order, and
+        the states are (layout.S, C, N)."""
+        if layout is not None and not layout.is_default:
+            if not self.accepts_layout(layout):
+                raise ValueError("a streamed SelectiveLRU (stream_chunk set) reads the default layout only")
+            return self._forward_piece(x, h_init, rate_scale, return_final_state, layout)
         K = self.stream_chunk
         if K is not None and x.shape[1] > K:
             h, ys = h_init, []
@@ -160,7 +175,7 @@ class SelectiveLRU(nn.Module):
             return (y, h) if return_final_state else y
         return self._forward_piece(x, h_init, rate_scale, return_final_state)
 
-    def _forward_piece(self, x, h_init, rate_scale, return_final_state):
+    def _forward_piece(self, x, h_init, rate_scale, return_final_state, layout=None):
         r, N = self.dt_rank, self.d_state
         x = x.float()
         dnu_r, dth_r, B_sel, C_sel = torch.split(self.x_proj(x), [r, r, 2 * N, 2 * N], dim=-1)
@@ -179,7 +194,7 @@ class SelectiveLRU(nn.Module):
             B_sel[..., :N], B_sel[..., N:], C_sel[..., :N], C_sel[..., N:],
             x, self.D, g, s, h0_re, h0_im,
             block_t=self.chunk_size, want_final_state=return_final_state,
-            input_gain=self.input_gain,
+            input_gain=self.input_gain, layout=layout,
         )
         if return_final_state:
             return y, torch.complex(hf_re, hf_im)
@@ -310,6 +325,11 @@ class SelectiveLRUMIMO(nn.Module):
             ws += [self.b_coef.weight, self.b_dir.weight, self.c_coef.weight, self.c_read.weight]
         ws.append(drive_weight(self.B))
         return torch.cat(ws, 0), torch.cat([self.dt_nu_proj.bias, self.dt_theta_proj.bias])
+
+    def accepts_layout(self, layout: TokenLayout) -> bool:
+        """The MIMO layer kernels read (batch, time, in_features) tensors in the default
+        sequence-major order only."""
+        return layout.is_default
 
     def forward(self, x: torch.Tensor, rate_scale: float | None = None) -> torch.Tensor:
         """Float32 input runs in float32; bfloat16 input (or float32 input under CUDA bf16

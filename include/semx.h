@@ -494,6 +494,49 @@ size_t semx_rms_norm_workspace_bytes(const SemxRmsNormArgs* args);
 int semx_rms_norm_fwd(const SemxRmsNormArgs* args, semx_stream_t stream);
 int semx_rms_norm_bwd(const SemxRmsNormArgs* args, semx_stream_t stream);
 
+/* ------------------------------------------------------------------------------------
+ * Low-rank selective-step projections of the SelectiveLRU layer (replaces
+ * delta_nu = softplus(dt_nu_up(dnu_r)) and delta_theta = dt_theta_up(dth_r),
+ * models/selective_lru/selective_lru.py:216-220, and the rate scale on delta_nu):
+ *   delta_nu[r, c]    = scale * softplus(sum_k W_nu[c, k] z_nu[r, k] + b_nu[c])
+ *   delta_theta[r, c] = sum_k W_th[c, k] z_th[r, k] + b_th[c]
+ * z_nu, z_th: rows x rank values at row stride ldz (the dnu_r / dth_r columns of the
+ * token projection rows, read in place), bf16 when `bf16` is set, else fp32; W (C, rank),
+ * b (C), delta_* (rows, C) fp32, 8-byte aligned when C is even; rank 1..8. Backward
+ * (d_delta_nu / d_delta_theta may be NULL: zero) writes dz_* (rows, rank, contiguous, the
+ * z dtype), dW_* and db_* (fp32, reduced over rows in a fixed order; workspace:
+ * semx_step_proj_workspace_bytes()).
+ * ---------------------------------------------------------------------------------- */
+typedef struct SemxStepProjArgs {
+  uint32_t struct_size;
+  int32_t bf16;
+  int32_t rank;
+  float scale;
+  int64_t rows, C, ldz;
+  const void* z_nu;
+  const void* z_th;
+  const float* W_nu;
+  const float* b_nu;
+  const float* W_th;
+  const float* b_th;
+  float* delta_nu;
+  float* delta_th;
+  const float* d_delta_nu;
+  const float* d_delta_th;
+  void* dz_nu;
+  void* dz_th;
+  float* dW_nu;
+  float* db_nu;
+  float* dW_th;
+  float* db_th;
+  void* workspace;
+} SemxStepProjArgs;
+
+size_t semx_step_proj_args_size(void);
+size_t semx_step_proj_workspace_bytes(const SemxStepProjArgs* args);
+int semx_step_proj_fwd(const SemxStepProjArgs* args, semx_stream_t stream);
+int semx_step_proj_bwd(const SemxStepProjArgs* args, semx_stream_t stream);
+
 size_t semx_mimo_layer_args_size(void);
 size_t semx_mimo_layer_ckpt_bytes(const SemxMimoLayerArgs* args);
 size_t semx_mimo_layer_workspace_bytes(const SemxMimoLayerArgs* args);

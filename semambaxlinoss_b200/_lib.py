@@ -208,6 +208,21 @@ class SemxRmsNormArgs(ctypes.Structure):
     ] + [(name, ctypes.c_void_p) for name in ("x", "weight", "y", "rstd", "dy", "dx", "dweight", "workspace")]
 
 
+class SemxStepProjArgs(ctypes.Structure):
+    _fields_ = [
+        ("struct_size", ctypes.c_uint32),
+        ("bf16", ctypes.c_int32),
+        ("rank", ctypes.c_int32),
+        ("scale", ctypes.c_float),
+        ("rows", ctypes.c_int64),
+        ("C", ctypes.c_int64),
+        ("ldz", ctypes.c_int64),
+    ] + [(n, ctypes.c_void_p) for n in (
+        "z_nu", "z_th", "W_nu", "b_nu", "W_th", "b_th", "delta_nu", "delta_th",
+        "d_delta_nu", "d_delta_th", "dz_nu", "dz_th", "dW_nu", "db_nu", "dW_th", "db_th",
+        "workspace")]
+
+
 # (python struct, C size query) for every argument struct in semx.h.
 STRUCTS = {
     "SemxLinossArgs": (SemxLinossArgs, "semx_linoss_args_size"),
@@ -218,6 +233,7 @@ STRUCTS = {
     "SemxConvSiluArgs": (SemxConvSiluArgs, "semx_conv_silu_args_size"),
     "SemxGateSiluArgs": (SemxGateSiluArgs, "semx_gate_silu_args_size"),
     "SemxRmsNormArgs": (SemxRmsNormArgs, "semx_rms_norm_args_size"),
+    "SemxStepProjArgs": (SemxStepProjArgs, "semx_step_proj_args_size"),
 }
 
 # Every symbol semx.h declares, with its ctypes signature.
@@ -264,6 +280,10 @@ _SIGNATURES = {
     "semx_rms_norm_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(SemxRmsNormArgs)]),
     "semx_rms_norm_fwd": (ctypes.c_int, [ctypes.POINTER(SemxRmsNormArgs), ctypes.c_void_p]),
     "semx_rms_norm_bwd": (ctypes.c_int, [ctypes.POINTER(SemxRmsNormArgs), ctypes.c_void_p]),
+    "semx_step_proj_args_size": (ctypes.c_size_t, []),
+    "semx_step_proj_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(SemxStepProjArgs)]),
+    "semx_step_proj_fwd": (ctypes.c_int, [ctypes.POINTER(SemxStepProjArgs), ctypes.c_void_p]),
+    "semx_step_proj_bwd": (ctypes.c_int, [ctypes.POINTER(SemxStepProjArgs), ctypes.c_void_p]),
     "semx_mimo_layer_args_size": (ctypes.c_size_t, []),
     "semx_mimo_layer_ckpt_bytes": (ctypes.c_size_t, [ctypes.POINTER(SemxMimoLayerArgs)]),
     "semx_mimo_layer_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(SemxMimoLayerArgs)]),

@@ -3,9 +3,12 @@
 Same constructor, parameter names, registration order, initial values and tags
 (``_no_weight_decay`` / ``_no_reinit``), so reference ``state_dict``s load and equal
 seeds give equal parameters. Forward contract: (batch, time, d_model) ->
-(batch, time, d_model) [+ final state]. The token projections are cuBLAS GEMMs; the
-discretisation, scan, readout, envelope and D skip run in the fused sm_100a scan
-(:func:`fused_selective_lru`), whose backward recomputes states chunk by chunk.
+(batch, time, d_model) [+ final state]. The token projection ``x_proj`` is a cuBLAS
+GEMM; the two low-rank step projections with the softplus and the rate scale run as one
+pass over the (batch, time, d_model) step tensors (``semx_step_proj``, reading dnu_r /
+dth_r in place from the x_proj rows); the discretisation, scan, readout, envelope and D
+skip run in the fused sm_100a scan (:func:`fused_selective_lru`), whose backward
+recomputes states chunk by chunk.
 
 There is one execution path (the CUDA scan). ``use_triton`` is kept for API
 compatibility; ``chunk_size`` is the checkpoint interval of the backward recompute
@@ -19,6 +22,7 @@ import torch
 import torch.nn.functional as F
 from torch import nn
 
+from .. import _lib
 from ..layout import TokenLayout
 from .scan import fused_selective_lru
 
@@ -47,6 +51,84 @@ def _step_projection(lin: nn.Linear, z: torch.Tensor) -> torch.Tensor:
         w1 = torch.cat([lin.weight.t(), lin.bias.unsqueeze(0)], dim=0).float()
         out = torch.mm(z1, w1)
     return out.reshape(*shp[:-1], lin.out_features)
+
+
+def _z_rows(z: torch.Tensor) -> tuple[torch.Tensor, int]:
+    """z (..., r) as a (rows, r) view and its row stride (a contiguous copy if the leading
+    dimensions do not collapse to one stride)."""
+    r = z.shape[-1]
+    try:
+        zz = z.view(-1, r)
+    except RuntimeError:
+        zz = z.contiguous().view(-1, r)
+    if zz.stride(1) != 1:
+        zz = zz.contiguous()
+    return zz, (zz.stride(0) if zz.shape[0] > 1 else r)
+
+
+class _StepProjections(torch.autograd.Function):
+    """semx_step_proj_fwd / _bwd: (delta_nu, delta_theta) from the dnu_r / dth_r columns of
+    the token projection rows (models/selective_lru/selective_lru.py:216-220)."""
+
+    @staticmethod
+    def forward(ctx, z_nu, z_th, W_nu, b_nu, W_th, b_th, scale):
+        if not z_nu.is_cuda:
+            raise RuntimeError("SelectiveLRU step projections require CUDA tensors.")
+        if z_nu.dtype not in (torch.float32, torch.bfloat16) or z_th.dtype != z_nu.dtype:
+            raise ValueError(f"step projections: unsupported z dtypes {z_nu.dtype}, {z_th.dtype}")
+        zn, ldn = _z_rows(z_nu)
+        zt, ldt = _z_rows(z_th)
+        if ldn != ldt:
+            zn, zt = zn.contiguous(), zt.contiguous()
+            ldn = zn.shape[1]
+        rows, r = zn.shape
+        C = W_nu.shape[0]
+        Wn, bn = W_nu.detach().float().contiguous(), b_nu.detach().float().contiguous()
+        Wt, bt = W_th.detach().float().contiguous(), b_th.detach().float().contiguous()
+        dnu = torch.empty((*z_nu.shape[:-1], C), dtype=torch.float32, device=z_nu.device)
+        dth = torch.empty_like(dnu)
+        a = _lib.new_args(_lib.SemxStepProjArgs)
+        a.bf16, a.rank, a.scale = int(zn.dtype == torch.bfloat16), r, float(scale)
+        a.rows, a.C, a.ldz = rows, C, ldn
+        a.z_nu, a.z_th = zn.data_ptr(), zt.data_ptr()
+        a.W_nu, a.b_nu, a.W_th, a.b_th = Wn.data_ptr(), bn.data_ptr(), Wt.data_ptr(), bt.data_ptr()
+        a.delta_nu, a.delta_th = dnu.data_ptr(), dth.data_ptr()
+        _lib.call("semx_step_proj_fwd", a, z_nu.device)
+        ctx.save_for_backward(zn, zt, Wn, bn, Wt, bt)
+        ctx.cfg = (float(scale), ldn, z_nu.shape, z_th.shape, W_nu.dtype, b_nu.dtype)
+        return dnu, dth
+
+    @staticmethod
+    def backward(ctx, g_nu, g_th):
+        zn, zt, Wn, bn, Wt, bt = ctx.saved_tensors
+        scale, ldz, shape_nu, shape_th, wdt, bdt = ctx.cfg
+        rows, r = zn.shape
+        C = Wn.shape[0]
+        dev = zn.device
+        g_nu = None if g_nu is None else g_nu.float().contiguous()
+        g_th = None if g_th is None else g_th.float().contiguous()
+        dzn = torch.empty((rows, r), dtype=zn.dtype, device=dev)
+        dzt = torch.empty_like(dzn)
+        dWn, dbn = torch.empty_like(Wn), torch.empty_like(bn)
+        dWt, dbt = torch.empty_like(Wt), torch.empty_like(bt)
+        a = _lib.new_args(_lib.SemxStepProjArgs)
+        a.bf16, a.rank, a.scale = int(zn.dtype == torch.bfloat16), r, scale
+        a.rows, a.C, a.ldz = rows, C, ldz
+        a.z_nu, a.z_th = zn.data_ptr(), zt.data_ptr()
+        a.W_nu, a.b_nu, a.W_th, a.b_th = Wn.data_ptr(), bn.data_ptr(), Wt.data_ptr(), bt.data_ptr()
+        a.d_delta_nu, a.d_delta_th = _lib.ptr(g_nu), _lib.ptr(g_th)
+        a.dz_nu, a.dz_th = dzn.data_ptr(), dzt.data_ptr()
+        a.dW_nu, a.db_nu, a.dW_th, a.db_th = dWn.data_ptr(), dbn.data_ptr(), dWt.data_ptr(), dbt.data_ptr()
+        ws = _lib.empty_f32(_lib.load().semx_step_proj_workspace_bytes(a), dev)
+        a.workspace = ws.data_ptr()
+        _lib.call("semx_step_proj_bwd", a, dev)
+        return (dzn.view(shape_nu), dzt.view(shape_th), dWn.to(wdt), dbn.to(bdt), dWt.to(wdt),
+                dbt.to(bdt), None)
+
+
+#: Largest dt_rank the fused step-projection kernels take; wider ranks (d_model > 512)
+#: use the GEMM formulation of :func:`_step_projection`.
+_MAX_FUSED_RANK = 8
 
 
 def _phase_grid(n_modes: int, n_real_modes: int, theta_max: float) -> torch.Tensor:
@@ -179,11 +261,16 @@ class SelectiveLRU(nn.Module):
         r, N = self.dt_rank, self.d_state
         x = x.float()
         dnu_r, dth_r, B_sel, C_sel = torch.split(self.x_proj(x), [r, r, 2 * N, 2 * N], dim=-1)
-        delta_nu = F.softplus(_step_projection(self.dt_nu_up, dnu_r))
         rs = self.rate_scale if rate_scale is None else float(rate_scale)
-        if rs != 1.0:
-            delta_nu = delta_nu * rs
-        delta_theta = _step_projection(self.dt_theta_up, dth_r)
+        if r <= _MAX_FUSED_RANK:
+            delta_nu, delta_theta = _StepProjections.apply(
+                dnu_r, dth_r, self.dt_nu_up.weight, self.dt_nu_up.bias, self.dt_theta_up.weight,
+                self.dt_theta_up.bias, rs)
+        else:
+            delta_nu = F.softplus(_step_projection(self.dt_nu_up, dnu_r))
+            if rs != 1.0:
+                delta_nu = delta_nu * rs
+            delta_theta = _step_projection(self.dt_theta_up, dth_r)
         a = torch.exp(self.A_log)
         g = self.env_gain if self.envelope_readout else None
         s = self.detune_gain if self.mode_detune else None

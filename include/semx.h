@@ -537,6 +537,36 @@ size_t semx_step_proj_workspace_bytes(const SemxStepProjArgs* args);
 int semx_step_proj_fwd(const SemxStepProjArgs* args, semx_stream_t stream);
 int semx_step_proj_bwd(const SemxStepProjArgs* args, semx_stream_t stream);
 
+/* ------------------------------------------------------------------------------------
+ * LinOSS readout and D skip (replaces Cy = einsum("fn,btn->btf", C, ys).real, Du = x * D,
+ * Cy + Du, models/linoss/linoss.py:118-120):
+ *   y[r, h] = sum_p Re(C[h, p] y2[r, p]) + D[h] x[r, h]
+ * x, y, dy, dx (rows, H) fp32; y2 (rows, P) complex; C (H, P, 2) fp32 (re, im); D (H);
+ * P <= 32. Backward writes dx = D dy and the parameter gradients dC (H, P, 2), dD (H),
+ * reduced over rows in a fixed order (workspace: semx_linoss_readout_workspace_bytes());
+ * the state gradient dy2 = dy conj(C) (a contraction over channels) is the caller's GEMM.
+ * ---------------------------------------------------------------------------------- */
+typedef struct SemxLinossReadoutArgs {
+  uint32_t struct_size;
+  int32_t reserved;
+  int64_t rows, H, P;
+  const float* x;
+  const float* y2;
+  const float* C;
+  const float* D;
+  float* y;
+  const float* dy;
+  float* dx;
+  float* dC;
+  float* dD;
+  void* workspace;
+} SemxLinossReadoutArgs;
+
+size_t semx_linoss_readout_args_size(void);
+size_t semx_linoss_readout_workspace_bytes(const SemxLinossReadoutArgs* args);
+int semx_linoss_readout_fwd(const SemxLinossReadoutArgs* args, semx_stream_t stream);
+int semx_linoss_readout_bwd(const SemxLinossReadoutArgs* args, semx_stream_t stream);
+
 size_t semx_mimo_layer_args_size(void);
 size_t semx_mimo_layer_ckpt_bytes(const SemxMimoLayerArgs* args);
 size_t semx_mimo_layer_workspace_bytes(const SemxMimoLayerArgs* args);

@@ -223,6 +223,16 @@ class SemxStepProjArgs(ctypes.Structure):
         "workspace")]
 
 
+class SemxLinossReadoutArgs(ctypes.Structure):
+    _fields_ = [
+        ("struct_size", ctypes.c_uint32),
+        ("reserved", ctypes.c_int32),
+        ("rows", ctypes.c_int64),
+        ("H", ctypes.c_int64),
+        ("P", ctypes.c_int64),
+    ] + [(n, ctypes.c_void_p) for n in ("x", "y2", "C", "D", "y", "dy", "dx", "dC", "dD", "workspace")]
+
+
 # (python struct, C size query) for every argument struct in semx.h.
 STRUCTS = {
     "SemxLinossArgs": (SemxLinossArgs, "semx_linoss_args_size"),
@@ -234,6 +244,7 @@ STRUCTS = {
     "SemxGateSiluArgs": (SemxGateSiluArgs, "semx_gate_silu_args_size"),
     "SemxRmsNormArgs": (SemxRmsNormArgs, "semx_rms_norm_args_size"),
     "SemxStepProjArgs": (SemxStepProjArgs, "semx_step_proj_args_size"),
+    "SemxLinossReadoutArgs": (SemxLinossReadoutArgs, "semx_linoss_readout_args_size"),
 }
 
 # Every symbol semx.h declares, with its ctypes signature.
@@ -284,6 +295,10 @@ _SIGNATURES = {
     "semx_step_proj_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(SemxStepProjArgs)]),
     "semx_step_proj_fwd": (ctypes.c_int, [ctypes.POINTER(SemxStepProjArgs), ctypes.c_void_p]),
     "semx_step_proj_bwd": (ctypes.c_int, [ctypes.POINTER(SemxStepProjArgs), ctypes.c_void_p]),
+    "semx_linoss_readout_args_size": (ctypes.c_size_t, []),
+    "semx_linoss_readout_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(SemxLinossReadoutArgs)]),
+    "semx_linoss_readout_fwd": (ctypes.c_int, [ctypes.POINTER(SemxLinossReadoutArgs), ctypes.c_void_p]),
+    "semx_linoss_readout_bwd": (ctypes.c_int, [ctypes.POINTER(SemxLinossReadoutArgs), ctypes.c_void_p]),
     "semx_mimo_layer_args_size": (ctypes.c_size_t, []),
     "semx_mimo_layer_ckpt_bytes": (ctypes.c_size_t, [ctypes.POINTER(SemxMimoLayerArgs)]),
     "semx_mimo_layer_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(SemxMimoLayerArgs)]),

@@ -8,7 +8,10 @@ for the GPU:
 * ``Bu = B x`` is one real GEMM producing the interleaved complex64 tensor directly;
 * the constraints, discretisation and recurrence run in one fused sm_100a scan
   (:func:`linoss_scan_fused`), whose backward recomputes states instead of storing them;
-* the readout ``Re(C y2) + D x`` is one real GEMM plus the skip term.
+* the readout ``Re(C y2) + D x`` is one fused pass over the token rows
+  (``semx_linoss_readout``, P <= 32 oscillators): forward y, backward dx, dC and dD, with
+  the state gradient dy2 = dy conj(C) as one GEMM; wider states use a real GEMM plus the
+  skip term.
 
 There is one execution path: the CUDA scan. ``use_triton`` is accepted for API
 compatibility; CPU tensors raise like the reference's GPU operator does.
@@ -21,8 +24,12 @@ from typing import Literal
 import torch
 import torch.nn as nn
 
+from .. import _lib
 from ..layout import TokenLayout
 from .scan import DEFAULT_CHUNK, linoss_scan_fused
+
+#: Largest state the fused readout kernels take (C[h, :] lives in one thread's registers).
+_MAX_FUSED_P = 32
 
 
 def _uniform_init(shape, std: float = 1.0) -> torch.Tensor:
@@ -60,6 +67,45 @@ def _readout(C_param: torch.Tensor, y2: torch.Tensor) -> torch.Tensor:
     W = torch.stack((C_param[..., 0], -C_param[..., 1]), dim=-1).reshape(H, 2 * P)
     y2r = torch.view_as_real(y2).reshape(*y2.shape[:-1], 2 * P)
     return torch.matmul(y2r, W.t())
+
+
+class _Readout(torch.autograd.Function):
+    """semx_linoss_readout_fwd / _bwd: y = Re(C y2) + D x (models/linoss/linoss.py:118-120)
+    for y2 (..., P) complex64, x (..., H) fp32, C (H, P, 2), D (H)."""
+
+    @staticmethod
+    def forward(ctx, y2, x, C, D):
+        H, P, _ = C.shape
+        y2c = y2.contiguous()
+        xc = x.contiguous()
+        Cf, Df = C.detach().float().contiguous(), D.detach().float().contiguous()
+        y = torch.empty(xc.shape, dtype=torch.float32, device=x.device)
+        a = _lib.new_args(_lib.SemxLinossReadoutArgs)
+        a.rows, a.H, a.P = xc.numel() // H, H, P
+        a.x, a.y2, a.C, a.D, a.y = xc.data_ptr(), y2c.data_ptr(), Cf.data_ptr(), Df.data_ptr(), y.data_ptr()
+        _lib.call("semx_linoss_readout_fwd", a, x.device)
+        ctx.save_for_backward(y2c, xc, Cf, Df)
+        ctx.dtypes = (C.dtype, D.dtype)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        y2, x, Cf, Df = ctx.saved_tensors
+        H, P, _ = Cf.shape
+        dy = dy.float().contiguous()
+        dx = torch.empty_like(x)
+        dC, dD = torch.empty_like(Cf), torch.empty_like(Df)
+        a = _lib.new_args(_lib.SemxLinossReadoutArgs)
+        a.rows, a.H, a.P = x.numel() // H, H, P
+        a.x, a.y2, a.C, a.D = x.data_ptr(), y2.data_ptr(), Cf.data_ptr(), Df.data_ptr()
+        a.dy, a.dx, a.dC, a.dD = dy.data_ptr(), dx.data_ptr(), dC.data_ptr(), dD.data_ptr()
+        ws = _lib.empty_f32(_lib.load().semx_linoss_readout_workspace_bytes(a), x.device)
+        a.workspace = ws.data_ptr()
+        _lib.call("semx_linoss_readout_bwd", a, x.device)
+        # dy2[p] = sum_h dy[h] conj(C[h, p]): one GEMM against [C_re | -C_im] as (re, im) pairs.
+        W = torch.stack((Cf[..., 0], -Cf[..., 1]), dim=-1).reshape(H, 2 * P)
+        dy2 = torch.view_as_complex(torch.mm(dy.view(-1, H), W).view(*y2.shape, 2))
+        return dy2, dx, dC.to(ctx.dtypes[0]), dD.to(ctx.dtypes[1])
 
 
 class LinOSS(nn.Module):
@@ -145,5 +191,8 @@ class LinOSS(nn.Module):
             self.variant, self.steps, self.A_diag, self.G_diag, Bu,
             a_from_g=self.A_from_G, chunk=self.chunk_size, reverse=reverse,
         )
-        y = _readout(self.C.float(), y2) + x3 * self.D
+        if self.state_dim <= _MAX_FUSED_P:
+            y = _Readout.apply(y2, x3.float(), self.C, self.D)
+        else:
+            y = _readout(self.C.float(), y2) + x3 * self.D
         return y.reshape(*lead, -1) if x.dim() != 3 else y

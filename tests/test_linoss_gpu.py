@@ -284,3 +284,52 @@ def test_full_size_linoss_workload_properties():
                 "IMEX", st32, A32, None, B2)
             assert_close(lhs, rhs, 1e-4, "linearity")
         del y, y2, Bu32, Bu2
+
+
+@pytest.mark.parametrize("rows,H,P", [(700, 256, 16), (1100, 300, 32), (37, 5, 3), (513, 64, 8), (1, 7, 1)])
+def test_fused_readout_matches_reference(rows, H, P):
+    """semx_linoss_readout (the LinOSS layer's y = Re(C y2) + D x, models/linoss/linoss.py:
+    118-120) against the float64 expression: output, dy2, dx, dC, dD, and the same bits on
+    a second call (fixed reduction order)."""
+    from semambaxlinoss_b200.linoss.linoss import _Readout
+
+    g = gen(rows * 3 + H + P)
+    y2 = crandn((rows, P), g)
+    x = randn((rows, H), g)
+    C = randn((H, P, 2), g, scale=0.3)
+    D = randn(H, g)
+    gy = randn((rows, H), g)
+    ins = [t.clone().requires_grad_(True) for t in (y2, x, C, D)]
+    Cc = torch.complex(ins[2][..., 0], ins[2][..., 1])
+    ref = torch.einsum("fn,bn->bf", Cc, ins[0]).real + ins[1] * ins[3]
+    ref_g = torch.autograd.grad((ref * gy).sum(), ins)
+    dev = cuda()
+    got_in = [to32(t, dev).requires_grad_(True) for t in (y2, x, C, D)]
+
+    def run():
+        for t in got_in:
+            t.grad = None
+        y = _Readout.apply(*got_in)
+        (y * to32(gy, dev)).sum().backward()
+        return [y.detach()] + [t.grad.clone() for t in got_in]
+
+    out = run()
+    assert_close(out[0], ref, FP32_TOL, "y")
+    for name, o, r in zip(["dy2", "dx", "dC", "dD"], out[1:], ref_g):
+        assert_close(o, r, FP32_TOL, name)
+    for a, b in zip(out[2:], run()[2:]):
+        assert torch.equal(a, b)
+
+
+def test_fused_readout_empty_rows():
+    from semambaxlinoss_b200.linoss.linoss import _Readout
+
+    dev = cuda()
+    y2 = torch.zeros(0, 4, dtype=torch.complex64, device=dev, requires_grad=True)
+    x = torch.zeros(0, 6, device=dev, requires_grad=True)
+    C = torch.randn(6, 4, 2, device=dev, requires_grad=True)
+    D = torch.randn(6, device=dev, requires_grad=True)
+    y = _Readout.apply(y2, x, C, D)
+    y.sum().backward()
+    assert y.shape == (0, 6)
+    assert torch.equal(C.grad, torch.zeros_like(C)) and torch.equal(D.grad, torch.zeros_like(D))

@@ -70,7 +70,8 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=None, help="timed steps (default per workload)")
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["semx", "reference"], default="semx")
-    ap.add_argument("--workload", choices=["scans", "linoss", "slru", "mimo", "ops", "generator", "inference"],
+    ap.add_argument("--workload", choices=["scans", "linoss", "slru", "mimo", "ops", "surround", "generator",
+                                           "inference"],
                     default="scans")
     ap.add_argument("--batch", type=int, default=16, help="generator: utterances per GPU")
     ap.add_argument("--micro-batch", type=int, default=8, help="inference: utterances per forward")
@@ -99,8 +100,8 @@ def parse_args():
                     help="skip the 1.5 s busy period before timing (for profiler runs)")
     args = ap.parse_args()
     if args.steps is None:
-        args.steps = {"scans": 20, "linoss": 200, "slru": 20, "mimo": 20, "ops": 20, "generator": 10,
-                      "inference": 1}[args.workload]
+        args.steps = {"scans": 20, "linoss": 200, "slru": 20, "mimo": 20, "ops": 20, "surround": 20,
+                      "generator": 10, "inference": 1}[args.workload]
     return args
 
 
@@ -684,6 +685,107 @@ def _ops_cpu_step(sample):
     ((y * sample["gy"]).sum() + (hr * gh[0] + hi * gh[1]).sum()).backward()
 
 
+# ---------------------------------------------------- layer surround kernels (generator)
+# One generator time-axis layer's token rows (16 utterances x 321 frames x 100 bins), its
+# d_inner, dt_rank and the frequency-axis LinOSS state.
+SUR_ROWS, SUR_C, SUR_R, SUR_P = 16 * 321 * 100, 256, 4, 16
+
+
+class StepProjPass:
+    """The SelectiveLRU step projections (semx_step_proj: delta_nu = softplus(dt_nu_up(dnu_r)),
+    delta_theta = dt_theta_up(dth_r)) on bf16 projection rows of 2r + 64 columns, fwd + bwd
+    with upstream gradients on both. Bytes per row: fwd z in (2r bf16) + 2 C fp32 out =
+    8 C + 4 r; bwd 2 C fp32 in + z in + dz out = 8 C + 8 r."""
+
+    kernels = ("step_proj_fwd_kernel", "step_proj_bwd_kernel")
+
+    def __init__(self, rows, seed, device):
+        C, r = SUR_C, SUR_R
+        g = torch.Generator(device=device).manual_seed(seed)
+        self.proj = torch.randn(rows, 2 * r + 64, generator=g, device=device).to(torch.bfloat16)
+        self.w = [torch.randn(C, r, generator=g, device=device) * 0.5, torch.randn(C, generator=g, device=device) - 1.0,
+                  torch.randn(C, r, generator=g, device=device) * 0.5, torch.randn(C, generator=g, device=device)]
+        self.g = [torch.randn(rows, C, generator=g, device=device) for _ in range(2)]
+        self.fwd_bytes_per_unit = 8 * C + 4 * r
+        self.bwd_bytes_per_unit = 8 * C + 8 * r
+        self.units, self.S, self.L = rows, rows, 1
+        self.inputs = [self.proj] + self.g
+        self.outputs = []
+
+    def fwd(self, sh):
+        from semambaxlinoss_b200.selective_lru.selective_lru import _StepProjections
+
+        r = SUR_R
+        self.leaf = [self.proj.detach().requires_grad_(True)] + [t.detach().requires_grad_(True) for t in self.w]
+        self.out = _StepProjections.apply(self.leaf[0][:, :r], self.leaf[0][:, r:2 * r], *self.leaf[1:], 1.0)
+
+    def bwd(self, sh):
+        torch.autograd.backward(self.out, self.g)
+        self.outputs = [self.out[0].detach(), self.out[1].detach(), self.leaf[0].grad]
+
+
+class ReadoutPass:
+    """The LinOSS readout and D skip (semx_linoss_readout: y = Re(C y2) + D x), fwd + bwd.
+    Bytes per row: fwd x in, y out (fp32) + y2 in = 8 H + 8 P; bwd dy, x in, dx out + y2
+    in = 12 H + 8 P (the fused kernel's own; the bwd time also holds the dy2 = dy conj(C)
+    GEMM, which reads dy once more)."""
+
+    kernels = ("linoss_readout_fwd_kernel", "linoss_readout_bwd_kernel")
+
+    def __init__(self, rows, seed, device):
+        H, P = SUR_C, SUR_P
+        g = torch.Generator(device=device).manual_seed(seed)
+        self.y2 = torch.randn(rows, P, dtype=torch.complex64, generator=g, device=device)
+        self.x = torch.randn(rows, H, generator=g, device=device)
+        self.C = torch.randn(H, P, 2, generator=g, device=device) * 0.3
+        self.D = torch.randn(H, generator=g, device=device)
+        self.gy = torch.randn(rows, H, generator=g, device=device)
+        self.fwd_bytes_per_unit = 8 * H + 8 * P
+        self.bwd_bytes_per_unit = 12 * H + 8 * P
+        self.units, self.S, self.L = rows, rows, 1
+        self.inputs = [self.y2, self.x, self.gy]
+        self.outputs = []
+
+    def fwd(self, sh):
+        from semambaxlinoss_b200.linoss.linoss import _Readout
+
+        self.leaf = [t.detach().requires_grad_(True) for t in (self.y2, self.x, self.C, self.D)]
+        self.out = _Readout.apply(*self.leaf)
+
+    def bwd(self, sh):
+        self.out.backward(self.gy)
+        self.outputs = [self.out.detach(), self.leaf[0].grad, self.leaf[1].grad]
+
+
+def _surround_cpu_sample(frac, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    rows = max(1, int(round(SUR_ROWS * frac)))
+    C, r, P = SUR_C, SUR_R, SUR_P
+    t = {"z": torch.randn(rows, 2 * r, generator=g), "wn": torch.randn(C, r, generator=g) * 0.5,
+         "bn": torch.randn(C, generator=g) - 1.0, "wt": torch.randn(C, r, generator=g) * 0.5,
+         "bt": torch.randn(C, generator=g), "y2": torch.randn(rows, P, dtype=torch.complex64, generator=g),
+         "x": torch.randn(rows, C, generator=g), "C": torch.randn(C, P, 2, generator=g) * 0.3,
+         "D": torch.randn(C, generator=g)}
+    gs = [torch.randn(rows, C, generator=g) for _ in range(3)]
+    return {"t": t, "g": gs, "desc": f"{rows} rows (both operations)",
+            "bytes": rows * (8 * C + 4 * r + 8 * C + 8 * r + 8 * C + 8 * P + 12 * C + 8 * P)}
+
+
+def _surround_cpu_step(sample):
+    """The reference's PyTorch expressions (models/selective_lru/selective_lru.py:216-220,
+    models/linoss/linoss.py:118-120), fwd + bwd."""
+    import torch.nn.functional as F
+
+    t = {k: v.clone().requires_grad_(True) for k, v in sample["t"].items()}
+    r = SUR_R
+    dnu = F.softplus(F.linear(t["z"][:, :r], t["wn"], t["bn"]))
+    dth = F.linear(t["z"][:, r:], t["wt"], t["bt"])
+    Cc = torch.complex(t["C"][..., 0], t["C"][..., 1])
+    y = torch.einsum("fn,bn->bf", Cc, t["y2"]).real + t["x"] * t["D"]
+    g = sample["g"]
+    ((dnu * g[0]).sum() + (dth * g[1]).sum() + (y * g[2]).sum()).backward()
+
+
 # ------------------------------------------------------------------------ scan workloads
 WORKLOADS = {
     "linoss": {
@@ -734,6 +836,18 @@ WORKLOADS["ops"] = {
     "l2": "no flush: every (404, 321, 128) operand is 66 MB and (404, 321, 256) 133 MB; a step moves "
           "6.7 GB, far beyond the 126 MB L2",
     "cpu_sample": _ops_cpu_sample, "cpu_step": _ops_cpu_step,
+}
+WORKLOADS["surround"] = {
+    "config": "surround",
+    "metric": "SelectiveLRU step projections + LinOSS readout fwd+bwd, algorithmic HBM GB/s "
+              "(generator layer shape: 513600 token rows, C=256, rank 4, P=16)",
+    "describe": "the fused step projections (bf16 z, rank 4) and the fused LinOSS readout + D skip (P=16) "
+                "of one generator layer, 513600 token rows x 256 channels, fwd + bwd",
+    "data": "synthetic, seeded: z, x, W ~ N(0, 1/4 .. 1), y2 ~ CN(0, 1), C ~ N(0, 0.09)",
+    "dtype": "bf16 z / f32",
+    "chunk": 0, "sample_frac": 2048.0 / SUR_ROWS,
+    "l2": "no flush: every (513600, 256) fp32 operand is 526 MB, far beyond the 126 MB L2",
+    "cpu_sample": _surround_cpu_sample, "cpu_step": _surround_cpu_step,
 }
 # The default workload: configs 0, 1 and 2 in one step, in this order.
 SCAN_SET = ("slru", "linoss", "mimo")
@@ -802,6 +916,13 @@ def _make_passes(name, rank, device, chunk, args, world=1, sharded=False):
         ps = [MimoOpPass(size(OPS_S), OPS_L, seed=1000 * rank, device=device),
               CscanPass(size(OPS_S), OPS_L, seed=1000 * rank + 1, device=device)]
         ps[0].workload, ps[1].workload = "ops", "ops_cscan"
+        for p in ps:
+            p.chunk = chunk
+        return ps
+    if name == "surround":
+        ps = [StepProjPass(size(SUR_ROWS), seed=1000 * rank, device=device),
+              ReadoutPass(size(SUR_ROWS), seed=1000 * rank + 1, device=device)]
+        ps[0].workload, ps[1].workload = "surround_step", "surround_readout"
         for p in ps:
             p.chunk = chunk
         return ps

@@ -34,6 +34,11 @@ CASES = [
     ("mimo_bwd_kernel", "ops", 40 * 128 + 12 * 256),
     ("cscan_fwd_kernel", "ops_cscan", 24 * 128),
     ("cscan_bwd_kernel", "ops_cscan", 40 * 128),
+    # per token row of the generator layer: C = 256, rank 4, P = 16
+    ("step_proj_fwd_kernel", "surround_step", 8 * 256 + 4 * 4),
+    ("step_proj_bwd_kernel", "surround_step", 8 * 256 + 8 * 4),
+    ("linoss_readout_fwd_kernel", "surround_readout", 8 * 256 + 8 * 16),
+    ("linoss_readout_bwd_kernel", "surround_readout", 12 * 256 + 8 * 16),
 ]
 
 

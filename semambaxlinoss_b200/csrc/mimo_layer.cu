@@ -50,7 +50,7 @@ struct LParams {
   int gain, detune, envelope, nchunks;
   int nck;  // checkpoints: one per kCk tokens
   int vec;  // 16-byte aligned rows: bit 0 x, bit 1 b_t / c_t, bit 2 dy, bit 3 dx,
-            // bit 4 the drive columns (proj and dproj)
+            // bit 4 the drive columns (proj and dproj), bit 5 the b_t / c_t columns of dproj
   float rs;
   const void* x;
   const void* proj;
@@ -2051,10 +2051,16 @@ __global__ void __launch_bounds__(kT, 5) mimo_layer_bwd_tc_kernel(const LParams 
         g0.y = fmaf(-drv, static_cast<float>(cr[NH + na]), g0.y);
         g1.y = fmaf(-drv, static_cast<float>(cr[NH + na + 1]), g1.y);
         const int64_t row = (s * p.L + t0 + t) * p.P + cols.ct + (int64_t)r * 2 * NH;
-        st<true>(p.dproj, row + na, drv * h0.x);
-        st<true>(p.dproj, row + na + 1, drv * h1.x);
-        st<true>(p.dproj, row + NH + na, -drv * h0.y);
-        st<true>(p.dproj, row + NH + na + 1, -drv * h1.y);
+        if ((p.vec & 32) != 0) {  // the mode pair's two columns as one 4-byte store each
+          __nv_bfloat16* dp = reinterpret_cast<__nv_bfloat16*>(p.dproj);
+          *reinterpret_cast<__nv_bfloat162*>(dp + row + na) = __floats2bfloat162_rn(drv * h0.x, drv * h1.x);
+          *reinterpret_cast<__nv_bfloat162*>(dp + row + NH + na) = __floats2bfloat162_rn(-drv * h0.y, -drv * h1.y);
+        } else {
+          st<true>(p.dproj, row + na, drv * h0.x);
+          st<true>(p.dproj, row + na + 1, drv * h1.x);
+          st<true>(p.dproj, row + NH + na, -drv * h0.y);
+          st<true>(p.dproj, row + NH + na + 1, -drv * h1.y);
+        }
       }
       gs[t * HW + na] = g0;
       gs[t * HW + na + 1] = g1;
@@ -2152,17 +2158,32 @@ __global__ void __launch_bounds__(kT, 5) mimo_layer_bwd_tc_kernel(const LParams 
         st<true>(p.dx, xo + 3, acc.w);
       }
     }
-    // H. Rank write: d s_b, d b_t.
+    // H. Rank write: d s_b, d b_t (the 16 b_t columns of a rank as two 16-byte stores).
     if (R > 0 && tid < nt * R) {
       const int t = tid / (R > 0 ? R : 1), r = tid % (R > 0 ? R : 1);
       const float sbv = sbs[t * R + r];
       const int64_t row = (s * p.L + t0 + t) * p.P;
       float acc = 0.f;
+      __nv_bfloat16* dp = reinterpret_cast<__nv_bfloat16*>(p.dproj) + row + cols.bt + r * NH;
 #pragma unroll
-      for (int n = 0; n < NH; ++n) {
-        const float g = db[t * HW + n].x;
-        acc = fmaf(static_cast<float>(bts[t * btw + r * NH + n]), g, acc);
-        st<true>(p.dproj, row + cols.bt + r * NH + n, sbv * g);
+      for (int n8 = 0; n8 < NH; n8 += 8) {
+        __nv_bfloat162 q[4];
+#pragma unroll
+        for (int n = n8; n < n8 + 8; n += 2) {
+          const float g0 = db[t * HW + n].x, g1 = db[t * HW + n + 1].x;
+          acc = fmaf(static_cast<float>(bts[t * btw + r * NH + n]), g0, acc);
+          acc = fmaf(static_cast<float>(bts[t * btw + r * NH + n + 1]), g1, acc);
+          q[(n - n8) / 2] = __floats2bfloat162_rn(sbv * g0, sbv * g1);
+        }
+        if ((p.vec & 32) != 0) {
+          *reinterpret_cast<uint4*>(dp + n8) = *reinterpret_cast<const uint4*>(q);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            dp[n8 + 2 * i] = q[i].x;
+            dp[n8 + 2 * i + 1] = q[i].y;
+          }
+        }
       }
       st<true>(p.dproj, row + cols.sb + r, acc);
     }
@@ -2295,7 +2316,12 @@ int vec_flags(const SemxMimoLayerArgs* a) {
   const int64_t bx0 = 2 * H + 2 * H * R + 3 * H * R * Nh;
   const bool vbx = semx::aligned(a->proj, 16) && (a->dproj == nullptr || semx::aligned(a->dproj, 16)) &&
                    (P * es) % 16 == 0 && (bx0 * es) % 16 == 0 && (2 * Nh * es) % 16 == 0;
-  return (vx ? 1 : 0) | (vp ? 2 : 0) | (vdy ? 4 : 0) | (vdx ? 8 : 0) | (vbx ? 16 : 0);
+  // dproj rows whose b_t columns of one (head, rank) start on 16 bytes and whose c_t mode
+  // pairs start on 4 bytes (the tensor-core backward's vector stores).
+  const int64_t bt0 = 2 * H + H * R, ct0 = 2 * H + 2 * H * R + H * R * Nh;
+  const bool vdp = a->dproj != nullptr && semx::aligned(a->dproj, 16) && (P * es) % 16 == 0 &&
+                   (bt0 * es) % 16 == 0 && (Nh * es) % 16 == 0 && (ct0 * es) % 4 == 0 && Nh % 2 == 0;
+  return (vx ? 1 : 0) | (vp ? 2 : 0) | (vdy ? 4 : 0) | (vdx ? 8 : 0) | (vbx ? 16 : 0) | (vdp ? 32 : 0);
 }
 
 // Segments per mode of the forward's parallel chunk scan (1: one thread per mode).

@@ -25,7 +25,7 @@
 //           shuffles; per-(t, n) gradients dB / dC are reduced over channels in a fixed
 //           order: transposed shuffles inside the warp, then shared memory across warps,
 //           then DSMEM across the CTAs of a thread-block cluster of up to kMaxClusterCTAs
-//           channel blocks every kFlush steps; when the sequence has more channel blocks
+//           channel blocks every flush_steps() steps; when the sequence has more channel blocks
 //           than one cluster, each cluster writes its sums per (t, n) and dbc_sum_kernel
 //           adds the clusters in order.
 // Per-(c, n) parameter gradients are summed per thread over time, written per sequence,
@@ -48,7 +48,10 @@ namespace {
 constexpr int kThreads = 128;
 constexpr int kGM = 4;      // modes per thread
 constexpr int kR = 4;       // steps per register-resident sub-block (backward)
-constexpr int kFlush = 8;   // steps per dB/dC cluster reduction (backward)
+// Steps per dB/dC cluster reduction (backward). The real kernels keep 8: their 6 CTAs per SM
+// are bounded by shared memory, which a longer flush window would cut to 5; the complex
+// kernels, bounded at 3 CTAs per SM by registers, take 16 and halve their cluster barriers.
+template <bool REAL> constexpr int flush_steps() { return REAL ? 8 : 16; }
 constexpr int kTileF = 32;  // steps per staged tile, forward (real)
 // Complex forwards stage 16 steps: their 40 KB of double-buffered 32-step tiles held 5 CTAs
 // per SM where registers allow 7 (404 x 321 gamma forward 0.852 -> 0.824 ms).
@@ -659,6 +662,7 @@ struct BwdLayout {
   static constexpr int kNV = NG * kV;         // values per warp per step
   static constexpr int kNW = kThreads / 32;
   __host__ __device__ static constexpr size_t tile_floats() { return 2 * (size_t)T::kBuf; }
+  static constexpr int kFlush = flush_steps<REAL>();
   __host__ __device__ static constexpr size_t red_floats() { return (size_t)2 * kFlush * kNW * kNV; }
   __host__ __device__ static size_t sub_floats(int chunk) {
     return (size_t)(chunk / kR) * kHS * kThreads * kGM;
@@ -718,6 +722,7 @@ __global__ void __launch_bounds__(kThreads, REAL ? 0 : (GAIN == SEMX_GAIN_GAMMA 
   constexpr int HS = Lay::kHS;
   extern __shared__ float4 bwd_smem4[];
   float* tiles = reinterpret_cast<float*>(bwd_smem4);
+  constexpr int kFlush = Lay::kFlush;
   float* red = tiles + Lay::tile_floats();                                  // [2][kFlush][NW][NV]
   float4* sub = reinterpret_cast<float4*>(red + Lay::red_floats());         // [chunk/kR][HS][kThreads]
   cg::cluster_group cluster = cg::this_cluster();

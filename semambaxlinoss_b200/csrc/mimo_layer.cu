@@ -2005,14 +2005,20 @@ __global__ void __launch_bounds__(kT, 5) mimo_layer_bwd_tc_kernel(const LParams 
       *reinterpret_cast<float*>(base + ((((n >> 2) + 4) ^ (t & 7)) << 4)) = -v.y;
     });
     __syncthreads();
-    // C. Rank read and its adjoint per (token, rank).
+    // C. Rank read and its adjoint per (token, rank), each item split over a thread pair
+    // (modes 0-7 / 8-15 of the read, channels 0-15 / 16-31 of the adjoint) so that all
+    // four warps share the phase; the halves are added with one shuffle.
     if (R > 0) {
-      if (tid < nt * R) {
-        const int t = tid / (R > 0 ? R : 1), r = tid % (R > 0 ? R : 1);
+      static_assert(R == 0 || kT >= 2 * CT * R, "two threads per (token, rank)");
+      const int item = tid >> 1, half = tid & 1;
+      const bool act = item < nt * R;
+      const int t = item / (R > 0 ? R : 1), r = item % (R > 0 ? R : 1);
+      float rd = 0.f, dyc = 0.f;
+      if (act) {
         const T* cr = cts + t * ctw + r * 2 * NH;
-        float rd = 0.f;
 #pragma unroll
-        for (int c4 = 0; c4 < 4; ++c4) {
+        for (int c = 0; c < 2; ++c) {
+          const int c4 = 2 * half + c;
           const float4 hre = *reinterpret_cast<const float4*>(htile + semx::tc::sw128(t, c4));
           const float4 hni = *reinterpret_cast<const float4*>(htile + semx::tc::sw128(t, c4 + 4));
           const float4 cre = ld4(cr + 4 * c4), cim = ld4(cr + NH + 4 * c4);
@@ -2021,17 +2027,21 @@ __global__ void __launch_bounds__(kT, 5) mimo_layer_bwd_tc_kernel(const LParams 
           rd = fmaf(cre.z, hre.z, fmaf(cim.z, hni.z, rd));
           rd = fmaf(cre.w, hre.w, fmaf(cim.w, hni.w, rd));
         }
-        float dyc = 0.f;
 #pragma unroll
-        for (int c4 = 0; c4 < 8; ++c4) {
+        for (int c = 0; c < 4; ++c) {
+          const int c4 = 4 * half + c;
           const float4 dv = *reinterpret_cast<const float4*>(reinterpret_cast<const char*>(sm + TcBLay::dyt) +
                                                              semx::tc::sw128(row0 + t, c4));
           const float* co = sm + TcBLay::Co + r * FH + 4 * c4;
           dyc = fmaf(dv.x, co[0], fmaf(dv.y, co[1], fmaf(dv.z, co[2], fmaf(dv.w, co[3], dyc))));
         }
+      }
+      rd += __shfl_xor_sync(0xffffffffu, rd, 1);
+      dyc += __shfl_xor_sync(0xffffffffu, dyc, 1);
+      if (act && half == 0) {
         const float scv = scs[t * R + r];
-        sm[TcBLay::sr + tid] = scv * rd;
-        sm[TcBLay::dr + tid] = scv * dyc;
+        sm[TcBLay::sr + item] = scv * rd;
+        sm[TcBLay::dr + item] = scv * dyc;
         st<true>(p.dproj, (s * p.L + t0 + t) * p.P + cols.sc + r, rd * dyc);
       }
     }
@@ -2158,15 +2168,18 @@ __global__ void __launch_bounds__(kT, 5) mimo_layer_bwd_tc_kernel(const LParams 
         st<true>(p.dx, xo + 3, acc.w);
       }
     }
-    // H. Rank write: d s_b, d b_t (the 16 b_t columns of a rank as two 16-byte stores).
-    if (R > 0 && tid < nt * R) {
-      const int t = tid / (R > 0 ? R : 1), r = tid % (R > 0 ? R : 1);
-      const float sbv = sbs[t * R + r];
-      const int64_t row = (s * p.L + t0 + t) * p.P;
+    // H. Rank write: d s_b, d b_t; a thread pair per (token, rank), each thread 8 of the 16
+    // b_t columns (one 16-byte store), the two halves of d s_b added with one shuffle.
+    if (R > 0) {
+      const int item = tid >> 1, half = tid & 1;
+      const bool act = item < nt * R;
+      const int t = item / (R > 0 ? R : 1), r = item % (R > 0 ? R : 1);
       float acc = 0.f;
-      __nv_bfloat16* dp = reinterpret_cast<__nv_bfloat16*>(p.dproj) + row + cols.bt + r * NH;
-#pragma unroll
-      for (int n8 = 0; n8 < NH; n8 += 8) {
+      if (act) {
+        const float sbv = sbs[t * R + r];
+        const int64_t row = (s * p.L + t0 + t) * p.P;
+        __nv_bfloat16* dp = reinterpret_cast<__nv_bfloat16*>(p.dproj) + row + cols.bt + r * NH;
+        const int n8 = 8 * half;
         __nv_bfloat162 q[4];
 #pragma unroll
         for (int n = n8; n < n8 + 8; n += 2) {
@@ -2185,7 +2198,8 @@ __global__ void __launch_bounds__(kT, 5) mimo_layer_bwd_tc_kernel(const LParams 
           }
         }
       }
-      st<true>(p.dproj, row + cols.sb + r, acc);
+      acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+      if (act && half == 0) st<true>(p.dproj, (s * p.L + t0 + t) * p.P + cols.sb + r, acc);
     }
     // I. dC, dc_out and dD sums over the chunk, fixed ownership.
     for (int t = 0; t < nt; ++t) {

@@ -917,23 +917,31 @@ __global__ void __launch_bounds__(kT, 6) mimo_layer_fwd_tc_kernel(const LParams 
       *reinterpret_cast<float*>(base + ((((n >> 2) + 4) ^ (row & 7)) << 4)) = v.y;
     });
     __syncthreads();
-    // Rank reads s_c Re(<c_t, h_t>) per (token, rank), from the A rows.
-    if (R > 0 && tid < nt * R) {
-      const int t = tid / (R > 0 ? R : 1), r = tid % (R > 0 ? R : 1);
+    // Rank reads s_c Re(<c_t, h_t>) per (token, rank), from the A rows; a thread pair per
+    // item (modes 0-7 / 8-15), the halves added with one shuffle.
+    if (R > 0) {
+      static_assert(R == 0 || kT >= 2 * CT * R, "two threads per (token, rank)");
+      const int item = tid >> 1, half = tid & 1;
+      const bool act = item < nt * R;
+      const int t = item / (R > 0 ? R : 1), r = item % (R > 0 ? R : 1);
       const int row = row0 + t;
-      const T* cr = cts + t * l.ctw + r * 2 * NH;
       float acc = 0.f;
+      if (act) {
+        const T* cr = cts + t * l.ctw + r * 2 * NH;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const float4 hre = *reinterpret_cast<const float4*>(atile + semx::tc::sw128(row, c));
-        const float4 him = *reinterpret_cast<const float4*>(atile + semx::tc::sw128(row, c + 4));
-        const float4 cre = ld4(cr + 4 * c), cim = ld4(cr + NH + 4 * c);
-        acc = fmaf(cre.x, hre.x, fmaf(-cim.x, him.x, acc));
-        acc = fmaf(cre.y, hre.y, fmaf(-cim.y, him.y, acc));
-        acc = fmaf(cre.z, hre.z, fmaf(-cim.z, him.z, acc));
-        acc = fmaf(cre.w, hre.w, fmaf(-cim.w, him.w, acc));
+        for (int cc = 0; cc < 2; ++cc) {
+          const int c = 2 * half + cc;
+          const float4 hre = *reinterpret_cast<const float4*>(atile + semx::tc::sw128(row, c));
+          const float4 him = *reinterpret_cast<const float4*>(atile + semx::tc::sw128(row, c + 4));
+          const float4 cre = ld4(cr + 4 * c), cim = ld4(cr + NH + 4 * c);
+          acc = fmaf(cre.x, hre.x, fmaf(-cim.x, him.x, acc));
+          acc = fmaf(cre.y, hre.y, fmaf(-cim.y, him.y, acc));
+          acc = fmaf(cre.z, hre.z, fmaf(-cim.z, him.z, acc));
+          acc = fmaf(cre.w, hre.w, fmaf(-cim.w, him.w, acc));
+        }
       }
-      sm[TcLay::srk + row * 4 + r] = scs[tid] * acc;
+      acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+      if (act && half == 0) sm[TcLay::srk + row * 4 + r] = scs[item] * acc;
     }
     if (q == 3 || k == nchunks - 1) {
       // The tile is complete: one thread issues its MMAs (the accumulator is free: the

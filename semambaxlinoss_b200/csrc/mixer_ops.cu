@@ -208,24 +208,30 @@ __global__ void __launch_bounds__(kT) conv_silu_bwd_kernel(const ConvParams p) {
       for (int j = 0; j < kCV; ++j) win[k][j] = tmp[j];
     }
   }
+  // The step's two loads (u[jt - left + K - 1], dv[jt]) are issued one step ahead.
+  float nu[kCV], ng[kCV];
+  auto fetch = [&](int jt) {
+    const int tt = jt - left + K - 1;
+#pragma unroll
+    for (int j = 0; j < kCV; ++j) nu[j] = ng[j] = 0.f;
+    if (jt < L && tt >= 0 && tt < L) ld4<BF16>(p.xz, (sb + p.rm.step(tt)) * p.ld + c0, vin, nu, cn);
+    if (jt < L) ld4<false>(p.dv, (sb + p.rm.step(jt)) * p.C + c0, vdv, ng, cn);
+  };
+  fetch(0);
   for (int jt = 0; jt < L + left; ++jt) {
+    float g[kCV];
+#pragma unroll
+    for (int j = 0; j < kCV; ++j) {
+      win[K - 1][j] = nu[j];
+      g[j] = ng[j];
+    }
+    if (jt + 1 < L + left) fetch(jt + 1);
     // dpre[jt] (zero beyond the sequence end).
 #pragma unroll
     for (int k = 0; k + 1 < K; ++k)
 #pragma unroll
       for (int j = 0; j < kCV; ++j) dp[k][j] = dp[k + 1][j];
     if (jt < L) {
-      const int tt = jt - left + K - 1;
-#pragma unroll
-      for (int j = 0; j < kCV; ++j) win[K - 1][j] = 0.f;
-      if (tt >= 0 && tt < L) {
-        float tmp[kCV];
-        ld4<BF16>(p.xz, (sb + p.rm.step(tt)) * p.ld + c0, vin, tmp, cn);
-#pragma unroll
-        for (int j = 0; j < kCV; ++j) win[K - 1][j] = tmp[j];
-      }
-      float g[kCV];
-      ld4<false>(p.dv, (sb + p.rm.step(jt)) * p.C + c0, vdv, g, cn);
 #pragma unroll
       for (int j = 0; j < kCV; ++j) {
         float a = bias[j];
@@ -431,7 +437,25 @@ __global__ void __launch_bounds__(kT) conv_silu_bwd_split_kernel(const ConvParam
         for (int j = 0; j < kCV; ++j) win[k][j] = tmp[j];
       }
     }
+    // The step's two loads (u[jt - left + K - 1], dv[jt]) are issued one step ahead, so
+    // each thread keeps a step of reads in flight while it computes.
+    float nu[kCV], ng[kCV];
+    auto fetch = [&](int jt) {
+      const int tt = jt - left + K - 1;
+#pragma unroll
+      for (int j = 0; j < kCV; ++j) nu[j] = ng[j] = 0.f;
+      if (jt < L && tt >= 0 && tt < L) ld4<BF16>(p.xz, (sb + p.rm.step(tt)) * p.ld + c0, vin, nu, cn);
+      if (jt >= 0 && jt < L) ld4<false>(p.dv, (sb + p.rm.step(jt)) * p.C + c0, vdv, ng, cn);
+    };
+    fetch(ja);
     auto step = [&](int jt) {
+      float g[kCV];
+#pragma unroll
+      for (int j = 0; j < kCV; ++j) {
+        win[K - 1][j] = nu[j];
+        g[j] = ng[j];
+      }
+      if (jt + 1 < jb) fetch(jt + 1);
 #pragma unroll
       for (int k = 0; k + 1 < K; ++k)
 #pragma unroll
@@ -439,18 +463,7 @@ __global__ void __launch_bounds__(kT) conv_silu_bwd_split_kernel(const ConvParam
 #pragma unroll
       for (int j = 0; j < kCV; ++j) dp[K - 1][j] = 0.f;
       if (jt < L) {
-        const int tt = jt - left + K - 1;
-#pragma unroll
-        for (int j = 0; j < kCV; ++j) win[K - 1][j] = 0.f;
-        if (tt >= 0 && tt < L) {
-          float tmp[kCV];
-          ld4<BF16>(p.xz, (sb + p.rm.step(tt)) * p.ld + c0, vin, tmp, cn);
-#pragma unroll
-          for (int j = 0; j < kCV; ++j) win[K - 1][j] = tmp[j];
-        }
         if (jt >= 0) {
-          float g[kCV];
-          ld4<false>(p.dv, (sb + p.rm.step(jt)) * p.C + c0, vdv, g, cn);
           const bool own = jt >= q.t0 && jt < q.t1;
 #pragma unroll
           for (int j = 0; j < kCV; ++j) {

@@ -25,7 +25,8 @@ namespace {
 constexpr int kThreads = 256;        // channels per CTA tile
 constexpr int kRowsPerCta = 512;
 constexpr int kStage = 32;           // y2 rows staged at a time
-constexpr int kUnroll = 16;          // rows whose loads a thread issues together
+constexpr int kUnroll = 16;          // rows whose loads a thread issues together (forward)
+constexpr int kUnrollB = 8;          // the same in the backward, whose accumulators leave fewer registers
 constexpr int kMaxP = 32;
 
 struct RParams {
@@ -115,16 +116,16 @@ __global__ void __launch_bounds__(kThreads) linoss_readout_bwd_kernel(const RPar
     __syncthreads();
     stage_y2<PT>(p, s_y2, rs, n);
     __syncthreads();
-    for (int i0 = 0; i0 < n; i0 += kUnroll) {
-      float gv[kUnroll], xv[kUnroll];
+    for (int i0 = 0; i0 < n; i0 += kUnrollB) {
+      float gv[kUnrollB], xv[kUnrollB];
 #pragma unroll
-      for (int u = 0; u < kUnroll; ++u) {
+      for (int u = 0; u < kUnrollB; ++u) {
         const bool ok = hv && i0 + u < n;
         gv[u] = ok ? __ldcs(p.dy + (rs + i0 + u) * p.H + h) : 0.f;
         xv[u] = ok ? __ldcs(p.x + (rs + i0 + u) * p.H + h) : 0.f;
       }
 #pragma unroll
-      for (int u = 0; u < kUnroll; ++u) {
+      for (int u = 0; u < kUnrollB; ++u) {
         if (i0 + u >= n) break;
         const float g = gv[u];
         if (hv) __stcs(p.dx + (rs + i0 + u) * p.H + h, d * g);

@@ -34,7 +34,16 @@ namespace {
 constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
 constexpr int kTileC = 64;   // channels per CTA tile (2 per lane)
-constexpr int kBatch = 4;    // consecutive rows a warp loads before it computes them
+// Consecutive rows a warp loads before it computes them: 4 in the forward. The backward
+// of ranks up to 4 takes 2 rows, which fit 80 registers and so 3 CTAs per SM (4 rows:
+// 112 registers, 2 CTAs; 513,600 x 256, rank 4: backward 0.844 -> 0.777 ms per call;
+// the forward with 2 rows went 0.343 -> 0.400 ms). Higher ranks would spill at 80
+// registers and keep 4 rows at the default bound.
+constexpr int kBatchF = 4;
+template <int R>
+constexpr int bwd_batch() { return R <= 4 ? 2 : 4; }
+template <int R>
+constexpr int bwd_min_ctas() { return R <= 4 ? 3 : 1; }
 constexpr int kRowsPerCta = 256;
 constexpr int kMaxRank = 8;
 
@@ -108,24 +117,24 @@ __device__ __forceinline__ void st2f(float* base, int64_t r, int64_t C, int64_t 
 // The z values of a batch of kBatch rows, spread over the lanes: value q = b * 2R + k
 // (row b of the batch; k < R: z_nu[k], else z_th[k - R]) is register q / 32 of lane
 // q % 32, read back with a shuffle. Rows past the end repeat the last row.
-template <int R>
-constexpr int z_regs() { return (kBatch * 2 * R + 31) / 32; }
-template <bool BF16, int R>
-__device__ __forceinline__ void load_batch_z(const PParams& p, int64_t rb, int lane, float (&zv)[z_regs<R>()]) {
+template <int R, int NB>
+constexpr int z_regs() { return (NB * 2 * R + 31) / 32; }
+template <bool BF16, int R, int NB>
+__device__ __forceinline__ void load_batch_z(const PParams& p, int64_t rb, int lane, float (&zv)[z_regs<R, NB>()]) {
 #pragma unroll
-  for (int i = 0; i < z_regs<R>(); ++i) {
+  for (int i = 0; i < z_regs<R, NB>(); ++i) {
     const int q = i * 32 + lane;
     const int b = q / (2 * R), k = q % (2 * R);
     float v = 0.f;
-    if (b < kBatch) {
+    if (b < NB) {
       const int64_t r = min(rb + b, p.rows - 1);
       v = k < R ? ldz<BF16>(p.zn, r * p.ldz + k) : ldz<BF16>(p.zt, r * p.ldz + k - R);
     }
     zv[i] = v;
   }
 }
-template <int R>
-__device__ __forceinline__ float batch_z(const float (&zv)[z_regs<R>()], int b, int k) {
+template <int R, int NB>
+__device__ __forceinline__ float batch_z(const float (&zv)[z_regs<R, NB>()], int b, int k) {
   const int q = b * 2 * R + k;
   return __shfl_sync(0xffffffffu, zv[q / 32], q % 32);
 }
@@ -140,23 +149,24 @@ __global__ void __launch_bounds__(kThreads) step_proj_fwd_kernel(const PParams p
   load_lane_w<R>(p, c0, w);
   const bool vec = (p.C % 2) == 0;
   const int64_t r0 = (int64_t)blockIdx.x * kRowsPerCta;
+  constexpr int kBatch = kBatchF;
   constexpr int kStep = kWarps * kBatch;
-  float zn_next[z_regs<R>()];
-  if (r0 + warp * kBatch < p.rows) load_batch_z<BF16, R>(p, r0 + warp * kBatch, lane, zn_next);
+  float zn_next[z_regs<R, kBatch>()];
+  if (r0 + warp * kBatch < p.rows) load_batch_z<BF16, R, kBatch>(p, r0 + warp * kBatch, lane, zn_next);
   for (int i0 = warp * kBatch; i0 < kRowsPerCta; i0 += kStep) {
     if (r0 + i0 >= p.rows) break;
-    float zv[z_regs<R>()];
+    float zv[z_regs<R, kBatch>()];
 #pragma unroll
-    for (int i = 0; i < z_regs<R>(); ++i) zv[i] = zn_next[i];
-    if (i0 + kStep < kRowsPerCta && r0 + i0 + kStep < p.rows) load_batch_z<BF16, R>(p, r0 + i0 + kStep, lane, zn_next);
+    for (int i = 0; i < z_regs<R, kBatch>(); ++i) zv[i] = zn_next[i];
+    if (i0 + kStep < kRowsPerCta && r0 + i0 + kStep < p.rows) load_batch_z<BF16, R, kBatch>(p, r0 + i0 + kStep, lane, zn_next);
 #pragma unroll
     for (int b = 0; b < kBatch; ++b) {
       const int64_t r = r0 + i0 + b;
       float zn[R], zt[R];
 #pragma unroll
       for (int k = 0; k < R; ++k) {
-        zn[k] = batch_z<R>(zv, b, k);
-        zt[k] = batch_z<R>(zv, b, R + k);
+        zn[k] = batch_z<R, kBatch>(zv, b, k);
+        zt[k] = batch_z<R, kBatch>(zv, b, R + k);
       }
       if (r >= p.rows) break;
       float on[2], ot[2];
@@ -213,7 +223,7 @@ constexpr int dz_values() {  // 2 R rounded up to a power of two
 }
 
 template <bool BF16, int R>
-__global__ void __launch_bounds__(kThreads) step_proj_bwd_kernel(const PParams p) {
+__global__ void __launch_bounds__(kThreads, bwd_min_ctas<R>()) step_proj_bwd_kernel(const PParams p) {
   constexpr int V = dz_values<R>();
   __shared__ float red[kWarps][kTileC];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -229,10 +239,11 @@ __global__ void __launch_bounds__(kThreads) step_proj_bwd_kernel(const PParams p
     for (int k = 0; k < R; ++k) dWn[j][k] = dWt[j][k] = 0.f;
   }
   const int64_t r0 = (int64_t)blockIdx.x * kRowsPerCta;
+  constexpr int kBatch = bwd_batch<R>();
   constexpr int kStep = kWarps * kBatch;
   // The batch at i0: z values spread over the lanes, and this lane's gradient pairs.
-  auto load = [&](int i0, float (&zv)[z_regs<R>()], float2 (&gn)[kBatch], float2 (&gt)[kBatch]) {
-    load_batch_z<BF16, R>(p, r0 + i0, lane, zv);
+  auto load = [&](int i0, float (&zv)[z_regs<R, kBatch>()], float2 (&gn)[kBatch], float2 (&gt)[kBatch]) {
+    load_batch_z<BF16, R, kBatch>(p, r0 + i0, lane, zv);
 #pragma unroll
     for (int b = 0; b < kBatch; ++b) {
       const int64_t r = min(r0 + i0 + b, p.rows - 1);
@@ -240,15 +251,15 @@ __global__ void __launch_bounds__(kThreads) step_proj_bwd_kernel(const PParams p
       gt[b] = p.gdth != nullptr ? ld2f(p.gdth, r, p.C, c0, vec) : make_float2(0.f, 0.f);
     }
   };
-  float zv_next[z_regs<R>()];
+  float zv_next[z_regs<R, kBatch>()];
   float2 gn_next[kBatch], gt_next[kBatch];
   if (r0 + warp * kBatch < p.rows) load(warp * kBatch, zv_next, gn_next, gt_next);
   for (int i0 = warp * kBatch; i0 < kRowsPerCta; i0 += kStep) {
     if (r0 + i0 >= p.rows) break;
-    float zv[z_regs<R>()];
+    float zv[z_regs<R, kBatch>()];
     float2 gn[kBatch], gt[kBatch];
 #pragma unroll
-    for (int i = 0; i < z_regs<R>(); ++i) zv[i] = zv_next[i];
+    for (int i = 0; i < z_regs<R, kBatch>(); ++i) zv[i] = zv_next[i];
 #pragma unroll
     for (int b = 0; b < kBatch; ++b) {
       gn[b] = gn_next[b];
@@ -261,8 +272,8 @@ __global__ void __launch_bounds__(kThreads) step_proj_bwd_kernel(const PParams p
       float zn[R], zt[R];
 #pragma unroll
       for (int k = 0; k < R; ++k) {
-        zn[k] = batch_z<R>(zv, b, k);
-        zt[k] = batch_z<R>(zv, b, R + k);
+        zn[k] = batch_z<R, kBatch>(zv, b, k);
+        zt[k] = batch_z<R, kBatch>(zv, b, R + k);
       }
       if (r >= p.rows) break;
       float g1[2] = {gn[b].x, gn[b].y}, g2[2] = {gt[b].x, gt[b].y};

@@ -1758,8 +1758,12 @@ __global__ void __launch_bounds__(kT) mimo_layer_bwd16_kernel(const LParams p) {
 struct TcBLay {
   static constexpr int dyt = 0;                          // 64 x 32 fp32, swizzled
   static constexpr int bwt = dyt + 64 * 32;              // 32 x 32 fp32, swizzled
-  static constexpr int ht = bwt + 32 * 32;               // 16 x 32 fp32, swizzled
-  static constexpr int Co = ht + 16 * 32;                // c_out (4 x 32)
+  // The chunk's states, row t = [h_re | -h_im], and its dy rows, both 16 x 32 fp32 in the
+  // 32-byte-based swizzle: the MN-major A operand (h; the dy rows behind it fill the
+  // accumulator rows 32-63, which are not read) and B operand (dy) of the dC sums.
+  static constexpr int ht = bwt + 32 * 32;
+  static constexpr int dy32 = ht + 16 * 32;
+  static constexpr int Co = dy32 + 16 * 32;              // c_out (4 x 32)
   static constexpr int Dp = Co + 4 * 32;
   static constexpr int prm = Dp + 32;                    // a, omega, detune (3 x 16)
   static constexpr int cin = prm + 48;                   // scan carry (16 float2)
@@ -1777,13 +1781,14 @@ struct TcBLay {
   static constexpr int db = gs + 16 * kB_HW * 2;
   static constexpr int sr = db + 16 * kB_HW * 2;
   static constexpr int dr = sr + 64;
-  static constexpr int bar = dr + 64;                    // the adjoint MMA's 8-byte mbarrier
+  static constexpr int bar = dr + 64;                    // two 8-byte mbarriers: readout adjoint, dC
   static constexpr int tslot = bar + 4;
   static constexpr int total = tslot + 4;
   static constexpr int red = lam;                        // end-of-kernel sums reuse lam + braw
   static constexpr int rb = lam + 3 * 16 * (kT / 8);
 };
-static_assert(TcBLay::bwt % 256 == 0 && TcBLay::ht % 256 == 0 && TcBLay::stg0 % 4 == 0 &&
+static_assert(TcBLay::bwt % 256 == 0 && TcBLay::ht % 256 == 0 && TcBLay::dy32 == TcBLay::ht + 512 &&
+                  TcBLay::stg0 % 4 == 0 &&
                   TcBLay::bar % 2 == 0 && TcBLay::rb + 2 * (kT / 8) <= TcBLay::gs,
               "tensor-core backward layout");
 
@@ -1818,8 +1823,8 @@ __device__ __forceinline__ float tcb_dy(const float* sm, int row, int f) {
 // h_t[n] from the h tile, which stores [h_re | -h_im].
 __device__ __forceinline__ float2 tcb_h(const float* sm, int t, int n) {
   const char* ht = reinterpret_cast<const char*>(sm + TcBLay::ht);
-  const float re = *reinterpret_cast<const float*>(ht + semx::tc::sw128(t, n >> 2) + 4 * (n & 3));
-  const float nim = *reinterpret_cast<const float*>(ht + semx::tc::sw128(t, (n >> 2) + 4) + 4 * (n & 3));
+  const float re = *reinterpret_cast<const float*>(ht + semx::tc::sw128_32b(t, n));
+  const float nim = *reinterpret_cast<const float*>(ht + semx::tc::sw128_32b(t, n + 16));
   return make_float2(re, -nim);
 }
 
@@ -1860,7 +1865,8 @@ __global__ void __launch_bounds__(kT, 5) mimo_layer_bwd_tc_kernel(const LParams 
     *reinterpret_cast<float4*>(reinterpret_cast<char*>(sm + TcBLay::bwt) + semx::tc::sw128(n2, c)) =
         make_float4(v[0], v[1], v[2], v[3]);
   }
-  for (int i = tid; i < 16 * 32; i += kT) sm[TcBLay::ht + i] = 0.f;  // rows past a partial chunk stay 0
+  // h and dy32 tiles: rows past a partial chunk stay 0.
+  for (int i = tid; i < 2 * 16 * 32; i += kT) sm[TcBLay::ht + i] = 0.f;
   for (int i = tid; i < R * FH; i += kT) sm[TcBLay::Co + i] = p.cout[(int64_t)h * R * FH + i];
   for (int i = tid; i < FH; i += kT) sm[TcBLay::Dp + i] = p.D[(int64_t)h * FH + i];
   if (tid < NH) {
@@ -1870,8 +1876,14 @@ __global__ void __launch_bounds__(kT, 5) mimo_layer_bwd_tc_kernel(const LParams 
     reinterpret_cast<float2*>(sm + TcBLay::cadj)[tid] = make_float2(0.f, 0.f);
   }
   uint64_t* bar_adj = reinterpret_cast<uint64_t*>(sm + TcBLay::bar);
-  if (tid < 32) semx::tc::tmem_alloc(reinterpret_cast<uint32_t*>(sm + TcBLay::tslot), 32);
-  if (tid == 0) semx::tc::mbar_init(bar_adj, 1);
+  uint64_t* bar_dc = bar_adj + 1;
+  // Tensor memory: columns 0-31 the readout adjoint of a 64-token tile, 32-63 the dC /
+  // dc_out sums over the whole sequence.
+  if (tid < 32) semx::tc::tmem_alloc(reinterpret_cast<uint32_t*>(sm + TcBLay::tslot), 64);
+  if (tid == 0) {
+    semx::tc::mbar_init(bar_adj, 1);
+    semx::tc::mbar_init(bar_dc, 1);
+  }
   semx::tc::fence_before_sync();
   __syncthreads();
   semx::tc::fence_after_sync();
@@ -1889,16 +1901,14 @@ __global__ void __launch_bounds__(kT, 5) mimo_layer_bwd_tc_kernel(const LParams 
 
   // Thread roles (fixed for the whole kernel).
   const int tA = tid / 8, npA = tid % 8;   // (token, mode pair) items
-  const int fC = tid / 4, nqC = tid % 4;   // dC items (channel, 4 modes)
   const int rO = tid / FH, fO = tid % FH;  // dcout items (rank, channel) when R = 4
   float acc_a[2] = {0.f, 0.f}, acc_om[2] = {0.f, 0.f}, acc_sd[2] = {0.f, 0.f};
-  float aCr[4] = {}, aCi[4] = {};
   float aO = 0.f, aD = 0.f;
   float aBnu = 0.f, aBth = 0.f;
   const float2 bias = dt_bias(p, h);
   const int nck = p.nck;
-  uint32_t ph_adj = 0;
-  bool bail = false, adj_pending = false;
+  uint32_t ph_adj = 0, ph_dc = 0;
+  bool bail = false, adj_pending = false, dc_pending = false;
   float pre[kPre];
   auto stage = [&](int k, int b) {
     const int t0 = k * CT, nt = min(CT, L - t0);
@@ -1956,7 +1966,15 @@ __global__ void __launch_bounds__(kT, 5) mimo_layer_bwd_tc_kernel(const LParams 
     const float* scs = sbs + CT * R;
     const int xw = fl.xw, bxw = fl.bxw, btw = fl.btw, ctw = fl.ctw;
 
-    // A. Poles, raw and gained drive per (token, mode pair); entry state.
+    // A. Poles, raw and gained drive per (token, mode pair); entry state. The chunk's dy
+    // rows into the dC operand tile, one 16-byte piece per thread.
+    {
+      static_assert(kT == 16 * 8, "one dy piece per thread");
+      const int t = tid >> 3, c = tid & 7;
+      *reinterpret_cast<float4*>(reinterpret_cast<char*>(sm + TcBLay::dy32) + semx::tc::sw128_32b(t, 4 * c)) =
+          *reinterpret_cast<const float4*>(reinterpret_cast<const char*>(sm + TcBLay::dyt) +
+                                           semx::tc::sw128(row0 + t, c));
+    }
     if (tid < NH) {
       const float2 c = reinterpret_cast<const float2*>(p.ckpt)[((s * nck + k) * p.H + h) * NH + tid];
       cin[tid] = c;
@@ -2008,9 +2026,8 @@ __global__ void __launch_bounds__(kT, 5) mimo_layer_bwd_tc_kernel(const LParams 
     __syncthreads();
     // B. States of the chunk from the checkpoint, into the h tile as [h_re | -h_im].
     chunk_scan_to<kB_SEG, CT>(lam, gs, cin, NH, HW, nt, [&](int t, int n, float2 v) {
-      char* base = htile + t * 128 + 4 * (n & 3);
-      *reinterpret_cast<float*>(base + (((n >> 2) ^ (t & 7)) << 4)) = v.x;
-      *reinterpret_cast<float*>(base + ((((n >> 2) + 4) ^ (t & 7)) << 4)) = -v.y;
+      *reinterpret_cast<float*>(htile + semx::tc::sw128_32b(t, n)) = v.x;
+      *reinterpret_cast<float*>(htile + semx::tc::sw128_32b(t, n + 16)) = -v.y;
     });
     __syncthreads();
     // C. Rank read and its adjoint per (token, rank), each item split over a thread pair
@@ -2027,8 +2044,8 @@ __global__ void __launch_bounds__(kT, 5) mimo_layer_bwd_tc_kernel(const LParams 
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
           const int c4 = 2 * half + c;
-          const float4 hre = *reinterpret_cast<const float4*>(htile + semx::tc::sw128(t, c4));
-          const float4 hni = *reinterpret_cast<const float4*>(htile + semx::tc::sw128(t, c4 + 4));
+          const float4 hre = *reinterpret_cast<const float4*>(htile + semx::tc::sw128_32b(t, 4 * c4));
+          const float4 hni = *reinterpret_cast<const float4*>(htile + semx::tc::sw128_32b(t, 4 * c4 + 16));
           const float4 cre = ld4(cr + 4 * c4), cim = ld4(cr + NH + 4 * c4);
           rd = fmaf(cre.x, hre.x, fmaf(cim.x, hni.x, rd));
           rd = fmaf(cre.y, hre.y, fmaf(cim.y, hni.y, rd));
@@ -2053,9 +2070,25 @@ __global__ void __launch_bounds__(kT, 5) mimo_layer_bwd_tc_kernel(const LParams 
         st<true>(p.dproj, (s * p.L + t0 + t) * p.P + cols.sc + r, rd * dyc);
       }
     }
+    // The chunk's dC terms on the tensor cores, accumulated in tensor memory over the whole
+    // sequence: D[m, f] += sum_t h[t, m] dy[t, f] (m < 32: h_re, -h_im), both tiles read
+    // MN-major; one MMA per 8 tokens. Waited for at the end of the chunk, before the tiles
+    // change.
+    semx::tc::fence_smem_to_async();
+    __syncthreads();
+    if (tid == 0) {
+      constexpr uint32_t idesc = semx::tc::idesc_tf32(64, 32, true);
+      const uint32_t a0 = semx::tc::smem_addr(sm + TcBLay::ht), b0 = semx::tc::smem_addr(sm + TcBLay::dy32);
+#pragma unroll
+      for (int kk = 0; kk < 2; ++kk)
+        semx::tc::mma_tf32(taddr + 32u, semx::tc::desc_sw128b32_mnmajor(a0 + 1024u * kk, 2048u),
+                           semx::tc::desc_sw128b32_mnmajor(b0 + 1024u * kk, 2048u), idesc,
+                           k < nck - 1 || kk > 0);
+      semx::tc::mma_commit(bar_dc);
+    }
+    dc_pending = true;
     // D. Readout adjoint (drained into db after phase A) plus the rank terms, and the c_t
     // gradient, per (token, mode pair).
-    if (R > 0) __syncthreads();
     if (tA < nt) {
       const int t = tA, na = 2 * npA;
       float2 g0 = db[t * HW + na], g1 = db[t * HW + na + 1];
@@ -2209,28 +2242,24 @@ __global__ void __launch_bounds__(kT, 5) mimo_layer_bwd_tc_kernel(const LParams 
       acc += __shfl_xor_sync(0xffffffffu, acc, 1);
       if (act && half == 0) st<true>(p.dproj, (s * p.L + t0 + t) * p.P + cols.sb + r, acc);
     }
-    // I. dC, dc_out and dD sums over the chunk, fixed ownership.
+    // I. dc_out and dD sums over the chunk, fixed ownership.
     for (int t = 0; t < nt; ++t) {
-      {  // dC[fC, 4 nqC .. +3] += dy (h_re, -h_im)
-        const float dv = tcb_dy(sm, row0 + t, fC);
-        const float4 hre = *reinterpret_cast<const float4*>(htile + semx::tc::sw128(t, nqC));
-        const float4 hni = *reinterpret_cast<const float4*>(htile + semx::tc::sw128(t, nqC + 4));
-        aCr[0] = fmaf(dv, hre.x, aCr[0]);
-        aCr[1] = fmaf(dv, hre.y, aCr[1]);
-        aCr[2] = fmaf(dv, hre.z, aCr[2]);
-        aCr[3] = fmaf(dv, hre.w, aCr[3]);
-        aCi[0] = fmaf(dv, hni.x, aCi[0]);
-        aCi[1] = fmaf(dv, hni.y, aCi[1]);
-        aCi[2] = fmaf(dv, hni.z, aCi[2]);
-        aCi[3] = fmaf(dv, hni.w, aCi[3]);
-      }
       if (R > 0) aO = fmaf(sm[TcBLay::sr + t * R + rO], tcb_dy(sm, row0 + t, fO), aO);
       if (tid < FH) aD = fmaf(tcb_dy(sm, row0 + t, tid), static_cast<float>(xs[t * xw + tid]), aD);
     }
     if (k > 0) store_small<RK, CT>(p, sm + smlo[b ^ 1], CT, pre);
-    // Every thread is past its reads of the chunk's dy rows: refill them with the same
-    // chunk of the previous tile.
-    __syncthreads();
+    // Every thread is past its reads of the chunk's dy rows, and the dC MMA is done with
+    // the h and dy32 tiles: refill the dy rows with the same chunk of the previous tile.
+    {
+      const bool ok = semx::tc::mbar_wait(bar_dc, ph_dc, kTcWaitLimit);
+      if (__syncthreads_or(!ok)) {
+        if (tid == 0) atomicAdd(&g_tc_timeouts, 1u);
+        bail = true;
+        break;
+      }
+      ph_dc ^= 1u;
+      dc_pending = false;
+    }
     if (k >= 4) tcb_load_dy(p, sm, s, h, row0, (k - 4) * CT, CT);
     cp_async_commit();
   }
@@ -2239,11 +2268,16 @@ __global__ void __launch_bounds__(kT, 5) mimo_layer_bwd_tc_kernel(const LParams 
   const int64_t H = p.H;
   float* row = p.part + s * p.K;
   if (!bail) {
+    // dC from tensor memory: accumulator row m is read by lane m % 16 of warp m / 16
+    // (rows 0-15: dC_re, 16-31: dC_im of mode m % 16), its 32 columns being the channels.
+    semx::tc::fence_after_sync();
+    if (warp < 2) {
+      float v[32];
+      semx::tc::tmem_ld32(taddr + 32u + ((uint32_t)(32 * warp) << 16), v);
+      if (lane < NH) {
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int64_t i = ((int64_t)h * FH + fC) * NH + 4 * nqC + j;
-      row[2 * i] = aCr[j];
-      row[2 * i + 1] = aCi[j];
+        for (int f = 0; f < FH; ++f) row[2 * (((int64_t)h * FH + f) * NH + lane) + warp] = nck > 0 ? v[f] : 0.f;
+      }
     }
     // Per-mode sums over the 16 token lanes that share a mode pair, fixed order.
     float* red = sm + TcBLay::red;  // [3][NH][kT / 8]
@@ -2280,14 +2314,15 @@ __global__ void __launch_bounds__(kT, 5) mimo_layer_bwd_tc_kernel(const LParams 
       for (int qq = 0; qq < kT / 8; ++qq) acc += sm[TcBLay::rb + tid * (kT / 8) + qq];
       row[off + tid * H + h] = acc;
     }
-  } else if (adj_pending) {
-    // After a give-up, let the outstanding MMA finish (bounded) before the tensor memory
-    // it writes is released.
-    semx::tc::mbar_wait(bar_adj, ph_adj, kTcWaitLimit);
+  } else {
+    // After a give-up, let the outstanding MMAs finish (bounded) before the tensor memory
+    // they write is released.
+    if (adj_pending) semx::tc::mbar_wait(bar_adj, ph_adj, kTcWaitLimit);
+    if (dc_pending) semx::tc::mbar_wait(bar_dc, ph_dc, kTcWaitLimit);
   }
   semx::tc::fence_before_sync();
   __syncthreads();
-  if (tid < 32) semx::tc::tmem_dealloc(taddr, 32);
+  if (tid < 32) semx::tc::tmem_dealloc(taddr, 64);
 }
 
 // ------------------------------------------------------------------------ host side

@@ -1,5 +1,6 @@
 // Fifth-generation tensor-core (tcgen05) helpers for sm_100a: tensor-memory allocation,
-// shared-memory matrix descriptors in the 128-byte-swizzled K-major layout, the single-
+// shared-memory matrix descriptors (128-byte-swizzled K-major, and the 32-byte-based
+// swizzle for MN-major tf32), the single-
 // thread MMA issue, its completion through an mbarrier (bounded wait), and the warp-wide
 // tensor-memory load of an accumulator row.
 //
@@ -8,6 +9,11 @@
 //     32 floats (128 bytes) per M / N index, 8-row atoms of 1024 bytes, the 16-byte chunk
 //     c of row r stored at chunk position c ^ (r & 7). Tiles start on 1024-byte boundaries.
 //     One MMA consumes 8 K values (32 bytes); K slice k starts 32 k bytes into the row.
+//   * MN-major tf32 operands (the transposed reading: rows are K indices, 32 M / N values
+//     per 128-byte row) use the 128-byte swizzle on a 32-byte base instead: the 32-byte
+//     granule g of row r stored at granule position g ^ (r & 3), 4-row atoms of 512 bytes
+//     (sw128_32b). One MMA consumes 8 rows (8 K values, 1024 bytes) per 32 M / N values.
+//     This is the only shared-memory layout the tensor cores read MN-major for tf32.
 //   * M = 64 accumulators (cta_group::1): row m lives in tensor-memory lane
 //     (m % 16) + 32 (m / 16), column n in column n. Warp w may read lanes 32 w .. 32 w + 31,
 //     so rows 16 w .. 16 w + 15 are read by lanes 0..15 of warp w.
@@ -34,11 +40,28 @@ __device__ __forceinline__ uint64_t desc_sw128_kmajor(uint32_t addr) {
          ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
 
-// Instruction descriptor of kind::tf32 with fp32 accumulation, both operands K-major.
-__host__ __device__ constexpr uint32_t idesc_tf32(int M, int N) {
+// Byte offset of column `c` (0..31, fp32) of row `r` in a tile of the 32-byte-based 128-byte
+// swizzle (MN-major tf32 operands).
+__host__ __device__ __forceinline__ int sw128_32b(int r, int c) {
+  return r * 128 + (((c >> 3) ^ (r & 3)) << 5) + 4 * (c & 7);
+}
+
+// Shared-memory descriptor of an MN-major tf32 operand in the 32-byte-based 128-byte
+// swizzle (layout type 1): `addr` is the start of its first 4-row K group (512-byte
+// aligned), the next 32 M / N values start `mn_stride` bytes further (leading-byte offset),
+// the next 4-row K group 512 bytes further (stride-byte offset), descriptor version 1.
+__device__ __forceinline__ uint64_t desc_sw128b32_mnmajor(uint32_t addr, uint32_t mn_stride) {
+  return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)((mn_stride >> 4) & 0x3FFFu) << 16) |
+         ((uint64_t)(512 >> 4) << 32) | ((uint64_t)1 << 46) | ((uint64_t)1 << 61);
+}
+
+// Instruction descriptor of kind::tf32 with fp32 accumulation; both operands K-major, or
+// both MN-major (`mn_major`).
+__host__ __device__ constexpr uint32_t idesc_tf32(int M, int N, bool mn_major = false) {
   return (1u << 4)            // accumulator format: f32
          | (2u << 7)          // A format: tf32
          | (2u << 10)         // B format: tf32
+         | (mn_major ? (1u << 15) | (1u << 16) : 0u)  // A, B major-ness
          | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 

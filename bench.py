@@ -1348,8 +1348,13 @@ def measure_generator(args, rank, local_rank, world, device, steps, clocks=True)
     n0 = _lib.launch_count()
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s.record(stream)
+    # cudaProfilerStart / Stop bracket the timed steps, so that a profiler run with
+    # --profile-from-start off captures exactly their launches, from every host thread
+    # (autograd runs the backward on its own thread).
+    torch.cuda.profiler.start()
     for _ in range(steps):
         loss = step(clean_d, noisy_d)
+    torch.cuda.profiler.stop()
     e.record(stream)
     _barrier(world, device)
     launches = _lib.launch_count() - n0

@@ -296,6 +296,19 @@ def test_bf16_layer_variants(extra):
     runs the CUDA-core kernels), 2 x 83 tokens (a partial 64-token tile and chunk),
     against the float64 oracle on the GPU's own projection rows, within the bf16-input
     tolerance."""
+    _check_bf16_variant(extra, 83)
+
+
+@pytest.mark.parametrize("T", [5, 16, 64, 65])
+def test_bf16_layer_chunk_and_tile_edges(T):
+    """The tensor-core kernels (rank 4) at sequence lengths on the edges of their 16-token
+    chunks and 64-token tiles: one partial chunk (the dC sums then come from a single MMA
+    pair that starts the accumulation), exactly one chunk, exactly one tile, one token
+    past a tile."""
+    _check_bf16_variant(dict(rank=4), T)
+
+
+def _check_bf16_variant(extra, T):
     import torch.nn.functional as F
 
     from semambaxlinoss_b200.selective_lru import SelectiveLRUMIMO
@@ -311,8 +324,8 @@ def test_bf16_layer_variants(extra):
         m.omega.copy_(torch.randn(m.omega.shape, generator=g) * 3.0)
         if extra.get("envelope_readout"):
             m.env_gain.copy_(torch.randn(m.env_gain.shape, generator=g) * 0.1)
-    x = randn((2, 83, 256), g, scale=0.5).to(torch.bfloat16)
-    gy = randn((2, 83, 256), g)
+    x = randn((2, T, 256), g, scale=0.5).to(torch.bfloat16)
+    gy = randn((2, T, 256), g)
     out = _layer_gpu(m, x, gy, torch.bfloat16)
     with torch.no_grad():
         W, _ = m._projection()

@@ -10,6 +10,10 @@ What runs (all on CPU, float64, through the reference's own modules and function
 * models/selective_lru/selective_lru.py  SelectiveLRU (every gain / option),
   SelectiveLRUMIMO (every gain / option, rank > 0) and _selective_recurrence
 * models/mixer.py                  MambaStyleMixer around SelectiveLRU and LinOSS
+* models/mamba_block.py            MambaBlock and TFMambaBlock (selective-LRU time mixers,
+  LinOSS frequency mixers), with the third-party mamba_ssm package it imports replaced by
+  the stand-in in mamba_ssm_standin/ (Block, RMSNorm restated from their documented
+  behaviour): the fixtures pin the reference's own block code above those two pieces
 
 Usage: SEMX_REFERENCE=<reference checkout> python tests/golden/make_golden.py
 """
@@ -18,6 +22,7 @@ from __future__ import annotations
 import importlib.util
 import os
 import sys
+import types
 from pathlib import Path
 
 import torch
@@ -44,6 +49,34 @@ def _import_reference():
     from models.mixer import MambaStyleMixer  # noqa: E402
 
     return SelectiveLRU, SelectiveLRUMIMO, _selective_recurrence, lin, MambaStyleMixer
+
+
+def _import_reference_blocks():
+    """The reference's models/mamba_block.py, on the mamba_ssm stand-in. Its
+    ``from models.linoss import ...`` goes through models/linoss/__init__.py, which imports
+    a module the reference does not contain, so ``models.linoss`` is registered from the
+    layer file with a placeholder for the selective LinOSS variant (not used here)."""
+    sys.path.insert(0, str(OUT / "mamba_ssm_standin"))
+    sys.path.insert(0, str(OUT.parent.parent))  # the stand-in's _init_weights restatement
+    import models  # noqa: F401,E402
+
+    spec = importlib.util.spec_from_file_location("models.linoss.linoss", REF / "models/linoss/linoss.py")
+    lin = importlib.util.module_from_spec(spec)
+    sys.modules["models.linoss.linoss"] = lin
+    spec.loader.exec_module(lin)
+    pkg = types.ModuleType("models.linoss")
+    pkg.__path__ = [str(REF / "models/linoss")]
+    pkg.LinOSS = lin.LinOSS
+
+    class SelectiveLinOSSIM:  # the module the reference's package file names is absent
+        def __init__(self, *args, **kwargs):
+            raise NotImplementedError
+
+    pkg.SelectiveLinOSSIM = SelectiveLinOSSIM
+    sys.modules["models.linoss"] = pkg
+    from models.mamba_block import MambaBlock, TFMambaBlock  # noqa: E402
+
+    return MambaBlock, TFMambaBlock
 
 
 def _run_module(module, x, fwd_kwargs, seed):
@@ -232,6 +265,66 @@ def mixer_cases(MambaStyleMixer, SelectiveLRU, lin):
     return cases
 
 
+def _tf_cfg(bidirectional, use_transpose):
+    time_mixer = dict(ssm="selective_lru", d_state=4, d_conv=4, expand=2, bidirectional=bidirectional,
+                      ssm_params=dict(dt_rank=2, n_real_modes=1))
+    freq_mixer = dict(ssm="linoss", d_state=6, d_conv=4, expand=2, bidirectional=True,
+                      ssm_params=dict(discretization="IMEX", damping=True))
+    return {"model_cfg": dict(hid_feature=8, use_transpose=use_transpose, time_mixer=time_mixer,
+                              freq_mixer=freq_mixer)}
+
+
+def _oracle_spec(block, cfg):
+    """How oracle/blocks.py evaluates one MambaBlock of the fixture: the scan layer's kind,
+    its configuration and the branch mode."""
+    ssm = block.forward_blocks[0].mixer.ssm
+    if cfg["ssm"] == "selective_lru":
+        scfg = dict(dt_rank=ssm.dt_rank, d_state=ssm.d_state, input_gain=ssm.input_gain)
+    else:
+        p = cfg.get("ssm_params", {})
+        scfg = dict(discretization=p.get("discretization", "IMEX"), damping=p.get("damping", True),
+                    a_from_g=p.get("a_from_g", True))
+    return dict(kind=cfg["ssm"], ssm=scfg, bidirectional=cfg.get("bidirectional", True))
+
+
+def block_cases(MambaBlock, TFMambaBlock):
+    cases = {}
+    # A bidirectional selective-LRU block and a unidirectional LinOSS block on (S, L, C).
+    specs = [
+        dict(ssm="selective_lru", d_state=4, d_conv=4, expand=2, bidirectional=True,
+             ssm_params=dict(dt_rank=2, input_gain="gamma")),
+        dict(ssm="linoss", d_state=6, d_conv=4, expand=2, bidirectional=False,
+             ssm_params=dict(discretization="IMEX", damping=True)),
+    ]
+    for i, cfg in enumerate(specs):
+        torch.manual_seed(1500 + i)
+        m = MambaBlock(8, cfg).double()
+        _perturb(m, seed=1600 + i, scale=0.1)
+        g = torch.Generator().manual_seed(1700 + i)
+        x = torch.randn(3, 11, 8, generator=g, dtype=torch.float64)
+        rec = _run_module(m, x, {}, seed=1800 + i)
+        rec["config"] = cfg
+        rec["oracle_spec"] = _oracle_spec(m, cfg)
+        cases[f"mamba_block_{i}_{cfg['ssm']}"] = rec
+    # TF-blocks on (b, c, t, f): bidirectional time branch with the transposed-conv
+    # projections, and a unidirectional time branch with the linear projections.
+    for i, (bi, tr) in enumerate([(True, True), (False, False)]):
+        torch.manual_seed(1900 + i)
+        cfg = _tf_cfg(bi, tr)
+        m = TFMambaBlock(cfg).double()
+        _perturb(m, seed=2000 + i, scale=0.05)
+        g = torch.Generator().manual_seed(2100 + i)
+        x = torch.randn(2, 8, 10, 6, generator=g, dtype=torch.float64)
+        rec = _run_module(m, x, {}, seed=2200 + i)
+        rec["config"] = cfg
+        mc = cfg["model_cfg"]
+        rec["oracle_spec"] = dict(time=_oracle_spec(m.time_mamba, mc["time_mixer"]),
+                                  freq=_oracle_spec(m.freq_mamba, mc["freq_mixer"]),
+                                  use_transpose=mc["use_transpose"])
+        cases[f"tf_block_{i}"] = rec
+    return cases
+
+
 def main():
     SelectiveLRU, SelectiveLRUMIMO, _selective_recurrence, lin, Mixer = _import_reference()
     groups = {
@@ -241,6 +334,7 @@ def main():
         "recurrence": recurrence_case(_selective_recurrence),
         "mixer": mixer_cases(Mixer, SelectiveLRU, lin),
     }
+    groups["blocks"] = block_cases(*_import_reference_blocks())
     for name, cases in groups.items():
         path = OUT / f"{name}.pt"
         torch.save(cases, path)

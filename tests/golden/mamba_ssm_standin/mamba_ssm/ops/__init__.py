@@ -1,0 +1,1 @@
+"""Part of the mamba_ssm stand-in (see the package docstring)."""

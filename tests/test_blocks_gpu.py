@@ -99,6 +99,52 @@ def test_tf_block_matches_oracle(bidirectional, use_transpose):
         assert_close(p.grad, ref, floor_tol(rel_err(g32[n], ref)), f"d{n}")
 
 
+@pytest.mark.parametrize("name", ["mamba_block_0_selective_lru", "mamba_block_1_linoss", "tf_block_0", "tf_block_1"])
+def test_blocks_match_golden(golden, name):
+    """MambaBlock and TFMambaBlock with the state dicts of the reference's own blocks (run
+    on the mamba_ssm stand-in by tests/golden/make_golden.py) against the reference's
+    float64 outputs and gradients; each tensor within the fp32 tolerance, floored at twice
+    the error of the float32 oracle (as for the oracle comparison above)."""
+    from semambaxlinoss_b200.mamba_block import MambaBlock, TFMambaBlock
+
+    rec = golden("blocks")[name]
+    sp = rec["oracle_spec"]
+
+    def branch(b):
+        return b["kind"], b["ssm"], dict(bidirectional=b["bidirectional"])
+
+    if name.startswith("tf"):
+        m = TFMambaBlock(rec["config"])
+
+        def fwd(p, x):
+            return oblk.tf_block_forward(p, x, branch(sp["time"]), branch(sp["freq"]), use_transpose=sp["use_transpose"])
+    else:
+        m = MambaBlock(rec["x"].shape[-1], rec["config"])
+
+        def fwd(p, x):
+            return oblk.mamba_block_forward(p, x, *branch(sp)[:2], **branch(sp)[2])
+    m.load_state_dict({k: v.float() for k, v in rec["state_dict"].items()})
+    # The float32 oracle's distance from the reference sets the floor of each tolerance.
+    p32 = {k: v.float().clone().requires_grad_(True) for k, v in rec["state_dict"].items()}
+    x32 = rec["x"].float().clone().requires_grad_(True)
+    y32 = fwd(p32, x32)
+    names = list(p32)
+    g32 = torch.autograd.grad((y32 * rec["grad_y"].float()).sum(), [x32] + [p32[n] for n in names],
+                              allow_unused=True)
+    g32 = dict(zip(["x"] + names, g32))
+    dev = cuda()
+    m = m.to(dev)
+    x = to32(rec["x"], dev).requires_grad_(True)
+    y = m(x)
+    (y * to32(rec["grad_y"], dev)).sum().backward()
+    assert_close(y, rec["y"], floor_tol(rel_err(y32.detach(), rec["y"])), f"{name} y")
+    assert_close(x.grad, rec["grad_x"], floor_tol(rel_err(g32["x"], rec["grad_x"])), f"{name} dx")
+    for n, p in m.named_parameters():
+        ref = rec["param_grads"][n]
+        got32 = g32[n] if g32[n] is not None else torch.zeros_like(ref)
+        assert_close(p.grad, ref, floor_tol(rel_err(got32, ref)), f"{name} d{n}")
+
+
 def test_tf_block_bf16_autocast():
     """bf16 autocast around fp32 scans: finite, and close to the fp32 block."""
     from semambaxlinoss_b200.mamba_block import TFMambaBlock

@@ -152,3 +152,27 @@ def test_mixer_matches_reference(golden, idx):
     rec = cases[sorted(cases)[idx]]
     cfg = rec["config"]
     _module_case(rec, lambda p, x: oblk.mixer_forward(p, x, cfg["kind"], cfg["ssm"], cfg["d_conv"], cfg["causal"]))
+
+
+def _branch(sp):
+    return sp["kind"], sp["ssm"], dict(bidirectional=sp["bidirectional"])
+
+
+@pytest.mark.parametrize("name", ["mamba_block_0_selective_lru", "mamba_block_1_linoss"])
+def test_mamba_blocks_match_reference(golden, name):
+    """MambaBlock (models/mamba_block.py:344-396 of the reference, run on the mamba_ssm
+    stand-in): the bidirectional branch flips, the residual stream and the concatenation."""
+    rec = golden("blocks")[name]
+    kind, scfg, kw = _branch(rec["oracle_spec"])
+    _module_case(rec, lambda p, x: oblk.mamba_block_forward(p, x, kind, scfg, **kw))
+
+
+@pytest.mark.parametrize("idx", [0, 1])
+def test_tf_blocks_match_reference(golden, idx):
+    """TFMambaBlock (models/mamba_block.py:419-508 of the reference): time blocks over the
+    (batch x bins) sequences, frequency blocks over the (batch x frames) sequences, the
+    channel projections (transposed conv or linear) and both residual adds."""
+    rec = golden("blocks")[f"tf_block_{idx}"]
+    sp = rec["oracle_spec"]
+    _module_case(rec, lambda p, x: oblk.tf_block_forward(p, x, _branch(sp["time"]), _branch(sp["freq"]),
+                                                          use_transpose=sp["use_transpose"]))
